@@ -1,0 +1,45 @@
+"""Shared fixtures. GPU tests are marked ``gpu``; everything else runs on a CPU-only host."""
+
+from __future__ import annotations
+
+import importlib
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+REPO = Path(__file__).resolve().parent.parent
+GOLDEN = REPO / "tests" / "golden"
+if str(REPO) not in sys.path:
+    sys.path.insert(0, str(REPO))
+
+PACKAGE = "inference-engine-from-scratch_b200"
+
+
+def pytest_configure(config) -> None:
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+def package():
+    return importlib.import_module(PACKAGE)
+
+
+def submodule(name: str):
+    return importlib.import_module(f"{PACKAGE}.{name}")
+
+
+def load_golden(name: str):
+    return torch.load(GOLDEN / name, weights_only=False)
+
+
+@pytest.fixture(scope="session")
+def pkg():
+    return package()
+
+
+@pytest.fixture(scope="session")
+def cuda_device():
+    if not torch.cuda.is_available():
+        pytest.fail("this test needs a CUDA device; run it with -m gpu on a B200")
+    return torch.device("cuda", 0)

@@ -1,0 +1,116 @@
+"""The CPU oracle reproduces the reference's own outputs (fixtures made by tests/golden/make_golden.py).
+
+This is what pins the oracle: every fixture came from the unmodified reference run on the CPU.
+"""
+
+from __future__ import annotations
+
+import json
+
+import pytest
+import torch
+
+from oracle import ngram, philox, qwen3, speculative, verify
+from tests.conftest import GOLDEN, load_golden, package
+
+FP32_LOGITS_ATOL = 1e-4
+BF16_LOGITS_ATOL = 2e-2
+
+
+def test_ngram_known_answers_and_random_histories() -> None:
+    cases = json.loads((GOLDEN / "ngram_cases.json").read_text())
+    assert cases[0]["expected"] == [3, 4, 5] and cases[1]["expected"] == []
+    for case in cases:
+        got = ngram.propose(case["history"], case["k"], case["max_ngram"])
+        fast = ngram.propose_numpy(case["history"], case["k"], case["max_ngram"])
+        assert got == case["expected"] == fast, case
+
+
+def test_philox_matches_the_published_known_answer() -> None:
+    # Random123 known-answer vectors for philox4x32-10 (zero, all-ones and pi-digit inputs)
+    assert philox.philox4x32_10((0, 0, 0, 0), (0, 0)) == (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)
+    ones = 0xFFFFFFFF
+    assert philox.philox4x32_10((ones,) * 4, (ones, ones)) == (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)
+    pi = philox.philox4x32_10((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0))
+    assert pi == (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1)
+
+
+def test_verify_proposal_with_injected_uniforms() -> None:
+    data = load_golden("verify_cases.pt")
+    assert data["cases"][0]["expected"] == [2, 4, 1, 5] and data["cases"][1]["expected"] == [2, 4]
+    for case in data["cases"]:
+        stream = philox.UniformStream(case["seed"])
+        got = verify.verify_proposal(
+            case["guesses"], None, case["logits"], case["temperature"], case["top_p"], stream
+        )
+        assert got == case["expected"], case["seed"]
+        assert stream.index == case["draws"], case["seed"]
+
+
+def test_top_p_keeps_the_same_tokens() -> None:
+    for case in load_golden("top_p_cases.pt")["cases"]:
+        probs = verify.token_probabilities(case["logits"], case["temperature"], case["top_p"])
+        assert torch.equal(probs > 0, case["kept"])
+        torch.testing.assert_close(probs, case["probs"], atol=1e-6, rtol=1e-5)
+
+
+def test_quantize_vectors_is_bit_exact() -> None:
+    for case in load_golden("quant_cases.pt")["cases"]:
+        q, s = qwen3.quantize_vectors(case["values"])
+        assert torch.equal(q, case["quantized"]) and torch.equal(s, case["scales"])
+        if case["values"].dtype == torch.float32:  # the reference's own bound (fp32 scales)
+            back = q.float() * s.float()
+            assert torch.all((back - case["values"]).abs() <= s / 2 + 1e-6)
+
+
+def _check_run(golden, cfg, weights, dtype, atol):
+    int8 = golden["int8"]
+    w = {k: v.to(dtype) for k, v in weights.items()}
+    if int8:
+        w = qwen3.quantize_weights(w)
+    runner = speculative.OracleRunner(w, cfg, golden["num_blocks"], 16, dtype, int8_kv=int8)
+    ids = golden["digest_ids"]
+    for index, record in enumerate(golden["records"]):
+        seq = speculative.Seq(
+            f"r{index}", list(record["prompt"]), len(record["prompt"]), golden["max_new"],
+            temperature=golden["temperature"], top_p=golden["top_p"], ignore_eos=True,
+        )
+        seed = record["seed"]
+        stream = philox.UniformStream(0 if seed is None else seed)
+        out = speculative.generate(runner, seq, golden["k"], golden["max_ngram"], uniforms=stream)
+        assert out.prefill_block_table == record["prefill_block_table"]
+        assert len(out.steps) == len(record["steps"])
+        for mine, ref in zip(out.steps, record["steps"]):
+            assert mine.draft == ref["draft"]
+            assert mine.block_table == ref["block_table"]
+            assert mine.new_tokens == ref["new_tokens"]
+            assert mine.uniforms_used == ref["draws"]
+            d = ref["logits"]
+            assert torch.equal(torch.argmax(mine.logits, dim=-1).to(torch.int32), d["argmax"])
+            torch.testing.assert_close(mine.logits.float()[:, ids], d["at_ids"], atol=atol, rtol=0)
+        assert out.tokens == record["tokens"]
+        assert len(runner.tables.blocks.free_blocks) == record["free_blocks_after"]
+
+
+@pytest.mark.parametrize(
+    "mode,dtype,atol",
+    [
+        ("fp32", torch.float32, FP32_LOGITS_ATOL),
+        ("bf16", torch.bfloat16, BF16_LOGITS_ATOL),
+        ("int8", torch.bfloat16, BF16_LOGITS_ATOL),
+        ("sampled", torch.bfloat16, BF16_LOGITS_ATOL),
+    ],
+)
+def test_serial_speculation_small_model(mode, dtype, atol) -> None:
+    pkg = package()
+    golden = load_golden(f"spec_small_{mode}.pt")
+    _check_run(golden, pkg.SMALL_TEST, pkg.make_weights(pkg.SMALL_TEST, seed=0), dtype, atol)
+
+
+def test_serial_speculation_config1_qwen3_0_6b_fp32() -> None:
+    """BASELINE config 1 exactly: 63 guesses proposed, 62 kept, 128 tokens, 12 blocks."""
+    pkg = package()
+    golden = load_golden("spec_config1_fp32.pt")
+    assert golden["proposed"] == 63 and golden["accepted"] == 62
+    _check_run(golden, pkg.QWEN3_0_6B, pkg.make_weights(pkg.QWEN3_0_6B, seed=0), torch.float32,
+               FP32_LOGITS_ATOL)
