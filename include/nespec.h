@@ -1,0 +1,258 @@
+/*
+ * nespec.h -- C ABI of the B200 (sm_100a) speculative-decoding step for nanoengine (Qwen3).
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream (``void* stream`` is a
+ * cudaStream_t; NULL = the legacy default stream), returns an int status (NE_OK = 0), and
+ * allocates no device memory: weights, the KV pool, the workspace and every output buffer come
+ * from the caller. All launches are stream-ordered and capturable in a CUDA graph.
+ *
+ * The reference (ak7270090/inference-engine-from-scratch, nanoengine) is pure Python; each entry
+ * below names the reference function it replaces (paths relative to nanoengine/src/nanoengine).
+ */
+#ifndef NESPEC_H
+#define NESPEC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NE_API __attribute__((visibility("default")))
+#else
+#define NE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status codes */
+#define NE_OK 0
+#define NE_ERR_INVALID 1        /* bad argument, shape or alignment */
+#define NE_ERR_CUDA 2           /* a CUDA runtime call or launch failed */
+#define NE_ERR_DEVICE 3         /* a kernel set a bit in the device status word */
+#define NE_ERR_UNSUPPORTED 4    /* a configuration this build does not implement */
+#define NE_ERR_WORKSPACE 5      /* workspace too small for the requested rows */
+
+/* device status word bits (int32 the kernels OR into; read with ne_read_status) */
+#define NE_DEV_TIMEOUT 1        /* a bounded wait ran out (pipeline stall) */
+#define NE_DEV_BAD_SLOT 2       /* a slot or block index outside the KV pool */
+#define NE_DEV_OUT_OF_BLOCKS 4  /* the free-block FIFO could not cover a reservation */
+#define NE_DEV_BAD_TOKEN 8      /* a token id outside [0, vocab) */
+#define NE_DEV_HISTORY_FULL 16  /* a sequence outgrew its history row or block-table row */
+
+#define NE_ABI_VERSION 1
+
+NE_API int ne_abi_version(void);
+NE_API const char* ne_status_string(int status);
+/* Copy the device status word to *host_out (synchronizes ``stream``) and optionally clear it. */
+NE_API int ne_read_status(const int32_t* device_status, int clear, int32_t* host_out, void* stream);
+
+/* ---------------------------------------------------------------- model description */
+typedef struct {
+  int vocab_size;
+  int hidden_size;
+  int intermediate_size;      /* per rank */
+  int num_layers;
+  int num_heads;              /* per rank */
+  int num_kv_heads;           /* per rank */
+  int head_dim;               /* 128 */
+  float rms_norm_eps;
+  int block_size;             /* KV block size: 16 */
+  int kv_int8;                /* 0: bf16 KV pool; 1: int8 KV + per (slot, head) bf16 scales */
+  int weight_int8;            /* 0: bf16 projections; 1: int8 + per-output-row bf16 scales */
+  long long num_cache_slots;  /* KV pool rows including the scratch slot (num_slots + 1) */
+  int max_positions;          /* rows of the RoPE tables */
+} ne_model_config;
+
+/*
+ * One decoder layer. Projection weights are row-major [out, in] bf16 (HF layout), except:
+ *   w_qkv    = cat(q_proj, k_proj, v_proj) rows          [(nh + 2 nkv) * 128, H]
+ *   w_gateup = gate_proj / up_proj interleaved in groups of 64 rows: rows 128 t .. 128 t + 63 are
+ *              gate rows 64 t .. 64 t + 63 and rows 128 t + 64 .. 128 t + 127 the matching up rows.
+ * The KV pool rows follow engine/memory/kv_cache_pool.py:34-69: [num_slots + 1, nkv, 128] with
+ * the last row the scratch slot that padded tokens write to.
+ */
+typedef struct {
+  const void* w_qkv;
+  const void* w_o;            /* [H, nh * 128] */
+  const void* w_gateup;
+  const void* w_down;         /* [H, I] */
+  const void* ln_in;          /* input_layernorm [H] bf16 */
+  const void* ln_post;        /* post_attention_layernorm [H] */
+  const void* q_norm;         /* [128] */
+  const void* k_norm;         /* [128] */
+  void* k_cache;              /* [slots + 1, nkv, 128] bf16 or int8 */
+  void* v_cache;
+  void* k_scale;              /* int8 KV: [slots + 1, nkv] bf16, else NULL */
+  void* v_scale;
+} ne_layer_weights;
+
+typedef struct {
+  const void* embed;          /* model.embed_tokens [V, H] bf16 */
+  const void* lm_head;        /* [V, H] bf16 (the embedding when tied) */
+  const void* final_norm;     /* model.norm [H] */
+  const void* rope_cos;       /* [max_positions, 128] bf16, models/qwen3.py:47-57 tables */
+  const void* rope_sin;
+} ne_head_weights;
+
+typedef struct ne_model ne_model;
+
+/* Replaces the construction in engine/runtime.py:132-182 (model + pool binding) for this path. */
+NE_API int ne_model_create(const ne_model_config* config, ne_model** out);
+NE_API int ne_model_destroy(ne_model* model);
+NE_API int ne_model_set_layer(ne_model* model, int layer, const ne_layer_weights* weights);
+NE_API int ne_model_set_head(ne_model* model, const ne_head_weights* head);
+/* Bytes of workspace for steps of up to ``max_rows`` token rows and ``max_seqs`` sequences. */
+NE_API int ne_model_workspace_bytes(const ne_model* model, int max_rows, int max_seqs, size_t* bytes);
+/* Bind the workspace (256-byte aligned). Creates the TMA descriptors of the activation buffers. */
+NE_API int ne_model_set_workspace(ne_model* model, void* workspace, size_t bytes, int max_rows, int max_seqs);
+/* Device status word the kernels of this model report into (inside the workspace). */
+NE_API int32_t* ne_model_status_word(ne_model* model);
+
+/* ---------------------------------------------------------------- forward over planned rows */
+/*
+ * Rows of one step (engine/generation/batch_builder.py:22-65, but packed: sequence b owns rows
+ * q_start[b] .. q_start[b] + q_len[b] - 1 and nothing is padded to the longest sequence).
+ * All pointers are device pointers; counts marked "device" are read by the kernels so that the
+ * launch shape (host bounds) stays fixed for CUDA-graph replay.
+ */
+typedef struct {
+  int max_rows;                  /* host bound on rows */
+  int num_seqs;                  /* batch entries */
+  const int32_t* num_rows;       /* device: rows this step (<= max_rows) */
+  const int32_t* token_ids;      /* [rows] */
+  const int32_t* positions;      /* [rows] */
+  const int32_t* slot_mapping;   /* [rows] */
+  const int32_t* q_start;        /* [num_seqs] */
+  const int32_t* q_len;          /* [num_seqs] (0 = idle) */
+  const int32_t* block_tables;   /* [*, block_table_stride] */
+  const int32_t* table_index;    /* [num_seqs] row of block_tables (NULL: row b) */
+  int block_table_stride;
+  int max_context;               /* host bound on context length */
+  const int32_t* lm_rows;        /* [lm_max] rows that get logits, in order */
+  const int32_t* lm_count;       /* device: number of lm rows */
+  int lm_max;
+} ne_rows;
+
+#define NE_LM_NONE 0     /* final hidden states only (in the workspace) */
+#define NE_LM_ARGMAX 1   /* argmax over the vocabulary per lm row (lowest index on ties) */
+#define NE_LM_LOGITS 2   /* bf16 logits [lm_max, V] into ``logits`` plus the argmax */
+
+/*
+ * The (k+1)-token verify forward: models/qwen3.py:164-178 + compute_logits (:197-203) with
+ * run_cached_attention (models/attention_context.py:66-109) reading 16-token blocks in place.
+ * argmax_out: [lm_max] int32 token ids (may be NULL for NE_LM_NONE / when not needed).
+ */
+NE_API int ne_forward(ne_model* model, const ne_rows* rows, int lm_mode, void* logits, int32_t* argmax_out,
+               void* stream);
+
+/* ---------------------------------------------------------------- device-resident batch state */
+/*
+ * Per-sequence state lives in "sequence slots" s; a step works on batch entries b that name a
+ * slot each (seq_slot[b], -1 = idle). This replaces engine/sequence_state.py:12-57 (token_ids,
+ * num_cached_tokens) and engine/memory/paged_allocator.py:21-79 (block tables) for this path;
+ * the free-block FIFO reproduces engine/memory/block_allocator.py:8-33 (popleft / append).
+ */
+typedef struct {
+  int max_seqs;                  /* sequence slots */
+  int history_stride;            /* int32 per history row (>= max_model_len + k + 1) */
+  int block_table_stride;        /* blocks per sequence row */
+  int num_blocks;                /* blocks in the pool */
+  int32_t* history;              /* [max_seqs, history_stride] prompt + generated token ids */
+  int32_t* seq_len;              /* [max_seqs] tokens in the history (len(token_ids)) */
+  int32_t* num_cached;           /* [max_seqs] num_cached_tokens */
+  int32_t* num_prompt;           /* [max_seqs] */
+  int32_t* max_new_tokens;       /* [max_seqs] */
+  int32_t* flags;                /* [max_seqs] NE_SEQ_* bits */
+  float* temperature;            /* [max_seqs] 0 = greedy */
+  float* top_p;                  /* [max_seqs] */
+  uint64_t* rng_seed;            /* [max_seqs] per-request Philox4x32-10 key */
+  uint64_t* rng_draws;           /* [max_seqs] uniforms consumed so far (Philox counter) */
+  int32_t* block_tables;         /* [max_seqs, block_table_stride] */
+  int32_t* num_blocks_used;      /* [max_seqs] */
+  int32_t* free_ring;            /* [num_blocks] FIFO of free block ids */
+  int64_t* ring_head_tail;       /* [2]: next pop, next push (monotonic) */
+  const int32_t* stop_ids;       /* [num_stop_ids] */
+  int num_stop_ids;
+} ne_batch_state;
+
+#define NE_SEQ_IGNORE_EOS 1
+#define NE_SEQ_FINISHED 2
+
+#define NE_FINISH_NONE 0
+#define NE_FINISH_STOP 1
+#define NE_FINISH_LENGTH 2
+
+/* Outputs of one step per batch entry b (row stride k + 1 in ``tokens``). */
+typedef struct {
+  int32_t* tokens;               /* [num_seqs, k + 1] emitted tokens */
+  int32_t* count;                /* [num_seqs] emitted this step (0 = idle) */
+  int32_t* finish;               /* [num_seqs] NE_FINISH_* */
+  int32_t* proposed;             /* [num_seqs] guesses proposed (len(proposal.token_ids)) */
+  int32_t* accepted;             /* [num_seqs] guesses kept */
+} ne_step_outputs;
+
+/* Initialise the free-block FIFO to 0 .. num_blocks - 1 (BlockAllocator.__init__). */
+NE_API int ne_state_reset_blocks(const ne_batch_state* state, void* stream);
+
+/*
+ * Return every block of the listed slots to the FIFO tail in table order and zero their counts
+ * (PagedSlotAllocator.free, engine/memory/paged_allocator.py:57-59).
+ */
+NE_API int ne_state_free_slots(const ne_batch_state* state, const int32_t* slots, int num_slots, void* stream);
+
+/*
+ * n-gram drafts (NgramProposer.propose, engine/speculative/proposers.py:44-57) for each batch
+ * entry: guess cap max(0, min(k, remaining - 1)) (speculative_generator.py:71-72); the guesses are
+ * written after the history (history[s][seq_len[s] ..]) like proposal tokens appended to
+ * token_ids (speculative_generator.py:75), and their count into draft_len[b] (-1 = idle).
+ */
+NE_API int ne_ngram_propose(const ne_batch_state* state, const int32_t* seq_slot, int num_seqs, int k,
+                     int max_ngram, int min_ngram, int32_t* draft_len, int32_t* status, void* stream);
+
+/*
+ * Prefill of newly admitted sequences (their prompts already in ``history``): reserve blocks,
+ * run the forward over every prompt token, pick the first token (greedy argmax or a sampled one)
+ * and append it. ModelRunner.run_step (engine/generation/model_runner.py:33-50,72-80) after
+ * allocator.reserve (speculative_generator.py:52-53). ``max_rows`` bounds the sum of prompt
+ * lengths; out->tokens has stride k + 1.
+ */
+NE_API int ne_prefill(ne_model* model, const ne_batch_state* state, const int32_t* seq_slot, int num_seqs,
+               int max_rows, int k, const ne_step_outputs* out, void* stream);
+
+/*
+ * One speculative step for every batch entry, entirely on the device:
+ * draft (ne_ngram_propose) -> reserve blocks for the guesses (allocator.reserve) -> (k+1)-token
+ * verify forward -> greedy acceptance (verify_proposal with one-hot drafts, verifier.py:27-60)
+ * or, where temperature > 0, rejection sampling on the per-request uniform stream -> commit:
+ * num_cached = len_before + kept, emitted tokens appended, stop / length finish
+ * (SpeculativeGenerator._run_speculative_step + _generate, speculative_generator.py:50-85).
+ */
+NE_API int ne_spec_step(ne_model* model, const ne_batch_state* state, const int32_t* seq_slot, int num_seqs,
+                 int k, int max_ngram, const ne_step_outputs* out, void* stream);
+
+/* ---------------------------------------------------------------- building blocks (tests) */
+/*
+ * y[m, n] = sum_k x[m, k] w[n, k] on tcgen05 tensor cores, bf16 in, fp32 accumulate, bf16 out
+ * (functional.linear, models/qwen3.py:100-129). x [M, K], w [N, K], y [M, N]; N % 128 == 0,
+ * K % 64 == 0; the three pointers 16-byte aligned.
+ */
+NE_API int ne_gemm_bf16(const void* x, const void* w, void* y, int M, int N, int K, int32_t* status, void* stream);
+
+/*
+ * Paged verify attention (run_cached_attention without the gather, attention_context.py:66-109):
+ * q [rows, nh, 128] bf16 -> out [rows, nh, 128] bf16, causal within each sequence by position,
+ * reading K/V in place through the block table. k_scale/v_scale NULL for a bf16 cache.
+ */
+NE_API int ne_paged_attention(const void* q, void* out, const void* k_cache, const void* v_cache, const void* k_scale,
+                       const void* v_scale, int kv_int8, const ne_rows* rows, int num_heads, int num_kv_heads,
+                       int block_size, long long num_cache_slots, int32_t* status, void* stream);
+
+/* RMSNorm rows (models/qwen3.py:39-44): y = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w). */
+NE_API int ne_rmsnorm(const void* x, const void* w, void* y, int rows, int hidden, float eps, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NESPEC_H */

@@ -1,0 +1,85 @@
+"""Build ``libnespec.so`` (the C-ABI library of include/nespec.h) in-tree for sm_100a.
+
+    python "inference-engine-from-scratch_b200/build.py"      # or __graft_entry__.build()
+
+nvcc compiles every ``csrc/*.cu`` with ``-gencode arch=compute_100a,code=sm_100a`` and links the
+CUDA runtime statically, so the library needs only the NVIDIA driver at run time (it resolves the
+driver's ``cuTensorMapEncodeTiled`` through ``cudaGetDriverEntryPoint``). The build is skipped when
+the library is newer than every source.
+"""
+
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PACKAGE_DIR = Path(__file__).resolve().parent
+REPO = PACKAGE_DIR.parent
+CSRC = PACKAGE_DIR / "csrc"
+INCLUDE = REPO / "include"
+LIBRARY = PACKAGE_DIR / "libnespec.so"
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = [
+    "-O3",
+    "-lineinfo",
+    "-std=c++17",
+    "--expt-relaxed-constexpr",
+    "-Xcompiler",
+    "-fPIC,-fvisibility=hidden",
+    "-Xptxas",
+    "-v",
+]
+
+
+def nvcc_path() -> str:
+    for candidate in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if candidate and Path(candidate).exists():
+            return candidate
+    raise RuntimeError("nvcc not found: the B200 kernels need the CUDA toolkit to build")
+
+
+def sources() -> list[Path]:
+    return sorted(CSRC.glob("*.cu"))
+
+
+def headers() -> list[Path]:
+    return sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
+
+
+def is_stale() -> bool:
+    if not LIBRARY.exists():
+        return True
+    built = LIBRARY.stat().st_mtime
+    return any(p.stat().st_mtime > built for p in sources() + headers())
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    if not force and not is_stale():
+        return LIBRARY
+    nvcc = nvcc_path()
+    objects = []
+    build_dir = PACKAGE_DIR / "_build"
+    build_dir.mkdir(exist_ok=True)
+    for src in sources():
+        obj = build_dir / (src.stem + ".o")
+        cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, f"-I{INCLUDE}", f"-I{CSRC}", "-c", str(src), "-o", str(obj)]
+        proc = subprocess.run(cmd, capture_output=True, text=True)
+        if proc.returncode != 0:
+            raise RuntimeError(f"nvcc failed on {src.name}:\n{proc.stderr}")
+        if verbose:
+            sys.stderr.write(proc.stderr)
+        objects.append(str(obj))
+    tmp = LIBRARY.with_suffix(".so.tmp")
+    cmd = [nvcc, *ARCH_FLAGS, "-shared", "-cudart", "static", "-o", str(tmp), *objects]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        raise RuntimeError(f"nvcc link failed:\n{proc.stderr}")
+    os.replace(tmp, LIBRARY)
+    return LIBRARY
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))

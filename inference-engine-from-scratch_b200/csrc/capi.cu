@@ -1,0 +1,416 @@
+// The C ABI of include/nespec.h: model handle, workspace binding, the forward orchestration and
+// the speculative step. Host code only; every kernel lives in gemm_tc.cu / kernels.cu.
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "gemm_tc.cuh"
+#include "kernels.cuh"
+
+using ne::GemmParams;
+
+struct ne_model {
+  ne_model_config cfg;
+  std::vector<ne_layer_weights> layers;
+  std::vector<CUtensorMap> tm_qkv, tm_o, tm_gateup, tm_down;
+  std::vector<char> layer_set;
+  ne_head_weights head{};
+  CUtensorMap tm_lm{};
+  bool head_set = false;
+  // workspace
+  char* ws = nullptr;
+  size_t ws_bytes = 0;
+  int max_rows = 0, max_seqs = 0;
+  int32_t* status = nullptr;
+  __nv_bfloat16 *h = nullptr, *x = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
+  unsigned long long* keys = nullptr;
+  ne::RowBuffers rb{};
+  CUtensorMap tm_x{}, tm_attn{}, tm_act{};
+  int num_sms = 148;
+};
+
+namespace {
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+struct Layout {
+  size_t status, h, x, q, attn, act, keys, rows_i32, seqs_i32, scalars, total;
+};
+
+Layout workspace_layout(const ne_model_config& c, int R, int B) {
+  Layout l{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = off;
+    off = align256(off + bytes);
+    return at;
+  };
+  const size_t qsz = (size_t)c.num_heads * c.head_dim;
+  l.status = take(64);
+  l.h = take((size_t)R * c.hidden_size * 2);
+  l.x = take((size_t)R * c.hidden_size * 2);
+  l.q = take((size_t)R * qsz * 2);
+  l.attn = take((size_t)R * qsz * 2);
+  l.act = take((size_t)R * c.intermediate_size * 2);
+  l.keys = take((size_t)R * 8);
+  l.rows_i32 = take((size_t)R * 4 * 4);   // token_ids, positions, slot_mapping, lm_rows
+  l.seqs_i32 = take((size_t)B * 4 * 4);   // q_start, q_len, lm_start, draft_len
+  l.scalars = take(64);                   // num_rows, lm_count
+  l.total = off;
+  return l;
+}
+
+cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+int run_gemm(ne_model* m, const CUtensorMap* tw, const CUtensorMap* tx, int M_max, const int32_t* M_dev, int N, int K,
+             const ne::Epilogue& epi, cudaStream_t stream) {
+  GemmParams p{};
+  p.M_max = M_max;
+  p.M_dev = M_dev;
+  p.N = N;
+  p.K = K;
+  p.status = m->status;
+  p.epi = epi;
+  int rc = ne::gemm_plan(p, m->num_sms);
+  if (rc != NE_OK) return rc;
+  return ne::gemm_launch(tw, tx, p, stream);
+}
+
+ne_rows make_step_rows(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int max_rows,
+                       int lm_max) {
+  ne_rows r{};
+  r.max_rows = max_rows;
+  r.num_seqs = num_seqs;
+  r.num_rows = m->rb.num_rows;
+  r.token_ids = m->rb.token_ids;
+  r.positions = m->rb.positions;
+  r.slot_mapping = m->rb.slot_mapping;
+  r.q_start = m->rb.q_start;
+  r.q_len = m->rb.q_len;
+  r.block_tables = st->block_tables;
+  r.table_index = seq_slot;
+  r.block_table_stride = st->block_table_stride;
+  r.max_context = st->history_stride;
+  r.lm_rows = m->rb.lm_rows;
+  r.lm_count = m->rb.lm_count;
+  r.lm_max = lm_max;
+  return r;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ne_abi_version(void) { return NE_ABI_VERSION; }
+
+const char* ne_status_string(int status) {
+  switch (status) {
+    case NE_OK: return "ok";
+    case NE_ERR_INVALID: return "invalid argument, shape or alignment";
+    case NE_ERR_CUDA: return "CUDA runtime error";
+    case NE_ERR_DEVICE: return "a kernel reported an error in the device status word";
+    case NE_ERR_UNSUPPORTED: return "unsupported configuration";
+    case NE_ERR_WORKSPACE: return "workspace too small";
+    default: return "unknown status";
+  }
+}
+
+int ne_read_status(const int32_t* device_status, int clear, int32_t* host_out, void* stream) {
+  if (!device_status || !host_out) return NE_ERR_INVALID;
+  cudaStream_t s = as_stream(stream);
+  if (cudaMemcpyAsync(host_out, device_status, sizeof(int32_t), cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return NE_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return NE_ERR_CUDA;
+  if (clear && cudaMemsetAsync(const_cast<int32_t*>(device_status), 0, sizeof(int32_t), s) != cudaSuccess)
+    return NE_ERR_CUDA;
+  return NE_OK;
+}
+
+int ne_model_create(const ne_model_config* cfg, ne_model** out) {
+  if (!cfg || !out) return NE_ERR_INVALID;
+  const ne_model_config& c = *cfg;
+  if (c.head_dim != 128 || c.block_size != 16 || c.num_kv_heads <= 0 || c.num_heads % c.num_kv_heads ||
+      c.hidden_size % 256 || c.intermediate_size % 64 || c.vocab_size % 128 || c.num_layers <= 0 ||
+      c.num_cache_slots < 2 || c.max_positions <= 0)
+    return NE_ERR_INVALID;
+  if (c.weight_int8) return NE_ERR_UNSUPPORTED;
+  ne_model* m = new (std::nothrow) ne_model();
+  if (!m) return NE_ERR_INVALID;
+  m->cfg = c;
+  m->layers.resize(c.num_layers);
+  m->tm_qkv.resize(c.num_layers);
+  m->tm_o.resize(c.num_layers);
+  m->tm_gateup.resize(c.num_layers);
+  m->tm_down.resize(c.num_layers);
+  m->layer_set.assign(c.num_layers, 0);
+  m->num_sms = sm_count();
+  *out = m;
+  return NE_OK;
+}
+
+int ne_model_destroy(ne_model* m) {
+  delete m;
+  return NE_OK;
+}
+
+int ne_model_set_layer(ne_model* m, int layer, const ne_layer_weights* w) {
+  if (!m || !w || layer < 0 || layer >= m->cfg.num_layers) return NE_ERR_INVALID;
+  const ne_model_config& c = m->cfg;
+  const int H = c.hidden_size, I = c.intermediate_size, qs = c.num_heads * 128, kvs = c.num_kv_heads * 128;
+  if (!w->w_qkv || !w->w_o || !w->w_gateup || !w->w_down || !w->ln_in || !w->ln_post || !w->q_norm || !w->k_norm ||
+      !w->k_cache || !w->v_cache || (c.kv_int8 && (!w->k_scale || !w->v_scale)))
+    return NE_ERR_INVALID;
+  bool ok = ne::make_tmap_bf16(&m->tm_qkv[layer], w->w_qkv, qs + 2 * kvs, H, ne::GEMM_BM, ne::GEMM_BK) &&
+            ne::make_tmap_bf16(&m->tm_o[layer], w->w_o, H, qs, ne::GEMM_BM, ne::GEMM_BK) &&
+            ne::make_tmap_bf16(&m->tm_gateup[layer], w->w_gateup, 2 * I, H, ne::GEMM_BM, ne::GEMM_BK) &&
+            ne::make_tmap_bf16(&m->tm_down[layer], w->w_down, H, I, ne::GEMM_BM, ne::GEMM_BK);
+  if (!ok) return NE_ERR_INVALID;
+  m->layers[layer] = *w;
+  m->layer_set[layer] = 1;
+  return NE_OK;
+}
+
+int ne_model_set_head(ne_model* m, const ne_head_weights* hw) {
+  if (!m || !hw || !hw->embed || !hw->lm_head || !hw->final_norm || !hw->rope_cos || !hw->rope_sin)
+    return NE_ERR_INVALID;
+  if (!ne::make_tmap_bf16(&m->tm_lm, hw->lm_head, m->cfg.vocab_size, m->cfg.hidden_size, ne::GEMM_BM, ne::GEMM_BK))
+    return NE_ERR_INVALID;
+  m->head = *hw;
+  m->head_set = true;
+  return NE_OK;
+}
+
+int ne_model_workspace_bytes(const ne_model* m, int max_rows, int max_seqs, size_t* bytes) {
+  if (!m || !bytes || max_rows <= 0 || max_seqs <= 0 || max_seqs > 1024) return NE_ERR_INVALID;
+  *bytes = workspace_layout(m->cfg, max_rows, max_seqs).total;
+  return NE_OK;
+}
+
+int ne_model_set_workspace(ne_model* m, void* ws, size_t bytes, int max_rows, int max_seqs) {
+  if (!m || !ws || max_rows <= 0 || max_seqs <= 0 || max_seqs > 1024) return NE_ERR_INVALID;
+  if (reinterpret_cast<uintptr_t>(ws) & 255u) return NE_ERR_INVALID;
+  Layout l = workspace_layout(m->cfg, max_rows, max_seqs);
+  if (bytes < l.total) return NE_ERR_WORKSPACE;
+  const ne_model_config& c = m->cfg;
+  char* base = static_cast<char*>(ws);
+  m->ws = base;
+  m->ws_bytes = bytes;
+  m->max_rows = max_rows;
+  m->max_seqs = max_seqs;
+  m->status = reinterpret_cast<int32_t*>(base + l.status);
+  m->h = reinterpret_cast<__nv_bfloat16*>(base + l.h);
+  m->x = reinterpret_cast<__nv_bfloat16*>(base + l.x);
+  m->q = reinterpret_cast<__nv_bfloat16*>(base + l.q);
+  m->attn = reinterpret_cast<__nv_bfloat16*>(base + l.attn);
+  m->act = reinterpret_cast<__nv_bfloat16*>(base + l.act);
+  m->keys = reinterpret_cast<unsigned long long*>(base + l.keys);
+  int32_t* ri = reinterpret_cast<int32_t*>(base + l.rows_i32);
+  m->rb.token_ids = ri;
+  m->rb.positions = ri + max_rows;
+  m->rb.slot_mapping = ri + 2 * max_rows;
+  m->rb.lm_rows = ri + 3 * max_rows;
+  int32_t* si = reinterpret_cast<int32_t*>(base + l.seqs_i32);
+  m->rb.q_start = si;
+  m->rb.q_len = si + max_seqs;
+  m->rb.lm_start = si + 2 * max_seqs;
+  m->rb.draft_len = si + 3 * max_seqs;
+  int32_t* sc = reinterpret_cast<int32_t*>(base + l.scalars);
+  m->rb.num_rows = sc;
+  m->rb.lm_count = sc + 1;
+  const int qs = c.num_heads * 128;
+  bool ok = ne::make_tmap_bf16(&m->tm_x, m->x, max_rows, c.hidden_size, ne::GEMM_XBOX, ne::GEMM_BK) &&
+            ne::make_tmap_bf16(&m->tm_attn, m->attn, max_rows, qs, ne::GEMM_XBOX, ne::GEMM_BK) &&
+            ne::make_tmap_bf16(&m->tm_act, m->act, max_rows, c.intermediate_size, ne::GEMM_XBOX, ne::GEMM_BK);
+  if (!ok) return NE_ERR_INVALID;
+  if (cudaMemset(ws, 0, l.total) != cudaSuccess) return NE_ERR_CUDA;
+  return NE_OK;
+}
+
+int32_t* ne_model_status_word(ne_model* m) { return m ? m->status : nullptr; }
+
+int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int32_t* argmax_out, void* stream) {
+  if (!m || !rows || !m->ws || !m->head_set) return NE_ERR_INVALID;
+  for (char set : m->layer_set)
+    if (!set) return NE_ERR_INVALID;
+  const ne_model_config& c = m->cfg;
+  const int R = rows->max_rows;
+  if (R <= 0 || R > m->max_rows || rows->lm_max > m->max_rows || rows->num_seqs > m->max_seqs) return NE_ERR_WORKSPACE;
+  if (lm_mode == NE_LM_LOGITS && !logits) return NE_ERR_INVALID;
+  cudaStream_t s = as_stream(stream);
+  const int H = c.hidden_size, I = c.intermediate_size, qs = c.num_heads * 128, kvs = c.num_kv_heads * 128;
+  const __nv_bfloat16* embed = static_cast<const __nv_bfloat16*>(m->head.embed);
+  int rc = ne::launch_embed(embed, rows->token_ids, rows->num_rows, R, H, c.vocab_size, m->h, m->status, s);
+  if (rc) return rc;
+  for (int l = 0; l < c.num_layers; ++l) {
+    const ne_layer_weights& w = m->layers[l];
+    rc = ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(w.ln_in), m->x, R, rows->num_rows, nullptr, H,
+                            c.rms_norm_eps, nullptr, s);
+    if (rc) return rc;
+    ne::Epilogue e{};
+    e.mode = ne::EPI_QKV;
+    e.status = m->status;
+    e.n_q_heads = c.num_heads;
+    e.n_kv_heads = c.num_kv_heads;
+    e.eps = c.rms_norm_eps;
+    e.q_norm_w = static_cast<const __nv_bfloat16*>(w.q_norm);
+    e.k_norm_w = static_cast<const __nv_bfloat16*>(w.k_norm);
+    e.rope_cos = static_cast<const __nv_bfloat16*>(m->head.rope_cos);
+    e.rope_sin = static_cast<const __nv_bfloat16*>(m->head.rope_sin);
+    e.max_positions = c.max_positions;
+    e.positions = rows->positions;
+    e.slot_mapping = rows->slot_mapping;
+    e.q_out = m->q;
+    e.k_cache = w.k_cache;
+    e.v_cache = w.v_cache;
+    e.k_scale = static_cast<__nv_bfloat16*>(w.k_scale);
+    e.v_scale = static_cast<__nv_bfloat16*>(w.v_scale);
+    e.kv_int8 = c.kv_int8;
+    e.num_cache_slots = c.num_cache_slots;
+    rc = run_gemm(m, &m->tm_qkv[l], &m->tm_x, R, rows->num_rows, qs + 2 * kvs, H, e, s);
+    if (rc) return rc;
+    rc = ne::launch_attention(m->q, m->attn, w.k_cache, w.v_cache, static_cast<const __nv_bfloat16*>(w.k_scale),
+                              static_cast<const __nv_bfloat16*>(w.v_scale), c.kv_int8, *rows, c.num_heads,
+                              c.num_kv_heads, c.block_size, c.num_cache_slots, m->status, s);
+    if (rc) return rc;
+    ne::Epilogue eo{};
+    eo.mode = ne::EPI_RESIDUAL;
+    eo.status = m->status;
+    eo.out = m->h;
+    eo.ldo = H;
+    rc = run_gemm(m, &m->tm_o[l], &m->tm_attn, R, rows->num_rows, H, qs, eo, s);
+    if (rc) return rc;
+    rc = ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(w.ln_post), m->x, R, rows->num_rows, nullptr, H,
+                            c.rms_norm_eps, nullptr, s);
+    if (rc) return rc;
+    ne::Epilogue eg{};
+    eg.mode = ne::EPI_SWIGLU;
+    eg.status = m->status;
+    eg.out = m->act;
+    eg.ldo = I;
+    rc = run_gemm(m, &m->tm_gateup[l], &m->tm_x, R, rows->num_rows, 2 * I, H, eg, s);
+    if (rc) return rc;
+    ne::Epilogue ed{};
+    ed.mode = ne::EPI_RESIDUAL;
+    ed.status = m->status;
+    ed.out = m->h;
+    ed.ldo = H;
+    rc = run_gemm(m, &m->tm_down[l], &m->tm_act, R, rows->num_rows, H, I, ed, s);
+    if (rc) return rc;
+  }
+  // final norm over the rows that get logits (gathered to the front of x), keys cleared
+  const int lm_max = rows->lm_max;
+  rc = ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(m->head.final_norm), m->x, lm_max, rows->lm_count,
+                          rows->lm_rows, H, c.rms_norm_eps, m->keys, s);
+  if (rc) return rc;
+  if (lm_mode == NE_LM_NONE) return NE_OK;
+  ne::Epilogue el{};
+  el.mode = lm_mode == NE_LM_LOGITS ? ne::EPI_LOGITS : ne::EPI_ARGMAX;
+  el.status = m->status;
+  el.out = static_cast<__nv_bfloat16*>(logits);
+  el.ldo = c.vocab_size;
+  el.argmax_keys = m->keys;
+  rc = run_gemm(m, &m->tm_lm, &m->tm_x, lm_max, rows->lm_count, c.vocab_size, H, el, s);
+  if (rc) return rc;
+  if (argmax_out) rc = ne::launch_keys_to_ids(m->keys, rows->lm_count, lm_max, argmax_out, s);
+  return rc;
+}
+
+int ne_state_reset_blocks(const ne_batch_state* st, void* stream) {
+  if (!st || !st->free_ring || !st->ring_head_tail || st->num_blocks <= 0) return NE_ERR_INVALID;
+  return ne::launch_reset_blocks(*st, as_stream(stream));
+}
+
+int ne_state_free_slots(const ne_batch_state* st, const int32_t* slots, int num_slots, void* stream) {
+  if (!st || (num_slots > 0 && !slots)) return NE_ERR_INVALID;
+  return ne::launch_free_slots(*st, slots, num_slots, as_stream(stream));
+}
+
+int ne_ngram_propose(const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int k, int max_ngram,
+                     int min_ngram, int32_t* draft_len, int32_t* status, void* stream) {
+  if (!st || !seq_slot || !draft_len) return NE_ERR_INVALID;
+  return ne::launch_ngram(*st, seq_slot, num_seqs, k, max_ngram, min_ngram, draft_len, status, as_stream(stream));
+}
+
+int ne_prefill(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int max_rows, int k,
+               const ne_step_outputs* out, void* stream) {
+  if (!m || !st || !seq_slot || !out || num_seqs <= 0 || k < 1) return NE_ERR_INVALID;
+  if (max_rows > m->max_rows || num_seqs > m->max_seqs) return NE_ERR_WORKSPACE;
+  cudaStream_t s = as_stream(stream);
+  int rc = ne::launch_plan(*st, seq_slot, num_seqs, ne::PLAN_PREFILL, max_rows, m->cfg.block_size,
+                           m->cfg.num_cache_slots, m->rb, m->status, s);
+  if (rc) return rc;
+  ne_rows rows = make_step_rows(m, st, seq_slot, num_seqs, max_rows, num_seqs);
+  rc = ne_forward(m, &rows, NE_LM_ARGMAX, nullptr, nullptr, stream);
+  if (rc) return rc;
+  return ne::launch_accept_greedy(*st, seq_slot, num_seqs, k, ne::PLAN_PREFILL, m->rb, m->keys, *out, m->status, s);
+}
+
+int ne_spec_step(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int k, int max_ngram,
+                 const ne_step_outputs* out, void* stream) {
+  if (!m || !st || !seq_slot || !out || num_seqs <= 0 || k < 1 || max_ngram < 1) return NE_ERR_INVALID;
+  const int max_rows = num_seqs * (k + 1);
+  if (max_rows > m->max_rows || num_seqs > m->max_seqs) return NE_ERR_WORKSPACE;
+  cudaStream_t s = as_stream(stream);
+  int rc = ne::launch_ngram(*st, seq_slot, num_seqs, k, max_ngram, 1, m->rb.draft_len, m->status, s);
+  if (rc) return rc;
+  rc = ne::launch_plan(*st, seq_slot, num_seqs, ne::PLAN_SPEC, max_rows, m->cfg.block_size, m->cfg.num_cache_slots,
+                       m->rb, m->status, s);
+  if (rc) return rc;
+  ne_rows rows = make_step_rows(m, st, seq_slot, num_seqs, max_rows, max_rows);
+  rc = ne_forward(m, &rows, NE_LM_ARGMAX, nullptr, nullptr, stream);
+  if (rc) return rc;
+  return ne::launch_accept_greedy(*st, seq_slot, num_seqs, k, ne::PLAN_SPEC, m->rb, m->keys, *out, m->status, s);
+}
+
+int ne_gemm_bf16(const void* x, const void* w, void* y, int M, int N, int K, int32_t* status, void* stream) {
+  if (!x || !w || !y || M <= 0 || N % ne::GEMM_BM || K % ne::GEMM_BK || !aligned16(x) || !aligned16(w) ||
+      !aligned16(y))
+    return NE_ERR_INVALID;
+  CUtensorMap tw, tx;
+  if (!ne::make_tmap_bf16(&tw, w, N, K, ne::GEMM_BM, ne::GEMM_BK) ||
+      !ne::make_tmap_bf16(&tx, x, M, K, ne::GEMM_XBOX, ne::GEMM_BK))
+    return NE_ERR_INVALID;
+  GemmParams p{};
+  p.M_max = M;
+  p.N = N;
+  p.K = K;
+  p.status = status;
+  p.epi.mode = ne::EPI_STORE;
+  p.epi.status = status;
+  p.epi.out = static_cast<__nv_bfloat16*>(y);
+  p.epi.ldo = N;
+  int rc = ne::gemm_plan(p, sm_count());
+  if (rc) return rc;
+  return ne::gemm_launch(&tw, &tx, p, as_stream(stream));
+}
+
+int ne_paged_attention(const void* q, void* out, const void* k_cache, const void* v_cache, const void* k_scale,
+                       const void* v_scale, int kv_int8, const ne_rows* rows, int num_heads, int num_kv_heads,
+                       int block_size, long long num_cache_slots, int32_t* status, void* stream) {
+  if (!q || !out || !k_cache || !v_cache || !rows || (kv_int8 && (!k_scale || !v_scale)) || num_cache_slots < 2)
+    return NE_ERR_INVALID;
+  const long long slots = num_cache_slots;
+  return ne::launch_attention(static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(out), k_cache,
+                              v_cache, static_cast<const __nv_bfloat16*>(k_scale),
+                              static_cast<const __nv_bfloat16*>(v_scale), kv_int8, *rows, num_heads, num_kv_heads,
+                              block_size, slots, status, as_stream(stream));
+}
+
+int ne_rmsnorm(const void* x, const void* w, void* y, int rows, int hidden, float eps, void* stream) {
+  if (!x || !w || !y || rows < 0) return NE_ERR_INVALID;
+  return ne::launch_rmsnorm(static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),
+                            static_cast<__nv_bfloat16*>(y), rows, nullptr, nullptr, hidden, eps, nullptr,
+                            as_stream(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,441 @@
+// tcgen05 / TMEM GEMM kernel with the fused epilogues of the verify forward (see gemm_tc.cuh).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "gemm_tc.cuh"
+
+namespace ne {
+
+namespace {
+
+
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t map_peer(uint32_t local_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    v = other > v ? other : v;
+  }
+  return v;
+}
+
+// Apply the epilogue to ``count`` token rows whose fp32 accumulators sit in shared memory
+// ``acc`` as [count][128]. ``m_begin`` is the global row of acc row 0; ``tile_n`` the N tile.
+__device__ void epilogue_rows(const Epilogue& e, int N, int tile_n, int m_begin, int count, const float* acc) {
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int n0 = tile_n * GEMM_BM;
+  switch (e.mode) {
+    case EPI_STORE:
+      for (int idx = tid; idx < count * GEMM_BM; idx += GEMM_THREADS) {
+        int m = idx >> 7, n = idx & 127;
+        e.out[(long long)(m_begin + m) * e.ldo + n0 + n] = __float2bfloat16_rn(acc[idx]);
+      }
+      break;
+    case EPI_RESIDUAL:
+      for (int idx = tid; idx < count * GEMM_BM; idx += GEMM_THREADS) {
+        int m = idx >> 7, n = idx & 127;
+        __nv_bfloat16* o = e.out + (long long)(m_begin + m) * e.ldo + n0 + n;
+        float y = bf16r(acc[idx]);
+        *o = __float2bfloat16_rn(__bfloat162float(*o) + y);
+      }
+      break;
+    case EPI_SWIGLU:
+      for (int idx = tid; idx < count * 64; idx += GEMM_THREADS) {
+        int m = idx >> 6, j = idx & 63;
+        float g = bf16r(acc[m * GEMM_BM + j]);
+        float u = bf16r(acc[m * GEMM_BM + 64 + j]);
+        float a = bf16r(g / (1.0f + expf(-g)));
+        e.out[(long long)(m_begin + m) * e.ldo + tile_n * 64 + j] = __float2bfloat16_rn(a * u);
+      }
+      break;
+    case EPI_QKV: {
+      const int head = tile_n;
+      const bool is_q = head < e.n_q_heads;
+      const bool is_k = !is_q && head < e.n_q_heads + e.n_kv_heads;
+      for (int m = warp; m < count; m += GEMM_THREADS / 32) {
+        const int row = m_begin + m;
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = bf16r(acc[m * GEMM_BM + lane + 32 * i]);
+        if (is_q || is_k) {
+          float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
+          float r = 1.0f / sqrtf(ss / 128.0f + e.eps);
+          const __nv_bfloat16* w = is_q ? e.q_norm_w : e.k_norm_w;
+          float nv[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) nv[i] = bf16r(bf16r(v[i] * r) * ld_bf16(w + lane + 32 * i));
+          int pos = e.positions[row];
+          pos = pos < 0 ? 0 : (pos >= e.max_positions ? e.max_positions - 1 : pos);
+          const __nv_bfloat16* cs = e.rope_cos + (long long)pos * 128;
+          const __nv_bfloat16* sn = e.rope_sin + (long long)pos * 128;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            int d = lane + 32 * i;
+            float rot = i < 2 ? -nv[i + 2] : nv[i - 2];
+            v[i] = bf16r(bf16r(nv[i] * ld_bf16(cs + d)) + bf16r(rot * ld_bf16(sn + d)));
+          }
+        }
+        if (is_q) {
+          __nv_bfloat16* q = e.q_out + (long long)row * (e.n_q_heads * 128) + head * 128;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) q[lane + 32 * i] = __float2bfloat16_rn(v[i]);
+        } else {
+          const int kvh = is_k ? head - e.n_q_heads : head - e.n_q_heads - e.n_kv_heads;
+          long long slot = e.slot_mapping[row];
+          if (slot < 0 || slot >= e.num_cache_slots) {
+            if (lane == 0) report(e.status, NE_DEV_BAD_SLOT);
+            continue;
+          }
+          long long base = (slot * e.n_kv_heads + kvh) * 128;
+          if (!e.kv_int8) {
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(is_k ? e.k_cache : e.v_cache) + base;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2bfloat16_rn(v[i]);
+          } else {
+            // models/int8_quantization.py:30-34: scale = max|x| / 127 in fp32 (clamped), stored in
+            // the model dtype; q = round(x / scale) clamped to +-127.
+            float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+            float scale = fmaxf(amax, 1e-8f) / 127.0f;
+            int8_t* dst = reinterpret_cast<int8_t*>(is_k ? e.k_cache : e.v_cache) + base;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              float q = rintf(v[i] / scale);
+              q = fminf(fmaxf(q, -127.0f), 127.0f);
+              dst[lane + 32 * i] = (int8_t)q;
+            }
+            if (lane == 0) {
+              __nv_bfloat16* sdst = is_k ? e.k_scale : e.v_scale;
+              sdst[slot * e.n_kv_heads + kvh] = __float2bfloat16_rn(scale);
+            }
+          }
+        }
+      }
+      break;
+    }
+    case EPI_ARGMAX:
+    case EPI_LOGITS: {
+      for (int m = warp; m < count; m += GEMM_THREADS / 32) {
+        const int row = m_begin + m;
+        unsigned long long best = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          int n = lane + 32 * i;
+          float y = bf16r(acc[m * GEMM_BM + n]);
+          if (e.mode == EPI_LOGITS) e.out[(long long)row * e.ldo + n0 + n] = __float2bfloat16_rn(y);
+          unsigned long long key = argmax_key(y, (uint32_t)(n0 + n));
+          best = key > best ? key : best;
+        }
+        best = warp_max_u64(best);
+        if (lane == 0 && e.argmax_keys) atomicMax(e.argmax_keys + row, best);
+      }
+      break;
+    }
+    default:
+      break;
+  }
+  (void)N;
+}
+
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                   const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int split = blockIdx.x;
+  const int S = p.splits;
+  const int tile_n = blockIdx.y;
+  const int m0 = blockIdx.z * p.t_block;
+
+  const int M = p.M_dev ? min(*p.M_dev, p.M_max) : p.M_max;
+  const int t_actual = min(p.t_block, M - m0);
+  if (t_actual <= 0) return;  // the whole cluster shares this m-block: all CTAs leave together
+
+  const int n_loads = (t_actual + GEMM_XBOX - 1) / GEMM_XBOX;
+  const int n_pad = (t_actual + 15) & ~15;
+  const int part0 = n_pad < 256 ? n_pad : 256;
+  const int part1 = n_pad - part0;
+  const int num_chunks = p.K / GEMM_BK;
+  const int cps = (num_chunks + S - 1) / S;
+  const int k_begin = split * cps;
+  const int nk = max(0, min(num_chunks, k_begin + cps) - k_begin);
+
+  const int w_bytes = GEMM_BM * GEMM_BK * 2;                                     // 16 KB
+  const int stage_bytes = w_bytes + ((p.t_block + GEMM_XBOX - 1) / GEMM_XBOX) * GEMM_XBOX * GEMM_BK * 2;
+  const int stages = p.stages;
+  // barriers sit past every region the pipeline or the epilogue staging can touch
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + GEMM_SMEM_DATA_BYTES);
+  uint64_t* empty = full + stages;
+  uint64_t* done = empty + stages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* consumed_slot = const_cast<int*>(reinterpret_cast<volatile int*>(tmem_slot + 2));
+
+  const uint32_t tmem_cols = p.t_block <= 32 ? 32 : p.t_block <= 64 ? 64 : p.t_block <= 128 ? 128
+                             : p.t_block <= 256 ? 256 : 512;
+
+  if (tid == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    *consumed_slot = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_x);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  int issued = 0;
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t tx = (uint32_t)(w_bytes + n_loads * GEMM_XBOX * GEMM_BK * 2);
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % stages;
+        const uint32_t round = (uint32_t)(i / stages);
+        if (!mbar_wait(&empty[s], (round & 1u) ^ 1u, abort_flag, p.status)) break;
+        uint8_t* st = smem + s * stage_bytes;
+        mbar_arrive_expect_tx(&full[s], tx);
+        const int kx = (k_begin + i) * GEMM_BK;
+        tma_load_2d(st, &tm_w, &full[s], kx, tile_n * GEMM_BM);
+        for (int l = 0; l < n_loads; ++l)
+          tma_load_2d(st + w_bytes + l * GEMM_XBOX * GEMM_BK * 2, &tm_x, &full[s], kx, m0 + l * GEMM_XBOX);
+        issued = i + 1;
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc0 = idesc_bf16_f32(GEMM_BM, part0);
+      const uint32_t idesc1 = part1 > 0 ? idesc_bf16_f32(GEMM_BM, part1) : 0u;
+      int i = 0;
+      for (; i < nk; ++i) {
+        const int s = i % stages;
+        const uint32_t round = (uint32_t)(i / stages);
+        if (!mbar_wait(&full[s], round & 1u, abort_flag, p.status)) break;
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem + s * stage_bytes);
+        const uint32_t b_addr = a_addr + w_bytes;
+#pragma unroll
+        for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+          const uint64_t a_desc = smem_desc_sw128(a_addr + kk * 32);
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          tc_mma_bf16(tmem_base, a_desc, smem_desc_sw128(b_addr + kk * 32), idesc0, acc);
+          if (part1 > 0)
+            tc_mma_bf16(tmem_base + 256, a_desc, smem_desc_sw128(b_addr + 256 * 128 + kk * 32), idesc1, acc);
+        }
+        tc_commit(&empty[s]);
+      }
+      *consumed_slot = i;
+      tc_commit(done);
+    }
+    __syncwarp();
+  }
+
+  // ------------------------------------------------------------------ epilogue
+  bool ok = (nk == 0) || mbar_wait(done, 0, abort_flag, p.status);
+  tc_fence_after();
+  __syncthreads();
+  if (*abort_flag) ok = false;
+
+  float* stage_acc = reinterpret_cast<float*>(smem);  // pipeline smem is free once ``done`` fired
+  const int m_begin = m0;
+  if (S == 1) {
+    for (int c0 = 0; c0 < t_actual; c0 += 128) {
+      const int cnt = min(128, t_actual - c0);
+      for (int c32 = 0; c32 < cnt; c32 += 32) {
+        float v[32];
+        if (ok) {
+          tmem_ld32(tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(c0 + c32), v);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (c32 + i < cnt) stage_acc[(c32 + i) * GEMM_BM + warp * 32 + lane] = v[i];
+      }
+      __syncthreads();
+      if (ok) epilogue_rows(p.epi, p.N, tile_n, m_begin + c0, cnt, stage_acc);
+      __syncthreads();
+    }
+  } else {
+    // park this split's partial tile [t_actual][128], then reduce our token slice over the cluster
+    for (int c32 = 0; c32 < t_actual; c32 += 32) {
+      float v[32];
+      if (ok && nk > 0) {
+        tmem_ld32(tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)c32, v);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (c32 + i < t_actual) stage_acc[(c32 + i) * GEMM_BM + warp * 32 + lane] = v[i];
+    }
+    __syncthreads();
+    cluster_sync_all();
+    const int slice = (t_actual + S - 1) / S;
+    const int s_begin = split * slice;
+    const int s_cnt = max(0, min(slice, t_actual - s_begin));
+    float* red = stage_acc + (size_t)p.t_block * GEMM_BM;
+    const uint32_t local_base = smem_u32(stage_acc);
+    for (int idx = tid; idx < s_cnt * (GEMM_BM / 4); idx += GEMM_THREADS) {
+      const int m = idx / (GEMM_BM / 4);
+      const int n4 = idx % (GEMM_BM / 4);
+      const uint32_t off = (uint32_t)(((s_begin + m) * GEMM_BM + n4 * 4) * 4);
+      float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int r = 0; r < S; ++r) {
+        float4 v = ld_cluster_f4(map_peer(local_base + off, (uint32_t)r));
+        sum.x += v.x;
+        sum.y += v.y;
+        sum.z += v.z;
+        sum.w += v.w;
+      }
+      reinterpret_cast<float4*>(red)[m * (GEMM_BM / 4) + n4] = sum;
+    }
+    __syncthreads();
+    if (ok && s_cnt > 0) epilogue_rows(p.epi, p.N, tile_n, m_begin + s_begin, s_cnt, red);
+    __syncthreads();
+    cluster_sync_all();  // peers may still be reading our partial tile
+  }
+
+  // ------------------------------------------------------------------ teardown
+  if (!ok && warp == 0 && lane == 0) {
+    // drain our own TMA copies still in flight (bounded) before the shared memory goes away
+    const int consumed = *consumed_slot;
+    for (int i = consumed; i < issued; ++i) mbar_wait(&full[i % stages], (uint32_t)(i / stages) & 1u, nullptr, p.status);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, tmem_cols);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+}  // namespace
+
+bool make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+                    uint32_t box_cols) {
+  auto encode = get_encode_fn();
+  if (!encode || !base || (reinterpret_cast<uintptr_t>(base) & 15u) || (cols * 2) % 16 != 0) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estrides[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                      estrides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Choose tokens per CTA, split-K (cluster size) and pipeline depth for an [M_max, K] x [N, K]^T GEMM.
+int gemm_plan(GemmParams& p, int num_sms) {
+  if (p.N % GEMM_BM || p.K % GEMM_BK || p.M_max <= 0) return NE_ERR_INVALID;
+  const int num_chunks = p.K / GEMM_BK;
+  const int n_tiles = p.N / GEMM_BM;
+  const int avail = GEMM_SMEM_DATA_BYTES;
+  int t_block = p.M_max <= GEMM_MAX_TOKENS ? ((p.M_max + 15) & ~15) : 256;
+  int m_blocks = (p.M_max + t_block - 1) / t_block;
+  int S = std::max(1, std::min(GEMM_MAX_SPLITS, num_sms / std::max(1, n_tiles * m_blocks)));
+  if (p.epi.mode == EPI_ARGMAX || p.epi.mode == EPI_LOGITS) S = 1;
+  auto fits = [&](int s, int tb) {
+    if (s == 1) return 128 * GEMM_BM * 4 <= avail;
+    int slice = (tb + s - 1) / s;
+    return (tb + slice) * GEMM_BM * 4 <= avail;
+  };
+  while (S > 1) {
+    int cps = (num_chunks + S - 1) / S;
+    bool every_split_has_work = cps * (S - 1) < num_chunks;
+    if (every_split_has_work && fits(S, t_block)) break;
+    --S;
+  }
+  if (S > 1 && !fits(S, t_block)) S = 1;
+  const int stage_bytes = GEMM_BM * GEMM_BK * 2 + ((t_block + GEMM_XBOX - 1) / GEMM_XBOX) * GEMM_XBOX * GEMM_BK * 2;
+  int stages = std::min(8, avail / stage_bytes);
+  if (stages < 2) return NE_ERR_INVALID;
+  p.t_block = t_block;
+  p.splits = S;
+  p.stages = stages;
+  return NE_OK;
+}
+
+int gemm_launch(const CUtensorMap* tm_w, const CUtensorMap* tm_x, const GemmParams& p, cudaStream_t stream) {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess) return NE_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.splits, p.N / GEMM_BM, (p.M_max + p.t_block - 1) / p.t_block);
+  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.dynamicSmemBytes = GEMM_SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = p.splits;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
+  cudaError_t err = cudaLaunchKernelEx(&cfg, gemm_tc_kernel, *tm_w, *tm_x, p);
+  return err == cudaSuccess ? NE_OK : NE_ERR_CUDA;
+}
+
+}  // namespace ne

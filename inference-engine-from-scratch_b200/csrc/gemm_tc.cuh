@@ -1,0 +1,87 @@
+// tcgen05 / TMEM GEMM for the verify forward: Y[m, n] = sum_k X[m, k] * W[n, k].
+//
+// Swap-AB: the weight matrix W [N, K] (row-major, K contiguous) is the MMA's A operand, so its
+// rows fill the 128-row M dimension of tcgen05.mma; the token rows X [M, K] are the B operand on
+// the MMA's N dimension (16..256 per instruction, two instructions for up to 512 tokens). Both
+// operands are K-major, staged by TMA with the 128-byte swizzle, 64 K-elements per stage.
+//
+// Split-K runs inside a thread-block cluster: the S CTAs of a cluster take disjoint K ranges of
+// the same 128 x T output tile, park their fp32 partial tiles in shared memory, and after a
+// cluster barrier each CTA sums the S partials of its own token slice (in split order, so the
+// result is deterministic) by reading its peers' shared memory (DSMEM). No global scratch.
+//
+// Roles (128 threads): warp 0 lane 0 issues TMA, warp 1 lane 0 issues tcgen05.mma, warp 2 owns
+// the TMEM allocation; all four warps run the epilogue (warp w reads TMEM lanes 32w..32w+31).
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace ne {
+
+constexpr int GEMM_BM = 128;         // weight rows per tile (MMA M)
+constexpr int GEMM_BK = 64;          // K elements per stage (128 bytes of bf16)
+constexpr int GEMM_XBOX = 64;        // token rows per X TMA box
+constexpr int GEMM_THREADS = 128;
+constexpr int GEMM_MAX_TOKENS = 512; // tokens per CTA (TMEM columns)
+constexpr int GEMM_SMEM_BYTES = 227 * 1024;
+// data region (pipeline stages, later the epilogue staging); then 256 B of barriers; the rest is
+// the slack that aligns the dynamic shared memory base to 1024 B
+constexpr int GEMM_SMEM_DATA_BYTES = GEMM_SMEM_BYTES - 1024 - 256;
+constexpr int GEMM_MAX_SPLITS = 8;   // portable cluster size
+
+enum EpilogueMode : int {
+  EPI_STORE = 0,     // out[m, n] = bf16(y)
+  EPI_RESIDUAL = 1,  // out[m, n] = bf16(out[m, n] + bf16(y))   (residual stream update)
+  EPI_SWIGLU = 2,    // tile = 64 gate rows + 64 up rows: out[m, j] = bf16(bf16(silu(g)) * u)
+  EPI_QKV = 3,       // q/k RMSNorm + RoPE, q -> q_out, k/v -> paged KV cache at slot_mapping
+  EPI_ARGMAX = 4,    // per-row max over the vocab tile into a 64-bit atomicMax key
+  EPI_LOGITS = 5,    // out[m, n] = bf16(y) (vocab row width) plus the argmax key
+};
+
+struct Epilogue {
+  int mode;
+  int* status;                    // device status word (bad slot reports)
+  __nv_bfloat16* out;
+  long long ldo;
+  // EPI_QKV
+  int n_q_heads;
+  int n_kv_heads;
+  float eps;
+  const __nv_bfloat16* q_norm_w;
+  const __nv_bfloat16* k_norm_w;
+  const __nv_bfloat16* rope_cos;  // [max_positions, 128]
+  const __nv_bfloat16* rope_sin;
+  int max_positions;
+  const int32_t* positions;       // [M]
+  const int32_t* slot_mapping;    // [M]
+  __nv_bfloat16* q_out;           // [M, n_q_heads * 128]
+  void* k_cache;                  // [slots + 1, n_kv_heads, 128] bf16 or int8
+  void* v_cache;
+  __nv_bfloat16* k_scale;         // int8 cache: [slots + 1, n_kv_heads]
+  __nv_bfloat16* v_scale;
+  int kv_int8;
+  long long num_cache_slots;      // slots + 1 (the scratch slot included)
+  // EPI_ARGMAX / EPI_LOGITS
+  unsigned long long* argmax_keys;  // [M]
+};
+
+struct GemmParams {
+  int M_max;             // rows of the X tensor map / upper bound of M
+  const int32_t* M_dev;  // device row count (nullptr: M_max)
+  int N, K;
+  int t_block;           // tokens per CTA (<= 512; <= 256 when splits > 1)
+  int splits;            // cluster size along K
+  int stages;
+  int* status;
+  Epilogue epi;
+};
+
+// Host side: build the params / launch (gemm_tc.cu).
+int gemm_launch(const CUtensorMap* tm_w, const CUtensorMap* tm_x, const GemmParams& p, cudaStream_t stream);
+int gemm_plan(GemmParams& p, int num_sms);
+bool make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+                    uint32_t box_cols);
+
+}  // namespace ne

@@ -1,0 +1,576 @@
+// Non-GEMM kernels of the speculative step: embedding gather, RMSNorm, paged verify attention,
+// n-gram drafting, step planning (block reservation + row metadata), greedy acceptance + commit,
+// and the device-side free-block FIFO.
+#include "kernels.cuh"
+
+namespace ne {
+
+namespace {
+
+#define kNegInf (-__int_as_float(0x7f800000))
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  return v;
+}
+
+// ------------------------------------------------------------------ embedding (models/qwen3.py:167)
+__global__ void embed_kernel(const __nv_bfloat16* __restrict__ embed, const int32_t* __restrict__ tokens,
+                             const int32_t* num_rows, int max_rows, int hidden, int vocab,
+                             __nv_bfloat16* __restrict__ out, int* status) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n = num_rows ? min(*num_rows, max_rows) : max_rows;
+  if (warp >= n) return;
+  int tok = tokens[warp];
+  if (tok < 0 || tok >= vocab) {
+    if (lane == 0) report(status, NE_DEV_BAD_TOKEN);
+    tok = 0;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(embed + (long long)tok * hidden);
+  uint4* dst = reinterpret_cast<uint4*>(out + (long long)warp * hidden);
+  for (int i = lane; i < hidden / 8; i += 32) dst[i] = src[i];
+}
+
+// ------------------------------------------------------------------ RMSNorm (models/qwen3.py:39-44)
+// fp32 mean of squares, x * rsqrt(var + eps) cast back to bf16, then times the bf16 weight.
+__global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                               __nv_bfloat16* __restrict__ y, int max_rows, const int32_t* rows_dev,
+                               const int32_t* gather, int hidden, float eps, unsigned long long* zero_keys) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int n = rows_dev ? min(*rows_dev, max_rows) : max_rows;
+  if (row >= n) return;
+  const int src = gather ? gather[row] : row;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (long long)src * hidden);
+  float ss = 0.f;
+  for (int i = lane; i < hidden / 8; i += 32) {
+    uint4 u = xr[i];
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float f = __bfloat162float(e[j]);
+      ss += f * f;
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = 1.0f / sqrtf(ss / (float)hidden + eps);
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  uint4* yr = reinterpret_cast<uint4*>(y + (long long)row * hidden);
+  for (int i = lane; i < hidden / 8; i += 32) {
+    uint4 u = xr[i], wv = wr[i], o;
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+    const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+    __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) oe[j] = __float2bfloat16_rn(bf16r(__bfloat162float(e[j]) * r) * __bfloat162float(we[j]));
+    yr[i] = o;
+  }
+  if (zero_keys && lane == 0) zero_keys[row] = 0ull;
+}
+
+// ------------------------------------------------------------------ paged verify attention
+// One CTA per (batch entry, KV head). Query vectors of the entry's rows x the KV head's query-head
+// group go in tiles of 16; keys/values stream block by block straight from the paged pool through
+// the block table (no gathered copy), with an online softmax in fp32.
+constexpr int ATT_THREADS = 128;
+constexpr int ATT_QT = 16;
+constexpr int ATT_D = 128;
+constexpr float ATT_SCALE = 0.08838834764831845f;  // 1 / sqrt(128)
+
+__global__ void __launch_bounds__(ATT_THREADS)
+    paged_attention_kernel(const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out,
+                           const void* __restrict__ k_cache, const void* __restrict__ v_cache,
+                           const __nv_bfloat16* __restrict__ k_scale, const __nv_bfloat16* __restrict__ v_scale,
+                           int kv_int8, ne_rows rows, int nh, int nkv, int bs, long long num_cache_slots,
+                           int* status) {
+  const int b = blockIdx.x;
+  const int h = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int ql = rows.q_len[b];
+  if (ql <= 0) return;
+  const int r0 = rows.q_start[b];
+  const int G = nh / nkv;
+  const int trow = rows.table_index ? rows.table_index[b] : b;
+  const int32_t* table = rows.block_tables + (long long)trow * rows.block_table_stride;
+
+  __shared__ float sq[ATT_QT][ATT_D];
+  __shared__ float sk[16][ATT_D + 1];
+  __shared__ float sv[16][ATT_D];
+  __shared__ float sp[ATT_QT][17];
+  __shared__ int spos[ATT_QT];
+  __shared__ float sm[ATT_QT], sl[ATT_QT], scorr[ATT_QT];
+
+  const int nvec = ql * G;
+  for (int vt = 0; vt < nvec; vt += ATT_QT) {
+    const int nv = min(ATT_QT, nvec - vt);
+    for (int idx = tid; idx < ATT_QT * ATT_D; idx += ATT_THREADS) {
+      const int v = idx / ATT_D, d = idx % ATT_D;
+      float val = 0.f;
+      if (v < nv) {
+        const int row = r0 + (vt + v) / G;
+        const int head = h * G + (vt + v) % G;
+        val = __bfloat162float(q[((long long)row * nh + head) * ATT_D + d]);
+      }
+      sq[v][d] = val;
+    }
+    if (tid < ATT_QT) {
+      spos[tid] = tid < nv ? rows.positions[r0 + (vt + tid) / G] : -1;
+      sm[tid] = kNegInf;
+      sl[tid] = 0.f;
+    }
+    float acc[ATT_QT];
+#pragma unroll
+    for (int v = 0; v < ATT_QT; ++v) acc[v] = 0.f;
+    __syncthreads();
+    int ctx_end = 0;
+    for (int v = 0; v < nv; ++v) ctx_end = max(ctx_end, spos[v] + 1);
+    const int nblk = (ctx_end + bs - 1) / bs;
+    for (int kb = 0; kb < nblk; ++kb) {
+      bool valid = kb < rows.block_table_stride;
+      long long blk = valid ? table[kb] : -1;
+      valid = valid && blk >= 0 && (blk + 1) * bs <= num_cache_slots - 1;
+      if (!valid && tid == 0) report(status, NE_DEV_BAD_SLOT);
+      for (int idx = tid; idx < 16 * ATT_D; idx += ATT_THREADS) {
+        const int t = idx / ATT_D, d = idx % ATT_D;
+        float kv = 0.f, vv = 0.f;
+        if (valid && t < bs) {
+          const long long slot = blk * bs + t;
+          const long long off = (slot * nkv + h) * ATT_D + d;
+          if (!kv_int8) {
+            kv = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(k_cache)[off]);
+            vv = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(v_cache)[off]);
+          } else {
+            // read_from_cache (attention_context.py:57-63): int8 -> bf16, times the bf16 scale
+            const float ksc = __bfloat162float(k_scale[slot * nkv + h]);
+            const float vsc = __bfloat162float(v_scale[slot * nkv + h]);
+            kv = bf16r((float)reinterpret_cast<const int8_t*>(k_cache)[off] * ksc);
+            vv = bf16r((float)reinterpret_cast<const int8_t*>(v_cache)[off] * vsc);
+          }
+        }
+        sk[t][d] = kv;
+        sv[t][d] = vv;
+      }
+      __syncthreads();
+      for (int p = tid; p < ATT_QT * 16; p += ATT_THREADS) {
+        const int v = p / 16, t = p % 16;
+        float s = kNegInf;
+        if (valid && v < nv && t < bs && kb * bs + t <= spos[v]) {
+          float dot = 0.f;
+#pragma unroll 8
+          for (int d = 0; d < ATT_D; ++d) dot += sq[v][d] * sk[t][d];
+          s = dot * ATT_SCALE;
+        }
+        sp[v][t] = s;
+      }
+      __syncthreads();
+      for (int v = warp; v < ATT_QT; v += ATT_THREADS / 32) {
+        const float s = lane < 16 ? sp[v][lane] : kNegInf;
+        const float mx = warp_max(s);
+        const float m_old = sm[v];
+        const float m_new = fmaxf(m_old, mx);
+        float p = 0.f, corr = 1.f;
+        if (m_new != kNegInf) {
+          p = s == kNegInf ? 0.f : expf(s - m_new);
+          corr = m_old == kNegInf ? 0.f : expf(m_old - m_new);
+        }
+        const float psum = warp_sum(p);
+        __syncwarp();
+        if (lane < 16) sp[v][lane] = p;
+        if (lane == 0) {
+          sm[v] = m_new;
+          sl[v] = sl[v] * corr + psum;
+          scorr[v] = corr;
+        }
+      }
+      __syncthreads();
+#pragma unroll
+      for (int v = 0; v < ATT_QT; ++v) {
+        float a = acc[v] * scorr[v];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) a += sp[v][t] * sv[t][tid];
+        acc[v] = a;
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int v = 0; v < ATT_QT; ++v) {
+      if (v < nv) {
+        const int row = r0 + (vt + v) / G;
+        const int head = h * G + (vt + v) % G;
+        const float l = sl[v];
+        out[((long long)row * nh + head) * ATT_D + tid] = __float2bfloat16_rn(l > 0.f ? acc[v] / l : 0.f);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void keys_to_ids_kernel(const unsigned long long* keys, const int32_t* count, int max_count,
+                                   int32_t* ids) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int n = count ? min(*count, max_count) : max_count;
+  if (i < n) ids[i] = (int32_t)argmax_key_index(keys[i]);
+}
+
+// ------------------------------------------------------------------ n-gram drafts
+// NgramProposer.propose (engine/speculative/proposers.py:44-57) for one batch entry per CTA:
+// for n = max_ngram .. min_ngram (skipped when len <= n), the most recent earlier occurrence of the
+// last n tokens (largest start in [0, len - n - 1]); the guesses are the (<= cap) tokens after it.
+__global__ void ngram_kernel(ne_batch_state st, const int32_t* __restrict__ seq_slot, int k, int max_ngram,
+                             int min_ngram, int32_t* __restrict__ draft_len, int* status) {
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int s = seq_slot[b];
+  if (s < 0 || s >= st.max_seqs || (st.flags[s] & NE_SEQ_FINISHED)) {
+    if (tid == 0) draft_len[b] = -1;
+    return;
+  }
+  const int L = st.seq_len[s];
+  const int remaining = st.max_new_tokens[s] - (L - st.num_prompt[s]);
+  const int cap = max(0, min(k, remaining - 1));  // speculative_generator.py:71-72
+  if (cap == 0) {
+    if (tid == 0) draft_len[b] = 0;
+    return;
+  }
+  if (L + cap > st.history_stride) {
+    if (tid == 0) {
+      report(status, NE_DEV_HISTORY_FULL);
+      draft_len[b] = 0;
+    }
+    return;
+  }
+  int32_t* hist = st.history + (long long)s * st.history_stride;
+  __shared__ int best;
+  for (int n = max_ngram; n >= min_ngram; --n) {
+    if (L <= n) continue;
+    if (tid == 0) best = -1;
+    __syncthreads();
+    for (int start = L - n - 1 - tid; start >= 0; start -= blockDim.x) {
+      bool match = true;
+      for (int j = 0; j < n && match; ++j) match = hist[start + j] == hist[L - n + j];
+      if (match) {
+        atomicMax(&best, start);
+        break;  // descending: this thread's first match is its most recent one
+      }
+    }
+    __syncthreads();
+    const int found = best;
+    if (found >= 0) {
+      const int follow = found + n;
+      const int g = min(cap, L - follow);
+      for (int j = tid; j < g; j += blockDim.x) hist[L + j] = hist[follow + j];
+      if (tid == 0) draft_len[b] = g;
+      return;
+    }
+    __syncthreads();
+  }
+  if (tid == 0) draft_len[b] = 0;
+}
+
+// ------------------------------------------------------------------ block-wide exclusive scan (<= 1024)
+__device__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(0xFFFFFFFFu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    int w = lane < nw ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xFFFFFFFFu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nw) warp_sums[lane] = w;
+    if (lane == nw - 1) *total = w;
+  }
+  __syncthreads();
+  const int before = warp > 0 ? warp_sums[warp - 1] : 0;
+  const int res = before + x - v;
+  __syncthreads();
+  return res;
+}
+
+// ------------------------------------------------------------------ step planning
+// Per batch entry: rows to score (uncached tokens + guesses), blocks to reserve so the table covers
+// len + guesses tokens (PagedSlotAllocator.reserve, paged_allocator.py:50-55, popped from the FIFO
+// in batch order), and per row the token, position and slot (batch_builder.py:33-53,
+// paged_allocator.py:69-79: slot = table[p // bs] * bs + p % bs).
+__global__ void __launch_bounds__(1024)
+    plan_kernel(ne_batch_state st, const int32_t* __restrict__ seq_slot, int num_seqs, int mode, int max_rows,
+                int bs, long long num_cache_slots, RowBuffers rb, int* status) {
+  __shared__ int warp_sums[32];
+  __shared__ int s_qstart[1024];
+  __shared__ int total_rows, total_need, fail;
+  __shared__ long long head;
+  const int tid = threadIdx.x;
+  int ql = 0, need = 0, s = -1;
+  if (tid < num_seqs) {
+    s = seq_slot[tid];
+    if (s >= 0 && s < st.max_seqs && !(st.flags[s] & NE_SEQ_FINISHED)) {
+      const int g = mode == PLAN_SPEC ? rb.draft_len[tid] : 0;
+      if (g >= 0) {
+        const int cached = st.num_cached[s];
+        ql = st.seq_len[s] - cached + g;
+        const int end = cached + ql;
+        const int blocks = (end + bs - 1) / bs;
+        if (blocks > st.block_table_stride || end > st.history_stride) {
+          report(status, NE_DEV_HISTORY_FULL);
+          ql = 0;
+        } else {
+          need = max(0, blocks - st.num_blocks_used[s]);
+        }
+      }
+    }
+  }
+  const int qstart = block_exclusive_scan(ql, warp_sums, &total_rows);
+  const int noff = block_exclusive_scan(need, warp_sums, &total_need);
+  if (tid == 0) {
+    head = st.ring_head_tail[0];
+    const long long avail = st.ring_head_tail[1] - head;
+    fail = 0;
+    if (total_need > avail) {
+      report(status, NE_DEV_OUT_OF_BLOCKS);
+      fail = 1;
+    }
+    if (total_rows > max_rows) {
+      report(status, NE_DEV_HISTORY_FULL);
+      fail = 1;
+    }
+  }
+  __syncthreads();
+  if (fail) {
+    if (tid < num_seqs) {
+      rb.q_start[tid] = 0;
+      rb.q_len[tid] = 0;
+      rb.lm_start[tid] = 0;
+    }
+    if (tid == 0) {
+      *rb.num_rows = 0;
+      *rb.lm_count = 0;
+    }
+    return;
+  }
+  if (tid < num_seqs) {
+    if (need > 0) {
+      const int used = st.num_blocks_used[s];
+      int32_t* row = st.block_tables + (long long)s * st.block_table_stride;
+      for (int j = 0; j < need; ++j) row[used + j] = st.free_ring[(head + noff + j) % st.num_blocks];
+      st.num_blocks_used[s] = used + need;
+    }
+    rb.q_start[tid] = qstart;
+    rb.q_len[tid] = ql;
+    rb.lm_start[tid] = mode == PLAN_SPEC ? qstart : tid;
+    s_qstart[tid] = qstart;
+    if (mode == PLAN_PREFILL) rb.lm_rows[tid] = ql > 0 ? qstart + ql - 1 : 0;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    st.ring_head_tail[0] = head + total_need;
+    *rb.num_rows = total_rows;
+    *rb.lm_count = mode == PLAN_SPEC ? total_rows : num_seqs;
+  }
+  for (int r = tid; r < total_rows; r += blockDim.x) {
+    int lo = 0, hi = num_seqs - 1;  // last entry with q_start <= r
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_qstart[mid] <= r) lo = mid;
+      else hi = mid - 1;
+    }
+    const int b = lo;
+    const int ss = seq_slot[b];
+    const int pos = st.num_cached[ss] + (r - s_qstart[b]);
+    const int tok = st.history[(long long)ss * st.history_stride + pos];
+    const long long blk = st.block_tables[(long long)ss * st.block_table_stride + pos / bs];
+    long long slot = blk * bs + pos % bs;
+    if (blk < 0 || slot >= num_cache_slots - 1) {
+      report(status, NE_DEV_BAD_SLOT);
+      slot = num_cache_slots - 1;
+    }
+    rb.token_ids[r] = tok;
+    rb.positions[r] = pos;
+    rb.slot_mapping[r] = (int32_t)slot;
+    if (mode == PLAN_SPEC) rb.lm_rows[r] = r;
+  }
+}
+
+// ------------------------------------------------------------------ greedy acceptance + commit
+// verify_proposal with one-hot drafts at temperature 0 (verifier.py:27-60): keep guesses while they
+// equal the target argmax, then add the target's token at the first mismatch (or the bonus);
+// then the commit of speculative_generator.py:81-83 and the emission / finish loop of :54-67.
+__global__ void accept_greedy_kernel(ne_batch_state st, const int32_t* __restrict__ seq_slot, int num_seqs, int k,
+                                     int mode, RowBuffers rb, const unsigned long long* __restrict__ keys,
+                                     ne_step_outputs out, int* status) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= num_seqs) return;
+  const int s = seq_slot[b];
+  const int ql = rb.q_len[b];
+  if (s < 0 || ql <= 0) {
+    out.count[b] = 0;
+    out.finish[b] = NE_FINISH_NONE;
+    out.proposed[b] = 0;
+    out.accepted[b] = 0;
+    return;
+  }
+  const int g = mode == PLAN_SPEC ? max(rb.draft_len[b], 0) : 0;
+  const int L = st.seq_len[s];
+  int32_t* hist = st.history + (long long)s * st.history_stride;
+  const int ls = rb.lm_start[b];
+  int kept = 0;
+  while (kept < g) {
+    const unsigned long long key = keys[ls + kept];
+    if (key == 0ull) report(status, NE_DEV_BAD_TOKEN);
+    if (hist[L + kept] != (int)argmax_key_index(key)) break;
+    ++kept;
+  }
+  const unsigned long long last = keys[ls + kept];
+  if (last == 0ull) report(status, NE_DEV_BAD_TOKEN);
+  hist[L + kept] = (int)argmax_key_index(last);
+  const int emit = kept + 1;
+  const bool ignore_eos = st.flags[s] & NE_SEQ_IGNORE_EOS;
+  int count = 0, fin = NE_FINISH_NONE;
+  for (int e = 0; e < emit; ++e) {
+    const int tok = hist[L + e];
+    out.tokens[(long long)b * (k + 1) + e] = tok;
+    ++count;
+    bool stop = false;
+    if (!ignore_eos)
+      for (int i = 0; i < st.num_stop_ids; ++i) stop |= st.stop_ids[i] == tok;
+    if (stop) {
+      fin = NE_FINISH_STOP;
+      break;
+    }
+    if (L + count - st.num_prompt[s] >= st.max_new_tokens[s]) {
+      fin = NE_FINISH_LENGTH;
+      break;
+    }
+  }
+  st.seq_len[s] = L + count;
+  st.num_cached[s] = st.num_cached[s] + ql - g + kept;
+  if (fin != NE_FINISH_NONE) st.flags[s] |= NE_SEQ_FINISHED;
+  out.count[b] = count;
+  out.finish[b] = fin;
+  out.proposed[b] = g;
+  out.accepted[b] = kept;
+}
+
+// ------------------------------------------------------------------ free-block FIFO
+__global__ void reset_blocks_kernel(ne_batch_state st) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < st.num_blocks; i += gridDim.x * blockDim.x)
+    st.free_ring[i] = i;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    st.ring_head_tail[0] = 0;
+    st.ring_head_tail[1] = st.num_blocks;
+  }
+}
+
+__global__ void free_slots_kernel(ne_batch_state st, const int32_t* slots, int num_slots) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  long long tail = st.ring_head_tail[1];
+  for (int i = 0; i < num_slots; ++i) {
+    const int s = slots[i];
+    if (s < 0 || s >= st.max_seqs) continue;
+    const int used = st.num_blocks_used[s];
+    const int32_t* row = st.block_tables + (long long)s * st.block_table_stride;
+    for (int j = 0; j < used; ++j) st.free_ring[(tail + j) % st.num_blocks] = row[j];
+    tail += used;
+    st.num_blocks_used[s] = 0;
+  }
+  st.ring_head_tail[1] = tail;
+}
+
+inline int check_launch() { return cudaGetLastError() == cudaSuccess ? NE_OK : NE_ERR_CUDA; }
+
+}  // namespace
+
+int launch_embed(const __nv_bfloat16* embed, const int32_t* tokens, const int32_t* num_rows, int max_rows, int hidden,
+                 int vocab, __nv_bfloat16* out, int* status, cudaStream_t stream) {
+  if (hidden % 8) return NE_ERR_INVALID;
+  const int threads = 128;
+  const int blocks = (max_rows * 32 + threads - 1) / threads;
+  if (blocks == 0) return NE_OK;
+  embed_kernel<<<blocks, threads, 0, stream>>>(embed, tokens, num_rows, max_rows, hidden, vocab, out, status);
+  return check_launch();
+}
+
+int launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int max_rows,
+                   const int32_t* rows_dev, const int32_t* gather, int hidden, float eps,
+                   unsigned long long* zero_keys, cudaStream_t stream) {
+  if (hidden % 256) return NE_ERR_INVALID;
+  const int blocks = (max_rows + 3) / 4;
+  if (blocks == 0) return NE_OK;
+  rmsnorm_kernel<<<blocks, 128, 0, stream>>>(x, w, y, max_rows, rows_dev, gather, hidden, eps, zero_keys);
+  return check_launch();
+}
+
+int launch_attention(const __nv_bfloat16* q, __nv_bfloat16* out, const void* k_cache, const void* v_cache,
+                     const __nv_bfloat16* k_scale, const __nv_bfloat16* v_scale, int kv_int8, const ne_rows& rows,
+                     int num_heads, int num_kv_heads, int block_size, long long num_cache_slots, int* status,
+                     cudaStream_t stream) {
+  if (num_kv_heads <= 0 || num_heads % num_kv_heads || block_size > 16 || rows.num_seqs <= 0) return NE_ERR_INVALID;
+  dim3 grid(rows.num_seqs, num_kv_heads);
+  paged_attention_kernel<<<grid, ATT_THREADS, 0, stream>>>(q, out, k_cache, v_cache, k_scale, v_scale, kv_int8, rows,
+                                                          num_heads, num_kv_heads, block_size, num_cache_slots,
+                                                          status);
+  return check_launch();
+}
+
+int launch_keys_to_ids(const unsigned long long* keys, const int32_t* count, int max_count, int32_t* ids,
+                       cudaStream_t stream) {
+  if (max_count <= 0) return NE_OK;
+  keys_to_ids_kernel<<<(max_count + 255) / 256, 256, 0, stream>>>(keys, count, max_count, ids);
+  return check_launch();
+}
+
+int launch_ngram(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int k, int max_ngram,
+                 int min_ngram, int32_t* draft_len, int* status, cudaStream_t stream) {
+  if (num_seqs <= 0) return NE_OK;
+  if (max_ngram < min_ngram || min_ngram < 1 || k < 1) return NE_ERR_INVALID;
+  ngram_kernel<<<num_seqs, 128, 0, stream>>>(st, seq_slot, k, max_ngram, min_ngram, draft_len, status);
+  return check_launch();
+}
+
+int launch_plan(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int mode, int max_rows,
+                int block_size, long long num_cache_slots, const RowBuffers& rb, int* status, cudaStream_t stream) {
+  if (num_seqs <= 0 || num_seqs > 1024) return NE_ERR_INVALID;
+  plan_kernel<<<1, 1024, 0, stream>>>(st, seq_slot, num_seqs, mode, max_rows, block_size, num_cache_slots, rb,
+                                      status);
+  return check_launch();
+}
+
+int launch_accept_greedy(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int k, int mode,
+                         const RowBuffers& rb, const unsigned long long* keys, const ne_step_outputs& out,
+                         int* status, cudaStream_t stream) {
+  if (num_seqs <= 0) return NE_OK;
+  accept_greedy_kernel<<<(num_seqs + 127) / 128, 128, 0, stream>>>(st, seq_slot, num_seqs, k, mode, rb, keys, out,
+                                                                   status);
+  return check_launch();
+}
+
+int launch_reset_blocks(const ne_batch_state& st, cudaStream_t stream) {
+  reset_blocks_kernel<<<64, 256, 0, stream>>>(st);
+  return check_launch();
+}
+
+int launch_free_slots(const ne_batch_state& st, const int32_t* slots, int num_slots, cudaStream_t stream) {
+  if (num_slots <= 0) return NE_OK;
+  free_slots_kernel<<<1, 32, 0, stream>>>(st, slots, num_slots);
+  return check_launch();
+}
+
+}  // namespace ne

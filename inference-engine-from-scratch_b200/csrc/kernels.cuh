@@ -1,0 +1,45 @@
+// Host launchers of the non-GEMM kernels of the speculative step (kernels.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace ne {
+
+enum PlanMode : int { PLAN_SPEC = 0, PLAN_PREFILL = 1 };
+
+// Row metadata the plan kernel writes and every later kernel of the step reads.
+struct RowBuffers {
+  int32_t* num_rows;      // [1]
+  int32_t* token_ids;     // [max_rows]
+  int32_t* positions;     // [max_rows]
+  int32_t* slot_mapping;  // [max_rows]
+  int32_t* lm_rows;       // [max_rows]
+  int32_t* lm_count;      // [1]
+  int32_t* q_start;       // [max_seqs]
+  int32_t* q_len;         // [max_seqs]
+  int32_t* lm_start;      // [max_seqs]
+  int32_t* draft_len;     // [max_seqs]
+};
+
+int launch_embed(const __nv_bfloat16* embed, const int32_t* tokens, const int32_t* num_rows, int max_rows, int hidden,
+                 int vocab, __nv_bfloat16* out, int* status, cudaStream_t stream);
+int launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int max_rows,
+                   const int32_t* rows_dev, const int32_t* gather, int hidden, float eps,
+                   unsigned long long* zero_keys, cudaStream_t stream);
+int launch_attention(const __nv_bfloat16* q, __nv_bfloat16* out, const void* k_cache, const void* v_cache,
+                     const __nv_bfloat16* k_scale, const __nv_bfloat16* v_scale, int kv_int8, const ne_rows& rows,
+                     int num_heads, int num_kv_heads, int block_size, long long num_cache_slots, int* status,
+                     cudaStream_t stream);
+int launch_keys_to_ids(const unsigned long long* keys, const int32_t* count, int max_count, int32_t* ids,
+                       cudaStream_t stream);
+int launch_ngram(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int k, int max_ngram,
+                 int min_ngram, int32_t* draft_len, int* status, cudaStream_t stream);
+int launch_plan(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int mode, int max_rows,
+                int block_size, long long num_cache_slots, const RowBuffers& rb, int* status, cudaStream_t stream);
+int launch_accept_greedy(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int k, int mode,
+                         const RowBuffers& rb, const unsigned long long* keys, const ne_step_outputs& out,
+                         int* status, cudaStream_t stream);
+int launch_reset_blocks(const ne_batch_state& st, cudaStream_t stream);
+int launch_free_slots(const ne_batch_state& st, const int32_t* slots, int num_slots, cudaStream_t stream);
+
+}  // namespace ne

@@ -1,0 +1,247 @@
+"""Batched speculative decoding on the B200 kernels: the drop-in for the runner's speculative step.
+
+``B200SpeculativeEngine.step(slots)`` runs, for every listed sequence slot and entirely on the GPU,
+what ``SpeculativeGenerator._run_speculative_step`` does for one sequence
+(engine/speculative/speculative_generator.py:70-85): n-gram draft with the guess cap
+``min(k, remaining - 1)``, block reservation for the guesses, one (k+1)-token verify forward,
+acceptance, and the commit ``num_cached = len_before + kept``; then the emission / finish loop of
+``_generate`` (:54-67). Per-sequence results equal the serial reference's, since batching changes
+no per-request arithmetic. With ``cuda_graphs`` every batch bucket (engine/generation/
+cuda_graph_runner.py:26 buckets) is captured once and replayed.
+
+Each step copies the step's batch-slot list host->device and reads the packed results
+device->host (tokens, counts, finish reasons, proposed / accepted) in one copy.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _lib
+from .model import B200Model
+from .state import DeviceBatchState
+
+BATCH_SIZE_BUCKETS = (1, 2, 4, 8, 16, 32, 64, 128, 256)
+FINISH_REASONS = {_lib.NE_FINISH_STOP: "stop", _lib.NE_FINISH_LENGTH: "length"}
+
+
+def build_buckets(largest: int, candidates=BATCH_SIZE_BUCKETS) -> list[int]:
+    """engine/generation/cuda_graph_runner.py:35-36."""
+    return sorted({v for v in candidates if v < largest} | {largest})
+
+
+def round_up_to_bucket(value: int, buckets: list[int]) -> int:
+    return next(b for b in buckets if b >= value)
+
+
+@dataclass
+class StepResult:
+    """Per listed slot: emitted tokens, finish reason (None while running), guesses proposed / kept."""
+
+    tokens: dict[int, list[int]] = field(default_factory=dict)
+    finish: dict[int, str | None] = field(default_factory=dict)
+    proposed: int = 0
+    accepted: int = 0
+
+
+class _Outputs:
+    """One flat int32 buffer: tokens [B, k+1] | count [B] | finish [B] | proposed [B] | accepted [B]."""
+
+    def __init__(self, max_seqs: int, k: int, device) -> None:
+        self.k = k
+        self.max_seqs = max_seqs
+        w = k + 1
+        self.buf = torch.zeros(max_seqs * (w + 4), dtype=torch.int32, device=device)
+        self.host = torch.zeros_like(self.buf, device="cpu").pin_memory()
+        n = max_seqs
+        base = self.buf.data_ptr()
+        self.struct = _lib.StepOutputs(
+            tokens=base, count=base + 4 * n * w, finish=base + 4 * n * (w + 1),
+            proposed=base + 4 * n * (w + 2), accepted=base + 4 * n * (w + 3),
+        )
+
+    def fetch(self, num: int):
+        """Copy the whole buffer device->host and split it (one D2H per step)."""
+        self.host.copy_(self.buf, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        n, w = self.max_seqs, self.k + 1
+        h = self.host
+        tokens = h[: n * w].view(n, w)[:num]
+        count = h[n * w: n * (w + 1)][:num]
+        finish = h[n * (w + 1): n * (w + 2)][:num]
+        proposed = h[n * (w + 2): n * (w + 3)][:num]
+        accepted = h[n * (w + 3): n * (w + 4)][:num]
+        return tokens, count, finish, proposed, accepted
+
+
+class B200SpeculativeEngine:
+    def __init__(
+        self,
+        model: B200Model,
+        k: int = 4,
+        max_ngram: int = 3,
+        max_seqs: int = 64,
+        max_model_len: int = 4096,
+        num_blocks: int | None = None,
+        stop_token_ids=(),
+        cuda_graphs: bool = True,
+        max_prefill_rows: int | None = None,
+    ) -> None:
+        self.lib = _lib.load()
+        self.model = model
+        self.k = k
+        self.max_ngram = max_ngram
+        self.max_seqs = max_seqs
+        if model.max_seqs < max_seqs or model.max_rows < max_seqs * (k + 1):
+            raise ValueError("the model workspace is smaller than max_seqs x (k + 1) rows")
+        if max_model_len + k + 1 > model.max_positions:
+            raise ValueError("max_model_len + k exceeds the RoPE table")
+        blocks = num_blocks if num_blocks is not None else model.num_slots // 16
+        if blocks * 16 > model.num_slots:
+            raise ValueError("more blocks than the KV pool holds")
+        self.state = DeviceBatchState(max_seqs, max_model_len, k, blocks, 16, stop_token_ids, model.device)
+        self.outputs = _Outputs(max_seqs, k, model.device)
+        self.max_prefill_rows = min(max_prefill_rows or model.max_rows, model.max_rows)
+        self.buckets = build_buckets(max_seqs)
+        self.cuda_graphs = cuda_graphs
+        self._slots_dev = torch.full((max_seqs,), -1, dtype=torch.int32, device=model.device)
+        self._slots_host = torch.full((max_seqs,), -1, dtype=torch.int32).pin_memory()
+        self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.proposed_total = 0
+        self.accepted_total = 0
+
+    # ------------------------------------------------------------------ request lifecycle
+    def add_request(self, prompt: list[int], max_new_tokens: int, *, ignore_eos: bool = False,
+                    temperature: float = 0.0, top_p: float = 1.0, seed: int = 0) -> int:
+        if temperature != 0.0:
+            raise NotImplementedError("sampled acceptance is not built in this version of the B200 step")
+        slot = self.state.acquire()
+        self.state.load(slot, prompt, max_new_tokens, ignore_eos=ignore_eos, temperature=temperature,
+                        top_p=top_p, seed=seed)
+        return slot
+
+    def release(self, slots: list[int]) -> None:
+        self.state.release(slots)
+
+    def _set_slots(self, slots: list[int], bucket: int) -> None:
+        self._slots_host.fill_(-1)
+        self._slots_host[: len(slots)] = torch.tensor(slots, dtype=torch.int32)
+        self._slots_dev[:bucket].copy_(self._slots_host[:bucket], non_blocking=True)
+
+    def _collect(self, slots: list[int]) -> StepResult:
+        tokens, count, finish, proposed, accepted = self.outputs.fetch(len(slots))
+        result = StepResult()
+        for i, slot in enumerate(slots):
+            c = int(count[i])
+            result.tokens[slot] = tokens[i, :c].tolist()
+            result.finish[slot] = FINISH_REASONS.get(int(finish[i]))
+        result.proposed = int(proposed.sum())
+        result.accepted = int(accepted.sum())
+        self.proposed_total += result.proposed
+        self.accepted_total += result.accepted
+        return result
+
+    # ------------------------------------------------------------------ prefill
+    def prefill(self, slots: list[int], prompt_lengths: list[int]) -> StepResult:
+        """Prefill the newly added slots (in groups of at most ``max_prefill_rows`` prompt tokens)."""
+        merged = StepResult()
+        group, rows = [], 0
+        for slot, length in zip(slots, prompt_lengths):
+            if group and rows + length > self.max_prefill_rows:
+                self._prefill_group(group, rows, merged)
+                group, rows = [], 0
+            group.append(slot)
+            rows += length
+        if group:
+            self._prefill_group(group, rows, merged)
+        return merged
+
+    def _prefill_group(self, slots: list[int], rows: int, merged: StepResult) -> None:
+        if rows > self.max_prefill_rows:
+            raise ValueError(f"a prompt of {rows} tokens exceeds the prefill workspace")
+        self._set_slots(slots, len(slots))
+        _lib.check(self.lib.ne_prefill(self.model.handle, self.state.ref, self._slots_dev.data_ptr(), len(slots),
+                                       rows, self.k, ctypes.byref(self.outputs.struct), _lib.stream_handle()),
+                   "ne_prefill")
+        res = self._collect(slots)
+        self.model.raise_on_device_error()
+        merged.tokens.update(res.tokens)
+        merged.finish.update(res.finish)
+
+    # ------------------------------------------------------------------ speculative step
+    def _launch_step(self, bucket: int) -> None:
+        _lib.check(self.lib.ne_spec_step(self.model.handle, self.state.ref, self._slots_dev.data_ptr(), bucket,
+                                         self.k, self.max_ngram, ctypes.byref(self.outputs.struct),
+                                         _lib.stream_handle()), "ne_spec_step")
+
+    def launch(self, slots: list[int]) -> int:
+        """Enqueue one step for ``slots`` (no host sync); returns the bucket used."""
+        bucket = round_up_to_bucket(len(slots), self.buckets)
+        self._set_slots(slots, bucket)
+        if not self.cuda_graphs:
+            self._launch_step(bucket)
+            return bucket
+        graph = self._graphs.get(bucket)
+        if graph is None:
+            graph = self._capture(bucket)
+        graph.replay()
+        return bucket
+
+    def step(self, slots: list[int]) -> StepResult:
+        self.launch(slots)
+        return self._collect(slots)
+
+    def _capture(self, bucket: int) -> torch.cuda.CUDAGraph:
+        """Capture one bucket's step. The capture itself changes no state: every slot in the
+        bucket is idle (-1) while capturing, so the captured kernels find no work."""
+        saved = self._slots_dev.clone()
+        self._slots_dev.fill_(-1)
+        torch.cuda.synchronize()
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            self._launch_step(bucket)  # warm-up outside capture (idle slots: no state change)
+        torch.cuda.current_stream().wait_stream(stream)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self._launch_step(bucket)
+        torch.cuda.synchronize()
+        self._slots_dev.copy_(saved)
+        self._graphs[bucket] = graph
+        return graph
+
+    # ------------------------------------------------------------------ whole requests
+    def generate(self, prompts: list[list[int]], max_new_tokens: int, ignore_eos: bool = True) -> list[list[int]]:
+        """Serve every prompt with continuous batching (up to ``max_seqs`` at a time)."""
+        outputs: list[list[int]] = [[] for _ in prompts]
+        pending = list(range(len(prompts)))
+        running: dict[int, int] = {}  # slot -> request index
+        while pending or running:
+            admitted = []
+            while pending and self.state.free_slots:
+                index = pending.pop(0)
+                slot = self.add_request(prompts[index], max_new_tokens, ignore_eos=ignore_eos)
+                running[slot] = index
+                admitted.append(slot)
+            if admitted:
+                res = self.prefill(admitted, [len(prompts[running[s]]) for s in admitted])
+                self._absorb(res, running, outputs)
+            if running:
+                slots = sorted(running)
+                res = self.step(slots)
+                self._absorb(res, running, outputs)
+        return outputs
+
+    def _absorb(self, res: StepResult, running: dict[int, int], outputs: list[list[int]]) -> None:
+        done = []
+        for slot, toks in res.tokens.items():
+            outputs[running[slot]].extend(toks)
+            if res.finish.get(slot) is not None:
+                done.append(slot)
+        for slot in done:
+            del running[slot]
+        self.release(done)

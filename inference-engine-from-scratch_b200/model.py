@@ -1,0 +1,185 @@
+"""Device-resident Qwen3 weights, KV pool and workspace bound to one ``ne_model`` handle.
+
+HBM layout (all bf16 unless noted; one CUDA device):
+
+* per layer: ``w_qkv`` = cat(q_proj, k_proj, v_proj) ``[(nh + 2 nkv) * 128, H]``; ``w_o`` ``[H, nh*128]``;
+  ``w_gateup`` = gate/up interleaved in 64-row groups ``[2 I, H]`` (so one 128-row GEMM tile holds 64
+  gate rows and the 64 matching up rows and the SwiGLU fuses into its epilogue); ``w_down`` ``[H, I]``;
+  the four RMSNorm weights;
+* ``embed`` ``[V, H]`` (also the LM head when tied), ``final_norm`` ``[H]``, RoPE cos/sin tables
+  ``[max_positions, 128]`` computed exactly as models/qwen3.py:47-57 (fp32 angles, cast to bf16);
+* the KV pool: one tensor ``[L, 2, num_slots + 1, nkv, 128]`` whose ``[l, 0]`` / ``[l, 1]`` views are the
+  reference's per-layer key / value caches (engine/memory/kv_cache_pool.py:34-69, last row = scratch
+  slot); an int8 pool adds ``[L, 2, num_slots + 1, nkv]`` bf16 scales;
+* the workspace (activations, row metadata, argmax keys), sized for ``max_rows`` token rows.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .config import Qwen3Config
+
+
+def rope_tables(max_positions: int, head_dim: int, theta: float, dtype=torch.bfloat16):
+    """cos / sin ``[max_positions, head_dim]`` with the arithmetic of models/qwen3.py:47-57."""
+    exponents = torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim
+    inverse = 1.0 / (theta**exponents)
+    angles = torch.arange(max_positions).float()[:, None] * inverse
+    angles = torch.cat((angles, angles), dim=-1)
+    return angles.cos().to(dtype), angles.sin().to(dtype)
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, group: int = 64) -> torch.Tensor:
+    rows, hidden = gate.shape
+    return torch.stack((gate.view(rows // group, group, hidden), up.view(rows // group, group, hidden)), dim=1).reshape(
+        2 * rows, hidden
+    )
+
+
+class B200Model:
+    """Packs a HF-named state dict onto one GPU and binds it to the native ``ne_model``."""
+
+    def __init__(
+        self,
+        cfg: Qwen3Config,
+        weights: dict[str, torch.Tensor],
+        num_slots: int,
+        device: torch.device | str = "cuda",
+        max_positions: int = 4096,
+        kv_int8: bool = False,
+        max_rows: int = 4096,
+        max_seqs: int = 256,
+    ) -> None:
+        self.lib = _lib.load()
+        self.cfg = cfg
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("B200Model lives on a CUDA device; the oracle is the CPU path")
+        self.num_slots = num_slots
+        self.max_positions = max_positions
+        self.kv_int8 = kv_int8
+        self.max_rows = max_rows
+        self.max_seqs = max_seqs
+        bf16 = torch.bfloat16
+        dev = self.device
+
+        def put(t: torch.Tensor) -> torch.Tensor:
+            return t.to(device=dev, dtype=bf16).contiguous()
+
+        L, nkv, d = cfg.num_hidden_layers, cfg.num_key_value_heads, cfg.head_dim
+        self.layers: list[dict[str, torch.Tensor]] = []
+        for layer in range(L):
+            p = f"model.layers.{layer}."
+            qkv = torch.cat(
+                [weights[p + "self_attn.q_proj.weight"], weights[p + "self_attn.k_proj.weight"],
+                 weights[p + "self_attn.v_proj.weight"]], dim=0)
+            self.layers.append({
+                "w_qkv": put(qkv),
+                "w_o": put(weights[p + "self_attn.o_proj.weight"]),
+                "w_gateup": put(interleave_gate_up(weights[p + "mlp.gate_proj.weight"], weights[p + "mlp.up_proj.weight"])),
+                "w_down": put(weights[p + "mlp.down_proj.weight"]),
+                "ln_in": put(weights[p + "input_layernorm.weight"]),
+                "ln_post": put(weights[p + "post_attention_layernorm.weight"]),
+                "q_norm": put(weights[p + "self_attn.q_norm.weight"]),
+                "k_norm": put(weights[p + "self_attn.k_norm.weight"]),
+            })
+        self.embed = put(weights["model.embed_tokens.weight"])
+        head = weights.get("lm_head.weight")
+        self.lm_head = self.embed if (cfg.tie_word_embeddings or head is None) else put(head)
+        self.final_norm = put(weights["model.norm.weight"])
+        cos, sin = rope_tables(max_positions, d, cfg.rope_theta)
+        self.rope_cos, self.rope_sin = cos.to(dev), sin.to(dev)
+
+        cache_dtype = torch.int8 if kv_int8 else bf16
+        self.kv = torch.zeros((L, 2, num_slots + 1, nkv, d), dtype=cache_dtype, device=dev)
+        self.kv_scales = torch.zeros((L, 2, num_slots + 1, nkv), dtype=bf16, device=dev) if kv_int8 else None
+
+        config = _lib.ModelConfig(
+            vocab_size=cfg.vocab_size, hidden_size=cfg.hidden_size, intermediate_size=cfg.intermediate_size,
+            num_layers=L, num_heads=cfg.num_attention_heads, num_kv_heads=nkv, head_dim=d,
+            rms_norm_eps=cfg.rms_norm_eps, block_size=16, kv_int8=int(kv_int8), weight_int8=0,
+            num_cache_slots=num_slots + 1, max_positions=max_positions,
+        )
+        handle = ctypes.c_void_p()
+        _lib.check(self.lib.ne_model_create(ctypes.byref(config), ctypes.byref(handle)), "ne_model_create")
+        self.handle = handle
+        self._layer_structs = []
+        for layer, w in enumerate(self.layers):
+            lw = _lib.LayerWeights(
+                w_qkv=w["w_qkv"].data_ptr(), w_o=w["w_o"].data_ptr(), w_gateup=w["w_gateup"].data_ptr(),
+                w_down=w["w_down"].data_ptr(), ln_in=w["ln_in"].data_ptr(), ln_post=w["ln_post"].data_ptr(),
+                q_norm=w["q_norm"].data_ptr(), k_norm=w["k_norm"].data_ptr(),
+                k_cache=self.k_cache(layer).data_ptr(), v_cache=self.v_cache(layer).data_ptr(),
+                k_scale=self.kv_scales[layer, 0].data_ptr() if kv_int8 else None,
+                v_scale=self.kv_scales[layer, 1].data_ptr() if kv_int8 else None,
+            )
+            _lib.check(self.lib.ne_model_set_layer(handle, layer, ctypes.byref(lw)), "ne_model_set_layer")
+            self._layer_structs.append(lw)
+        hw = _lib.HeadWeights(
+            embed=self.embed.data_ptr(), lm_head=self.lm_head.data_ptr(), final_norm=self.final_norm.data_ptr(),
+            rope_cos=self.rope_cos.data_ptr(), rope_sin=self.rope_sin.data_ptr(),
+        )
+        _lib.check(self.lib.ne_model_set_head(handle, ctypes.byref(hw)), "ne_model_set_head")
+        self._head_struct = hw
+        nbytes = ctypes.c_size_t()
+        _lib.check(self.lib.ne_model_workspace_bytes(handle, max_rows, max_seqs, ctypes.byref(nbytes)),
+                   "ne_model_workspace_bytes")
+        self.workspace = torch.empty(nbytes.value + 256, dtype=torch.uint8, device=dev)
+        base = (self.workspace.data_ptr() + 255) // 256 * 256
+        _lib.check(self.lib.ne_model_set_workspace(handle, base, nbytes.value, max_rows, max_seqs),
+                   "ne_model_set_workspace")
+        self.status_ptr = self.lib.ne_model_status_word(handle)
+
+    # ------------------------------------------------------------------ views
+    def k_cache(self, layer: int) -> torch.Tensor:
+        return self.kv[layer, 0]
+
+    def v_cache(self, layer: int) -> torch.Tensor:
+        return self.kv[layer, 1]
+
+    @property
+    def scratch_slot(self) -> int:
+        return self.num_slots
+
+    @property
+    def weight_bytes(self) -> int:
+        """Unique weight bytes one verify step streams (linear weights + LM head + norms)."""
+        seen, total = set(), 0
+        tensors = [t for w in self.layers for t in w.values()] + [self.lm_head, self.final_norm]
+        for t in tensors:
+            if t.data_ptr() not in seen:
+                seen.add(t.data_ptr())
+                total += t.numel() * t.element_size()
+        return total
+
+    def kv_bytes_per_token(self) -> int:
+        """engine/memory/kv_cache_pool.py:11-24."""
+        per_head = self.cfg.head_dim * (1 if self.kv_int8 else 2) + (2 if self.kv_int8 else 0)
+        return 2 * self.cfg.num_hidden_layers * self.cfg.num_key_value_heads * per_head
+
+    # ------------------------------------------------------------------ status
+    def read_status(self, clear: bool = True) -> int:
+        word = ctypes.c_int32()
+        _lib.check(self.lib.ne_read_status(self.status_ptr, int(clear), ctypes.byref(word), _lib.stream_handle()),
+                   "ne_read_status")
+        return word.value
+
+    def raise_on_device_error(self) -> None:
+        word = self.read_status(clear=True)
+        if word:
+            raise _lib.NativeError(f"device reported: {_lib.describe_device_status(word)} (0x{word:x})")
+
+    def close(self) -> None:
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            self.lib.ne_model_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass

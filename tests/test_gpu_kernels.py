@@ -1,0 +1,156 @@
+"""Kernel-level parity on the GPU: each kernel through the C ABI against a plain fp32 torch reference
+(GEMM, RMSNorm, attention) or the CPU oracle (n-gram drafts, bit-exact)."""
+
+from __future__ import annotations
+
+import ctypes
+import json
+
+import pytest
+import torch
+
+from oracle import qwen3 as oq
+from tests.conftest import GOLDEN, submodule
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def lib():
+    submodule("build").build()
+    return submodule("_lib").load()
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+@pytest.mark.parametrize(
+    "M,N,K",
+    [(1, 128, 64), (5, 256, 1024), (16, 4096, 1024), (100, 1024, 2048), (128, 1024, 3072), (320, 6144, 1024),
+     (330, 1024, 2048), (600, 384, 256), (2048, 512, 256)],
+)
+def test_gemm_matches_fp32_torch(lib, cuda_device, M, N, K) -> None:
+    g = torch.Generator(device="cpu").manual_seed(M * 7 + N + K)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(cuda_device)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16).to(cuda_device)
+    y = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    rc = lib.ne_gemm_bf16(x.data_ptr(), w.data_ptr(), y.data_ptr(), M, N, K, status.data_ptr(), _stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    ref = (x.float() @ w.float().T)
+    # fp32 accumulation in both; only the summation order differs -> within one bf16 rounding step
+    torch.testing.assert_close(y.float(), ref, rtol=8e-3, atol=2e-3)
+
+
+def test_gemm_is_deterministic(lib, cuda_device) -> None:
+    x = torch.randn(320, 2048, device=cuda_device).to(torch.bfloat16)
+    w = (torch.randn(1024, 2048, device=cuda_device) * 0.02).to(torch.bfloat16)
+    outs = []
+    for _ in range(3):
+        y = torch.empty(320, 1024, dtype=torch.bfloat16, device=cuda_device)
+        assert lib.ne_gemm_bf16(x.data_ptr(), w.data_ptr(), y.data_ptr(), 320, 1024, 2048, None, _stream()) == 0
+        outs.append(y)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+
+
+@pytest.mark.parametrize("rows,hidden", [(1, 1024), (37, 1024), (320, 256), (5, 4096)])
+def test_rmsnorm_matches_reference_arithmetic(lib, cuda_device, rows, hidden) -> None:
+    x = torch.randn(rows, hidden).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(hidden)).to(torch.bfloat16)
+    y = torch.empty(rows, hidden, dtype=torch.bfloat16, device=cuda_device)
+    assert lib.ne_rmsnorm(x.to(cuda_device).data_ptr(), w.to(cuda_device).data_ptr(), y.data_ptr(), rows, hidden,
+                          1e-6, _stream()) == 0
+    want = oq.rms_norm(x, w, 1e-6)
+    got = y.cpu()
+    # the only freedom is the fp32 summation order of mean(x^2): at most one bf16 step apart
+    torch.testing.assert_close(got.float(), want.float(), rtol=8e-3, atol=1e-3)
+    assert (got == want).float().mean() > 0.99
+
+
+def test_ngram_kernel_is_bit_exact_on_the_reference_cases(lib, cuda_device) -> None:
+    cases = json.loads((GOLDEN / "ngram_cases.json").read_text())
+    groups: dict[tuple[int, int], list[dict]] = {}
+    for case in cases:
+        groups.setdefault((case["k"], case["max_ngram"]), []).append(case)
+    state_mod = submodule("state")
+    for (k, max_ngram), group in groups.items():
+        st = state_mod.DeviceBatchState(len(group), 256, k, 4, device=cuda_device)
+        for slot, case in enumerate(group):
+            st.load(slot, case["history"], max_new_tokens=k + 1)
+        slots = torch.arange(len(group), dtype=torch.int32, device=cuda_device)
+        draft_len = torch.zeros(len(group), dtype=torch.int32, device=cuda_device)
+        status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+        rc = lib.ne_ngram_propose(st.ref, slots.data_ptr(), len(group), k, max_ngram, 1, draft_len.data_ptr(),
+                                  status.data_ptr(), _stream())
+        assert rc == 0
+        lens = draft_len.tolist()
+        assert int(status.item()) == 0
+        for slot, case in enumerate(group):
+            L = len(case["history"])
+            got = st.history[slot, L:L + lens[slot]].tolist() if lens[slot] > 0 else []
+            assert got == case["expected"], case
+
+
+def _attention_reference(q, k_cache, v_cache, tables, q_start, q_len, positions, nh, nkv):
+    out = torch.zeros_like(q, dtype=torch.float32)
+    G = nh // nkv
+    for b in range(len(q_len)):
+        for j in range(q_len[b]):
+            row = q_start[b] + j
+            pos = positions[row]
+            slots = [tables[b][p // 16] * 16 + p % 16 for p in range(pos + 1)]
+            keys = k_cache[slots].float()  # [c, nkv, d]
+            vals = v_cache[slots].float()
+            for head in range(nh):
+                kv = head // G
+                s = (keys[:, kv, :] @ q[row, head].float()) / (128 ** 0.5)
+                p = torch.softmax(s, dim=0)
+                out[row, head] = p @ vals[:, kv, :]
+    return out
+
+
+@pytest.mark.parametrize("nh,nkv,q_lens,ctx", [(16, 8, [5, 1, 3], [69, 16, 200]), (32, 8, [9, 2], [40, 17]),
+                                               (4, 2, [64], [64])])
+def test_paged_attention_matches_fp32_reference(lib, cuda_device, nh, nkv, q_lens, ctx) -> None:
+    g = torch.Generator().manual_seed(sum(ctx))
+    num_blocks = 64
+    k_cache = torch.randn(num_blocks * 16 + 1, nkv, 128, generator=g).to(torch.bfloat16)
+    v_cache = torch.randn(num_blocks * 16 + 1, nkv, 128, generator=g).to(torch.bfloat16)
+    perm = torch.randperm(num_blocks, generator=g).tolist()
+    tables, q_start, positions = [], [], []
+    row = 0
+    for b, (ql, c) in enumerate(zip(q_lens, ctx)):
+        nb = (c + 15) // 16
+        tables.append(perm[:nb])
+        perm = perm[nb:]
+        q_start.append(row)
+        positions += list(range(c - ql, c))
+        row += ql
+    M = row
+    q = torch.randn(M, nh, 128, generator=g).to(torch.bfloat16)
+    stride = max(len(t) for t in tables)
+    table_t = torch.full((len(q_lens), stride), -1, dtype=torch.int32)
+    for b, t in enumerate(tables):
+        table_t[b, :len(t)] = torch.tensor(t)
+    dev = cuda_device
+    dq, dk, dv = q.to(dev), k_cache.to(dev), v_cache.to(dev)
+    out = torch.zeros(M, nh, 128, dtype=torch.bfloat16, device=dev)
+    i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)  # noqa: E731
+    t_qs, t_ql, t_pos, t_tab = i32(q_start), i32(q_lens), i32(positions), table_t.to(dev)
+    rows = submodule("_lib").Rows(
+        max_rows=M, num_seqs=len(q_lens), num_rows=None, token_ids=None, positions=t_pos.data_ptr(),
+        slot_mapping=None, q_start=t_qs.data_ptr(), q_len=t_ql.data_ptr(), block_tables=t_tab.data_ptr(),
+        table_index=None, block_table_stride=stride, max_context=stride * 16, lm_rows=None, lm_count=None, lm_max=0,
+    )
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    rc = lib.ne_paged_attention(dq.data_ptr(), out.data_ptr(), dk.data_ptr(), dv.data_ptr(), None, None, 0,
+                                ctypes.byref(rows), nh, nkv, 16, num_blocks * 16 + 1, status.data_ptr(), _stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    want = _attention_reference(q, k_cache, v_cache, tables, q_start, q_lens, positions, nh, nkv)
+    torch.testing.assert_close(out.cpu().float(), want, rtol=1e-2, atol=1e-2)
