@@ -1,0 +1,443 @@
+#!/usr/bin/env python
+"""Accepted tokens/s of the B200 speculative step on BASELINE config 2 (Qwen3-0.6B, bf16, n-gram k=4,
+64 users, short_chat: 64-token prompts, 128 outputs).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+* ``value``: steady-state speculative steps (draft -> (k+1)-token verify -> accept -> commit for all
+  64 users, one CUDA graph per step) timed with CUDA events over exactly K steps, inputs and state
+  resident in HBM; emitted tokens / device time. Every step streams 1.19 GB of weights plus the KV
+  cache, far more than the 126 MB L2, so no L2 flush is needed between steps.
+* ``e2e``: the whole short_chat job (64 prompts from pinned host memory, prefill, every step until
+  each user has 128 tokens, one device->host read of the results per step) through the public API
+  ``B200SpeculativeEngine.generate``; emitted tokens / time.
+* ``roofline``: the dominant kernel of one profiled step (CUDA events around every launch), its
+  algorithmic bytes per launch over its average duration, against MEASURED_PEAKS.json.
+* ``cpu_baseline``: the CPU oracle (the reference's serial speculative path restated, fp32, config 1's
+  prompt) on this host's cores for a bounded sample.
+
+Multi-GPU: one process per GPU (torchrun); each rank serves its own 64 users on an independent
+replica (no collectives on the data path); NCCL only carries the barrier and the max-over-ranks
+timing. ``--impl reference`` times the reference's CPU path (the oracle port) on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import importlib
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+PACKAGE = "inference-engine-from-scratch_b200"
+METRIC = "accepted tok/s, Qwen3-0.6B spec-decode at 64 users (n-gram k=4, greedy)"
+UNIT = "tok/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=30)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--users", type=int, default=64)
+    p.add_argument("--k", type=int, default=4)
+    p.add_argument("--prompt-len", type=int, default=64)
+    p.add_argument("--max-new", type=int, default=128)
+    p.add_argument("--cpu-seconds", type=float, default=15.0)
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------- distributed plumbing
+class _RankZero:
+    rank = 0
+    world = 1
+
+
+class Dist:
+    def __init__(self, gpus: int) -> None:
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.enabled = self.world > 1
+        if self.enabled:
+            import torch.distributed as dist
+
+            torch.cuda.set_device(self.local_rank)
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local_rank))
+            self.dist = dist
+
+    def barrier(self) -> None:
+        if self.enabled:
+            self.dist.barrier()
+
+    def max(self, value: float) -> float:
+        if not self.enabled:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device=f"cuda:{self.local_rank}")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, value: float) -> float:
+        if not self.enabled:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device=f"cuda:{self.local_rank}")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self) -> None:
+        if self.enabled:
+            self.dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------- clocks (NVML, read-only)
+class ClockSampler:
+    """Samples SM clock and clock-event reasons every ``interval`` s while the timed region runs."""
+
+    REASONS = {
+        0x0000000000000008: "hw_slowdown",
+        0x0000000000000040: "hw_thermal_slowdown",
+        0x0000000000000020: "sw_thermal_slowdown",
+        0x0000000000000004: "sw_power_cap",
+        0x0000000000000080: "hw_power_brake_slowdown",
+    }
+
+    def __init__(self, device_index: int, interval: float = 0.005) -> None:
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception:  # no NVML: report no clocks rather than guess
+            self.nvml = None
+        self.interval = interval
+
+    def _run(self) -> None:
+        get_reasons = getattr(self.nvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            self.nvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                mhz = self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM)
+                reasons = get_reasons(self.handle)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(self.interval)
+
+    def __enter__(self):
+        if self.nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict | None:
+        if self.nvml is None:
+            return None
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mhz = [m for m, _ in self.samples]
+        active = 0
+        for _, r in self.samples:
+            active |= r
+        reasons = [name for bit, name in self.REASONS.items() if active & bit]
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(mhz)}
+
+
+def measured_peak() -> tuple[float, str]:
+    path = REPO / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic() -> dict:
+    path = REPO / "profiles" / "ncu_traffic.json"
+    try:
+        return json.loads(path.read_text())
+    except Exception:
+        return {}
+
+
+# ---------------------------------------------------------------------------- CPU side (oracle)
+def cpu_oracle_run(pkg, seconds: float, warmup_steps: int = 0, timed_steps: int | None = None):
+    """The reference's serial speculative path restated (oracle), fp32 on this host's cores.
+
+    Returns (emitted tokens, seconds, steps) over a bounded sample: prefill of config 1's prompt,
+    then speculative steps until ``timed_steps`` steps or ``seconds`` elapse.
+    """
+    from oracle import ngram, speculative as ospec, verify
+
+    cfg = pkg.QWEN3_0_6B
+    weights = pkg.make_weights(cfg, seed=0)
+    runner = ospec.OracleRunner(weights, cfg, 64, 16, torch.float32)
+    prompt = pkg.make_prompt(cfg.vocab_size, 64, 0, True)
+    seq = ospec.Seq("cpu", list(prompt), len(prompt), 128, ignore_eos=True)
+    runner.tables.reserve("cpu", seq.num_tokens)
+    first, _ = runner.run_step([seq])
+    seq.token_ids.append(first[0])
+
+    def one_step() -> int:
+        remaining = seq.max_new_tokens - seq.num_generated_tokens
+        g = max(0, min(4, remaining - 1))
+        draft = ngram.propose(seq.token_ids, g, 3) if g else []
+        before = seq.num_tokens
+        seq.token_ids.extend(draft)
+        runner.tables.reserve("cpu", seq.num_tokens)
+        logits = runner.score_tokens(seq, 1 + len(draft))
+        new = verify.verify_proposal(draft, None, logits, 0.0, 1.0, iter(()))
+        del seq.token_ids[before:]
+        seq.num_cached_tokens = before + len(new) - 1
+        seq.token_ids.extend(new)
+        return len(new)
+
+    for _ in range(warmup_steps):
+        one_step()
+    emitted, steps = 0, 0
+    start = time.perf_counter()
+    while True:
+        if seq.num_generated_tokens >= seq.max_new_tokens - 1:
+            break
+        emitted += one_step()
+        steps += 1
+        elapsed = time.perf_counter() - start
+        if timed_steps is not None and steps >= timed_steps:
+            break
+        if timed_steps is None and elapsed >= seconds:
+            break
+    return emitted, time.perf_counter() - start, steps
+
+
+def run_reference(args, dist: Dist) -> None:
+    """The reference arm: the reference's CPU speculative path (oracle port) on the host cores."""
+    if dist.rank != 0:
+        return
+    pkg = importlib.import_module(PACKAGE)
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    emitted, seconds, steps = cpu_oracle_run(pkg, args.cpu_seconds, warmup_steps=args.warmup,
+                                             timed_steps=args.steps)
+    value = emitted / seconds
+    sample = (f"1 user (requests are served one at a time by the reference, so its 64-user rate equals "
+              f"this), config 1 prompt, {steps} speculative steps after {args.warmup} warm-up, fp32")
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": 1000 * seconds / max(steps, 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": workload_config(args),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args) -> dict:
+    return {
+        "workload": f"BASELINE config 2: Qwen3-0.6B random-init (seed 0), short_chat ({args.prompt_len}-token "
+                    f"prompts, 50% motif-repeated / 50% uniform, {args.max_new} outputs), {args.users} users "
+                    f"per GPU, n-gram n=3 k={args.k}, greedy, 16-token paged KV",
+        "users_per_gpu": args.users,
+        "k": args.k,
+        "parallelism": f"dp{args.gpus} (independent replicas)",
+        "l2": "no flush: every step streams 1.19 GB of weights + KV (> 126 MB L2)",
+    }
+
+
+# ---------------------------------------------------------------------------- B200 arm
+def algorithmic_bytes(kind: str, cfg, M: int, ctx_sum: int, kv_bytes_per_token_layer: int) -> float:
+    """Unique bytes one launch of ``kind`` must move (weights, activations in/out, KV)."""
+    H, I, V = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size
+    q, kv = cfg.num_attention_heads * 128, cfg.num_key_value_heads * 128
+    if kind == "gemm_qkv":
+        return (q + 2 * kv) * H * 2 + M * H * 2 + M * q * 2 + 2 * M * kv * 2
+    if kind == "gemm_o":
+        return H * q * 2 + M * q * 2 + 2 * M * H * 2
+    if kind == "gemm_gateup":
+        return 2 * I * H * 2 + M * H * 2 + M * I * 2
+    if kind == "gemm_down":
+        return H * I * 2 + M * I * 2 + 2 * M * H * 2
+    if kind == "lm_head":
+        return V * H * 2 + M * H * 2 + M * 8
+    if kind == "attention":
+        return ctx_sum * kv_bytes_per_token_layer + 2 * M * q * 2
+    return 0.0
+
+
+def run_b200(args, dist: Dist) -> None:
+    pkg = importlib.import_module(PACKAGE)
+    model_mod = importlib.import_module(f"{PACKAGE}.model")
+    engine_mod = importlib.import_module(f"{PACKAGE}.engine")
+    lib_mod = importlib.import_module(f"{PACKAGE}._lib")
+    importlib.import_module(f"{PACKAGE}.build").build()
+    device = torch.device("cuda", dist.local_rank)
+    torch.cuda.set_device(device)
+    cfg = pkg.QWEN3_0_6B
+    users, k = args.users, args.k
+    steady_new = max(args.max_new, (args.warmup + args.steps + 3) * (k + 1))
+    max_model_len = args.prompt_len + steady_new + 8
+    blocks_per_user = -(-(max_model_len + k + 1) // 16)
+    num_blocks = users * blocks_per_user + 16
+    weights = pkg.make_weights(cfg, seed=0)
+    model = model_mod.B200Model(cfg, weights, num_slots=num_blocks * 16, device=device,
+                                max_positions=max_model_len + k + 16, max_rows=max(users * args.prompt_len, users * (k + 1)),
+                                max_seqs=users)
+    del weights
+    engine = engine_mod.B200SpeculativeEngine(model, k=k, max_ngram=3, max_seqs=users, max_model_len=max_model_len,
+                                              num_blocks=num_blocks, cuda_graphs=True)
+    prompts = pkg.make_prompts(users, cfg.vocab_size, args.prompt_len, seed=dist.rank * users)
+
+    # ------------------------------------------------------------ steady state (value)
+    slots = [engine.add_request(p, steady_new, ignore_eos=True) for p in prompts]
+    engine.prefill(slots, [len(p) for p in prompts])
+    for _ in range(args.warmup):
+        engine.step(slots)
+    model.raise_on_device_error()
+    engine._set_slots(slots, engine_mod.round_up_to_bucket(len(slots), engine.buckets))
+    lens_before = engine.state.seq_len.sum().item()
+    graph = engine._graphs[engine_mod.round_up_to_bucket(len(slots), engine.buckets)]
+    stream = torch.cuda.current_stream()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dist.local_rank) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+    dist.barrier()
+    ms = start.elapsed_time(end)
+    emitted = engine.state.seq_len.sum().item() - lens_before
+    model.raise_on_device_error()
+    max_ms = dist.max(ms)
+    total_emitted = dist.sum(emitted)
+    value = total_emitted / (max_ms / 1000.0)
+
+    # ------------------------------------------------------------ one profiled (eager) step: roofline
+    lens = engine.state.seq_len[torch.tensor(slots, device=device).long()]
+    ctx_before = int(lens.sum().item())
+    launches_before = model.lib.ne_model_launch_count(model.handle)
+    ms_by = (ctypes.c_float * 12)()
+    n_by = (ctypes.c_int * 12)()
+    lib_mod.check(model.lib.ne_model_profile_begin(model.handle, stream.cuda_stream), "profile_begin")
+    engine._set_slots(slots, len(slots))
+    engine._launch_step(len(slots))
+    lib_mod.check(model.lib.ne_model_profile_end(model.handle, ms_by, n_by, 12), "profile_end")
+    res = engine._collect(slots)
+    launches_per_step = model.lib.ne_model_launch_count(model.handle) - launches_before
+    M = len(slots) + res.proposed
+    ctx_sum = ctx_before + res.proposed  # keys visible to the last row of every sequence
+    per_layer_kv = model.kv_bytes_per_token() // cfg.num_hidden_layers
+    kinds = lib_mod.KERNEL_KINDS
+    profile = {kinds[i]: {"ms": round(ms_by[i], 4), "launches": n_by[i]} for i in range(12) if n_by[i]}
+    step_ms_profiled = sum(ms_by[i] for i in range(12))
+    dominant = max((kinds[i] for i in range(12) if n_by[i]), key=lambda kk: ms_by[kinds.index(kk)])
+    di = kinds.index(dominant)
+    avg_ms = ms_by[di] / n_by[di]
+    bytes_launch = algorithmic_bytes(dominant, cfg, M, ctx_sum, per_layer_kv)
+    peak, peak_src = measured_peak()
+    achieved = bytes_launch / (avg_ms / 1000.0) / 1e9
+    traffic = ncu_traffic().get(dominant)
+    roofline = {"bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_src,
+                "bytes_per_launch": int(bytes_launch), "avg_launch_ms": round(avg_ms, 5)}
+    step_bytes = model.weight_bytes + ctx_sum * model.kv_bytes_per_token() + M * model.kv_bytes_per_token()
+    step_time_s = max_ms / 1000.0 / args.steps
+    step_roofline = {"bytes_per_step": int(step_bytes), "ms_per_step": round(1000 * step_time_s, 4),
+                     "achieved_gbs": round(step_bytes / step_time_s / 1e9, 1),
+                     "frac": round(step_bytes / step_time_s / 1e9 / peak, 4),
+                     "profiled_rows": M, "profiled_ms_sum": round(step_ms_profiled, 4)}
+    engine.release(slots)
+
+    # ------------------------------------------------------------ e2e: the whole job through the public API
+    e2e = None
+    if not args.no_e2e:
+        engine.h2d_bytes = engine.d2h_bytes = 0
+        dist.barrier()
+        torch.cuda.synchronize()
+        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_start.record(stream)
+        steps_before = engine.steps_run
+        outs = engine.generate(prompts, args.max_new, ignore_eos=True)
+        e_end.record(stream)
+        torch.cuda.synchronize()
+        e_ms = dist.max(e_start.elapsed_time(e_end))
+        tokens = dist.sum(sum(len(o) for o in outs))
+        n_steps = max(1, engine.steps_run - steps_before)
+        e2e = {"value": tokens / (e_ms / 1000.0), "unit": UNIT,
+               "h2d_bytes_per_step": int(engine.h2d_bytes / n_steps),
+               "d2h_bytes_per_step": int(engine.d2h_bytes / n_steps),
+               "steps": n_steps, "tokens": int(tokens), "ms": round(e_ms, 3)}
+        model.raise_on_device_error()
+
+    # ------------------------------------------------------------ CPU baseline (rank 0, N = 1)
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        threads = len(os.sched_getaffinity(0))
+        torch.set_num_threads(threads)
+        c_emitted, c_seconds, c_steps = cpu_oracle_run(pkg, args.cpu_seconds)
+        cpu = {"value": c_emitted / c_seconds, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"CPU oracle (reference serial speculative path restated), fp32, 1 user, config 1 prompt, "
+                         f"{c_steps} speculative steps in {c_seconds:.1f} s"}
+
+    if dist.rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded token-ID prompts, random-init weights)",
+            "config": workload_config(args) | {"steady_state_max_new_tokens": steady_new},
+            "e2e": e2e, "roofline": roofline, "step_roofline": step_roofline, "cpu_baseline": cpu,
+            "clocks": clocks.summary(), "gpu_launches": int(launches_per_step * args.steps),
+            "launches_per_step": int(launches_per_step), "emitted_tokens": int(total_emitted),
+            "tokens_per_step_per_user": round(total_emitted / dist.world / args.steps / users, 3),
+            "kernel_profile": profile,
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        # CPU work only: no process group; under torchrun the ranks other than 0 exit at once
+        if int(os.environ.get("RANK", "0")) == 0:
+            run_reference(args, _RankZero())
+        return
+    dist = Dist(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference(args, dist)
+        else:
+            run_b200(args, dist)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -231,6 +231,32 @@ NE_API int ne_prefill(ne_model* model, const ne_batch_state* state, const int32_
 NE_API int ne_spec_step(ne_model* model, const ne_batch_state* state, const int32_t* seq_slot, int num_seqs,
                  int k, int max_ngram, const ne_step_outputs* out, void* stream);
 
+/* ---------------------------------------------------------------- launch accounting */
+/* Kernel classes of a step, for per-kernel device timing (ne_model_profile_*). */
+#define NE_K_EMBED 0
+#define NE_K_RMSNORM 1
+#define NE_K_GEMM_QKV 2      /* QKV projection + q/k RMSNorm + RoPE + KV append */
+#define NE_K_ATTENTION 3
+#define NE_K_GEMM_O 4        /* o_proj + residual */
+#define NE_K_GEMM_GATEUP 5   /* gate/up projection + SwiGLU */
+#define NE_K_GEMM_DOWN 6     /* down_proj + residual */
+#define NE_K_LM_HEAD 7       /* LM head + argmax / logits */
+#define NE_K_NGRAM 8
+#define NE_K_PLAN 9
+#define NE_K_ACCEPT 10
+#define NE_K_OTHER 11
+#define NE_NUM_KINDS 12
+
+/* Kernels this model has launched so far (every entry point that takes the model counts). */
+NE_API long long ne_model_launch_count(const ne_model* model);
+/*
+ * Time every kernel the model launches on ``stream`` between begin and end with CUDA events
+ * (eager launches only, not inside a graph capture). end synchronizes and fills, per kind,
+ * the summed device milliseconds and the number of launches.
+ */
+NE_API int ne_model_profile_begin(ne_model* model, void* stream);
+NE_API int ne_model_profile_end(ne_model* model, float* ms_by_kind, int* launches_by_kind, int num_kinds);
+
 /* ---------------------------------------------------------------- building blocks (tests) */
 /*
  * y[m, n] = sum_k x[m, k] w[n, k] on tcgen05 tensor cores, bf16 in, fp32 accumulate, bf16 out

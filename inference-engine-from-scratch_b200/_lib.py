@@ -7,7 +7,7 @@ is missing or a CUDA device is absent, the calls below raise instead of computin
 from __future__ import annotations
 
 import ctypes
-from ctypes import POINTER, c_float, c_int, c_int32, c_int64, c_longlong, c_size_t, c_uint64, c_void_p
+from ctypes import POINTER, c_float, c_int, c_int32, c_longlong, c_size_t, c_void_p
 from pathlib import Path
 
 import torch
@@ -51,7 +51,13 @@ EXPORTS = {
          c_longlong, c_void_p, c_void_p],
     ),
     "ne_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p]),
+    "ne_model_launch_count": (c_longlong, [c_void_p]),
+    "ne_model_profile_begin": (c_int, [c_void_p, c_void_p]),
+    "ne_model_profile_end": (c_int, [c_void_p, POINTER(c_float), POINTER(c_int), c_int]),
 }
+
+KERNEL_KINDS = ("embed", "rmsnorm", "gemm_qkv", "attention", "gemm_o", "gemm_gateup", "gemm_down", "lm_head",
+                "ngram", "plan", "accept", "other")
 
 
 class ModelConfig(ctypes.Structure):

@@ -29,6 +29,16 @@ struct ne_model {
   ne::RowBuffers rb{};
   CUtensorMap tm_x{}, tm_attn{}, tm_act{};
   int num_sms = 148;
+  // launch accounting / profiling
+  long long launches = 0;
+  bool profiling = false;
+  cudaStream_t profile_stream = nullptr;
+  std::vector<cudaEvent_t> events;   // events[0] = begin; events[i + 1] after the i-th launch
+  std::vector<int> event_kinds;
+  size_t events_used = 0;
+  ~ne_model() {
+    for (cudaEvent_t e : events) cudaEventDestroy(e);
+  }
 };
 
 namespace {
@@ -63,6 +73,23 @@ Layout workspace_layout(const ne_model_config& c, int R, int B) {
 }
 
 cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Count one launch of ``kind``; while profiling, close its timing interval with an event.
+int note(ne_model* m, int kind, int rc, cudaStream_t stream) {
+  if (rc != NE_OK) return rc;
+  ++m->launches;
+  if (m->profiling && stream == m->profile_stream) {
+    if (m->events_used >= m->events.size()) {
+      cudaEvent_t e;
+      if (cudaEventCreate(&e) != cudaSuccess) return NE_ERR_CUDA;
+      m->events.push_back(e);
+    }
+    if (cudaEventRecord(m->events[m->events_used], stream) != cudaSuccess) return NE_ERR_CUDA;
+    m->event_kinds.push_back(kind);
+    ++m->events_used;
+  }
+  return NE_OK;
+}
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -249,12 +276,14 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
   cudaStream_t s = as_stream(stream);
   const int H = c.hidden_size, I = c.intermediate_size, qs = c.num_heads * 128, kvs = c.num_kv_heads * 128;
   const __nv_bfloat16* embed = static_cast<const __nv_bfloat16*>(m->head.embed);
-  int rc = ne::launch_embed(embed, rows->token_ids, rows->num_rows, R, H, c.vocab_size, m->h, m->status, s);
+  int rc = note(m, NE_K_EMBED,
+                ne::launch_embed(embed, rows->token_ids, rows->num_rows, R, H, c.vocab_size, m->h, m->status, s), s);
   if (rc) return rc;
   for (int l = 0; l < c.num_layers; ++l) {
     const ne_layer_weights& w = m->layers[l];
-    rc = ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(w.ln_in), m->x, R, rows->num_rows, nullptr, H,
-                            c.rms_norm_eps, nullptr, s);
+    rc = note(m, NE_K_RMSNORM,
+              ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(w.ln_in), m->x, R, rows->num_rows, nullptr,
+                                 H, c.rms_norm_eps, nullptr, s), s);
     if (rc) return rc;
     ne::Epilogue e{};
     e.mode = ne::EPI_QKV;
@@ -276,41 +305,44 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
     e.v_scale = static_cast<__nv_bfloat16*>(w.v_scale);
     e.kv_int8 = c.kv_int8;
     e.num_cache_slots = c.num_cache_slots;
-    rc = run_gemm(m, &m->tm_qkv[l], &m->tm_x, R, rows->num_rows, qs + 2 * kvs, H, e, s);
+    rc = note(m, NE_K_GEMM_QKV, run_gemm(m, &m->tm_qkv[l], &m->tm_x, R, rows->num_rows, qs + 2 * kvs, H, e, s), s);
     if (rc) return rc;
-    rc = ne::launch_attention(m->q, m->attn, w.k_cache, w.v_cache, static_cast<const __nv_bfloat16*>(w.k_scale),
-                              static_cast<const __nv_bfloat16*>(w.v_scale), c.kv_int8, *rows, c.num_heads,
-                              c.num_kv_heads, c.block_size, c.num_cache_slots, m->status, s);
+    rc = note(m, NE_K_ATTENTION,
+              ne::launch_attention(m->q, m->attn, w.k_cache, w.v_cache, static_cast<const __nv_bfloat16*>(w.k_scale),
+                                   static_cast<const __nv_bfloat16*>(w.v_scale), c.kv_int8, *rows, c.num_heads,
+                                   c.num_kv_heads, c.block_size, c.num_cache_slots, m->status, s), s);
     if (rc) return rc;
     ne::Epilogue eo{};
     eo.mode = ne::EPI_RESIDUAL;
     eo.status = m->status;
     eo.out = m->h;
     eo.ldo = H;
-    rc = run_gemm(m, &m->tm_o[l], &m->tm_attn, R, rows->num_rows, H, qs, eo, s);
+    rc = note(m, NE_K_GEMM_O, run_gemm(m, &m->tm_o[l], &m->tm_attn, R, rows->num_rows, H, qs, eo, s), s);
     if (rc) return rc;
-    rc = ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(w.ln_post), m->x, R, rows->num_rows, nullptr, H,
-                            c.rms_norm_eps, nullptr, s);
+    rc = note(m, NE_K_RMSNORM,
+              ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(w.ln_post), m->x, R, rows->num_rows, nullptr,
+                                 H, c.rms_norm_eps, nullptr, s), s);
     if (rc) return rc;
     ne::Epilogue eg{};
     eg.mode = ne::EPI_SWIGLU;
     eg.status = m->status;
     eg.out = m->act;
     eg.ldo = I;
-    rc = run_gemm(m, &m->tm_gateup[l], &m->tm_x, R, rows->num_rows, 2 * I, H, eg, s);
+    rc = note(m, NE_K_GEMM_GATEUP, run_gemm(m, &m->tm_gateup[l], &m->tm_x, R, rows->num_rows, 2 * I, H, eg, s), s);
     if (rc) return rc;
     ne::Epilogue ed{};
     ed.mode = ne::EPI_RESIDUAL;
     ed.status = m->status;
     ed.out = m->h;
     ed.ldo = H;
-    rc = run_gemm(m, &m->tm_down[l], &m->tm_act, R, rows->num_rows, H, I, ed, s);
+    rc = note(m, NE_K_GEMM_DOWN, run_gemm(m, &m->tm_down[l], &m->tm_act, R, rows->num_rows, H, I, ed, s), s);
     if (rc) return rc;
   }
   // final norm over the rows that get logits (gathered to the front of x), keys cleared
   const int lm_max = rows->lm_max;
-  rc = ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(m->head.final_norm), m->x, lm_max, rows->lm_count,
-                          rows->lm_rows, H, c.rms_norm_eps, m->keys, s);
+  rc = note(m, NE_K_RMSNORM,
+            ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(m->head.final_norm), m->x, lm_max,
+                               rows->lm_count, rows->lm_rows, H, c.rms_norm_eps, m->keys, s), s);
   if (rc) return rc;
   if (lm_mode == NE_LM_NONE) return NE_OK;
   ne::Epilogue el{};
@@ -319,10 +351,46 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
   el.out = static_cast<__nv_bfloat16*>(logits);
   el.ldo = c.vocab_size;
   el.argmax_keys = m->keys;
-  rc = run_gemm(m, &m->tm_lm, &m->tm_x, lm_max, rows->lm_count, c.vocab_size, H, el, s);
+  rc = note(m, NE_K_LM_HEAD, run_gemm(m, &m->tm_lm, &m->tm_x, lm_max, rows->lm_count, c.vocab_size, H, el, s), s);
   if (rc) return rc;
-  if (argmax_out) rc = ne::launch_keys_to_ids(m->keys, rows->lm_count, lm_max, argmax_out, s);
+  if (argmax_out) rc = note(m, NE_K_OTHER, ne::launch_keys_to_ids(m->keys, rows->lm_count, lm_max, argmax_out, s), s);
   return rc;
+}
+
+long long ne_model_launch_count(const ne_model* m) { return m ? m->launches : -1; }
+
+int ne_model_profile_begin(ne_model* m, void* stream) {
+  if (!m) return NE_ERR_INVALID;
+  cudaStream_t s = as_stream(stream);
+  if (m->events.empty()) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) return NE_ERR_CUDA;
+    m->events.push_back(e);
+  }
+  m->event_kinds.clear();
+  m->events_used = 1;
+  m->profile_stream = s;
+  m->profiling = true;
+  return cudaEventRecord(m->events[0], s) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
+}
+
+int ne_model_profile_end(ne_model* m, float* ms_by_kind, int* launches_by_kind, int num_kinds) {
+  if (!m || !m->profiling || !ms_by_kind || !launches_by_kind || num_kinds < NE_NUM_KINDS) return NE_ERR_INVALID;
+  m->profiling = false;
+  for (int k = 0; k < num_kinds; ++k) {
+    ms_by_kind[k] = 0.f;
+    launches_by_kind[k] = 0;
+  }
+  if (m->events_used == 0) return NE_OK;
+  if (cudaEventSynchronize(m->events[m->events_used - 1]) != cudaSuccess) return NE_ERR_CUDA;
+  for (size_t i = 1; i < m->events_used; ++i) {
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, m->events[i - 1], m->events[i]) != cudaSuccess) return NE_ERR_CUDA;
+    const int kind = m->event_kinds[i - 1];
+    ms_by_kind[kind] += ms;
+    launches_by_kind[kind] += 1;
+  }
+  return NE_OK;
 }
 
 int ne_state_reset_blocks(const ne_batch_state* st, void* stream) {
@@ -346,13 +414,16 @@ int ne_prefill(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, i
   if (!m || !st || !seq_slot || !out || num_seqs <= 0 || k < 1) return NE_ERR_INVALID;
   if (max_rows > m->max_rows || num_seqs > m->max_seqs) return NE_ERR_WORKSPACE;
   cudaStream_t s = as_stream(stream);
-  int rc = ne::launch_plan(*st, seq_slot, num_seqs, ne::PLAN_PREFILL, max_rows, m->cfg.block_size,
-                           m->cfg.num_cache_slots, m->rb, m->status, s);
+  int rc = note(m, NE_K_PLAN,
+                ne::launch_plan(*st, seq_slot, num_seqs, ne::PLAN_PREFILL, max_rows, m->cfg.block_size,
+                                m->cfg.num_cache_slots, m->rb, m->status, s), s);
   if (rc) return rc;
   ne_rows rows = make_step_rows(m, st, seq_slot, num_seqs, max_rows, num_seqs);
   rc = ne_forward(m, &rows, NE_LM_ARGMAX, nullptr, nullptr, stream);
   if (rc) return rc;
-  return ne::launch_accept_greedy(*st, seq_slot, num_seqs, k, ne::PLAN_PREFILL, m->rb, m->keys, *out, m->status, s);
+  return note(m, NE_K_ACCEPT,
+              ne::launch_accept_greedy(*st, seq_slot, num_seqs, k, ne::PLAN_PREFILL, m->rb, m->keys, *out, m->status,
+                                       s), s);
 }
 
 int ne_spec_step(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int k, int max_ngram,
@@ -361,15 +432,19 @@ int ne_spec_step(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot,
   const int max_rows = num_seqs * (k + 1);
   if (max_rows > m->max_rows || num_seqs > m->max_seqs) return NE_ERR_WORKSPACE;
   cudaStream_t s = as_stream(stream);
-  int rc = ne::launch_ngram(*st, seq_slot, num_seqs, k, max_ngram, 1, m->rb.draft_len, m->status, s);
+  int rc = note(m, NE_K_NGRAM, ne::launch_ngram(*st, seq_slot, num_seqs, k, max_ngram, 1, m->rb.draft_len, m->status, s),
+                s);
   if (rc) return rc;
-  rc = ne::launch_plan(*st, seq_slot, num_seqs, ne::PLAN_SPEC, max_rows, m->cfg.block_size, m->cfg.num_cache_slots,
-                       m->rb, m->status, s);
+  rc = note(m, NE_K_PLAN,
+            ne::launch_plan(*st, seq_slot, num_seqs, ne::PLAN_SPEC, max_rows, m->cfg.block_size,
+                            m->cfg.num_cache_slots, m->rb, m->status, s), s);
   if (rc) return rc;
   ne_rows rows = make_step_rows(m, st, seq_slot, num_seqs, max_rows, max_rows);
   rc = ne_forward(m, &rows, NE_LM_ARGMAX, nullptr, nullptr, stream);
   if (rc) return rc;
-  return ne::launch_accept_greedy(*st, seq_slot, num_seqs, k, ne::PLAN_SPEC, m->rb, m->keys, *out, m->status, s);
+  return note(m, NE_K_ACCEPT,
+              ne::launch_accept_greedy(*st, seq_slot, num_seqs, k, ne::PLAN_SPEC, m->rb, m->keys, *out, m->status, s),
+              s);
 }
 
 int ne_gemm_bf16(const void* x, const void* w, void* y, int M, int N, int K, int32_t* status, void* stream) {

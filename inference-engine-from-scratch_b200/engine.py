@@ -112,6 +112,9 @@ class B200SpeculativeEngine:
         self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.proposed_total = 0
         self.accepted_total = 0
+        self.h2d_bytes = 0  # host->device bytes copied for requests and steps
+        self.d2h_bytes = 0  # device->host bytes read back (step results)
+        self.steps_run = 0  # prefill and speculative steps whose results were read
 
     # ------------------------------------------------------------------ request lifecycle
     def add_request(self, prompt: list[int], max_new_tokens: int, *, ignore_eos: bool = False,
@@ -121,6 +124,7 @@ class B200SpeculativeEngine:
         slot = self.state.acquire()
         self.state.load(slot, prompt, max_new_tokens, ignore_eos=ignore_eos, temperature=temperature,
                         top_p=top_p, seed=seed)
+        self.h2d_bytes += 4 * len(prompt) + 5 * 4 + 4 + 4 + 8 + 8
         return slot
 
     def release(self, slots: list[int]) -> None:
@@ -130,9 +134,12 @@ class B200SpeculativeEngine:
         self._slots_host.fill_(-1)
         self._slots_host[: len(slots)] = torch.tensor(slots, dtype=torch.int32)
         self._slots_dev[:bucket].copy_(self._slots_host[:bucket], non_blocking=True)
+        self.h2d_bytes += 4 * bucket
 
     def _collect(self, slots: list[int]) -> StepResult:
         tokens, count, finish, proposed, accepted = self.outputs.fetch(len(slots))
+        self.d2h_bytes += self.outputs.buf.numel() * 4
+        self.steps_run += 1
         result = StepResult()
         for i, slot in enumerate(slots):
             c = int(count[i])
