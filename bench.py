@@ -58,6 +58,8 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=15.0)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--profile-step", action="store_true",
+                   help="prefill, then two eager speculative steps and exit (a short target for ncu)")
     return p.parse_args()
 
 
@@ -315,6 +317,14 @@ def run_b200(args, dist: Dist) -> None:
     # ------------------------------------------------------------ steady state (value)
     slots = [engine.add_request(p, steady_new, ignore_eos=True) for p in prompts]
     engine.prefill(slots, [len(p) for p in prompts])
+    if args.profile_step:
+        for _ in range(2):
+            engine._set_slots(slots, len(slots))
+            engine._launch_step(len(slots))
+            engine._collect(slots)
+        model.raise_on_device_error()
+        model.close()
+        return
     for _ in range(args.warmup):
         engine.step(slots)
     model.raise_on_device_error()

@@ -22,10 +22,10 @@ __device__ __forceinline__ uint32_t map_peer(uint32_t local_addr, uint32_t rank)
 }
 __device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
   float4 v;
+  // no memory clobber: the partial tiles are read-only between the two cluster barriers
   asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
+               : "r"(addr));
   return v;
 }
 
@@ -45,12 +45,13 @@ __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v)
 
 // Apply the epilogue to ``count`` token rows whose fp32 accumulators sit in shared memory
 // ``acc`` as [count][128]. ``m_begin`` is the global row of acc row 0; ``tile_n`` the N tile.
+template <int MODE>
 __device__ void epilogue_rows(const Epilogue& e, int N, int tile_n, int m_begin, int count, const float* acc) {
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
   const int n0 = tile_n * GEMM_BM;
-  switch (e.mode) {
+  switch (MODE) {
     case EPI_STORE:
       for (int idx = tid; idx < count * GEMM_BM; idx += GEMM_THREADS) {
         int m = idx >> 7, n = idx & 127;
@@ -149,7 +150,7 @@ __device__ void epilogue_rows(const Epilogue& e, int N, int tile_n, int m_begin,
         for (int i = 0; i < 4; ++i) {
           int n = lane + 32 * i;
           float y = bf16r(acc[m * GEMM_BM + n]);
-          if (e.mode == EPI_LOGITS) e.out[(long long)row * e.ldo + n0 + n] = __float2bfloat16_rn(y);
+          if (MODE == EPI_LOGITS) e.out[(long long)row * e.ldo + n0 + n] = __float2bfloat16_rn(y);
           unsigned long long key = argmax_key(y, (uint32_t)(n0 + n));
           best = key > best ? key : best;
         }
@@ -164,6 +165,7 @@ __device__ void epilogue_rows(const Epilogue& e, int N, int tile_n, int m_begin,
   (void)N;
 }
 
+template <int MODE>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                    const GemmParams p) {
@@ -297,7 +299,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (c32 + i < cnt) stage_acc[(c32 + i) * GEMM_BM + warp * 32 + lane] = v[i];
       }
       __syncthreads();
-      if (ok) epilogue_rows(p.epi, p.N, tile_n, m_begin + c0, cnt, stage_acc);
+      if (ok) epilogue_rows<MODE>(p.epi, p.N, tile_n, m_begin + c0, cnt, stage_acc);
       __syncthreads();
     }
   } else {
@@ -325,18 +327,24 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const int m = idx / (GEMM_BM / 4);
       const int n4 = idx % (GEMM_BM / 4);
       const uint32_t off = (uint32_t)(((s_begin + m) * GEMM_BM + n4 * 4) * 4);
+      float4 part[GEMM_MAX_SPLITS];
+#pragma unroll
+      for (int r = 0; r < GEMM_MAX_SPLITS; ++r)
+        if (r < S) part[r] = ld_cluster_f4(map_peer(local_base + off, (uint32_t)r));
       float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int r = 0; r < S; ++r) {
-        float4 v = ld_cluster_f4(map_peer(local_base + off, (uint32_t)r));
-        sum.x += v.x;
-        sum.y += v.y;
-        sum.z += v.z;
-        sum.w += v.w;
+#pragma unroll
+      for (int r = 0; r < GEMM_MAX_SPLITS; ++r) {  // fixed split order: deterministic sums
+        if (r < S) {
+          sum.x += part[r].x;
+          sum.y += part[r].y;
+          sum.z += part[r].z;
+          sum.w += part[r].w;
+        }
       }
       reinterpret_cast<float4*>(red)[m * (GEMM_BM / 4) + n4] = sum;
     }
     __syncthreads();
-    if (ok && s_cnt > 0) epilogue_rows(p.epi, p.N, tile_n, m_begin + s_begin, s_cnt, red);
+    if (ok && s_cnt > 0) epilogue_rows<MODE>(p.epi, p.N, tile_n, m_begin + s_begin, s_cnt, red);
     __syncthreads();
     cluster_sync_all();  // peers may still be reading our partial tile
   }
@@ -415,13 +423,20 @@ int gemm_plan(GemmParams& p, int num_sms) {
   return NE_OK;
 }
 
-int gemm_launch(const CUtensorMap* tm_w, const CUtensorMap* tm_x, const GemmParams& p, cudaStream_t stream) {
+template <int MODE>
+cudaError_t launch_mode(const cudaLaunchConfig_t& cfg, const CUtensorMap* tm_w, const CUtensorMap* tm_x,
+                        const GemmParams& p) {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM_BYTES);
+    attr_err = cudaFuncSetAttribute(gemm_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    GEMM_SMEM_BYTES);
   });
-  if (attr_err != cudaSuccess) return NE_ERR_CUDA;
+  if (attr_err != cudaSuccess) return attr_err;
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<MODE>, *tm_w, *tm_x, p);
+}
+
+int gemm_launch(const CUtensorMap* tm_w, const CUtensorMap* tm_x, const GemmParams& p, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.splits, p.N / GEMM_BM, (p.M_max + p.t_block - 1) / p.t_block);
   cfg.blockDim = dim3(GEMM_THREADS);
@@ -434,7 +449,16 @@ int gemm_launch(const CUtensorMap* tm_w, const CUtensorMap* tm_x, const GemmPara
   attrs[0].val.clusterDim.z = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = 1;
-  cudaError_t err = cudaLaunchKernelEx(&cfg, gemm_tc_kernel, *tm_w, *tm_x, p);
+  cudaError_t err;
+  switch (p.epi.mode) {
+    case EPI_STORE: err = launch_mode<EPI_STORE>(cfg, tm_w, tm_x, p); break;
+    case EPI_RESIDUAL: err = launch_mode<EPI_RESIDUAL>(cfg, tm_w, tm_x, p); break;
+    case EPI_SWIGLU: err = launch_mode<EPI_SWIGLU>(cfg, tm_w, tm_x, p); break;
+    case EPI_QKV: err = launch_mode<EPI_QKV>(cfg, tm_w, tm_x, p); break;
+    case EPI_ARGMAX: err = launch_mode<EPI_ARGMAX>(cfg, tm_w, tm_x, p); break;
+    case EPI_LOGITS: err = launch_mode<EPI_LOGITS>(cfg, tm_w, tm_x, p); break;
+    default: return NE_ERR_INVALID;
+  }
   return err == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 
