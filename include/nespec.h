@@ -129,6 +129,7 @@ typedef struct {
   const int32_t* table_index;    /* [num_seqs] row of block_tables (NULL: row b) */
   int block_table_stride;
   int max_context;               /* host bound on context length */
+  int max_q_len;                 /* host bound on rows per sequence */
   const int32_t* lm_rows;        /* [lm_max] rows that get logits, in order */
   const int32_t* lm_count;       /* device: number of lm rows */
   int lm_max;
@@ -269,10 +270,14 @@ NE_API int ne_gemm_bf16(const void* x, const void* w, void* y, int M, int N, int
  * Paged verify attention (run_cached_attention without the gather, attention_context.py:66-109):
  * q [rows, nh, 128] bf16 -> out [rows, nh, 128] bf16, causal within each sequence by position,
  * reading K/V in place through the block table. k_scale/v_scale NULL for a bf16 cache.
+ * ``scratch`` (256-byte aligned, may be NULL) holds split-KV partials when few sequences leave
+ * SMs idle; the kernel then splits each context and a combine pass merges the splits. The
+ * split count is chosen from the grid size and ``scratch_bytes`` (no scratch: one split).
  */
 NE_API int ne_paged_attention(const void* q, void* out, const void* k_cache, const void* v_cache, const void* k_scale,
-                       const void* v_scale, int kv_int8, const ne_rows* rows, int num_heads, int num_kv_heads,
-                       int block_size, long long num_cache_slots, int32_t* status, void* stream);
+                              const void* v_scale, int kv_int8, const ne_rows* rows, int num_heads, int num_kv_heads,
+                              int block_size, long long num_cache_slots, void* scratch, size_t scratch_bytes,
+                              int32_t* status, void* stream);
 
 /* RMSNorm rows (models/qwen3.py:39-44): y = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w). */
 NE_API int ne_rmsnorm(const void* x, const void* w, void* y, int rows, int hidden, float eps, void* stream);

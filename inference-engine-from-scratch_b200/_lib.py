@@ -48,7 +48,7 @@ EXPORTS = {
     "ne_paged_attention": (
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int,
-         c_longlong, c_void_p, c_void_p],
+         c_longlong, c_void_p, c_size_t, c_void_p, c_void_p],
     ),
     "ne_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p]),
     "ne_model_launch_count": (c_longlong, [c_void_p]),
@@ -102,6 +102,7 @@ class Rows(ctypes.Structure):
         ("table_index", c_void_p),
         ("block_table_stride", c_int),
         ("max_context", c_int),
+        ("max_q_len", c_int),
         ("lm_rows", c_void_p),
         ("lm_count", c_void_p),
         ("lm_max", c_int),

@@ -1,0 +1,520 @@
+// Paged verify attention on tensor cores (mma.sync m16n8k16, bf16 in, fp32 accumulate).
+//
+// run_cached_attention (models/attention_context.py:66-109) without the gathered copy: one CTA per
+// (batch entry, KV head, split) reads the entry's 16-token KV blocks in place through its block
+// table. The query vectors of the entry (its q_len rows x the G query heads sharing the KV head)
+// form 16-row tiles. Per 16-token block: S = Q K^T (2 x 8 MMAs), an online softmax in fp32, P
+// rounded to bf16, O += P V (16 MMAs). Keys after a query's own position are masked (causal).
+//
+// * One query tile (the speculative step: (k+1) x G <= 16 vectors): the four warps take every
+//   fourth block of the split, each with its own cp.async double buffer, and merge their
+//   (max, sum, O) through shared memory at the end.
+// * More tiles (prefill): the CTA loads each block once into a shared double buffer and warp w
+//   works on query tiles w, w+4, ...
+// * Split-KV (few sequences): each split writes its unnormalised partial (O, max, sum) and
+//   combine_kernel merges the splits; otherwise the CTA writes the bf16 output directly.
+// * int8 KV: blocks are dequantised while staged (int8 -> bf16, times the bf16 per (slot, head)
+//   scale, as read_from_cache, attention_context.py:57-63).
+#include "attention.cuh"
+
+namespace ne {
+
+namespace {
+
+constexpr int D = 128;
+constexpr int ROW_BYTES = D * 2 + 16;            // padded smem row: conflict-free ldmatrix
+constexpr int BLOCK_BYTES = 16 * ROW_BYTES;      // one 16-token K (or V) block in smem
+constexpr int THREADS = 128;
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float SCALE_LOG2 = 0.08838834764831845f * LOG2E;  // 1/sqrt(128) folded into exp2
+#define NEG_INF (-__int_as_float(0x7f800000))
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+struct Ctx {
+  const __nv_bfloat16* q;
+  __nv_bfloat16* out;
+  const void* kc;
+  const void* vc;
+  const __nv_bfloat16* ks;
+  const __nv_bfloat16* vs;
+  const int32_t* table;
+  int nh, nkv, h, G, r0, nvec;
+  long long num_cache_slots;
+  int* status;
+};
+
+// Stage one 16-token K and V block (block id ``blk``) into smem at k_s / v_s, using ``nthr``
+// threads numbered ``t`` (a warp: 32, the CTA: 128). bf16 pools go through cp.async.
+template <bool INT8>
+__device__ __forceinline__ void stage_block(const Ctx& c, long long blk, uint32_t k_s, uint32_t v_s, int t,
+                                            int nthr) {
+  if (!INT8) {
+    for (int i = t; i < 16 * 16; i += nthr) {  // 16 tokens x 16 chunks of 16 B, K and V
+      const int tok = i >> 4, ch = i & 15;
+      const long long off = ((blk * 16 + tok) * c.nkv + c.h) * D + ch * 8;
+      cp_async16(k_s + tok * ROW_BYTES + ch * 16, reinterpret_cast<const __nv_bfloat16*>(c.kc) + off);
+      cp_async16(v_s + tok * ROW_BYTES + ch * 16, reinterpret_cast<const __nv_bfloat16*>(c.vc) + off);
+    }
+  } else {
+    for (int i = t; i < 16 * 8; i += nthr) {  // 16 tokens x 8 chunks of 16 int8
+      const int tok = i >> 3, ch = i & 7;
+      const long long slot = blk * 16 + tok;
+      const long long off = (slot * c.nkv + c.h) * D + ch * 16;
+      const float ksc = __bfloat162float(c.ks[slot * c.nkv + c.h]);
+      const float vsc = __bfloat162float(c.vs[slot * c.nkv + c.h]);
+      const int4 kq = *reinterpret_cast<const int4*>(reinterpret_cast<const int8_t*>(c.kc) + off);
+      const int4 vq = *reinterpret_cast<const int4*>(reinterpret_cast<const int8_t*>(c.vc) + off);
+      const int8_t* kb = reinterpret_cast<const int8_t*>(&kq);
+      const int8_t* vb = reinterpret_cast<const int8_t*>(&vq);
+      uint32_t kw[8], vw[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        kw[j] = pack_bf16(bf16r((float)kb[2 * j] * ksc), bf16r((float)kb[2 * j + 1] * ksc));
+        vw[j] = pack_bf16(bf16r((float)vb[2 * j] * vsc), bf16r((float)vb[2 * j + 1] * vsc));
+      }
+      const uint32_t ko = k_s + tok * ROW_BYTES + ch * 32, vo = v_s + tok * ROW_BYTES + ch * 32;
+      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(ko), "r"(kw[0]), "r"(kw[1]), "r"(kw[2]), "r"(kw[3]));
+      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(ko + 16), "r"(kw[4]), "r"(kw[5]), "r"(kw[6]),
+                   "r"(kw[7]));
+      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(vo), "r"(vw[0]), "r"(vw[1]), "r"(vw[2]), "r"(vw[3]));
+      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(vo + 16), "r"(vw[4]), "r"(vw[5]), "r"(vw[6]),
+                   "r"(vw[7]));
+    }
+  }
+}
+
+// Valid block id of logical block ``kb`` or -1 (reported) when the table names no pool block.
+__device__ __forceinline__ long long block_id(const Ctx& c, int kb, int stride) {
+  long long blk = kb < stride ? c.table[kb] : -1;
+  if (blk < 0 || (blk + 1) * 16 > c.num_cache_slots - 1) {
+    report(c.status, NE_DEV_BAD_SLOT);
+    return -1;
+  }
+  return blk;
+}
+
+// Load the 16-vector query tile starting at vector ``v0`` (rows past nvec are zero) into smem.
+__device__ __forceinline__ void load_q_tile(const Ctx& c, int v0, uint8_t* q_s, int t, int nthr) {
+  for (int i = t; i < 16 * 16; i += nthr) {
+    const int v = i >> 4, ch = i & 15;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (v0 + v < c.nvec) {
+      const int row = c.r0 + (v0 + v) / c.G;
+      const int head = c.h * c.G + (v0 + v) % c.G;
+      val = *reinterpret_cast<const uint4*>(c.q + ((long long)row * c.nh + head) * D + ch * 8);
+    }
+    *reinterpret_cast<uint4*>(q_s + v * ROW_BYTES + ch * 16) = val;
+  }
+}
+
+struct TileState {
+  uint32_t qa[8][4];  // Q A-fragments for the 8 k-steps of 16 dims
+  float o[16][4];     // O accumulators: 16 tiles of 8 dims
+  float m[2], l[2];   // running max (log2 domain) and sum for rows lane/4 and lane/4 + 8
+  int pos[2];         // positions of those rows (-1: padding row)
+};
+
+__device__ __forceinline__ void tile_init(TileState& ts, uint32_t q_s, const int* spos, int lane) {
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const int row = (lane & 7) + 8 * ((lane >> 3) & 1);
+    const int col = 16 * kk + 8 * (lane >> 4);
+    ldsm_x4(ts.qa[kk], q_s + row * ROW_BYTES + col * 2);
+  }
+#pragma unroll
+  for (int t = 0; t < 16; ++t) ts.o[t][0] = ts.o[t][1] = ts.o[t][2] = ts.o[t][3] = 0.f;
+  ts.m[0] = ts.m[1] = NEG_INF;
+  ts.l[0] = ts.l[1] = 0.f;
+  ts.pos[0] = spos[lane >> 2];
+  ts.pos[1] = spos[(lane >> 2) + 8];
+}
+
+// One 16-token block (logical index kb) staged at k_s / v_s against the tile.
+__device__ __forceinline__ void tile_block(TileState& ts, uint32_t k_s, uint32_t v_s, int kb, int lane) {
+  float s[2][4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 8; kk += 2) {
+      uint32_t b[4];
+      const int tok = 8 * j + (lane & 7);
+      const int col = 16 * kk + 8 * (lane >> 3);
+      ldsm_x4(b, k_s + tok * ROW_BYTES + col * 2);
+      mma16816(s[j], ts.qa[kk], b[0], b[1]);
+      mma16816(s[j], ts.qa[kk + 1], b[2], b[3]);
+    }
+  }
+  // scale (log2 domain), causal mask, online softmax per row
+  float mx[2] = {NEG_INF, NEG_INF};
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int r = e >> 1;
+      const int key = kb * 16 + 8 * j + 2 * (lane & 3) + (e & 1);
+      float v = s[j][e] * SCALE_LOG2;
+      if (key > ts.pos[r]) v = NEG_INF;
+      s[j][e] = v;
+      mx[r] = fmaxf(mx[r], v);
+    }
+  float corr[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xFFFFFFFFu, mx[r], 1));
+    mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xFFFFFFFFu, mx[r], 2));
+    const float m_new = fmaxf(ts.m[r], mx[r]);
+    corr[r] = (m_new == NEG_INF || ts.m[r] == NEG_INF) ? (m_new == NEG_INF ? 1.f : 0.f) : exp2f(ts.m[r] - m_new);
+    ts.m[r] = m_new;
+  }
+  float psum[2] = {0.f, 0.f};
+  uint32_t pa[4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    float p[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int r = e >> 1;
+      p[e] = (s[j][e] == NEG_INF) ? 0.f : exp2f(s[j][e] - ts.m[r]);
+      psum[r] += p[e];
+    }
+    pa[2 * j] = pack_bf16(p[0], p[1]);
+    pa[2 * j + 1] = pack_bf16(p[2], p[3]);
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    psum[r] += __shfl_xor_sync(0xFFFFFFFFu, psum[r], 1);
+    psum[r] += __shfl_xor_sync(0xFFFFFFFFu, psum[r], 2);
+    ts.l[r] = ts.l[r] * corr[r] + psum[r];
+  }
+#pragma unroll
+  for (int t = 0; t < 16; ++t) {
+    ts.o[t][0] *= corr[0];
+    ts.o[t][1] *= corr[0];
+    ts.o[t][2] *= corr[1];
+    ts.o[t][3] *= corr[1];
+  }
+#pragma unroll
+  for (int t = 0; t < 16; t += 2) {
+    uint32_t b[4];
+    const int tok = (lane & 7) + 8 * ((lane >> 3) & 1);
+    const int col = 8 * t + 8 * (lane >> 4);
+    ldsm_x4_t(b, v_s + tok * ROW_BYTES + col * 2);
+    mma16816(ts.o[t], pa, b[0], b[1]);
+    mma16816(ts.o[t + 1], pa, b[2], b[3]);
+  }
+}
+
+// Write a finished tile: normalised bf16 output (one split) or the unnormalised partial.
+__device__ __forceinline__ void tile_store(const Ctx& c, const AttnSplit& sp, const TileState& ts, int v0, int lane,
+                                           int b, int split) {
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int v = v0 + (lane >> 2) + 8 * r;
+    if (v >= c.nvec) continue;
+    if (sp.splits == 1) {
+      const float inv = ts.l[r] > 0.f ? 1.f / ts.l[r] : 0.f;
+      const int row = c.r0 + v / c.G;
+      const int head = c.h * c.G + v % c.G;
+      __nv_bfloat16* o = c.out + ((long long)row * c.nh + head) * D;
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        const int d = 8 * t + 2 * (lane & 3);
+        *reinterpret_cast<__nv_bfloat162*>(o + d) = __floats2bfloat162_rn(ts.o[t][2 * r] * inv, ts.o[t][2 * r + 1] * inv);
+      }
+    } else {
+      const long long base = (((long long)b * c.nkv + c.h) * sp.splits + split) * sp.max_vec + v;
+      float* o = sp.part_o + base * D;
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        const int d = 8 * t + 2 * (lane & 3);
+        *reinterpret_cast<float2*>(o + d) = make_float2(ts.o[t][2 * r], ts.o[t][2 * r + 1]);
+      }
+      if ((lane & 3) == 0) {
+        sp.part_m[base] = ts.m[r];
+        sp.part_l[base] = ts.l[r];
+      }
+    }
+  }
+}
+
+template <bool INT8>
+__global__ void __launch_bounds__(THREADS)
+    attention_kernel(const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out, const void* __restrict__ kc,
+                     const void* __restrict__ vc, const __nv_bfloat16* __restrict__ ks,
+                     const __nv_bfloat16* __restrict__ vs, ne_rows rows, int nh, int nkv, long long num_cache_slots,
+                     AttnSplit sp, int* status) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int b = blockIdx.x, h = blockIdx.y, split = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ql = rows.q_len[b];
+  if (ql <= 0) return;
+  Ctx c;
+  c.q = q;
+  c.out = out;
+  c.kc = kc;
+  c.vc = vc;
+  c.ks = ks;
+  c.vs = vs;
+  c.nh = nh;
+  c.nkv = nkv;
+  c.h = h;
+  c.G = nh / nkv;
+  c.r0 = rows.q_start[b];
+  c.nvec = ql * c.G;
+  c.num_cache_slots = num_cache_slots;
+  c.status = status;
+  c.table = rows.block_tables + (long long)(rows.table_index ? rows.table_index[b] : b) * rows.block_table_stride;
+  const int ctx = rows.positions[c.r0 + ql - 1] + 1;  // the last row sees the whole context
+  const int nblk = (ctx + 15) / 16;
+  const int bps = (nblk + sp.splits - 1) / sp.splits;
+  const int kb0 = split * bps, kb1 = min(nblk, kb0 + bps);
+  const int ntiles = (c.nvec + 15) / 16;
+
+  uint8_t* q_s = smem;                                   // 16 x ROW_BYTES
+  int* spos = reinterpret_cast<int*>(smem + BLOCK_BYTES);  // 16 ints (+pad)
+  uint8_t* buf = smem + BLOCK_BYTES + 256;               // K/V stages
+  const uint32_t buf_u = smem_u32(buf);
+
+  if (ntiles == 1) {
+    // ---------------------------------------------------------------- one tile, warps split blocks
+    load_q_tile(c, 0, q_s, tid, THREADS);
+    if (tid < 16) spos[tid] = tid < c.nvec ? rows.positions[c.r0 + tid / c.G] : -1;
+    __syncthreads();
+    TileState ts;
+    tile_init(ts, smem_u32(q_s), spos, lane);
+    const uint32_t wbuf = buf_u + warp * 4 * BLOCK_BYTES;  // [stage][K,V]
+    int kb = kb0 + warp;
+    long long blk = kb < kb1 ? block_id(c, kb, rows.block_table_stride) : -1;
+    if (blk >= 0) stage_block<INT8>(c, blk, wbuf, wbuf + BLOCK_BYTES, lane, 32);
+    cp_commit();
+    int stage = 0;
+    for (; kb < kb1; kb += 4) {
+      const int nkb = kb + 4;
+      long long nblk_id = nkb < kb1 ? block_id(c, nkb, rows.block_table_stride) : -1;
+      const uint32_t nxt = wbuf + (stage ^ 1) * 2 * BLOCK_BYTES;
+      if (nblk_id >= 0) stage_block<INT8>(c, nblk_id, nxt, nxt + BLOCK_BYTES, lane, 32);
+      cp_commit();
+      cp_wait<1>();
+      __syncwarp();
+      const uint32_t cur = wbuf + stage * 2 * BLOCK_BYTES;
+      if (blk >= 0) tile_block(ts, cur, cur + BLOCK_BYTES, kb, lane);
+      __syncwarp();
+      blk = nblk_id;
+      stage ^= 1;
+    }
+    cp_wait<0>();
+    // merge the four warps through smem (reusing the stage buffers)
+    __syncthreads();
+    float* mo = reinterpret_cast<float*>(buf);          // [4][16][128]
+    float* mm = mo + 4 * 16 * D;                        // [4][16]
+    float* ml = mm + 4 * 16;                            // [4][16]
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int row = (lane >> 2) + 8 * r;
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        const int d = 8 * t + 2 * (lane & 3);
+        mo[(warp * 16 + row) * D + d] = ts.o[t][2 * r];
+        mo[(warp * 16 + row) * D + d + 1] = ts.o[t][2 * r + 1];
+      }
+      if ((lane & 3) == 0) {
+        mm[warp * 16 + row] = ts.m[r];
+        ml[warp * 16 + row] = ts.l[r];
+      }
+    }
+    __syncthreads();
+    for (int v = 0; v < min(16, c.nvec); ++v) {
+      float m = NEG_INF;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) m = fmaxf(m, mm[w * 16 + v]);
+      float l = 0.f, o = 0.f;
+      if (m != NEG_INF) {
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const float mw = mm[w * 16 + v];
+          const float f = mw == NEG_INF ? 0.f : exp2f(mw - m);
+          l += ml[w * 16 + v] * f;
+          o += mo[(w * 16 + v) * D + tid] * f;
+        }
+      }
+      if (sp.splits == 1) {
+        const int row = c.r0 + v / c.G;
+        const int head = c.h * c.G + v % c.G;
+        out[((long long)row * nh + head) * D + tid] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
+      } else {
+        const long long base = (((long long)b * nkv + h) * sp.splits + split) * sp.max_vec + v;
+        sp.part_o[base * D + tid] = o;
+        if (tid == 0) {
+          sp.part_m[base] = m;
+          sp.part_l[base] = l;
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- many tiles, shared blocks
+    for (int t0 = 0; t0 < ntiles; t0 += 4) {
+      const int tile = t0 + warp;
+      __syncthreads();
+      // each warp stages its own query tile into its slot of the Q area (4 tiles)
+      uint8_t* my_q = buf + 4 * BLOCK_BYTES + warp * BLOCK_BYTES;
+      int* my_pos = spos;  // not used for positions here
+      (void)my_pos;
+      if (tile < ntiles) load_q_tile(c, tile * 16, my_q, lane, 32);
+      __syncwarp();
+      __shared__ int tpos[4][16];
+      if (lane < 16) {
+        const int v = tile * 16 + lane;
+        tpos[warp][lane] = (tile < ntiles && v < c.nvec) ? rows.positions[c.r0 + v / c.G] : -1;
+      }
+      __syncwarp();
+      TileState ts;
+      if (tile < ntiles) tile_init(ts, smem_u32(my_q), tpos[warp], lane);
+      // the last query row of this tile group bounds the blocks it needs
+      const int v_last = min(c.nvec, (t0 + 4) * 16) - 1;
+      const int grp_end = min(kb1, (rows.positions[c.r0 + v_last / c.G]) / 16 + 1);
+      long long blk = kb0 < grp_end ? block_id(c, kb0, rows.block_table_stride) : -1;
+      if (blk >= 0) stage_block<INT8>(c, blk, buf_u, buf_u + BLOCK_BYTES, tid, THREADS);
+      cp_commit();
+      int stage = 0;
+      for (int kb = kb0; kb < grp_end; ++kb) {
+        long long nb = kb + 1 < grp_end ? block_id(c, kb + 1, rows.block_table_stride) : -1;
+        const uint32_t nxt = buf_u + (stage ^ 1) * 2 * BLOCK_BYTES;
+        if (nb >= 0) stage_block<INT8>(c, nb, nxt, nxt + BLOCK_BYTES, tid, THREADS);
+        cp_commit();
+        cp_wait<1>();
+        __syncthreads();
+        const uint32_t cur = buf_u + stage * 2 * BLOCK_BYTES;
+        if (tile < ntiles && blk >= 0) tile_block(ts, cur, cur + BLOCK_BYTES, kb, lane);
+        __syncthreads();
+        blk = nb;
+        stage ^= 1;
+      }
+      cp_wait<0>();
+      if (tile < ntiles) tile_store(c, sp, ts, tile * 16, lane, b, split);
+    }
+  }
+}
+
+// Merge the split partials of every (entry, KV head): softmax-weighted sum in fp32, bf16 output.
+__global__ void __launch_bounds__(D) combine_kernel(const ne_rows rows, int nh, int nkv, AttnSplit sp,
+                                                    __nv_bfloat16* __restrict__ out) {
+  const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  const int ql = rows.q_len[b];
+  if (ql <= 0) return;
+  const int G = nh / nkv;
+  const int nvec = ql * G;
+  const int r0 = rows.q_start[b];
+  for (int v = 0; v < nvec && v < sp.max_vec; ++v) {
+    const long long base0 = (((long long)b * nkv + h) * sp.splits) * sp.max_vec + v;
+    float m = NEG_INF;
+    for (int s = 0; s < sp.splits; ++s) m = fmaxf(m, sp.part_m[base0 + (long long)s * sp.max_vec]);
+    float l = 0.f, o = 0.f;
+    if (m != NEG_INF) {
+      for (int s = 0; s < sp.splits; ++s) {
+        const long long base = base0 + (long long)s * sp.max_vec;
+        const float ms = sp.part_m[base];
+        const float f = ms == NEG_INF ? 0.f : exp2f(ms - m);
+        l += sp.part_l[base] * f;
+        o += sp.part_o[base * D + d] * f;
+      }
+    }
+    const int row = r0 + v / G;
+    const int head = h * G + v % G;
+    out[((long long)row * nh + head) * D + d] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
+  }
+}
+
+// Splits whose range holds no block must still publish an empty partial (max -inf, sum 0).
+__global__ void clear_partials_kernel(AttnSplit sp, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    sp.part_m[i] = NEG_INF;
+    sp.part_l[i] = 0.f;
+  }
+}
+
+}  // namespace
+
+size_t attention_smem_bytes() {
+  // Q tile + positions + max(4 warps x 2 stages x (K, V) blocks, the merge area, 2 shared stages + 4 Q tiles)
+  const size_t stages = 4 * 4 * BLOCK_BYTES;
+  const size_t merge = (4 * 16 * D + 2 * 4 * 16) * sizeof(float);
+  const size_t shared_mode = 4 * BLOCK_BYTES + 4 * BLOCK_BYTES;
+  size_t body = stages > merge ? stages : merge;
+  body = body > shared_mode ? body : shared_mode;
+  return BLOCK_BYTES + 256 + body;
+}
+
+int attention_plan_splits(int num_seqs, int nkv, int max_context, int max_vec, int num_sms, size_t partial_bytes) {
+  const int pairs = num_seqs * nkv;
+  int splits = (2 * num_sms + pairs - 1) / pairs;
+  const int max_blocks = (max_context + 15) / 16;
+  splits = splits < 1 ? 1 : splits;
+  splits = splits > max_blocks ? max_blocks : splits;
+  splits = splits > 32 ? 32 : splits;
+  if (splits > 1 && max_vec > 16) splits = 1;  // split-KV only for the one-tile (speculative) case
+  // the partials must fit the scratch area the caller gave
+  while (splits > 1 && (size_t)pairs * splits * max_vec * (D + 2) * sizeof(float) > partial_bytes) --splits;
+  return splits;
+}
+
+int launch_attention_tc(const __nv_bfloat16* q, __nv_bfloat16* out, const void* k_cache, const void* v_cache,
+                        const __nv_bfloat16* k_scale, const __nv_bfloat16* v_scale, int kv_int8, const ne_rows& rows,
+                        int num_heads, int num_kv_heads, long long num_cache_slots, const AttnSplit& sp, int* status,
+                        cudaStream_t stream) {
+  if (num_kv_heads <= 0 || num_heads % num_kv_heads || rows.num_seqs <= 0 || sp.splits < 1) return NE_ERR_INVALID;
+  if (sp.splits > 1 && (!sp.part_o || !sp.part_m || !sp.part_l || sp.max_vec < 1)) return NE_ERR_INVALID;
+  const size_t smem = attention_smem_bytes();
+  static bool attr_set[2] = {false, false};
+  auto kernel = kv_int8 ? attention_kernel<true> : attention_kernel<false>;
+  if (!attr_set[kv_int8 ? 1 : 0]) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return NE_ERR_CUDA;
+    attr_set[kv_int8 ? 1 : 0] = true;
+  }
+  if (sp.splits > 1) {
+    const long long n = (long long)rows.num_seqs * num_kv_heads * sp.splits * sp.max_vec;
+    clear_partials_kernel<<<(int)((n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024), 256, 0, stream>>>(sp, n);
+    if (cudaGetLastError() != cudaSuccess) return NE_ERR_CUDA;
+  }
+  dim3 grid(rows.num_seqs, num_kv_heads, sp.splits);
+  kernel<<<grid, THREADS, smem, stream>>>(q, out, k_cache, v_cache, k_scale, v_scale, rows, num_heads, num_kv_heads,
+                                         num_cache_slots, sp, status);
+  if (cudaGetLastError() != cudaSuccess) return NE_ERR_CUDA;
+  if (sp.splits > 1) {
+    combine_kernel<<<dim3(rows.num_seqs, num_kv_heads), D, 0, stream>>>(rows, num_heads, num_kv_heads, sp, out);
+    if (cudaGetLastError() != cudaSuccess) return NE_ERR_CUDA;
+  }
+  return NE_OK;
+}
+
+}  // namespace ne

@@ -6,6 +6,7 @@
 #include <new>
 #include <vector>
 
+#include "attention.cuh"
 #include "gemm_tc.cuh"
 #include "kernels.cuh"
 
@@ -26,6 +27,8 @@ struct ne_model {
   int32_t* status = nullptr;
   __nv_bfloat16 *h = nullptr, *x = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
   unsigned long long* keys = nullptr;
+  void* attn_scratch = nullptr;
+  size_t attn_scratch_bytes = 0;
   ne::RowBuffers rb{};
   CUtensorMap tm_x{}, tm_attn{}, tm_act{};
   int num_sms = 148;
@@ -45,8 +48,10 @@ namespace {
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
+constexpr size_t ATTN_SCRATCH_BYTES = 16u << 20;  // split-KV partials (few sequences, long contexts)
+
 struct Layout {
-  size_t status, h, x, q, attn, act, keys, rows_i32, seqs_i32, scalars, total;
+  size_t status, h, x, q, attn, act, keys, rows_i32, seqs_i32, scalars, attn_scratch, total;
 };
 
 Layout workspace_layout(const ne_model_config& c, int R, int B) {
@@ -68,6 +73,7 @@ Layout workspace_layout(const ne_model_config& c, int R, int B) {
   l.rows_i32 = take((size_t)R * 4 * 4);   // token_ids, positions, slot_mapping, lm_rows
   l.seqs_i32 = take((size_t)B * 4 * 4);   // q_start, q_len, lm_start, draft_len
   l.scalars = take(64);                   // num_rows, lm_count
+  l.attn_scratch = take(ATTN_SCRATCH_BYTES);
   l.total = off;
   return l;
 }
@@ -128,6 +134,7 @@ ne_rows make_step_rows(ne_model* m, const ne_batch_state* st, const int32_t* seq
   r.table_index = seq_slot;
   r.block_table_stride = st->block_table_stride;
   r.max_context = st->history_stride;
+  r.max_q_len = max_rows;
   r.lm_rows = m->rb.lm_rows;
   r.lm_count = m->rb.lm_count;
   r.lm_max = lm_max;
@@ -254,6 +261,8 @@ int ne_model_set_workspace(ne_model* m, void* ws, size_t bytes, int max_rows, in
   int32_t* sc = reinterpret_cast<int32_t*>(base + l.scalars);
   m->rb.num_rows = sc;
   m->rb.lm_count = sc + 1;
+  m->attn_scratch = base + l.attn_scratch;
+  m->attn_scratch_bytes = ATTN_SCRATCH_BYTES;
   const int qs = c.num_heads * 128;
   bool ok = ne::make_tmap_bf16(&m->tm_x, m->x, max_rows, c.hidden_size, ne::GEMM_XBOX, ne::GEMM_BK) &&
             ne::make_tmap_bf16(&m->tm_attn, m->attn, max_rows, qs, ne::GEMM_XBOX, ne::GEMM_BK) &&
@@ -279,6 +288,12 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
   int rc = note(m, NE_K_EMBED,
                 ne::launch_embed(embed, rows->token_ids, rows->num_rows, R, H, c.vocab_size, m->h, m->status, s), s);
   if (rc) return rc;
+  const int group = c.num_heads / c.num_kv_heads;
+  const int max_vec = std::max(1, rows->max_q_len) * group;
+  const int splits = ne::attention_plan_splits(rows->num_seqs, c.num_kv_heads, rows->max_context, max_vec,
+                                               m->num_sms, m->attn_scratch_bytes);
+  const ne::AttnSplit attn = ne::attention_split_view(m->attn_scratch, (long long)rows->num_seqs * c.num_kv_heads,
+                                                      splits, max_vec);
   for (int l = 0; l < c.num_layers; ++l) {
     const ne_layer_weights& w = m->layers[l];
     rc = note(m, NE_K_RMSNORM,
@@ -308,9 +323,10 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
     rc = note(m, NE_K_GEMM_QKV, run_gemm(m, &m->tm_qkv[l], &m->tm_x, R, rows->num_rows, qs + 2 * kvs, H, e, s), s);
     if (rc) return rc;
     rc = note(m, NE_K_ATTENTION,
-              ne::launch_attention(m->q, m->attn, w.k_cache, w.v_cache, static_cast<const __nv_bfloat16*>(w.k_scale),
-                                   static_cast<const __nv_bfloat16*>(w.v_scale), c.kv_int8, *rows, c.num_heads,
-                                   c.num_kv_heads, c.block_size, c.num_cache_slots, m->status, s), s);
+              ne::launch_attention_tc(m->q, m->attn, w.k_cache, w.v_cache,
+                                      static_cast<const __nv_bfloat16*>(w.k_scale),
+                                      static_cast<const __nv_bfloat16*>(w.v_scale), c.kv_int8, *rows, c.num_heads,
+                                      c.num_kv_heads, c.num_cache_slots, attn, m->status, s), s);
     if (rc) return rc;
     ne::Epilogue eo{};
     eo.mode = ne::EPI_RESIDUAL;
@@ -471,14 +487,22 @@ int ne_gemm_bf16(const void* x, const void* w, void* y, int M, int N, int K, int
 
 int ne_paged_attention(const void* q, void* out, const void* k_cache, const void* v_cache, const void* k_scale,
                        const void* v_scale, int kv_int8, const ne_rows* rows, int num_heads, int num_kv_heads,
-                       int block_size, long long num_cache_slots, int32_t* status, void* stream) {
-  if (!q || !out || !k_cache || !v_cache || !rows || (kv_int8 && (!k_scale || !v_scale)) || num_cache_slots < 2)
+                       int block_size, long long num_cache_slots, void* scratch, size_t scratch_bytes, int32_t* status,
+                       void* stream) {
+  if (!q || !out || !k_cache || !v_cache || !rows || (kv_int8 && (!k_scale || !v_scale)) || num_cache_slots < 2 ||
+      block_size != 16 || num_kv_heads <= 0 || num_heads % num_kv_heads || rows->num_seqs <= 0)
     return NE_ERR_INVALID;
-  const long long slots = num_cache_slots;
-  return ne::launch_attention(static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(out), k_cache,
-                              v_cache, static_cast<const __nv_bfloat16*>(k_scale),
-                              static_cast<const __nv_bfloat16*>(v_scale), kv_int8, *rows, num_heads, num_kv_heads,
-                              block_size, slots, status, as_stream(stream));
+  if (scratch && (reinterpret_cast<uintptr_t>(scratch) & 255u)) return NE_ERR_INVALID;
+  const int max_vec = std::max(1, rows->max_q_len) * (num_heads / num_kv_heads);
+  const int splits = scratch ? ne::attention_plan_splits(rows->num_seqs, num_kv_heads, rows->max_context, max_vec,
+                                                         sm_count(), scratch_bytes)
+                             : 1;
+  const ne::AttnSplit sp =
+      ne::attention_split_view(scratch, (long long)rows->num_seqs * num_kv_heads, splits, max_vec);
+  return ne::launch_attention_tc(static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(out), k_cache,
+                                 v_cache, static_cast<const __nv_bfloat16*>(k_scale),
+                                 static_cast<const __nv_bfloat16*>(v_scale), kv_int8, *rows, num_heads, num_kv_heads,
+                                 num_cache_slots, sp, status, as_stream(stream));
 }
 
 int ne_rmsnorm(const void* x, const void* w, void* y, int rows, int hidden, float eps, void* stream) {

@@ -7,16 +7,9 @@ namespace ne {
 
 namespace {
 
-#define kNegInf (-__int_as_float(0x7f800000))
-
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
-  return v;
-}
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
   return v;
 }
 
@@ -73,145 +66,6 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_b
     yr[i] = o;
   }
   if (zero_keys && lane == 0) zero_keys[row] = 0ull;
-}
-
-// ------------------------------------------------------------------ paged verify attention
-// One CTA per (batch entry, KV head). Query vectors of the entry's rows x the KV head's query-head
-// group go in tiles of 16; keys/values stream block by block straight from the paged pool through
-// the block table (no gathered copy), with an online softmax in fp32.
-constexpr int ATT_THREADS = 128;
-constexpr int ATT_QT = 16;
-constexpr int ATT_D = 128;
-constexpr float ATT_SCALE = 0.08838834764831845f;  // 1 / sqrt(128)
-
-__global__ void __launch_bounds__(ATT_THREADS)
-    paged_attention_kernel(const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out,
-                           const void* __restrict__ k_cache, const void* __restrict__ v_cache,
-                           const __nv_bfloat16* __restrict__ k_scale, const __nv_bfloat16* __restrict__ v_scale,
-                           int kv_int8, ne_rows rows, int nh, int nkv, int bs, long long num_cache_slots,
-                           int* status) {
-  const int b = blockIdx.x;
-  const int h = blockIdx.y;
-  const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const int warp = tid >> 5;
-  const int ql = rows.q_len[b];
-  if (ql <= 0) return;
-  const int r0 = rows.q_start[b];
-  const int G = nh / nkv;
-  const int trow = rows.table_index ? rows.table_index[b] : b;
-  const int32_t* table = rows.block_tables + (long long)trow * rows.block_table_stride;
-
-  __shared__ float sq[ATT_QT][ATT_D];
-  __shared__ float sk[16][ATT_D + 1];
-  __shared__ float sv[16][ATT_D];
-  __shared__ float sp[ATT_QT][17];
-  __shared__ int spos[ATT_QT];
-  __shared__ float sm[ATT_QT], sl[ATT_QT], scorr[ATT_QT];
-
-  const int nvec = ql * G;
-  for (int vt = 0; vt < nvec; vt += ATT_QT) {
-    const int nv = min(ATT_QT, nvec - vt);
-    for (int idx = tid; idx < ATT_QT * ATT_D; idx += ATT_THREADS) {
-      const int v = idx / ATT_D, d = idx % ATT_D;
-      float val = 0.f;
-      if (v < nv) {
-        const int row = r0 + (vt + v) / G;
-        const int head = h * G + (vt + v) % G;
-        val = __bfloat162float(q[((long long)row * nh + head) * ATT_D + d]);
-      }
-      sq[v][d] = val;
-    }
-    if (tid < ATT_QT) {
-      spos[tid] = tid < nv ? rows.positions[r0 + (vt + tid) / G] : -1;
-      sm[tid] = kNegInf;
-      sl[tid] = 0.f;
-    }
-    float acc[ATT_QT];
-#pragma unroll
-    for (int v = 0; v < ATT_QT; ++v) acc[v] = 0.f;
-    __syncthreads();
-    int ctx_end = 0;
-    for (int v = 0; v < nv; ++v) ctx_end = max(ctx_end, spos[v] + 1);
-    const int nblk = (ctx_end + bs - 1) / bs;
-    for (int kb = 0; kb < nblk; ++kb) {
-      bool valid = kb < rows.block_table_stride;
-      long long blk = valid ? table[kb] : -1;
-      valid = valid && blk >= 0 && (blk + 1) * bs <= num_cache_slots - 1;
-      if (!valid && tid == 0) report(status, NE_DEV_BAD_SLOT);
-      for (int idx = tid; idx < 16 * ATT_D; idx += ATT_THREADS) {
-        const int t = idx / ATT_D, d = idx % ATT_D;
-        float kv = 0.f, vv = 0.f;
-        if (valid && t < bs) {
-          const long long slot = blk * bs + t;
-          const long long off = (slot * nkv + h) * ATT_D + d;
-          if (!kv_int8) {
-            kv = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(k_cache)[off]);
-            vv = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(v_cache)[off]);
-          } else {
-            // read_from_cache (attention_context.py:57-63): int8 -> bf16, times the bf16 scale
-            const float ksc = __bfloat162float(k_scale[slot * nkv + h]);
-            const float vsc = __bfloat162float(v_scale[slot * nkv + h]);
-            kv = bf16r((float)reinterpret_cast<const int8_t*>(k_cache)[off] * ksc);
-            vv = bf16r((float)reinterpret_cast<const int8_t*>(v_cache)[off] * vsc);
-          }
-        }
-        sk[t][d] = kv;
-        sv[t][d] = vv;
-      }
-      __syncthreads();
-      for (int p = tid; p < ATT_QT * 16; p += ATT_THREADS) {
-        const int v = p / 16, t = p % 16;
-        float s = kNegInf;
-        if (valid && v < nv && t < bs && kb * bs + t <= spos[v]) {
-          float dot = 0.f;
-#pragma unroll 8
-          for (int d = 0; d < ATT_D; ++d) dot += sq[v][d] * sk[t][d];
-          s = dot * ATT_SCALE;
-        }
-        sp[v][t] = s;
-      }
-      __syncthreads();
-      for (int v = warp; v < ATT_QT; v += ATT_THREADS / 32) {
-        const float s = lane < 16 ? sp[v][lane] : kNegInf;
-        const float mx = warp_max(s);
-        const float m_old = sm[v];
-        const float m_new = fmaxf(m_old, mx);
-        float p = 0.f, corr = 1.f;
-        if (m_new != kNegInf) {
-          p = s == kNegInf ? 0.f : expf(s - m_new);
-          corr = m_old == kNegInf ? 0.f : expf(m_old - m_new);
-        }
-        const float psum = warp_sum(p);
-        __syncwarp();
-        if (lane < 16) sp[v][lane] = p;
-        if (lane == 0) {
-          sm[v] = m_new;
-          sl[v] = sl[v] * corr + psum;
-          scorr[v] = corr;
-        }
-      }
-      __syncthreads();
-#pragma unroll
-      for (int v = 0; v < ATT_QT; ++v) {
-        float a = acc[v] * scorr[v];
-#pragma unroll
-        for (int t = 0; t < 16; ++t) a += sp[v][t] * sv[t][tid];
-        acc[v] = a;
-      }
-      __syncthreads();
-    }
-#pragma unroll
-    for (int v = 0; v < ATT_QT; ++v) {
-      if (v < nv) {
-        const int row = r0 + (vt + v) / G;
-        const int head = h * G + (vt + v) % G;
-        const float l = sl[v];
-        out[((long long)row * nh + head) * ATT_D + tid] = __float2bfloat16_rn(l > 0.f ? acc[v] / l : 0.f);
-      }
-    }
-    __syncthreads();
-  }
 }
 
 __global__ void keys_to_ids_kernel(const unsigned long long* keys, const int32_t* count, int max_count,
@@ -515,18 +369,6 @@ int launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16
   const int blocks = (max_rows + 3) / 4;
   if (blocks == 0) return NE_OK;
   rmsnorm_kernel<<<blocks, 128, 0, stream>>>(x, w, y, max_rows, rows_dev, gather, hidden, eps, zero_keys);
-  return check_launch();
-}
-
-int launch_attention(const __nv_bfloat16* q, __nv_bfloat16* out, const void* k_cache, const void* v_cache,
-                     const __nv_bfloat16* k_scale, const __nv_bfloat16* v_scale, int kv_int8, const ne_rows& rows,
-                     int num_heads, int num_kv_heads, int block_size, long long num_cache_slots, int* status,
-                     cudaStream_t stream) {
-  if (num_kv_heads <= 0 || num_heads % num_kv_heads || block_size > 16 || rows.num_seqs <= 0) return NE_ERR_INVALID;
-  dim3 grid(rows.num_seqs, num_kv_heads);
-  paged_attention_kernel<<<grid, ATT_THREADS, 0, stream>>>(q, out, k_cache, v_cache, k_scale, v_scale, kv_int8, rows,
-                                                          num_heads, num_kv_heads, block_size, num_cache_slots,
-                                                          status);
   return check_launch();
 }
 

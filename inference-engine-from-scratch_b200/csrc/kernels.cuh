@@ -26,10 +26,6 @@ int launch_embed(const __nv_bfloat16* embed, const int32_t* tokens, const int32_
 int launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int max_rows,
                    const int32_t* rows_dev, const int32_t* gather, int hidden, float eps,
                    unsigned long long* zero_keys, cudaStream_t stream);
-int launch_attention(const __nv_bfloat16* q, __nv_bfloat16* out, const void* k_cache, const void* v_cache,
-                     const __nv_bfloat16* k_scale, const __nv_bfloat16* v_scale, int kv_int8, const ne_rows& rows,
-                     int num_heads, int num_kv_heads, int block_size, long long num_cache_slots, int* status,
-                     cudaStream_t stream);
 int launch_keys_to_ids(const unsigned long long* keys, const int32_t* count, int max_count, int32_t* ids,
                        cudaStream_t stream);
 int launch_ngram(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int k, int max_ngram,

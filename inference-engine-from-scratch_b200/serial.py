@@ -197,7 +197,7 @@ class _HostRows:
             max_rows=max(n, 1), num_seqs=1, num_rows=base + 4 * meta, token_ids=base, positions=base + 4 * R,
             slot_mapping=base + 8 * R, q_start=base + 4 * (meta + 2), q_len=base + 4 * (meta + 3),
             block_tables=base + 4 * (meta + 4), table_index=None, block_table_stride=T, max_context=T * 16,
-            lm_rows=base + 12 * R, lm_count=base + 4 * (meta + 1), lm_max=max(nl, 1),
+            max_q_len=max(n, 1), lm_rows=base + 12 * R, lm_count=base + 4 * (meta + 1), lm_max=max(nl, 1),
         )
 
 

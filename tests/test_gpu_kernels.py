@@ -95,7 +95,7 @@ def test_ngram_kernel_is_bit_exact_on_the_reference_cases(lib, cuda_device) -> N
             assert got == case["expected"], case
 
 
-def _attention_reference(q, k_cache, v_cache, tables, q_start, q_len, positions, nh, nkv):
+def _attention_reference(q, k_cache, v_cache, tables, q_start, q_len, positions, nh, nkv, k_scale=None, v_scale=None):
     out = torch.zeros_like(q, dtype=torch.float32)
     G = nh // nkv
     for b in range(len(q_len)):
@@ -103,8 +103,11 @@ def _attention_reference(q, k_cache, v_cache, tables, q_start, q_len, positions,
             row = q_start[b] + j
             pos = positions[row]
             slots = [tables[b][p // 16] * 16 + p % 16 for p in range(pos + 1)]
-            keys = k_cache[slots].float()  # [c, nkv, d]
-            vals = v_cache[slots].float()
+            if k_scale is None:
+                keys, vals = k_cache[slots].float(), v_cache[slots].float()
+            else:  # read_from_cache: int8 -> bf16 times the bf16 scale, in bf16
+                keys = (k_cache[slots].to(torch.bfloat16) * k_scale[slots]).float()
+                vals = (v_cache[slots].to(torch.bfloat16) * v_scale[slots]).float()
             for head in range(nh):
                 kv = head // G
                 s = (keys[:, kv, :] @ q[row, head].float()) / (128 ** 0.5)
@@ -113,17 +116,33 @@ def _attention_reference(q, k_cache, v_cache, tables, q_start, q_len, positions,
     return out
 
 
-@pytest.mark.parametrize("nh,nkv,q_lens,ctx", [(16, 8, [5, 1, 3], [69, 16, 200]), (32, 8, [9, 2], [40, 17]),
-                                               (4, 2, [64], [64])])
-def test_paged_attention_matches_fp32_reference(lib, cuda_device, nh, nkv, q_lens, ctx) -> None:
-    g = torch.Generator().manual_seed(sum(ctx))
-    num_blocks = 64
-    k_cache = torch.randn(num_blocks * 16 + 1, nkv, 128, generator=g).to(torch.bfloat16)
-    v_cache = torch.randn(num_blocks * 16 + 1, nkv, 128, generator=g).to(torch.bfloat16)
+ATTENTION_CASES = [
+    # (nh, nkv, q_lens, contexts, scratch MB): speculative rows, prefill-like rows, split-KV
+    (16, 8, [5, 1, 3], [69, 16, 200], 0),
+    (16, 8, [5, 2], [333, 90], 8),
+    (32, 8, [9, 2], [40, 17], 0),
+    (32, 8, [5], [700], 8),
+    (4, 2, [64], [64], 0),
+    (16, 8, [40, 3], [40, 130], 0),
+]
+
+
+@pytest.mark.parametrize("nh,nkv,q_lens,ctx,scratch_mb", ATTENTION_CASES)
+@pytest.mark.parametrize("kv_int8", [False, True])
+def test_paged_attention_matches_fp32_reference(lib, cuda_device, nh, nkv, q_lens, ctx, scratch_mb, kv_int8) -> None:
+    g = torch.Generator().manual_seed(sum(ctx) + kv_int8)
+    num_blocks = 96
+    shape = (num_blocks * 16 + 1, nkv, 128)
+    k_cache = torch.randn(shape, generator=g).to(torch.bfloat16)
+    v_cache = torch.randn(shape, generator=g).to(torch.bfloat16)
+    k_scale = v_scale = None
+    if kv_int8:
+        k_cache, k_scale = oq.quantize_vectors(k_cache)
+        v_cache, v_scale = oq.quantize_vectors(v_cache)
     perm = torch.randperm(num_blocks, generator=g).tolist()
     tables, q_start, positions = [], [], []
     row = 0
-    for b, (ql, c) in enumerate(zip(q_lens, ctx)):
+    for ql, c in zip(q_lens, ctx):
         nb = (c + 15) // 16
         tables.append(perm[:nb])
         perm = perm[nb:]
@@ -137,20 +156,28 @@ def test_paged_attention_matches_fp32_reference(lib, cuda_device, nh, nkv, q_len
     for b, t in enumerate(tables):
         table_t[b, :len(t)] = torch.tensor(t)
     dev = cuda_device
-    dq, dk, dv = q.to(dev), k_cache.to(dev), v_cache.to(dev)
     out = torch.zeros(M, nh, 128, dtype=torch.bfloat16, device=dev)
     i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)  # noqa: E731
     t_qs, t_ql, t_pos, t_tab = i32(q_start), i32(q_lens), i32(positions), table_t.to(dev)
     rows = submodule("_lib").Rows(
         max_rows=M, num_seqs=len(q_lens), num_rows=None, token_ids=None, positions=t_pos.data_ptr(),
         slot_mapping=None, q_start=t_qs.data_ptr(), q_len=t_ql.data_ptr(), block_tables=t_tab.data_ptr(),
-        table_index=None, block_table_stride=stride, max_context=stride * 16, lm_rows=None, lm_count=None, lm_max=0,
+        table_index=None, block_table_stride=stride, max_context=stride * 16, max_q_len=max(q_lens), lm_rows=None,
+        lm_count=None, lm_max=0,
     )
     status = torch.zeros(1, dtype=torch.int32, device=dev)
-    rc = lib.ne_paged_attention(dq.data_ptr(), out.data_ptr(), dk.data_ptr(), dv.data_ptr(), None, None, 0,
-                                ctypes.byref(rows), nh, nkv, 16, num_blocks * 16 + 1, status.data_ptr(), _stream())
+    scratch = torch.empty(scratch_mb << 20, dtype=torch.uint8, device=dev) if scratch_mb else None
+    dk, dv = k_cache.to(dev), v_cache.to(dev)
+    dks = k_scale.squeeze(-1).contiguous().to(dev) if kv_int8 else None
+    dvs = v_scale.squeeze(-1).contiguous().to(dev) if kv_int8 else None
+    rc = lib.ne_paged_attention(q.to(dev).data_ptr(), out.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                                dks.data_ptr() if kv_int8 else None, dvs.data_ptr() if kv_int8 else None,
+                                int(kv_int8), ctypes.byref(rows), nh, nkv, 16, num_blocks * 16 + 1,
+                                scratch.data_ptr() if scratch is not None else None, scratch_mb << 20,
+                                status.data_ptr(), _stream())
     assert rc == 0
     torch.cuda.synchronize()
     assert int(status.item()) == 0
-    want = _attention_reference(q, k_cache, v_cache, tables, q_start, q_lens, positions, nh, nkv)
-    torch.testing.assert_close(out.cpu().float(), want, rtol=1e-2, atol=1e-2)
+    want = _attention_reference(q, k_cache, v_cache, tables, q_start, q_lens, positions, nh, nkv, k_scale, v_scale)
+    # P is rounded to bf16 before the PV product (as flash attention does); outputs are bf16
+    torch.testing.assert_close(out.cpu().float(), want, rtol=2e-2, atol=2e-2)
