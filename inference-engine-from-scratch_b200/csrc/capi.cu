@@ -120,7 +120,7 @@ int run_gemm(ne_model* m, const CUtensorMap* tw, const CUtensorMap* tx, int M_ma
 }
 
 ne_rows make_step_rows(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int max_rows,
-                       int lm_max) {
+                       int lm_max, int max_q_len) {
   ne_rows r{};
   r.max_rows = max_rows;
   r.num_seqs = num_seqs;
@@ -134,7 +134,7 @@ ne_rows make_step_rows(ne_model* m, const ne_batch_state* st, const int32_t* seq
   r.table_index = seq_slot;
   r.block_table_stride = st->block_table_stride;
   r.max_context = st->history_stride;
-  r.max_q_len = max_rows;
+  r.max_q_len = max_q_len;
   r.lm_rows = m->rb.lm_rows;
   r.lm_count = m->rb.lm_count;
   r.lm_max = lm_max;
@@ -434,7 +434,7 @@ int ne_prefill(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, i
                 ne::launch_plan(*st, seq_slot, num_seqs, ne::PLAN_PREFILL, max_rows, m->cfg.block_size,
                                 m->cfg.num_cache_slots, m->rb, m->status, s), s);
   if (rc) return rc;
-  ne_rows rows = make_step_rows(m, st, seq_slot, num_seqs, max_rows, num_seqs);
+  ne_rows rows = make_step_rows(m, st, seq_slot, num_seqs, max_rows, num_seqs, max_rows);
   rc = ne_forward(m, &rows, NE_LM_ARGMAX, nullptr, nullptr, stream);
   if (rc) return rc;
   return note(m, NE_K_ACCEPT,
@@ -455,7 +455,7 @@ int ne_spec_step(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot,
             ne::launch_plan(*st, seq_slot, num_seqs, ne::PLAN_SPEC, max_rows, m->cfg.block_size,
                             m->cfg.num_cache_slots, m->rb, m->status, s), s);
   if (rc) return rc;
-  ne_rows rows = make_step_rows(m, st, seq_slot, num_seqs, max_rows, max_rows);
+  ne_rows rows = make_step_rows(m, st, seq_slot, num_seqs, max_rows, max_rows, k + 1);
   rc = ne_forward(m, &rows, NE_LM_ARGMAX, nullptr, nullptr, stream);
   if (rc) return rc;
   return note(m, NE_K_ACCEPT,
