@@ -279,6 +279,25 @@ NE_API int ne_paged_attention(const void* q, void* out, const void* k_cache, con
                               int block_size, long long num_cache_slots, void* scratch, size_t scratch_bytes,
                               int32_t* status, void* stream);
 
+/*
+ * ne_paged_attention for callers that cannot allocate device memory: a host framework whose
+ * caching allocator has reserved the device's memory up front and forbids foreign allocations, or
+ * code that must not call cudaMalloc at all once it is running. This entry allocates nothing: its
+ * split-KV partials live in a fixed 4 MiB array compiled into the library, which every GPU that
+ * loads the library holds until the process exits. ``splits`` KV splits are used (1 = none); a
+ * call whose partials (num_seqs x num_kv_heads x splits x max_q_len x G x 520 bytes) exceed 4 MiB,
+ * or that asks for splits with more than 16 query vectors per sequence, returns NE_ERR_WORKSPACE /
+ * NE_ERR_INVALID and launches nothing. The first call on each device looks up the array's device
+ * address (make that first call before any stream capture). All calls on one device share that
+ * device's array, which keeps the last call's contents: calls that can run at the same time on one
+ * device (on different streams) race on it, so issue them on one stream. There is no counterpart
+ * in the reference, which allocates through PyTorch.
+ */
+NE_API int ne_paged_attention_static_scratch(const void* q, void* out, const void* k_cache, const void* v_cache,
+                                             const void* k_scale, const void* v_scale, int kv_int8,
+                                             const ne_rows* rows, int num_heads, int num_kv_heads, int block_size,
+                                             long long num_cache_slots, int splits, int32_t* status, void* stream);
+
 /* RMSNorm rows (models/qwen3.py:39-44): y = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w). */
 NE_API int ne_rmsnorm(const void* x, const void* w, void* y, int rows, int hidden, float eps, void* stream);
 

@@ -50,6 +50,11 @@ EXPORTS = {
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int,
          c_longlong, c_void_p, c_size_t, c_void_p, c_void_p],
     ),
+    "ne_paged_attention_static_scratch": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int,
+         c_longlong, c_int, c_void_p, c_void_p],
+    ),
     "ne_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p]),
     "ne_model_launch_count": (c_longlong, [c_void_p]),
     "ne_model_profile_begin": (c_int, [c_void_p, c_void_p]),
