@@ -273,6 +273,7 @@ __global__ void __launch_bounds__(THREADS)
                      const void* __restrict__ vc, const __nv_bfloat16* __restrict__ ks,
                      const __nv_bfloat16* __restrict__ vs, ne_rows rows, int nh, int nkv, long long num_cache_slots,
                      AttnSplit sp, int* status) {
+  pdl_prologue();
   extern __shared__ __align__(16) uint8_t smem[];
   const int b = blockIdx.x, h = blockIdx.y, split = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -428,6 +429,7 @@ __global__ void __launch_bounds__(THREADS)
 // Merge the split partials of every (entry, KV head): softmax-weighted sum in fp32, bf16 output.
 __global__ void __launch_bounds__(D) combine_kernel(const ne_rows rows, int nh, int nkv, AttnSplit sp,
                                                     __nv_bfloat16* __restrict__ out) {
+  pdl_prologue();
   const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const int ql = rows.q_len[b];
   if (ql <= 0) return;
@@ -456,6 +458,7 @@ __global__ void __launch_bounds__(D) combine_kernel(const ne_rows rows, int nh, 
 
 // Splits whose range holds no block must still publish an empty partial (max -inf, sum 0).
 __global__ void clear_partials_kernel(AttnSplit sp, long long n) {
+  pdl_prologue();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     sp.part_m[i] = NEG_INF;
     sp.part_l[i] = 0.f;
@@ -503,16 +506,18 @@ int launch_attention_tc(const __nv_bfloat16* q, __nv_bfloat16* out, const void* 
   }
   if (sp.splits > 1) {
     const long long n = (long long)rows.num_seqs * num_kv_heads * sp.splits * sp.max_vec;
-    clear_partials_kernel<<<(int)((n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024), 256, 0, stream>>>(sp, n);
-    if (cudaGetLastError() != cudaSuccess) return NE_ERR_CUDA;
+    const int blocks = (int)((n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024);
+    if (launch_kernel(clear_partials_kernel, dim3(blocks), dim3(256), 0, stream, sp, n) != cudaSuccess)
+      return NE_ERR_CUDA;
   }
   dim3 grid(rows.num_seqs, num_kv_heads, sp.splits);
-  kernel<<<grid, THREADS, smem, stream>>>(q, out, k_cache, v_cache, k_scale, v_scale, rows, num_heads, num_kv_heads,
-                                         num_cache_slots, sp, status);
-  if (cudaGetLastError() != cudaSuccess) return NE_ERR_CUDA;
+  if (launch_kernel(kernel, grid, dim3(THREADS), smem, stream, q, out, k_cache, v_cache, k_scale, v_scale, rows,
+                    num_heads, num_kv_heads, num_cache_slots, sp, status) != cudaSuccess)
+    return NE_ERR_CUDA;
   if (sp.splits > 1) {
-    combine_kernel<<<dim3(rows.num_seqs, num_kv_heads), D, 0, stream>>>(rows, num_heads, num_kv_heads, sp, out);
-    if (cudaGetLastError() != cudaSuccess) return NE_ERR_CUDA;
+    if (launch_kernel(combine_kernel, dim3(rows.num_seqs, num_kv_heads), dim3(D), 0, stream, rows, num_heads,
+                      num_kv_heads, sp, out) != cudaSuccess)
+      return NE_ERR_CUDA;
   }
   return NE_OK;
 }

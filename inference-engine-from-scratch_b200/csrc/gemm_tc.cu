@@ -181,14 +181,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int tile_n = blockIdx.y;
   const int m0 = blockIdx.z * p.t_block;
 
-  const int M = p.M_dev ? min(*p.M_dev, p.M_max) : p.M_max;
-  const int t_actual = min(p.t_block, M - m0);
-  if (t_actual <= 0) return;  // the whole cluster shares this m-block: all CTAs leave together
-
-  const int n_loads = (t_actual + GEMM_XBOX - 1) / GEMM_XBOX;
-  const int n_pad = (t_actual + 15) & ~15;
-  const int part0 = n_pad < 256 ? n_pad : 256;
-  const int part1 = n_pad - part0;
   const int num_chunks = p.K / GEMM_BK;
   const int cps = (num_chunks + S - 1) / S;
   const int k_begin = split * cps;
@@ -198,7 +190,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int stage_bytes = w_bytes + ((p.t_block + GEMM_XBOX - 1) / GEMM_XBOX) * GEMM_XBOX * GEMM_BK * 2;
   const int stages = p.stages;
   // barriers sit past every region the pipeline or the epilogue staging can touch
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + GEMM_SMEM_DATA_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.smem_data);
   uint64_t* empty = full + stages;
   uint64_t* done = empty + stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
@@ -208,6 +200,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const uint32_t tmem_cols = p.t_block <= 32 ? 32 : p.t_block <= 64 ? 64 : p.t_block <= 128 ? 128
                              : p.t_block <= 256 ? 256 : 512;
 
+  pdl_trigger();
   if (tid == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
@@ -229,16 +222,58 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  int issued = 0;
+  // Weights do not depend on the previous kernel: stream the first stages' weight tiles before
+  // waiting for it. Their barriers get no arrival yet, so the phase cannot complete before the
+  // activation tile's bytes are added below.
+  const int pre = min(stages, nk);
+  if (warp == 0 && lane == 0) {
+    for (int i = 0; i < pre; ++i) {
+      mbar_expect_tx(&full[i], (uint32_t)w_bytes);
+      tma_load_2d(smem + i * stage_bytes, &tm_w, &full[i], (k_begin + i) * GEMM_BK, tile_n * GEMM_BM);
+    }
+  }
+  pdl_wait();
+
+  const int M = p.M_dev ? min(*p.M_dev, p.M_max) : p.M_max;
+  const int t_actual = min(p.t_block, M - m0);
+  int issued = pre;
+  if (t_actual <= 0) {
+    // no rows for this m-block (the whole cluster shares it): retire the prefetched weight copies
+    if (warp == 0 && lane == 0) {
+      for (int i = 0; i < pre; ++i) mbar_arrive(&full[i]);
+      for (int i = 0; i < pre; ++i) mbar_wait(&full[i], 0, nullptr, p.status);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 2) {
+      tc_fence_after();
+      tmem_dealloc(tmem_base, tmem_cols);
+    }
+    return;
+  }
+
+  const int n_loads = (t_actual + GEMM_XBOX - 1) / GEMM_XBOX;
+  const int n_pad = (t_actual + 15) & ~15;
+  const int part0 = n_pad < 256 ? n_pad : 256;
+  const int part1 = n_pad - part0;
+  const uint32_t x_bytes = (uint32_t)(n_loads * GEMM_XBOX * GEMM_BK * 2);
+
   if (warp == 0) {
     if (lane == 0) {
-      const uint32_t tx = (uint32_t)(w_bytes + n_loads * GEMM_XBOX * GEMM_BK * 2);
-      for (int i = 0; i < nk; ++i) {
+      for (int i = 0; i < pre; ++i) {
+        uint8_t* st = smem + i * stage_bytes;
+        mbar_expect_tx(&full[i], x_bytes);
+        for (int l = 0; l < n_loads; ++l)
+          tma_load_2d(st + w_bytes + l * GEMM_XBOX * GEMM_BK * 2, &tm_x, &full[i], (k_begin + i) * GEMM_BK,
+                      m0 + l * GEMM_XBOX);
+        mbar_arrive(&full[i]);
+      }
+      for (int i = pre; i < nk; ++i) {
         const int s = i % stages;
         const uint32_t round = (uint32_t)(i / stages);
         if (!mbar_wait(&empty[s], (round & 1u) ^ 1u, abort_flag, p.status)) break;
         uint8_t* st = smem + s * stage_bytes;
-        mbar_arrive_expect_tx(&full[s], tx);
+        mbar_arrive_expect_tx(&full[s], (uint32_t)w_bytes + x_bytes);
         const int kx = (k_begin + i) * GEMM_BK;
         tma_load_2d(st, &tm_w, &full[s], kx, tile_n * GEMM_BM);
         for (int l = 0; l < n_loads; ++l)
@@ -415,11 +450,23 @@ int gemm_plan(GemmParams& p, int num_sms) {
   }
   if (S > 1 && !fits(S, t_block)) S = 1;
   const int stage_bytes = GEMM_BM * GEMM_BK * 2 + ((t_block + GEMM_XBOX - 1) / GEMM_XBOX) * GEMM_XBOX * GEMM_BK * 2;
-  int stages = std::min(8, avail / stage_bytes);
-  if (stages < 2) return NE_ERR_INVALID;
+  const int cps = (num_chunks + S - 1) / S;
+  int stages = std::min(std::min(GEMM_MAX_STAGES, cps), avail / stage_bytes);
+  if (stages < 1) return NE_ERR_INVALID;
+  const int staging = S == 1 ? 128 * GEMM_BM * 4 : (t_block + (t_block + S - 1) / S) * GEMM_BM * 4;
+  int data = std::max(stages * stage_bytes, staging);
+  // Never let more CTAs share an SM than its 512 TMEM columns can hold: CTAs of one cluster that
+  // landed on one SM would otherwise wait on each other (one in tcgen05.alloc, the rest at the
+  // cluster barrier). The shared memory request caps the CTAs per SM (228 KB per SM).
+  const int tmem_cols = t_block <= 32 ? 32 : t_block <= 64 ? 64 : t_block <= 128 ? 128 : t_block <= 256 ? 256 : 512;
+  const int max_ctas = 512 / tmem_cols;
+  const int min_total = 228 * 1024 / (max_ctas + 1) + 1024;
+  data = std::max(data, min_total - 1280);
+  if (data > avail) return NE_ERR_INVALID;
   p.t_block = t_block;
   p.splits = S;
   p.stages = stages;
+  p.smem_data = (data + 1023) & ~1023;
   return NE_OK;
 }
 
@@ -440,15 +487,17 @@ int gemm_launch(const CUtensorMap* tm_w, const CUtensorMap* tm_x, const GemmPara
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.splits, p.N / GEMM_BM, (p.M_max + p.t_block - 1) / p.t_block);
   cfg.blockDim = dim3(GEMM_THREADS);
-  cfg.dynamicSmemBytes = GEMM_SMEM_BYTES;
+  cfg.dynamicSmemBytes = p.smem_data + 256 + 1024;
   cfg.stream = stream;
-  cudaLaunchAttribute attrs[1];
+  cudaLaunchAttribute attrs[2];
   attrs[0].id = cudaLaunchAttributeClusterDimension;
   attrs[0].val.clusterDim.x = p.splits;
   attrs[0].val.clusterDim.y = 1;
   attrs[0].val.clusterDim.z = 1;
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   cudaError_t err;
   switch (p.epi.mode) {
     case EPI_STORE: err = launch_mode<EPI_STORE>(cfg, tm_w, tm_x, p); break;

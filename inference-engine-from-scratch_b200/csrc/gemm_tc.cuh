@@ -29,6 +29,7 @@ constexpr int GEMM_SMEM_BYTES = 227 * 1024;
 // data region (pipeline stages, later the epilogue staging); then 256 B of barriers; the rest is
 // the slack that aligns the dynamic shared memory base to 1024 B
 constexpr int GEMM_SMEM_DATA_BYTES = GEMM_SMEM_BYTES - 1024 - 256;
+constexpr int GEMM_MAX_STAGES = 8;
 constexpr int GEMM_MAX_SPLITS = 8;   // portable cluster size
 
 enum EpilogueMode : int {
@@ -74,6 +75,7 @@ struct GemmParams {
   int t_block;           // tokens per CTA (<= 512; <= 256 when splits > 1)
   int splits;            // cluster size along K
   int stages;
+  int smem_data;         // bytes of the data region (pipeline stages / epilogue staging)
   int* status;
   Epilogue epi;
 };

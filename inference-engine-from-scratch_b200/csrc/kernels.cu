@@ -17,6 +17,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 __global__ void embed_kernel(const __nv_bfloat16* __restrict__ embed, const int32_t* __restrict__ tokens,
                              const int32_t* num_rows, int max_rows, int hidden, int vocab,
                              __nv_bfloat16* __restrict__ out, int* status) {
+  pdl_prologue();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int n = num_rows ? min(*num_rows, max_rows) : max_rows;
@@ -36,6 +37,7 @@ __global__ void embed_kernel(const __nv_bfloat16* __restrict__ embed, const int3
 __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                                __nv_bfloat16* __restrict__ y, int max_rows, const int32_t* rows_dev,
                                const int32_t* gather, int hidden, float eps, unsigned long long* zero_keys) {
+  pdl_prologue();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int n = rows_dev ? min(*rows_dev, max_rows) : max_rows;
@@ -70,6 +72,7 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_b
 
 __global__ void keys_to_ids_kernel(const unsigned long long* keys, const int32_t* count, int max_count,
                                    int32_t* ids) {
+  pdl_prologue();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   const int n = count ? min(*count, max_count) : max_count;
   if (i < n) ids[i] = (int32_t)argmax_key_index(keys[i]);
@@ -81,6 +84,7 @@ __global__ void keys_to_ids_kernel(const unsigned long long* keys, const int32_t
 // last n tokens (largest start in [0, len - n - 1]); the guesses are the (<= cap) tokens after it.
 __global__ void ngram_kernel(ne_batch_state st, const int32_t* __restrict__ seq_slot, int k, int max_ngram,
                              int min_ngram, int32_t* __restrict__ draft_len, int* status) {
+  pdl_prologue();
   const int b = blockIdx.x;
   const int tid = threadIdx.x;
   const int s = seq_slot[b];
@@ -168,6 +172,7 @@ __device__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
 __global__ void __launch_bounds__(1024)
     plan_kernel(ne_batch_state st, const int32_t* __restrict__ seq_slot, int num_seqs, int mode, int max_rows,
                 int bs, long long num_cache_slots, RowBuffers rb, int* status) {
+  pdl_prologue();
   __shared__ int warp_sums[32];
   __shared__ int s_qstart[1024];
   __shared__ int total_rows, total_need, fail;
@@ -270,6 +275,7 @@ __global__ void __launch_bounds__(1024)
 __global__ void accept_greedy_kernel(ne_batch_state st, const int32_t* __restrict__ seq_slot, int num_seqs, int k,
                                      int mode, RowBuffers rb, const unsigned long long* __restrict__ keys,
                                      ne_step_outputs out, int* status) {
+  pdl_prologue();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= num_seqs) return;
   const int s = seq_slot[b];
@@ -325,6 +331,7 @@ __global__ void accept_greedy_kernel(ne_batch_state st, const int32_t* __restric
 
 // ------------------------------------------------------------------ free-block FIFO
 __global__ void reset_blocks_kernel(ne_batch_state st) {
+  pdl_prologue();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < st.num_blocks; i += gridDim.x * blockDim.x)
     st.free_ring[i] = i;
   if (blockIdx.x == 0 && threadIdx.x == 0) {
@@ -334,6 +341,7 @@ __global__ void reset_blocks_kernel(ne_batch_state st) {
 }
 
 __global__ void free_slots_kernel(ne_batch_state st, const int32_t* slots, int num_slots) {
+  pdl_prologue();
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   long long tail = st.ring_head_tail[1];
   for (int i = 0; i < num_slots; ++i) {
@@ -348,8 +356,6 @@ __global__ void free_slots_kernel(ne_batch_state st, const int32_t* slots, int n
   st.ring_head_tail[1] = tail;
 }
 
-inline int check_launch() { return cudaGetLastError() == cudaSuccess ? NE_OK : NE_ERR_CUDA; }
-
 }  // namespace
 
 int launch_embed(const __nv_bfloat16* embed, const int32_t* tokens, const int32_t* num_rows, int max_rows, int hidden,
@@ -358,8 +364,8 @@ int launch_embed(const __nv_bfloat16* embed, const int32_t* tokens, const int32_
   const int threads = 128;
   const int blocks = (max_rows * 32 + threads - 1) / threads;
   if (blocks == 0) return NE_OK;
-  embed_kernel<<<blocks, threads, 0, stream>>>(embed, tokens, num_rows, max_rows, hidden, vocab, out, status);
-  return check_launch();
+  return launch_kernel(embed_kernel, dim3(blocks), dim3(threads), 0, stream, embed, tokens, num_rows, max_rows, hidden,
+                       vocab, out, status) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 
 int launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int max_rows,
@@ -368,51 +374,48 @@ int launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16
   if (hidden % 256) return NE_ERR_INVALID;
   const int blocks = (max_rows + 3) / 4;
   if (blocks == 0) return NE_OK;
-  rmsnorm_kernel<<<blocks, 128, 0, stream>>>(x, w, y, max_rows, rows_dev, gather, hidden, eps, zero_keys);
-  return check_launch();
+  return launch_kernel(rmsnorm_kernel, dim3(blocks), dim3(128), 0, stream, x, w, y, max_rows, rows_dev, gather, hidden,
+                       eps, zero_keys) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 
 int launch_keys_to_ids(const unsigned long long* keys, const int32_t* count, int max_count, int32_t* ids,
                        cudaStream_t stream) {
   if (max_count <= 0) return NE_OK;
-  keys_to_ids_kernel<<<(max_count + 255) / 256, 256, 0, stream>>>(keys, count, max_count, ids);
-  return check_launch();
+  return launch_kernel(keys_to_ids_kernel, dim3((max_count + 255) / 256), dim3(256), 0, stream, keys, count, max_count,
+                       ids) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 
 int launch_ngram(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int k, int max_ngram,
                  int min_ngram, int32_t* draft_len, int* status, cudaStream_t stream) {
   if (num_seqs <= 0) return NE_OK;
   if (max_ngram < min_ngram || min_ngram < 1 || k < 1) return NE_ERR_INVALID;
-  ngram_kernel<<<num_seqs, 128, 0, stream>>>(st, seq_slot, k, max_ngram, min_ngram, draft_len, status);
-  return check_launch();
+  return launch_kernel(ngram_kernel, dim3(num_seqs), dim3(128), 0, stream, st, seq_slot, k, max_ngram, min_ngram,
+                       draft_len, status) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 
 int launch_plan(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int mode, int max_rows,
                 int block_size, long long num_cache_slots, const RowBuffers& rb, int* status, cudaStream_t stream) {
   if (num_seqs <= 0 || num_seqs > 1024) return NE_ERR_INVALID;
-  plan_kernel<<<1, 1024, 0, stream>>>(st, seq_slot, num_seqs, mode, max_rows, block_size, num_cache_slots, rb,
-                                      status);
-  return check_launch();
+  return launch_kernel(plan_kernel, dim3(1), dim3(1024), 0, stream, st, seq_slot, num_seqs, mode, max_rows, block_size,
+                       num_cache_slots, rb, status) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 
 int launch_accept_greedy(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int k, int mode,
                          const RowBuffers& rb, const unsigned long long* keys, const ne_step_outputs& out,
                          int* status, cudaStream_t stream) {
   if (num_seqs <= 0) return NE_OK;
-  accept_greedy_kernel<<<(num_seqs + 127) / 128, 128, 0, stream>>>(st, seq_slot, num_seqs, k, mode, rb, keys, out,
-                                                                   status);
-  return check_launch();
+  return launch_kernel(accept_greedy_kernel, dim3((num_seqs + 127) / 128), dim3(128), 0, stream, st, seq_slot, num_seqs,
+                       k, mode, rb, keys, out, status) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 
 int launch_reset_blocks(const ne_batch_state& st, cudaStream_t stream) {
-  reset_blocks_kernel<<<64, 256, 0, stream>>>(st);
-  return check_launch();
+  return launch_kernel(reset_blocks_kernel, dim3(64), dim3(256), 0, stream, st) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 
 int launch_free_slots(const ne_batch_state& st, const int32_t* slots, int num_slots, cudaStream_t stream) {
   if (num_slots <= 0) return NE_OK;
-  free_slots_kernel<<<1, 32, 0, stream>>>(st, slots, num_slots);
-  return check_launch();
+  return launch_kernel(free_slots_kernel, dim3(1), dim3(32), 0, stream, st, slots, num_slots) == cudaSuccess ? NE_OK
+                                                                                                     : NE_ERR_CUDA;
 }
 
 }  // namespace ne
