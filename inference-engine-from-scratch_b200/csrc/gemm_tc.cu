@@ -2,7 +2,9 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "gemm_tc.cuh"
 
@@ -12,21 +14,54 @@ namespace {
 
 
 
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Bulk copy of ``bytes`` from this CTA's shared memory to a peer's (cluster address), completing
+// ``bytes`` on the peer's mbarrier (cluster address).
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes,
+                                                  uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst_cluster),
+      "r"(src_cta), "r"(bytes), "r"(bar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// 32 lanes x 8 consecutive fp32 columns (no wait: pair with tmem_ld_wait()).
+__device__ __forceinline__ void tmem_ld8_nowait(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Copy TMEM columns [c0, c0 + cnt) (tokens) of this warp's 32 lanes (output rows) into smem
+// ``dst`` laid out [token][128]. cnt is a multiple of 8; all lanes of the warp call this.
+__device__ __forceinline__ void tmem_to_smem(uint32_t tmem_lane_base, int c0, int cnt, float* dst, int row) {
+  for (int c = 0; c < cnt; c += 32) {
+    uint32_t r[4][8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (c + 8 * q < cnt) tmem_ld8_nowait(tmem_lane_base + (uint32_t)(c0 + c + 8 * q), r[q]);
+    tmem_ld_wait();
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (c + 8 * q < cnt)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[(c + 8 * q + i) * GEMM_BM + row] = __uint_as_float(r[q][i]);
+  }
 }
 __device__ __forceinline__ uint32_t map_peer(uint32_t local_addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
   return r;
-}
-__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
-  float4 v;
-  // no memory clobber: the partial tiles are read-only between the two cluster barriers
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr));
-  return v;
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -193,7 +228,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.smem_data);
   uint64_t* empty = full + stages;
   uint64_t* done = empty + stages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* recv_bar = done + 1;  // split-K: peers' partial slices landed in our receive area
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* consumed_slot = const_cast<int*>(reinterpret_cast<volatile int*>(tmem_slot + 2));
 
@@ -207,6 +243,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(done, 1);
+    mbar_init(recv_bar, 1);
     *abort_flag = 0;
     *consumed_slot = 0;
     fence_mbar_init();
@@ -239,6 +276,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   int issued = pre;
   if (t_actual <= 0) {
     // no rows for this m-block (the whole cluster shares it): retire the prefetched weight copies
+    if (S > 1) {
+      if (tid == 0) mbar_arrive(recv_bar);
+      cluster_arrive();
+      cluster_wait();
+    }
     if (warp == 0 && lane == 0) {
       for (int i = 0; i < pre; ++i) mbar_arrive(&full[i]);
       for (int i = 0; i < pre; ++i) mbar_wait(&full[i], 0, nullptr, p.status);
@@ -252,6 +294,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     return;
   }
 
+  // split-K: CTA r of the cluster owns tokens [r * slice, r * slice + own_cnt) and receives the
+  // other splits' partials of those tokens (S - 1 pushes of own_cnt rows)
+  const int slice = (((t_actual + S - 1) / S) + 7) & ~7;
+  const int own_cnt = max(0, min(slice, t_actual - split * slice));
+  if (S > 1 && tid == 0) mbar_arrive_expect_tx(recv_bar, (uint32_t)((S - 1) * own_cnt * GEMM_BM * 4));
   const int n_loads = (t_actual + GEMM_XBOX - 1) / GEMM_XBOX;
   const int n_pad = (t_actual + 15) & ~15;
   const int part0 = n_pad < 256 ? n_pad : 256;
@@ -338,56 +385,69 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       __syncthreads();
     }
   } else {
-    // park this split's partial tile [t_actual][128], then reduce our token slice over the cluster
-    for (int c32 = 0; c32 < t_actual; c32 += 32) {
-      float v[32];
-      if (ok && nk > 0) {
-        tmem_ld32(tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)c32, v);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+    // Split-K over the cluster. Once every CTA's mainloop is done (cluster barrier), each CTA
+    // pushes, for every peer, the peer's token slice of its own partial tile straight into the
+    // peer's receive area (one bulk DSMEM copy per peer, two staging buffers); the owner then
+    // sums the S partials of its slice in split order (deterministic) and runs the epilogue.
+    float* send = stage_acc;                                   // [2][slice][128]
+    float* recv = stage_acc + 2 * (size_t)slice * GEMM_BM;     // [S - 1][slice][128]
+    const uint32_t lane_base = tmem_base + ((uint32_t)(warp * 32) << 16);
+    const uint32_t recv_local = smem_u32(recv);
+    const uint32_t recv_bar_local = smem_u32(recv_bar);
+    cluster_arrive();   // our mainloop is done: peers may now write our receive area
+    bool waited = false;
+    int j_sent = 0;
+    for (int j = 0; j < S - 1; ++j) {
+      const int peer = (split + 1 + j) % S;
+      const int cnt = max(0, min(slice, t_actual - peer * slice));
+      if (cnt == 0) continue;
+      float* buf = send + (size_t)(j_sent & 1) * slice * GEMM_BM;
+      if (j_sent >= 2) {  // the buffer's previous copy must have been read
+        if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+        __syncthreads();
       }
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (c32 + i < t_actual) stage_acc[(c32 + i) * GEMM_BM + warp * 32 + lane] = v[i];
+      if (ok) tmem_to_smem(lane_base, peer * slice, (cnt + 7) & ~7, buf, warp * 32 + lane);
+      fence_proxy_async_smem();
+      __syncthreads();
+      if (!waited) {
+        cluster_wait();  // every CTA's receive area is free and its barrier initialised
+        waited = true;
+      }
+      if (tid == 0) {
+        const int slot = split < peer ? split : split - 1;
+        const uint32_t dst = map_peer(recv_local + (uint32_t)(slot * slice * GEMM_BM * 4), (uint32_t)peer);
+        bulk_copy_to_peer(dst, smem_u32(buf), (uint32_t)(cnt * GEMM_BM * 4), map_peer(recv_bar_local, (uint32_t)peer));
+        bulk_commit();
+      }
+      ++j_sent;
     }
+    if (!waited) cluster_wait();
+    if (tid == 0) bulk_wait_read_all();
     __syncthreads();
-    cluster_sync_all();
-    const int slice = (t_actual + S - 1) / S;
-    const int s_begin = split * slice;
-    const int s_cnt = max(0, min(slice, t_actual - s_begin));
-    float* red = stage_acc + (size_t)p.t_block * GEMM_BM;
-    const uint32_t local_base = smem_u32(stage_acc);
-    for (int idx = tid; idx < s_cnt * (GEMM_BM / 4); idx += GEMM_THREADS) {
-      const int m = idx / (GEMM_BM / 4);
-      const int n4 = idx % (GEMM_BM / 4);
-      const uint32_t off = (uint32_t)(((s_begin + m) * GEMM_BM + n4 * 4) * 4);
-      float4 part[GEMM_MAX_SPLITS];
-#pragma unroll
-      for (int r = 0; r < GEMM_MAX_SPLITS; ++r)
-        if (r < S) part[r] = ld_cluster_f4(map_peer(local_base + off, (uint32_t)r));
-      float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int r = 0; r < GEMM_MAX_SPLITS; ++r) {  // fixed split order: deterministic sums
-        if (r < S) {
-          sum.x += part[r].x;
-          sum.y += part[r].y;
-          sum.z += part[r].z;
-          sum.w += part[r].w;
+    // our own slice: wait for the S - 1 pushes, add them to our partial in split order
+    const bool got = mbar_wait(recv_bar, 0, abort_flag, p.status);
+    float* red = send;  // the send buffers are free again
+    if (own_cnt > 0) {
+      if (ok) tmem_to_smem(lane_base, split * slice, (own_cnt + 7) & ~7, red, warp * 32 + lane);
+      __syncthreads();
+      for (int idx = tid; idx < own_cnt * GEMM_BM; idx += GEMM_THREADS) {
+        float acc = 0.f;
+        for (int r = 0; r < S; ++r) {
+          const float v = r == split ? red[idx] : recv[(size_t)(r < split ? r : r - 1) * slice * GEMM_BM + idx];
+          acc += v;
         }
+        red[idx] = acc;
       }
-      reinterpret_cast<float4*>(red)[m * (GEMM_BM / 4) + n4] = sum;
+      __syncthreads();
+      if (ok && got) epilogue_rows<MODE>(p.epi, p.N, tile_n, m_begin + split * slice, own_cnt, red);
+      __syncthreads();
     }
-    __syncthreads();
-    if (ok && s_cnt > 0) epilogue_rows<MODE>(p.epi, p.N, tile_n, m_begin + s_begin, s_cnt, red);
-    __syncthreads();
-    cluster_sync_all();  // peers may still be reading our partial tile
   }
 
   // ------------------------------------------------------------------ teardown
   if (!ok && warp == 0 && lane == 0) {
     // drain our own TMA copies still in flight (bounded) before the shared memory goes away
-    const int consumed = *consumed_slot;
+    const int consumed = *consumed_slot;  // (split-K pushes were drained before the reduction)
     for (int i = consumed; i < issued; ++i) mbar_wait(&full[i % stages], (uint32_t)(i / stages) & 1u, nullptr, p.status);
   }
   tc_fence_before();
@@ -427,8 +487,104 @@ bool make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
   return r == CUDA_SUCCESS;
 }
 
+template <int MODE>
+cudaError_t prepare_mode() {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(gemm_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    GEMM_SMEM_BYTES);
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(gemm_tc_kernel<MODE>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  });
+  return attr_err;
+}
+
+template <int MODE>
+cudaError_t launch_mode(const cudaLaunchConfig_t& cfg, const CUtensorMap* tm_w, const CUtensorMap* tm_x,
+                        const GemmParams& p) {
+  cudaError_t err = prepare_mode<MODE>();
+  if (err != cudaSuccess) return err;
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<MODE>, *tm_w, *tm_x, p);
+}
+
+// Clusters of ``splits`` CTAs with ``smem`` bytes each that the GPU holds at once (0 on error).
+template <int MODE>
+int active_clusters_mode(int splits, int smem) {
+  if (prepare_mode<MODE>() != cudaSuccess) return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(splits, 1, 1);
+  cfg.blockDim = dim3(GEMM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tc_kernel<MODE>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return clusters;
+}
+
+int active_clusters(int mode, int splits, int smem) {
+  switch (mode) {
+    case EPI_STORE: return active_clusters_mode<EPI_STORE>(splits, smem);
+    case EPI_RESIDUAL: return active_clusters_mode<EPI_RESIDUAL>(splits, smem);
+    case EPI_SWIGLU: return active_clusters_mode<EPI_SWIGLU>(splits, smem);
+    case EPI_QKV: return active_clusters_mode<EPI_QKV>(splits, smem);
+    case EPI_ARGMAX: return active_clusters_mode<EPI_ARGMAX>(splits, smem);
+    case EPI_LOGITS: return active_clusters_mode<EPI_LOGITS>(splits, smem);
+    default: return 0;
+  }
+}
+
 // Choose tokens per CTA, split-K (cluster size) and pipeline depth for an [M_max, K] x [N, K]^T GEMM.
+namespace {
+struct PlanKey {
+  int M, N, K, mode, sms;
+  bool operator<(const PlanKey& o) const {
+    return std::tie(M, N, K, mode, sms) < std::tie(o.M, o.N, o.K, o.mode, o.sms);
+  }
+};
+struct PlanVal {
+  int t_block, splits, stages, smem_data;
+};
+std::mutex g_plan_mutex;
+std::map<PlanKey, PlanVal> g_plans;
+
+int plan_uncached(GemmParams& p, int num_sms);
+int plan_with_occupancy(GemmParams& p, int num_sms);
+}  // namespace
+
+// Cached per (rows, N, K, epilogue, SMs); the first plan of a shape queries cluster occupancy.
 int gemm_plan(GemmParams& p, int num_sms) {
+  const PlanKey key{p.M_max, p.N, p.K, p.epi.mode, num_sms};
+  {
+    std::lock_guard<std::mutex> lock(g_plan_mutex);
+    auto it = g_plans.find(key);
+    if (it != g_plans.end()) {
+      p.t_block = it->second.t_block;
+      p.splits = it->second.splits;
+      p.stages = it->second.stages;
+      p.smem_data = it->second.smem_data;
+      return NE_OK;
+    }
+  }
+  const int rc = plan_with_occupancy(p, num_sms);
+  if (rc == NE_OK) {
+    std::lock_guard<std::mutex> lock(g_plan_mutex);
+    g_plans[key] = PlanVal{p.t_block, p.splits, p.stages, p.smem_data};
+  }
+  return rc;
+}
+
+namespace {
+int plan_uncached(GemmParams& p, int num_sms) {
   if (p.N % GEMM_BM || p.K % GEMM_BK || p.M_max <= 0) return NE_ERR_INVALID;
   const int num_chunks = p.K / GEMM_BK;
   const int n_tiles = p.N / GEMM_BM;
@@ -437,11 +593,12 @@ int gemm_plan(GemmParams& p, int num_sms) {
   int m_blocks = (p.M_max + t_block - 1) / t_block;
   int S = std::max(1, std::min(GEMM_MAX_SPLITS, num_sms / std::max(1, n_tiles * m_blocks)));
   if (p.epi.mode == EPI_ARGMAX || p.epi.mode == EPI_LOGITS) S = 1;
-  auto fits = [&](int s, int tb) {
-    if (s == 1) return 128 * GEMM_BM * 4 <= avail;
-    int slice = (tb + s - 1) / s;
-    return (tb + slice) * GEMM_BM * 4 <= avail;
+  auto staging_bytes = [&](int s, int tb) {
+    if (s == 1) return 128 * GEMM_BM * 4;
+    const int slice = (((tb + s - 1) / s) + 7) & ~7;
+    return (s + 1) * slice * GEMM_BM * 4;
   };
+  auto fits = [&](int s, int tb) { return staging_bytes(s, tb) <= avail; };
   while (S > 1) {
     int cps = (num_chunks + S - 1) / S;
     bool every_split_has_work = cps * (S - 1) < num_chunks;
@@ -453,7 +610,7 @@ int gemm_plan(GemmParams& p, int num_sms) {
   const int cps = (num_chunks + S - 1) / S;
   int stages = std::min(std::min(GEMM_MAX_STAGES, cps), avail / stage_bytes);
   if (stages < 1) return NE_ERR_INVALID;
-  const int staging = S == 1 ? 128 * GEMM_BM * 4 : (t_block + (t_block + S - 1) / S) * GEMM_BM * 4;
+  const int staging = staging_bytes(S, t_block);
   int data = std::max(stages * stage_bytes, staging);
   // Never let more CTAs share an SM than its 512 TMEM columns can hold: CTAs of one cluster that
   // landed on one SM would otherwise wait on each other (one in tcgen05.alloc, the rest at the
@@ -470,18 +627,25 @@ int gemm_plan(GemmParams& p, int num_sms) {
   return NE_OK;
 }
 
-template <int MODE>
-cudaError_t launch_mode(const cudaLaunchConfig_t& cfg, const CUtensorMap* tm_w, const CUtensorMap* tm_x,
-                        const GemmParams& p) {
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    GEMM_SMEM_BYTES);
-  });
-  if (attr_err != cudaSuccess) return attr_err;
-  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<MODE>, *tm_w, *tm_x, p);
+int plan_with_occupancy(GemmParams& p, int num_sms) {
+  // try the SM-filling split first, then smaller clusters until every cluster fits in one wave
+  const int n_tiles = p.N / GEMM_BM;
+  int rc = plan_uncached(p, num_sms);
+  if (rc != NE_OK) return rc;
+  const int m_blocks = (p.M_max + p.t_block - 1) / p.t_block;
+  while (p.splits > 1) {
+    const int fit = active_clusters(p.epi.mode, p.splits, p.smem_data + 256 + 1024);
+    if (fit >= n_tiles * m_blocks) break;
+    const int want = p.splits - 1;
+    GemmParams q = p;
+    int sms = want * n_tiles * m_blocks;  // steer plan_uncached towards ``want`` splits
+    rc = plan_uncached(q, sms);
+    if (rc != NE_OK || q.splits >= p.splits) break;
+    p = q;
+  }
+  return NE_OK;
 }
+}  // namespace
 
 int gemm_launch(const CUtensorMap* tm_w, const CUtensorMap* tm_x, const GemmParams& p, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
