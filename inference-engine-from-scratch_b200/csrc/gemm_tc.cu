@@ -14,6 +14,15 @@ namespace {
 
 
 
+__device__ __forceinline__ float4 lds_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void sts_f4(uint32_t addr, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
 __device__ __forceinline__ void cluster_arrive() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
@@ -232,6 +241,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* consumed_slot = const_cast<int*>(reinterpret_cast<volatile int*>(tmem_slot + 2));
+  volatile int* done_ok = reinterpret_cast<volatile int*>(tmem_slot + 3);  // broadcast flags (barrier area)
+  volatile int* recv_ok = reinterpret_cast<volatile int*>(tmem_slot + 4);
 
   const uint32_t tmem_cols = p.t_block <= 32 ? 32 : p.t_block <= 64 ? 64 : p.t_block <= 128 ? 128
                              : p.t_block <= 256 ? 256 : 512;
@@ -358,10 +369,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
 
   // ------------------------------------------------------------------ epilogue
-  bool ok = (nk == 0) || mbar_wait(done, 0, abort_flag, p.status);
-  tc_fence_after();
+  // one thread waits for the accumulator; the rest wait at the CTA barrier (no spinning)
+  if (tid == 64) *done_ok = ((nk == 0) || mbar_wait(done, 0, abort_flag, p.status)) ? 1 : 0;
   __syncthreads();
-  if (*abort_flag) ok = false;
+  tc_fence_after();
+  bool ok = *done_ok != 0 && !*abort_flag;
 
   float* stage_acc = reinterpret_cast<float*>(smem);  // pipeline smem is free once ``done`` fired
   const int m_begin = m0;
@@ -419,24 +431,44 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         bulk_copy_to_peer(dst, smem_u32(buf), (uint32_t)(cnt * GEMM_BM * 4), map_peer(recv_bar_local, (uint32_t)peer));
         bulk_commit();
       }
+      __syncwarp();  // reconverge warp 0 before the next warp-collective TMEM load
       ++j_sent;
     }
-    if (!waited) cluster_wait();
-    if (tid == 0) bulk_wait_read_all();
     __syncthreads();
-    // our own slice: wait for the S - 1 pushes, add them to our partial in split order
-    const bool got = mbar_wait(recv_bar, 0, abort_flag, p.status);
+    if (!waited) cluster_wait();
+    // our own slice: wait (one thread) for the S - 1 pushes and for our own pushes to be read
+    if (tid == 0) {
+      bulk_wait_read_all();
+      *recv_ok = mbar_wait(recv_bar, 0, abort_flag, p.status) ? 1 : 0;
+    }
+    __syncthreads();
+    const bool got = *recv_ok != 0;
     float* red = send;  // the send buffers are free again
     if (own_cnt > 0) {
       if (ok) tmem_to_smem(lane_base, split * slice, (own_cnt + 7) & ~7, red, warp * 32 + lane);
       __syncthreads();
-      for (int idx = tid; idx < own_cnt * GEMM_BM; idx += GEMM_THREADS) {
-        float acc = 0.f;
-        for (int r = 0; r < S; ++r) {
-          const float v = r == split ? red[idx] : recv[(size_t)(r < split ? r : r - 1) * slice * GEMM_BM + idx];
-          acc += v;
+      // float4 per thread, all S partial loads issued before the adds (the CTA has only 4 warps,
+      // so latency is hidden by instruction-level parallelism, not by other warps)
+      const uint32_t red_s = smem_u32(red);
+      const uint32_t slot_bytes = (uint32_t)(slice * GEMM_BM * 4);
+      for (int i = tid; i < own_cnt * (GEMM_BM / 4); i += GEMM_THREADS) {
+        float4 part[GEMM_MAX_SPLITS];
+#pragma unroll
+        for (int r = 0; r < GEMM_MAX_SPLITS; ++r)
+          if (r < S)
+            part[r] = lds_f4(r == split ? red_s + i * 16
+                                        : recv_local + (uint32_t)(r < split ? r : r - 1) * slot_bytes + i * 16);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int r = 0; r < GEMM_MAX_SPLITS; ++r) {  // split order: deterministic sums
+          if (r < S) {
+            acc.x += part[r].x;
+            acc.y += part[r].y;
+            acc.z += part[r].z;
+            acc.w += part[r].w;
+          }
         }
-        red[idx] = acc;
+        sts_f4(red_s + i * 16, acc);
       }
       __syncthreads();
       if (ok && got) epilogue_rows<MODE>(p.epi, p.N, tile_n, m_begin + split * slice, own_cnt, red);
