@@ -87,126 +87,194 @@ __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v)
   return v;
 }
 
-// Apply the epilogue to ``count`` token rows whose fp32 accumulators sit in shared memory
-// ``acc`` as [count][128]. ``m_begin`` is the global row of acc row 0; ``tile_n`` the N tile.
+__device__ __forceinline__ uint4 pack8_bf16(const float* v) {
+  uint4 u;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return u;
+}
+__device__ __forceinline__ void unpack8_bf16(uint4 u, float* v) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void unpack4_bf16(uint2 u, float* v) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+  float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+  v[0] = a.x;
+  v[1] = a.y;
+  v[2] = b.x;
+  v[3] = b.y;
+}
+
+// Apply the epilogue to ``count`` token rows whose fp32 accumulators sit in shared memory at
+// ``acc_s`` as [count][128]. ``m_begin`` is the global row of the first; ``tile_n`` the N tile.
+// The CTA has only four warps, so every path keeps several independent 16-byte loads in flight
+// per thread (latency is hidden by instruction-level parallelism, not by other warps).
 template <int MODE>
-__device__ void epilogue_rows(const Epilogue& e, int N, int tile_n, int m_begin, int count, const float* acc) {
+__device__ void epilogue_rows(const Epilogue& e, int tile_n, int m_begin, int count, uint32_t acc_s) {
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
   const int n0 = tile_n * GEMM_BM;
-  switch (MODE) {
-    case EPI_STORE:
-      for (int idx = tid; idx < count * GEMM_BM; idx += GEMM_THREADS) {
-        int m = idx >> 7, n = idx & 127;
-        e.out[(long long)(m_begin + m) * e.ldo + n0 + n] = __float2bfloat16_rn(acc[idx]);
-      }
-      break;
-    case EPI_RESIDUAL:
-      for (int idx = tid; idx < count * GEMM_BM; idx += GEMM_THREADS) {
-        int m = idx >> 7, n = idx & 127;
-        __nv_bfloat16* o = e.out + (long long)(m_begin + m) * e.ldo + n0 + n;
-        float y = bf16r(acc[idx]);
-        *o = __float2bfloat16_rn(__bfloat162float(*o) + y);
-      }
-      break;
-    case EPI_SWIGLU:
-      for (int idx = tid; idx < count * 64; idx += GEMM_THREADS) {
-        int m = idx >> 6, j = idx & 63;
-        float g = bf16r(acc[m * GEMM_BM + j]);
-        float u = bf16r(acc[m * GEMM_BM + 64 + j]);
-        float a = bf16r(g / (1.0f + expf(-g)));
-        e.out[(long long)(m_begin + m) * e.ldo + tile_n * 64 + j] = __float2bfloat16_rn(a * u);
-      }
-      break;
-    case EPI_QKV: {
-      const int head = tile_n;
-      const bool is_q = head < e.n_q_heads;
-      const bool is_k = !is_q && head < e.n_q_heads + e.n_kv_heads;
-      for (int m = warp; m < count; m += GEMM_THREADS / 32) {
-        const int row = m_begin + m;
-        float v[4];
+  if (MODE == EPI_STORE || MODE == EPI_RESIDUAL) {
+    // unit = 8 consecutive outputs of one row (16 bytes of bf16); 4 units per thread per round
+    const int units = count * (GEMM_BM / 8);
+    for (int u0 = tid; u0 < units; u0 += 4 * GEMM_THREADS) {
+      float v[4][8];
+      uint4 res[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = bf16r(acc[m * GEMM_BM + lane + 32 * i]);
-        if (is_q || is_k) {
-          float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
-          float r = 1.0f / sqrtf(ss / 128.0f + e.eps);
-          const __nv_bfloat16* w = is_q ? e.q_norm_w : e.k_norm_w;
-          float nv[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) nv[i] = bf16r(bf16r(v[i] * r) * ld_bf16(w + lane + 32 * i));
-          int pos = e.positions[row];
-          pos = pos < 0 ? 0 : (pos >= e.max_positions ? e.max_positions - 1 : pos);
-          const __nv_bfloat16* cs = e.rope_cos + (long long)pos * 128;
-          const __nv_bfloat16* sn = e.rope_sin + (long long)pos * 128;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            int d = lane + 32 * i;
-            float rot = i < 2 ? -nv[i + 2] : nv[i - 2];
-            v[i] = bf16r(bf16r(nv[i] * ld_bf16(cs + d)) + bf16r(rot * ld_bf16(sn + d)));
-          }
+      for (int j = 0; j < 4; ++j) {
+        const int u = u0 + j * GEMM_THREADS;
+        if (u < units) {
+          const int m = u >> 4, c = (u & 15) * 8;
+          const float4 a = lds_f4(acc_s + (uint32_t)((m * GEMM_BM + c) * 4));
+          const float4 b = lds_f4(acc_s + (uint32_t)((m * GEMM_BM + c + 4) * 4));
+          v[j][0] = a.x; v[j][1] = a.y; v[j][2] = a.z; v[j][3] = a.w;
+          v[j][4] = b.x; v[j][5] = b.y; v[j][6] = b.z; v[j][7] = b.w;
+          if (MODE == EPI_RESIDUAL)
+            res[j] = *reinterpret_cast<const uint4*>(e.out + (long long)(m_begin + m) * e.ldo + n0 + c);
         }
-        if (is_q) {
-          __nv_bfloat16* q = e.q_out + (long long)row * (e.n_q_heads * 128) + head * 128;
+      }
 #pragma unroll
-          for (int i = 0; i < 4; ++i) q[lane + 32 * i] = __float2bfloat16_rn(v[i]);
-        } else {
-          const int kvh = is_k ? head - e.n_q_heads : head - e.n_q_heads - e.n_kv_heads;
-          long long slot = e.slot_mapping[row];
-          if (slot < 0 || slot >= e.num_cache_slots) {
-            if (lane == 0) report(e.status, NE_DEV_BAD_SLOT);
-            continue;
-          }
-          long long base = (slot * e.n_kv_heads + kvh) * 128;
-          if (!e.kv_int8) {
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(is_k ? e.k_cache : e.v_cache) + base;
+      for (int j = 0; j < 4; ++j) {
+        const int u = u0 + j * GEMM_THREADS;
+        if (u < units) {
+          const int m = u >> 4, c = (u & 15) * 8;
+          float o[8];
+          if (MODE == EPI_RESIDUAL) {
+            float h[8];
+            unpack8_bf16(res[j], h);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = __float2bfloat16_rn(v[i]);
+            for (int i = 0; i < 8; ++i) o[i] = h[i] + bf16r(v[j][i]);  // residual + rounded projection
           } else {
-            // models/int8_quantization.py:30-34: scale = max|x| / 127 in fp32 (clamped), stored in
-            // the model dtype; q = round(x / scale) clamped to +-127.
-            float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-            float scale = fmaxf(amax, 1e-8f) / 127.0f;
-            int8_t* dst = reinterpret_cast<int8_t*>(is_k ? e.k_cache : e.v_cache) + base;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              float q = rintf(v[i] / scale);
-              q = fminf(fmaxf(q, -127.0f), 127.0f);
-              dst[lane + 32 * i] = (int8_t)q;
-            }
-            if (lane == 0) {
-              __nv_bfloat16* sdst = is_k ? e.k_scale : e.v_scale;
-              sdst[slot * e.n_kv_heads + kvh] = __float2bfloat16_rn(scale);
-            }
+            for (int i = 0; i < 8; ++i) o[i] = v[j][i];
           }
+          *reinterpret_cast<uint4*>(e.out + (long long)(m_begin + m) * e.ldo + n0 + c) = pack8_bf16(o);
         }
       }
-      break;
     }
-    case EPI_ARGMAX:
-    case EPI_LOGITS: {
-      for (int m = warp; m < count; m += GEMM_THREADS / 32) {
-        const int row = m_begin + m;
-        unsigned long long best = 0;
+  } else if (MODE == EPI_SWIGLU) {
+    // unit = 8 consecutive features j of one row: gate rows j, up rows 64 + j of the tile
+    const int units = count * 8;
+    for (int u = tid; u < units; u += GEMM_THREADS) {
+      const int m = u >> 3, c = (u & 7) * 8;
+      const uint32_t row = acc_s + (uint32_t)(m * GEMM_BM * 4);
+      const float4 g0 = lds_f4(row + c * 4), g1 = lds_f4(row + (c + 4) * 4);
+      const float4 u0 = lds_f4(row + (64 + c) * 4), u1 = lds_f4(row + (64 + c + 4) * 4);
+      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+      const float up[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+      float o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float gg = bf16r(g[i]);
+        const float a = bf16r(gg / (1.0f + expf(-gg)));  // silu in fp32, rounded (torch bf16 silu)
+        o[i] = a * bf16r(up[i]);
+      }
+      *reinterpret_cast<uint4*>(e.out + (long long)(m_begin + m) * e.ldo + tile_n * 64 + c) = pack8_bf16(o);
+    }
+  } else if (MODE == EPI_QKV) {
+    // a warp per token; lane holds dims 4*lane .. 4*lane+3, RoPE partner dims are in lane ^ 16
+    const int head = tile_n;
+    const bool is_q = head < e.n_q_heads;
+    const bool is_k = !is_q && head < e.n_q_heads + e.n_kv_heads;
+    const int d0 = 4 * lane;
+    float wn[4] = {1.f, 1.f, 1.f, 1.f};
+    if (is_q || is_k) unpack4_bf16(*reinterpret_cast<const uint2*>((is_q ? e.q_norm_w : e.k_norm_w) + d0), wn);
+    const int kvh = is_q ? 0 : (is_k ? head - e.n_q_heads : head - e.n_q_heads - e.n_kv_heads);
+    for (int m = warp; m < count; m += GEMM_THREADS / 32) {
+      const int row = m_begin + m;
+      const float4 a = lds_f4(acc_s + (uint32_t)((m * GEMM_BM + d0) * 4));
+      float v[4] = {bf16r(a.x), bf16r(a.y), bf16r(a.z), bf16r(a.w)};
+      if (is_q || is_k) {
+        int pos = e.positions[row];
+        pos = pos < 0 ? 0 : (pos >= e.max_positions ? e.max_positions - 1 : pos);
+        float cs[4], sn[4];
+        unpack4_bf16(*reinterpret_cast<const uint2*>(e.rope_cos + (long long)pos * 128 + d0), cs);
+        unpack4_bf16(*reinterpret_cast<const uint2*>(e.rope_sin + (long long)pos * 128 + d0), sn);
+        // models/qwen3.py:39-44 per head: fp32 mean of squares, cast back, times the bf16 weight
+        const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
+        const float r = 1.0f / sqrtf(ss / 128.0f + e.eps);
+        float nv[4], partner[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) nv[i] = bf16r(bf16r(v[i] * r) * wn[i]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) partner[i] = __shfl_xor_sync(0xFFFFFFFFu, nv[i], 16);
+        // models/qwen3.py:60-68: x * cos + rotate_half(x) * sin, three bf16 roundings
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          int n = lane + 32 * i;
-          float y = bf16r(acc[m * GEMM_BM + n]);
-          if (MODE == EPI_LOGITS) e.out[(long long)row * e.ldo + n0 + n] = __float2bfloat16_rn(y);
-          unsigned long long key = argmax_key(y, (uint32_t)(n0 + n));
-          best = key > best ? key : best;
+          const float rot = lane < 16 ? -partner[i] : partner[i];
+          v[i] = bf16r(bf16r(nv[i] * cs[i]) + bf16r(rot * sn[i]));
         }
-        best = warp_max_u64(best);
-        if (lane == 0 && e.argmax_keys) atomicMax(e.argmax_keys + row, best);
       }
-      break;
+      uint2 packed;
+      {
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]), h1 = __floats2bfloat162_rn(v[2], v[3]);
+        packed.x = *reinterpret_cast<uint32_t*>(&h0);
+        packed.y = *reinterpret_cast<uint32_t*>(&h1);
+      }
+      if (is_q) {
+        *reinterpret_cast<uint2*>(e.q_out + (long long)row * (e.n_q_heads * 128) + head * 128 + d0) = packed;
+      } else {
+        const long long slot = e.slot_mapping[row];
+        if (slot < 0 || slot >= e.num_cache_slots) {
+          if (lane == 0) report(e.status, NE_DEV_BAD_SLOT);
+          continue;
+        }
+        const long long base = (slot * e.n_kv_heads + kvh) * 128;
+        if (!e.kv_int8) {
+          *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(is_k ? e.k_cache : e.v_cache) + base + d0) =
+              packed;
+        } else {
+          // models/int8_quantization.py:30-34: scale = max|x| / 127 in fp32 (clamped), stored in the
+          // model dtype; q = round(x / scale) clamped to +-127
+          float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+          const float scale = fmaxf(amax, 1e-8f) / 127.0f;
+          uint32_t q4 = 0;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float q = fminf(fmaxf(rintf(v[i] / scale), -127.0f), 127.0f);
+            q4 |= (uint32_t)(uint8_t)(int8_t)q << (8 * i);
+          }
+          *reinterpret_cast<uint32_t*>(reinterpret_cast<int8_t*>(is_k ? e.k_cache : e.v_cache) + base + d0) = q4;
+          if (lane == 0) (is_k ? e.k_scale : e.v_scale)[slot * e.n_kv_heads + kvh] = __float2bfloat16_rn(scale);
+        }
+      }
     }
-    default:
-      break;
+  } else if (MODE == EPI_ARGMAX || MODE == EPI_LOGITS) {
+    // a warp per token; lane holds vocab columns 4*lane .. 4*lane+3 of the tile
+    for (int m = warp; m < count; m += GEMM_THREADS / 32) {
+      const int row = m_begin + m;
+      const float4 a = lds_f4(acc_s + (uint32_t)((m * GEMM_BM + 4 * lane) * 4));
+      const float y[4] = {bf16r(a.x), bf16r(a.y), bf16r(a.z), bf16r(a.w)};
+      if (MODE == EPI_LOGITS) {
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(y[0], y[1]), h1 = __floats2bfloat162_rn(y[2], y[3]);
+        uint2 packed;
+        packed.x = *reinterpret_cast<uint32_t*>(&h0);
+        packed.y = *reinterpret_cast<uint32_t*>(&h1);
+        *reinterpret_cast<uint2*>(e.out + (long long)row * e.ldo + n0 + 4 * lane) = packed;
+      }
+      unsigned long long best = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const unsigned long long key = argmax_key(y[i], (uint32_t)(n0 + 4 * lane + i));
+        best = key > best ? key : best;
+      }
+      best = warp_max_u64(best);
+      if (lane == 0 && e.argmax_keys) atomicMax(e.argmax_keys + row, best);
+    }
   }
-  (void)N;
 }
 
 template <int MODE>
@@ -273,7 +341,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   // Weights do not depend on the previous kernel: stream the first stages' weight tiles before
   // waiting for it. Their barriers get no arrival yet, so the phase cannot complete before the
   // activation tile's bytes are added below.
-  const int pre = min(stages, nk);
+  // only m-block 0 prefetches: a later m-block may find no rows (the step's rows are a device count)
+  const int pre = blockIdx.z == 0 ? min(stages, nk) : 0;
   if (warp == 0 && lane == 0) {
     for (int i = 0; i < pre; ++i) {
       mbar_expect_tx(&full[i], (uint32_t)w_bytes);
@@ -393,7 +462,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (c32 + i < cnt) stage_acc[(c32 + i) * GEMM_BM + warp * 32 + lane] = v[i];
       }
       __syncthreads();
-      if (ok) epilogue_rows<MODE>(p.epi, p.N, tile_n, m_begin + c0, cnt, stage_acc);
+      if (ok) epilogue_rows<MODE>(p.epi, tile_n, m_begin + c0, cnt, smem_u32(stage_acc));
       __syncthreads();
     }
   } else {
@@ -471,7 +540,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         sts_f4(red_s + i * 16, acc);
       }
       __syncthreads();
-      if (ok && got) epilogue_rows<MODE>(p.epi, p.N, tile_n, m_begin + split * slice, own_cnt, red);
+      if (ok && got) epilogue_rows<MODE>(p.epi, tile_n, m_begin + split * slice, own_cnt, red_s);
       __syncthreads();
     }
   }
@@ -621,7 +690,7 @@ int plan_uncached(GemmParams& p, int num_sms) {
   const int num_chunks = p.K / GEMM_BK;
   const int n_tiles = p.N / GEMM_BM;
   const int avail = GEMM_SMEM_DATA_BYTES;
-  int t_block = p.M_max <= GEMM_MAX_TOKENS ? ((p.M_max + 15) & ~15) : 256;
+  int t_block = p.M_max <= 256 ? ((p.M_max + 15) & ~15) : 256;
   int m_blocks = (p.M_max + t_block - 1) / t_block;
   int S = std::max(1, std::min(GEMM_MAX_SPLITS, num_sms / std::max(1, n_tiles * m_blocks)));
   if (p.epi.mode == EPI_ARGMAX || p.epi.mode == EPI_LOGITS) S = 1;
