@@ -692,7 +692,10 @@ int plan_uncached(GemmParams& p, int num_sms) {
   const int avail = GEMM_SMEM_DATA_BYTES;
   int t_block = p.M_max <= 256 ? ((p.M_max + 15) & ~15) : 256;
   int m_blocks = (p.M_max + t_block - 1) / t_block;
-  int S = std::max(1, std::min(GEMM_MAX_SPLITS, num_sms / std::max(1, n_tiles * m_blocks)));
+  // a verify step's row count is a device value well below its bound: size split-K for the first
+  // m-block (a later one that gets rows is a second wave); prefill-sized steps split by m-blocks
+  const int par = n_tiles * (p.M_max > 512 ? m_blocks : 1);
+  int S = std::max(1, std::min(GEMM_MAX_SPLITS, num_sms / std::max(1, par)));
   if (p.epi.mode == EPI_ARGMAX || p.epi.mode == EPI_LOGITS) S = 1;
   auto staging_bytes = [&](int s, int tb) {
     if (s == 1) return 128 * GEMM_BM * 4;
@@ -734,12 +737,13 @@ int plan_with_occupancy(GemmParams& p, int num_sms) {
   int rc = plan_uncached(p, num_sms);
   if (rc != NE_OK) return rc;
   const int m_blocks = (p.M_max + p.t_block - 1) / p.t_block;
+  const int par = n_tiles * (p.M_max > 512 ? m_blocks : 1);
   while (p.splits > 1) {
     const int fit = active_clusters(p.epi.mode, p.splits, p.smem_data + 256 + 1024);
-    if (fit >= n_tiles * m_blocks) break;
+    if (fit >= par) break;
     const int want = p.splits - 1;
     GemmParams q = p;
-    int sms = want * n_tiles * m_blocks;  // steer plan_uncached towards ``want`` splits
+    int sms = want * par;  // steer plan_uncached towards ``want`` splits
     rc = plan_uncached(q, sms);
     if (rc != NE_OK || q.splits >= p.splits) break;
     p = q;
