@@ -308,16 +308,17 @@ __global__ void __launch_bounds__(THREADS)
 
   if (ntiles == 1) {
     // ---------------------------------------------------------------- one tile, warps split blocks
-    load_q_tile(c, 0, q_s, tid, THREADS);
-    if (tid < 16) spos[tid] = tid < c.nvec ? rows.positions[c.r0 + tid / c.G] : -1;
-    __syncthreads();
-    TileState ts;
-    tile_init(ts, smem_u32(q_s), spos, lane);
+    // each warp's first K/V block goes out before the query tile (they do not depend on it)
     const uint32_t wbuf = buf_u + warp * 4 * BLOCK_BYTES;  // [stage][K,V]
     int kb = kb0 + warp;
     long long blk = kb < kb1 ? block_id(c, kb, rows.block_table_stride) : -1;
     if (blk >= 0) stage_block<INT8>(c, blk, wbuf, wbuf + BLOCK_BYTES, lane, 32);
     cp_commit();
+    load_q_tile(c, 0, q_s, tid, THREADS);
+    if (tid < 16) spos[tid] = tid < c.nvec ? rows.positions[c.r0 + tid / c.G] : -1;
+    __syncthreads();
+    TileState ts;
+    tile_init(ts, smem_u32(q_s), spos, lane);
     int stage = 0;
     for (; kb < kb1; kb += 4) {
       const int nkb = kb + 4;
@@ -342,11 +343,11 @@ __global__ void __launch_bounds__(THREADS)
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       const int row = (lane >> 2) + 8 * r;
+      if (row >= c.nvec) continue;  // padding rows of the tile are never read
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
         const int d = 8 * t + 2 * (lane & 3);
-        mo[(warp * 16 + row) * D + d] = ts.o[t][2 * r];
-        mo[(warp * 16 + row) * D + d + 1] = ts.o[t][2 * r + 1];
+        *reinterpret_cast<float2*>(&mo[(warp * 16 + row) * D + d]) = make_float2(ts.o[t][2 * r], ts.o[t][2 * r + 1]);
       }
       if ((lane & 3) == 0) {
         mm[warp * 16 + row] = ts.m[r];

@@ -183,49 +183,75 @@ __device__ void epilogue_rows(const Epilogue& e, int tile_n, int m_begin, int co
       *reinterpret_cast<uint4*>(e.out + (long long)(m_begin + m) * e.ldo + tile_n * 64 + c) = pack8_bf16(o);
     }
   } else if (MODE == EPI_QKV) {
-    // a warp per token; lane holds dims 4*lane .. 4*lane+3, RoPE partner dims are in lane ^ 16
+    // a warp per token; lane holds dims 4*lane .. 4*lane+3, RoPE partner dims are in lane ^ 16.
+    // Positions and slots of the rows come first (one load per thread); then each warp takes its
+    // tokens four at a time with the four tokens' cos/sin loads in flight together.
     const int head = tile_n;
     const bool is_q = head < e.n_q_heads;
     const bool is_k = !is_q && head < e.n_q_heads + e.n_kv_heads;
+    const bool rope = is_q || is_k;
     const int d0 = 4 * lane;
     float wn[4] = {1.f, 1.f, 1.f, 1.f};
-    if (is_q || is_k) unpack4_bf16(*reinterpret_cast<const uint2*>((is_q ? e.q_norm_w : e.k_norm_w) + d0), wn);
+    if (rope) unpack4_bf16(*reinterpret_cast<const uint2*>((is_q ? e.q_norm_w : e.k_norm_w) + d0), wn);
     const int kvh = is_q ? 0 : (is_k ? head - e.n_q_heads : head - e.n_q_heads - e.n_kv_heads);
-    for (int m = warp; m < count; m += GEMM_THREADS / 32) {
-      const int row = m_begin + m;
-      const float4 a = lds_f4(acc_s + (uint32_t)((m * GEMM_BM + d0) * 4));
-      float v[4] = {bf16r(a.x), bf16r(a.y), bf16r(a.z), bf16r(a.w)};
-      if (is_q || is_k) {
-        int pos = e.positions[row];
-        pos = pos < 0 ? 0 : (pos >= e.max_positions ? e.max_positions - 1 : pos);
-        float cs[4], sn[4];
-        unpack4_bf16(*reinterpret_cast<const uint2*>(e.rope_cos + (long long)pos * 128 + d0), cs);
-        unpack4_bf16(*reinterpret_cast<const uint2*>(e.rope_sin + (long long)pos * 128 + d0), sn);
-        // models/qwen3.py:39-44 per head: fp32 mean of squares, cast back, times the bf16 weight
-        const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
-        const float r = 1.0f / sqrtf(ss / 128.0f + e.eps);
-        float nv[4], partner[4];
+    int* pos_s = reinterpret_cast<int*>(e.scratch_smem);   // [count] positions, then [count] slots
+    int* slot_s = pos_s + GEMM_MAX_TOKENS;
+    for (int m = tid; m < count; m += GEMM_THREADS) {
+      int pos = rope ? e.positions[m_begin + m] : 0;
+      pos_s[m] = pos < 0 ? 0 : (pos >= e.max_positions ? e.max_positions - 1 : pos);
+      slot_s[m] = is_q ? 0 : e.slot_mapping[m_begin + m];
+    }
+    __syncthreads();
+    for (int m0t = warp; m0t < count; m0t += 4 * (GEMM_THREADS / 32)) {
+      uint2 cs_raw[4], sn_raw[4];
+      float4 acc4[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) nv[i] = bf16r(bf16r(v[i] * r) * wn[i]);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) partner[i] = __shfl_xor_sync(0xFFFFFFFFu, nv[i], 16);
-        // models/qwen3.py:60-68: x * cos + rotate_half(x) * sin, three bf16 roundings
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float rot = lane < 16 ? -partner[i] : partner[i];
-          v[i] = bf16r(bf16r(nv[i] * cs[i]) + bf16r(rot * sn[i]));
+      for (int t = 0; t < 4; ++t) {
+        const int m = m0t + t * (GEMM_THREADS / 32);
+        if (m < count) {
+          acc4[t] = lds_f4(acc_s + (uint32_t)((m * GEMM_BM + d0) * 4));
+          if (rope) {
+            cs_raw[t] = *reinterpret_cast<const uint2*>(e.rope_cos + (long long)pos_s[m] * 128 + d0);
+            sn_raw[t] = *reinterpret_cast<const uint2*>(e.rope_sin + (long long)pos_s[m] * 128 + d0);
+          }
         }
       }
-      uint2 packed;
-      {
-        __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]), h1 = __floats2bfloat162_rn(v[2], v[3]);
-        packed.x = *reinterpret_cast<uint32_t*>(&h0);
-        packed.y = *reinterpret_cast<uint32_t*>(&h1);
-      }
-      if (is_q) {
-        *reinterpret_cast<uint2*>(e.q_out + (long long)row * (e.n_q_heads * 128) + head * 128 + d0) = packed;
-      } else {
-        const long long slot = e.slot_mapping[row];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int m = m0t + t * (GEMM_THREADS / 32);
+        if (m >= count) continue;  // warp-uniform
+        const int row = m_begin + m;
+        float v[4] = {bf16r(acc4[t].x), bf16r(acc4[t].y), bf16r(acc4[t].z), bf16r(acc4[t].w)};
+        if (rope) {
+          float cs[4], sn[4];
+          unpack4_bf16(cs_raw[t], cs);
+          unpack4_bf16(sn_raw[t], sn);
+          // models/qwen3.py:39-44 per head: fp32 mean of squares, cast back, times the bf16 weight
+          const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
+          const float r = 1.0f / sqrtf(ss / 128.0f + e.eps);
+          float nv[4], partner[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) nv[i] = bf16r(bf16r(v[i] * r) * wn[i]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) partner[i] = __shfl_xor_sync(0xFFFFFFFFu, nv[i], 16);
+          // models/qwen3.py:60-68: x * cos + rotate_half(x) * sin, three bf16 roundings
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float rot = lane < 16 ? -partner[i] : partner[i];
+            v[i] = bf16r(bf16r(nv[i] * cs[i]) + bf16r(rot * sn[i]));
+          }
+        }
+        uint2 packed;
+        {
+          __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]), h1 = __floats2bfloat162_rn(v[2], v[3]);
+          packed.x = *reinterpret_cast<uint32_t*>(&h0);
+          packed.y = *reinterpret_cast<uint32_t*>(&h1);
+        }
+        if (is_q) {
+          *reinterpret_cast<uint2*>(e.q_out + (long long)row * (e.n_q_heads * 128) + head * 128 + d0) = packed;
+          continue;
+        }
+        const long long slot = slot_s[m];
         if (slot < 0 || slot >= e.num_cache_slots) {
           if (lane == 0) report(e.status, NE_DEV_BAD_SLOT);
           continue;
@@ -462,7 +488,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (c32 + i < cnt) stage_acc[(c32 + i) * GEMM_BM + warp * 32 + lane] = v[i];
       }
       __syncthreads();
-      if (ok) epilogue_rows<MODE>(p.epi, tile_n, m_begin + c0, cnt, smem_u32(stage_acc));
+      if (ok) {
+        Epilogue epi = p.epi;
+        epi.scratch_smem = stage_acc + 128 * GEMM_BM;  // past the [128][128] accumulator block
+        epilogue_rows<MODE>(epi, tile_n, m_begin + c0, cnt, smem_u32(stage_acc));
+      }
       __syncthreads();
     }
   } else {
@@ -540,7 +570,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         sts_f4(red_s + i * 16, acc);
       }
       __syncthreads();
-      if (ok && got) epilogue_rows<MODE>(p.epi, tile_n, m_begin + split * slice, own_cnt, red_s);
+      if (ok && got) {
+        Epilogue epi = p.epi;
+        epi.scratch_smem = send + (size_t)slice * GEMM_BM;  // the second send buffer is free now
+        epilogue_rows<MODE>(epi, tile_n, m_begin + split * slice, own_cnt, red_s);
+      }
       __syncthreads();
     }
   }
@@ -698,7 +732,7 @@ int plan_uncached(GemmParams& p, int num_sms) {
   int S = std::max(1, std::min(GEMM_MAX_SPLITS, num_sms / std::max(1, par)));
   if (p.epi.mode == EPI_ARGMAX || p.epi.mode == EPI_LOGITS) S = 1;
   auto staging_bytes = [&](int s, int tb) {
-    if (s == 1) return 128 * GEMM_BM * 4;
+    if (s == 1) return 128 * GEMM_BM * 4 + 2 * GEMM_MAX_TOKENS * 4;  // accumulator block + epilogue scratch
     const int slice = (((tb + s - 1) / s) + 7) & ~7;
     return (s + 1) * slice * GEMM_BM * 4;
   };

@@ -43,6 +43,7 @@ enum EpilogueMode : int {
 
 struct Epilogue {
   int mode;
+  void* scratch_smem;             // set by the kernel: 2 x GEMM_MAX_TOKENS ints of shared memory
   int* status;                    // device status word (bad slot reports)
   __nv_bfloat16* out;
   long long ldo;
