@@ -51,6 +51,22 @@ __device__ __forceinline__ void tmem_ld8_nowait(uint32_t taddr, uint32_t (&r)[8]
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Copy TMEM columns [c0, c0 + cnt) of all 128 lanes into smem ``dst`` as [token][128]. Warp w
+// reads lane quarter w % 4 (the only lanes a warp may address); warps w and w + 4 split the
+// columns in multiples of 8. Every warp of the CTA calls this (warp-collective TMEM loads).
+__device__ __forceinline__ void tmem_to_smem(uint32_t tmem_lane_base, int c0, int cnt, float* dst, int row);
+__device__ __forceinline__ void tmem_tile_to_smem(uint32_t tmem_base, int c0, int cnt, float* dst) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q = warp & 3, h = warp >> 2;
+  const int cnt8 = (cnt + 7) & ~7;
+  const int first = ((cnt8 / 2) + 7) & ~7;
+  const int begin = h == 0 ? 0 : first;
+  const int len = h == 0 ? first : cnt8 - first;
+  if (len > 0)
+    tmem_to_smem(tmem_base + ((uint32_t)(q * 32) << 16), c0 + begin, len, dst + (size_t)begin * GEMM_BM,
+                 q * 32 + lane);
+}
+
 // Copy TMEM columns [c0, c0 + cnt) (tokens) of this warp's 32 lanes (output rows) into smem
 // ``dst`` laid out [token][128]. cnt is a multiple of 8; all lanes of the warp call this.
 __device__ __forceinline__ void tmem_to_smem(uint32_t tmem_lane_base, int c0, int cnt, float* dst, int row) {
@@ -475,18 +491,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   if (S == 1) {
     for (int c0 = 0; c0 < t_actual; c0 += 128) {
       const int cnt = min(128, t_actual - c0);
-      for (int c32 = 0; c32 < cnt; c32 += 32) {
-        float v[32];
-        if (ok) {
-          tmem_ld32(tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(c0 + c32), v);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0.0f;
-        }
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c32 + i < cnt) stage_acc[(c32 + i) * GEMM_BM + warp * 32 + lane] = v[i];
-      }
+      if (ok) tmem_tile_to_smem(tmem_base, c0, cnt, stage_acc);
       __syncthreads();
       if (ok) {
         Epilogue epi = p.epi;
@@ -502,7 +507,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // sums the S partials of its slice in split order (deterministic) and runs the epilogue.
     float* send = stage_acc;                                   // [2][slice][128]
     float* recv = stage_acc + 2 * (size_t)slice * GEMM_BM;     // [S - 1][slice][128]
-    const uint32_t lane_base = tmem_base + ((uint32_t)(warp * 32) << 16);
     const uint32_t recv_local = smem_u32(recv);
     const uint32_t recv_bar_local = smem_u32(recv_bar);
     cluster_arrive();   // our mainloop is done: peers may now write our receive area
@@ -517,7 +521,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
         __syncthreads();
       }
-      if (ok) tmem_to_smem(lane_base, peer * slice, (cnt + 7) & ~7, buf, warp * 32 + lane);
+      if (ok) tmem_tile_to_smem(tmem_base, peer * slice, cnt, buf);
       fence_proxy_async_smem();
       __syncthreads();
       if (!waited) {
@@ -544,7 +548,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const bool got = *recv_ok != 0;
     float* red = send;  // the send buffers are free again
     if (own_cnt > 0) {
-      if (ok) tmem_to_smem(lane_base, split * slice, (own_cnt + 7) & ~7, red, warp * 32 + lane);
+      if (ok) tmem_tile_to_smem(tmem_base, split * slice, own_cnt, red);
       __syncthreads();
       // float4 per thread, all S partial loads issued before the adds (the CTA has only 4 warps,
       // so latency is hidden by instruction-level parallelism, not by other warps)

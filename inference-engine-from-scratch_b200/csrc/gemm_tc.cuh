@@ -10,8 +10,9 @@
 // cluster barrier each CTA sums the S partials of its own token slice (in split order, so the
 // result is deterministic) by reading its peers' shared memory (DSMEM). No global scratch.
 //
-// Roles (128 threads): warp 0 lane 0 issues TMA, warp 1 lane 0 issues tcgen05.mma, warp 2 owns
-// the TMEM allocation; all four warps run the epilogue (warp w reads TMEM lanes 32w..32w+31).
+// Roles (256 threads): warp 0 lane 0 issues TMA, warp 1 lane 0 issues tcgen05.mma, warp 2 owns
+// the TMEM allocation; all eight warps run the epilogue (warp w reads TMEM lanes 32(w%4)..+31, and
+// warps w and w+4 split the token columns).
 #pragma once
 
 #include <cuda.h>
@@ -23,7 +24,7 @@ namespace ne {
 constexpr int GEMM_BM = 128;         // weight rows per tile (MMA M)
 constexpr int GEMM_BK = 64;          // K elements per stage (128 bytes of bf16)
 constexpr int GEMM_XBOX = 64;        // token rows per X TMA box
-constexpr int GEMM_THREADS = 128;
+constexpr int GEMM_THREADS = 256;  // warps 0-3 run TMA / MMA / TMEM roles, all 8 run the epilogue
 constexpr int GEMM_MAX_TOKENS = 512; // tokens per CTA (TMEM columns)
 constexpr int GEMM_SMEM_BYTES = 227 * 1024;
 // data region (pipeline stages, later the epilogue staging); then 256 B of barriers; the rest is
