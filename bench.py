@@ -353,21 +353,22 @@ def run_b200(args, dist: Dist) -> None:
     lens = engine.state.seq_len[torch.tensor(slots, device=device).long()]
     ctx_before = int(lens.sum().item())
     launches_before = model.lib.ne_model_launch_count(model.handle)
-    ms_by = (ctypes.c_float * 12)()
-    n_by = (ctypes.c_int * 12)()
+    nk = len(lib_mod.KERNEL_KINDS)
+    ms_by = (ctypes.c_float * nk)()
+    n_by = (ctypes.c_int * nk)()
     lib_mod.check(model.lib.ne_model_profile_begin(model.handle, stream.cuda_stream), "profile_begin")
     engine._set_slots(slots, len(slots))
     engine._launch_step(len(slots))
-    lib_mod.check(model.lib.ne_model_profile_end(model.handle, ms_by, n_by, 12), "profile_end")
+    lib_mod.check(model.lib.ne_model_profile_end(model.handle, ms_by, n_by, nk), "profile_end")
     res = engine._collect(slots)
     launches_per_step = model.lib.ne_model_launch_count(model.handle) - launches_before
     M = len(slots) + res.proposed
     ctx_sum = ctx_before + res.proposed  # keys visible to the last row of every sequence
     per_layer_kv = model.kv_bytes_per_token() // cfg.num_hidden_layers
     kinds = lib_mod.KERNEL_KINDS
-    profile = {kinds[i]: {"ms": round(ms_by[i], 4), "launches": n_by[i]} for i in range(12) if n_by[i]}
-    step_ms_profiled = sum(ms_by[i] for i in range(12))
-    dominant = max((kinds[i] for i in range(12) if n_by[i]), key=lambda kk: ms_by[kinds.index(kk)])
+    profile = {kinds[i]: {"ms": round(ms_by[i], 4), "launches": n_by[i]} for i in range(nk) if n_by[i]}
+    step_ms_profiled = sum(ms_by[i] for i in range(nk))
+    dominant = max((kinds[i] for i in range(nk) if n_by[i]), key=lambda kk: ms_by[kinds.index(kk)])
     di = kinds.index(dominant)
     avg_ms = ms_by[di] / n_by[di]
     bytes_launch = algorithmic_bytes(dominant, cfg, M, ctx_sum, per_layer_kv)

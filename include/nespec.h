@@ -39,6 +39,7 @@ extern "C" {
 #define NE_DEV_OUT_OF_BLOCKS 4  /* the free-block FIFO could not cover a reservation */
 #define NE_DEV_BAD_TOKEN 8      /* a token id outside [0, vocab) */
 #define NE_DEV_HISTORY_FULL 16  /* a sequence outgrew its history row or block-table row */
+#define NE_DEV_NO_SAMPLER 32    /* temperature > 0 on a model without a sampling buffer */
 
 #define NE_ABI_VERSION 1
 
@@ -232,6 +233,36 @@ NE_API int ne_prefill(ne_model* model, const ne_batch_state* state, const int32_
 NE_API int ne_spec_step(ne_model* model, const ne_batch_state* state, const int32_t* seq_slot, int num_seqs,
                  int k, int max_ngram, const ne_step_outputs* out, void* stream);
 
+/* ---------------------------------------------------------------- sampled acceptance */
+/*
+ * Sequences with temperature > 0 are verified against their full target distribution
+ * (compute_token_probabilities, engine/sampling.py:30-38: softmax(logits / T), then top-p) by
+ * rejection sampling (verify_proposal, verifier.py:27-60), which needs each lm row's logits. A
+ * model that serves such sequences gets a sampling buffer: bf16 logits of up to ``max_lm_rows``
+ * rows plus per-row statistics, ne_sampling_buffer_bytes() bytes, 256-byte aligned. With a buffer
+ * bound, ne_prefill / ne_spec_step write the logits and sample where temperature > 0 (greedy
+ * sequences of the same batch still take the argmax); without one, a sampled sequence sets
+ * NE_DEV_NO_SAMPLER. Random numbers: uniform(seed, i) = (Philox4x32-10(counter = (i_lo, i_hi, 0, 0),
+ * key = (seed_lo, seed_hi)) word 0 >> 8) * 2^-24, i = rng_draws[s] advanced once per uniform used,
+ * in verify_proposal's order (one per guess with 0 < acceptance < 1, one per drawn token); a
+ * token is drawn by inverse CDF (the first id whose prefix mass exceeds u * total). Top-p ties
+ * at the cut are kept lowest id first.
+ */
+NE_API size_t ne_sampling_buffer_bytes(const ne_model* model, int max_lm_rows);
+NE_API int ne_model_set_sampling_buffer(ne_model* model, void* buffer, size_t bytes, int max_lm_rows);
+
+/*
+ * verify_proposal over caller-given target logits (a building block; the step calls the same
+ * kernels): for batch entry b of slot s = seq_slot[b], the guesses are history[s][seq_len[s] ..
+ * + draft_len[b]) and their target rows are logits[lm_start[b] .. + draft_len[b]] ([rows, vocab]
+ * bf16). Acceptance and commit as in ne_spec_step with q_len = draft_len + 1 (draft_len < 0:
+ * idle entry). ``scratch`` holds lm_rows x 32 bytes of row statistics.
+ */
+NE_API int ne_verify_logits(const ne_batch_state* state, const int32_t* seq_slot, int num_seqs, int k,
+                            const int32_t* draft_len, const int32_t* lm_start, const void* logits, int vocab,
+                            int lm_rows, void* scratch, size_t scratch_bytes, const ne_step_outputs* out,
+                            int32_t* status, void* stream);
+
 /* ---------------------------------------------------------------- launch accounting */
 /* Kernel classes of a step, for per-kernel device timing (ne_model_profile_*). */
 #define NE_K_EMBED 0
@@ -246,7 +277,8 @@ NE_API int ne_spec_step(ne_model* model, const ne_batch_state* state, const int3
 #define NE_K_PLAN 9
 #define NE_K_ACCEPT 10
 #define NE_K_OTHER 11
-#define NE_NUM_KINDS 12
+#define NE_K_SAMPLE 12       /* per-row softmax / top-p statistics of sampled sequences */
+#define NE_NUM_KINDS 13
 
 /* Kernels this model has launched so far (every entry point that takes the model counts). */
 NE_API long long ne_model_launch_count(const ne_model* model);

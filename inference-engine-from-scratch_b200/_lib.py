@@ -24,6 +24,7 @@ DEVICE_STATUS_BITS = {
     4: "the free-block FIFO could not cover a reservation (out of KV blocks)",
     8: "a token id outside the vocabulary",
     16: "a sequence outgrew its history or block-table row",
+    32: "a sequence with temperature > 0 on a model without a sampling buffer",
 }
 
 # (name, restype, argtypes) for every entry point of include/nespec.h
@@ -56,13 +57,20 @@ EXPORTS = {
          c_longlong, c_int, c_void_p, c_void_p],
     ),
     "ne_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p]),
+    "ne_sampling_buffer_bytes": (c_size_t, [c_void_p, c_int]),
+    "ne_model_set_sampling_buffer": (c_int, [c_void_p, c_void_p, c_size_t, c_int]),
+    "ne_verify_logits": (
+        c_int,
+        [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p,
+         c_void_p, c_void_p],
+    ),
     "ne_model_launch_count": (c_longlong, [c_void_p]),
     "ne_model_profile_begin": (c_int, [c_void_p, c_void_p]),
     "ne_model_profile_end": (c_int, [c_void_p, POINTER(c_float), POINTER(c_int), c_int]),
 }
 
 KERNEL_KINDS = ("embed", "rmsnorm", "gemm_qkv", "attention", "gemm_o", "gemm_gateup", "gemm_down", "lm_head",
-                "ngram", "plan", "accept", "other")
+                "ngram", "plan", "accept", "other", "sample")
 
 
 class ModelConfig(ctypes.Structure):

@@ -9,6 +9,7 @@
 #include "attention.cuh"
 #include "gemm_tc.cuh"
 #include "kernels.cuh"
+#include "sampling.cuh"
 
 using ne::GemmParams;
 
@@ -30,6 +31,10 @@ struct ne_model {
   void* attn_scratch = nullptr;
   size_t attn_scratch_bytes = 0;
   ne::RowBuffers rb{};
+  // sampling buffer: bf16 logits [sample_rows, vocab] + per-row statistics
+  __nv_bfloat16* sample_logits = nullptr;
+  ne::SampleStats* sample_stats = nullptr;
+  int sample_rows = 0;
   CUtensorMap tm_x{}, tm_attn{}, tm_act{};
   int num_sms = 148;
   // launch accounting / profiling
@@ -48,7 +53,11 @@ namespace {
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-constexpr size_t ATTN_SCRATCH_BYTES = 16u << 20;  // split-KV partials (few sequences, long contexts)
+constexpr size_t ATTN_SCRATCH_BYTES = 16u << 20;
+
+size_t sampling_logits_bytes(const ne_model_config& c, int rows) {
+  return align256((size_t)rows * c.vocab_size * 2);
+}  // split-KV partials (few sequences, long contexts)
 
 struct Layout {
   size_t status, h, x, q, attn, act, keys, rows_i32, seqs_i32, scalars, attn_scratch, total;
@@ -425,6 +434,68 @@ int ne_ngram_propose(const ne_batch_state* st, const int32_t* seq_slot, int num_
   return ne::launch_ngram(*st, seq_slot, num_seqs, k, max_ngram, min_ngram, draft_len, status, as_stream(stream));
 }
 
+}  // extern "C"
+
+namespace {
+
+// Forward with logits into the sampling buffer, per-row statistics, then acceptance for greedy
+// and sampled entries alike.
+int sampled_tail(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int k,
+                 const ne_rows& rows, bool spec, const ne_step_outputs* out, cudaStream_t s) {
+  int rc = ne_forward(m, &rows, NE_LM_LOGITS, m->sample_logits, nullptr, s);
+  if (rc) return rc;
+  rc = note(m, NE_K_SAMPLE,
+            ne::launch_sample_stats(*st, seq_slot, num_seqs, m->rb.lm_start, m->rb.q_len, m->rb.lm_count, rows.lm_max,
+                                    m->sample_logits, m->cfg.vocab_size, m->sample_stats, s), s);
+  if (rc) return rc;
+  return note(m, NE_K_ACCEPT,
+              ne::launch_accept_sampled(*st, seq_slot, num_seqs, k, spec ? m->rb.draft_len : nullptr, m->rb.q_len,
+                                        m->rb.lm_start, m->sample_logits, m->cfg.vocab_size, m->sample_stats,
+                                        m->keys, *out, m->status, s), s);
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t ne_sampling_buffer_bytes(const ne_model* m, int max_lm_rows) {
+  if (!m || max_lm_rows <= 0) return 0;
+  return sampling_logits_bytes(m->cfg, max_lm_rows) + align256((size_t)max_lm_rows * sizeof(ne::SampleStats));
+}
+
+int ne_model_set_sampling_buffer(ne_model* m, void* buffer, size_t bytes, int max_lm_rows) {
+  if (!m) return NE_ERR_INVALID;
+  if (!buffer) {  // unbind
+    m->sample_logits = nullptr;
+    m->sample_stats = nullptr;
+    m->sample_rows = 0;
+    return NE_OK;
+  }
+  if (max_lm_rows <= 0 || (reinterpret_cast<uintptr_t>(buffer) & 255u)) return NE_ERR_INVALID;
+  if (bytes < ne_sampling_buffer_bytes(m, max_lm_rows)) return NE_ERR_WORKSPACE;
+  m->sample_logits = static_cast<__nv_bfloat16*>(buffer);
+  m->sample_stats =
+      reinterpret_cast<ne::SampleStats*>(static_cast<char*>(buffer) + sampling_logits_bytes(m->cfg, max_lm_rows));
+  m->sample_rows = max_lm_rows;
+  return NE_OK;
+}
+
+int ne_verify_logits(const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int k, const int32_t* draft_len,
+                     const int32_t* lm_start, const void* logits, int vocab, int lm_rows, void* scratch,
+                     size_t scratch_bytes, const ne_step_outputs* out, int32_t* status, void* stream) {
+  if (!st || !seq_slot || !draft_len || !lm_start || !logits || !out || num_seqs <= 0 || k < 1 || vocab <= 0 ||
+      lm_rows <= 0 || !scratch || !st->temperature || !st->top_p || !st->rng_seed || !st->rng_draws)
+    return NE_ERR_INVALID;
+  if (scratch_bytes < (size_t)lm_rows * sizeof(ne::SampleStats)) return NE_ERR_WORKSPACE;
+  cudaStream_t s = as_stream(stream);
+  const __nv_bfloat16* lg = static_cast<const __nv_bfloat16*>(logits);
+  ne::SampleStats* stats = static_cast<ne::SampleStats*>(scratch);
+  int rc = ne::launch_sample_stats(*st, seq_slot, num_seqs, lm_start, nullptr, nullptr, lm_rows, lg, vocab, stats, s);
+  if (rc) return rc;
+  return ne::launch_accept_sampled(*st, seq_slot, num_seqs, k, draft_len, nullptr, lm_start, lg, vocab, stats,
+                                   nullptr, *out, status, s);
+}
+
 int ne_prefill(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int max_rows, int k,
                const ne_step_outputs* out, void* stream) {
   if (!m || !st || !seq_slot || !out || num_seqs <= 0 || k < 1) return NE_ERR_INVALID;
@@ -435,6 +506,10 @@ int ne_prefill(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, i
                                 m->cfg.num_cache_slots, m->rb, m->status, s), s);
   if (rc) return rc;
   ne_rows rows = make_step_rows(m, st, seq_slot, num_seqs, max_rows, num_seqs, max_rows);
+  if (m->sample_logits) {
+    if (num_seqs > m->sample_rows) return NE_ERR_WORKSPACE;
+    return sampled_tail(m, st, seq_slot, num_seqs, k, rows, false, out, s);
+  }
   rc = ne_forward(m, &rows, NE_LM_ARGMAX, nullptr, nullptr, stream);
   if (rc) return rc;
   return note(m, NE_K_ACCEPT,
@@ -456,6 +531,10 @@ int ne_spec_step(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot,
                             m->cfg.num_cache_slots, m->rb, m->status, s), s);
   if (rc) return rc;
   ne_rows rows = make_step_rows(m, st, seq_slot, num_seqs, max_rows, max_rows, k + 1);
+  if (m->sample_logits) {
+    if (max_rows > m->sample_rows) return NE_ERR_WORKSPACE;
+    return sampled_tail(m, st, seq_slot, num_seqs, k, rows, true, out, s);
+  }
   rc = ne_forward(m, &rows, NE_LM_ARGMAX, nullptr, nullptr, stream);
   if (rc) return rc;
   return note(m, NE_K_ACCEPT,

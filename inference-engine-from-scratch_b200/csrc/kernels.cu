@@ -287,6 +287,7 @@ __global__ void accept_greedy_kernel(ne_batch_state st, const int32_t* __restric
     out.accepted[b] = 0;
     return;
   }
+  if (st.temperature && st.temperature[s] > 0.f) report(status, NE_DEV_NO_SAMPLER);  // needs the logits
   const int g = mode == PLAN_SPEC ? max(rb.draft_len[b], 0) : 0;
   const int L = st.seq_len[s];
   int32_t* hist = st.history + (long long)s * st.history_stride;

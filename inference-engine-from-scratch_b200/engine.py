@@ -4,7 +4,8 @@
 what ``SpeculativeGenerator._run_speculative_step`` does for one sequence
 (engine/speculative/speculative_generator.py:70-85): n-gram draft with the guess cap
 ``min(k, remaining - 1)``, block reservation for the guesses, one (k+1)-token verify forward,
-acceptance, and the commit ``num_cached = len_before + kept``; then the emission / finish loop of
+acceptance (greedy, or rejection sampling on each request's Philox stream where temperature > 0),
+and the commit ``num_cached = len_before + kept``; then the emission / finish loop of
 ``_generate`` (:54-67). Per-sequence results equal the serial reference's, since batching changes
 no per-request arithmetic. With ``cuda_graphs`` every batch bucket (engine/generation/
 cuda_graph_runner.py:26 buckets) is captured once and replayed.
@@ -89,6 +90,7 @@ class B200SpeculativeEngine:
         stop_token_ids=(),
         cuda_graphs: bool = True,
         max_prefill_rows: int | None = None,
+        sampling: bool = False,
     ) -> None:
         self.lib = _lib.load()
         self.model = model
@@ -110,6 +112,14 @@ class B200SpeculativeEngine:
         self._slots_dev = torch.full((max_seqs,), -1, dtype=torch.int32, device=model.device)
         self._slots_host = torch.full((max_seqs,), -1, dtype=torch.int32).pin_memory()
         self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        # sampled requests (temperature > 0) need every lm row's logits: bind a sampling buffer
+        # (bound to the model before each eager launch or capture, since engines may share a model)
+        self.sampling = sampling
+        self._sample_rows = max_seqs * (k + 1)
+        self._sample_buf = None
+        if sampling:
+            nbytes = int(self.lib.ne_sampling_buffer_bytes(model.handle, self._sample_rows))
+            self._sample_buf = torch.empty(nbytes, dtype=torch.uint8, device=model.device)
         self.proposed_total = 0
         self.accepted_total = 0
         self.h2d_bytes = 0  # host->device bytes copied for requests and steps
@@ -119,13 +129,27 @@ class B200SpeculativeEngine:
     # ------------------------------------------------------------------ request lifecycle
     def add_request(self, prompt: list[int], max_new_tokens: int, *, ignore_eos: bool = False,
                     temperature: float = 0.0, top_p: float = 1.0, seed: int = 0) -> int:
-        if temperature != 0.0:
-            raise NotImplementedError("sampled acceptance is not built in this version of the B200 step")
+        """Load a request into a free slot. ``seed`` keys the request's Philox stream."""
+        if temperature != 0.0 and not self.sampling:
+            raise ValueError("temperature > 0 needs an engine built with sampling=True")
         slot = self.state.acquire()
         self.state.load(slot, prompt, max_new_tokens, ignore_eos=ignore_eos, temperature=temperature,
                         top_p=top_p, seed=seed)
         self.h2d_bytes += 4 * len(prompt) + 5 * 4 + 4 + 4 + 8 + 8
         return slot
+
+    def _bind_sampler(self) -> None:
+        buf = self._sample_buf
+        _lib.check(self.lib.ne_model_set_sampling_buffer(
+            self.model.handle, _lib.ptr(buf), 0 if buf is None else buf.numel(), self._sample_rows),
+            "ne_model_set_sampling_buffer")
+
+    def sampled_logits(self, rows: int) -> torch.Tensor:
+        """The last sampled step's target logits ``[rows, vocab]`` (bf16, lm-row order)."""
+        if self._sample_buf is None:
+            raise ValueError("the engine was built without sampling")
+        vocab = self.model.cfg.vocab_size
+        return self._sample_buf[: rows * vocab * 2].view(torch.bfloat16).view(rows, vocab)
 
     def release(self, slots: list[int]) -> None:
         self.state.release(slots)
@@ -170,6 +194,7 @@ class B200SpeculativeEngine:
         if rows > self.max_prefill_rows:
             raise ValueError(f"a prompt of {rows} tokens exceeds the prefill workspace")
         self._set_slots(slots, len(slots))
+        self._bind_sampler()
         _lib.check(self.lib.ne_prefill(self.model.handle, self.state.ref, self._slots_dev.data_ptr(), len(slots),
                                        rows, self.k, ctypes.byref(self.outputs.struct), _lib.stream_handle()),
                    "ne_prefill")
@@ -180,6 +205,7 @@ class B200SpeculativeEngine:
 
     # ------------------------------------------------------------------ speculative step
     def _launch_step(self, bucket: int) -> None:
+        self._bind_sampler()
         _lib.check(self.lib.ne_spec_step(self.model.handle, self.state.ref, self._slots_dev.data_ptr(), bucket,
                                          self.k, self.max_ngram, ctypes.byref(self.outputs.struct),
                                          _lib.stream_handle()), "ne_spec_step")
@@ -222,8 +248,10 @@ class B200SpeculativeEngine:
         return graph
 
     # ------------------------------------------------------------------ whole requests
-    def generate(self, prompts: list[list[int]], max_new_tokens: int, ignore_eos: bool = True) -> list[list[int]]:
-        """Serve every prompt with continuous batching (up to ``max_seqs`` at a time)."""
+    def generate(self, prompts: list[list[int]], max_new_tokens: int, ignore_eos: bool = True, *,
+                 temperature: float = 0.0, top_p: float = 1.0, seeds: list[int] | None = None) -> list[list[int]]:
+        """Serve every prompt with continuous batching (up to ``max_seqs`` at a time); request i
+        samples with ``seeds[i]`` (default i) when ``temperature`` > 0."""
         outputs: list[list[int]] = [[] for _ in prompts]
         pending = list(range(len(prompts)))
         running: dict[int, int] = {}  # slot -> request index
@@ -231,7 +259,9 @@ class B200SpeculativeEngine:
             admitted = []
             while pending and self.state.free_slots:
                 index = pending.pop(0)
-                slot = self.add_request(prompts[index], max_new_tokens, ignore_eos=ignore_eos)
+                slot = self.add_request(prompts[index], max_new_tokens, ignore_eos=ignore_eos,
+                                        temperature=temperature, top_p=top_p,
+                                        seed=seeds[index] if seeds is not None else index)
                 running[slot] = index
                 admitted.append(slot)
             if admitted:

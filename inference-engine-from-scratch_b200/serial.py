@@ -8,7 +8,9 @@ Same names, arguments and semantics as the reference (paths relative to nanoengi
 * ``PagedSlotAllocator``       engine/memory/paged_allocator.py:21-79
 * ``B200ModelRunner``          engine/generation/model_runner.py:14-80 (``run_step``, ``score_tokens``)
 * ``NgramProposer``            engine/speculative/proposers.py:39-60 (the suffix match runs on the GPU)
-* ``verify_proposal``          engine/speculative/verifier.py:27-60 (greedy: kernel argmax per row)
+* ``create_sampling_generator`` engine/sampling.py:12-18 (a Philox4x32-10 stream instead of torch's)
+* ``verify_proposal``          engine/speculative/verifier.py:27-60 (greedy: kernel argmax per row;
+  sampled: ``ne_verify_logits``, rejection sampling on the request's Philox stream)
 * ``SpeculativeGenerator``     engine/speculative/speculative_generator.py:21-90
 
 so that a reference user can swap the runner (and proposer) of the serial speculative path. The
@@ -19,6 +21,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 from collections import deque
 from collections.abc import Iterator
 from dataclasses import dataclass, field
@@ -28,6 +31,7 @@ import torch
 from . import _lib
 from .model import B200Model
 from .state import DeviceBatchState
+from .state import seed_as_int64 as _seed_as_int64
 
 GREEDY_TEMPERATURE = 0.0
 PADDING_TOKEN_ID = 0
@@ -57,17 +61,36 @@ class TokenEvent:
     finish_reason: str | None
 
 
+class PhiloxGenerator:
+    """A request's random stream: uniform i = (Philox4x32-10(counter=i, key=seed) word 0 >> 8) * 2^-24.
+
+    Stands where the reference keeps a ``torch.Generator`` (create_sampling_generator,
+    engine/sampling.py:12-18): a fixed seed always gives the same tokens, no seed draws one from
+    the OS. ``draws`` counts the uniforms consumed (the kernels advance it)."""
+
+    def __init__(self, seed: int | None = None) -> None:
+        self.seed = int(seed) if seed is not None else int.from_bytes(os.urandom(8), "little")
+        self.draws = 0
+
+
+def create_sampling_generator(seed: int | None, device=None) -> PhiloxGenerator:
+    """engine/sampling.py:12-18."""
+    return PhiloxGenerator(seed)
+
+
 @dataclass(eq=False)
 class Sequence:
     request: GenerationRequest
     token_ids: list[int]
     num_prompt_tokens: int
     num_cached_tokens: int = 0
+    sampling_generator: PhiloxGenerator | None = None
 
     @classmethod
     def from_request(cls, request: GenerationRequest, device=None) -> "Sequence":
         return cls(request=request, token_ids=list(request.prompt_token_ids),
-                   num_prompt_tokens=len(request.prompt_token_ids))
+                   num_prompt_tokens=len(request.prompt_token_ids),
+                   sampling_generator=create_sampling_generator(request.sampling_params.seed, device))
 
     @property
     def request_id(self) -> str:
@@ -234,15 +257,21 @@ class B200ModelRunner:
         return ids
 
     def run_step(self, sequences, token_counts=None) -> list[int]:
-        """Prefill (or continue) one sequence and return its next token (greedy argmax)."""
+        """Prefill (or continue) each sequence and return its next token: the argmax, or one draw
+        from its target distribution when sampling (ModelRunner._sample, model_runner.py:72-80)."""
         out = []
         for i, seq in enumerate(sequences):
-            if seq.sampling_params.temperature != GREEDY_TEMPERATURE:
-                raise NotImplementedError("sampled decoding is not built in this version of the B200 step")
             count = token_counts[i] if token_counts else seq.num_uncached_tokens
-            ids = self._forward(seq, count, [count - 1], None)
+            params = seq.sampling_params
+            sampled = params.temperature != GREEDY_TEMPERATURE
+            logits = None
+            if sampled:
+                logits = torch.empty((1, self.vocab_size), dtype=torch.bfloat16, device=self._device)
+            ids = self._forward(seq, count, [count - 1], logits)
             seq.num_cached_tokens += count
             self.allocator.on_tokens_cached(seq)
+            if sampled:
+                ids = _logits_verifier(self._device).verify([], logits, params, seq.sampling_generator)
             out.append(ids[0])
         return out
 
@@ -293,16 +322,92 @@ class NgramProposer:
         return None
 
 
+class _LogitsVerifier:
+    """``ne_verify_logits`` for one proposal at a time: a one-slot device state holds the guesses,
+    the request's sampling parameters and its Philox position."""
+
+    MAX_GUESSES = 16
+
+    def __init__(self, device) -> None:
+        self.lib = _lib.load()
+        self.device = torch.device(device)
+        k = self.MAX_GUESSES
+        self.state = DeviceBatchState(1, 8, k, 1, device=self.device)
+        self.state.flags.fill_(_lib.NE_SEQ_IGNORE_EOS)
+        i32 = dict(dtype=torch.int32, device=self.device)
+        self.slot = torch.zeros(1, **i32)
+        self.lm_start = torch.zeros(1, **i32)
+        self.draft_len = torch.zeros(1, **i32)
+        self.scratch = torch.zeros((k + 1) * 32, dtype=torch.uint8, device=self.device)
+        self.out = torch.zeros(k + 1 + 4, **i32)
+        base = self.out.data_ptr()
+        self.out_struct = _lib.StepOutputs(tokens=base, count=base + 4 * (k + 1), finish=base + 4 * (k + 2),
+                                           proposed=base + 4 * (k + 3), accepted=base + 4 * (k + 4))
+        self.status = torch.zeros(1, **i32)
+
+    def verify(self, guesses: list[int], logits: torch.Tensor, params: SamplingParams,
+               generator: PhiloxGenerator | None) -> list[int]:
+        g = len(guesses)
+        if g > self.MAX_GUESSES:
+            raise ValueError(f"at most {self.MAX_GUESSES} guesses per proposal")
+        if logits.dim() != 2 or logits.shape[0] < g + 1 or logits.dtype != torch.bfloat16 or not logits.is_cuda:
+            raise ValueError("target logits must be a CUDA bf16 tensor of [len(guesses) + 1, vocab]")
+        sampled = params.temperature != GREEDY_TEMPERATURE
+        if sampled and generator is None:
+            raise ValueError("sampled verification needs the request's generator")
+        st = self.state
+        hist = torch.zeros(st.history_stride, dtype=torch.int32)
+        hist[:g] = torch.tensor(guesses, dtype=torch.int32)
+        st.history[0].copy_(hist)
+        st.seq_len.zero_()
+        st.num_cached.zero_()
+        st.num_prompt.zero_()
+        st.max_new_tokens.fill_(1 << 30)
+        st.temperature.fill_(float(params.temperature))
+        st.top_p.fill_(float(params.top_p))
+        if sampled:
+            st.rng_seed.fill_(_seed_as_int64(generator.seed))
+            st.rng_draws.fill_(generator.draws)
+        self.draft_len.fill_(g)
+        logits = logits.contiguous()
+        _lib.check(self.lib.ne_verify_logits(
+            st.ref, self.slot.data_ptr(), 1, self.MAX_GUESSES, self.draft_len.data_ptr(), self.lm_start.data_ptr(),
+            logits.data_ptr(), logits.shape[1], g + 1, self.scratch.data_ptr(), self.scratch.numel(),
+            ctypes.byref(self.out_struct), self.status.data_ptr(), _lib.stream_handle()), "ne_verify_logits")
+        out = self.out.tolist()
+        count = out[self.MAX_GUESSES + 1]
+        word = int(self.status.item())
+        if word:
+            self.status.zero_()
+            raise _lib.NativeError(f"device reported: {_lib.describe_device_status(word)} (0x{word:x})")
+        if sampled:
+            generator.draws = int(st.rng_draws[0].item())
+        return out[:count]
+
+
+_VERIFIERS: dict[str, _LogitsVerifier] = {}
+
+
+def _logits_verifier(device) -> _LogitsVerifier:
+    key = str(torch.device(device))
+    if key not in _VERIFIERS:
+        _VERIFIERS[key] = _LogitsVerifier(device)
+    return _VERIFIERS[key]
+
+
 def verify_proposal(proposal: Proposal, target_logits: torch.Tensor, params: SamplingParams, generator=None,
                     target_argmax: list[int] | None = None) -> list[int]:
-    """Greedy verification (verifier.py:27-60 at temperature 0): kept guesses + one target token.
+    """verifier.py:27-60 with one-hot (n-gram) drafts: kept guesses + one target token.
 
-    ``target_argmax`` are the kernel's per-row argmax ids (lowest index on ties) of ``target_logits``.
+    Greedy: ``target_argmax`` (the kernel's per-row argmax ids, lowest index on ties) are compared
+    on the host; without them the verify kernel takes the argmax itself. Sampled: rejection
+    sampling on the GPU with ``generator`` (the request's ``PhiloxGenerator``), which advances.
     """
-    if params.temperature != GREEDY_TEMPERATURE:
-        raise NotImplementedError("sampled verification is not built in this version of the B200 step")
-    if target_argmax is None:
-        raise ValueError("the B200 verify needs the kernel's argmax ids (B200ModelRunner.last_argmax)")
+    if proposal.probabilities is not None:
+        raise ValueError("the B200 verify takes one-hot (n-gram) drafts")
+    if params.temperature != GREEDY_TEMPERATURE or target_argmax is None:
+        return _logits_verifier(target_logits.device).verify(list(proposal.token_ids), target_logits, params,
+                                                             generator)
     kept: list[int] = []
     for index, guess in enumerate(proposal.token_ids):
         if guess == target_argmax[index]:
@@ -374,8 +479,9 @@ class SpeculativeGenerator:
         self._runner.allocator.reserve(sequence, sequence.num_tokens)
         table = self._runner.allocator.block_table(sequence)
         target_logits = self._runner.score_tokens(sequence, 1 + len(proposal.token_ids))
-        new_tokens = verify_proposal(proposal, target_logits, sequence.sampling_params,
-                                     target_argmax=self._runner.last_argmax)
+        sampled = sequence.sampling_params.temperature != GREEDY_TEMPERATURE
+        new_tokens = verify_proposal(proposal, target_logits, sequence.sampling_params, sequence.sampling_generator,
+                                     target_argmax=None if sampled else self._runner.last_argmax)
         num_kept = len(new_tokens) - 1
         del sequence.token_ids[length_before:]
         sequence.num_cached_tokens = length_before + num_kept

@@ -18,6 +18,20 @@ import torch
 from . import _lib
 
 
+def check_sampling(temperature: float, top_p: float) -> None:
+    """The request API's bounds (api/schemas.py: temperature >= 0, 0 < top_p <= 1)."""
+    if not temperature >= 0.0:
+        raise ValueError(f"temperature must be >= 0, got {temperature}")
+    if not 0.0 < top_p <= 1.0:
+        raise ValueError(f"top_p must be in (0, 1], got {top_p}")
+
+
+def seed_as_int64(seed: int) -> int:
+    """A 64-bit Philox key as the signed value an int64 tensor holds (same bits)."""
+    seed = int(seed) & 0xFFFFFFFFFFFFFFFF
+    return seed - (1 << 64) if seed >= 1 << 63 else seed
+
+
 class DeviceBatchState:
     def __init__(
         self,
@@ -83,6 +97,7 @@ class DeviceBatchState:
         """Copy one request into sequence slot ``slot`` (Sequence.from_request)."""
         if len(prompt) == 0 or len(prompt) + max_new_tokens > self.max_model_len:
             raise ValueError(f"prompt of {len(prompt)} + {max_new_tokens} new tokens exceeds max_model_len")
+        check_sampling(temperature, top_p)
         L = len(prompt)
         self.history[slot, :L].copy_(torch.tensor(prompt, dtype=torch.int32), non_blocking=False)
         scalars = torch.tensor([L, 0, L, max_new_tokens, _lib.NE_SEQ_IGNORE_EOS if ignore_eos else 0],
@@ -95,7 +110,7 @@ class DeviceBatchState:
         self.flags[slot] = vals[4]
         self.temperature[slot] = float(temperature)
         self.top_p[slot] = float(top_p)
-        self.rng_seed[slot] = int(seed)
+        self.rng_seed[slot] = seed_as_int64(seed)
         self.rng_draws[slot] = 0
 
     def acquire(self) -> int:

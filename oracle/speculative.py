@@ -156,7 +156,7 @@ class OracleRunner:
         return hidden
 
     @torch.inference_mode()
-    def run_step(self, seqs: list[Seq], uniforms_by_seq=None) -> tuple[list[int], torch.Tensor]:
+    def run_step(self, seqs: list[Seq], uniforms_by_seq=None, stable: bool = False) -> tuple[list[int], torch.Tensor]:
         """model_runner.py:33-50,64-80: prefill all uncached tokens, sample one token each."""
         counts = [s.num_tokens - s.num_cached_tokens for s in seqs]
         hidden = self.forward_rows(seqs, counts)
@@ -165,7 +165,7 @@ class OracleRunner:
         tokens = torch.argmax(logits, dim=-1).tolist()
         for row, s in enumerate(seqs):
             if s.temperature != verify.GREEDY_TEMPERATURE:
-                probs = verify.token_probabilities(logits[row], s.temperature, s.top_p)
+                probs = verify.token_probabilities(logits[row], s.temperature, s.top_p, stable)
                 tokens[row] = verify.inverse_cdf(probs, next(uniforms_by_seq[row]))
         return tokens, logits
 
@@ -219,14 +219,16 @@ def generate(
     uniforms=None,
     keep_logits: bool = True,
     free_at_end: bool = True,
+    stable: bool = False,
 ) -> Generation:
-    """engine/speculative/speculative_generator.py:42-85 with ``NgramProposer`` drafts."""
+    """engine/speculative/speculative_generator.py:42-85 with ``NgramProposer`` drafts
+    (``stable``: top-p ties by ascending id, as ``verify.apply_top_p`` documents)."""
     stream = _CountingStream(uniforms if uniforms is not None else iter(()))
     out = Generation()
     try:
         runner.tables.reserve(seq.request_id, seq.num_tokens)
         out.prefill_block_table = list(runner.tables.tables[seq.request_id])
-        new_tokens, logits = runner.run_step([seq], [stream])
+        new_tokens, logits = runner.run_step([seq], [stream], stable)
         out.prefill_logits = logits[0] if keep_logits else None
         while True:
             for token in new_tokens:
@@ -246,7 +248,7 @@ def generate(
             table = list(runner.tables.tables[seq.request_id])
             target_logits = runner.score_tokens(seq, 1 + len(draft))
             new_tokens = verify.verify_proposal(
-                draft, None, target_logits, seq.temperature, seq.top_p, stream
+                draft, None, target_logits, seq.temperature, seq.top_p, stream, stable
             )
             kept = len(new_tokens) - 1
             del seq.token_ids[length_before:]

@@ -28,22 +28,26 @@ from torch.nn import functional
 GREEDY_TEMPERATURE = 0.0
 
 
-def apply_top_p(probabilities: torch.Tensor, top_p: float) -> torch.Tensor:
-    """engine/sampling.py:21-27: keep tokens whose sorted mass-before is < top_p, renormalise."""
-    sorted_p, order = torch.sort(probabilities, descending=True)
+def apply_top_p(probabilities: torch.Tensor, top_p: float, stable: bool = False) -> torch.Tensor:
+    """engine/sampling.py:21-27: keep tokens whose sorted mass-before is < top_p, renormalise.
+
+    ``stable=False`` is the reference's own (unstable) ``torch.sort``; ``stable=True`` orders equal
+    probabilities by ascending token id, the convention of the CUDA kernels (which tokens of a tie
+    group straddling the cut survive is otherwise implementation-defined)."""
+    sorted_p, order = torch.sort(probabilities, descending=True, stable=stable)
     before = torch.cumsum(sorted_p, dim=-1) - sorted_p
     sorted_p[before >= top_p] = 0.0
     kept = torch.zeros_like(probabilities).scatter(-1, order, sorted_p)
     return kept / kept.sum(dim=-1, keepdim=True)
 
 
-def token_probabilities(logits: torch.Tensor, temperature: float, top_p: float) -> torch.Tensor:
+def token_probabilities(logits: torch.Tensor, temperature: float, top_p: float, stable: bool = False) -> torch.Tensor:
     """engine/sampling.py:30-38 (one-hot argmax when greedy)."""
     if temperature == GREEDY_TEMPERATURE:
         return functional.one_hot(torch.argmax(logits, dim=-1), logits.shape[-1]).float()
     probabilities = torch.softmax(logits.float() / temperature, dim=-1)
     if top_p < 1.0:
-        probabilities = apply_top_p(probabilities, top_p)
+        probabilities = apply_top_p(probabilities, top_p, stable)
     return probabilities
 
 
@@ -67,9 +71,10 @@ def verify_proposal(
     temperature: float,
     top_p: float,
     uniforms,
+    stable: bool = False,
 ) -> list[int]:
     """engine/speculative/verifier.py:27-60: kept guesses plus one target token."""
-    target = token_probabilities(target_logits, temperature, top_p)
+    target = token_probabilities(target_logits, temperature, top_p, stable)
     vocab = target.shape[-1]
     kept: list[int] = []
     for index, guess in enumerate(guesses):

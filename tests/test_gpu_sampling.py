@@ -1,0 +1,399 @@
+"""Sampled acceptance on the GPU (temperature + top-p, rejection sampling on the Philox stream).
+
+The kernels follow compute_token_probabilities / apply_top_p (engine/sampling.py:21-38) and
+verify_proposal (engine/speculative/verifier.py:27-60) with one-hot drafts; the random numbers
+come from each request's Philox4x32-10 stream in the reference's draw order.
+
+Exactness: the GPU computes the softmax with its own exp and sums, so a decision whose two sides
+are closer than float rounding (a uniform within MARGIN of an acceptance probability or of a
+prefix-mass boundary of the inverse CDF, or the top-p cut within TOPP_MARGIN of a token's
+mass-before) may fall the other way. Every mismatch with the oracle must be such a near-tie, and
+most cases must match exactly. Against the reference itself, a cut that splits a group of equal
+probabilities is also a tie: torch.sort is not stable there, the kernels keep the lowest ids.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ngram as ongram
+from oracle import philox
+from oracle import verify as overify
+from tests.conftest import load_golden, package, submodule
+
+pytestmark = pytest.mark.gpu
+
+MARGIN = 1e-5        # |u - acceptance|, |u - prefix / total|
+TOPP_MARGIN = 1e-6   # |mass-before - top_p| at the top-p cut
+MIN_EXACT = 0.9      # fraction of cases that must match bit for bit
+CHI_SQUARE_CRITICAL_4_DEGREES_999 = 18.47  # tests/engine/test_speculative_decoding.py:27
+CHI_SQUARE_CRITICAL_2_DEGREES_999 = 13.82
+CHI_SQUARE_TRIALS = 6000
+
+
+@pytest.fixture(scope="module")
+def lib():
+    submodule("build").build()
+    return submodule("_lib").load()
+
+
+# ------------------------------------------------------------------ batched ne_verify_logits
+def run_verify(lib, cases, device="cuda:0"):
+    """cases: dicts with logits ([g + 1, V], one V for all), guesses, temperature, top_p, seed,
+    start (Philox position). Returns (tokens per case, Philox position after each case)."""
+    _lib = submodule("_lib")
+    state_mod = submodule("state")
+    B = len(cases)
+    K = max(1, max(len(c["guesses"]) for c in cases))
+    vocab = cases[0]["logits"].shape[-1]
+    st = state_mod.DeviceBatchState(B, 8, K, 1, device=device)
+    hist = torch.zeros(B, st.history_stride, dtype=torch.int32)
+    starts, draft = [], []
+    rows = 0
+    for b, c in enumerate(cases):
+        g = len(c["guesses"])
+        if g:
+            hist[b, :g] = torch.tensor(c["guesses"], dtype=torch.int32)
+        starts.append(rows)
+        draft.append(g)
+        rows += g + 1
+    st.history.copy_(hist)
+    st.seq_len.zero_()
+    st.num_cached.zero_()
+    st.num_prompt.zero_()
+    st.max_new_tokens.fill_(1 << 30)
+    st.flags.fill_(_lib.NE_SEQ_IGNORE_EOS)
+    st.temperature.copy_(torch.tensor([float(c["temperature"]) for c in cases]))
+    st.top_p.copy_(torch.tensor([float(c["top_p"]) for c in cases]))
+    st.rng_seed.copy_(torch.tensor([state_mod.seed_as_int64(c["seed"]) for c in cases], dtype=torch.int64))
+    st.rng_draws.copy_(torch.tensor([int(c.get("start", 0)) for c in cases], dtype=torch.int64))
+    logits = torch.cat([c["logits"].to(torch.bfloat16) for c in cases]).to(device).contiguous()
+    i32 = dict(dtype=torch.int32, device=device)
+    slots = torch.arange(B, **i32)
+    lm_start = torch.tensor(starts, **i32)
+    draft_len = torch.tensor(draft, **i32)
+    scratch = torch.zeros(rows * 32, dtype=torch.uint8, device=device)
+    out = torch.zeros(B * (K + 1) + 4 * B, **i32)
+    base = out.data_ptr()
+    w = K + 1
+    outs = _lib.StepOutputs(tokens=base, count=base + 4 * B * w, finish=base + 4 * B * (w + 1),
+                            proposed=base + 4 * B * (w + 2), accepted=base + 4 * B * (w + 3))
+    status = torch.zeros(1, **i32)
+    _lib.check(lib.ne_verify_logits(st.ref, slots.data_ptr(), B, K, draft_len.data_ptr(), lm_start.data_ptr(),
+                                    logits.data_ptr(), vocab, rows, scratch.data_ptr(), scratch.numel(),
+                                    ctypes.byref(outs), status.data_ptr(), _lib.stream_handle()), "ne_verify_logits")
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    host = out.cpu()
+    tokens = host[: B * w].view(B, w)
+    count = host[B * w: B * (w + 1)]
+    got = [tokens[b, : int(count[b])].tolist() for b in range(B)]
+    return got, st.rng_draws.cpu().tolist()
+
+
+# ------------------------------------------------------------------ float64 decision margins
+def decision_margins(logits, guesses, temperature, top_p, seed, start):
+    """Replays verify_proposal in float64 (stable top-p) and returns (smallest distance of a
+    uniform to the threshold it was compared with, smallest distance of a mass-before to top_p at
+    a cut, whether a cut splits a group of equal probabilities)."""
+    x = logits.float()
+    if temperature == 0.0:
+        return 1.0, 1.0, False
+    y = (x / temperature).double()
+    p = torch.softmax(y, dim=-1).numpy()
+    p32 = torch.softmax(x / temperature, dim=-1).numpy()
+    topp_margin, tie_split = 1.0, False
+    if top_p < 1.0:
+        rows = []
+        for r in range(p.shape[0]):
+            order = np.argsort(-p[r], kind="stable")
+            srt = p[r][order]
+            before = np.cumsum(srt) - srt
+            cut = int((before < top_p).sum())
+            for i in (cut - 1, cut):
+                if 0 <= i < len(before):
+                    topp_margin = min(topp_margin, abs(before[i] - top_p))
+            if 0 < cut < len(srt):
+                s32 = p32[r][order]
+                tie_split |= bool(s32[cut - 1] == s32[cut])
+            kept = np.zeros_like(p[r])
+            kept[order[:cut]] = srt[:cut]
+            rows.append(kept / kept.sum())
+        p = np.stack(rows)
+    stream = philox.UniformStream(seed, start)
+    margin = 1.0
+
+    def draw(dist):
+        nonlocal margin
+        u = next(stream)
+        c = np.cumsum(dist) / dist.sum()
+        i = int(np.searchsorted(c, u, side="right"))
+        for j in (i - 1, i):
+            if 0 <= j < len(c):
+                margin = min(margin, abs(c[j] - u))
+
+    for j, g in enumerate(guesses):
+        a = min(p[j, g], 1.0)
+        margin = min(margin, abs(1.0 - p[j, g]))
+        if a >= 1.0:
+            continue
+        if a < MARGIN:
+            margin = min(margin, a)
+        if a > 0.0:
+            u = next(stream)
+            margin = min(margin, abs(u - a))
+            if u < a:
+                continue
+        residual = p[j].copy()
+        residual[g] = 0.0
+        if residual.sum() <= 0:
+            residual = p[j]
+        draw(residual)
+        return margin, topp_margin, tie_split
+    draw(p[len(guesses)])
+    return margin, topp_margin, tie_split
+
+
+def excused(case, unstable_reference=False) -> bool:
+    m, tm, tie = decision_margins(case["logits"], case["guesses"], case["temperature"], case["top_p"],
+                                  case["seed"], case.get("start", 0))
+    return m < MARGIN or tm < TOPP_MARGIN or (unstable_reference and tie)
+
+
+def oracle_verify(case, stable=True):
+    stream = philox.UniformStream(case["seed"], case.get("start", 0))
+    got = overify.verify_proposal(case["guesses"], None, case["logits"].float(), case["temperature"],
+                                  case["top_p"], stream, stable)
+    return got, stream.index
+
+
+def check_against(cases, got, draws, expected, expected_draws, unstable_reference=False):
+    exact = 0
+    for case, g, d, e, ed in zip(cases, got, draws, expected, expected_draws):
+        if g == e and d == ed:
+            exact += 1
+            continue
+        assert excused(case, unstable_reference), (
+            f"mismatch without a near-tie: got {g} (draws {d}), expected {e} (draws {ed}), "
+            f"T={case['temperature']} top_p={case['top_p']} guesses={case['guesses']}")
+    assert exact >= MIN_EXACT * len(cases), f"only {exact} of {len(cases)} cases match exactly"
+
+
+# ------------------------------------------------------------------ tests
+def test_verify_matches_the_reference_golden_cases(lib) -> None:
+    """verify_cases.pt: the reference's verify_proposal with the same injected Philox uniforms."""
+    cases = [c for c in load_golden("verify_cases.pt")["cases"] if c["logits"].dtype == torch.bfloat16]
+    assert len(cases) >= 30
+    by_vocab: dict[int, list] = {}
+    for c in cases:
+        by_vocab.setdefault(c["logits"].shape[-1], []).append(dict(c, start=0))
+    for group in by_vocab.values():
+        got, draws = run_verify(lib, group)
+        check_against(group, got, draws, [c["expected"] for c in group], [c["draws"] for c in group],
+                      unstable_reference=True)
+
+
+def _random_cases(n, vocab, seed):
+    g = torch.Generator().manual_seed(seed)
+    cases = []
+    for i in range(n):
+        k = int(torch.randint(0, 9, (1,), generator=g))
+        temperature = [0.8, 1.0, 0.3, 0.0][i % 4]
+        top_p = [1.0, 0.95, 0.5][(i // 4) % 3]
+        scale = [1.0, 4.0, 12.0][(i // 12) % 3]
+        logits = (torch.randn(k + 1, vocab, generator=g) * scale).to(torch.bfloat16)
+        best = torch.argmax(logits.float(), dim=-1)
+        probs = torch.softmax(logits.float() / max(temperature, 1e-3), dim=-1)
+        guesses = []
+        for j in range(k):  # the target's favourite, a sample from the target, or a random id
+            r = float(torch.rand((), generator=g))
+            if r < 0.4:
+                guesses.append(int(best[j]))
+            elif r < 0.8:
+                guesses.append(int(torch.multinomial(probs[j], 1, generator=g)))
+            else:
+                guesses.append(int(torch.randint(0, vocab, (1,), generator=g)))
+        cases.append({"logits": logits, "guesses": guesses, "temperature": temperature, "top_p": top_p,
+                      "seed": 7919 * i + 17, "start": int(torch.randint(0, 1 << 40, (1,), generator=g))})
+    return cases
+
+
+@pytest.mark.parametrize("vocab,n", [(1000, 192), (4096, 96), (151936, 24)])
+def test_verify_matches_the_stable_oracle(lib, vocab, n) -> None:
+    cases = _random_cases(n, vocab, seed=vocab)
+    got, draws = run_verify(lib, cases)
+    expected = [oracle_verify(c) for c in cases]
+    check_against(cases, got, draws, [e[0] for e in expected], [e[1] for e in expected])
+
+
+def test_same_seed_same_tokens_and_seeds_differ(lib) -> None:
+    base = _random_cases(64, 4096, seed=3)
+    cases = [dict(c, temperature=1.0, top_p=0.95) for c in base]
+    first = run_verify(lib, cases)
+    second = run_verify(lib, cases)
+    assert first == second
+    reseeded = run_verify(lib, [dict(c, seed=c["seed"] + 1) for c in cases])
+    assert reseeded[0] != first[0]
+
+
+@pytest.mark.parametrize("top_p,kept", [(1.0, 5), (0.8, 3)])
+def test_first_token_follows_the_target_distribution(lib, top_p, kept) -> None:
+    """tests/engine/test_speculative_decoding.py:58-74 with one-hot (n-gram) drafts: a guess drawn
+    from a disagreeing draft, verified against the target; the first token must be distributed like
+    the target itself (chi-square, 99.9%)."""
+    target = torch.tensor([0.4, 0.3, 0.15, 0.1, 0.05])
+    draft = torch.tensor([0.05, 0.1, 0.15, 0.3, 0.4])
+    logits = torch.log(target).repeat(2, 1).to(torch.bfloat16)
+    g = torch.Generator().manual_seed(7)
+    cases = []
+    for t in range(CHI_SQUARE_TRIALS):
+        guess = int(torch.multinomial(draft, 1, generator=g))
+        cases.append({"logits": logits, "guesses": [guess], "temperature": 1.0, "top_p": top_p, "seed": t})
+    got, _ = run_verify(lib, cases)
+    counts = torch.zeros(5)
+    for tokens in got:
+        counts[tokens[0]] += 1
+    expected_p = overify.token_probabilities(logits[0].float(), 1.0, top_p, True)
+    assert int((expected_p > 0).sum()) == kept
+    assert counts[expected_p == 0].sum() == 0
+    mask = expected_p > 0
+    expected = expected_p[mask] * CHI_SQUARE_TRIALS
+    chi_square = float(((counts[mask] - expected) ** 2 / expected).sum())
+    critical = CHI_SQUARE_CRITICAL_4_DEGREES_999 if kept == 5 else CHI_SQUARE_CRITICAL_2_DEGREES_999
+    assert chi_square < critical
+
+
+def test_tiny_top_p_always_picks_the_top_token(lib) -> None:
+    """tests/engine/test_sampling_and_generation.py:55-60."""
+    logits = torch.tensor([[0.0, 5.0, 1.0]]).to(torch.bfloat16)
+    cases = [{"logits": logits, "guesses": [], "temperature": 1.0, "top_p": 0.01, "seed": s} for s in range(20)]
+    got, _ = run_verify(lib, cases)
+    assert {t[0] for t in got} == {1}
+
+
+def test_greedy_rows_take_the_argmax(lib) -> None:
+    """tests/engine/test_speculative_decoding.py:45-55 through the logits path (temperature 0)."""
+    logits = torch.full((4, 6), -10.0)
+    for row, best in enumerate([2, 4, 1, 5]):
+        logits[row, best] = 10.0
+    cases = [{"logits": logits, "guesses": gs, "temperature": 0.0, "top_p": 1.0, "seed": 0}
+             for gs in ([2, 4, 1], [2, 3, 1])]
+    got, draws = run_verify(lib, cases)
+    assert got == [[2, 4, 1, 5], [2, 4]]
+    assert draws == [0, 0]
+
+
+# ------------------------------------------------------------------ the batched engine, sampled
+@pytest.fixture(scope="module")
+def small_model():
+    submodule("build").build()
+    pkg = package()
+    cfg = pkg.SMALL_TEST
+    weights = pkg.make_weights(cfg, seed=0)
+    model = submodule("model").B200Model(cfg, weights, num_slots=128 * 16, device="cuda:0", max_positions=512,
+                                         max_rows=512, max_seqs=16)
+    return cfg, model
+
+
+@pytest.mark.parametrize("cuda_graphs", [False, True])
+def test_engine_sampled_steps_match_the_oracle_on_their_logits(small_model, cuda_graphs) -> None:
+    """Every step of the batched engine (mixed greedy and sampled requests) is replayed by the
+    oracle's verify_proposal on the step's own target logits and Philox positions."""
+    cfg, model = small_model
+    pkg = package()
+    engine_mod = submodule("engine")
+    k, max_ngram, max_new = 4, 3, 40
+    eng = engine_mod.B200SpeculativeEngine(model, k=k, max_ngram=max_ngram, max_seqs=8, max_model_len=256,
+                                           num_blocks=96, cuda_graphs=cuda_graphs, sampling=True)
+    eng.state.reset_blocks()
+    prompts = pkg.make_prompts(6, cfg.vocab_size, length=48, seed=5)
+    params = [(0.8, 0.95), (1.0, 1.0), (0.0, 1.0), (0.3, 0.5), (0.8, 0.95), (1.0, 0.9)]
+    slots, meta = [], {}
+    for i, (prompt, (t, p)) in enumerate(zip(prompts, params)):
+        slot = eng.add_request(prompt, max_new, ignore_eos=True, temperature=t, top_p=p, seed=100 + i)
+        slots.append(slot)
+        meta[slot] = (t, p, 100 + i)
+    cases, got_all, draws_all, expected_all, expected_draws = [], [], [], [], []
+
+    def record(active, res, g_by_slot, hist_before, draws_before, draws_after, first):
+        logits = eng.sampled_logits(sum(g_by_slot[s] + 1 for s in active) if not first else len(active))
+        row = 0
+        for s in active:
+            t, p, seed = meta[s]
+            g = 0 if first else g_by_slot[s]
+            guesses = [] if first else ongram.propose(hist_before[s], g, max_ngram)
+            assert len(guesses) == g
+            case = {"logits": logits[row:row + g + 1].float().cpu(), "guesses": guesses, "temperature": t,
+                    "top_p": p, "seed": seed, "start": draws_before[s]}
+            row += g + 1
+            exp, exp_draws = oracle_verify(case)
+            emitted = res.tokens[s]
+            cases.append(case)
+            got_all.append(emitted)
+            draws_all.append(draws_after[s])
+            expected_all.append(exp[: len(emitted)])
+            expected_draws.append(exp_draws)
+
+    hist_before = {s: eng.state.tokens(s) for s in slots}
+    draws_before = dict(zip(slots, eng.state.rng_draws.cpu().tolist()))
+    res = eng.prefill(slots, [len(p) for p in prompts])
+    draws_after = eng.state.rng_draws.cpu().tolist()
+    record(slots, res, None, hist_before, draws_before, draws_after, first=True)
+    running = [s for s in slots if res.finish[s] is None]
+    while running:
+        hist_before = {s: eng.state.tokens(s) for s in running}
+        draws_before = {s: eng.state.rng_draws[s].item() for s in running}
+        g_by_slot = {}
+        for s in running:
+            remaining = max_new - (len(hist_before[s]) - len(prompts[slots.index(s)]))
+            g_by_slot[s] = len(ongram.propose(hist_before[s], max(0, min(k, remaining - 1)), max_ngram))
+        res = eng.step(running)
+        draws_after = eng.state.rng_draws.cpu().tolist()
+        record(running, res, g_by_slot, hist_before, draws_before, draws_after, first=False)
+        running = [s for s in running if res.finish[s] is None]
+    model.raise_on_device_error()
+    check_against(cases, got_all, draws_all, expected_all, expected_draws)
+    assert any(c["temperature"] > 0 and len(c["guesses"]) > 0 for c in cases)
+
+
+def test_engine_refuses_sampling_without_a_buffer(small_model) -> None:
+    _, model = small_model
+    eng = submodule("engine").B200SpeculativeEngine(model, k=4, max_seqs=4, max_model_len=256, num_blocks=32,
+                                                    cuda_graphs=False)
+    with pytest.raises(ValueError):
+        eng.add_request([1, 2, 3], 8, temperature=0.8)
+
+
+def test_serial_sampled_generation_is_reproducible_and_replays_on_the_oracle(small_model) -> None:
+    cfg, model = small_model
+    serial = submodule("serial")
+    pkg = package()
+    prompt = pkg.make_prompts(1, cfg.vocab_size, length=48, seed=9)[0]
+    runs = []
+    for _ in range(2):
+        allocator = serial.PagedSlotAllocator(64, 16)
+        runner = serial.B200ModelRunner(model, allocator)
+        proposer = serial.NgramProposer(3, max_model_len=256, device="cuda:0")
+        counters = serial.SpeculativeCounters()
+        gen = serial.SpeculativeGenerator(runner, proposer, 4, frozenset(), metrics=counters)
+        params = serial.SamplingParams(max_new_tokens=32, temperature=0.8, top_p=0.95, seed=42, ignore_eos=True)
+        tokens = [e.token_id for e in gen.generate(serial.GenerationRequest("r", prompt, params))]
+        runs.append((tokens, counters.steps))
+    assert runs[0][0] == runs[1][0]
+    assert len(runs[0][0]) == 32
+    # replay the speculative steps on the oracle (positions follow the oracle's own draw counts)
+    cases, got, expected = [], [], []
+    start = 1  # the prefill drew one uniform
+    for draft, _table, logits, new_tokens in runs[0][1]:
+        case = {"logits": logits.float().cpu(), "guesses": list(draft), "temperature": 0.8, "top_p": 0.95,
+                "seed": 42, "start": start}
+        exp, end = oracle_verify(case)
+        cases.append(case)
+        got.append(list(new_tokens))
+        expected.append(exp)
+        start = end
+    check_against(cases, got, [0] * len(got), expected, [0] * len(got))

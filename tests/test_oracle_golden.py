@@ -54,6 +54,28 @@ def test_top_p_keeps_the_same_tokens() -> None:
         torch.testing.assert_close(probs, case["probs"], atol=1e-6, rtol=1e-5)
 
 
+def test_stable_top_p_differs_from_the_reference_only_inside_a_split_tie_group() -> None:
+    """The kernels' convention (ties at the cut kept lowest id first) keeps as many tokens as the
+    reference, with the same normaliser; only which members of an equal-probability group that
+    straddles the cut survive may differ."""
+    g = torch.Generator().manual_seed(21)
+    rows = [case["logits"] for case in load_golden("top_p_cases.pt")["cases"]]
+    rows += [(torch.randn(4, 4096, generator=g) * 0.7).to(torch.bfloat16) for _ in range(8)]
+    for logits in rows:
+        for temperature, top_p in ((0.8, 0.95), (1.0, 0.5)):
+            ref = verify.token_probabilities(logits, temperature, top_p)
+            ours = verify.token_probabilities(logits, temperature, top_p, stable=True)
+            assert torch.equal((ref > 0).sum(-1), (ours > 0).sum(-1))
+            plain = torch.softmax(logits.float() / temperature, dim=-1)
+            differ = (ref > 0) != (ours > 0)
+            for r in range(logits.shape[0]):
+                if differ[r].any():  # every differing token shares the cut-off probability
+                    tau = plain[r][ours[r] > 0].min()
+                    assert torch.all(plain[r][differ[r]] == tau)
+                else:
+                    torch.testing.assert_close(ours[r], ref[r], atol=0, rtol=0)
+
+
 def test_quantize_vectors_is_bit_exact() -> None:
     for case in load_golden("quant_cases.pt")["cases"]:
         q, s = qwen3.quantize_vectors(case["values"])
