@@ -41,7 +41,7 @@ extern "C" {
 #define NE_DEV_HISTORY_FULL 16  /* a sequence outgrew its history row or block-table row */
 #define NE_DEV_NO_SAMPLER 32    /* temperature > 0 on a model without a sampling buffer */
 
-#define NE_ABI_VERSION 1
+#define NE_ABI_VERSION 2
 
 NE_API int ne_abi_version(void);
 NE_API const char* ne_status_string(int status);
@@ -86,6 +86,12 @@ typedef struct {
   void* v_cache;
   void* k_scale;              /* int8 KV: [slots + 1, nkv] bf16, else NULL */
   void* v_scale;
+  /* weight_int8: the four projections above are int8 [out, in] (same row order) and these are
+   * their per-output-row bf16 scales [out] (models/int8_quantization.py:30-57); else NULL */
+  const void* w_qkv_scale;
+  const void* w_o_scale;
+  const void* w_gateup_scale;
+  const void* w_down_scale;
 } ne_layer_weights;
 
 typedef struct {
@@ -297,6 +303,14 @@ NE_API int ne_model_profile_end(ne_model* model, float* ms_by_kind, int* launche
  * K % 64 == 0; the three pointers 16-byte aligned.
  */
 NE_API int ne_gemm_bf16(const void* x, const void* w, void* y, int M, int N, int K, int32_t* status, void* stream);
+
+/*
+ * ne_gemm_bf16 with int8 weights (Int8Linear.forward, models/int8_quantization.py:55-57):
+ * y = x . bf16(w_int8 * scale)^T, the dequantised tile built in shared memory per stage.
+ * w [N, K] int8, scale [N] bf16; same shape rules as ne_gemm_bf16.
+ */
+NE_API int ne_gemm_w8(const void* x, const void* w, const void* scale, void* y, int M, int N, int K, int32_t* status,
+                      void* stream);
 
 /*
  * Paged verify attention (run_cached_attention without the gather, attention_context.py:66-109):

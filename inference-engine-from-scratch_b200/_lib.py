@@ -46,6 +46,7 @@ EXPORTS = {
     "ne_prefill": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "ne_spec_step": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "ne_gemm_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "ne_gemm_w8": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "ne_paged_attention": (
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int,
@@ -94,7 +95,8 @@ class ModelConfig(ctypes.Structure):
 class LayerWeights(ctypes.Structure):
     _fields_ = [(name, c_void_p) for name in (
         "w_qkv", "w_o", "w_gateup", "w_down", "ln_in", "ln_post", "q_norm", "k_norm",
-        "k_cache", "v_cache", "k_scale", "v_scale")]
+        "k_cache", "v_cache", "k_scale", "v_scale",
+        "w_qkv_scale", "w_o_scale", "w_gateup_scale", "w_down_scale")]
 
 
 class HeadWeights(ctypes.Structure):

@@ -115,8 +115,9 @@ int sm_count() {
 }
 
 int run_gemm(ne_model* m, const CUtensorMap* tw, const CUtensorMap* tx, int M_max, const int32_t* M_dev, int N, int K,
-             const ne::Epilogue& epi, cudaStream_t stream) {
+             const ne::Epilogue& epi, cudaStream_t stream, const void* w_scale = nullptr) {
   GemmParams p{};
+  p.w_scale = static_cast<const __nv_bfloat16*>(w_scale);
   p.M_max = M_max;
   p.M_dev = M_dev;
   p.N = N;
@@ -186,7 +187,6 @@ int ne_model_create(const ne_model_config* cfg, ne_model** out) {
       c.hidden_size % 256 || c.intermediate_size % 64 || c.vocab_size % 128 || c.num_layers <= 0 ||
       c.num_cache_slots < 2 || c.max_positions <= 0)
     return NE_ERR_INVALID;
-  if (c.weight_int8) return NE_ERR_UNSUPPORTED;
   ne_model* m = new (std::nothrow) ne_model();
   if (!m) return NE_ERR_INVALID;
   m->cfg = c;
@@ -213,12 +213,20 @@ int ne_model_set_layer(ne_model* m, int layer, const ne_layer_weights* w) {
   if (!w->w_qkv || !w->w_o || !w->w_gateup || !w->w_down || !w->ln_in || !w->ln_post || !w->q_norm || !w->k_norm ||
       !w->k_cache || !w->v_cache || (c.kv_int8 && (!w->k_scale || !w->v_scale)))
     return NE_ERR_INVALID;
-  bool ok = ne::make_tmap_bf16(&m->tm_qkv[layer], w->w_qkv, qs + 2 * kvs, H, ne::GEMM_BM, ne::GEMM_BK) &&
-            ne::make_tmap_bf16(&m->tm_o[layer], w->w_o, H, qs, ne::GEMM_BM, ne::GEMM_BK) &&
-            ne::make_tmap_bf16(&m->tm_gateup[layer], w->w_gateup, 2 * I, H, ne::GEMM_BM, ne::GEMM_BK) &&
-            ne::make_tmap_bf16(&m->tm_down[layer], w->w_down, H, I, ne::GEMM_BM, ne::GEMM_BK);
+  if (c.weight_int8 && (!w->w_qkv_scale || !w->w_o_scale || !w->w_gateup_scale || !w->w_down_scale))
+    return NE_ERR_INVALID;
+  auto wmap = [&](CUtensorMap* map, const void* base, int rows, int cols) {
+    return c.weight_int8 ? ne::make_tmap_w8(map, base, rows, cols)
+                         : ne::make_tmap_bf16(map, base, rows, cols, ne::GEMM_BM, ne::GEMM_BK);
+  };
+  bool ok = wmap(&m->tm_qkv[layer], w->w_qkv, qs + 2 * kvs, H) && wmap(&m->tm_o[layer], w->w_o, H, qs) &&
+            wmap(&m->tm_gateup[layer], w->w_gateup, 2 * I, H) && wmap(&m->tm_down[layer], w->w_down, H, I);
   if (!ok) return NE_ERR_INVALID;
   m->layers[layer] = *w;
+  if (!c.weight_int8) {  // bf16 projections: the GEMMs must not see scales
+    ne_layer_weights& stored = m->layers[layer];
+    stored.w_qkv_scale = stored.w_o_scale = stored.w_gateup_scale = stored.w_down_scale = nullptr;
+  }
   m->layer_set[layer] = 1;
   return NE_OK;
 }
@@ -329,7 +337,7 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
     e.v_scale = static_cast<__nv_bfloat16*>(w.v_scale);
     e.kv_int8 = c.kv_int8;
     e.num_cache_slots = c.num_cache_slots;
-    rc = note(m, NE_K_GEMM_QKV, run_gemm(m, &m->tm_qkv[l], &m->tm_x, R, rows->num_rows, qs + 2 * kvs, H, e, s), s);
+    rc = note(m, NE_K_GEMM_QKV, run_gemm(m, &m->tm_qkv[l], &m->tm_x, R, rows->num_rows, qs + 2 * kvs, H, e, s, w.w_qkv_scale), s);
     if (rc) return rc;
     rc = note(m, NE_K_ATTENTION,
               ne::launch_attention_tc(m->q, m->attn, w.k_cache, w.v_cache,
@@ -342,7 +350,7 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
     eo.status = m->status;
     eo.out = m->h;
     eo.ldo = H;
-    rc = note(m, NE_K_GEMM_O, run_gemm(m, &m->tm_o[l], &m->tm_attn, R, rows->num_rows, H, qs, eo, s), s);
+    rc = note(m, NE_K_GEMM_O, run_gemm(m, &m->tm_o[l], &m->tm_attn, R, rows->num_rows, H, qs, eo, s, w.w_o_scale), s);
     if (rc) return rc;
     rc = note(m, NE_K_RMSNORM,
               ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(w.ln_post), m->x, R, rows->num_rows, nullptr,
@@ -353,14 +361,14 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
     eg.status = m->status;
     eg.out = m->act;
     eg.ldo = I;
-    rc = note(m, NE_K_GEMM_GATEUP, run_gemm(m, &m->tm_gateup[l], &m->tm_x, R, rows->num_rows, 2 * I, H, eg, s), s);
+    rc = note(m, NE_K_GEMM_GATEUP, run_gemm(m, &m->tm_gateup[l], &m->tm_x, R, rows->num_rows, 2 * I, H, eg, s, w.w_gateup_scale), s);
     if (rc) return rc;
     ne::Epilogue ed{};
     ed.mode = ne::EPI_RESIDUAL;
     ed.status = m->status;
     ed.out = m->h;
     ed.ldo = H;
-    rc = note(m, NE_K_GEMM_DOWN, run_gemm(m, &m->tm_down[l], &m->tm_act, R, rows->num_rows, H, I, ed, s), s);
+    rc = note(m, NE_K_GEMM_DOWN, run_gemm(m, &m->tm_down[l], &m->tm_act, R, rows->num_rows, H, I, ed, s, w.w_down_scale), s);
     if (rc) return rc;
   }
   // final norm over the rows that get logits (gathered to the front of x), keys cleared
@@ -555,6 +563,29 @@ int ne_gemm_bf16(const void* x, const void* w, void* y, int M, int N, int K, int
   p.N = N;
   p.K = K;
   p.status = status;
+  p.epi.mode = ne::EPI_STORE;
+  p.epi.status = status;
+  p.epi.out = static_cast<__nv_bfloat16*>(y);
+  p.epi.ldo = N;
+  int rc = ne::gemm_plan(p, sm_count());
+  if (rc) return rc;
+  return ne::gemm_launch(&tw, &tx, p, as_stream(stream));
+}
+
+int ne_gemm_w8(const void* x, const void* w, const void* scale, void* y, int M, int N, int K, int32_t* status,
+               void* stream) {
+  if (!x || !w || !scale || !y || M <= 0 || N % ne::GEMM_BM || K % ne::GEMM_BK || !aligned16(x) || !aligned16(w) ||
+      !aligned16(y))
+    return NE_ERR_INVALID;
+  CUtensorMap tw, tx;
+  if (!ne::make_tmap_w8(&tw, w, N, K) || !ne::make_tmap_bf16(&tx, x, M, K, ne::GEMM_XBOX, ne::GEMM_BK))
+    return NE_ERR_INVALID;
+  GemmParams p{};
+  p.M_max = M;
+  p.N = N;
+  p.K = K;
+  p.status = status;
+  p.w_scale = static_cast<const __nv_bfloat16*>(scale);
   p.epi.mode = ne::EPI_STORE;
   p.epi.status = status;
   p.epi.out = static_cast<__nv_bfloat16*>(y);

@@ -319,7 +319,40 @@ __device__ void epilogue_rows(const Epilogue& e, int tile_n, int m_begin, int co
   }
 }
 
-template <int MODE>
+// int8 weights: one converter thread per weight row of the tile turns the stage's int8 row
+// (64 bytes, 64-byte TMA swizzle) into bf16(q * scale) in the 128-byte-swizzled bf16 operand tile.
+// q is made exact in bf16 from byte magic (0x4300 | (q & 0x7f)) - (0x4300 | (q & 0x80)), i.e.
+// (128 + (q mod 128)) - (128 or 256); the product is one bf16x2 multiply, rounded once as torch's
+// bf16 multiply of int8.to(bf16) by the scale.
+__device__ __forceinline__ uint32_t w8_pair(uint32_t word, uint32_t sel, uint32_t scale2) {
+  const uint32_t p = __byte_perm(word, 0x43434343u, sel);
+  const uint32_t v = p & 0x437F437Fu, b = p & 0x43804380u;
+  uint32_t q, r;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(v), "r"(b));
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(q), "r"(scale2));
+  return r;
+}
+__device__ __forceinline__ void w8_convert_row(uint32_t src_tile, uint32_t dst_tile, int row, uint32_t scale2) {
+  const uint32_t src = src_tile + (uint32_t)row * 64u;
+  const uint32_t dst = dst_tile + (uint32_t)row * 128u;
+  const uint32_t sw64 = (uint32_t)((row >> 1) & 3), sw128 = (uint32_t)(row & 7);
+  uint32_t w[16];
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(w[4 * c]), "=r"(w[4 * c + 1]), "=r"(w[4 * c + 2]), "=r"(w[4 * c + 3])
+                 : "r"(src + (((uint32_t)c ^ sw64) << 4)));
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {  // bf16 chunk j = elements 8j .. 8j+7 = int8 words 2j, 2j+1
+    const uint32_t a = w8_pair(w[2 * j], 0x4140u, scale2), b = w8_pair(w[2 * j], 0x4342u, scale2);
+    const uint32_t c = w8_pair(w[2 * j + 1], 0x4140u, scale2), d = w8_pair(w[2 * j + 1], 0x4342u, scale2);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst + (((uint32_t)j ^ sw128) << 4)), "r"(a),
+                 "r"(b), "r"(c), "r"(d)
+                 : "memory");
+  }
+}
+
+template <int MODE, bool W8>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                    const GemmParams p) {
@@ -340,15 +373,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int k_begin = split * cps;
   const int nk = max(0, min(num_chunks, k_begin + cps) - k_begin);
 
+  // stage: [bf16 W tile 16 KB][X tile][int8 W tile 8 KB when W8]
   const int w_bytes = GEMM_BM * GEMM_BK * 2;                                     // 16 KB
-  const int stage_bytes = w_bytes + ((p.t_block + GEMM_XBOX - 1) / GEMM_XBOX) * GEMM_XBOX * GEMM_BK * 2;
+  const int x_region = ((p.t_block + GEMM_XBOX - 1) / GEMM_XBOX) * GEMM_XBOX * GEMM_BK * 2;
+  const int stage_bytes = w_bytes + x_region + (W8 ? GEMM_W8_TILE_BYTES : 0);
+  const int w_dst_off = W8 ? w_bytes + x_region : 0;          // where the W TMA lands in a stage
+  const uint32_t w_load_bytes = W8 ? (uint32_t)GEMM_W8_TILE_BYTES : (uint32_t)w_bytes;
   const int stages = p.stages;
   // barriers sit past every region the pipeline or the epilogue staging can touch
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.smem_data);
   uint64_t* empty = full + stages;
   uint64_t* done = empty + stages;
   uint64_t* recv_bar = done + 1;  // split-K: peers' partial slices landed in our receive area
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
+  uint64_t* conv = recv_bar + 1;  // W8: the stage's bf16 operand tile is built (4 converter warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(conv + (W8 ? stages : 0));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* consumed_slot = const_cast<int*>(reinterpret_cast<volatile int*>(tmem_slot + 2));
   volatile int* done_ok = reinterpret_cast<volatile int*>(tmem_slot + 3);  // broadcast flags (barrier area)
@@ -365,6 +403,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     mbar_init(done, 1);
     mbar_init(recv_bar, 1);
+    if (W8)
+      for (int s = 0; s < stages; ++s) mbar_init(&conv[s], 4);
     *abort_flag = 0;
     *consumed_slot = 0;
     fence_mbar_init();
@@ -387,8 +427,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int pre = blockIdx.z == 0 ? min(stages, nk) : 0;
   if (warp == 0 && lane == 0) {
     for (int i = 0; i < pre; ++i) {
-      mbar_expect_tx(&full[i], (uint32_t)w_bytes);
-      tma_load_2d(smem + i * stage_bytes, &tm_w, &full[i], (k_begin + i) * GEMM_BK, tile_n * GEMM_BM);
+      mbar_expect_tx(&full[i], w_load_bytes);
+      tma_load_2d(smem + i * stage_bytes + w_dst_off, &tm_w, &full[i], (k_begin + i) * GEMM_BK, tile_n * GEMM_BM);
     }
   }
   pdl_wait();
@@ -442,9 +482,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const uint32_t round = (uint32_t)(i / stages);
         if (!mbar_wait(&empty[s], (round & 1u) ^ 1u, abort_flag, p.status)) break;
         uint8_t* st = smem + s * stage_bytes;
-        mbar_arrive_expect_tx(&full[s], (uint32_t)w_bytes + x_bytes);
+        mbar_arrive_expect_tx(&full[s], w_load_bytes + x_bytes);
         const int kx = (k_begin + i) * GEMM_BK;
-        tma_load_2d(st, &tm_w, &full[s], kx, tile_n * GEMM_BM);
+        tma_load_2d(st + w_dst_off, &tm_w, &full[s], kx, tile_n * GEMM_BM);
         for (int l = 0; l < n_loads; ++l)
           tma_load_2d(st + w_bytes + l * GEMM_XBOX * GEMM_BK * 2, &tm_x, &full[s], kx, m0 + l * GEMM_XBOX);
         issued = i + 1;
@@ -460,6 +500,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const int s = i % stages;
         const uint32_t round = (uint32_t)(i / stages);
         if (!mbar_wait(&full[s], round & 1u, abort_flag, p.status)) break;
+        if (W8 && !mbar_wait(&conv[s], round & 1u, abort_flag, p.status)) break;
         tc_fence_after();
         const uint32_t a_addr = smem_u32(smem + s * stage_bytes);
         const uint32_t b_addr = a_addr + w_bytes;
@@ -477,6 +518,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_commit(done);
     }
     __syncwarp();
+  } else if (W8 && warp >= 4) {
+    // converters: thread c builds weight row c of every stage's bf16 operand tile. The TMA of a
+    // stage is issued only after the MMA released the stage, so once ``full`` fires the bf16
+    // tile is free as well.
+    const int row = tid - 128;
+    const uint16_t sbits = __bfloat16_as_ushort(p.w_scale[(size_t)tile_n * GEMM_BM + row]);
+    const uint32_t scale2 = (uint32_t)sbits | ((uint32_t)sbits << 16);
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % stages;
+      const uint32_t round = (uint32_t)(i / stages);
+      if (!mbar_wait(&full[s], round & 1u, abort_flag, p.status)) break;
+      const uint32_t st = smem_u32(smem + s * stage_bytes);
+      w8_convert_row(st + (uint32_t)w_dst_off, st, row, scale2);
+      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&conv[s]);
+    }
   }
 
   // ------------------------------------------------------------------ epilogue
@@ -626,31 +684,44 @@ bool make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
   return r == CUDA_SUCCESS;
 }
 
-template <int MODE>
+bool make_tmap_w8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
+  auto encode = get_encode_fn();
+  if (!encode || !base || (reinterpret_cast<uintptr_t>(base) & 15u) || cols % 16 != 0) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols};
+  cuuint32_t box[2] = {(cuuint32_t)GEMM_BK, (cuuint32_t)GEMM_BM};
+  cuuint32_t estrides[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estrides,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int MODE, bool W8>
 cudaError_t prepare_mode() {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_tc_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    attr_err = cudaFuncSetAttribute(gemm_tc_kernel<MODE, W8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     GEMM_SMEM_BYTES);
     if (attr_err == cudaSuccess)
-      attr_err = cudaFuncSetAttribute(gemm_tc_kernel<MODE>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      attr_err = cudaFuncSetAttribute(gemm_tc_kernel<MODE, W8>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   });
   return attr_err;
 }
 
-template <int MODE>
+template <int MODE, bool W8>
 cudaError_t launch_mode(const cudaLaunchConfig_t& cfg, const CUtensorMap* tm_w, const CUtensorMap* tm_x,
                         const GemmParams& p) {
-  cudaError_t err = prepare_mode<MODE>();
+  cudaError_t err = prepare_mode<MODE, W8>();
   if (err != cudaSuccess) return err;
-  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<MODE>, *tm_w, *tm_x, p);
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<MODE, W8>, *tm_w, *tm_x, p);
 }
 
 // Clusters of ``splits`` CTAs with ``smem`` bytes each that the GPU holds at once (0 on error).
-template <int MODE>
+template <int MODE, bool W8>
 int active_clusters_mode(int splits, int smem) {
-  if (prepare_mode<MODE>() != cudaSuccess) return 0;
+  if (prepare_mode<MODE, W8>() != cudaSuccess) return 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(splits, 1, 1);
   cfg.blockDim = dim3(GEMM_THREADS);
@@ -663,21 +734,30 @@ int active_clusters_mode(int splits, int smem) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int clusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tc_kernel<MODE>, &cfg) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tc_kernel<MODE, W8>, &cfg) != cudaSuccess) {
     cudaGetLastError();
     return 0;
   }
   return clusters;
 }
 
-int active_clusters(int mode, int splits, int smem) {
+int active_clusters(int mode, bool w8, int splits, int smem) {
+  if (w8) {
+    switch (mode) {
+      case EPI_STORE: return active_clusters_mode<EPI_STORE, true>(splits, smem);
+      case EPI_RESIDUAL: return active_clusters_mode<EPI_RESIDUAL, true>(splits, smem);
+      case EPI_SWIGLU: return active_clusters_mode<EPI_SWIGLU, true>(splits, smem);
+      case EPI_QKV: return active_clusters_mode<EPI_QKV, true>(splits, smem);
+      default: return 0;
+    }
+  }
   switch (mode) {
-    case EPI_STORE: return active_clusters_mode<EPI_STORE>(splits, smem);
-    case EPI_RESIDUAL: return active_clusters_mode<EPI_RESIDUAL>(splits, smem);
-    case EPI_SWIGLU: return active_clusters_mode<EPI_SWIGLU>(splits, smem);
-    case EPI_QKV: return active_clusters_mode<EPI_QKV>(splits, smem);
-    case EPI_ARGMAX: return active_clusters_mode<EPI_ARGMAX>(splits, smem);
-    case EPI_LOGITS: return active_clusters_mode<EPI_LOGITS>(splits, smem);
+    case EPI_STORE: return active_clusters_mode<EPI_STORE, false>(splits, smem);
+    case EPI_RESIDUAL: return active_clusters_mode<EPI_RESIDUAL, false>(splits, smem);
+    case EPI_SWIGLU: return active_clusters_mode<EPI_SWIGLU, false>(splits, smem);
+    case EPI_QKV: return active_clusters_mode<EPI_QKV, false>(splits, smem);
+    case EPI_ARGMAX: return active_clusters_mode<EPI_ARGMAX, false>(splits, smem);
+    case EPI_LOGITS: return active_clusters_mode<EPI_LOGITS, false>(splits, smem);
     default: return 0;
   }
 }
@@ -685,9 +765,9 @@ int active_clusters(int mode, int splits, int smem) {
 // Choose tokens per CTA, split-K (cluster size) and pipeline depth for an [M_max, K] x [N, K]^T GEMM.
 namespace {
 struct PlanKey {
-  int M, N, K, mode, sms;
+  int M, N, K, mode, w8, sms;
   bool operator<(const PlanKey& o) const {
-    return std::tie(M, N, K, mode, sms) < std::tie(o.M, o.N, o.K, o.mode, o.sms);
+    return std::tie(M, N, K, mode, w8, sms) < std::tie(o.M, o.N, o.K, o.mode, o.w8, o.sms);
   }
 };
 struct PlanVal {
@@ -702,7 +782,7 @@ int plan_with_occupancy(GemmParams& p, int num_sms);
 
 // Cached per (rows, N, K, epilogue, SMs); the first plan of a shape queries cluster occupancy.
 int gemm_plan(GemmParams& p, int num_sms) {
-  const PlanKey key{p.M_max, p.N, p.K, p.epi.mode, num_sms};
+  const PlanKey key{p.M_max, p.N, p.K, p.epi.mode, p.w_scale != nullptr, num_sms};
   {
     std::lock_guard<std::mutex> lock(g_plan_mutex);
     auto it = g_plans.find(key);
@@ -725,6 +805,7 @@ int gemm_plan(GemmParams& p, int num_sms) {
 namespace {
 int plan_uncached(GemmParams& p, int num_sms) {
   if (p.N % GEMM_BM || p.K % GEMM_BK || p.M_max <= 0) return NE_ERR_INVALID;
+  if (p.w_scale && (p.epi.mode == EPI_ARGMAX || p.epi.mode == EPI_LOGITS)) return NE_ERR_UNSUPPORTED;
   const int num_chunks = p.K / GEMM_BK;
   const int n_tiles = p.N / GEMM_BM;
   const int avail = GEMM_SMEM_DATA_BYTES;
@@ -748,7 +829,8 @@ int plan_uncached(GemmParams& p, int num_sms) {
     --S;
   }
   if (S > 1 && !fits(S, t_block)) S = 1;
-  const int stage_bytes = GEMM_BM * GEMM_BK * 2 + ((t_block + GEMM_XBOX - 1) / GEMM_XBOX) * GEMM_XBOX * GEMM_BK * 2;
+  const int stage_bytes = GEMM_BM * GEMM_BK * 2 + ((t_block + GEMM_XBOX - 1) / GEMM_XBOX) * GEMM_XBOX * GEMM_BK * 2 +
+                          (p.w_scale ? GEMM_W8_TILE_BYTES : 0);
   const int cps = (num_chunks + S - 1) / S;
   int stages = std::min(std::min(GEMM_MAX_STAGES, cps), avail / stage_bytes);
   if (stages < 1) return NE_ERR_INVALID;
@@ -777,7 +859,7 @@ int plan_with_occupancy(GemmParams& p, int num_sms) {
   const int m_blocks = (p.M_max + p.t_block - 1) / p.t_block;
   const int par = n_tiles * (p.M_max > 512 ? m_blocks : 1);
   while (p.splits > 1) {
-    const int fit = active_clusters(p.epi.mode, p.splits, p.smem_data + 256 + 1024);
+    const int fit = active_clusters(p.epi.mode, p.w_scale != nullptr, p.splits, p.smem_data + 256 + 1024);
     if (fit >= par) break;
     const int want = p.splits - 1;
     GemmParams q = p;
@@ -806,14 +888,24 @@ int gemm_launch(const CUtensorMap* tm_w, const CUtensorMap* tm_x, const GemmPara
   cfg.attrs = attrs;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
   cudaError_t err;
-  switch (p.epi.mode) {
-    case EPI_STORE: err = launch_mode<EPI_STORE>(cfg, tm_w, tm_x, p); break;
-    case EPI_RESIDUAL: err = launch_mode<EPI_RESIDUAL>(cfg, tm_w, tm_x, p); break;
-    case EPI_SWIGLU: err = launch_mode<EPI_SWIGLU>(cfg, tm_w, tm_x, p); break;
-    case EPI_QKV: err = launch_mode<EPI_QKV>(cfg, tm_w, tm_x, p); break;
-    case EPI_ARGMAX: err = launch_mode<EPI_ARGMAX>(cfg, tm_w, tm_x, p); break;
-    case EPI_LOGITS: err = launch_mode<EPI_LOGITS>(cfg, tm_w, tm_x, p); break;
-    default: return NE_ERR_INVALID;
+  if (p.w_scale) {
+    switch (p.epi.mode) {
+      case EPI_STORE: err = launch_mode<EPI_STORE, true>(cfg, tm_w, tm_x, p); break;
+      case EPI_RESIDUAL: err = launch_mode<EPI_RESIDUAL, true>(cfg, tm_w, tm_x, p); break;
+      case EPI_SWIGLU: err = launch_mode<EPI_SWIGLU, true>(cfg, tm_w, tm_x, p); break;
+      case EPI_QKV: err = launch_mode<EPI_QKV, true>(cfg, tm_w, tm_x, p); break;
+      default: return NE_ERR_UNSUPPORTED;
+    }
+  } else {
+    switch (p.epi.mode) {
+      case EPI_STORE: err = launch_mode<EPI_STORE, false>(cfg, tm_w, tm_x, p); break;
+      case EPI_RESIDUAL: err = launch_mode<EPI_RESIDUAL, false>(cfg, tm_w, tm_x, p); break;
+      case EPI_SWIGLU: err = launch_mode<EPI_SWIGLU, false>(cfg, tm_w, tm_x, p); break;
+      case EPI_QKV: err = launch_mode<EPI_QKV, false>(cfg, tm_w, tm_x, p); break;
+      case EPI_ARGMAX: err = launch_mode<EPI_ARGMAX, false>(cfg, tm_w, tm_x, p); break;
+      case EPI_LOGITS: err = launch_mode<EPI_LOGITS, false>(cfg, tm_w, tm_x, p); break;
+      default: return NE_ERR_INVALID;
+    }
   }
   return err == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }

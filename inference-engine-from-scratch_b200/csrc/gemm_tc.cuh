@@ -11,8 +11,9 @@
 // result is deterministic) by reading its peers' shared memory (DSMEM). No global scratch.
 //
 // Roles (256 threads): warp 0 lane 0 issues TMA, warp 1 lane 0 issues tcgen05.mma, warp 2 owns
-// the TMEM allocation; all eight warps run the epilogue (warp w reads TMEM lanes 32(w%4)..+31, and
-// warps w and w+4 split the token columns).
+// the TMEM allocation; with int8 weights warps 4-7 turn each stage's int8 tile into the bf16
+// operand tile; all eight warps run the epilogue (warp w reads TMEM lanes 32(w%4)..+31, and warps
+// w and w+4 split the token columns).
 #pragma once
 
 #include <cuda.h>
@@ -79,6 +80,9 @@ struct GemmParams {
   int stages;
   int smem_data;         // bytes of the data region (pipeline stages / epilogue staging)
   int* status;
+  // int8 weights (nullptr: bf16): W is int8 [N, K] with one bf16 scale per row, and the MMA
+  // operand is bf16(q * scale), the reference's Int8Linear dequantisation, built in shared memory
+  const __nv_bfloat16* w_scale;
   Epilogue epi;
 };
 
@@ -87,5 +91,8 @@ int gemm_launch(const CUtensorMap* tm_w, const CUtensorMap* tm_x, const GemmPara
 int gemm_plan(GemmParams& p, int num_sms);
 bool make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
                     uint32_t box_cols);
+// int8 weights [rows, cols]: box 128 rows x 64 columns, 64-byte swizzle (conflict-free row reads)
+bool make_tmap_w8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols);
+constexpr int GEMM_W8_TILE_BYTES = GEMM_BM * GEMM_BK;  // int8 staging per stage
 
 }  // namespace ne

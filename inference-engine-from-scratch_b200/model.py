@@ -11,6 +11,8 @@ HBM layout (all bf16 unless noted; one CUDA device):
 * the KV pool: one tensor ``[L, 2, num_slots + 1, nkv, 128]`` whose ``[l, 0]`` / ``[l, 1]`` views are the
   reference's per-layer key / value caches (engine/memory/kv_cache_pool.py:34-69, last row = scratch
   slot); an int8 pool adds ``[L, 2, num_slots + 1, nkv]`` bf16 scales;
+* int8 weights (``weight_int8``): the four projections become int8 ``[out, in]`` in the same row order
+  plus one bf16 scale per output row (models/int8_quantization.py:30-73, the LM head stays bf16);
 * the workspace (activations, row metadata, argmax keys), sized for ``max_rows`` token rows.
 """
 
@@ -33,6 +35,18 @@ def rope_tables(max_positions: int, head_dim: int, theta: float, dtype=torch.bfl
     return angles.cos().to(dtype), angles.sin().to(dtype)
 
 
+INT8_MAX = 127
+MIN_SCALE = 1e-8
+
+
+def quantize_rows(values: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """One symmetric int8 scale per row (quantize_vectors, models/int8_quantization.py:30-34): the
+    scale max|w| / 127 in fp32 (at least 1e-8), stored in the weight dtype; q = round(w / scale)."""
+    scales = values.abs().amax(dim=-1, keepdim=True).float().clamp(min=MIN_SCALE) / INT8_MAX
+    quantized = torch.round(values.float() / scales).clamp(-INT8_MAX, INT8_MAX).to(torch.int8)
+    return quantized, scales.to(values.dtype)
+
+
 def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, group: int = 64) -> torch.Tensor:
     rows, hidden = gate.shape
     return torch.stack((gate.view(rows // group, group, hidden), up.view(rows // group, group, hidden)), dim=1).reshape(
@@ -53,6 +67,7 @@ class B200Model:
         kv_int8: bool = False,
         max_rows: int = 4096,
         max_seqs: int = 256,
+        weight_int8: bool = False,
     ) -> None:
         self.lib = _lib.load()
         self.cfg = cfg
@@ -62,6 +77,7 @@ class B200Model:
         self.num_slots = num_slots
         self.max_positions = max_positions
         self.kv_int8 = kv_int8
+        self.weight_int8 = weight_int8
         self.max_rows = max_rows
         self.max_seqs = max_seqs
         bf16 = torch.bfloat16
@@ -71,22 +87,40 @@ class B200Model:
             return t.to(device=dev, dtype=bf16).contiguous()
 
         L, nkv, d = cfg.num_hidden_layers, cfg.num_key_value_heads, cfg.head_dim
+
+        def proj(name: str) -> tuple[torch.Tensor, torch.Tensor | None]:
+            """A projection in the model dtype, or its int8 rows and bf16 row scales. Quantised on
+            the host CPU, where torch's division and rounding are the reference's bit for bit (the
+            GPU's elementwise division is not always the correctly rounded one)."""
+            if not weight_int8:
+                return put(weights[name]), None
+            q, s = quantize_rows(weights[name].to("cpu", bf16))
+            return q.to(dev).contiguous(), s.to(dev).contiguous()
+
         self.layers: list[dict[str, torch.Tensor]] = []
         for layer in range(L):
             p = f"model.layers.{layer}."
-            qkv = torch.cat(
-                [weights[p + "self_attn.q_proj.weight"], weights[p + "self_attn.k_proj.weight"],
-                 weights[p + "self_attn.v_proj.weight"]], dim=0)
-            self.layers.append({
-                "w_qkv": put(qkv),
-                "w_o": put(weights[p + "self_attn.o_proj.weight"]),
-                "w_gateup": put(interleave_gate_up(weights[p + "mlp.gate_proj.weight"], weights[p + "mlp.up_proj.weight"])),
-                "w_down": put(weights[p + "mlp.down_proj.weight"]),
+            parts = [proj(p + f"self_attn.{n}_proj.weight") for n in ("q", "k", "v")]
+            o, o_s = proj(p + "self_attn.o_proj.weight")
+            gate, gate_s = proj(p + "mlp.gate_proj.weight")
+            up, up_s = proj(p + "mlp.up_proj.weight")
+            down, down_s = proj(p + "mlp.down_proj.weight")
+            entry = {
+                "w_qkv": torch.cat([t for t, _ in parts], dim=0).contiguous(),
+                "w_o": o,
+                "w_gateup": interleave_gate_up(gate, up).contiguous(),
+                "w_down": down,
                 "ln_in": put(weights[p + "input_layernorm.weight"]),
                 "ln_post": put(weights[p + "post_attention_layernorm.weight"]),
                 "q_norm": put(weights[p + "self_attn.q_norm.weight"]),
                 "k_norm": put(weights[p + "self_attn.k_norm.weight"]),
-            })
+            }
+            if weight_int8:
+                entry["w_qkv_scale"] = torch.cat([t for _, t in parts], dim=0).reshape(-1).contiguous()
+                entry["w_o_scale"] = o_s.reshape(-1).contiguous()
+                entry["w_gateup_scale"] = interleave_gate_up(gate_s, up_s).reshape(-1).contiguous()
+                entry["w_down_scale"] = down_s.reshape(-1).contiguous()
+            self.layers.append(entry)
         self.embed = put(weights["model.embed_tokens.weight"])
         head = weights.get("lm_head.weight")
         self.lm_head = self.embed if (cfg.tie_word_embeddings or head is None) else put(head)
@@ -101,7 +135,7 @@ class B200Model:
         config = _lib.ModelConfig(
             vocab_size=cfg.vocab_size, hidden_size=cfg.hidden_size, intermediate_size=cfg.intermediate_size,
             num_layers=L, num_heads=cfg.num_attention_heads, num_kv_heads=nkv, head_dim=d,
-            rms_norm_eps=cfg.rms_norm_eps, block_size=16, kv_int8=int(kv_int8), weight_int8=0,
+            rms_norm_eps=cfg.rms_norm_eps, block_size=16, kv_int8=int(kv_int8), weight_int8=int(weight_int8),
             num_cache_slots=num_slots + 1, max_positions=max_positions,
         )
         handle = ctypes.c_void_p()
@@ -116,6 +150,8 @@ class B200Model:
                 k_cache=self.k_cache(layer).data_ptr(), v_cache=self.v_cache(layer).data_ptr(),
                 k_scale=self.kv_scales[layer, 0].data_ptr() if kv_int8 else None,
                 v_scale=self.kv_scales[layer, 1].data_ptr() if kv_int8 else None,
+                **{k: w[k].data_ptr() for k in ("w_qkv_scale", "w_o_scale", "w_gateup_scale", "w_down_scale")
+                   if weight_int8},
             )
             _lib.check(self.lib.ne_model_set_layer(handle, layer, ctypes.byref(lw)), "ne_model_set_layer")
             self._layer_structs.append(lw)

@@ -17,6 +17,7 @@ from tests.conftest import load_golden, package, submodule
 pytestmark = pytest.mark.gpu
 
 LOGITS_ATOL_BF16 = 2e-2
+LOGITS_ATOL_INT8 = 5e-2
 
 
 @pytest.fixture(scope="module")
@@ -30,14 +31,29 @@ def small():
     return cfg, weights, model
 
 
+@pytest.fixture(scope="module")
+def small_int8():
+    submodule("build").build()
+    pkg = package()
+    cfg = pkg.SMALL_TEST
+    weights = pkg.make_weights(cfg, seed=0)
+    model = submodule("model").B200Model(cfg, weights, num_slots=64 * 16, device="cuda:0", max_positions=512,
+                                         max_rows=512, max_seqs=8, kv_int8=True, weight_int8=True)
+    return cfg, weights, model
+
+
 def _reset_pool(model) -> None:
     model.kv.zero_()
 
 
-def test_serial_drop_in_matches_the_reference_step_by_step(small) -> None:
-    cfg, _, model = small
+@pytest.mark.parametrize("variant", ["bf16", "int8"])
+def test_serial_drop_in_matches_the_reference_step_by_step(small, small_int8, variant) -> None:
+    """int8: int8 weights (bf16(q * scale) operands) and the int8 KV pool, logits within 5e-2."""
+    cfg, _, model = small if variant == "bf16" else small_int8
+    atol = LOGITS_ATOL_BF16 if variant == "bf16" else LOGITS_ATOL_INT8
     serial = submodule("serial")
-    golden = load_golden("spec_small_bf16.pt")
+    golden = load_golden(f"spec_small_{variant}.pt")
+    assert golden["int8"] == (variant == "int8")
     ids = golden["digest_ids"]
     allocator = serial.PagedSlotAllocator(golden["num_blocks"], 16)
     runner = serial.B200ModelRunner(model, allocator)
@@ -54,9 +70,9 @@ def test_serial_drop_in_matches_the_reference_step_by_step(small) -> None:
             assert table == ref["block_table"]
             assert new_tokens == ref["new_tokens"]
             got = logits.float().cpu()
-            torch.testing.assert_close(got[:, ids], ref["logits"]["at_ids"], atol=LOGITS_ATOL_BF16, rtol=0)
+            torch.testing.assert_close(got[:, ids], ref["logits"]["at_ids"], atol=atol, rtol=0)
             top2 = torch.topk(got, 2, dim=-1).values
-            torch.testing.assert_close(top2, ref["logits"]["top2"], atol=LOGITS_ATOL_BF16, rtol=0)
+            torch.testing.assert_close(top2, ref["logits"]["top2"], atol=atol, rtol=0)
         assert allocator.num_free_blocks == record["free_blocks_after"]
 
 
@@ -97,6 +113,17 @@ def test_continuous_batching_gives_each_request_its_serial_output(small, graphs)
     outs = eng.generate(prompts, golden["max_new"])
     assert outs == [r["tokens"] for r in golden["records"]]
     assert eng.accepted_total == golden["accepted"] and eng.proposed_total == golden["proposed"]
+    model.raise_on_device_error()
+
+
+def test_int8_engine_serves_the_int8_reference_outputs(small_int8) -> None:
+    """Config 3's arithmetic (int8 weights + int8 KV) through the batched engine with CUDA graphs."""
+    _, _, model = small_int8
+    golden = load_golden("spec_small_int8.pt")
+    prompts = [r["prompt"] for r in golden["records"]]
+    eng = _engine(model, 2, True)
+    outs = eng.generate(prompts, golden["max_new"])
+    assert outs == [r["tokens"] for r in golden["records"]]
     model.raise_on_device_error()
 
 

@@ -45,6 +45,40 @@ def test_gemm_matches_fp32_torch(lib, cuda_device, M, N, K) -> None:
     torch.testing.assert_close(y.float(), ref, rtol=8e-3, atol=2e-3)
 
 
+@pytest.mark.parametrize(
+    "M,N,K",
+    [(1, 128, 64), (7, 256, 1024), (64, 4096, 1024), (140, 1024, 2048), (140, 6144, 1024), (330, 1024, 3072),
+     (600, 384, 256)],
+)
+def test_int8_weight_gemm_matches_the_dequantised_reference(lib, cuda_device, M, N, K) -> None:
+    """Int8Linear.forward (models/int8_quantization.py:55-57): x . bf16(q * scale)^T."""
+    model_mod = submodule("model")
+    g = torch.Generator(device="cpu").manual_seed(M * 3 + N + K)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+    q, s = oq.quantize_vectors(w)
+    dequant = q.to(torch.bfloat16) * s  # the reference's bf16 dequantisation
+    y = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    xd, qd, sd = x.to(cuda_device), q.to(cuda_device), s.reshape(-1).contiguous().to(cuda_device)
+    rc = lib.ne_gemm_w8(xd.data_ptr(), qd.data_ptr(), sd.data_ptr(), y.data_ptr(), M, N, K, status.data_ptr(),
+                        _stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    ref = x.float() @ dequant.float().T
+    torch.testing.assert_close(y.float().cpu(), ref, rtol=8e-3, atol=2e-3)
+    # and the same bits as the bf16 GEMM on the dequantised weights (same tiles, same order)
+    y16 = torch.empty_like(y)
+    dq = dequant.to(cuda_device)
+    assert lib.ne_gemm_bf16(xd.data_ptr(), dq.data_ptr(), y16.data_ptr(), M, N, K, None, _stream()) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(y, y16)
+    # the model's own row quantisation equals the reference's, bit for bit
+    q2, s2 = model_mod.quantize_rows(w)
+    assert torch.equal(q2, q) and torch.equal(s2, s)
+
+
 def test_gemm_is_deterministic(lib, cuda_device) -> None:
     x = torch.randn(320, 2048, device=cuda_device).to(torch.bfloat16)
     w = (torch.randn(1024, 2048, device=cuda_device) * 0.02).to(torch.bfloat16)
