@@ -90,8 +90,8 @@ class B200Model:
 
         def proj(name: str) -> tuple[torch.Tensor, torch.Tensor | None]:
             """A projection in the model dtype, or its int8 rows and bf16 row scales. Quantised on
-            the host CPU, where torch's division and rounding are the reference's bit for bit (the
-            GPU's elementwise division is not always the correctly rounded one)."""
+            the host CPU like the reference's CPU run: the same torch ops on the GPU were seen to
+            give a different int8 value for rare elements (a quotient near .5)."""
             if not weight_int8:
                 return put(weights[name]), None
             q, s = quantize_rows(weights[name].to("cpu", bf16))
