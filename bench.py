@@ -16,6 +16,11 @@
 * ``cpu_baseline``: the CPU oracle (the reference's serial speculative path restated, fp32, config 1's
   prompt) on this host's cores for a bounded sample.
 
+Other BASELINE workloads (not the default line): ``--workload c3`` (int8 weights + int8 KV, 64 users,
+k=8, 1024-token prompts whose first 512 tokens are one shared prefix served from shared KV blocks,
+256 outputs) and ``--workload c4`` (256 users, sampled T=0.8 / top-p 0.95 on per-request Philox
+streams, prompt lengths uniform in [32, 2048], chunked prefill of 512 tokens, 256 outputs, k=4).
+
 Multi-GPU: one process per GPU (torchrun); each rank serves its own 64 users on an independent
 replica (no collectives on the data path); NCCL only carries the barrier and the max-over-ranks
 timing. ``--impl reference`` times the reference's CPU path (the oracle port) on rank 0.
@@ -51,6 +56,8 @@ def parse_args():
     p.add_argument("--steps", type=int, default=30)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--workload", choices=("c2", "c3", "c4"), default="c2",
+                   help="BASELINE config: c2 (default, the headline), c3 (int8, shared prefix), c4 (sampled)")
     p.add_argument("--users", type=int, default=64)
     p.add_argument("--k", type=int, default=4)
     p.add_argument("--prompt-len", type=int, default=64)
@@ -271,19 +278,68 @@ def workload_config(args) -> dict:
     }
 
 
+class Workload:
+    """One BASELINE configuration on one GPU: model arithmetic, users, prompts and decoding."""
+
+    def __init__(self, args, pkg, vocab: int, rank: int) -> None:
+        self.name = args.workload
+        self.weight_int8 = self.kv_int8 = False
+        self.temperature, self.top_p = 0.0, 1.0
+        self.shared_prefix, self.prefill_chunk = 0, None
+        if self.name == "c2":
+            self.users, self.k, self.max_new = args.users, args.k, args.max_new
+            self.prompts = pkg.make_prompts(self.users, vocab, args.prompt_len, seed=rank * self.users)
+            self.metric = METRIC
+            self.config = workload_config(args)
+        elif self.name == "c3":
+            self.users, self.k, self.max_new = 64, 8, 256
+            self.weight_int8 = self.kv_int8 = True
+            g = torch.Generator().manual_seed(1000 + rank)
+            prefix = torch.randint(0, vocab, (512,), generator=g).tolist()
+            self.prompts = [prefix + torch.randint(0, vocab, (512,), generator=g).tolist() for _ in range(self.users)]
+            self.shared_prefix = 512
+            self.metric = "accepted tok/s, Qwen3-0.6B int8 spec-decode at 64 users (n-gram k=8, greedy)"
+            self.config = {
+                "workload": "BASELINE config 3: Qwen3-0.6B random-init (seed 0), int8 per-output-channel weights "
+                            "(scales from the bf16 init) + int8 KV (bf16 scales per token and head), 64 users, "
+                            "1024-token prompts = one seeded 512-token prefix served from shared KV blocks + 512 "
+                            "seeded uniform IDs, 256 outputs, n-gram n=3 k=8, greedy",
+                "users_per_gpu": 64, "k": 8, "parallelism": f"dp{args.gpus} (independent replicas)",
+                "l2": "no flush: every step streams 0.75 GB of weights + 2.4 GB of KV (> 126 MB L2)"}
+        else:
+            self.users, self.k, self.max_new = 256, 4, 256
+            self.temperature, self.top_p = 0.8, 0.95
+            self.prefill_chunk = 512
+            g = torch.Generator().manual_seed(2000 + rank)
+            lengths = torch.randint(32, 2049, (self.users,), generator=g).tolist()
+            self.prompts = [pkg.make_prompt(vocab, n, 5000 + rank * self.users + i, motif=(i % 2 == 0))
+                            for i, n in enumerate(lengths)]
+            self.metric = "accepted tok/s, Qwen3-0.6B spec-decode at 256 users (sampled T=0.8 top-p 0.95, k=4)"
+            self.config = {
+                "workload": "BASELINE config 4: Qwen3-0.6B random-init (seed 0) bf16, 256 users, sampled decoding "
+                            "T=0.8 top-p 0.95 with rejection sampling on per-request Philox4x32-10 streams "
+                            "(seed = request index), prompt lengths uniform in [32, 2048] (seeded; 50% "
+                            "motif-repeated), chunked prefill 512, 256 outputs, n-gram n=3 k=4",
+                "users_per_gpu": 256, "k": 4, "parallelism": f"dp{args.gpus} (independent replicas)",
+                "l2": "no flush: every step streams 1.19 GB of weights + ~35 GB of KV (> 126 MB L2)"}
+        self.sampled = self.temperature > 0.0
+
+
 # ---------------------------------------------------------------------------- B200 arm
-def algorithmic_bytes(kind: str, cfg, M: int, ctx_sum: int, kv_bytes_per_token_layer: int) -> float:
-    """Unique bytes one launch of ``kind`` must move (weights, activations in/out, KV)."""
+def algorithmic_bytes(kind: str, cfg, M: int, ctx_sum: int, kv_bytes_per_token_layer: int, wb: float = 2.0) -> float:
+    """Unique bytes one launch of ``kind`` must move (weights at ``wb`` bytes per element plus one
+    bf16 scale per row when int8, activations in/out, KV)."""
     H, I, V = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size
     q, kv = cfg.num_attention_heads * 128, cfg.num_key_value_heads * 128
+    sc = 2 if wb == 1 else 0
     if kind == "gemm_qkv":
-        return (q + 2 * kv) * H * 2 + M * H * 2 + M * q * 2 + 2 * M * kv * 2
+        return (q + 2 * kv) * (H * wb + sc) + M * H * 2 + M * q * 2 + 2 * M * kv * 2
     if kind == "gemm_o":
-        return H * q * 2 + M * q * 2 + 2 * M * H * 2
+        return H * (q * wb + sc) + M * q * 2 + 2 * M * H * 2
     if kind == "gemm_gateup":
-        return 2 * I * H * 2 + M * H * 2 + M * I * 2
+        return 2 * I * (H * wb + sc) + M * H * 2 + M * I * 2
     if kind == "gemm_down":
-        return H * I * 2 + M * I * 2 + 2 * M * H * 2
+        return H * (I * wb + sc) + M * I * 2 + 2 * M * H * 2
     if kind == "lm_head":
         return V * H * 2 + M * H * 2 + M * 8
     if kind == "attention":
@@ -300,23 +356,28 @@ def run_b200(args, dist: Dist) -> None:
     device = torch.device("cuda", dist.local_rank)
     torch.cuda.set_device(device)
     cfg = pkg.QWEN3_0_6B
-    users, k = args.users, args.k
-    steady_new = max(args.max_new, (args.warmup + args.steps + 3) * (k + 1))
-    max_model_len = args.prompt_len + steady_new + 8
+    wl = Workload(args, pkg, cfg.vocab_size, dist.rank)
+    users, k, prompts = wl.users, wl.k, wl.prompts
+    longest = max(len(p) for p in prompts)
+    steady_new = max(wl.max_new, (args.warmup + args.steps + 3) * (k + 1))
+    max_model_len = longest + steady_new + 8
     blocks_per_user = -(-(max_model_len + k + 1) // 16)
-    num_blocks = users * blocks_per_user + 16
+    num_blocks = (users + 1) * blocks_per_user + 16  # (+1: the holder of a shared prefix)
+    max_rows = max(users * (k + 1), min(sum(len(p) for p in prompts), 16384))
     weights = pkg.make_weights(cfg, seed=0)
     model = model_mod.B200Model(cfg, weights, num_slots=num_blocks * 16, device=device,
-                                max_positions=max_model_len + k + 16, max_rows=max(users * args.prompt_len, users * (k + 1)),
-                                max_seqs=users)
+                                max_positions=max_model_len + k + 16, max_rows=max_rows, max_seqs=users + 1,
+                                kv_int8=wl.kv_int8, weight_int8=wl.weight_int8)
     del weights
-    engine = engine_mod.B200SpeculativeEngine(model, k=k, max_ngram=3, max_seqs=users, max_model_len=max_model_len,
-                                              num_blocks=num_blocks, cuda_graphs=True)
-    prompts = pkg.make_prompts(users, cfg.vocab_size, args.prompt_len, seed=dist.rank * users)
+    engine = engine_mod.B200SpeculativeEngine(model, k=k, max_ngram=3, max_seqs=users + (1 if wl.shared_prefix else 0),
+                                              max_model_len=max_model_len, num_blocks=num_blocks, cuda_graphs=True,
+                                              sampling=wl.sampled)
 
     # ------------------------------------------------------------ steady state (value)
-    slots = [engine.add_request(p, steady_new, ignore_eos=True) for p in prompts]
-    engine.prefill(slots, [len(p) for p in prompts])
+    prefix = engine.add_prefix(prompts[0][: wl.shared_prefix]) if wl.shared_prefix else None
+    slots = [engine.add_request(p, steady_new, ignore_eos=True, temperature=wl.temperature, top_p=wl.top_p,
+                                seed=i, prefix=prefix) for i, p in enumerate(prompts)]
+    engine.prefill(slots, chunk=wl.prefill_chunk)
     if args.profile_step:
         for _ in range(2):
             engine._set_slots(slots, len(slots))
@@ -371,20 +432,25 @@ def run_b200(args, dist: Dist) -> None:
     dominant = max((kinds[i] for i in range(nk) if n_by[i]), key=lambda kk: ms_by[kinds.index(kk)])
     di = kinds.index(dominant)
     avg_ms = ms_by[di] / n_by[di]
-    bytes_launch = algorithmic_bytes(dominant, cfg, M, ctx_sum, per_layer_kv)
+    wb = 1.0 if wl.weight_int8 else 2.0
+    bytes_launch = algorithmic_bytes(dominant, cfg, M, ctx_sum, per_layer_kv, wb)
     peak, peak_src = measured_peak()
     achieved = bytes_launch / (avg_ms / 1000.0) / 1e9
     traffic = ncu_traffic().get(dominant)
     roofline = {"bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_src,
                 "bytes_per_launch": int(bytes_launch), "avg_launch_ms": round(avg_ms, 5)}
-    step_bytes = model.weight_bytes + ctx_sum * model.kv_bytes_per_token() + M * model.kv_bytes_per_token()
+    # shared prefix blocks are read once per step (unique bytes), not once per user
+    unique_ctx = ctx_sum - (len(slots) - 1) * (wl.shared_prefix // 16 * 16) if wl.shared_prefix else ctx_sum
+    step_bytes = model.weight_bytes + unique_ctx * model.kv_bytes_per_token() + M * model.kv_bytes_per_token()
     step_time_s = max_ms / 1000.0 / args.steps
     step_roofline = {"bytes_per_step": int(step_bytes), "ms_per_step": round(1000 * step_time_s, 4),
                      "achieved_gbs": round(step_bytes / step_time_s / 1e9, 1),
                      "frac": round(step_bytes / step_time_s / 1e9 / peak, 4),
                      "profiled_rows": M, "profiled_ms_sum": round(step_ms_profiled, 4)}
     engine.release(slots)
+    if prefix is not None:
+        engine.drop_prefix(prefix)
 
     # ------------------------------------------------------------ e2e: the whole job through the public API
     e2e = None
@@ -395,7 +461,8 @@ def run_b200(args, dist: Dist) -> None:
         e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e_start.record(stream)
         steps_before = engine.steps_run
-        outs = engine.generate(prompts, args.max_new, ignore_eos=True)
+        outs = engine.generate(prompts, wl.max_new, ignore_eos=True, temperature=wl.temperature, top_p=wl.top_p,
+                               shared_prefix=wl.shared_prefix, prefill_chunk=wl.prefill_chunk)
         e_end.record(stream)
         torch.cuda.synchronize()
         e_ms = dist.max(e_start.elapsed_time(e_end))
@@ -409,7 +476,7 @@ def run_b200(args, dist: Dist) -> None:
 
     # ------------------------------------------------------------ CPU baseline (rank 0, N = 1)
     cpu = None
-    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and wl.name == "c2":
         threads = len(os.sched_getaffinity(0))
         torch.set_num_threads(threads)
         c_emitted, c_seconds, c_steps = cpu_oracle_run(pkg, args.cpu_seconds)
@@ -419,10 +486,11 @@ def run_b200(args, dist: Dist) -> None:
 
     if dist.rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
+            "metric": wl.metric, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded token-ID prompts, random-init weights)",
-            "config": workload_config(args) | {"steady_state_max_new_tokens": steady_new},
+            "vs_baseline": None, "dtype": "bf16 (int8 weights / KV dequantised to bf16)" if wl.weight_int8 else "bf16",
+            "data": "synthetic (seeded token-ID prompts, random-init weights)",
+            "config": wl.config | {"steady_state_max_new_tokens": steady_new},
             "e2e": e2e, "roofline": roofline, "step_roofline": step_roofline, "cpu_baseline": cpu,
             "clocks": clocks.summary(), "gpu_launches": int(launches_per_step * args.steps),
             "launches_per_step": int(launches_per_step), "emitted_tokens": int(total_emitted),

@@ -178,6 +178,7 @@ typedef struct {
   uint64_t* rng_draws;           /* [max_seqs] uniforms consumed so far (Philox counter) */
   int32_t* block_tables;         /* [max_seqs, block_table_stride] */
   int32_t* num_blocks_used;      /* [max_seqs] */
+  int32_t* num_shared_blocks;    /* [max_seqs] leading table entries owned by a shared prefix (or NULL) */
   int32_t* free_ring;            /* [num_blocks] FIFO of free block ids */
   int64_t* ring_head_tail;       /* [2]: next pop, next push (monotonic) */
   const int32_t* stop_ids;       /* [num_stop_ids] */
@@ -210,6 +211,18 @@ NE_API int ne_state_reset_blocks(const ne_batch_state* state, void* stream);
 NE_API int ne_state_free_slots(const ne_batch_state* state, const int32_t* slots, int num_slots, void* stream);
 
 /*
+ * Prefix sharing: the first ``num_blocks`` block-table entries of ``src_slot`` (full 16-token
+ * blocks holding the KV of a prompt prefix that src_slot has prefilled) become the first entries of
+ * each slot in dst_slots, which then count those tokens as cached (num_cached = num_blocks * 16)
+ * and never return the shared blocks to the FIFO (num_shared_blocks). The dst slots' histories
+ * must already hold the same prefix tokens. src_slot keeps ownership: free it only after every
+ * sharer has been freed. (The reference reaches the same KV reuse through its prefix cache,
+ * engine/memory/paged_allocator.py; here the sharing is explicit.)
+ */
+NE_API int ne_state_share_blocks(const ne_batch_state* state, int src_slot, const int32_t* dst_slots, int num_dst,
+                                 int num_blocks, int32_t* status, void* stream);
+
+/*
  * n-gram drafts (NgramProposer.propose, engine/speculative/proposers.py:44-57) for each batch
  * entry: guess cap max(0, min(k, remaining - 1)) (speculative_generator.py:71-72); the guesses are
  * written after the history (history[s][seq_len[s] ..]) like proposal tokens appended to
@@ -222,11 +235,13 @@ NE_API int ne_ngram_propose(const ne_batch_state* state, const int32_t* seq_slot
  * Prefill of newly admitted sequences (their prompts already in ``history``): reserve blocks,
  * run the forward over every prompt token, pick the first token (greedy argmax or a sampled one)
  * and append it. ModelRunner.run_step (engine/generation/model_runner.py:33-50,72-80) after
- * allocator.reserve (speculative_generator.py:52-53). ``max_rows`` bounds the sum of prompt
- * lengths; out->tokens has stride k + 1.
+ * allocator.reserve (speculative_generator.py:52-53). ``max_rows`` bounds the rows of the call;
+ * out->tokens has stride k + 1. ``chunk`` > 0: chunked prefill, at most ``chunk`` uncached tokens
+ * per sequence per call; a sequence whose prompt is not finished by the call only advances
+ * num_cached (count 0); the first token comes with its last chunk.
  */
 NE_API int ne_prefill(ne_model* model, const ne_batch_state* state, const int32_t* seq_slot, int num_seqs,
-               int max_rows, int k, const ne_step_outputs* out, void* stream);
+               int max_rows, int k, int chunk, const ne_step_outputs* out, void* stream);
 
 /*
  * One speculative step for every batch entry, entirely on the device:

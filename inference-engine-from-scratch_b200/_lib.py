@@ -43,7 +43,8 @@ EXPORTS = {
     "ne_state_reset_blocks": (c_int, [c_void_p, c_void_p]),
     "ne_state_free_slots": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
     "ne_ngram_propose": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
-    "ne_prefill": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "ne_prefill": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "ne_state_share_blocks": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "ne_spec_step": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "ne_gemm_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "ne_gemm_w8": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
@@ -142,6 +143,7 @@ class BatchState(ctypes.Structure):
         ("rng_draws", c_void_p),
         ("block_tables", c_void_p),
         ("num_blocks_used", c_void_p),
+        ("num_shared_blocks", c_void_p),
         ("free_ring", c_void_p),
         ("ring_head_tail", c_void_p),
         ("stop_ids", c_void_p),

@@ -436,6 +436,14 @@ int ne_state_free_slots(const ne_batch_state* st, const int32_t* slots, int num_
   return ne::launch_free_slots(*st, slots, num_slots, as_stream(stream));
 }
 
+int ne_state_share_blocks(const ne_batch_state* st, int src_slot, const int32_t* dst_slots, int num_dst, int num_blocks,
+                          int32_t* status, void* stream) {
+  if (!st || !st->num_shared_blocks || src_slot < 0 || src_slot >= st->max_seqs || num_blocks < 0 ||
+      (num_dst > 0 && !dst_slots))
+    return NE_ERR_INVALID;
+  return ne::launch_share_blocks(*st, src_slot, dst_slots, num_dst, num_blocks, 16, status, as_stream(stream));
+}
+
 int ne_ngram_propose(const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int k, int max_ngram,
                      int min_ngram, int32_t* draft_len, int32_t* status, void* stream) {
   if (!st || !seq_slot || !draft_len) return NE_ERR_INVALID;
@@ -505,12 +513,12 @@ int ne_verify_logits(const ne_batch_state* st, const int32_t* seq_slot, int num_
 }
 
 int ne_prefill(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int max_rows, int k,
-               const ne_step_outputs* out, void* stream) {
-  if (!m || !st || !seq_slot || !out || num_seqs <= 0 || k < 1) return NE_ERR_INVALID;
+               int chunk, const ne_step_outputs* out, void* stream) {
+  if (!m || !st || !seq_slot || !out || num_seqs <= 0 || k < 1 || chunk < 0) return NE_ERR_INVALID;
   if (max_rows > m->max_rows || num_seqs > m->max_seqs) return NE_ERR_WORKSPACE;
   cudaStream_t s = as_stream(stream);
   int rc = note(m, NE_K_PLAN,
-                ne::launch_plan(*st, seq_slot, num_seqs, ne::PLAN_PREFILL, max_rows, m->cfg.block_size,
+                ne::launch_plan(*st, seq_slot, num_seqs, ne::PLAN_PREFILL, max_rows, chunk, m->cfg.block_size,
                                 m->cfg.num_cache_slots, m->rb, m->status, s), s);
   if (rc) return rc;
   ne_rows rows = make_step_rows(m, st, seq_slot, num_seqs, max_rows, num_seqs, max_rows);
@@ -535,7 +543,7 @@ int ne_spec_step(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot,
                 s);
   if (rc) return rc;
   rc = note(m, NE_K_PLAN,
-            ne::launch_plan(*st, seq_slot, num_seqs, ne::PLAN_SPEC, max_rows, m->cfg.block_size,
+            ne::launch_plan(*st, seq_slot, num_seqs, ne::PLAN_SPEC, max_rows, 0, m->cfg.block_size,
                             m->cfg.num_cache_slots, m->rb, m->status, s), s);
   if (rc) return rc;
   ne_rows rows = make_step_rows(m, st, seq_slot, num_seqs, max_rows, max_rows, k + 1);

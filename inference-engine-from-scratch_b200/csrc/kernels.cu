@@ -171,7 +171,7 @@ __device__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
 // paged_allocator.py:69-79: slot = table[p // bs] * bs + p % bs).
 __global__ void __launch_bounds__(1024)
     plan_kernel(ne_batch_state st, const int32_t* __restrict__ seq_slot, int num_seqs, int mode, int max_rows,
-                int bs, long long num_cache_slots, RowBuffers rb, int* status) {
+                int chunk, int bs, long long num_cache_slots, RowBuffers rb, int* status) {
   pdl_prologue();
   __shared__ int warp_sums[32];
   __shared__ int s_qstart[1024];
@@ -186,6 +186,7 @@ __global__ void __launch_bounds__(1024)
       if (g >= 0) {
         const int cached = st.num_cached[s];
         ql = st.seq_len[s] - cached + g;
+        if (mode == PLAN_PREFILL && chunk > 0) ql = min(ql, chunk);  // chunked prefill
         const int end = cached + ql;
         const int blocks = (end + bs - 1) / bs;
         if (blocks > st.block_table_stride || end > st.history_stride) {
@@ -287,9 +288,17 @@ __global__ void accept_greedy_kernel(ne_batch_state st, const int32_t* __restric
     out.accepted[b] = 0;
     return;
   }
+  const int L = st.seq_len[s];
+  if (mode == PLAN_PREFILL && st.num_cached[s] + ql < L) {  // a prefill chunk short of the prompt end
+    st.num_cached[s] += ql;
+    out.count[b] = 0;
+    out.finish[b] = NE_FINISH_NONE;
+    out.proposed[b] = 0;
+    out.accepted[b] = 0;
+    return;
+  }
   if (st.temperature && st.temperature[s] > 0.f) report(status, NE_DEV_NO_SAMPLER);  // needs the logits
   const int g = mode == PLAN_SPEC ? max(rb.draft_len[b], 0) : 0;
-  const int L = st.seq_len[s];
   int32_t* hist = st.history + (long long)s * st.history_stride;
   const int ls = rb.lm_start[b];
   int kept = 0;
@@ -349,15 +358,49 @@ __global__ void free_slots_kernel(ne_batch_state st, const int32_t* slots, int n
     const int s = slots[i];
     if (s < 0 || s >= st.max_seqs) continue;
     const int used = st.num_blocks_used[s];
+    const int shared = st.num_shared_blocks ? min(st.num_shared_blocks[s], used) : 0;  // owned elsewhere
     const int32_t* row = st.block_tables + (long long)s * st.block_table_stride;
-    for (int j = 0; j < used; ++j) st.free_ring[(tail + j) % st.num_blocks] = row[j];
-    tail += used;
+    for (int j = shared; j < used; ++j) st.free_ring[(tail + j - shared) % st.num_blocks] = row[j];
+    tail += used - shared;
     st.num_blocks_used[s] = 0;
+    if (st.num_shared_blocks) st.num_shared_blocks[s] = 0;
   }
   st.ring_head_tail[1] = tail;
 }
 
+// Prefix sharing: entry i of dst_slots gets the first ``num_blocks`` table entries of src_slot (full
+// blocks of a prompt prefix whose KV src_slot computed), marked shared (never freed by this slot),
+// and those tokens count as cached.
+__global__ void share_blocks_kernel(ne_batch_state st, int src_slot, const int32_t* dst_slots, int num_dst,
+                                    int num_blocks, int bs, int* status) {
+  pdl_prologue();
+  const int i = blockIdx.x;
+  if (i >= num_dst) return;
+  const int d = dst_slots[i];
+  if (d < 0 || d >= st.max_seqs || d == src_slot) return;
+  if (num_blocks > st.num_blocks_used[src_slot] || num_blocks > st.block_table_stride ||
+      num_blocks * bs > st.seq_len[d]) {
+    if (threadIdx.x == 0) report(status, NE_DEV_HISTORY_FULL);
+    return;
+  }
+  const int32_t* src = st.block_tables + (long long)src_slot * st.block_table_stride;
+  int32_t* dst = st.block_tables + (long long)d * st.block_table_stride;
+  for (int j = threadIdx.x; j < num_blocks; j += blockDim.x) dst[j] = src[j];
+  if (threadIdx.x == 0) {
+    st.num_blocks_used[d] = num_blocks;
+    st.num_shared_blocks[d] = num_blocks;
+    st.num_cached[d] = num_blocks * bs;
+  }
+}
+
 }  // namespace
+
+int launch_share_blocks(const ne_batch_state& st, int src_slot, const int32_t* dst_slots, int num_dst, int num_blocks,
+                        int block_size, int* status, cudaStream_t stream) {
+  if (num_dst <= 0) return NE_OK;
+  return launch_kernel(share_blocks_kernel, dim3(num_dst), dim3(128), 0, stream, st, src_slot, dst_slots, num_dst,
+                       num_blocks, block_size, status) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
+}
 
 int launch_embed(const __nv_bfloat16* embed, const int32_t* tokens, const int32_t* num_rows, int max_rows, int hidden,
                  int vocab, __nv_bfloat16* out, int* status, cudaStream_t stream) {
@@ -394,11 +437,11 @@ int launch_ngram(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs
                        draft_len, status) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 
-int launch_plan(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int mode, int max_rows,
+int launch_plan(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int mode, int max_rows, int chunk,
                 int block_size, long long num_cache_slots, const RowBuffers& rb, int* status, cudaStream_t stream) {
   if (num_seqs <= 0 || num_seqs > 1024) return NE_ERR_INVALID;
-  return launch_kernel(plan_kernel, dim3(1), dim3(1024), 0, stream, st, seq_slot, num_seqs, mode, max_rows, block_size,
-                       num_cache_slots, rb, status) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
+  return launch_kernel(plan_kernel, dim3(1), dim3(1024), 0, stream, st, seq_slot, num_seqs, mode, max_rows, chunk,
+                       block_size, num_cache_slots, rb, status) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 
 int launch_accept_greedy(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int k, int mode,

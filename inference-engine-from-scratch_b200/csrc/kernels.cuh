@@ -30,8 +30,10 @@ int launch_keys_to_ids(const unsigned long long* keys, const int32_t* count, int
                        cudaStream_t stream);
 int launch_ngram(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int k, int max_ngram,
                  int min_ngram, int32_t* draft_len, int* status, cudaStream_t stream);
-int launch_plan(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int mode, int max_rows,
+int launch_plan(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int mode, int max_rows, int chunk,
                 int block_size, long long num_cache_slots, const RowBuffers& rb, int* status, cudaStream_t stream);
+int launch_share_blocks(const ne_batch_state& st, int src_slot, const int32_t* dst_slots, int num_dst, int num_blocks,
+                        int block_size, int* status, cudaStream_t stream);
 int launch_accept_greedy(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int k, int mode,
                          const RowBuffers& rb, const unsigned long long* keys, const ne_step_outputs& out,
                          int* status, cudaStream_t stream);

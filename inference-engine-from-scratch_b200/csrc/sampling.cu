@@ -484,6 +484,16 @@ __global__ void __launch_bounds__(THREADS)
     return;
   }
   const int L = st.seq_len[s];
+  if (!draft_len && q_len_arr && st.num_cached[s] + ql < L) {  // a prefill chunk short of the prompt end
+    if (threadIdx.x == 0) {
+      st.num_cached[s] += ql;
+      out.count[b] = 0;
+      out.finish[b] = NE_FINISH_NONE;
+      out.proposed[b] = 0;
+      out.accepted[b] = 0;
+    }
+    return;
+  }
   int32_t* hist = st.history + (long long)s * st.history_stride;
   const int ls = lm_start[b];
   const float T = st.temperature[s];

@@ -120,6 +120,9 @@ class B200SpeculativeEngine:
         if sampling:
             nbytes = int(self.lib.ne_sampling_buffer_bytes(model.handle, self._sample_rows))
             self._sample_buf = torch.empty(nbytes, dtype=torch.uint8, device=model.device)
+        self._uncached: dict[int, int] = {}       # slot -> prompt tokens still to prefill
+        self._prefixes: dict[int, list] = {}      # holder slot -> [tokens, shared blocks, users]
+        self._prefix_of: dict[int, int] = {}      # slot -> holder slot of its shared prefix
         self.proposed_total = 0
         self.accepted_total = 0
         self.h2d_bytes = 0  # host->device bytes copied for requests and steps
@@ -128,15 +131,43 @@ class B200SpeculativeEngine:
 
     # ------------------------------------------------------------------ request lifecycle
     def add_request(self, prompt: list[int], max_new_tokens: int, *, ignore_eos: bool = False,
-                    temperature: float = 0.0, top_p: float = 1.0, seed: int = 0) -> int:
-        """Load a request into a free slot. ``seed`` keys the request's Philox stream."""
+                    temperature: float = 0.0, top_p: float = 1.0, seed: int = 0, prefix: int | None = None) -> int:
+        """Load a request into a free slot. ``seed`` keys the request's Philox stream; ``prefix``
+        (from ``add_prefix``) shares the KV blocks of a prompt prefix the request starts with."""
         if temperature != 0.0 and not self.sampling:
             raise ValueError("temperature > 0 needs an engine built with sampling=True")
+        if prefix is not None:
+            tokens = self._prefixes[prefix][0]
+            if prompt[: len(tokens)] != tokens:
+                raise ValueError("the prompt does not start with the shared prefix")
         slot = self.state.acquire()
         self.state.load(slot, prompt, max_new_tokens, ignore_eos=ignore_eos, temperature=temperature,
                         top_p=top_p, seed=seed)
         self.h2d_bytes += 4 * len(prompt) + 5 * 4 + 4 + 4 + 8 + 8
+        shared = 0
+        if prefix is not None:
+            # whole blocks only, and at least one prompt token left to prefill (it yields the first token)
+            blocks = min(self._prefixes[prefix][1], (len(prompt) - 1) // 16)
+            self.state.share_blocks(prefix, [slot], blocks)
+            self._prefixes[prefix][2] += 1
+            self._prefix_of[slot] = prefix
+            shared = blocks * 16
+        self._uncached[slot] = len(prompt) - shared
         return slot
+
+    def add_prefix(self, tokens: list[int]) -> int:
+        """Prefill a prompt prefix once (its own slot holds the blocks); requests that start with it
+        pass the returned handle as ``prefix`` and reuse its full 16-token blocks."""
+        holder = self.add_request(tokens, 1, ignore_eos=True)
+        self.prefill([holder])
+        self._prefixes[holder] = [list(tokens), len(tokens) // 16, 0]
+        return holder
+
+    def drop_prefix(self, prefix: int) -> None:
+        if self._prefixes[prefix][2]:
+            raise RuntimeError("requests still share this prefix")
+        del self._prefixes[prefix]
+        self.state.release([prefix])
 
     def _bind_sampler(self) -> None:
         buf = self._sample_buf
@@ -153,6 +184,11 @@ class B200SpeculativeEngine:
 
     def release(self, slots: list[int]) -> None:
         self.state.release(slots)
+        for s in slots:
+            self._uncached.pop(s, None)
+            holder = self._prefix_of.pop(s, None)
+            if holder is not None:
+                self._prefixes[holder][2] -= 1
 
     def _set_slots(self, slots: list[int], bucket: int) -> None:
         self._slots_host.fill_(-1)
@@ -176,32 +212,45 @@ class B200SpeculativeEngine:
         return result
 
     # ------------------------------------------------------------------ prefill
-    def prefill(self, slots: list[int], prompt_lengths: list[int]) -> StepResult:
-        """Prefill the newly added slots (in groups of at most ``max_prefill_rows`` prompt tokens)."""
+    def prefill(self, slots: list[int], prompt_lengths: list[int] | None = None,
+                chunk: int | None = None) -> StepResult:
+        """Prefill the newly added slots: calls of at most ``max_prefill_rows`` rows; with ``chunk``,
+        at most ``chunk`` prompt tokens per sequence per call (chunked prefill), the first token
+        arriving with a sequence's last chunk. (``prompt_lengths`` is accepted for the older call
+        form; the uncached counts are known from ``add_request``.)"""
         merged = StepResult()
-        group, rows = [], 0
-        for slot, length in zip(slots, prompt_lengths):
-            if group and rows + length > self.max_prefill_rows:
-                self._prefill_group(group, rows, merged)
-                group, rows = [], 0
-            group.append(slot)
-            rows += length
-        if group:
-            self._prefill_group(group, rows, merged)
+        remaining = {s: self._uncached.get(s, 0) for s in slots}
+        pending = list(slots)
+        while pending:
+            group, rows, take = [], 0, {}
+            for s in pending:
+                r = min(remaining[s], chunk) if chunk else remaining[s]
+                if group and rows + r > self.max_prefill_rows:
+                    break
+                group.append(s)
+                take[s] = r
+                rows += r
+            if rows > self.max_prefill_rows:
+                raise ValueError(f"a prefill call of {rows} rows exceeds the workspace; use chunk=")
+            res = self._prefill_call(group, rows, chunk or 0)
+            for s in group:
+                remaining[s] -= take[s]
+                if remaining[s] == 0:
+                    merged.tokens[s] = res.tokens[s]
+                    merged.finish[s] = res.finish[s]
+                    self._uncached[s] = 0
+            pending = [s for s in pending if remaining[s] > 0]
         return merged
 
-    def _prefill_group(self, slots: list[int], rows: int, merged: StepResult) -> None:
-        if rows > self.max_prefill_rows:
-            raise ValueError(f"a prompt of {rows} tokens exceeds the prefill workspace")
+    def _prefill_call(self, slots: list[int], rows: int, chunk: int) -> StepResult:
         self._set_slots(slots, len(slots))
         self._bind_sampler()
         _lib.check(self.lib.ne_prefill(self.model.handle, self.state.ref, self._slots_dev.data_ptr(), len(slots),
-                                       rows, self.k, ctypes.byref(self.outputs.struct), _lib.stream_handle()),
-                   "ne_prefill")
+                                       max(rows, 1), self.k, chunk, ctypes.byref(self.outputs.struct),
+                                       _lib.stream_handle()), "ne_prefill")
         res = self._collect(slots)
         self.model.raise_on_device_error()
-        merged.tokens.update(res.tokens)
-        merged.finish.update(res.finish)
+        return res
 
     # ------------------------------------------------------------------ speculative step
     def _launch_step(self, bucket: int) -> None:
@@ -249,28 +298,34 @@ class B200SpeculativeEngine:
 
     # ------------------------------------------------------------------ whole requests
     def generate(self, prompts: list[list[int]], max_new_tokens: int, ignore_eos: bool = True, *,
-                 temperature: float = 0.0, top_p: float = 1.0, seeds: list[int] | None = None) -> list[list[int]]:
+                 temperature: float = 0.0, top_p: float = 1.0, seeds: list[int] | None = None,
+                 shared_prefix: int = 0, prefill_chunk: int | None = None) -> list[list[int]]:
         """Serve every prompt with continuous batching (up to ``max_seqs`` at a time); request i
-        samples with ``seeds[i]`` (default i) when ``temperature`` > 0."""
+        samples with ``seeds[i]`` (default i) when ``temperature`` > 0. ``shared_prefix`` > 0: the
+        prompts' common first tokens are prefilled once and their KV blocks shared (one slot holds
+        them); ``prefill_chunk``: chunked prefill."""
         outputs: list[list[int]] = [[] for _ in prompts]
         pending = list(range(len(prompts)))
         running: dict[int, int] = {}  # slot -> request index
+        prefix = self.add_prefix(prompts[0][:shared_prefix]) if shared_prefix else None
         while pending or running:
             admitted = []
             while pending and self.state.free_slots:
                 index = pending.pop(0)
                 slot = self.add_request(prompts[index], max_new_tokens, ignore_eos=ignore_eos,
                                         temperature=temperature, top_p=top_p,
-                                        seed=seeds[index] if seeds is not None else index)
+                                        seed=seeds[index] if seeds is not None else index, prefix=prefix)
                 running[slot] = index
                 admitted.append(slot)
             if admitted:
-                res = self.prefill(admitted, [len(prompts[running[s]]) for s in admitted])
+                res = self.prefill(admitted, chunk=prefill_chunk)
                 self._absorb(res, running, outputs)
             if running:
                 slots = sorted(running)
                 res = self.step(slots)
                 self._absorb(res, running, outputs)
+        if prefix is not None:
+            self.drop_prefix(prefix)
         return outputs
 
     def _absorb(self, res: StepResult, running: dict[int, int], outputs: list[list[int]]) -> None:

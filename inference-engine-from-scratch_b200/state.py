@@ -66,6 +66,7 @@ class DeviceBatchState:
         self.rng_draws = torch.zeros(max_seqs, dtype=torch.int64, device=dev)
         self.block_tables = torch.full((max_seqs, self.block_table_stride), -1, **i32)
         self.num_blocks_used = torch.zeros(max_seqs, **i32)
+        self.num_shared_blocks = torch.zeros(max_seqs, **i32)
         self.free_ring = torch.zeros(num_blocks, **i32)
         self.ring_head_tail = torch.zeros(2, dtype=torch.int64, device=dev)
         stops = list(stop_token_ids) or [-1]
@@ -78,6 +79,7 @@ class DeviceBatchState:
             temperature=self.temperature.data_ptr(), top_p=self.top_p.data_ptr(),
             rng_seed=self.rng_seed.data_ptr(), rng_draws=self.rng_draws.data_ptr(),
             block_tables=self.block_tables.data_ptr(), num_blocks_used=self.num_blocks_used.data_ptr(),
+            num_shared_blocks=self.num_shared_blocks.data_ptr(),
             free_ring=self.free_ring.data_ptr(), ring_head_tail=self.ring_head_tail.data_ptr(),
             stop_ids=self.stop_ids.data_ptr(), num_stop_ids=len(stop_token_ids),
         )
@@ -130,6 +132,19 @@ class DeviceBatchState:
             if s not in self.free_slots:
                 self.free_slots.append(s)
         self._keepalive = ids
+
+    def share_blocks(self, src_slot: int, dst_slots: list[int], num_blocks: int) -> None:
+        """The first ``num_blocks`` table entries of ``src_slot`` become shared, cached blocks of
+        each slot in ``dst_slots`` (ne_state_share_blocks)."""
+        if not dst_slots or num_blocks <= 0:
+            return
+        ids = torch.tensor(dst_slots, dtype=torch.int32).to(self.device)
+        status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        _lib.check(self.lib.ne_state_share_blocks(self.ref, src_slot, ids.data_ptr(), len(dst_slots), num_blocks,
+                                                  status.data_ptr(), _lib.stream_handle()), "ne_state_share_blocks")
+        word = int(status.item())
+        if word:
+            raise _lib.NativeError(f"device reported: {_lib.describe_device_status(word)} (0x{word:x})")
 
     # ------------------------------------------------------------------ inspection (host copies)
     def block_table(self, slot: int) -> list[int]:

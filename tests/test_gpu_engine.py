@@ -127,6 +127,24 @@ def test_int8_engine_serves_the_int8_reference_outputs(small_int8) -> None:
     model.raise_on_device_error()
 
 
+@pytest.mark.parametrize("chunk", [None, 16, 40])
+def test_shared_prefix_blocks_and_chunked_prefill_serve_the_same_outputs(small, chunk) -> None:
+    """Config 3's shared-prefix blocks and config 4's chunked prefill change no request's output;
+    every block returns to the FIFO afterwards."""
+    cfg, _, model = small
+    pkg = package()
+    g = torch.Generator().manual_seed(17)
+    prefix = torch.randint(0, cfg.vocab_size, (40,), generator=g).tolist()  # 2 full blocks + 8 tokens
+    prompts = [prefix + t for t in pkg.make_prompts(4, cfg.vocab_size, length=30, seed=3)]
+    plain = _engine(model, 2, True).generate(prompts, 24)
+    eng = _engine(model, 2, True)
+    free_before = eng.state.num_free_blocks()
+    shared = eng.generate(prompts, 24, shared_prefix=len(prefix), prefill_chunk=chunk)
+    assert shared == plain
+    assert eng.state.num_free_blocks() == free_before
+    model.raise_on_device_error()
+
+
 def test_verify_with_full_length_drafts_matches_the_oracle(small) -> None:
     """Random-init greedy output collapses to 1-token drafts; force k-token drafts through the
     serial runner to check the k+1-row verify forward and greedy acceptance against the oracle."""
