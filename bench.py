@@ -19,7 +19,8 @@
 Other BASELINE workloads (not the default line): ``--workload c3`` (int8 weights + int8 KV, 64 users,
 k=8, 1024-token prompts whose first 512 tokens are one shared prefix served from shared KV blocks,
 256 outputs) and ``--workload c4`` (256 users, sampled T=0.8 / top-p 0.95 on per-request Philox
-streams, prompt lengths uniform in [32, 2048], chunked prefill of 512 tokens, 256 outputs, k=4).
+streams, prompt lengths uniform in [32, 2048], chunked prefill of 512 tokens, 256 outputs, k=4), ``--workload c5b`` (Qwen3-8B shape, bf16, tensor-parallel over the N torchrun ranks
+with NCCL all-reduce after o_proj and down_proj, 32 users, 512-token prompts, 256 outputs, k=4).
 
 Multi-GPU: one process per GPU (torchrun); each rank serves its own 64 users on an independent
 replica (no collectives on the data path); NCCL only carries the barrier and the max-over-ranks
@@ -56,8 +57,9 @@ def parse_args():
     p.add_argument("--steps", type=int, default=30)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
-    p.add_argument("--workload", choices=("c2", "c3", "c4"), default="c2",
-                   help="BASELINE config: c2 (default, the headline), c3 (int8, shared prefix), c4 (sampled)")
+    p.add_argument("--workload", choices=("c2", "c3", "c4", "c5b"), default="c2",
+                   help="BASELINE config: c2 (default, the headline), c3 (int8, shared prefix), c4 (sampled), "
+                        "c5b (Qwen3-8B shape, tensor parallel over the torchrun ranks)")
     p.add_argument("--users", type=int, default=64)
     p.add_argument("--k", type=int, default=4)
     p.add_argument("--prompt-len", type=int, default=64)
@@ -107,6 +109,13 @@ class Dist:
         t = torch.tensor([value], dtype=torch.float64, device=f"cuda:{self.local_rank}")
         self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
         return float(t.item())
+
+    def broadcast_bytes(self, data: bytes | None) -> bytes:
+        if not self.enabled:
+            return data
+        box = [data]
+        self.dist.broadcast_object_list(box, src=0)
+        return box[0]
 
     def close(self) -> None:
         if self.enabled:
@@ -283,6 +292,8 @@ class Workload:
 
     def __init__(self, args, pkg, vocab: int, rank: int) -> None:
         self.name = args.workload
+        self.cfg = pkg.QWEN3_0_6B
+        self.tp = False
         self.weight_int8 = self.kv_int8 = False
         self.temperature, self.top_p = 0.0, 1.0
         self.shared_prefix, self.prefill_chunk = 0, None
@@ -306,6 +317,19 @@ class Workload:
                             "seeded uniform IDs, 256 outputs, n-gram n=3 k=8, greedy",
                 "users_per_gpu": 64, "k": 8, "parallelism": f"dp{args.gpus} (independent replicas)",
                 "l2": "no flush: every step streams 0.75 GB of weights + 2.4 GB of KV (> 126 MB L2)"}
+        elif self.name == "c5b":
+            self.cfg = pkg.QWEN3_8B_SHAPE
+            self.tp = True
+            self.users, self.k, self.max_new = 32, 4, 256
+            self.prompts = pkg.make_prompts(self.users, vocab, 512, seed=7000)  # the same on every rank
+            self.metric = "accepted tok/s, Qwen3-8B-shape spec-decode at 32 users (n-gram k=4, greedy), tensor parallel"
+            self.config = {
+                "workload": "BASELINE config 5b: Qwen3-8B shape (36 layers, hidden 4096, 32/8 heads, MLP 12288, "
+                            "vocab 151936, untied head) random-init bf16, tensor-parallel over the GPUs (NCCL "
+                            "all-reduce of fp32 partials after o_proj and down_proj, vocabulary-split LM head), "
+                            "32 users, 512-token prompts (50% motif-repeated), 256 outputs, n-gram n=3 k=4, greedy",
+                "users": 32, "k": 4, "parallelism": f"tp{args.gpus}",
+                "l2": "no flush: every step streams 15.1 GB / N of weights + KV (> 126 MB L2)"}
         else:
             self.users, self.k, self.max_new = 256, 4, 256
             self.temperature, self.top_p = 0.8, 0.95
@@ -355,8 +379,8 @@ def run_b200(args, dist: Dist) -> None:
     importlib.import_module(f"{PACKAGE}.build").build()
     device = torch.device("cuda", dist.local_rank)
     torch.cuda.set_device(device)
-    cfg = pkg.QWEN3_0_6B
-    wl = Workload(args, pkg, cfg.vocab_size, dist.rank)
+    wl = Workload(args, pkg, pkg.QWEN3_0_6B.vocab_size, dist.rank)
+    cfg = wl.cfg
     users, k, prompts = wl.users, wl.k, wl.prompts
     longest = max(len(p) for p in prompts)
     steady_new = max(wl.max_new, (args.warmup + args.steps + 3) * (k + 1))
@@ -364,10 +388,22 @@ def run_b200(args, dist: Dist) -> None:
     blocks_per_user = -(-(max_model_len + k + 1) // 16)
     num_blocks = (users + 1) * blocks_per_user + 16  # (+1: the holder of a shared prefix)
     max_rows = max(users * (k + 1), min(sum(len(p) for p in prompts), 16384))
-    weights = pkg.make_weights(cfg, seed=0)
-    model = model_mod.B200Model(cfg, weights, num_slots=num_blocks * 16, device=device,
-                                max_positions=max_model_len + k + 16, max_rows=max_rows, max_seqs=users + 1,
-                                kv_int8=wl.kv_int8, weight_int8=wl.weight_int8)
+    if wl.tp:
+        tp_mod = importlib.import_module(f"{PACKAGE}.tp")
+        plan = tp_mod.shard_plan(cfg, dist.rank, dist.world)
+        lib_path = tp_mod.nccl_library_path()
+        uid = dist.broadcast_bytes(tp_mod.unique_id(lib_path) if dist.rank == 0 else None)
+        weights = tp_mod.make_sharded_weights(cfg, plan, seed=0, device=device)
+        model = model_mod.B200Model(tp_mod.rank_config(cfg, plan), weights, num_slots=num_blocks * 16, device=device,
+                                    max_positions=max_model_len + k + 16, max_rows=max_rows, max_seqs=users + 1,
+                                    tp=tp_mod.TensorParallel(dist.rank, dist.world, uid, lib_path),
+                                    lm_offset=plan.vocab[0])
+        cfg = tp_mod.rank_config(cfg, plan)  # per-rank shapes for the byte counts below
+    else:
+        weights = pkg.make_weights(cfg, seed=0)
+        model = model_mod.B200Model(cfg, weights, num_slots=num_blocks * 16, device=device,
+                                    max_positions=max_model_len + k + 16, max_rows=max_rows, max_seqs=users + 1,
+                                    kv_int8=wl.kv_int8, weight_int8=wl.weight_int8)
     del weights
     engine = engine_mod.B200SpeculativeEngine(model, k=k, max_ngram=3, max_seqs=users + (1 if wl.shared_prefix else 0),
                                               max_model_len=max_model_len, num_blocks=num_blocks, cuda_graphs=True,
@@ -407,7 +443,7 @@ def run_b200(args, dist: Dist) -> None:
     emitted = engine.state.seq_len.sum().item() - lens_before
     model.raise_on_device_error()
     max_ms = dist.max(ms)
-    total_emitted = dist.sum(emitted)
+    total_emitted = emitted if wl.tp else dist.sum(emitted)  # a split model's ranks emit the same tokens
     value = total_emitted / (max_ms / 1000.0)
 
     # ------------------------------------------------------------ one profiled (eager) step: roofline
@@ -429,7 +465,9 @@ def run_b200(args, dist: Dist) -> None:
     kinds = lib_mod.KERNEL_KINDS
     profile = {kinds[i]: {"ms": round(ms_by[i], 4), "launches": n_by[i]} for i in range(nk) if n_by[i]}
     step_ms_profiled = sum(ms_by[i] for i in range(nk))
-    dominant = max((kinds[i] for i in range(nk) if n_by[i]), key=lambda kk: ms_by[kinds.index(kk)])
+    # the dominant kernel of ours (NCCL's all-reduce is timed in the profile but is not one of ours)
+    dominant = max((kinds[i] for i in range(nk) if n_by[i] and kinds[i] != "collective"),
+                   key=lambda kk: ms_by[kinds.index(kk)])
     di = kinds.index(dominant)
     avg_ms = ms_by[di] / n_by[di]
     wb = 1.0 if wl.weight_int8 else 2.0
@@ -466,7 +504,7 @@ def run_b200(args, dist: Dist) -> None:
         e_end.record(stream)
         torch.cuda.synchronize()
         e_ms = dist.max(e_start.elapsed_time(e_end))
-        tokens = dist.sum(sum(len(o) for o in outs))
+        tokens = sum(len(o) for o in outs) if wl.tp else dist.sum(sum(len(o) for o in outs))
         n_steps = max(1, engine.steps_run - steps_before)
         e2e = {"value": tokens / (e_ms / 1000.0), "unit": UNIT,
                "h2d_bytes_per_step": int(engine.h2d_bytes / n_steps),
@@ -487,17 +525,23 @@ def run_b200(args, dist: Dist) -> None:
     if dist.rank == 0:
         line = {
             "metric": wl.metric, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if wl.tp else "weak",
             "vs_baseline": None, "dtype": "bf16 (int8 weights / KV dequantised to bf16)" if wl.weight_int8 else "bf16",
             "data": "synthetic (seeded token-ID prompts, random-init weights)",
             "config": wl.config | {"steady_state_max_new_tokens": steady_new},
             "e2e": e2e, "roofline": roofline, "step_roofline": step_roofline, "cpu_baseline": cpu,
             "clocks": clocks.summary(), "gpu_launches": int(launches_per_step * args.steps),
             "launches_per_step": int(launches_per_step), "emitted_tokens": int(total_emitted),
-            "tokens_per_step_per_user": round(total_emitted / dist.world / args.steps / users, 3),
+            "tokens_per_step_per_user": round(total_emitted / (1 if wl.tp else dist.world) / args.steps / users, 3),
             "kernel_profile": profile,
         }
         print(json.dumps(line), flush=True)
+    # CUDA graphs hold the model's NCCL calls (tensor parallel): release them before the communicator
+    del graph
+    engine._graphs.clear()
+    del engine
+    torch.cuda.synchronize()
     model.close()
 
 

@@ -63,6 +63,8 @@ typedef struct {
   int weight_int8;            /* 0: bf16 projections; 1: int8 + per-output-row bf16 scales */
   long long num_cache_slots;  /* KV pool rows including the scratch slot (num_slots + 1) */
   int max_positions;          /* rows of the RoPE tables */
+  int lm_rows;                /* LM-head rows on this rank (0: vocab_size); a multiple of 128 */
+  int lm_offset;              /* vocabulary id of this rank's first LM-head row (tensor parallelism) */
 } ne_model_config;
 
 /*
@@ -284,6 +286,24 @@ NE_API int ne_verify_logits(const ne_batch_state* state, const int32_t* seq_slot
                             int lm_rows, void* scratch, size_t scratch_bytes, const ne_step_outputs* out,
                             int32_t* status, void* stream);
 
+/* ---------------------------------------------------------------- tensor parallelism */
+/*
+ * A model split over 2/4/8 GPUs, one process per GPU: column-parallel QKV (whole KV heads per rank)
+ * and gate/up, row-parallel o_proj and down_proj whose fp32 partial outputs are summed by an NCCL
+ * all-reduce before the residual add (then rounded as the unsplit model rounds its projection),
+ * and the LM head split by vocabulary rows (each rank's argmax keys max-reduced across ranks, so
+ * every rank takes the same acceptance decisions on its own copy of the batch state). The config's
+ * num_heads / num_kv_heads / intermediate_size are this rank's share, lm_rows / lm_offset its
+ * vocabulary rows; the embedding and the norms are whole on every rank. Greedy only: sampled
+ * steps return NE_ERR_UNSUPPORTED on a split model.
+ * ``nccl_library`` is the path of the NCCL library to load (the one PyTorch uses). Rank 0 makes
+ * the unique id (128 bytes) and the caller hands the same bytes to every rank; ne_model_set_tp
+ * comes before ne_model_workspace_bytes / ne_model_set_workspace (the workspace then holds the
+ * fp32 partial buffer of the all-reduce).
+ */
+NE_API int ne_tp_unique_id(const char* nccl_library, void* unique_id);
+NE_API int ne_model_set_tp(ne_model* model, const char* nccl_library, int rank, int world, const void* unique_id);
+
 /* ---------------------------------------------------------------- launch accounting */
 /* Kernel classes of a step, for per-kernel device timing (ne_model_profile_*). */
 #define NE_K_EMBED 0
@@ -299,7 +319,8 @@ NE_API int ne_verify_logits(const ne_batch_state* state, const int32_t* seq_slot
 #define NE_K_ACCEPT 10
 #define NE_K_OTHER 11
 #define NE_K_SAMPLE 12       /* per-row softmax / top-p statistics of sampled sequences */
-#define NE_NUM_KINDS 13
+#define NE_K_COLLECTIVE 13   /* NCCL all-reduce (tensor parallelism; not counted as a launch of ours) */
+#define NE_NUM_KINDS 14
 
 /* Kernels this model has launched so far (every entry point that takes the model counts). */
 NE_API long long ne_model_launch_count(const ne_model* model);

@@ -66,13 +66,15 @@ EXPORTS = {
         [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p,
          c_void_p, c_void_p],
     ),
+    "ne_tp_unique_id": (c_int, [ctypes.c_char_p, c_void_p]),
+    "ne_model_set_tp": (c_int, [c_void_p, ctypes.c_char_p, c_int, c_int, c_void_p]),
     "ne_model_launch_count": (c_longlong, [c_void_p]),
     "ne_model_profile_begin": (c_int, [c_void_p, c_void_p]),
     "ne_model_profile_end": (c_int, [c_void_p, POINTER(c_float), POINTER(c_int), c_int]),
 }
 
 KERNEL_KINDS = ("embed", "rmsnorm", "gemm_qkv", "attention", "gemm_o", "gemm_gateup", "gemm_down", "lm_head",
-                "ngram", "plan", "accept", "other", "sample")
+                "ngram", "plan", "accept", "other", "sample", "collective")
 
 
 class ModelConfig(ctypes.Structure):
@@ -90,6 +92,8 @@ class ModelConfig(ctypes.Structure):
         ("weight_int8", c_int),
         ("num_cache_slots", c_longlong),
         ("max_positions", c_int),
+        ("lm_rows", c_int),
+        ("lm_offset", c_int),
     ]
 
 

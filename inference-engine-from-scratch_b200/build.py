@@ -41,6 +41,35 @@ def nvcc_path() -> str:
     raise RuntimeError("nvcc not found: the B200 kernels need the CUDA toolkit to build")
 
 
+def nccl_include() -> list[str]:
+    """NCCL's public header (types only: the library is dlopen'ed at run time, tp.cu)."""
+    try:
+        import importlib.util
+
+        spec = importlib.util.find_spec("nvidia.nccl")
+        for root in (spec.submodule_search_locations or []) if spec else []:
+            if (Path(root) / "include" / "nccl.h").exists():
+                return [f"-I{Path(root) / 'include'}"]
+    except Exception:
+        pass
+    return []  # the system include path (/usr/include/nccl.h)
+
+
+def nccl_library() -> str | None:
+    """The NCCL shared library PyTorch loads (tensor parallelism uses the same one)."""
+    try:
+        import importlib.util
+
+        spec = importlib.util.find_spec("nvidia.nccl")
+        for root in (spec.submodule_search_locations or []) if spec else []:
+            lib = Path(root) / "lib" / "libnccl.so.2"
+            if lib.exists():
+                return str(lib)
+    except Exception:
+        pass
+    return None
+
+
 def sources() -> list[Path]:
     return sorted(CSRC.glob("*.cu"))
 
@@ -57,23 +86,36 @@ def is_stale() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
+    """Build if stale. Concurrent callers (several ranks of one job) serialise on a lock file; the
+    first builds, the others then find the library fresh."""
     if not force and not is_stale():
         return LIBRARY
-    nvcc = nvcc_path()
-    objects = []
+    import fcntl
+
     build_dir = PACKAGE_DIR / "_build"
     build_dir.mkdir(exist_ok=True)
+    with open(build_dir / ".lock", "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        if not force and not is_stale():
+            return LIBRARY
+        return _build(build_dir, verbose)
+
+
+def _build(build_dir: Path, verbose: bool) -> Path:
+    nvcc = nvcc_path()
+    objects = []
     for src in sources():
         obj = build_dir / (src.stem + ".o")
-        cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, f"-I{INCLUDE}", f"-I{CSRC}", "-c", str(src), "-o", str(obj)]
+        cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, f"-I{INCLUDE}", f"-I{CSRC}", *nccl_include(), "-c", str(src), "-o",
+               str(obj)]
         proc = subprocess.run(cmd, capture_output=True, text=True)
         if proc.returncode != 0:
             raise RuntimeError(f"nvcc failed on {src.name}:\n{proc.stderr}")
         if verbose:
             sys.stderr.write(proc.stderr)
         objects.append(str(obj))
-    tmp = LIBRARY.with_suffix(".so.tmp")
-    cmd = [nvcc, *ARCH_FLAGS, "-shared", "-cudart", "static", "-o", str(tmp), *objects]
+    tmp = LIBRARY.with_suffix(f".so.{os.getpid()}.tmp")
+    cmd = [nvcc, *ARCH_FLAGS, "-shared", "-cudart", "static", "-o", str(tmp), *objects, "-ldl"]
     proc = subprocess.run(cmd, capture_output=True, text=True)
     if proc.returncode != 0:
         raise RuntimeError(f"nvcc link failed:\n{proc.stderr}")

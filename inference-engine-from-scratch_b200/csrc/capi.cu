@@ -10,6 +10,7 @@
 #include "gemm_tc.cuh"
 #include "kernels.cuh"
 #include "sampling.cuh"
+#include "tp.cuh"
 
 using ne::GemmParams;
 
@@ -35,6 +36,10 @@ struct ne_model {
   __nv_bfloat16* sample_logits = nullptr;
   ne::SampleStats* sample_stats = nullptr;
   int sample_rows = 0;
+  // tensor parallelism
+  void* tp_comm = nullptr;
+  int tp_rank = 0, tp_world = 1;
+  float* partial = nullptr;  // fp32 [max_rows, H]: row-parallel projection outputs, all-reduced
   CUtensorMap tm_x{}, tm_attn{}, tm_act{};
   int num_sms = 148;
   // launch accounting / profiling
@@ -46,6 +51,7 @@ struct ne_model {
   size_t events_used = 0;
   ~ne_model() {
     for (cudaEvent_t e : events) cudaEventDestroy(e);
+    ne::tp_comm_destroy(tp_comm);
   }
 };
 
@@ -60,10 +66,10 @@ size_t sampling_logits_bytes(const ne_model_config& c, int rows) {
 }  // split-KV partials (few sequences, long contexts)
 
 struct Layout {
-  size_t status, h, x, q, attn, act, keys, rows_i32, seqs_i32, scalars, attn_scratch, total;
+  size_t status, h, x, q, attn, act, keys, rows_i32, seqs_i32, scalars, attn_scratch, partial, total;
 };
 
-Layout workspace_layout(const ne_model_config& c, int R, int B) {
+Layout workspace_layout(const ne_model_config& c, int R, int B, int tp_world) {
   Layout l{};
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -83,6 +89,7 @@ Layout workspace_layout(const ne_model_config& c, int R, int B) {
   l.seqs_i32 = take((size_t)B * 4 * 4);   // q_start, q_len, lm_start, draft_len
   l.scalars = take(64);                   // num_rows, lm_count
   l.attn_scratch = take(ATTN_SCRATCH_BYTES);
+  l.partial = tp_world > 1 ? take((size_t)R * c.hidden_size * 4) : 0;
   l.total = off;
   return l;
 }
@@ -92,7 +99,7 @@ cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 // Count one launch of ``kind``; while profiling, close its timing interval with an event.
 int note(ne_model* m, int kind, int rc, cudaStream_t stream) {
   if (rc != NE_OK) return rc;
-  ++m->launches;
+  if (kind != NE_K_COLLECTIVE) ++m->launches;
   if (m->profiling && stream == m->profile_stream) {
     if (m->events_used >= m->events.size()) {
       cudaEvent_t e;
@@ -185,11 +192,16 @@ int ne_model_create(const ne_model_config* cfg, ne_model** out) {
   const ne_model_config& c = *cfg;
   if (c.head_dim != 128 || c.block_size != 16 || c.num_kv_heads <= 0 || c.num_heads % c.num_kv_heads ||
       c.hidden_size % 256 || c.intermediate_size % 64 || c.vocab_size % 128 || c.num_layers <= 0 ||
-      c.num_cache_slots < 2 || c.max_positions <= 0)
+      c.num_cache_slots < 2 || c.max_positions <= 0 || c.lm_rows < 0 || c.lm_rows % 128 || c.lm_offset < 0 ||
+      c.lm_offset + c.lm_rows > c.vocab_size)
     return NE_ERR_INVALID;
   ne_model* m = new (std::nothrow) ne_model();
   if (!m) return NE_ERR_INVALID;
   m->cfg = c;
+  if (m->cfg.lm_rows == 0) {  // the whole vocabulary
+    m->cfg.lm_rows = c.vocab_size;
+    m->cfg.lm_offset = 0;
+  }
   m->layers.resize(c.num_layers);
   m->tm_qkv.resize(c.num_layers);
   m->tm_o.resize(c.num_layers);
@@ -234,7 +246,7 @@ int ne_model_set_layer(ne_model* m, int layer, const ne_layer_weights* w) {
 int ne_model_set_head(ne_model* m, const ne_head_weights* hw) {
   if (!m || !hw || !hw->embed || !hw->lm_head || !hw->final_norm || !hw->rope_cos || !hw->rope_sin)
     return NE_ERR_INVALID;
-  if (!ne::make_tmap_bf16(&m->tm_lm, hw->lm_head, m->cfg.vocab_size, m->cfg.hidden_size, ne::GEMM_BM, ne::GEMM_BK))
+  if (!ne::make_tmap_bf16(&m->tm_lm, hw->lm_head, m->cfg.lm_rows, m->cfg.hidden_size, ne::GEMM_BM, ne::GEMM_BK))
     return NE_ERR_INVALID;
   m->head = *hw;
   m->head_set = true;
@@ -243,14 +255,14 @@ int ne_model_set_head(ne_model* m, const ne_head_weights* hw) {
 
 int ne_model_workspace_bytes(const ne_model* m, int max_rows, int max_seqs, size_t* bytes) {
   if (!m || !bytes || max_rows <= 0 || max_seqs <= 0 || max_seqs > 1024) return NE_ERR_INVALID;
-  *bytes = workspace_layout(m->cfg, max_rows, max_seqs).total;
+  *bytes = workspace_layout(m->cfg, max_rows, max_seqs, m->tp_world).total;
   return NE_OK;
 }
 
 int ne_model_set_workspace(ne_model* m, void* ws, size_t bytes, int max_rows, int max_seqs) {
   if (!m || !ws || max_rows <= 0 || max_seqs <= 0 || max_seqs > 1024) return NE_ERR_INVALID;
   if (reinterpret_cast<uintptr_t>(ws) & 255u) return NE_ERR_INVALID;
-  Layout l = workspace_layout(m->cfg, max_rows, max_seqs);
+  Layout l = workspace_layout(m->cfg, max_rows, max_seqs, m->tp_world);
   if (bytes < l.total) return NE_ERR_WORKSPACE;
   const ne_model_config& c = m->cfg;
   char* base = static_cast<char*>(ws);
@@ -280,6 +292,7 @@ int ne_model_set_workspace(ne_model* m, void* ws, size_t bytes, int max_rows, in
   m->rb.lm_count = sc + 1;
   m->attn_scratch = base + l.attn_scratch;
   m->attn_scratch_bytes = ATTN_SCRATCH_BYTES;
+  m->partial = m->tp_world > 1 ? reinterpret_cast<float*>(base + l.partial) : nullptr;
   const int qs = c.num_heads * 128;
   bool ok = ne::make_tmap_bf16(&m->tm_x, m->x, max_rows, c.hidden_size, ne::GEMM_XBOX, ne::GEMM_BK) &&
             ne::make_tmap_bf16(&m->tm_attn, m->attn, max_rows, qs, ne::GEMM_XBOX, ne::GEMM_BK) &&
@@ -291,6 +304,25 @@ int ne_model_set_workspace(ne_model* m, void* ws, size_t bytes, int max_rows, in
 
 int32_t* ne_model_status_word(ne_model* m) { return m ? m->status : nullptr; }
 
+int ne_tp_unique_id(const char* nccl_library, void* unique_id) {
+  if (!nccl_library || !unique_id) return NE_ERR_INVALID;
+  const int rc = ne::tp_load(nccl_library);
+  return rc ? rc : ne::tp_unique_id(unique_id);
+}
+
+int ne_model_set_tp(ne_model* m, const char* nccl_library, int rank, int world, const void* unique_id) {
+  if (!m || !nccl_library || !unique_id || world < 1 || rank < 0 || rank >= world || m->ws || m->tp_comm)
+    return NE_ERR_INVALID;
+  if (world == 1) return NE_OK;
+  int rc = ne::tp_load(nccl_library);
+  if (rc) return rc;
+  rc = ne::tp_comm_init(&m->tp_comm, world, unique_id, rank);
+  if (rc) return rc;
+  m->tp_rank = rank;
+  m->tp_world = world;
+  return NE_OK;
+}
+
 int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int32_t* argmax_out, void* stream) {
   if (!m || !rows || !m->ws || !m->head_set) return NE_ERR_INVALID;
   for (char set : m->layer_set)
@@ -299,6 +331,8 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
   const int R = rows->max_rows;
   if (R <= 0 || R > m->max_rows || rows->lm_max > m->max_rows || rows->num_seqs > m->max_seqs) return NE_ERR_WORKSPACE;
   if (lm_mode == NE_LM_LOGITS && !logits) return NE_ERR_INVALID;
+  const bool tp = m->tp_world > 1;
+  if (tp && lm_mode == NE_LM_LOGITS) return NE_ERR_UNSUPPORTED;  // logits are split over the ranks
   cudaStream_t s = as_stream(stream);
   const int H = c.hidden_size, I = c.intermediate_size, qs = c.num_heads * 128, kvs = c.num_kv_heads * 128;
   const __nv_bfloat16* embed = static_cast<const __nv_bfloat16*>(m->head.embed);
@@ -313,9 +347,10 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
                                                       splits, max_vec);
   for (int l = 0; l < c.num_layers; ++l) {
     const ne_layer_weights& w = m->layers[l];
+    // (tensor parallel: the previous layer's all-reduced down_proj output joins the residual here)
     rc = note(m, NE_K_RMSNORM,
               ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(w.ln_in), m->x, R, rows->num_rows, nullptr,
-                                 H, c.rms_norm_eps, nullptr, s), s);
+                                 H, c.rms_norm_eps, nullptr, s, tp && l > 0 ? m->partial : nullptr), s);
     if (rc) return rc;
     ne::Epilogue e{};
     e.mode = ne::EPI_QKV;
@@ -346,15 +381,20 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
                                       c.num_kv_heads, c.num_cache_slots, attn, m->status, s), s);
     if (rc) return rc;
     ne::Epilogue eo{};
-    eo.mode = ne::EPI_RESIDUAL;
+    eo.mode = tp ? ne::EPI_STORE_F32 : ne::EPI_RESIDUAL;
     eo.status = m->status;
     eo.out = m->h;
+    eo.out_f32 = m->partial;
     eo.ldo = H;
     rc = note(m, NE_K_GEMM_O, run_gemm(m, &m->tm_o[l], &m->tm_attn, R, rows->num_rows, H, qs, eo, s, w.w_o_scale), s);
     if (rc) return rc;
+    if (tp) {
+      rc = note(m, NE_K_COLLECTIVE, ne::tp_allreduce_sum_f32(m->partial, (size_t)R * H, m->tp_comm, s), s);
+      if (rc) return rc;
+    }
     rc = note(m, NE_K_RMSNORM,
               ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(w.ln_post), m->x, R, rows->num_rows, nullptr,
-                                 H, c.rms_norm_eps, nullptr, s), s);
+                                 H, c.rms_norm_eps, nullptr, s, tp ? m->partial : nullptr), s);
     if (rc) return rc;
     ne::Epilogue eg{};
     eg.mode = ne::EPI_SWIGLU;
@@ -364,28 +404,39 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
     rc = note(m, NE_K_GEMM_GATEUP, run_gemm(m, &m->tm_gateup[l], &m->tm_x, R, rows->num_rows, 2 * I, H, eg, s, w.w_gateup_scale), s);
     if (rc) return rc;
     ne::Epilogue ed{};
-    ed.mode = ne::EPI_RESIDUAL;
+    ed.mode = tp ? ne::EPI_STORE_F32 : ne::EPI_RESIDUAL;
     ed.status = m->status;
     ed.out = m->h;
+    ed.out_f32 = m->partial;
     ed.ldo = H;
     rc = note(m, NE_K_GEMM_DOWN, run_gemm(m, &m->tm_down[l], &m->tm_act, R, rows->num_rows, H, I, ed, s, w.w_down_scale), s);
     if (rc) return rc;
+    if (tp) {
+      rc = note(m, NE_K_COLLECTIVE, ne::tp_allreduce_sum_f32(m->partial, (size_t)R * H, m->tp_comm, s), s);
+      if (rc) return rc;
+    }
   }
   // final norm over the rows that get logits (gathered to the front of x), keys cleared
   const int lm_max = rows->lm_max;
   rc = note(m, NE_K_RMSNORM,
             ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(m->head.final_norm), m->x, lm_max,
-                               rows->lm_count, rows->lm_rows, H, c.rms_norm_eps, m->keys, s), s);
+                               rows->lm_count, rows->lm_rows, H, c.rms_norm_eps, m->keys, s,
+                               tp ? m->partial : nullptr), s);
   if (rc) return rc;
   if (lm_mode == NE_LM_NONE) return NE_OK;
   ne::Epilogue el{};
   el.mode = lm_mode == NE_LM_LOGITS ? ne::EPI_LOGITS : ne::EPI_ARGMAX;
   el.status = m->status;
   el.out = static_cast<__nv_bfloat16*>(logits);
-  el.ldo = c.vocab_size;
+  el.ldo = c.lm_rows;
   el.argmax_keys = m->keys;
-  rc = note(m, NE_K_LM_HEAD, run_gemm(m, &m->tm_lm, &m->tm_x, lm_max, rows->lm_count, c.vocab_size, H, el, s), s);
+  el.index_offset = c.lm_offset;
+  rc = note(m, NE_K_LM_HEAD, run_gemm(m, &m->tm_lm, &m->tm_x, lm_max, rows->lm_count, c.lm_rows, H, el, s), s);
   if (rc) return rc;
+  if (tp) {  // the vocabulary is split: the largest key over the ranks is the argmax
+    rc = note(m, NE_K_COLLECTIVE, ne::tp_allreduce_max_u64(m->keys, (size_t)lm_max, m->tp_comm, s), s);
+    if (rc) return rc;
+  }
   if (argmax_out) rc = note(m, NE_K_OTHER, ne::launch_keys_to_ids(m->keys, rows->lm_count, lm_max, argmax_out, s), s);
   return rc;
 }
@@ -458,6 +509,7 @@ namespace {
 // and sampled entries alike.
 int sampled_tail(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int k,
                  const ne_rows& rows, bool spec, const ne_step_outputs* out, cudaStream_t s) {
+  if (m->tp_world > 1) return NE_ERR_UNSUPPORTED;
   int rc = ne_forward(m, &rows, NE_LM_LOGITS, m->sample_logits, nullptr, s);
   if (rc) return rc;
   rc = note(m, NE_K_SAMPLE,
@@ -625,7 +677,7 @@ int ne_paged_attention(const void* q, void* out, const void* k_cache, const void
 
 int ne_rmsnorm(const void* x, const void* w, void* y, int rows, int hidden, float eps, void* stream) {
   if (!x || !w || !y || rows < 0) return NE_ERR_INVALID;
-  return ne::launch_rmsnorm(static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),
+  return ne::launch_rmsnorm(static_cast<__nv_bfloat16*>(const_cast<void*>(x)), static_cast<const __nv_bfloat16*>(w),
                             static_cast<__nv_bfloat16*>(y), rows, nullptr, nullptr, hidden, eps, nullptr,
                             as_stream(stream));
 }

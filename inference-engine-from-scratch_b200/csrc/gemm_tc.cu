@@ -179,6 +179,14 @@ __device__ void epilogue_rows(const Epilogue& e, int tile_n, int m_begin, int co
         }
       }
     }
+  } else if (MODE == EPI_STORE_F32) {
+    // unit = 4 consecutive fp32 outputs of one row (16 bytes)
+    const int units = count * (GEMM_BM / 4);
+    for (int u = tid; u < units; u += GEMM_THREADS) {
+      const int m = u >> 5, c = (u & 31) * 4;
+      const float4 a = lds_f4(acc_s + (uint32_t)((m * GEMM_BM + c) * 4));
+      *reinterpret_cast<float4*>(e.out_f32 + (long long)(m_begin + m) * e.ldo + n0 + c) = a;
+    }
   } else if (MODE == EPI_SWIGLU) {
     // unit = 8 consecutive features j of one row: gate rows j, up rows 64 + j of the tile
     const int units = count * 8;
@@ -310,7 +318,7 @@ __device__ void epilogue_rows(const Epilogue& e, int tile_n, int m_begin, int co
       unsigned long long best = 0;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const unsigned long long key = argmax_key(y[i], (uint32_t)(n0 + 4 * lane + i));
+        const unsigned long long key = argmax_key(y[i], (uint32_t)(e.index_offset + n0 + 4 * lane + i));
         best = key > best ? key : best;
       }
       best = warp_max_u64(best);
@@ -758,6 +766,7 @@ int active_clusters(int mode, bool w8, int splits, int smem) {
     case EPI_QKV: return active_clusters_mode<EPI_QKV, false>(splits, smem);
     case EPI_ARGMAX: return active_clusters_mode<EPI_ARGMAX, false>(splits, smem);
     case EPI_LOGITS: return active_clusters_mode<EPI_LOGITS, false>(splits, smem);
+    case EPI_STORE_F32: return active_clusters_mode<EPI_STORE_F32, false>(splits, smem);
     default: return 0;
   }
 }
@@ -904,6 +913,7 @@ int gemm_launch(const CUtensorMap* tm_w, const CUtensorMap* tm_x, const GemmPara
       case EPI_QKV: err = launch_mode<EPI_QKV, false>(cfg, tm_w, tm_x, p); break;
       case EPI_ARGMAX: err = launch_mode<EPI_ARGMAX, false>(cfg, tm_w, tm_x, p); break;
       case EPI_LOGITS: err = launch_mode<EPI_LOGITS, false>(cfg, tm_w, tm_x, p); break;
+      case EPI_STORE_F32: err = launch_mode<EPI_STORE_F32, false>(cfg, tm_w, tm_x, p); break;
       default: return NE_ERR_INVALID;
     }
   }

@@ -41,6 +41,7 @@ enum EpilogueMode : int {
   EPI_QKV = 3,       // q/k RMSNorm + RoPE, q -> q_out, k/v -> paged KV cache at slot_mapping
   EPI_ARGMAX = 4,    // per-row max over the vocab tile into a 64-bit atomicMax key
   EPI_LOGITS = 5,    // out[m, n] = bf16(y) (vocab row width) plus the argmax key
+  EPI_STORE_F32 = 6, // out_f32[m, n] = y (fp32 partial sums of a row-parallel shard, for an all-reduce)
 };
 
 struct Epilogue {
@@ -69,6 +70,9 @@ struct Epilogue {
   long long num_cache_slots;      // slots + 1 (the scratch slot included)
   // EPI_ARGMAX / EPI_LOGITS
   unsigned long long* argmax_keys;  // [M]
+  int index_offset;                 // vocabulary id of the tile's first row (LM-head shard offset)
+  // EPI_STORE_F32
+  float* out_f32;
 };
 
 struct GemmParams {

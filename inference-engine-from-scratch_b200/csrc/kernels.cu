@@ -34,20 +34,29 @@ __global__ void embed_kernel(const __nv_bfloat16* __restrict__ embed, const int3
 
 // ------------------------------------------------------------------ RMSNorm (models/qwen3.py:39-44)
 // fp32 mean of squares, x * rsqrt(var + eps) cast back to bf16, then times the bf16 weight.
-__global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+__global__ void rmsnorm_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                                __nv_bfloat16* __restrict__ y, int max_rows, const int32_t* rows_dev,
-                               const int32_t* gather, int hidden, float eps, unsigned long long* zero_keys) {
+                               const int32_t* gather, int hidden, float eps, unsigned long long* zero_keys,
+                               const float* __restrict__ add) {
   pdl_prologue();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int n = rows_dev ? min(*rows_dev, max_rows) : max_rows;
   if (row >= n) return;
   const int src = gather ? gather[row] : row;
-  const uint4* xr = reinterpret_cast<const uint4*>(x + (long long)src * hidden);
+  uint4* xr = reinterpret_cast<uint4*>(x + (long long)src * hidden);
   float ss = 0.f;
   for (int i = lane; i < hidden / 8; i += 32) {
     uint4 u = xr[i];
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
+    __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&u);
+    if (add) {  // residual update first: x = bf16(x + bf16(add)) (the all-reduced projection)
+      const float4* ar = reinterpret_cast<const float4*>(add + (long long)src * hidden + i * 8);
+      const float4 a0 = ar[0], a1 = ar[1];
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) e[j] = __float2bfloat16_rn(__bfloat162float(e[j]) + bf16r(av[j]));
+      xr[i] = u;
+    }
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       float f = __bfloat162float(e[j]);
@@ -412,14 +421,14 @@ int launch_embed(const __nv_bfloat16* embed, const int32_t* tokens, const int32_
                        vocab, out, status) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 
-int launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int max_rows,
+int launch_rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int max_rows,
                    const int32_t* rows_dev, const int32_t* gather, int hidden, float eps,
-                   unsigned long long* zero_keys, cudaStream_t stream) {
+                   unsigned long long* zero_keys, cudaStream_t stream, const float* add) {
   if (hidden % 256) return NE_ERR_INVALID;
   const int blocks = (max_rows + 3) / 4;
   if (blocks == 0) return NE_OK;
   return launch_kernel(rmsnorm_kernel, dim3(blocks), dim3(128), 0, stream, x, w, y, max_rows, rows_dev, gather, hidden,
-                       eps, zero_keys) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
+                       eps, zero_keys, add) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 
 int launch_keys_to_ids(const unsigned long long* keys, const int32_t* count, int max_count, int32_t* ids,

@@ -23,9 +23,11 @@ struct RowBuffers {
 
 int launch_embed(const __nv_bfloat16* embed, const int32_t* tokens, const int32_t* num_rows, int max_rows, int hidden,
                  int vocab, __nv_bfloat16* out, int* status, cudaStream_t stream);
-int launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int max_rows,
+// ``add`` (fp32 [rows, hidden], may be NULL): first x[src] = bf16(x[src] + bf16(add[src])) in place (the
+// residual update after a tensor-parallel all-reduce), then the norm of the updated row.
+int launch_rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int max_rows,
                    const int32_t* rows_dev, const int32_t* gather, int hidden, float eps,
-                   unsigned long long* zero_keys, cudaStream_t stream);
+                   unsigned long long* zero_keys, cudaStream_t stream, const float* add = nullptr);
 int launch_keys_to_ids(const unsigned long long* keys, const int32_t* count, int max_count, int32_t* ids,
                        cudaStream_t stream);
 int launch_ngram(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int k, int max_ngram,

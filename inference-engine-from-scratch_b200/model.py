@@ -68,7 +68,12 @@ class B200Model:
         max_rows: int = 4096,
         max_seqs: int = 256,
         weight_int8: bool = False,
+        tp=None,
+        lm_offset: int = 0,
     ) -> None:
+        """``tp`` (tp.TensorParallel): this process is one rank of a split model; ``cfg`` is then the
+        rank's shape (tp.rank_config), ``weights`` its shard (tp.shard_weights / make_sharded_weights)
+        and ``lm_offset`` the first vocabulary id of its LM-head rows."""
         self.lib = _lib.load()
         self.cfg = cfg
         self.device = torch.device(device)
@@ -123,7 +128,12 @@ class B200Model:
             self.layers.append(entry)
         self.embed = put(weights["model.embed_tokens.weight"])
         head = weights.get("lm_head.weight")
-        self.lm_head = self.embed if (cfg.tie_word_embeddings or head is None) else put(head)
+        if tp is not None and head is None:
+            raise ValueError("a tensor-parallel rank needs its LM-head shard (lm_head.weight)")
+        tied = head is None or (cfg.tie_word_embeddings and tp is None)
+        self.lm_head = self.embed if tied else put(head)
+        self.tp = tp
+        self.lm_offset = lm_offset
         self.final_norm = put(weights["model.norm.weight"])
         cos, sin = rope_tables(max_positions, d, cfg.rope_theta)
         self.rope_cos, self.rope_sin = cos.to(dev), sin.to(dev)
@@ -137,10 +147,15 @@ class B200Model:
             num_layers=L, num_heads=cfg.num_attention_heads, num_kv_heads=nkv, head_dim=d,
             rms_norm_eps=cfg.rms_norm_eps, block_size=16, kv_int8=int(kv_int8), weight_int8=int(weight_int8),
             num_cache_slots=num_slots + 1, max_positions=max_positions,
+            lm_rows=0 if tp is None else self.lm_head.shape[0], lm_offset=0 if tp is None else lm_offset,
         )
         handle = ctypes.c_void_p()
         _lib.check(self.lib.ne_model_create(ctypes.byref(config), ctypes.byref(handle)), "ne_model_create")
         self.handle = handle
+        if tp is not None and tp.world > 1:
+            uid = ctypes.create_string_buffer(tp.unique_id, 128)
+            _lib.check(self.lib.ne_model_set_tp(handle, tp.nccl_library.encode(), tp.rank, tp.world, uid),
+                       "ne_model_set_tp")
         self._layer_structs = []
         for layer, w in enumerate(self.layers):
             lw = _lib.LayerWeights(
