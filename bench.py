@@ -69,6 +69,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--profile-step", action="store_true",
                    help="prefill, then two eager speculative steps and exit (a short target for ncu)")
+    p.add_argument("--profile-users", type=int, default=0,
+                   help="with --profile-step: serve this many users instead of the workload's (small ncu captures)")
     return p.parse_args()
 
 
@@ -347,6 +349,9 @@ class Workload:
                 "users_per_gpu": 256, "k": 4, "parallelism": f"dp{args.gpus} (independent replicas)",
                 "l2": "no flush: every step streams 1.19 GB of weights + ~35 GB of KV (> 126 MB L2)"}
         self.sampled = self.temperature > 0.0
+        if args.profile_step and args.profile_users:
+            self.users = min(self.users, args.profile_users)
+            self.prompts = self.prompts[: self.users]
 
 
 # ---------------------------------------------------------------------------- B200 arm

@@ -812,6 +812,22 @@ int gemm_plan(GemmParams& p, int num_sms) {
 }
 
 namespace {
+// Upper bounds on the split-K cluster size and the pipeline depth: GEMM_MAX_SPLITS /
+// GEMM_MAX_STAGES, or NE_GEMM_MAX_SPLITS / NE_GEMM_MAX_STAGES (1..8) when set (tuning knobs).
+int env_cap(const char* name, int dflt) {
+  const char* v = getenv(name);
+  const int n = v ? atoi(v) : dflt;
+  return n >= 1 && n <= dflt ? n : dflt;
+}
+int max_splits() {
+  static const int cap = env_cap("NE_GEMM_MAX_SPLITS", GEMM_MAX_SPLITS);
+  return cap;
+}
+int max_stages() {
+  static const int cap = env_cap("NE_GEMM_MAX_STAGES", GEMM_MAX_STAGES);
+  return cap;
+}
+
 int plan_uncached(GemmParams& p, int num_sms) {
   if (p.N % GEMM_BM || p.K % GEMM_BK || p.M_max <= 0) return NE_ERR_INVALID;
   if (p.w_scale && (p.epi.mode == EPI_ARGMAX || p.epi.mode == EPI_LOGITS)) return NE_ERR_UNSUPPORTED;
@@ -823,7 +839,7 @@ int plan_uncached(GemmParams& p, int num_sms) {
   // a verify step's row count is a device value well below its bound: size split-K for the first
   // m-block (a later one that gets rows is a second wave); prefill-sized steps split by m-blocks
   const int par = n_tiles * (p.M_max > 512 ? m_blocks : 1);
-  int S = std::max(1, std::min(GEMM_MAX_SPLITS, num_sms / std::max(1, par)));
+  int S = std::max(1, std::min(max_splits(), num_sms / std::max(1, par)));
   if (p.epi.mode == EPI_ARGMAX || p.epi.mode == EPI_LOGITS) S = 1;
   auto staging_bytes = [&](int s, int tb) {
     if (s == 1) return 128 * GEMM_BM * 4 + 2 * GEMM_MAX_TOKENS * 4;  // accumulator block + epilogue scratch
@@ -841,7 +857,7 @@ int plan_uncached(GemmParams& p, int num_sms) {
   const int stage_bytes = GEMM_BM * GEMM_BK * 2 + ((t_block + GEMM_XBOX - 1) / GEMM_XBOX) * GEMM_XBOX * GEMM_BK * 2 +
                           (p.w_scale ? GEMM_W8_TILE_BYTES : 0);
   const int cps = (num_chunks + S - 1) / S;
-  int stages = std::min(std::min(GEMM_MAX_STAGES, cps), avail / stage_bytes);
+  int stages = std::min(std::min(max_stages(), cps), avail / stage_bytes);
   if (stages < 1) return NE_ERR_INVALID;
   const int staging = staging_bytes(S, t_block);
   int data = std::max(stages * stage_bytes, staging);
