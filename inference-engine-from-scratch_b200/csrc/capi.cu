@@ -40,6 +40,8 @@ struct ne_model {
   void* tp_comm = nullptr;
   int tp_rank = 0, tp_world = 1;
   float* partial = nullptr;  // fp32 [max_rows, H]: row-parallel projection outputs, all-reduced
+  float* ssq = nullptr;      // fp32 [max_rows, H / 128]: residual rows' sums of squares per 128-wide tile
+  CUtensorMap tm_h{};        // the residual rows as a GEMM X operand (RMSNorm fused into the GEMM)
   CUtensorMap tm_x{}, tm_attn{}, tm_act{};
   int num_sms = 148;
   // launch accounting / profiling
@@ -66,7 +68,7 @@ size_t sampling_logits_bytes(const ne_model_config& c, int rows) {
 }  // split-KV partials (few sequences, long contexts)
 
 struct Layout {
-  size_t status, h, x, q, attn, act, keys, rows_i32, seqs_i32, scalars, attn_scratch, partial, total;
+  size_t status, h, x, q, attn, act, keys, rows_i32, seqs_i32, scalars, attn_scratch, partial, ssq, total;
 };
 
 Layout workspace_layout(const ne_model_config& c, int R, int B, int tp_world) {
@@ -90,6 +92,7 @@ Layout workspace_layout(const ne_model_config& c, int R, int B, int tp_world) {
   l.scalars = take(64);                   // num_rows, lm_count
   l.attn_scratch = take(ATTN_SCRATCH_BYTES);
   l.partial = tp_world > 1 ? take((size_t)R * c.hidden_size * 4) : 0;
+  l.ssq = take((size_t)R * (c.hidden_size / 128) * 4);
   l.total = off;
   return l;
 }
@@ -115,16 +118,37 @@ int note(ne_model* m, int kind, int rc, cudaStream_t stream) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// RMSNorm folded into the following GEMMs when NE_FUSED_NORM=1 (converter warps normalise the X
+// tiles in shared memory). Off by default: measured on B200 at 64 users it is slower than the
+// separate RMSNorm launch (2.13 vs 2.02 ms per step): the conversion sits on every GEMM's
+// critical path, while in a CUDA graph with programmatic launch the RMSNorm launch mostly overlaps.
+bool fused_norm_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("NE_FUSED_NORM");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
+
 int sm_count() {
   int dev = 0, n = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   return n;
 }
 
+// ``x_norm_w`` (may be NULL): X is the residual stream h and RMSNorm with this weight is applied to
+// it inside the GEMM (statistics from m->ssq).
 int run_gemm(ne_model* m, const CUtensorMap* tw, const CUtensorMap* tx, int M_max, const int32_t* M_dev, int N, int K,
-             const ne::Epilogue& epi, cudaStream_t stream, const void* w_scale = nullptr) {
+             const ne::Epilogue& epi, cudaStream_t stream, const void* w_scale = nullptr,
+             const void* x_norm_w = nullptr) {
   GemmParams p{};
   p.w_scale = static_cast<const __nv_bfloat16*>(w_scale);
+  if (x_norm_w) {
+    p.x_norm_w = static_cast<const __nv_bfloat16*>(x_norm_w);
+    p.x_ssq = m->ssq;
+    p.ssq_tiles = m->cfg.hidden_size / 128;
+    p.x_eps = m->cfg.rms_norm_eps;
+  }
   p.M_max = M_max;
   p.M_dev = M_dev;
   p.N = N;
@@ -293,8 +317,10 @@ int ne_model_set_workspace(ne_model* m, void* ws, size_t bytes, int max_rows, in
   m->attn_scratch = base + l.attn_scratch;
   m->attn_scratch_bytes = ATTN_SCRATCH_BYTES;
   m->partial = m->tp_world > 1 ? reinterpret_cast<float*>(base + l.partial) : nullptr;
+  m->ssq = reinterpret_cast<float*>(base + l.ssq);
   const int qs = c.num_heads * 128;
   bool ok = ne::make_tmap_bf16(&m->tm_x, m->x, max_rows, c.hidden_size, ne::GEMM_XBOX, ne::GEMM_BK) &&
+            ne::make_tmap_bf16(&m->tm_h, m->h, max_rows, c.hidden_size, ne::GEMM_XBOX, ne::GEMM_BK) &&
             ne::make_tmap_bf16(&m->tm_attn, m->attn, max_rows, qs, ne::GEMM_XBOX, ne::GEMM_BK) &&
             ne::make_tmap_bf16(&m->tm_act, m->act, max_rows, c.intermediate_size, ne::GEMM_XBOX, ne::GEMM_BK);
   if (!ok) return NE_ERR_INVALID;
@@ -333,11 +359,15 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
   if (lm_mode == NE_LM_LOGITS && !logits) return NE_ERR_INVALID;
   const bool tp = m->tp_world > 1;
   if (tp && lm_mode == NE_LM_LOGITS) return NE_ERR_UNSUPPORTED;  // logits are split over the ranks
+  // RMSNorm folded into the QKV and gate/up GEMMs (statistics from the producing epilogue); a
+  // split model adds the all-reduced projections in the RMSNorm launch instead
+  const bool fuse = !tp && fused_norm_enabled();
   cudaStream_t s = as_stream(stream);
   const int H = c.hidden_size, I = c.intermediate_size, qs = c.num_heads * 128, kvs = c.num_kv_heads * 128;
   const __nv_bfloat16* embed = static_cast<const __nv_bfloat16*>(m->head.embed);
   int rc = note(m, NE_K_EMBED,
-                ne::launch_embed(embed, rows->token_ids, rows->num_rows, R, H, c.vocab_size, m->h, m->status, s), s);
+                ne::launch_embed(embed, rows->token_ids, rows->num_rows, R, H, c.vocab_size, m->h, m->status, s,
+                                 fuse ? m->ssq : nullptr), s);
   if (rc) return rc;
   const int group = c.num_heads / c.num_kv_heads;
   const int max_vec = std::max(1, rows->max_q_len) * group;
@@ -348,10 +378,12 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
   for (int l = 0; l < c.num_layers; ++l) {
     const ne_layer_weights& w = m->layers[l];
     // (tensor parallel: the previous layer's all-reduced down_proj output joins the residual here)
-    rc = note(m, NE_K_RMSNORM,
-              ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(w.ln_in), m->x, R, rows->num_rows, nullptr,
-                                 H, c.rms_norm_eps, nullptr, s, tp && l > 0 ? m->partial : nullptr), s);
-    if (rc) return rc;
+    if (!fuse) {
+      rc = note(m, NE_K_RMSNORM,
+                ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(w.ln_in), m->x, R, rows->num_rows, nullptr,
+                                   H, c.rms_norm_eps, nullptr, s, tp && l > 0 ? m->partial : nullptr), s);
+      if (rc) return rc;
+    }
     ne::Epilogue e{};
     e.mode = ne::EPI_QKV;
     e.status = m->status;
@@ -372,7 +404,8 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
     e.v_scale = static_cast<__nv_bfloat16*>(w.v_scale);
     e.kv_int8 = c.kv_int8;
     e.num_cache_slots = c.num_cache_slots;
-    rc = note(m, NE_K_GEMM_QKV, run_gemm(m, &m->tm_qkv[l], &m->tm_x, R, rows->num_rows, qs + 2 * kvs, H, e, s, w.w_qkv_scale), s);
+    rc = note(m, NE_K_GEMM_QKV, run_gemm(m, &m->tm_qkv[l], fuse ? &m->tm_h : &m->tm_x, R, rows->num_rows, qs + 2 * kvs, H,
+                                         e, s, w.w_qkv_scale, fuse ? w.ln_in : nullptr), s);
     if (rc) return rc;
     rc = note(m, NE_K_ATTENTION,
               ne::launch_attention_tc(m->q, m->attn, w.k_cache, w.v_cache,
@@ -386,22 +419,27 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
     eo.out = m->h;
     eo.out_f32 = m->partial;
     eo.ldo = H;
+    eo.ssq_out = fuse ? m->ssq : nullptr;
+    eo.ssq_tiles = H / 128;
     rc = note(m, NE_K_GEMM_O, run_gemm(m, &m->tm_o[l], &m->tm_attn, R, rows->num_rows, H, qs, eo, s, w.w_o_scale), s);
     if (rc) return rc;
     if (tp) {
       rc = note(m, NE_K_COLLECTIVE, ne::tp_allreduce_sum_f32(m->partial, (size_t)R * H, m->tp_comm, s), s);
       if (rc) return rc;
     }
-    rc = note(m, NE_K_RMSNORM,
-              ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(w.ln_post), m->x, R, rows->num_rows, nullptr,
-                                 H, c.rms_norm_eps, nullptr, s, tp ? m->partial : nullptr), s);
-    if (rc) return rc;
+    if (!fuse) {
+      rc = note(m, NE_K_RMSNORM,
+                ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(w.ln_post), m->x, R, rows->num_rows,
+                                   nullptr, H, c.rms_norm_eps, nullptr, s, tp ? m->partial : nullptr), s);
+      if (rc) return rc;
+    }
     ne::Epilogue eg{};
     eg.mode = ne::EPI_SWIGLU;
     eg.status = m->status;
     eg.out = m->act;
     eg.ldo = I;
-    rc = note(m, NE_K_GEMM_GATEUP, run_gemm(m, &m->tm_gateup[l], &m->tm_x, R, rows->num_rows, 2 * I, H, eg, s, w.w_gateup_scale), s);
+    rc = note(m, NE_K_GEMM_GATEUP, run_gemm(m, &m->tm_gateup[l], fuse ? &m->tm_h : &m->tm_x, R, rows->num_rows, 2 * I,
+                                            H, eg, s, w.w_gateup_scale, fuse ? w.ln_post : nullptr), s);
     if (rc) return rc;
     ne::Epilogue ed{};
     ed.mode = tp ? ne::EPI_STORE_F32 : ne::EPI_RESIDUAL;
@@ -409,6 +447,8 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
     ed.out = m->h;
     ed.out_f32 = m->partial;
     ed.ldo = H;
+    ed.ssq_out = fuse ? m->ssq : nullptr;
+    ed.ssq_tiles = H / 128;
     rc = note(m, NE_K_GEMM_DOWN, run_gemm(m, &m->tm_down[l], &m->tm_act, R, rows->num_rows, H, I, ed, s, w.w_down_scale), s);
     if (rc) return rc;
     if (tp) {

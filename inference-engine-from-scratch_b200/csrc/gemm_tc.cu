@@ -175,7 +175,23 @@ __device__ void epilogue_rows(const Epilogue& e, int tile_n, int m_begin, int co
 #pragma unroll
             for (int i = 0; i < 8; ++i) o[i] = v[j][i];
           }
-          *reinterpret_cast<uint4*>(e.out + (long long)(m_begin + m) * e.ldo + n0 + c) = pack8_bf16(o);
+          const uint4 packed = pack8_bf16(o);
+          *reinterpret_cast<uint4*>(e.out + (long long)(m_begin + m) * e.ldo + n0 + c) = packed;
+          if (MODE == EPI_RESIDUAL && e.ssq_out) {
+            // sum of squares of the row's 128 new (bf16) values: 8 here, then the 16 threads of
+            // the half-warp that hold the row (fixed tree: deterministic)
+            float h2[8];
+            unpack8_bf16(packed, h2);
+            float sq = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sq += h2[i] * h2[i];
+            const unsigned half = 0xFFFFu << (lane & 16);
+            sq += __shfl_xor_sync(half, sq, 8);
+            sq += __shfl_xor_sync(half, sq, 4);
+            sq += __shfl_xor_sync(half, sq, 2);
+            sq += __shfl_xor_sync(half, sq, 1);
+            if ((tid & 15) == 0) e.ssq_out[(long long)(m_begin + m) * e.ssq_tiles + tile_n] = sq;
+          }
         }
       }
     }
@@ -360,10 +376,32 @@ __device__ __forceinline__ void w8_convert_row(uint32_t src_tile, uint32_t dst_t
   }
 }
 
-template <int MODE, bool W8>
+// Fused RMSNorm of the X operand: 8 consecutive K elements of one token row of a stage's X tile
+// (64-row TMA boxes, 128-byte swizzle), in place: bf16(bf16(h * rstd) * w) pairwise; h * rstd is
+// rounded to fp32 then to bf16 as torch rounds x.float() * rsqrt(...) and .to(bf16), and the weight
+// product is one bf16x2 multiply (one rounding of the exact product, as torch's bf16 multiply).
+__device__ __forceinline__ void nx_convert_chunk(uint32_t addr, float rstd, uint4 w) {
+  uint32_t v[4];
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]) : "r"(addr));
+  const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float lo = __uint_as_float(v[i] << 16) * rstd, hi = __uint_as_float(v[i] & 0xFFFF0000u) * rstd;
+    uint32_t packed, r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(packed) : "f"(hi), "f"(lo));
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(packed), "r"(wv[i]));
+    v[i] = r;
+  }
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3])
+               : "memory");
+}
+
+template <int MODE, int CONV>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                    const GemmParams p) {
+  constexpr bool W8 = (CONV & CONV_W8) != 0;
+  constexpr bool NX = (CONV & CONV_NX) != 0;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -393,8 +431,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint64_t* empty = full + stages;
   uint64_t* done = empty + stages;
   uint64_t* recv_bar = done + 1;  // split-K: peers' partial slices landed in our receive area
-  uint64_t* conv = recv_bar + 1;  // W8: the stage's bf16 operand tile is built (4 converter warps)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(conv + (W8 ? stages : 0));
+  uint64_t* conv = recv_bar + 1;  // W8 / NX: the stage's operand tiles are converted (4 converter warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(conv + (CONV ? stages : 0));
+  float* rstd_s = reinterpret_cast<float*>(smem + p.smem_data + 256);  // NX: per-token 1 / rms
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* consumed_slot = const_cast<int*>(reinterpret_cast<volatile int*>(tmem_slot + 2));
   volatile int* done_ok = reinterpret_cast<volatile int*>(tmem_slot + 3);  // broadcast flags (barrier area)
@@ -411,7 +450,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     mbar_init(done, 1);
     mbar_init(recv_bar, 1);
-    if (W8)
+    if (CONV)
       for (int s = 0; s < stages; ++s) mbar_init(&conv[s], 4);
     *abort_flag = 0;
     *consumed_slot = 0;
@@ -508,7 +547,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const int s = i % stages;
         const uint32_t round = (uint32_t)(i / stages);
         if (!mbar_wait(&full[s], round & 1u, abort_flag, p.status)) break;
-        if (W8 && !mbar_wait(&conv[s], round & 1u, abort_flag, p.status)) break;
+        if (CONV && !mbar_wait(&conv[s], round & 1u, abort_flag, p.status)) break;
         tc_fence_after();
         const uint32_t a_addr = smem_u32(smem + s * stage_bytes);
         const uint32_t b_addr = a_addr + w_bytes;
@@ -526,19 +565,41 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_commit(done);
     }
     __syncwarp();
-  } else if (W8 && warp >= 4) {
-    // converters: thread c builds weight row c of every stage's bf16 operand tile. The TMA of a
-    // stage is issued only after the MMA released the stage, so once ``full`` fires the bf16
-    // tile is free as well.
-    const int row = tid - 128;
-    const uint16_t sbits = __bfloat16_as_ushort(p.w_scale[(size_t)tile_n * GEMM_BM + row]);
-    const uint32_t scale2 = (uint32_t)sbits | ((uint32_t)sbits << 16);
+  } else if (CONV && warp >= 4) {
+    // converters (128 threads). W8: thread c builds weight row c of every stage's bf16 operand
+    // tile. NX: the stage's X rows are normalised in place. The TMA of a stage is issued only
+    // after the MMA released the stage, so once ``full`` fires the whole stage is ours.
+    const int c = tid - 128;
+    uint32_t scale2 = 0;
+    if (W8) {
+      const uint16_t sbits = __bfloat16_as_ushort(p.w_scale[(size_t)tile_n * GEMM_BM + c]);
+      scale2 = (uint32_t)sbits | ((uint32_t)sbits << 16);
+    }
+    if (NX) {  // 1 / rms of this CTA's tokens from the producer's per-tile sums of squares
+      for (int r = c; r < t_actual; r += 128) {
+        const float* q = p.x_ssq + (size_t)(m0 + r) * p.ssq_tiles;
+        float ss = 0.f;
+        for (int t = 0; t < p.ssq_tiles; ++t) ss += q[t];
+        rstd_s[r] = 1.0f / sqrtf(ss / (float)p.K + p.x_eps);
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // converter warps only
+    }
+    const int units = t_actual * 8;  // NX: (row, 16-byte chunk) pairs of a stage's X tile
     for (int i = 0; i < nk; ++i) {
       const int s = i % stages;
       const uint32_t round = (uint32_t)(i / stages);
       if (!mbar_wait(&full[s], round & 1u, abort_flag, p.status)) break;
       const uint32_t st = smem_u32(smem + s * stage_bytes);
-      w8_convert_row(st + (uint32_t)w_dst_off, st, row, scale2);
+      if (W8) w8_convert_row(st + (uint32_t)w_dst_off, st, c, scale2);
+      if (NX) {
+        const uint32_t xs = st + (uint32_t)w_bytes;
+        const uint4* wk = reinterpret_cast<const uint4*>(p.x_norm_w + (size_t)(k_begin + i) * GEMM_BK);
+        for (int u = c; u < units; u += 128) {
+          const int row = u >> 3, j = u & 7, r64 = row & 63;
+          const uint32_t addr = xs + (uint32_t)((row >> 6) * GEMM_XBOX * GEMM_BK * 2 + r64 * 128 + ((j ^ (r64 & 7)) << 4));
+          nx_convert_chunk(addr, rstd_s[row], __ldg(wk + j));
+        }
+      }
       fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
       __syncwarp();
       if (lane == 0) mbar_arrive(&conv[s]);
@@ -705,31 +766,31 @@ bool make_tmap_w8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t co
   return r == CUDA_SUCCESS;
 }
 
-template <int MODE, bool W8>
+template <int MODE, int CONV>
 cudaError_t prepare_mode() {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_tc_kernel<MODE, W8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    attr_err = cudaFuncSetAttribute(gemm_tc_kernel<MODE, CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     GEMM_SMEM_BYTES);
     if (attr_err == cudaSuccess)
-      attr_err = cudaFuncSetAttribute(gemm_tc_kernel<MODE, W8>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      attr_err = cudaFuncSetAttribute(gemm_tc_kernel<MODE, CONV>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   });
   return attr_err;
 }
 
-template <int MODE, bool W8>
+template <int MODE, int CONV>
 cudaError_t launch_mode(const cudaLaunchConfig_t& cfg, const CUtensorMap* tm_w, const CUtensorMap* tm_x,
                         const GemmParams& p) {
-  cudaError_t err = prepare_mode<MODE, W8>();
+  cudaError_t err = prepare_mode<MODE, CONV>();
   if (err != cudaSuccess) return err;
-  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<MODE, W8>, *tm_w, *tm_x, p);
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<MODE, CONV>, *tm_w, *tm_x, p);
 }
 
 // Clusters of ``splits`` CTAs with ``smem`` bytes each that the GPU holds at once (0 on error).
-template <int MODE, bool W8>
+template <int MODE, int CONV>
 int active_clusters_mode(int splits, int smem) {
-  if (prepare_mode<MODE, W8>() != cudaSuccess) return 0;
+  if (prepare_mode<MODE, CONV>() != cudaSuccess) return 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(splits, 1, 1);
   cfg.blockDim = dim3(GEMM_THREADS);
@@ -742,41 +803,36 @@ int active_clusters_mode(int splits, int smem) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int clusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tc_kernel<MODE, W8>, &cfg) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveClusters(&clusters, gemm_tc_kernel<MODE, CONV>, &cfg) != cudaSuccess) {
     cudaGetLastError();
     return 0;
   }
   return clusters;
 }
 
-int active_clusters(int mode, bool w8, int splits, int smem) {
-  if (w8) {
-    switch (mode) {
-      case EPI_STORE: return active_clusters_mode<EPI_STORE, true>(splits, smem);
-      case EPI_RESIDUAL: return active_clusters_mode<EPI_RESIDUAL, true>(splits, smem);
-      case EPI_SWIGLU: return active_clusters_mode<EPI_SWIGLU, true>(splits, smem);
-      case EPI_QKV: return active_clusters_mode<EPI_QKV, true>(splits, smem);
-      default: return 0;
-    }
-  }
-  switch (mode) {
-    case EPI_STORE: return active_clusters_mode<EPI_STORE, false>(splits, smem);
-    case EPI_RESIDUAL: return active_clusters_mode<EPI_RESIDUAL, false>(splits, smem);
-    case EPI_SWIGLU: return active_clusters_mode<EPI_SWIGLU, false>(splits, smem);
-    case EPI_QKV: return active_clusters_mode<EPI_QKV, false>(splits, smem);
-    case EPI_ARGMAX: return active_clusters_mode<EPI_ARGMAX, false>(splits, smem);
-    case EPI_LOGITS: return active_clusters_mode<EPI_LOGITS, false>(splits, smem);
-    case EPI_STORE_F32: return active_clusters_mode<EPI_STORE_F32, false>(splits, smem);
-    default: return 0;
-  }
+// The (epilogue, conversion) pairs the forward uses: conversions only on the layer projections.
+#define NE_GEMM_VARIANTS(X)                                                                        \
+  X(EPI_STORE, 0) X(EPI_STORE, CONV_W8) X(EPI_RESIDUAL, 0) X(EPI_RESIDUAL, CONV_W8) X(EPI_SWIGLU, 0)   \
+  X(EPI_SWIGLU, CONV_W8) X(EPI_SWIGLU, CONV_NX) X(EPI_SWIGLU, CONV_W8 | CONV_NX) X(EPI_QKV, 0)          \
+  X(EPI_QKV, CONV_W8) X(EPI_QKV, CONV_NX) X(EPI_QKV, CONV_W8 | CONV_NX) X(EPI_ARGMAX, 0) X(EPI_LOGITS, 0) \
+  X(EPI_STORE_F32, 0)
+
+int conv_bits(const GemmParams& p) { return (p.w_scale ? CONV_W8 : 0) | (p.x_norm_w ? CONV_NX : 0); }
+
+int active_clusters(int mode, int conv, int splits, int smem) {
+#define NE_CASE(M, C) \
+  if (mode == M && conv == (C)) return active_clusters_mode<M, C>(splits, smem);
+  NE_GEMM_VARIANTS(NE_CASE)
+#undef NE_CASE
+  return 0;
 }
 
 // Choose tokens per CTA, split-K (cluster size) and pipeline depth for an [M_max, K] x [N, K]^T GEMM.
 namespace {
 struct PlanKey {
-  int M, N, K, mode, w8, sms;
+  int M, N, K, mode, conv, sms;
   bool operator<(const PlanKey& o) const {
-    return std::tie(M, N, K, mode, w8, sms) < std::tie(o.M, o.N, o.K, o.mode, o.w8, o.sms);
+    return std::tie(M, N, K, mode, conv, sms) < std::tie(o.M, o.N, o.K, o.mode, o.conv, o.sms);
   }
 };
 struct PlanVal {
@@ -791,7 +847,7 @@ int plan_with_occupancy(GemmParams& p, int num_sms);
 
 // Cached per (rows, N, K, epilogue, SMs); the first plan of a shape queries cluster occupancy.
 int gemm_plan(GemmParams& p, int num_sms) {
-  const PlanKey key{p.M_max, p.N, p.K, p.epi.mode, p.w_scale != nullptr, num_sms};
+  const PlanKey key{p.M_max, p.N, p.K, p.epi.mode, conv_bits(p), num_sms};
   {
     std::lock_guard<std::mutex> lock(g_plan_mutex);
     auto it = g_plans.find(key);
@@ -830,7 +886,11 @@ int max_stages() {
 
 int plan_uncached(GemmParams& p, int num_sms) {
   if (p.N % GEMM_BM || p.K % GEMM_BK || p.M_max <= 0) return NE_ERR_INVALID;
-  if (p.w_scale && (p.epi.mode == EPI_ARGMAX || p.epi.mode == EPI_LOGITS)) return NE_ERR_UNSUPPORTED;
+  if ((p.w_scale && p.epi.mode != EPI_STORE && p.epi.mode != EPI_RESIDUAL && p.epi.mode != EPI_SWIGLU &&
+       p.epi.mode != EPI_QKV) ||
+      (p.x_norm_w && p.epi.mode != EPI_SWIGLU && p.epi.mode != EPI_QKV) ||
+      (p.x_norm_w && (!p.x_ssq || p.ssq_tiles <= 0)))
+    return NE_ERR_UNSUPPORTED;
   const int num_chunks = p.K / GEMM_BK;
   const int n_tiles = p.N / GEMM_BM;
   const int avail = GEMM_SMEM_DATA_BYTES;
@@ -867,7 +927,7 @@ int plan_uncached(GemmParams& p, int num_sms) {
   const int tmem_cols = t_block <= 32 ? 32 : t_block <= 64 ? 64 : t_block <= 128 ? 128 : t_block <= 256 ? 256 : 512;
   const int max_ctas = 512 / tmem_cols;
   const int min_total = 228 * 1024 / (max_ctas + 1) + 1024;
-  data = std::max(data, min_total - 1280);
+  data = std::max(data, min_total - 1280 - GEMM_RSTD_BYTES);
   if (data > avail) return NE_ERR_INVALID;
   p.t_block = t_block;
   p.splits = S;
@@ -884,7 +944,7 @@ int plan_with_occupancy(GemmParams& p, int num_sms) {
   const int m_blocks = (p.M_max + p.t_block - 1) / p.t_block;
   const int par = n_tiles * (p.M_max > 512 ? m_blocks : 1);
   while (p.splits > 1) {
-    const int fit = active_clusters(p.epi.mode, p.w_scale != nullptr, p.splits, p.smem_data + 256 + 1024);
+    const int fit = active_clusters(p.epi.mode, conv_bits(p), p.splits, p.smem_data + 256 + GEMM_RSTD_BYTES + 1024);
     if (fit >= par) break;
     const int want = p.splits - 1;
     GemmParams q = p;
@@ -901,7 +961,7 @@ int gemm_launch(const CUtensorMap* tm_w, const CUtensorMap* tm_x, const GemmPara
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.splits, p.N / GEMM_BM, (p.M_max + p.t_block - 1) / p.t_block);
   cfg.blockDim = dim3(GEMM_THREADS);
-  cfg.dynamicSmemBytes = p.smem_data + 256 + 1024;
+  cfg.dynamicSmemBytes = p.smem_data + 256 + GEMM_RSTD_BYTES + 1024;
   cfg.stream = stream;
   cudaLaunchAttribute attrs[2];
   attrs[0].id = cudaLaunchAttributeClusterDimension;
@@ -912,27 +972,17 @@ int gemm_launch(const CUtensorMap* tm_w, const CUtensorMap* tm_x, const GemmPara
   attrs[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  cudaError_t err;
-  if (p.w_scale) {
-    switch (p.epi.mode) {
-      case EPI_STORE: err = launch_mode<EPI_STORE, true>(cfg, tm_w, tm_x, p); break;
-      case EPI_RESIDUAL: err = launch_mode<EPI_RESIDUAL, true>(cfg, tm_w, tm_x, p); break;
-      case EPI_SWIGLU: err = launch_mode<EPI_SWIGLU, true>(cfg, tm_w, tm_x, p); break;
-      case EPI_QKV: err = launch_mode<EPI_QKV, true>(cfg, tm_w, tm_x, p); break;
-      default: return NE_ERR_UNSUPPORTED;
-    }
-  } else {
-    switch (p.epi.mode) {
-      case EPI_STORE: err = launch_mode<EPI_STORE, false>(cfg, tm_w, tm_x, p); break;
-      case EPI_RESIDUAL: err = launch_mode<EPI_RESIDUAL, false>(cfg, tm_w, tm_x, p); break;
-      case EPI_SWIGLU: err = launch_mode<EPI_SWIGLU, false>(cfg, tm_w, tm_x, p); break;
-      case EPI_QKV: err = launch_mode<EPI_QKV, false>(cfg, tm_w, tm_x, p); break;
-      case EPI_ARGMAX: err = launch_mode<EPI_ARGMAX, false>(cfg, tm_w, tm_x, p); break;
-      case EPI_LOGITS: err = launch_mode<EPI_LOGITS, false>(cfg, tm_w, tm_x, p); break;
-      case EPI_STORE_F32: err = launch_mode<EPI_STORE_F32, false>(cfg, tm_w, tm_x, p); break;
-      default: return NE_ERR_INVALID;
-    }
+  cudaError_t err = cudaErrorInvalidValue;
+  const int conv = conv_bits(p);
+  bool found = false;
+#define NE_CASE(M, C)                                      \
+  if (!found && p.epi.mode == M && conv == (C)) {           \
+    err = launch_mode<M, C>(cfg, tm_w, tm_x, p);            \
+    found = true;                                          \
   }
+  NE_GEMM_VARIANTS(NE_CASE)
+#undef NE_CASE
+  if (!found) return NE_ERR_UNSUPPORTED;
   return err == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 

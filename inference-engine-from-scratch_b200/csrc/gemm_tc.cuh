@@ -28,9 +28,11 @@ constexpr int GEMM_XBOX = 64;        // token rows per X TMA box
 constexpr int GEMM_THREADS = 256;  // warps 0-3 run TMA / MMA / TMEM roles, all 8 run the epilogue
 constexpr int GEMM_MAX_TOKENS = 512; // tokens per CTA (TMEM columns)
 constexpr int GEMM_SMEM_BYTES = 227 * 1024;
-// data region (pipeline stages, later the epilogue staging); then 256 B of barriers; the rest is
-// the slack that aligns the dynamic shared memory base to 1024 B
-constexpr int GEMM_SMEM_DATA_BYTES = GEMM_SMEM_BYTES - 1024 - 256;
+// data region (pipeline stages, later the epilogue staging); then 256 B of barriers and the
+// per-token RMSNorm scales of a normalised X operand; the rest is the slack that aligns the
+// dynamic shared memory base to 1024 B
+constexpr int GEMM_RSTD_BYTES = GEMM_MAX_TOKENS * 4;
+constexpr int GEMM_SMEM_DATA_BYTES = GEMM_SMEM_BYTES - 1024 - 256 - GEMM_RSTD_BYTES;
 constexpr int GEMM_MAX_STAGES = 8;
 constexpr int GEMM_MAX_SPLITS = 8;   // portable cluster size
 
@@ -73,7 +75,14 @@ struct Epilogue {
   int index_offset;                 // vocabulary id of the tile's first row (LM-head shard offset)
   // EPI_STORE_F32
   float* out_f32;
+  // EPI_RESIDUAL: per (row, 128-wide output tile) fp32 sums of squares of the updated residual
+  // rows, [M, ssq_tiles] (the RMSNorm statistics the next GEMM's normalised X operand needs)
+  float* ssq_out;
+  int ssq_tiles;
 };
+
+// Operand conversions done in shared memory by the converter warps (4-7) between TMA and MMA.
+enum : int { CONV_W8 = 1, CONV_NX = 2 };
 
 struct GemmParams {
   int M_max;             // rows of the X tensor map / upper bound of M
@@ -87,6 +96,13 @@ struct GemmParams {
   // int8 weights (nullptr: bf16): W is int8 [N, K] with one bf16 scale per row, and the MMA
   // operand is bf16(q * scale), the reference's Int8Linear dequantisation, built in shared memory
   const __nv_bfloat16* w_scale;
+  // RMSNorm fused into the X operand (nullptr: X is used as loaded): X holds the residual rows h,
+  // and the MMA sees bf16(bf16(h * rstd) * x_norm_w) (models/qwen3.py:39-44 rounding points) with
+  // rstd = 1 / sqrt(sum(x_ssq[row, :ssq_tiles]) / K + x_eps)
+  const __nv_bfloat16* x_norm_w;
+  const float* x_ssq;
+  int ssq_tiles;
+  float x_eps;
   Epilogue epi;
 };
 

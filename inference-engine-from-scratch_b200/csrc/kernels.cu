@@ -16,7 +16,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 // ------------------------------------------------------------------ embedding (models/qwen3.py:167)
 __global__ void embed_kernel(const __nv_bfloat16* __restrict__ embed, const int32_t* __restrict__ tokens,
                              const int32_t* num_rows, int max_rows, int hidden, int vocab,
-                             __nv_bfloat16* __restrict__ out, int* status) {
+                             __nv_bfloat16* __restrict__ out, int* status, float* __restrict__ ssq) {
   pdl_prologue();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -29,7 +29,21 @@ __global__ void embed_kernel(const __nv_bfloat16* __restrict__ embed, const int3
   }
   const uint4* src = reinterpret_cast<const uint4*>(embed + (long long)tok * hidden);
   uint4* dst = reinterpret_cast<uint4*>(out + (long long)warp * hidden);
-  for (int i = lane; i < hidden / 8; i += 32) dst[i] = src[i];
+  for (int i = lane; i < hidden / 8; i += 32) {
+    const uint4 v = src[i];
+    dst[i] = v;
+    if (ssq) {  // sums of squares per 128-wide tile (16 chunks = one half-warp), for a fused RMSNorm
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+      float sq = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sq += __bfloat162float(e[j]) * __bfloat162float(e[j]);
+      sq += __shfl_xor_sync(0xFFFFFFFFu, sq, 8);
+      sq += __shfl_xor_sync(0xFFFFFFFFu, sq, 4);
+      sq += __shfl_xor_sync(0xFFFFFFFFu, sq, 2);
+      sq += __shfl_xor_sync(0xFFFFFFFFu, sq, 1);
+      if ((lane & 15) == 0) ssq[(long long)warp * (hidden / 128) + i / 16] = sq;
+    }
+  }
 }
 
 // ------------------------------------------------------------------ RMSNorm (models/qwen3.py:39-44)
@@ -412,13 +426,13 @@ int launch_share_blocks(const ne_batch_state& st, int src_slot, const int32_t* d
 }
 
 int launch_embed(const __nv_bfloat16* embed, const int32_t* tokens, const int32_t* num_rows, int max_rows, int hidden,
-                 int vocab, __nv_bfloat16* out, int* status, cudaStream_t stream) {
-  if (hidden % 8) return NE_ERR_INVALID;
+                 int vocab, __nv_bfloat16* out, int* status, cudaStream_t stream, float* ssq) {
+  if (hidden % 256) return NE_ERR_INVALID;
   const int threads = 128;
   const int blocks = (max_rows * 32 + threads - 1) / threads;
   if (blocks == 0) return NE_OK;
   return launch_kernel(embed_kernel, dim3(blocks), dim3(threads), 0, stream, embed, tokens, num_rows, max_rows, hidden,
-                       vocab, out, status) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
+                       vocab, out, status, ssq) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 
 int launch_rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int max_rows,

@@ -21,8 +21,9 @@ struct RowBuffers {
   int32_t* draft_len;     // [max_seqs]
 };
 
+// ``ssq`` (may be NULL): per (row, 128-wide tile) fp32 sums of squares of the embedded rows.
 int launch_embed(const __nv_bfloat16* embed, const int32_t* tokens, const int32_t* num_rows, int max_rows, int hidden,
-                 int vocab, __nv_bfloat16* out, int* status, cudaStream_t stream);
+                 int vocab, __nv_bfloat16* out, int* status, cudaStream_t stream, float* ssq = nullptr);
 // ``add`` (fp32 [rows, hidden], may be NULL): first x[src] = bf16(x[src] + bf16(add[src])) in place (the
 // residual update after a tensor-parallel all-reduce), then the norm of the updated row.
 int launch_rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int max_rows,

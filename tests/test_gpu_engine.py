@@ -184,3 +184,20 @@ def test_verify_with_full_length_drafts_matches_the_oracle(small) -> None:
             seq.num_cached_tokens = seq.num_tokens + keep
             seq.token_ids.extend(new_tokens)
         assert mine.token_ids == ref.token_ids
+
+
+def test_fused_rmsnorm_path_serves_the_reference_outputs() -> None:
+    """NE_FUSED_NORM=1 (RMSNorm folded into the QKV and gate/up GEMMs' X operand) in a fresh
+    process: the serial drop-in and continuous batching still reproduce the reference fixtures."""
+    import os
+    import subprocess
+    import sys
+
+    from tests.conftest import REPO
+
+    env = dict(os.environ, NE_FUSED_NORM="1")
+    proc = subprocess.run(
+        [sys.executable, "-m", "pytest", "-q", "-x", "-p", "no:cacheprovider", "tests/test_gpu_engine.py",
+         "-k", "serial_drop_in or continuous_batching or int8_engine"],
+        cwd=REPO, env=env, capture_output=True, text=True, timeout=900)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-2000:]
