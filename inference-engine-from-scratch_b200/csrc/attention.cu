@@ -112,6 +112,66 @@ __device__ __forceinline__ void stage_block(const Ctx& c, long long blk, uint32_
   }
 }
 
+// int8 pool, per-warp path: issue one block's raw K and V rows (16 tokens x 128 int8 each) into
+// smem at raw (K) and raw + 2048 (V) with cp.async (lane-strided 16-byte chunks).
+__device__ __forceinline__ void stage_raw_int8(const Ctx& c, long long blk, uint32_t raw, int lane) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int i = lane + 32 * j, tok = i >> 3, ch = i & 7;
+    const long long off = ((blk * 16 + tok) * c.nkv + c.h) * D + ch * 16;
+    cp_async16(raw + tok * 128 + ch * 16, reinterpret_cast<const int8_t*>(c.kc) + off);
+    cp_async16(raw + 2048 + tok * 128 + ch * 16, reinterpret_cast<const int8_t*>(c.vc) + off);
+  }
+}
+// The block's bf16 scales, one per lane: lanes 0-15 the K scale of token lane, 16-31 the V scale of
+// token lane - 16 (plain loads, issued a block ahead of their use).
+__device__ __forceinline__ uint32_t load_scales_int8(const Ctx& c, long long blk, int lane) {
+  const long long slot = blk * 16 + (lane & 15);
+  const __nv_bfloat16* src = lane < 16 ? c.ks : c.vs;
+  return (uint32_t)__bfloat16_as_ushort(src[slot * c.nkv + c.h]);
+}
+// bf16(q * scale) for a pair of int8 values in the low 16 bits of ``word`` (selector 0x4140) or
+// the high 16 bits (0x4342): q exact in bf16 from byte magic, then one bf16x2 multiply (the
+// rounding of read_from_cache's int8.to(bf16) * scale).
+__device__ __forceinline__ uint32_t dq_pair(uint32_t word, uint32_t sel, uint32_t scale2) {
+  const uint32_t p = __byte_perm(word, 0x43434343u, sel);
+  const uint32_t v = p & 0x437F437Fu, b = p & 0x43804380u;
+  uint32_t q, r;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(v), "r"(b));
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(q), "r"(scale2));
+  return r;
+}
+// Raw int8 block (staged by stage_raw_int8) -> bf16 K / V blocks in the padded row layout.
+__device__ __forceinline__ void convert_raw_int8(uint32_t raw, uint32_t k_s, uint32_t v_s, uint32_t scales,
+                                                 int lane) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int i = lane + 32 * j, tok = i >> 3, ch = i & 7;
+    const uint32_t ks = __shfl_sync(0xFFFFFFFFu, scales, tok), vs = __shfl_sync(0xFFFFFFFFu, scales, 16 + tok);
+    const uint32_t ks2 = ks | (ks << 16), vs2 = vs | (vs << 16);
+#pragma unroll
+    for (int kv = 0; kv < 2; ++kv) {
+      uint32_t w[4];
+      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
+                   : "r"(raw + kv * 2048 + tok * 128 + ch * 16));
+      const uint32_t s2 = kv ? vs2 : ks2;
+      uint32_t o[8];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        o[2 * t] = dq_pair(w[t], 0x4140u, s2);
+        o[2 * t + 1] = dq_pair(w[t], 0x4342u, s2);
+      }
+      const uint32_t dst = (kv ? v_s : k_s) + tok * ROW_BYTES + ch * 32;
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3])
+                   : "memory");
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst + 16), "r"(o[4]), "r"(o[5]), "r"(o[6]),
+                   "r"(o[7])
+                   : "memory");
+    }
+  }
+}
+
 // Valid block id of logical block ``kb`` or -1 (reported) when the table names no pool block.
 __device__ __forceinline__ long long block_id(const Ctx& c, int kb, int stride) {
   long long blk = kb < stride ? c.table[kb] : -1;
@@ -267,8 +327,125 @@ __device__ __forceinline__ void tile_store(const Ctx& c, const AttnSplit& sp, co
   }
 }
 
+// One or two query tiles (the speculative step): warp w serves query tile w % NT and every
+// (4 / NT)-th block of the split from its own double buffer (bf16: two K/V stages; int8: two raw
+// stages + one converted K/V pair); the warps of a tile merge (max, sum, O) through smem at the end.
+template <bool INT8, int NT>
+__device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& rows, const AttnSplit& sp, int b, int h,
+                                                 int split, int kb0, int kb1, uint8_t* q_s, int* spos, uint8_t* buf,
+                                                 __nv_bfloat16* out, int nh, int nkv) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t buf_u = smem_u32(buf);
+  const int per_tile = 4 / NT, my_tile = warp % NT, phase = warp / NT;
+  const uint32_t wbuf = buf_u + warp * 4 * BLOCK_BYTES;
+  int kb = kb0 + phase;
+  long long blk = kb < kb1 ? block_id(c, kb, rows.block_table_stride) : -1;
+  uint32_t scales = 0;
+  // each warp's first K/V block goes out before the query tiles (they do not depend on it)
+  if (blk >= 0) {
+    if (INT8) {
+      stage_raw_int8(c, blk, wbuf, lane);
+      scales = load_scales_int8(c, blk, lane);
+    } else {
+      stage_block<INT8>(c, blk, wbuf, wbuf + BLOCK_BYTES, lane, 32);
+    }
+  }
+  cp_commit();
+  if (tid < 32) spos[tid] = tid < c.nvec ? rows.positions[c.r0 + tid / c.G] : -1;
+  TileState ts;
+  for (int t = 0; t < NT; ++t) {  // one Q staging area: tile t's warps take their fragments in turn
+    if (t > 0) __syncthreads();
+    load_q_tile(c, 16 * t, q_s, tid, THREADS);
+    __syncthreads();
+    if (my_tile == t) tile_init(ts, smem_u32(q_s), spos + 16 * t, lane);
+  }
+  int stage = 0;
+  for (; kb < kb1; kb += per_tile) {
+    const int nkb = kb + per_tile;
+    long long nblk_id = nkb < kb1 ? block_id(c, nkb, rows.block_table_stride) : -1;
+    uint32_t next_scales = 0;
+    if (INT8) {
+      const uint32_t nraw = wbuf + (stage ^ 1) * 4096;
+      if (nblk_id >= 0) {
+        stage_raw_int8(c, nblk_id, nraw, lane);
+        next_scales = load_scales_int8(c, nblk_id, lane);
+      }
+      cp_commit();
+      cp_wait<1>();
+      __syncwarp();
+      const uint32_t kv = wbuf + 8192;  // converted K, V
+      if (blk >= 0) {
+        convert_raw_int8(wbuf + stage * 4096, kv, kv + BLOCK_BYTES, scales, lane);
+        __syncwarp();
+        tile_block(ts, kv, kv + BLOCK_BYTES, kb, lane);
+      }
+      __syncwarp();
+      scales = next_scales;
+    } else {
+      const uint32_t nxt = wbuf + (stage ^ 1) * 2 * BLOCK_BYTES;
+      if (nblk_id >= 0) stage_block<INT8>(c, nblk_id, nxt, nxt + BLOCK_BYTES, lane, 32);
+      cp_commit();
+      cp_wait<1>();
+      __syncwarp();
+      const uint32_t cur = wbuf + stage * 2 * BLOCK_BYTES;
+      if (blk >= 0) tile_block(ts, cur, cur + BLOCK_BYTES, kb, lane);
+      __syncwarp();
+    }
+    blk = nblk_id;
+    stage ^= 1;
+  }
+  cp_wait<0>();
+  // merge the warps of each tile through smem (reusing the stage buffers)
+  __syncthreads();
+  float* mo = reinterpret_cast<float*>(buf);          // [4][16][128]
+  float* mm = mo + 4 * 16 * D;                        // [4][16]
+  float* ml = mm + 4 * 16;                            // [4][16]
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = (lane >> 2) + 8 * r;
+    if (my_tile * 16 + row >= c.nvec) continue;  // padding rows of the tile are never read
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      const int d = 8 * t + 2 * (lane & 3);
+      *reinterpret_cast<float2*>(&mo[(warp * 16 + row) * D + d]) = make_float2(ts.o[t][2 * r], ts.o[t][2 * r + 1]);
+    }
+    if ((lane & 3) == 0) {
+      mm[warp * 16 + row] = ts.m[r];
+      ml[warp * 16 + row] = ts.l[r];
+    }
+  }
+  __syncthreads();
+  for (int v = 0; v < min(16 * NT, c.nvec); ++v) {
+    const int t = v >> 4, row = v & 15;
+    float m = NEG_INF;
+    for (int i = 0; i < per_tile; ++i) m = fmaxf(m, mm[(t + NT * i) * 16 + row]);
+    float l = 0.f, o = 0.f;
+    if (m != NEG_INF) {
+      for (int i = 0; i < per_tile; ++i) {
+        const int w = t + NT * i;
+        const float mw = mm[w * 16 + row];
+        const float f = mw == NEG_INF ? 0.f : exp2f(mw - m);
+        l += ml[w * 16 + row] * f;
+        o += mo[(w * 16 + row) * D + tid] * f;
+      }
+    }
+    if (sp.splits == 1) {
+      const int orow = c.r0 + v / c.G;
+      const int head = c.h * c.G + v % c.G;
+      out[((long long)orow * nh + head) * D + tid] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
+    } else {
+      const long long base = (((long long)b * nkv + h) * sp.splits + split) * sp.max_vec + v;
+      sp.part_o[base * D + tid] = o;
+      if (tid == 0) {
+        sp.part_m[base] = m;
+        sp.part_l[base] = l;
+      }
+    }
+  }
+}
+
 template <bool INT8>
-__global__ void __launch_bounds__(THREADS)
+__global__ void __launch_bounds__(THREADS, 3)  // three CTAs per SM (registers <= 168)
     attention_kernel(const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out, const void* __restrict__ kc,
                      const void* __restrict__ vc, const __nv_bfloat16* __restrict__ ks,
                      const __nv_bfloat16* __restrict__ vs, ne_rows rows, int nh, int nkv, long long num_cache_slots,
@@ -307,81 +484,9 @@ __global__ void __launch_bounds__(THREADS)
   const uint32_t buf_u = smem_u32(buf);
 
   if (ntiles == 1) {
-    // ---------------------------------------------------------------- one tile, warps split blocks
-    // each warp's first K/V block goes out before the query tile (they do not depend on it)
-    const uint32_t wbuf = buf_u + warp * 4 * BLOCK_BYTES;  // [stage][K,V]
-    int kb = kb0 + warp;
-    long long blk = kb < kb1 ? block_id(c, kb, rows.block_table_stride) : -1;
-    if (blk >= 0) stage_block<INT8>(c, blk, wbuf, wbuf + BLOCK_BYTES, lane, 32);
-    cp_commit();
-    load_q_tile(c, 0, q_s, tid, THREADS);
-    if (tid < 16) spos[tid] = tid < c.nvec ? rows.positions[c.r0 + tid / c.G] : -1;
-    __syncthreads();
-    TileState ts;
-    tile_init(ts, smem_u32(q_s), spos, lane);
-    int stage = 0;
-    for (; kb < kb1; kb += 4) {
-      const int nkb = kb + 4;
-      long long nblk_id = nkb < kb1 ? block_id(c, nkb, rows.block_table_stride) : -1;
-      const uint32_t nxt = wbuf + (stage ^ 1) * 2 * BLOCK_BYTES;
-      if (nblk_id >= 0) stage_block<INT8>(c, nblk_id, nxt, nxt + BLOCK_BYTES, lane, 32);
-      cp_commit();
-      cp_wait<1>();
-      __syncwarp();
-      const uint32_t cur = wbuf + stage * 2 * BLOCK_BYTES;
-      if (blk >= 0) tile_block(ts, cur, cur + BLOCK_BYTES, kb, lane);
-      __syncwarp();
-      blk = nblk_id;
-      stage ^= 1;
-    }
-    cp_wait<0>();
-    // merge the four warps through smem (reusing the stage buffers)
-    __syncthreads();
-    float* mo = reinterpret_cast<float*>(buf);          // [4][16][128]
-    float* mm = mo + 4 * 16 * D;                        // [4][16]
-    float* ml = mm + 4 * 16;                            // [4][16]
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const int row = (lane >> 2) + 8 * r;
-      if (row >= c.nvec) continue;  // padding rows of the tile are never read
-#pragma unroll
-      for (int t = 0; t < 16; ++t) {
-        const int d = 8 * t + 2 * (lane & 3);
-        *reinterpret_cast<float2*>(&mo[(warp * 16 + row) * D + d]) = make_float2(ts.o[t][2 * r], ts.o[t][2 * r + 1]);
-      }
-      if ((lane & 3) == 0) {
-        mm[warp * 16 + row] = ts.m[r];
-        ml[warp * 16 + row] = ts.l[r];
-      }
-    }
-    __syncthreads();
-    for (int v = 0; v < min(16, c.nvec); ++v) {
-      float m = NEG_INF;
-#pragma unroll
-      for (int w = 0; w < 4; ++w) m = fmaxf(m, mm[w * 16 + v]);
-      float l = 0.f, o = 0.f;
-      if (m != NEG_INF) {
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          const float mw = mm[w * 16 + v];
-          const float f = mw == NEG_INF ? 0.f : exp2f(mw - m);
-          l += ml[w * 16 + v] * f;
-          o += mo[(w * 16 + v) * D + tid] * f;
-        }
-      }
-      if (sp.splits == 1) {
-        const int row = c.r0 + v / c.G;
-        const int head = c.h * c.G + v % c.G;
-        out[((long long)row * nh + head) * D + tid] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
-      } else {
-        const long long base = (((long long)b * nkv + h) * sp.splits + split) * sp.max_vec + v;
-        sp.part_o[base * D + tid] = o;
-        if (tid == 0) {
-          sp.part_m[base] = m;
-          sp.part_l[base] = l;
-        }
-      }
-    }
+    warp_split_tiles<INT8, 1>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv);
+  } else if (ntiles == 2) {
+    warp_split_tiles<INT8, 2>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv);
   } else {
     // ---------------------------------------------------------------- many tiles, shared blocks
     for (int t0 = 0; t0 < ntiles; t0 += 4) {
@@ -479,13 +584,22 @@ size_t attention_smem_bytes() {
 }
 
 int attention_plan_splits(int num_seqs, int nkv, int max_context, int max_vec, int num_sms, size_t partial_bytes) {
+  // Enough CTAs to fill the SMs twice over (three CTAs fit an SM), but no split shorter than 8
+  // blocks (128 tokens) of the longest context the launch allows.
+  static const int cap = [] {  // NE_ATTN_MAX_SPLITS (tuning knob): upper bound on the splits
+    const char* v = getenv("NE_ATTN_MAX_SPLITS");
+    const int n = v ? atoi(v) : 32;
+    return n >= 1 && n <= 32 ? n : 32;
+  }();
   const int pairs = num_seqs * nkv;
-  int splits = (2 * num_sms + pairs - 1) / pairs;
+  int splits = (2 * 3 * num_sms + pairs - 1) / pairs;
   const int max_blocks = (max_context + 15) / 16;
+  const int by_length = max_blocks / 8;
+  splits = splits > by_length ? by_length : splits;
+  splits = splits > cap ? cap : splits;
   splits = splits < 1 ? 1 : splits;
-  splits = splits > max_blocks ? max_blocks : splits;
   splits = splits > 32 ? 32 : splits;
-  if (splits > 1 && max_vec > 16) splits = 1;  // split-KV only for the one-tile (speculative) case
+  if (splits > 1 && max_vec > 32) splits = 1;  // split-KV for the one- or two-tile (speculative) case
   // the partials must fit the scratch area the caller gave
   while (splits > 1 && (size_t)pairs * splits * max_vec * (D + 2) * sizeof(float) > partial_bytes) --splits;
   return splits;

@@ -61,7 +61,7 @@ namespace {
 
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-constexpr size_t ATTN_SCRATCH_BYTES = 16u << 20;
+constexpr size_t ATTN_SCRATCH_BYTES = 64u << 20;
 
 size_t sampling_logits_bytes(const ne_model_config& c, int rows) {
   return align256((size_t)rows * c.vocab_size * 2);

@@ -158,6 +158,9 @@ ATTENTION_CASES = [
     (32, 8, [5], [700], 8),
     (4, 2, [64], [64], 0),
     (16, 8, [40, 3], [40, 130], 0),
+    # two query tiles per KV head (k = 8 drafts, G = 2): warp-split path, with and without split-KV
+    (16, 8, [9, 3, 9], [700, 40, 300], 8),
+    (16, 8, [9, 7], [1100, 160], 0),
 ]
 
 
