@@ -60,7 +60,9 @@ __device__ __forceinline__ float scaled(const __nv_bfloat16* row, int i, float T
   return __bfloat162float(row[i]) / T;  // logits.float() / temperature
 }
 __device__ __forceinline__ float prob(float y, float m, float z) { return expf(y - m) / z; }
-__device__ __forceinline__ unsigned long long to_fix(float p) { return __double2ull_rn((double)p * FIX_ONE); }
+// 2^60 fixed point: p * 2^60 is exact in fp32 (a power-of-two scale), so a float-to-u64 conversion
+// rounds exactly as the conversion of the same value in fp64 would.
+__device__ __forceinline__ unsigned long long to_fix(float p) { return __float2ull_rn(p * 1152921504606846976.0f); }
 
 // Target probability after top-p (0 if cut) given the tie rank of a token whose p == tau.
 __device__ __forceinline__ float kept_p(float p, const SampleStats& s, int tie_rank) {
@@ -256,6 +258,137 @@ __device__ SampleStats row_stats(const __nv_bfloat16* row, int vocab, float T, f
   return s;
 }
 
+// ---------------------------------------------------------------- statistics from a logit histogram
+// p depends on a token only through its bf16 logit, so one pass that counts the 65,536 possible
+// bf16 values (16-bit counters, two per word, 128 KB of shared memory) gives the softmax and the
+// top-p cut without touching the row again: m from the largest value present, z = sum over
+// values of count * exp(x / T - m), and the cut from a descending scan of count * p in fixed point.
+// Values whose probabilities are equal in fp32 (p is monotone in the value, so they are adjacent)
+// form one tie group, as the per-token test p == tau in the acceptance sees them. A value held by
+// more than 65,535 tokens would overflow its counter: the caller then falls back to row_stats.
+constexpr int HIST_WORDS = 32768;  // 65,536 16-bit counters
+constexpr int HIST_KEYS_PER_THREAD = 65536 / THREADS;
+
+__device__ __forceinline__ uint32_t order_key(uint32_t b) { return (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u); }
+__device__ __forceinline__ float key_value(uint32_t key) {
+  const uint32_t b = (key & 0x8000u) ? (key & 0x7FFFu) : (~key & 0xFFFFu);
+  return __uint_as_float(b << 16);
+}
+__device__ __forceinline__ uint32_t key_count(const uint32_t* hist, uint32_t key) {
+  return (hist[key >> 1] >> ((key & 1u) * 16)) & 0xFFFFu;
+}
+
+template <typename V, typename Op>
+__device__ V block_reduce(V v, V* sh, Op op) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(FULL, v, o));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  V r = sh[0];
+  for (int w = 1; w < WARPS; ++w) r = op(r, sh[w]);  // fixed order: the same result in every thread
+  __syncthreads();
+  return r;
+}
+
+// Returns false (and nothing else) when a counter overflowed.
+__device__ bool row_stats_hist(const __nv_bfloat16* row, int vocab, float T, float top_p, uint32_t* hist,
+                               SampleStats& s) {
+  __shared__ unsigned long long sh64[WARPS];
+  __shared__ float shf[WARPS];
+  __shared__ int shi[WARPS];
+  __shared__ int overflow;
+  for (int i = threadIdx.x; i < HIST_WORDS; i += THREADS) hist[i] = 0u;
+  if (threadIdx.x == 0) overflow = 0;
+  __syncthreads();
+  const uint16_t* bits = reinterpret_cast<const uint16_t*>(row);
+  for (int i = threadIdx.x; i < vocab; i += THREADS) {
+    const uint32_t key = order_key(bits[i]);
+    const uint32_t shift = (key & 1u) * 16;
+    const uint32_t old = atomicAdd(hist + (key >> 1), 1u << shift);
+    if (((old >> shift) & 0xFFFFu) == 0xFFFFu) overflow = 1;
+  }
+  __syncthreads();
+  if (overflow) return false;
+  const uint32_t k0 = threadIdx.x * HIST_KEYS_PER_THREAD;
+  // m: the largest value present (over x / T)
+  int top = -1;
+  for (int k = HIST_KEYS_PER_THREAD - 1; k >= 0; --k)
+    if (key_count(hist, k0 + k)) {
+      top = (int)(k0 + k);
+      break;
+    }
+  top = block_reduce(top, shi, [](int a, int b) { return a > b ? a : b; });
+  const float m = key_value((uint32_t)top) / T;
+  float zp = 0.f;
+  for (int k = 0; k < HIST_KEYS_PER_THREAD; ++k) {
+    const uint32_t c = key_count(hist, k0 + k);
+    if (c) zp += (float)c * expf(key_value(k0 + k) / T - m);
+  }
+  const float z = block_reduce(zp, shf, [](float a, float b) { return a + b; });
+  s.m = m;
+  s.z = z;
+  s.tau = 0.f;
+  s.kept_sum = 1.f;
+  s.tie_keep = 0;
+  s.tie_count = 0;
+  s.top_p_active = 0;
+  s.sampled = 1;
+  if (!(top_p < 1.0f)) return true;
+  const unsigned long long limit = to_fix(top_p);
+  // mass above this thread's key range: an exclusive scan from the top
+  unsigned long long mine = 0;
+  for (int k = 0; k < HIST_KEYS_PER_THREAD; ++k) {
+    const uint32_t c = key_count(hist, k0 + k);
+    if (c) mine += (unsigned long long)c * to_fix(prob(key_value(k0 + k) / T, m, z));
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned long long incl = mine;  // inclusive suffix sum within the warp (higher lanes = higher keys)
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long t = __shfl_down_sync(FULL, incl, o);
+    if (lane + o < 32) incl += t;
+  }
+  if (lane == 0) sh64[warp] = incl;  // the warp's total
+  __syncthreads();
+  unsigned long long above = incl - mine;
+  for (int w = warp + 1; w < WARPS; ++w) above += sh64[w];
+  __syncthreads();
+  // the lowest key whose largest token still has mass-before < top_p
+  int cand = 0x7FFFFFFF;
+  unsigned long long acc = above;
+  for (int k = HIST_KEYS_PER_THREAD - 1; k >= 0 && acc < limit; --k) {
+    const uint32_t c = key_count(hist, k0 + k);
+    if (!c) continue;
+    cand = (int)(k0 + k);
+    acc += (unsigned long long)c * to_fix(prob(key_value(k0 + k) / T, m, z));
+  }
+  cand = block_reduce(cand, shi, [](int a, int b) { return a < b ? a : b; });
+  const float tau = prob(key_value((uint32_t)cand) / T, m, z);
+  // the tie group of tau and the mass of every larger probability
+  unsigned long long gt = 0, eq = 0;
+  for (int k = 0; k < HIST_KEYS_PER_THREAD; ++k) {
+    const uint32_t c = key_count(hist, k0 + k);
+    if (!c) continue;
+    const float p = prob(key_value(k0 + k) / T, m, z);
+    if (p > tau) gt += (unsigned long long)c * to_fix(p);
+    else if (p == tau) eq += c;
+  }
+  gt = block_reduce(gt, sh64, [](unsigned long long a, unsigned long long b) { return a + b; });
+  eq = block_reduce(eq, sh64, [](unsigned long long a, unsigned long long b) { return a + b; });
+  const unsigned long long step = to_fix(tau);
+  unsigned long long keep = eq;
+  if (gt >= limit) keep = 0;
+  else if (step > 0ull) keep = min(eq, (limit - gt - 1ull) / step + 1ull);
+  s.tau = tau;
+  s.tie_keep = (int)keep;
+  s.tie_count = (int)eq;
+  s.kept_sum = (float)((double)(gt + keep * step) / FIX_ONE);
+  s.top_p_active = 1;
+  return true;
+}
+
 // One CTA per lm row; rows of greedy sequences are skipped (their argmax keys decide).
 __global__ void __launch_bounds__(THREADS)
     sample_stats_kernel(ne_batch_state st, const int32_t* __restrict__ seq_slot, int num_seqs,
@@ -277,7 +410,10 @@ __global__ void __launch_bounds__(THREADS)
   if (s < 0 || (q_len && q_len[lo] <= 0) || lm_start[lo] > r) return;
   const float T = st.temperature[s];
   if (!(T > 0.f)) return;
-  const SampleStats out = row_stats(logits + (long long)r * vocab, vocab, T, st.top_p[s]);
+  extern __shared__ uint32_t hist_smem[];
+  const __nv_bfloat16* row = logits + (long long)r * vocab;
+  SampleStats out;
+  if (!row_stats_hist(row, vocab, T, st.top_p[s], hist_smem, out)) out = row_stats(row, vocab, T, st.top_p[s]);
   if (threadIdx.x == 0) stats[r] = out;
 }
 
@@ -286,7 +422,11 @@ __global__ void __launch_bounds__(THREADS)
                              const float* __restrict__ top_p, SampleStats* __restrict__ stats) {
   pdl_prologue();
   const int r = blockIdx.x;
-  const SampleStats out = row_stats(logits + (long long)r * vocab, vocab, temperature[r], top_p[r]);
+  extern __shared__ uint32_t hist_smem[];
+  const __nv_bfloat16* row = logits + (long long)r * vocab;
+  SampleStats out;
+  if (!row_stats_hist(row, vocab, temperature[r], top_p[r], hist_smem, out))
+    out = row_stats(row, vocab, temperature[r], top_p[r]);
   if (threadIdx.x == 0) stats[r] = out;
 }
 
@@ -592,11 +732,20 @@ __global__ void __launch_bounds__(THREADS)
 
 }  // namespace
 
+namespace {
+template <typename K>
+bool allow_hist_smem(K kernel) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, HIST_WORDS * 4) == cudaSuccess;
+}
+}  // namespace
+
 int launch_sample_stats(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, const int32_t* lm_start,
                         const int32_t* q_len, const int32_t* lm_count, int lm_max, const __nv_bfloat16* logits,
                         int vocab, SampleStats* stats, cudaStream_t stream) {
   if (lm_max <= 0 || num_seqs <= 0) return NE_OK;
-  return launch_kernel(sample_stats_kernel, dim3(lm_max), dim3(THREADS), 0, stream, st, seq_slot, num_seqs, lm_start,
+  static const bool attr = allow_hist_smem(sample_stats_kernel);
+  if (!attr) return NE_ERR_CUDA;
+  return launch_kernel(sample_stats_kernel, dim3(lm_max), dim3(THREADS), HIST_WORDS * 4, stream, st, seq_slot, num_seqs, lm_start,
                        q_len, lm_count, lm_max, logits, vocab, stats) == cudaSuccess
              ? NE_OK
              : NE_ERR_CUDA;
@@ -617,7 +766,9 @@ int launch_accept_sampled(const ne_batch_state& st, const int32_t* seq_slot, int
 int launch_sample_stats_rows(const __nv_bfloat16* logits, int rows, int vocab, const float* temperature,
                              const float* top_p, SampleStats* stats, cudaStream_t stream) {
   if (rows <= 0) return NE_OK;
-  return launch_kernel(sample_stats_rows_kernel, dim3(rows), dim3(THREADS), 0, stream, logits, vocab, temperature,
+  static const bool attr = allow_hist_smem(sample_stats_rows_kernel);
+  if (!attr) return NE_ERR_CUDA;
+  return launch_kernel(sample_stats_rows_kernel, dim3(rows), dim3(THREADS), HIST_WORDS * 4, stream, logits, vocab, temperature,
                        top_p, stats) == cudaSuccess
              ? NE_OK
              : NE_ERR_CUDA;
