@@ -172,6 +172,15 @@ __device__ __forceinline__ void convert_raw_int8(uint32_t raw, uint32_t k_s, uin
   }
 }
 
+// A block-table entry checked against the pool: the id, or -1 (reported) when it names no block.
+__device__ __forceinline__ long long checked_block(const Ctx& c, long long blk) {
+  if (blk < 0 || (blk + 1) * 16 > c.num_cache_slots - 1) {
+    report(c.status, NE_DEV_BAD_SLOT);
+    return -1;
+  }
+  return blk;
+}
+
 // Valid block id of logical block ``kb`` or -1 (reported) when the table names no pool block.
 __device__ __forceinline__ long long block_id(const Ctx& c, int kb, int stride) {
   long long blk = kb < stride ? c.table[kb] : -1;
@@ -338,8 +347,16 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
   const uint32_t buf_u = smem_u32(buf);
   const int per_tile = 4 / NT, my_tile = warp % NT, phase = warp / NT;
   const uint32_t wbuf = buf_u + warp * 4 * BLOCK_BYTES;
+  // the table entries of this warp's blocks (the j-th is logical block kb0 + phase + per_tile * j),
+  // 32 at a time in the lanes of a register: no dependent global load inside the block loop
+  const int stride = rows.block_table_stride;
+  auto table_chunk = [&](int j0) -> int {
+    const int kbj = kb0 + phase + per_tile * (j0 + lane);
+    return (kbj < kb1 && kbj < stride) ? c.table[kbj] : -1;
+  };
+  int tbl = table_chunk(0);
   int kb = kb0 + phase;
-  long long blk = kb < kb1 ? block_id(c, kb, rows.block_table_stride) : -1;
+  long long blk = kb < kb1 ? (kb < stride ? checked_block(c, __shfl_sync(0xFFFFFFFFu, tbl, 0)) : block_id(c, kb, stride)) : -1;
   uint32_t scales = 0;
   // each warp's first K/V block goes out before the query tiles (they do not depend on it)
   if (blk >= 0) {
@@ -360,9 +377,11 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
     if (my_tile == t) tile_init(ts, smem_u32(q_s), spos + 16 * t, lane);
   }
   int stage = 0;
-  for (; kb < kb1; kb += per_tile) {
+  for (int j = 0; kb < kb1; kb += per_tile, ++j) {
     const int nkb = kb + per_tile;
-    long long nblk_id = nkb < kb1 ? block_id(c, nkb, rows.block_table_stride) : -1;
+    if (((j + 1) & 31) == 0) tbl = table_chunk(j + 1);  // warp-uniform
+    const int nraw_id = __shfl_sync(0xFFFFFFFFu, tbl, (j + 1) & 31);
+    long long nblk_id = nkb < kb1 ? (nkb < stride ? checked_block(c, nraw_id) : block_id(c, nkb, stride)) : -1;
     uint32_t next_scales = 0;
     if (INT8) {
       const uint32_t nraw = wbuf + (stage ^ 1) * 4096;
