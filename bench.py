@@ -420,10 +420,16 @@ def run_b200(args, dist: Dist) -> None:
                                 seed=i, prefix=prefix) for i, p in enumerate(prompts)]
     engine.prefill(slots, chunk=wl.prefill_chunk)
     if args.profile_step:
-        for _ in range(2):
+        # two eager steps; print what each processed so that ncu byte counts can be scaled per unit
+        for i in range(2):
+            idx = torch.tensor(slots, device=device).long()
+            ctx_before = int(engine.state.seq_len[idx].sum().item())
             engine._set_slots(slots, len(slots))
             engine._launch_step(len(slots))
-            engine._collect(slots)
+            res = engine._collect(slots)
+            rows = len(slots) + res.proposed
+            print(json.dumps({"profile_step": i, "rows": rows, "attention_ctx_sum": ctx_before + res.proposed,
+                              "users": len(slots)}), flush=True)
         model.raise_on_device_error()
         model.close()
         return

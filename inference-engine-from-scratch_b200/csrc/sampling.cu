@@ -274,8 +274,11 @@ __device__ __forceinline__ float key_value(uint32_t key) {
   const uint32_t b = (key & 0x8000u) ? (key & 0x7FFFu) : (~key & 0xFFFFu);
   return __uint_as_float(b << 16);
 }
+// Counter word of a key: keys 64t .. 64t+63 (thread t's range in the key sweeps) stay in words
+// 32t .. 32t+31, XOR-swizzled by t so that the 32 lanes of a sweep step hit 32 different banks.
+__device__ __forceinline__ uint32_t key_word(uint32_t key) { return (key >> 1) ^ ((key >> 6) & 31u); }
 __device__ __forceinline__ uint32_t key_count(const uint32_t* hist, uint32_t key) {
-  return (hist[key >> 1] >> ((key & 1u) * 16)) & 0xFFFFu;
+  return (hist[key_word(key)] >> ((key & 1u) * 16)) & 0xFFFFu;
 }
 
 template <typename V, typename Op>
@@ -306,7 +309,7 @@ __device__ bool row_stats_hist(const __nv_bfloat16* row, int vocab, float T, flo
   for (int i = threadIdx.x; i < vocab; i += THREADS) {
     const uint32_t key = order_key(bits[i]);
     const uint32_t shift = (key & 1u) * 16;
-    const uint32_t old = atomicAdd(hist + (key >> 1), 1u << shift);
+    const uint32_t old = atomicAdd(hist + key_word(key), 1u << shift);
     if (((old >> shift) & 0xFFFFu) == 0xFFFFu) overflow = 1;
   }
   __syncthreads();
