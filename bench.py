@@ -485,7 +485,14 @@ def run_b200(args, dist: Dist) -> None:
     bytes_launch = algorithmic_bytes(dominant, cfg, M, ctx_sum, per_layer_kv, wb)
     peak, peak_src = measured_peak()
     achieved = bytes_launch / (avg_ms / 1000.0) / 1e9
-    traffic = ncu_traffic().get(dominant)
+    # DRAM bytes per launch from the committed ncu capture (attention scaled to this step's context)
+    t_rec = ncu_traffic().get(dominant)
+    traffic = None
+    if isinstance(t_rec, dict) and "dram_bytes" in t_rec:
+        traffic = float(t_rec["dram_bytes"])
+        if dominant == "attention" and t_rec.get("ctx_sum"):
+            traffic *= ctx_sum / float(t_rec["ctx_sum"])
+        traffic = int(traffic)
     roofline = {"bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_src,
                 "bytes_per_launch": int(bytes_launch), "avg_launch_ms": round(avg_ms, 5)}

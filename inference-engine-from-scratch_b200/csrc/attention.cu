@@ -603,15 +603,16 @@ size_t attention_smem_bytes() {
 }
 
 int attention_plan_splits(int num_seqs, int nkv, int max_context, int max_vec, int num_sms, size_t partial_bytes) {
-  // Enough CTAs to fill the SMs twice over (three CTAs fit an SM), but no split shorter than 8
-  // blocks (128 tokens) of the longest context the launch allows.
+  // About two CTAs per SM (a split-KV launch adds a partial reset and a combine kernel, which cost
+  // more than they save once the (entry, head) pairs alone fill the GPU), and no split shorter
+  // than 8 blocks (128 tokens) of the longest context the launch allows.
   static const int cap = [] {  // NE_ATTN_MAX_SPLITS (tuning knob): upper bound on the splits
     const char* v = getenv("NE_ATTN_MAX_SPLITS");
     const int n = v ? atoi(v) : 32;
     return n >= 1 && n <= 32 ? n : 32;
   }();
   const int pairs = num_seqs * nkv;
-  int splits = (2 * 3 * num_sms + pairs - 1) / pairs;
+  int splits = (2 * num_sms + pairs - 1) / pairs;
   const int max_blocks = (max_context + 15) / 16;
   const int by_length = max_blocks / 8;
   splits = splits > by_length ? by_length : splits;
