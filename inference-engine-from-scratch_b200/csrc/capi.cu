@@ -219,6 +219,8 @@ int ne_model_create(const ne_model_config* cfg, ne_model** out) {
       c.num_cache_slots < 2 || c.max_positions <= 0 || c.lm_rows < 0 || c.lm_rows % 128 || c.lm_offset < 0 ||
       c.lm_offset + c.lm_rows > c.vocab_size)
     return NE_ERR_INVALID;
+  const int chunks = c.hidden_size / 256;  // the RMSNorm kernel keeps a row in registers
+  if (chunks != 1 && chunks != 2 && chunks != 4 && chunks != 8 && chunks != 16) return NE_ERR_UNSUPPORTED;
   ne_model* m = new (std::nothrow) ne_model();
   if (!m) return NE_ERR_INVALID;
   m->cfg = c;

@@ -47,48 +47,59 @@ __global__ void embed_kernel(const __nv_bfloat16* __restrict__ embed, const int3
 }
 
 // ------------------------------------------------------------------ RMSNorm (models/qwen3.py:39-44)
-// fp32 mean of squares, x * rsqrt(var + eps) cast back to bf16, then times the bf16 weight.
+// fp32 mean of squares, x * rsqrt(var + eps) cast back to bf16, then times the bf16 weight. A warp
+// per row; the row stays in registers (CPL 16-byte chunks per lane, hidden = 256 * CPL), and the
+// weight is read before waiting for the previous kernel (it does not depend on it).
+template <int CPL>
 __global__ void rmsnorm_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                                __nv_bfloat16* __restrict__ y, int max_rows, const int32_t* rows_dev,
                                const int32_t* gather, int hidden, float eps, unsigned long long* zero_keys,
                                const float* __restrict__ add) {
-  pdl_prologue();
+  pdl_trigger();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  uint4 wv[CPL];
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) wv[j] = wr[lane + 32 * j];
+  pdl_wait();
   const int n = rows_dev ? min(*rows_dev, max_rows) : max_rows;
   if (row >= n) return;
   const int src = gather ? gather[row] : row;
   uint4* xr = reinterpret_cast<uint4*>(x + (long long)src * hidden);
+  uint4 u[CPL];
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) u[j] = xr[lane + 32 * j];
   float ss = 0.f;
-  for (int i = lane; i < hidden / 8; i += 32) {
-    uint4 u = xr[i];
-    __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&u);
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) {
+    __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&u[j]);
     if (add) {  // residual update first: x = bf16(x + bf16(add)) (the all-reduced projection)
-      const float4* ar = reinterpret_cast<const float4*>(add + (long long)src * hidden + i * 8);
+      const float4* ar = reinterpret_cast<const float4*>(add + (long long)src * hidden + (lane + 32 * j) * 8);
       const float4 a0 = ar[0], a1 = ar[1];
       const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-      for (int j = 0; j < 8; ++j) e[j] = __float2bfloat16_rn(__bfloat162float(e[j]) + bf16r(av[j]));
-      xr[i] = u;
+      for (int k = 0; k < 8; ++k) e[k] = __float2bfloat16_rn(__bfloat162float(e[k]) + bf16r(av[k]));
+      xr[lane + 32 * j] = u[j];
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float f = __bfloat162float(e[j]);
+    for (int k = 0; k < 8; ++k) {
+      const float f = __bfloat162float(e[k]);
       ss += f * f;
     }
   }
   ss = warp_sum(ss);
   const float r = 1.0f / sqrtf(ss / (float)hidden + eps);
-  const uint4* wr = reinterpret_cast<const uint4*>(w);
   uint4* yr = reinterpret_cast<uint4*>(y + (long long)row * hidden);
-  for (int i = lane; i < hidden / 8; i += 32) {
-    uint4 u = xr[i], wv = wr[i], o;
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u);
-    const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) {
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u[j]);
+    const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv[j]);
+    uint4 o;
     __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&o);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) oe[j] = __float2bfloat16_rn(bf16r(__bfloat162float(e[j]) * r) * __bfloat162float(we[j]));
-    yr[i] = o;
+    for (int k = 0; k < 8; ++k) oe[k] = __float2bfloat16_rn(bf16r(__bfloat162float(e[k]) * r) * __bfloat162float(we[k]));
+    yr[lane + 32 * j] = o;
   }
   if (zero_keys && lane == 0) zero_keys[row] = 0ull;
 }
@@ -438,11 +449,23 @@ int launch_embed(const __nv_bfloat16* embed, const int32_t* tokens, const int32_
 int launch_rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int max_rows,
                    const int32_t* rows_dev, const int32_t* gather, int hidden, float eps,
                    unsigned long long* zero_keys, cudaStream_t stream, const float* add) {
-  if (hidden % 256) return NE_ERR_INVALID;
   const int blocks = (max_rows + 3) / 4;
   if (blocks == 0) return NE_OK;
-  return launch_kernel(rmsnorm_kernel, dim3(blocks), dim3(128), 0, stream, x, w, y, max_rows, rows_dev, gather, hidden,
-                       eps, zero_keys, add) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
+  cudaError_t err;
+  switch (hidden) {  // 256 x chunks per lane
+    case 1024: err = launch_kernel(rmsnorm_kernel<4>, dim3(blocks), dim3(128), 0, stream, x, w, y, max_rows, rows_dev,
+                                   gather, hidden, eps, zero_keys, add); break;
+    case 2048: err = launch_kernel(rmsnorm_kernel<8>, dim3(blocks), dim3(128), 0, stream, x, w, y, max_rows, rows_dev,
+                                   gather, hidden, eps, zero_keys, add); break;
+    case 4096: err = launch_kernel(rmsnorm_kernel<16>, dim3(blocks), dim3(128), 0, stream, x, w, y, max_rows, rows_dev,
+                                   gather, hidden, eps, zero_keys, add); break;
+    case 256: err = launch_kernel(rmsnorm_kernel<1>, dim3(blocks), dim3(128), 0, stream, x, w, y, max_rows, rows_dev,
+                                  gather, hidden, eps, zero_keys, add); break;
+    case 512: err = launch_kernel(rmsnorm_kernel<2>, dim3(blocks), dim3(128), 0, stream, x, w, y, max_rows, rows_dev,
+                                  gather, hidden, eps, zero_keys, add); break;
+    default: return NE_ERR_UNSUPPORTED;  // hidden sizes other than 256 x {1, 2, 4, 8, 16}
+  }
+  return err == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 
 int launch_keys_to_ids(const unsigned long long* keys, const int32_t* count, int max_count, int32_t* ids,
