@@ -15,6 +15,8 @@
 //   combine_kernel merges the splits; otherwise the CTA writes the bf16 output directly.
 // * int8 KV: blocks are dequantised while staged (int8 -> bf16, times the bf16 per (slot, head)
 //   scale, as read_from_cache, attention_context.py:57-63).
+#include <algorithm>
+
 #include "attention.cuh"
 
 namespace ne {
@@ -339,13 +341,13 @@ __device__ __forceinline__ void tile_store(const Ctx& c, const AttnSplit& sp, co
 // One or two query tiles (the speculative step): warp w serves query tile w % NT and every
 // (4 / NT)-th block of the split from its own double buffer (bf16: two K/V stages; int8: two raw
 // stages + one converted K/V pair); the warps of a tile merge (max, sum, O) through smem at the end.
-template <bool INT8, int NT>
+template <bool INT8, int NT, int NW>
 __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& rows, const AttnSplit& sp, int b, int h,
                                                  int split, int kb0, int kb1, uint8_t* q_s, int* spos, uint8_t* buf,
                                                  __nv_bfloat16* out, int nh, int nkv) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t buf_u = smem_u32(buf);
-  const int per_tile = 4 / NT, my_tile = warp % NT, phase = warp / NT;
+  const int per_tile = NW / NT, my_tile = warp % NT, phase = warp / NT;
   const uint32_t wbuf = buf_u + warp * 4 * BLOCK_BYTES;
   // the table entries of this warp's blocks (the j-th is logical block kb0 + phase + per_tile * j),
   // 32 at a time in the lanes of a register: no dependent global load inside the block loop
@@ -372,7 +374,7 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
   TileState ts;
   for (int t = 0; t < NT; ++t) {  // one Q staging area: tile t's warps take their fragments in turn
     if (t > 0) __syncthreads();
-    load_q_tile(c, 16 * t, q_s, tid, THREADS);
+    load_q_tile(c, 16 * t, q_s, tid, 32 * NW);
     __syncthreads();
     if (my_tile == t) tile_init(ts, smem_u32(q_s), spos + 16 * t, lane);
   }
@@ -416,9 +418,9 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
   cp_wait<0>();
   // merge the warps of each tile through smem (reusing the stage buffers)
   __syncthreads();
-  float* mo = reinterpret_cast<float*>(buf);          // [4][16][128]
-  float* mm = mo + 4 * 16 * D;                        // [4][16]
-  float* ml = mm + 4 * 16;                            // [4][16]
+  float* mo = reinterpret_cast<float*>(buf);          // [NW][16][128]
+  float* mm = mo + NW * 16 * D;                       // [NW][16]
+  float* ml = mm + NW * 16;                           // [NW][16]
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const int row = (lane >> 2) + 8 * r;
@@ -438,33 +440,38 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
     const int t = v >> 4, row = v & 15;
     float m = NEG_INF;
     for (int i = 0; i < per_tile; ++i) m = fmaxf(m, mm[(t + NT * i) * 16 + row]);
-    float l = 0.f, o = 0.f;
-    if (m != NEG_INF) {
-      for (int i = 0; i < per_tile; ++i) {
-        const int w = t + NT * i;
-        const float mw = mm[w * 16 + row];
-        const float f = mw == NEG_INF ? 0.f : exp2f(mw - m);
-        l += ml[w * 16 + row] * f;
-        o += mo[(w * 16 + row) * D + tid] * f;
+#pragma unroll
+    for (int d = tid; d < D; d += 32 * NW) {
+      float l = 0.f, o = 0.f;
+      if (m != NEG_INF) {
+        for (int i = 0; i < per_tile; ++i) {
+          const int w = t + NT * i;
+          const float mw = mm[w * 16 + row];
+          const float f = mw == NEG_INF ? 0.f : exp2f(mw - m);
+          l += ml[w * 16 + row] * f;
+          o += mo[(w * 16 + row) * D + d] * f;
+        }
       }
-    }
-    if (sp.splits == 1) {
-      const int orow = c.r0 + v / c.G;
-      const int head = c.h * c.G + v % c.G;
-      out[((long long)orow * nh + head) * D + tid] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
-    } else {
-      const long long base = (((long long)b * nkv + h) * sp.splits + split) * sp.max_vec + v;
-      sp.part_o[base * D + tid] = o;
-      if (tid == 0) {
-        sp.part_m[base] = m;
-        sp.part_l[base] = l;
+      if (sp.splits == 1) {
+        const int orow = c.r0 + v / c.G;
+        const int head = c.h * c.G + v % c.G;
+        out[((long long)orow * nh + head) * D + d] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
+      } else {
+        const long long base = (((long long)b * nkv + h) * sp.splits + split) * sp.max_vec + v;
+        sp.part_o[base * D + d] = o;
+        if (d == 0) {
+          sp.part_m[base] = m;
+          sp.part_l[base] = l;
+        }
       }
     }
   }
 }
 
-template <bool INT8>
-__global__ void __launch_bounds__(THREADS, 3)  // three CTAs per SM (registers <= 168)
+// NW warps per CTA: 4 (three CTAs per SM, registers <= 168; every path), or 2 (one query tile
+// only: five CTAs per SM, so that a speculative step's (entry, KV head) pairs fit in one wave).
+template <bool INT8, int NW>
+__global__ void __launch_bounds__(32 * NW, NW == 4 ? 3 : 5)
     attention_kernel(const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out, const void* __restrict__ kc,
                      const void* __restrict__ vc, const __nv_bfloat16* __restrict__ ks,
                      const __nv_bfloat16* __restrict__ vs, ne_rows rows, int nh, int nkv, long long num_cache_slots,
@@ -503,9 +510,11 @@ __global__ void __launch_bounds__(THREADS, 3)  // three CTAs per SM (registers <
   const uint32_t buf_u = smem_u32(buf);
 
   if (ntiles == 1) {
-    warp_split_tiles<INT8, 1>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv);
+    warp_split_tiles<INT8, 1, NW>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv);
+  } else if (NW != 4) {
+    report(status, NE_DEV_BAD_SLOT);  // the host launches the 2-warp kernel only for one-tile rows
   } else if (ntiles == 2) {
-    warp_split_tiles<INT8, 2>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv);
+    warp_split_tiles<INT8, 2, 4>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv);
   } else {
     // ---------------------------------------------------------------- many tiles, shared blocks
     for (int t0 = 0; t0 < ntiles; t0 += 4) {
@@ -592,6 +601,14 @@ __global__ void clear_partials_kernel(AttnSplit sp, long long n) {
 
 }  // namespace
 
+size_t attention_smem_bytes_nw(int nw) {
+  if (nw == 4) return attention_smem_bytes();
+  // Q tile + positions + max(nw warps x 2 stages x (K, V) blocks, the merge area)
+  const size_t stages = (size_t)nw * 4 * BLOCK_BYTES;
+  const size_t merge = ((size_t)nw * 16 * D + 2 * nw * 16) * sizeof(float);
+  return BLOCK_BYTES + 256 + (stages > merge ? stages : merge);
+}
+
 size_t attention_smem_bytes() {
   // Q tile + positions + max(4 warps x 2 stages x (K, V) blocks, the merge area, 2 shared stages + 4 Q tiles)
   const size_t stages = 4 * 4 * BLOCK_BYTES;
@@ -631,13 +648,23 @@ int launch_attention_tc(const __nv_bfloat16* q, __nv_bfloat16* out, const void* 
                         cudaStream_t stream) {
   if (num_kv_heads <= 0 || num_heads % num_kv_heads || rows.num_seqs <= 0 || sp.splits < 1) return NE_ERR_INVALID;
   if (sp.splits > 1 && (!sp.part_o || !sp.part_m || !sp.part_l || sp.max_vec < 1)) return NE_ERR_INVALID;
-  const size_t smem = attention_smem_bytes();
-  static bool attr_set[2] = {false, false};
-  auto kernel = kv_int8 ? attention_kernel<true> : attention_kernel<false>;
-  if (!attr_set[kv_int8 ? 1 : 0]) {
+  // one query tile per (entry, KV head) (the speculative step) and a grid that five 2-warp CTAs
+  // per SM hold in one wave but three 4-warp CTAs do not: the 2-warp kernel (measured: faster at
+  // 64 users with short contexts, slower than the 4-warp kernel when several waves remain anyway)
+  const int max_vec = std::max(1, rows.max_q_len) * (num_heads / num_kv_heads);
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long ctas = (long long)rows.num_seqs * num_kv_heads * sp.splits;
+  const int nw = (max_vec <= 16 && ctas <= 5LL * sms && ctas > 3LL * sms) ? 2 : 4;
+  const size_t smem = attention_smem_bytes_nw(nw);
+  static bool attr_set[4] = {false, false, false, false};
+  auto kernel = kv_int8 ? (nw == 2 ? attention_kernel<true, 2> : attention_kernel<true, 4>)
+                        : (nw == 2 ? attention_kernel<false, 2> : attention_kernel<false, 4>);
+  const int ai = (kv_int8 ? 2 : 0) + (nw == 2 ? 1 : 0);
+  if (!attr_set[ai]) {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return NE_ERR_CUDA;
-    attr_set[kv_int8 ? 1 : 0] = true;
+    attr_set[ai] = true;
   }
   if (sp.splits > 1) {
     const long long n = (long long)rows.num_seqs * num_kv_heads * sp.splits * sp.max_vec;
@@ -646,7 +673,7 @@ int launch_attention_tc(const __nv_bfloat16* q, __nv_bfloat16* out, const void* 
       return NE_ERR_CUDA;
   }
   dim3 grid(rows.num_seqs, num_kv_heads, sp.splits);
-  if (launch_kernel(kernel, grid, dim3(THREADS), smem, stream, q, out, k_cache, v_cache, k_scale, v_scale, rows,
+  if (launch_kernel(kernel, grid, dim3(32 * nw), smem, stream, q, out, k_cache, v_cache, k_scale, v_scale, rows,
                     num_heads, num_kv_heads, num_cache_slots, sp, status) != cudaSuccess)
     return NE_ERR_CUDA;
   if (sp.splits > 1) {
