@@ -918,6 +918,12 @@ int plan_uncached(GemmParams& p, int num_sms) {
                           (p.w_scale ? GEMM_W8_TILE_BYTES : 0);
   const int cps = (num_chunks + S - 1) / S;
   int stages = std::min(std::min(max_stages(), cps), avail / stage_bytes);
+  if (p.epi.mode == EPI_ARGMAX || p.epi.mode == EPI_LOGITS) {
+    // the LM head runs many waves of CTAs: a shallow pipeline lets two CTAs share an SM, so one
+    // streams its weights while the other finishes its epilogue (NE_LM_MAX_STAGES overrides)
+    static const int lm_cap = getenv("NE_LM_MAX_STAGES") ? env_cap("NE_LM_MAX_STAGES", GEMM_MAX_STAGES) : 2;
+    stages = std::min(stages, lm_cap);
+  }
   if (stages < 1) return NE_ERR_INVALID;
   const int staging = staging_bytes(S, t_block);
   int data = std::max(stages * stage_bytes, staging);
