@@ -438,7 +438,7 @@ def run_b200(args, dist: Dist) -> None:
     model.raise_on_device_error()
     engine._set_slots(slots, engine_mod.round_up_to_bucket(len(slots), engine.buckets))
     lens_before = engine.state.seq_len.sum().item()
-    graph = engine._graphs[engine_mod.round_up_to_bucket(len(slots), engine.buckets)]
+    graph = engine._graphs[(engine_mod.round_up_to_bucket(len(slots), engine.buckets), 0)]
     stream = torch.cuda.current_stream()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     dist.barrier()

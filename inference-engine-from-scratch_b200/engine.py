@@ -64,10 +64,18 @@ class _Outputs:
             proposed=base + 4 * n * (w + 2), accepted=base + 4 * n * (w + 3),
         )
 
-    def fetch(self, num: int):
-        """Copy the whole buffer device->host and split it (one D2H per step)."""
+    def start_fetch(self) -> None:
+        """Enqueue the device->host copy of the results and an event after it (no host wait)."""
         self.host.copy_(self.buf, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+        self.event = torch.cuda.Event()
+        self.event.record()
+
+    def fetch(self, num: int):
+        """Copy the whole buffer device->host (unless start_fetch did) and split it (one D2H per step)."""
+        if getattr(self, "event", None) is None:
+            self.start_fetch()
+        self.event.synchronize()
+        self.event = None
         n, w = self.max_seqs, self.k + 1
         h = self.host
         tokens = h[: n * w].view(n, w)[:num]
@@ -105,13 +113,16 @@ class B200SpeculativeEngine:
         if blocks * 16 > model.num_slots:
             raise ValueError("more blocks than the KV pool holds")
         self.state = DeviceBatchState(max_seqs, max_model_len, k, blocks, 16, stop_token_ids, model.device)
-        self.outputs = _Outputs(max_seqs, k, model.device)
+        # two result buffers: generate() reads step i's results while step i + 1 runs
+        self._outs = [_Outputs(max_seqs, k, model.device), _Outputs(max_seqs, k, model.device)]
+        self.outputs = self._outs[0]
         self.max_prefill_rows = min(max_prefill_rows or model.max_rows, model.max_rows)
         self.buckets = build_buckets(max_seqs)
         self.cuda_graphs = cuda_graphs
         self._slots_dev = torch.full((max_seqs,), -1, dtype=torch.int32, device=model.device)
-        self._slots_host = torch.full((max_seqs,), -1, dtype=torch.int32).pin_memory()
-        self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self._slots_hosts = [torch.full((max_seqs,), -1, dtype=torch.int32).pin_memory() for _ in range(2)]
+        self._slots_host = self._slots_hosts[0]
+        self._graphs: dict[tuple[int, int], torch.cuda.CUDAGraph] = {}
         # sampled requests (temperature > 0) need every lm row's logits: bind a sampling buffer
         # (bound to the model before each eager launch or capture, since engines may share a model)
         self.sampling = sampling
@@ -190,15 +201,19 @@ class B200SpeculativeEngine:
             if holder is not None:
                 self._prefixes[holder][2] -= 1
 
-    def _set_slots(self, slots: list[int], bucket: int) -> None:
-        self._slots_host.fill_(-1)
-        self._slots_host[: len(slots)] = torch.tensor(slots, dtype=torch.int32)
-        self._slots_dev[:bucket].copy_(self._slots_host[:bucket], non_blocking=True)
+    def _set_slots(self, slots: list[int], bucket: int, host: int = 0) -> None:
+        # the pinned source of an asynchronous copy must not change before the copy runs: the two
+        # in-flight steps of generate() use two host buffers
+        h = self._slots_hosts[host]
+        h.fill_(-1)
+        h[: len(slots)] = torch.tensor(slots, dtype=torch.int32)
+        self._slots_dev[:bucket].copy_(h[:bucket], non_blocking=True)
         self.h2d_bytes += 4 * bucket
 
-    def _collect(self, slots: list[int]) -> StepResult:
-        tokens, count, finish, proposed, accepted = self.outputs.fetch(len(slots))
-        self.d2h_bytes += self.outputs.buf.numel() * 4
+    def _collect(self, slots: list[int], outs: _Outputs | None = None) -> StepResult:
+        outs = outs or self.outputs
+        tokens, count, finish, proposed, accepted = outs.fetch(len(slots))
+        self.d2h_bytes += outs.buf.numel() * 4
         self.steps_run += 1
         result = StepResult()
         for i, slot in enumerate(slots):
@@ -253,22 +268,25 @@ class B200SpeculativeEngine:
         return res
 
     # ------------------------------------------------------------------ speculative step
-    def _launch_step(self, bucket: int) -> None:
+    def _launch_step(self, bucket: int, buf: int = 0) -> None:
         self._bind_sampler()
         _lib.check(self.lib.ne_spec_step(self.model.handle, self.state.ref, self._slots_dev.data_ptr(), bucket,
-                                         self.k, self.max_ngram, ctypes.byref(self.outputs.struct),
+                                         self.k, self.max_ngram, ctypes.byref(self._outs[buf].struct),
                                          _lib.stream_handle()), "ne_spec_step")
 
-    def launch(self, slots: list[int]) -> int:
-        """Enqueue one step for ``slots`` (no host sync); returns the bucket used."""
+    def launch(self, slots: list[int], buf: int = 0) -> int:
+        """Enqueue one step for ``slots`` (no host sync) writing result buffer ``buf``; returns the
+        bucket used."""
         bucket = round_up_to_bucket(len(slots), self.buckets)
-        self._set_slots(slots, bucket)
+        self._set_slots(slots, bucket, buf)
         if not self.cuda_graphs:
-            self._launch_step(bucket)
+            self._launch_step(bucket, buf)
             return bucket
-        graph = self._graphs.get(bucket)
+        graph = self._graphs.get((bucket, buf))
         if graph is None:
-            graph = self._capture(bucket)
+            for b in (0, 1):  # both result buffers at once: generate() alternates them
+                self._capture(bucket, b)
+            graph = self._graphs[(bucket, buf)]
         graph.replay()
         return bucket
 
@@ -276,7 +294,7 @@ class B200SpeculativeEngine:
         self.launch(slots)
         return self._collect(slots)
 
-    def _capture(self, bucket: int) -> torch.cuda.CUDAGraph:
+    def _capture(self, bucket: int, buf: int = 0) -> torch.cuda.CUDAGraph:
         """Capture one bucket's step. The capture itself changes no state: every slot in the
         bucket is idle (-1) while capturing, so the captured kernels find no work."""
         saved = self._slots_dev.clone()
@@ -285,15 +303,15 @@ class B200SpeculativeEngine:
         stream = torch.cuda.Stream()
         stream.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(stream):
-            self._launch_step(bucket)  # warm-up outside capture (idle slots: no state change)
+            self._launch_step(bucket, buf)  # warm-up outside capture (idle slots: no state change)
         torch.cuda.current_stream().wait_stream(stream)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            self._launch_step(bucket)
+            self._launch_step(bucket, buf)
         torch.cuda.synchronize()
         self._slots_dev.copy_(saved)
-        self._graphs[bucket] = graph
+        self._graphs[(bucket, buf)] = graph
         return graph
 
     # ------------------------------------------------------------------ whole requests
@@ -308,7 +326,8 @@ class B200SpeculativeEngine:
         pending = list(range(len(prompts)))
         running: dict[int, int] = {}  # slot -> request index
         prefix = self.add_prefix(prompts[0][:shared_prefix]) if shared_prefix else None
-        while pending or running:
+
+        def admit() -> None:
             admitted = []
             while pending and self.state.free_slots:
                 index = pending.pop(0)
@@ -320,10 +339,38 @@ class B200SpeculativeEngine:
             if admitted:
                 res = self.prefill(admitted, chunk=prefill_chunk)
                 self._absorb(res, running, outputs)
+
+        # Steps run one ahead of the host: step i + 1 is enqueued before step i's results are
+        # read, so the host work of a step overlaps the next one on the GPU. A sequence that
+        # finished at step i is still listed in step i + 1, where the device treats it as idle
+        # (finished flag); its slot is released after step i's results arrive.
+        inflight = None  # (slots, result buffer) of the step on the GPU
+        buf = 0
+        while pending or running or inflight:
+            if inflight is None:
+                admit()
+                if running:
+                    slots = sorted(running)
+                    self.launch(slots, buf)
+                    self._outs[buf].start_fetch()
+                    inflight = (slots, buf)
+                    buf ^= 1
+                continue
+            nxt = None
             if running:
                 slots = sorted(running)
-                res = self.step(slots)
+                self.launch(slots, buf)
+                self._outs[buf].start_fetch()
+                nxt = (slots, buf)
+                buf ^= 1
+            res = self._collect(inflight[0], self._outs[inflight[1]])
+            self._absorb(res, running, outputs)
+            inflight = nxt
+            if pending and self.state.free_slots and inflight is not None:
+                # admission needs a prefill: read the step in flight first (its slots are current)
+                res = self._collect(inflight[0], self._outs[inflight[1]])
                 self._absorb(res, running, outputs)
+                inflight = None
         if prefix is not None:
             self.drop_prefix(prefix)
         return outputs
@@ -331,6 +378,8 @@ class B200SpeculativeEngine:
     def _absorb(self, res: StepResult, running: dict[int, int], outputs: list[list[int]]) -> None:
         done = []
         for slot, toks in res.tokens.items():
+            if slot not in running:  # finished at the previous step (idle in this one)
+                continue
             outputs[running[slot]].extend(toks)
             if res.finish.get(slot) is not None:
                 done.append(slot)
