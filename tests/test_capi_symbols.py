@@ -39,3 +39,30 @@ def test_invalid_arguments_are_rejected_without_a_gpu() -> None:
                                         kv_int8=0, weight_int8=0, num_cache_slots=17, max_positions=64)
     handle = ctypes.c_void_p()
     assert lib.ne_model_create(ctypes.byref(cfg), ctypes.byref(handle)) == 1  # head_dim must be 128
+
+
+def test_new_entry_points_refuse_bad_arguments_without_a_gpu() -> None:
+    """Argument checks of the sampling, tensor-parallel, sharing and int8 entries (no device work)."""
+    _lib = submodule("_lib")
+    lib = _lib.load()
+    assert lib.ne_sampling_buffer_bytes(None, 16) == 0
+    assert lib.ne_model_set_sampling_buffer(None, None, 0, 0) == 1
+    assert lib.ne_verify_logits(None, None, 1, 4, None, None, None, 4096, 5, None, 0, None, None, None) == 1
+    assert lib.ne_state_share_blocks(None, 0, None, 0, 1, None, None) == 1
+    assert lib.ne_gemm_w8(None, None, None, None, 1, 128, 64, None, None) == 1
+    assert lib.ne_tp_unique_id(None, None) == 1
+    assert lib.ne_model_set_tp(None, b"libnccl.so.2", 0, 2, None) == 1
+    # an unknown NCCL library path is reported, not crashed on
+    buf = (ctypes.c_char * 128)()
+    assert lib.ne_tp_unique_id(b"/nonexistent/libnccl.so.2", buf) == _lib_status(lib, "unsupported")
+    cfg = _lib.ModelConfig(vocab_size=4096, hidden_size=256, intermediate_size=512, num_layers=1, num_heads=4,
+                           num_kv_heads=2, head_dim=128, rms_norm_eps=1e-6, block_size=16, kv_int8=0, weight_int8=0,
+                           num_cache_slots=17, max_positions=64, lm_rows=100, lm_offset=0)
+    handle = ctypes.c_void_p()
+    assert lib.ne_model_create(ctypes.byref(cfg), ctypes.byref(handle)) == 1  # LM-head rows: whole 128-row tiles
+    cfg.lm_rows, cfg.hidden_size = 0, 768
+    assert lib.ne_model_create(ctypes.byref(cfg), ctypes.byref(handle)) == 4  # hidden 768: no RMSNorm variant
+
+
+def _lib_status(lib, name: str) -> int:
+    return {"invalid": 1, "cuda": 2, "device": 3, "unsupported": 4, "workspace": 5}[name]

@@ -397,3 +397,19 @@ def test_serial_sampled_generation_is_reproducible_and_replays_on_the_oracle(sma
         expected.append(exp)
         start = end
     check_against(cases, got, [0] * len(got), expected, [0] * len(got))
+
+
+def test_a_sampled_sequence_on_a_model_without_a_sampling_buffer_is_reported(small_model) -> None:
+    """The device flags NE_DEV_NO_SAMPLER (the host API refuses such requests earlier)."""
+    cfg, model = small_model
+    _lib = submodule("_lib")
+    eng = submodule("engine").B200SpeculativeEngine(model, k=4, max_seqs=2, max_model_len=256, num_blocks=32,
+                                                    cuda_graphs=False)
+    eng.state.reset_blocks()
+    slot = eng.add_request(package().make_prompts(1, cfg.vocab_size, 32, seed=2)[0], 8, ignore_eos=True)
+    eng.prefill([slot])
+    eng.state.temperature[slot] = 0.8  # behind the API's back
+    eng.step([slot])
+    word = model.read_status(clear=True)
+    assert word & 32, f"status 0x{word:x}"
+    eng.release([slot])
