@@ -19,8 +19,10 @@
 Other BASELINE workloads (not the default line): ``--workload c3`` (int8 weights + int8 KV, 64 users,
 k=8, 1024-token prompts whose first 512 tokens are one shared prefix served from shared KV blocks,
 256 outputs) and ``--workload c4`` (256 users, sampled T=0.8 / top-p 0.95 on per-request Philox
-streams, prompt lengths uniform in [32, 2048], chunked prefill of 512 tokens, 256 outputs, k=4), ``--workload c5b`` (Qwen3-8B shape, bf16, tensor-parallel over the N torchrun ranks
-with NCCL all-reduce after o_proj and down_proj, 32 users, 512-token prompts, 256 outputs, k=4).
+streams, prompt lengths uniform in [32, 2048], chunked prefill of 512 tokens, 256 outputs, k=4), ``--workload c5b`` (Qwen3-8B shape, bf16, tensor-parallel over the N torchrun ranks:
+o_proj / down_proj push their fp32 partials into every rank's exchange region over NVLink for
+steps of up to ``--tp-exchange-rows`` rows, NCCL all-reduce above that; 32 users, 512-token
+prompts, 256 outputs, k=4).
 
 Multi-GPU: one process per GPU (torchrun); each rank serves its own 64 users on an independent
 replica (no collectives on the data path); NCCL only carries the barrier and the max-over-ranks
@@ -57,6 +59,8 @@ def parse_args():
     p.add_argument("--steps", type=int, default=30)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--tp-exchange-rows", type=int, default=512,
+                   help="c5b: steps of up to this many rows use the NVLink peer exchange (0: NCCL only)")
     p.add_argument("--workload", choices=("c2", "c3", "c4", "c5b"), default="c2",
                    help="BASELINE config: c2 (default, the headline), c3 (int8, shared prefix), c4 (sampled), "
                         "c5b (Qwen3-8B shape, tensor parallel over the torchrun ranks)")
@@ -337,10 +341,12 @@ class Workload:
             self.metric = "accepted tok/s, Qwen3-8B-shape spec-decode at 32 users (n-gram k=4, greedy), tensor parallel"
             self.config = {
                 "workload": "BASELINE config 5b: Qwen3-8B shape (36 layers, hidden 4096, 32/8 heads, MLP 12288, "
-                            "vocab 151936, untied head) random-init bf16, tensor-parallel over the GPUs (NCCL "
-                            "all-reduce of fp32 partials after o_proj and down_proj, vocabulary-split LM head), "
+                            "vocab 151936, untied head) random-init bf16, tensor-parallel over the GPUs (fp32 "
+                            "partials of o_proj and down_proj pushed to every rank over NVLink peer memory and "
+                            "summed in the next RMSNorm launch for steps of up to tp_exchange_rows rows, NCCL "
+                            "all-reduce above; vocabulary-split LM head, argmax keys exchanged the same way), "
                             "32 users, 512-token prompts (50% motif-repeated), 256 outputs, n-gram n=3 k=4, greedy",
-                "users": 32, "k": 4, "parallelism": f"tp{args.gpus}",
+                "users": 32, "k": 4, "parallelism": f"tp{args.gpus}", "tp_exchange_rows": args.tp_exchange_rows,
                 "l2": "no flush: every step streams 15.1 GB / N of weights + KV (> 126 MB L2)"}
         else:
             self.users, self.k, self.max_new = 256, 4, 256
@@ -411,7 +417,8 @@ def run_b200(args, dist: Dist) -> None:
         weights = tp_mod.make_sharded_weights(cfg, plan, seed=0, device=device)
         model = model_mod.B200Model(tp_mod.rank_config(cfg, plan), weights, num_slots=num_blocks * 16, device=device,
                                     max_positions=max_model_len + k + 16, max_rows=max_rows, max_seqs=users + 1,
-                                    tp=tp_mod.TensorParallel(dist.rank, dist.world, uid, lib_path),
+                                    tp=tp_mod.TensorParallel(dist.rank, dist.world, uid, lib_path,
+                                                             exchange_rows=args.tp_exchange_rows),
                                     lm_offset=plan.vocab[0])
         cfg = tp_mod.rank_config(cfg, plan)  # per-rank shapes for the byte counts below
     else:

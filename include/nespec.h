@@ -304,6 +304,23 @@ NE_API int ne_verify_logits(const ne_batch_state* state, const int32_t* seq_slot
 NE_API int ne_tp_unique_id(const char* nccl_library, void* unique_id);
 NE_API int ne_model_set_tp(ne_model* model, const char* nccl_library, int rank, int world, const void* unique_id);
 
+/*
+ * Peer exchange (replaces the NCCL calls of a step of up to ``max_rows`` rows): every rank
+ * allocates an exchange region in its own GPU memory (ne_model_tp_exchange_create, after
+ * ne_model_set_tp; it returns the region's CUDA IPC handle, NE_TP_HANDLE_BYTES bytes), the caller
+ * gathers the handles of all ranks in rank order and hands them to ne_model_tp_exchange_open on
+ * every rank. From then on o_proj and down_proj store their fp32 partial tiles straight into every
+ * rank's region over NVLink and signal each rank (one release reduction per CTA and rank); the next
+ * RMSNorm launch waits for all ranks (bounded: NE_DEV_TIMEOUT), adds the partials in rank order
+ * to the residual stream and normalises; the LM head's argmax keys are exchanged the same way.
+ * Larger steps (prefill) keep the NCCL path. Every rank must make the same sequence of forward
+ * calls. Before a rank destroys its model, all ranks' work on the split model must be finished
+ * (synchronise, then a barrier): a peer's kernels write into this rank's region.
+ */
+#define NE_TP_HANDLE_BYTES 64
+NE_API int ne_model_tp_exchange_create(ne_model* model, int max_rows, void* ipc_handle);
+NE_API int ne_model_tp_exchange_open(ne_model* model, const void* ipc_handles);
+
 /* ---------------------------------------------------------------- launch accounting */
 /* Kernel classes of a step, for per-kernel device timing (ne_model_profile_*). */
 #define NE_K_EMBED 0

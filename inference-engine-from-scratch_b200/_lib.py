@@ -28,6 +28,8 @@ DEVICE_STATUS_BITS = {
 }
 
 # (name, restype, argtypes) for every entry point of include/nespec.h
+TP_HANDLE_BYTES = 64  # NE_TP_HANDLE_BYTES (CUDA IPC handle)
+
 EXPORTS = {
     "ne_abi_version": (c_int, []),
     "ne_status_string": (ctypes.c_char_p, [c_int]),
@@ -68,6 +70,8 @@ EXPORTS = {
     ),
     "ne_tp_unique_id": (c_int, [ctypes.c_char_p, c_void_p]),
     "ne_model_set_tp": (c_int, [c_void_p, ctypes.c_char_p, c_int, c_int, c_void_p]),
+    "ne_model_tp_exchange_create": (c_int, [c_void_p, c_int, c_void_p]),
+    "ne_model_tp_exchange_open": (c_int, [c_void_p, c_void_p]),
     "ne_model_launch_count": (c_longlong, [c_void_p]),
     "ne_model_profile_begin": (c_int, [c_void_p, c_void_p]),
     "ne_model_profile_end": (c_int, [c_void_p, POINTER(c_float), POINTER(c_int), c_int]),

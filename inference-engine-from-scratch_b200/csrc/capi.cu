@@ -40,6 +40,12 @@ struct ne_model {
   void* tp_comm = nullptr;
   int tp_rank = 0, tp_world = 1;
   float* partial = nullptr;  // fp32 [max_rows, H]: row-parallel projection outputs, all-reduced
+  // peer exchange (steps of up to link.max_rows rows): own region, peers' regions mapped here
+  void* tp_region = nullptr;
+  size_t tp_region_bytes = 0;
+  int tp_exchange_rows = 0;
+  void* tp_peer[ne::TP_MAX_WORLD] = {};
+  ne::TpLink link{};         // link.world > 0 once every peer region is open
   float* ssq = nullptr;      // fp32 [max_rows, H / 128]: residual rows' sums of squares per 128-wide tile
   CUtensorMap tm_h{};        // the residual rows as a GEMM X operand (RMSNorm fused into the GEMM)
   CUtensorMap tm_x{}, tm_attn{}, tm_act{};
@@ -53,6 +59,8 @@ struct ne_model {
   size_t events_used = 0;
   ~ne_model() {
     for (cudaEvent_t e : events) cudaEventDestroy(e);
+    for (void* p : tp_peer) ne::tp_exchange_close(p, false);
+    ne::tp_exchange_close(tp_region, true);
     ne::tp_comm_destroy(tp_comm);
   }
 };
@@ -351,6 +359,40 @@ int ne_model_set_tp(ne_model* m, const char* nccl_library, int rank, int world, 
   return NE_OK;
 }
 
+int ne_model_tp_exchange_create(ne_model* m, int max_rows, void* ipc_handle) {
+  if (!m || !ipc_handle || m->tp_world < 2 || m->tp_region || max_rows < 1 || max_rows > (1 << 16))
+    return NE_ERR_INVALID;
+  const ne::TpRegionLayout lay = ne::tp_region_layout(m->tp_world, max_rows, m->cfg.hidden_size);
+  const int rc = ne::tp_exchange_alloc(lay.total, &m->tp_region, ipc_handle);
+  if (rc) return rc;
+  m->tp_region_bytes = lay.total;
+  m->tp_exchange_rows = max_rows;
+  return NE_OK;
+}
+
+int ne_model_tp_exchange_open(ne_model* m, const void* ipc_handles) {
+  if (!m || !ipc_handles || !m->tp_region || m->link.world) return NE_ERR_INVALID;
+  void* bases[ne::TP_MAX_WORLD] = {};
+  for (int r = 0; r < m->tp_world; ++r) {
+    if (r == m->tp_rank) {
+      bases[r] = m->tp_region;
+      continue;
+    }
+    const int rc = ne::tp_exchange_open(static_cast<const char*>(ipc_handles) + (size_t)r * ne::TP_HANDLE_BYTES,
+                                        &m->tp_peer[r]);
+    if (rc) {
+      for (void*& p : m->tp_peer) {
+        ne::tp_exchange_close(p, false);
+        p = nullptr;
+      }
+      return rc;
+    }
+    bases[r] = m->tp_peer[r];
+  }
+  m->link = ne::tp_make_link(bases, m->tp_world, m->tp_rank, m->tp_exchange_rows, m->cfg.hidden_size);
+  return NE_OK;
+}
+
 int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int32_t* argmax_out, void* stream) {
   if (!m || !rows || !m->ws || !m->head_set) return NE_ERR_INVALID;
   for (char set : m->layer_set)
@@ -361,6 +403,11 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
   if (lm_mode == NE_LM_LOGITS && !logits) return NE_ERR_INVALID;
   const bool tp = m->tp_world > 1;
   if (tp && lm_mode == NE_LM_LOGITS) return NE_ERR_UNSUPPORTED;  // logits are split over the ranks
+  // a split model exchanges partial rows through peer memory when they fit the exchange slots
+  // (every rank takes the same branch: R and lm_max are the same host values on all ranks)
+  const bool px = tp && m->link.world > 0 && R <= m->link.max_rows && rows->lm_max <= m->link.max_rows;
+  const ne::TpLink* lk = px ? &m->link : nullptr;
+  float* nccl_add = tp && !px ? m->partial : nullptr;
   // RMSNorm folded into the QKV and gate/up GEMMs (statistics from the producing epilogue); a
   // split model adds the all-reduced projections in the RMSNorm launch instead
   const bool fuse = !tp && fused_norm_enabled();
@@ -383,7 +430,8 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
     if (!fuse) {
       rc = note(m, NE_K_RMSNORM,
                 ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(w.ln_in), m->x, R, rows->num_rows, nullptr,
-                                   H, c.rms_norm_eps, nullptr, s, tp && l > 0 ? m->partial : nullptr), s);
+                                   H, c.rms_norm_eps, nullptr, s, l > 0 ? nccl_add : nullptr, l > 0 ? lk : nullptr,
+                                   m->status), s);
       if (rc) return rc;
     }
     ne::Epilogue e{};
@@ -416,7 +464,8 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
                                       c.num_kv_heads, c.num_cache_slots, attn, m->status, s), s);
     if (rc) return rc;
     ne::Epilogue eo{};
-    eo.mode = tp ? ne::EPI_STORE_F32 : ne::EPI_RESIDUAL;
+    eo.mode = px ? ne::EPI_PUSH_F32 : tp ? ne::EPI_STORE_F32 : ne::EPI_RESIDUAL;
+    eo.link = m->link;
     eo.status = m->status;
     eo.out = m->h;
     eo.out_f32 = m->partial;
@@ -425,14 +474,14 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
     eo.ssq_tiles = H / 128;
     rc = note(m, NE_K_GEMM_O, run_gemm(m, &m->tm_o[l], &m->tm_attn, R, rows->num_rows, H, qs, eo, s, w.w_o_scale), s);
     if (rc) return rc;
-    if (tp) {
+    if (tp && !px) {
       rc = note(m, NE_K_COLLECTIVE, ne::tp_allreduce_sum_f32(m->partial, (size_t)R * H, m->tp_comm, s), s);
       if (rc) return rc;
     }
     if (!fuse) {
       rc = note(m, NE_K_RMSNORM,
                 ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(w.ln_post), m->x, R, rows->num_rows,
-                                   nullptr, H, c.rms_norm_eps, nullptr, s, tp ? m->partial : nullptr), s);
+                                   nullptr, H, c.rms_norm_eps, nullptr, s, nccl_add, lk, m->status), s);
       if (rc) return rc;
     }
     ne::Epilogue eg{};
@@ -444,7 +493,8 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
                                             H, eg, s, w.w_gateup_scale, fuse ? w.ln_post : nullptr), s);
     if (rc) return rc;
     ne::Epilogue ed{};
-    ed.mode = tp ? ne::EPI_STORE_F32 : ne::EPI_RESIDUAL;
+    ed.mode = px ? ne::EPI_PUSH_F32 : tp ? ne::EPI_STORE_F32 : ne::EPI_RESIDUAL;
+    ed.link = m->link;
     ed.status = m->status;
     ed.out = m->h;
     ed.out_f32 = m->partial;
@@ -453,7 +503,7 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
     ed.ssq_tiles = H / 128;
     rc = note(m, NE_K_GEMM_DOWN, run_gemm(m, &m->tm_down[l], &m->tm_act, R, rows->num_rows, H, I, ed, s, w.w_down_scale), s);
     if (rc) return rc;
-    if (tp) {
+    if (tp && !px) {
       rc = note(m, NE_K_COLLECTIVE, ne::tp_allreduce_sum_f32(m->partial, (size_t)R * H, m->tp_comm, s), s);
       if (rc) return rc;
     }
@@ -462,8 +512,8 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
   const int lm_max = rows->lm_max;
   rc = note(m, NE_K_RMSNORM,
             ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(m->head.final_norm), m->x, lm_max,
-                               rows->lm_count, rows->lm_rows, H, c.rms_norm_eps, m->keys, s,
-                               tp ? m->partial : nullptr), s);
+                               rows->lm_count, rows->lm_rows, H, c.rms_norm_eps, m->keys, s, nccl_add, lk,
+                               m->status), s);
   if (rc) return rc;
   if (lm_mode == NE_LM_NONE) return NE_OK;
   ne::Epilogue el{};
@@ -475,7 +525,12 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
   el.index_offset = c.lm_offset;
   rc = note(m, NE_K_LM_HEAD, run_gemm(m, &m->tm_lm, &m->tm_x, lm_max, rows->lm_count, c.lm_rows, H, el, s), s);
   if (rc) return rc;
-  if (tp) {  // the vocabulary is split: the largest key over the ranks is the argmax
+  if (px) {  // the vocabulary is split: the largest key over the ranks is the argmax
+    rc = note(m, NE_K_COLLECTIVE, ne::launch_tp_keys_exchange(m->keys, rows->lm_count, lm_max, m->link, m->status, s),
+              s);
+    if (rc) return rc;
+    ++m->launches;  // (our kernel, unlike the NCCL collectives)
+  } else if (tp) {
     rc = note(m, NE_K_COLLECTIVE, ne::tp_allreduce_max_u64(m->keys, (size_t)lm_max, m->tp_comm, s), s);
     if (rc) return rc;
   }

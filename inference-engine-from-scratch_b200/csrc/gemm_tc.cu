@@ -203,6 +203,21 @@ __device__ void epilogue_rows(const Epilogue& e, int tile_n, int m_begin, int co
       const float4 a = lds_f4(acc_s + (uint32_t)((m * GEMM_BM + c) * 4));
       *reinterpret_cast<float4*>(e.out_f32 + (long long)(m_begin + m) * e.ldo + n0 + c) = a;
     }
+  } else if (MODE == EPI_PUSH_F32) {
+    // unit = 4 consecutive fp32 outputs of one row, stored to every rank's slot [parity][own rank]
+    // (the world's stores of a unit issued together; the parity is the exchange count's)
+    const TpLink& l = e.link;
+    const unsigned par = __ldcg(l.instance) & 1u;
+    const size_t slot = ((size_t)par * l.world + l.rank) * l.max_rows * (size_t)l.hidden;
+    const int units = count * (GEMM_BM / 4);
+    for (int u = tid; u < units; u += GEMM_THREADS) {
+      const int m = u >> 5, c = (u & 31) * 4;
+      const float4 a = lds_f4(acc_s + (uint32_t)((m * GEMM_BM + c) * 4));
+      const size_t off = slot + (size_t)(m_begin + m) * l.hidden + n0 + c;
+#pragma unroll
+      for (int r = 0; r < TP_MAX_WORLD; ++r)
+        if (r < l.world) *reinterpret_cast<float4*>(l.rows[r] + off) = a;
+    }
   } else if (MODE == EPI_SWIGLU) {
     // unit = 8 consecutive features j of one row: gate rows j, up rows 64 + j of the tile
     const int units = count * 8;
@@ -500,6 +515,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_fence_after();
       tmem_dealloc(tmem_base, tmem_cols);
     }
+    if (MODE == EPI_PUSH_F32) tp_signal_cta(p.epi.link);  // every CTA counts, rows or not
     return;
   }
 
@@ -710,6 +726,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   }
 
+  // every CTA signals, whatever its rows and even after a timeout, so that no peer waits on it
+  if (MODE == EPI_PUSH_F32) tp_signal_cta(p.epi.link);
+
   // ------------------------------------------------------------------ teardown
   if (!ok && warp == 0 && lane == 0) {
     // drain our own TMA copies still in flight (bounded) before the shared memory goes away
@@ -815,7 +834,7 @@ int active_clusters_mode(int splits, int smem) {
   X(EPI_STORE, 0) X(EPI_STORE, CONV_W8) X(EPI_RESIDUAL, 0) X(EPI_RESIDUAL, CONV_W8) X(EPI_SWIGLU, 0)   \
   X(EPI_SWIGLU, CONV_W8) X(EPI_SWIGLU, CONV_NX) X(EPI_SWIGLU, CONV_W8 | CONV_NX) X(EPI_QKV, 0)          \
   X(EPI_QKV, CONV_W8) X(EPI_QKV, CONV_NX) X(EPI_QKV, CONV_W8 | CONV_NX) X(EPI_ARGMAX, 0) X(EPI_LOGITS, 0) \
-  X(EPI_STORE_F32, 0)
+  X(EPI_STORE_F32, 0) X(EPI_PUSH_F32, 0)
 
 int conv_bits(const GemmParams& p) { return (p.w_scale ? CONV_W8 : 0) | (p.x_norm_w ? CONV_NX : 0); }
 

@@ -19,6 +19,7 @@
 #include <cuda.h>
 
 #include "common.cuh"
+#include "tp.cuh"
 
 namespace ne {
 
@@ -44,6 +45,8 @@ enum EpilogueMode : int {
   EPI_ARGMAX = 4,    // per-row max over the vocab tile into a 64-bit atomicMax key
   EPI_LOGITS = 5,    // out[m, n] = bf16(y) (vocab row width) plus the argmax key
   EPI_STORE_F32 = 6, // out_f32[m, n] = y (fp32 partial sums of a row-parallel shard, for an all-reduce)
+  EPI_PUSH_F32 = 7,  // y (fp32 partial sums) stored into every rank's exchange slot over NVLink, then
+                     // each CTA signals every rank (peer exchange of a tensor-parallel split)
 };
 
 struct Epilogue {
@@ -79,6 +82,8 @@ struct Epilogue {
   // rows, [M, ssq_tiles] (the RMSNorm statistics the next GEMM's normalised X operand needs)
   float* ssq_out;
   int ssq_tiles;
+  // EPI_PUSH_F32: the exchange regions of all ranks (ldo = hidden)
+  TpLink link;
 };
 
 // Operand conversions done in shared memory by the converter warps (4-7) between TMA and MMA.

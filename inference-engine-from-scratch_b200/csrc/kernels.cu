@@ -1,6 +1,8 @@
 // Non-GEMM kernels of the speculative step: embedding gather, RMSNorm, paged verify attention,
 // n-gram drafting, step planning (block reservation + row metadata), greedy acceptance + commit,
 // and the device-side free-block FIFO.
+#include <algorithm>
+
 #include "kernels.cuh"
 
 namespace ne {
@@ -54,7 +56,7 @@ template <int CPL>
 __global__ void rmsnorm_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                                __nv_bfloat16* __restrict__ y, int max_rows, const int32_t* rows_dev,
                                const int32_t* gather, int hidden, float eps, unsigned long long* zero_keys,
-                               const float* __restrict__ add) {
+                               const float* __restrict__ add, const TpLink link, int* status) {
   pdl_trigger();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -64,44 +66,66 @@ __global__ void rmsnorm_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat1
   for (int j = 0; j < CPL; ++j) wv[j] = wr[lane + 32 * j];
   pdl_wait();
   const int n = rows_dev ? min(*rows_dev, max_rows) : max_rows;
-  if (row >= n) return;
-  const int src = gather ? gather[row] : row;
-  uint4* xr = reinterpret_cast<uint4*>(x + (long long)src * hidden);
-  uint4 u[CPL];
+  // peer exchange: every CTA waits for the sources, reads its rows' slots, and counts itself done
+  const bool exch = link.world > 0;
+  const unsigned inst = exch ? tp_wait_all(link, status) : 0u;
+  if (row < n) {
+    const int src = gather ? gather[row] : row;
+    uint4* xr = reinterpret_cast<uint4*>(x + (long long)src * hidden);
+    uint4 u[CPL];
 #pragma unroll
-  for (int j = 0; j < CPL; ++j) u[j] = xr[lane + 32 * j];
-  float ss = 0.f;
+    for (int j = 0; j < CPL; ++j) u[j] = xr[lane + 32 * j];
+    float ss = 0.f;
 #pragma unroll
-  for (int j = 0; j < CPL; ++j) {
-    __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&u[j]);
-    if (add) {  // residual update first: x = bf16(x + bf16(add)) (the all-reduced projection)
-      const float4* ar = reinterpret_cast<const float4*>(add + (long long)src * hidden + (lane + 32 * j) * 8);
-      const float4 a0 = ar[0], a1 = ar[1];
-      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    for (int j = 0; j < CPL; ++j) {
+      __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&u[j]);
+      if (add || exch) {
+        // residual update first: x = bf16(x + bf16(sum of the ranks' partials)), the sum in rank
+        // order (an all-reduced buffer, or the exchange slots of the current parity)
+        float av[8];
+        if (exch) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) e[k] = __float2bfloat16_rn(__bfloat162float(e[k]) + bf16r(av[k]));
-      xr[lane + 32 * j] = u[j];
+          for (int k = 0; k < 8; ++k) av[k] = 0.f;
+          for (int q = 0; q < link.world; ++q) {
+            const float4* ar = reinterpret_cast<const float4*>(tp_row_slot(link, inst & 1u, q, src) +
+                                                               (lane + 32 * j) * 8);
+            const float4 a0 = __ldcg(ar), a1 = __ldcg(ar + 1);
+            av[0] += a0.x; av[1] += a0.y; av[2] += a0.z; av[3] += a0.w;
+            av[4] += a1.x; av[5] += a1.y; av[6] += a1.z; av[7] += a1.w;
+          }
+        } else {
+          const float4* ar = reinterpret_cast<const float4*>(add + (long long)src * hidden + (lane + 32 * j) * 8);
+          const float4 a0 = ar[0], a1 = ar[1];
+          av[0] = a0.x; av[1] = a0.y; av[2] = a0.z; av[3] = a0.w;
+          av[4] = a1.x; av[5] = a1.y; av[6] = a1.z; av[7] = a1.w;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) e[k] = __float2bfloat16_rn(__bfloat162float(e[k]) + bf16r(av[k]));
+        xr[lane + 32 * j] = u[j];
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float f = __bfloat162float(e[k]);
+        ss += f * f;
+      }
     }
+    ss = warp_sum(ss);
+    const float r = 1.0f / sqrtf(ss / (float)hidden + eps);
+    uint4* yr = reinterpret_cast<uint4*>(y + (long long)row * hidden);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float f = __bfloat162float(e[k]);
-      ss += f * f;
+    for (int j = 0; j < CPL; ++j) {
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u[j]);
+      const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv[j]);
+      uint4 o;
+      __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        oe[k] = __float2bfloat16_rn(bf16r(__bfloat162float(e[k]) * r) * __bfloat162float(we[k]));
+      yr[lane + 32 * j] = o;
     }
+    if (zero_keys && lane == 0) zero_keys[row] = 0ull;
   }
-  ss = warp_sum(ss);
-  const float r = 1.0f / sqrtf(ss / (float)hidden + eps);
-  uint4* yr = reinterpret_cast<uint4*>(y + (long long)row * hidden);
-#pragma unroll
-  for (int j = 0; j < CPL; ++j) {
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u[j]);
-    const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv[j]);
-    uint4 o;
-    __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&o);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) oe[k] = __float2bfloat16_rn(bf16r(__bfloat162float(e[k]) * r) * __bfloat162float(we[k]));
-    yr[lane + 32 * j] = o;
-  }
-  if (zero_keys && lane == 0) zero_keys[row] = 0ull;
+  if (exch) tp_reader_done(link, inst);
 }
 
 __global__ void keys_to_ids_kernel(const unsigned long long* keys, const int32_t* count, int max_count,
@@ -110,6 +134,34 @@ __global__ void keys_to_ids_kernel(const unsigned long long* keys, const int32_t
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   const int n = count ? min(*count, max_count) : max_count;
   if (i < n) ids[i] = (int32_t)argmax_key_index(keys[i]);
+}
+
+// Argmax keys of a vocabulary-split LM head: every rank pushes its per-row maxima into every
+// rank's key slot [parity][own rank], signals, waits for all ranks and keeps the largest key per
+// row (the ordered value with the lowest index on ties, as over the whole vocabulary).
+__global__ void tp_keys_exchange_kernel(unsigned long long* keys, const int32_t* count, int max_count,
+                                        const TpLink link, int* status) {
+  pdl_prologue();
+  const int n = count ? min(*count, max_count) : max_count;
+  const unsigned inst = __ldcg(link.instance);
+  const unsigned par = inst & 1u;
+  const size_t own = ((size_t)par * link.world + link.rank) * link.max_rows;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const unsigned long long k = keys[i];
+    for (int r = 0; r < link.world; ++r) link.keys[r][own + i] = k;
+  }
+  __syncthreads();
+  if ((int)threadIdx.x < link.world) tp_signal(link, (int)threadIdx.x, TP_QUANTUM);
+  if ((int)threadIdx.x < link.world)
+    tp_wait_source(link, (int)threadIdx.x, (unsigned long long)(inst + 1u) * TP_QUANTUM, status);
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    unsigned long long best = 0ull;
+    for (int q = 0; q < link.world; ++q)
+      best = max(best, __ldcg(link.keys[link.rank] + ((size_t)par * link.world + q) * link.max_rows + i));
+    keys[i] = best;
+  }
+  tp_reader_done(link, inst);
 }
 
 // ------------------------------------------------------------------ n-gram drafts
@@ -448,24 +500,37 @@ int launch_embed(const __nv_bfloat16* embed, const int32_t* tokens, const int32_
 
 int launch_rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int max_rows,
                    const int32_t* rows_dev, const int32_t* gather, int hidden, float eps,
-                   unsigned long long* zero_keys, cudaStream_t stream, const float* add) {
-  const int blocks = (max_rows + 3) / 4;
+                   unsigned long long* zero_keys, cudaStream_t stream, const float* add, const TpLink* link,
+                   int* status) {
+  if (link && (link->world < 1 || link->hidden != hidden || max_rows > link->max_rows || add)) return NE_ERR_INVALID;
+  // a reader launch runs even without rows: it closes the exchange its writer opened
+  const int blocks = std::max((max_rows + 3) / 4, link ? 1 : 0);
   if (blocks == 0) return NE_OK;
+  const TpLink lk = link ? *link : TpLink{};
   cudaError_t err;
   switch (hidden) {  // 256 x chunks per lane
-    case 1024: err = launch_kernel(rmsnorm_kernel<4>, dim3(blocks), dim3(128), 0, stream, x, w, y, max_rows, rows_dev,
-                                   gather, hidden, eps, zero_keys, add); break;
-    case 2048: err = launch_kernel(rmsnorm_kernel<8>, dim3(blocks), dim3(128), 0, stream, x, w, y, max_rows, rows_dev,
-                                   gather, hidden, eps, zero_keys, add); break;
-    case 4096: err = launch_kernel(rmsnorm_kernel<16>, dim3(blocks), dim3(128), 0, stream, x, w, y, max_rows, rows_dev,
-                                   gather, hidden, eps, zero_keys, add); break;
-    case 256: err = launch_kernel(rmsnorm_kernel<1>, dim3(blocks), dim3(128), 0, stream, x, w, y, max_rows, rows_dev,
-                                  gather, hidden, eps, zero_keys, add); break;
-    case 512: err = launch_kernel(rmsnorm_kernel<2>, dim3(blocks), dim3(128), 0, stream, x, w, y, max_rows, rows_dev,
-                                  gather, hidden, eps, zero_keys, add); break;
+#define NE_NORM_CASE(H, CPL)                                                                                   \
+  case H:                                                                                                      \
+    err = launch_kernel(rmsnorm_kernel<CPL>, dim3(blocks), dim3(128), 0, stream, x, w, y, max_rows, rows_dev,  \
+                        gather, hidden, eps, zero_keys, add, lk, status);                                      \
+    break;
+    NE_NORM_CASE(256, 1)
+    NE_NORM_CASE(512, 2)
+    NE_NORM_CASE(1024, 4)
+    NE_NORM_CASE(2048, 8)
+    NE_NORM_CASE(4096, 16)
+#undef NE_NORM_CASE
     default: return NE_ERR_UNSUPPORTED;  // hidden sizes other than 256 x {1, 2, 4, 8, 16}
   }
   return err == cudaSuccess ? NE_OK : NE_ERR_CUDA;
+}
+
+int launch_tp_keys_exchange(unsigned long long* keys, const int32_t* count, int max_count, const TpLink& link,
+                            int* status, cudaStream_t stream) {
+  if (link.world < 1 || max_count > link.max_rows) return NE_ERR_INVALID;
+  if (max_count <= 0) return NE_OK;
+  return launch_kernel(tp_keys_exchange_kernel, dim3(1), dim3(256), 0, stream, keys, count, max_count, link,
+                       status) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 
 int launch_keys_to_ids(const unsigned long long* keys, const int32_t* count, int max_count, int32_t* ids,

@@ -88,4 +88,60 @@ int tp_allreduce_max_u64(unsigned long long* buf, size_t count, void* comm, cuda
              : NE_ERR_CUDA;
 }
 
+TpRegionLayout tp_region_layout(int world, int max_rows, int hidden) {
+  TpRegionLayout l{};
+  l.rows = 0;
+  l.keys = 2ull * world * max_rows * hidden * sizeof(float);
+  l.counters = (l.keys + 2ull * world * max_rows * sizeof(unsigned long long) + 255) & ~(size_t)255;
+  l.total = l.counters + 256;
+  return l;
+}
+
+TpLink tp_make_link(void* const* bases, int world, int rank, int max_rows, int hidden) {
+  const TpRegionLayout lay = tp_region_layout(world, max_rows, hidden);
+  TpLink l{};
+  for (int r = 0; r < world; ++r) {
+    char* b = static_cast<char*>(bases[r]);
+    l.rows[r] = reinterpret_cast<float*>(b + lay.rows);
+    l.keys[r] = reinterpret_cast<unsigned long long*>(b + lay.keys);
+    l.arrivals[r] = reinterpret_cast<unsigned long long*>(b + lay.counters);
+  }
+  char* own = static_cast<char*>(bases[rank]) + lay.counters + TP_MAX_WORLD * sizeof(unsigned long long);
+  l.instance = reinterpret_cast<unsigned int*>(own);
+  l.done = reinterpret_cast<unsigned int*>(own + 4);
+  l.world = world;
+  l.rank = rank;
+  l.max_rows = max_rows;
+  l.hidden = hidden;
+  return l;
+}
+
+int tp_exchange_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == TP_HANDLE_BYTES, "CUDA IPC handle size");
+  if (!ptr || !ipc_handle) return NE_ERR_INVALID;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return NE_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return NE_ERR_CUDA;
+  }
+  memcpy(ipc_handle, &h, sizeof(h));
+  *ptr = p;
+  return NE_OK;
+}
+
+int tp_exchange_open(const void* ipc_handle, void** ptr) {
+  if (!ipc_handle || !ptr) return NE_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
+}
+
+void tp_exchange_close(void* ptr, bool own) {
+  if (!ptr) return;
+  if (own) cudaFree(ptr);
+  else cudaIpcCloseMemHandle(ptr);
+}
+
 }  // namespace ne

@@ -156,6 +156,9 @@ class B200Model:
             uid = ctypes.create_string_buffer(tp.unique_id, 128)
             _lib.check(self.lib.ne_model_set_tp(handle, tp.nccl_library.encode(), tp.rank, tp.world, uid),
                        "ne_model_set_tp")
+        from .tp import open_exchange
+
+        self.peer_exchange = tp is not None and open_exchange(self.lib, handle, tp, max_rows)
         self._layer_structs = []
         for layer, w in enumerate(self.layers):
             lw = _lib.LayerWeights(
@@ -225,12 +228,20 @@ class B200Model:
             raise _lib.NativeError(f"device reported: {_lib.describe_device_status(word)} (0x{word:x})")
 
     def close(self) -> None:
+        """Destroy the native model. A split model with a peer exchange is collective here: every
+        rank's kernels must be done before any rank frees its exchange region."""
         if getattr(self, "handle", None) is not None and self.handle.value:
+            if getattr(self, "peer_exchange", False):
+                from .tp import quiesce
+
+                quiesce(self.device)
             self.lib.ne_model_destroy(self.handle)
             self.handle = ctypes.c_void_p()
 
     def __del__(self) -> None:
         try:
+            if getattr(self, "peer_exchange", False):
+                return  # never free an exchange region without the collective close()
             self.close()
         except Exception:
             pass

@@ -8,9 +8,12 @@ One process per GPU. Rank r holds:
 * a contiguous run of whole 128-row tiles of the LM head (the vocabulary split as evenly as the
   1,187 tiles of 151,936 allow); embedding and norms whole.
 
-The row-parallel outputs (o_proj, down_proj) are fp32 partial sums, added by an NCCL all-reduce
-before the residual update (``ne_model_set_tp`` in include/nespec.h); the argmax keys of the
-vocabulary shards are max-reduced. Random-init weights for the big shape are drawn on the GPU one
+The row-parallel outputs (o_proj, down_proj) are fp32 partial sums. For steps of up to
+``exchange_rows`` rows the GEMM stores them straight into every rank's exchange region over NVLink
+and the next RMSNorm launch sums them (``ne_model_tp_exchange_create`` / ``_open`` in
+include/nespec.h); larger steps add them with an NCCL all-reduce (``ne_model_set_tp``). Either
+way the sum joins the residual stream before the norm, and the argmax keys of the vocabulary
+shards are max-reduced. Random-init weights for the big shape are drawn on the GPU one
 tensor at a time from a per-tensor seed, so every rank (and an unsplit run) sees the same full
 tensors and keeps only its shard.
 """
@@ -34,6 +37,9 @@ class TensorParallel:
     world: int
     unique_id: bytes  # 128 bytes from ne_tp_unique_id on rank 0, the same on every rank
     nccl_library: str
+    # steps of up to this many rows exchange partial rows through peer memory (0: NCCL only);
+    # needs torch.distributed initialised (the IPC handles are gathered over it)
+    exchange_rows: int = 512
 
 
 @dataclass(frozen=True)
@@ -150,3 +156,35 @@ def nccl_library_path() -> str:
     if path is None:
         raise RuntimeError("no NCCL library found next to PyTorch (nvidia.nccl)")
     return path
+
+
+def open_exchange(lib, handle, tp: TensorParallel, max_rows: int) -> bool:
+    """Create this rank's exchange region, gather every rank's IPC handle over torch.distributed
+    and map the peers' regions (collective: every rank calls it with the same ``max_rows``)."""
+    import torch.distributed as dist
+
+    rows = min(tp.exchange_rows, max_rows)
+    if tp.world < 2 or rows <= 0:
+        return False
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() != tp.world:
+        raise RuntimeError("the peer exchange gathers IPC handles over torch.distributed: initialise it first")
+    buf = (ctypes.c_char * _lib.TP_HANDLE_BYTES)()
+    _lib.check(lib.ne_model_tp_exchange_create(handle, rows, buf), "ne_model_tp_exchange_create")
+    gathered: list = [None] * tp.world
+    dist.all_gather_object(gathered, bytes(buf))
+    if dist.get_rank() != tp.rank:
+        raise RuntimeError(f"torch.distributed rank {dist.get_rank()} is not the split's rank {tp.rank}")
+    joined = b"".join(gathered)
+    _lib.check(lib.ne_model_tp_exchange_open(handle, ctypes.create_string_buffer(joined, len(joined))),
+               "ne_model_tp_exchange_open")
+    return True
+
+
+def quiesce(device) -> None:
+    """Every rank's work on a split model finished (the peers write into this rank's exchange
+    region): synchronise, then a barrier. Call before destroying a model with an open exchange."""
+    import torch.distributed as dist
+
+    torch.cuda.synchronize(device)
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier()

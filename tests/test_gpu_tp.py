@@ -1,4 +1,5 @@
-"""Tensor parallelism on 2 GPUs: a split model serves exactly what the unsplit model serves.
+"""Tensor parallelism on 2 GPUs: a split model serves exactly what the unsplit model serves, over
+the peer exchange and over NCCL, and a rank left alone reports a timeout instead of hanging.
 
 Skipped on a host with fewer than two GPUs. The ranks run as child processes under torchrun
 (tests/tp_worker.py) with NVLS off, bounded by a timeout.
@@ -38,8 +39,13 @@ def test_two_rank_split_serves_the_unsplit_outputs(tmp_path) -> None:
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
     r0 = json.loads((tmp_path / "rank.0.json").read_text())
     r1 = json.loads((tmp_path / "rank.1.json").read_text())
-    # both ranks take the same decisions (max-reduced argmax keys), eagerly and through graphs
-    assert r0["eager"] == r1["eager"] == r0["graphs"] == r1["graphs"]
+    assert r0["peer_exchange"] and r1["peer_exchange"]
+    # both ranks take the same decisions (max-reduced argmax keys), eagerly and through graphs,
+    # over the peer exchange, the exchange for steps only, and NCCL only
+    for name in ("eager", "graphs", "mixed", "nccl"):
+        assert r0[name] == r1[name] == r0["graphs"], name
     # and they equal the unsplit model's tokens (fp32 partial sums: only the summation order differs)
     assert r0["graphs"] == r0["unsplit"]
     assert all(len(o) == 32 for o in r0["unsplit"])
+    # a rank whose peer launches nothing: its exchange waits end (bounded) with the timeout status
+    assert "bounded device wait ran out" in r0["lone_rank"], r0["lone_rank"]

@@ -1,8 +1,11 @@
 """One rank of the tensor-parallel GPU test (launched by tests/test_gpu_tp.py under torchrun).
 
 Every rank serves the same prompts on its shard of a small Qwen3-8B-like model (TP = world size,
-greedy, CUDA graphs); rank 0 then serves them again on the unsplit model (TP = 1, the oracle for
-the split: the same seeded weights). Each rank writes its outputs to ``<out>.<rank>.json``.
+greedy): with the peer exchange for every call (eagerly and through CUDA graphs), with the
+exchange for the steps only (prefill through NCCL), and through NCCL only. Then rank 0 prefills
+alone on a split model, so that its bounded exchange waits run out. Rank 0 finally serves the
+prompts on the unsplit model (TP = 1, the oracle for the split: the same seeded weights). Each rank
+writes its outputs to ``<out>.<rank>.json``.
 """
 
 from __future__ import annotations
@@ -49,17 +52,43 @@ def main() -> None:
     submodule("build").build()
     cfg = pkg.Qwen3Config(**SMALL_TP)
     lib_path = tp.nccl_library_path()
-    box = [tp.unique_id(lib_path) if rank == 0 else None]
-    dist.broadcast_object_list(box, src=0)
     plan = tp.shard_plan(cfg, rank, world)
     weights = tp.make_sharded_weights(cfg, plan, seed=0, device=device)
     prompts = pkg.make_prompts(4, cfg.vocab_size, length=48, seed=1)
     result = {"rank": rank, "plan": [plan.q_heads, plan.kv_heads, plan.inter, plan.vocab]}
-    model = model_mod.B200Model(tp.rank_config(cfg, plan), weights, num_slots=128 * 16, device=device,
-                                max_positions=512, max_rows=512, max_seqs=4,
-                                tp=tp.TensorParallel(rank, world, box[0], lib_path), lm_offset=plan.vocab[0])
+
+    def split_model(exchange_rows: int):
+        box = [tp.unique_id(lib_path) if rank == 0 else None]  # one NCCL id per communicator
+        dist.broadcast_object_list(box, src=0)
+        return model_mod.B200Model(tp.rank_config(cfg, plan), weights, num_slots=128 * 16, device=device,
+                                   max_positions=512, max_rows=512, max_seqs=4,
+                                   tp=tp.TensorParallel(rank, world, box[0], lib_path, exchange_rows=exchange_rows),
+                                   lm_offset=plan.vocab[0])
+
+    # peer exchange for every call (prefill of 192 rows and the steps)
+    model = split_model(512)
+    result["peer_exchange"] = model.peer_exchange
     result["eager"] = serve(model, prompts, graphs=False)
     result["graphs"] = serve(model, prompts, graphs=True)
+    model.close()
+    # prefill through NCCL (192 rows > 64), steps (20 rows) through the exchange; then NCCL only
+    for name, rows in (("mixed", 64), ("nccl", 0)):
+        model = split_model(rows)
+        result[name] = serve(model, prompts, graphs=True)
+        model.close()
+    # a rank that stops taking part: rank 0 prefills alone, its bounded waits run out (1 s per
+    # exchange) and the device status reports the timeout; rank 1 launches nothing
+    model = split_model(512)
+    if rank == 0:
+        eng = submodule("engine").B200SpeculativeEngine(model, k=4, max_ngram=3, max_seqs=4, max_model_len=256,
+                                                        num_blocks=96, cuda_graphs=False)
+        slot = eng.add_request(prompts[0], 8, ignore_eos=True)
+        try:
+            eng.prefill([slot])
+            result["lone_rank"] = "no error"
+        except Exception as exc:  # NativeError naming the device status
+            result["lone_rank"] = str(exc)
+        del eng
     model.close()
     if rank == 0:
         whole_plan = tp.shard_plan(cfg, 0, 1)
