@@ -46,6 +46,8 @@ struct ne_model {
   int tp_exchange_rows = 0;
   void* tp_peer[ne::TP_MAX_WORLD] = {};
   ne::TpLink link{};         // link.world > 0 once every peer region is open
+  float* split = nullptr;    // fp32 split-K partials of the residual GEMMs (split_rows x H)
+  long long split_rows = 0;
   float* ssq = nullptr;      // fp32 [max_rows, H / 128]: residual rows' sums of squares per 128-wide tile
   CUtensorMap tm_h{};        // the residual rows as a GEMM X operand (RMSNorm fused into the GEMM)
   CUtensorMap tm_x{}, tm_attn{}, tm_act{};
@@ -75,8 +77,12 @@ size_t sampling_logits_bytes(const ne_model_config& c, int rows) {
   return align256((size_t)rows * c.vocab_size * 2);
 }  // split-KV partials (few sequences, long contexts)
 
+// Split-K partials of o_proj / down_proj left for the next RMSNorm: room for GEMM_MAX_SPLITS
+// slices of up to 512 rows (verify steps; larger steps run unsplit or keep the in-GEMM reduction).
+size_t split_rows_cap(int R) { return (size_t)ne::GEMM_MAX_SPLITS * std::min(R, 512); }
+
 struct Layout {
-  size_t status, h, x, q, attn, act, keys, rows_i32, seqs_i32, scalars, attn_scratch, partial, ssq, total;
+  size_t status, h, x, q, attn, act, keys, rows_i32, seqs_i32, scalars, attn_scratch, partial, split, ssq, total;
 };
 
 Layout workspace_layout(const ne_model_config& c, int R, int B, int tp_world) {
@@ -100,6 +106,7 @@ Layout workspace_layout(const ne_model_config& c, int R, int B, int tp_world) {
   l.scalars = take(64);                   // num_rows, lm_count
   l.attn_scratch = take(ATTN_SCRATCH_BYTES);
   l.partial = tp_world > 1 ? take((size_t)R * c.hidden_size * 4) : 0;
+  l.split = tp_world > 1 ? 0 : take(split_rows_cap(R) * c.hidden_size * 4);
   l.ssq = take((size_t)R * (c.hidden_size / 128) * 4);
   l.total = off;
   return l;
@@ -166,6 +173,50 @@ int run_gemm(ne_model* m, const CUtensorMap* tw, const CUtensorMap* tx, int M_ma
   int rc = ne::gemm_plan(p, m->num_sms);
   if (rc != NE_OK) return rc;
   return ne::gemm_launch(tw, tx, p, stream);
+}
+
+// Split-K partials of the residual GEMMs summed by the next RMSNorm (default); NE_SPLIT_PARTIALS=0
+// keeps the reduction inside the GEMM (cluster exchange, then the residual epilogue).
+bool split_partials_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("NE_SPLIT_PARTIALS");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+// o_proj / down_proj of an unsplit model: out = h + bf16(X W^T). Split over K, the partial tiles
+// stay in m->split for the next RMSNorm to add (*splits = the slice count); unsplit (or when the
+// slices do not fit) the GEMM adds to h itself (*splits = 0).
+int residual_gemm(ne_model* m, const CUtensorMap* tw, const CUtensorMap* tx, int R, const int32_t* M_dev, int N, int K,
+                  cudaStream_t stream, const void* w_scale, int* splits) {
+  *splits = 0;
+  GemmParams p{};
+  p.w_scale = static_cast<const __nv_bfloat16*>(w_scale);
+  p.M_max = R;
+  p.M_dev = M_dev;
+  p.N = N;
+  p.K = K;
+  p.status = m->status;
+  p.epi.status = m->status;
+  p.epi.ldo = N;
+  if (m->split && split_partials_enabled()) {
+    p.epi.mode = ne::EPI_SPLIT_F32;
+    p.epi.out_f32 = m->split;
+    p.epi.split_stride = (long long)R * N;
+    int rc = ne::gemm_plan(p, m->num_sms);
+    if (rc != NE_OK) return rc;
+    if (p.splits > 1 && (long long)p.splits * R <= m->split_rows) {
+      *splits = p.splits;
+      return ne::gemm_launch(tw, tx, p, stream);
+    }
+  }
+  ne::Epilogue e{};
+  e.mode = ne::EPI_RESIDUAL;
+  e.status = m->status;
+  e.out = m->h;
+  e.ldo = N;
+  return run_gemm(m, tw, tx, R, M_dev, N, K, e, stream, w_scale);
 }
 
 ne_rows make_step_rows(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int max_rows,
@@ -327,6 +378,8 @@ int ne_model_set_workspace(ne_model* m, void* ws, size_t bytes, int max_rows, in
   m->attn_scratch = base + l.attn_scratch;
   m->attn_scratch_bytes = ATTN_SCRATCH_BYTES;
   m->partial = m->tp_world > 1 ? reinterpret_cast<float*>(base + l.partial) : nullptr;
+  m->split = m->tp_world > 1 ? nullptr : reinterpret_cast<float*>(base + l.split);
+  m->split_rows = m->tp_world > 1 ? 0 : (long long)split_rows_cap(max_rows);
   m->ssq = reinterpret_cast<float*>(base + l.ssq);
   const int qs = c.num_heads * 128;
   bool ok = ne::make_tmap_bf16(&m->tm_x, m->x, max_rows, c.hidden_size, ne::GEMM_XBOX, ne::GEMM_BK) &&
@@ -411,6 +464,9 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
   // RMSNorm folded into the QKV and gate/up GEMMs (statistics from the producing epilogue); a
   // split model adds the all-reduced projections in the RMSNorm launch instead
   const bool fuse = !tp && fused_norm_enabled();
+  // the unsplit model's residual GEMMs may leave split-K partials for the next RMSNorm
+  const bool split_res = !tp && !fuse;
+  int pending = 0;  // slices of m->split the next RMSNorm adds to the residual stream
   cudaStream_t s = as_stream(stream);
   const int H = c.hidden_size, I = c.intermediate_size, qs = c.num_heads * 128, kvs = c.num_kv_heads * 128;
   const __nv_bfloat16* embed = static_cast<const __nv_bfloat16*>(m->head.embed);
@@ -430,8 +486,9 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
     if (!fuse) {
       rc = note(m, NE_K_RMSNORM,
                 ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(w.ln_in), m->x, R, rows->num_rows, nullptr,
-                                   H, c.rms_norm_eps, nullptr, s, l > 0 ? nccl_add : nullptr, l > 0 ? lk : nullptr,
-                                   m->status), s);
+                                   H, c.rms_norm_eps, nullptr, s, pending ? m->split : l > 0 ? nccl_add : nullptr,
+                                   pending ? pending : 1, (long long)R * H, l > 0 ? lk : nullptr, m->status), s);
+      pending = 0;
       if (rc) return rc;
     }
     ne::Epilogue e{};
@@ -472,7 +529,9 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
     eo.ldo = H;
     eo.ssq_out = fuse ? m->ssq : nullptr;
     eo.ssq_tiles = H / 128;
-    rc = note(m, NE_K_GEMM_O, run_gemm(m, &m->tm_o[l], &m->tm_attn, R, rows->num_rows, H, qs, eo, s, w.w_o_scale), s);
+    rc = note(m, NE_K_GEMM_O,
+              split_res ? residual_gemm(m, &m->tm_o[l], &m->tm_attn, R, rows->num_rows, H, qs, s, w.w_o_scale, &pending)
+                        : run_gemm(m, &m->tm_o[l], &m->tm_attn, R, rows->num_rows, H, qs, eo, s, w.w_o_scale), s);
     if (rc) return rc;
     if (tp && !px) {
       rc = note(m, NE_K_COLLECTIVE, ne::tp_allreduce_sum_f32(m->partial, (size_t)R * H, m->tp_comm, s), s);
@@ -481,7 +540,9 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
     if (!fuse) {
       rc = note(m, NE_K_RMSNORM,
                 ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(w.ln_post), m->x, R, rows->num_rows,
-                                   nullptr, H, c.rms_norm_eps, nullptr, s, nccl_add, lk, m->status), s);
+                                   nullptr, H, c.rms_norm_eps, nullptr, s, pending ? m->split : nccl_add,
+                                   pending ? pending : 1, (long long)R * H, lk, m->status), s);
+      pending = 0;
       if (rc) return rc;
     }
     ne::Epilogue eg{};
@@ -501,7 +562,10 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
     ed.ldo = H;
     ed.ssq_out = fuse ? m->ssq : nullptr;
     ed.ssq_tiles = H / 128;
-    rc = note(m, NE_K_GEMM_DOWN, run_gemm(m, &m->tm_down[l], &m->tm_act, R, rows->num_rows, H, I, ed, s, w.w_down_scale), s);
+    rc = note(m, NE_K_GEMM_DOWN,
+              split_res ? residual_gemm(m, &m->tm_down[l], &m->tm_act, R, rows->num_rows, H, I, s, w.w_down_scale,
+                                        &pending)
+                        : run_gemm(m, &m->tm_down[l], &m->tm_act, R, rows->num_rows, H, I, ed, s, w.w_down_scale), s);
     if (rc) return rc;
     if (tp && !px) {
       rc = note(m, NE_K_COLLECTIVE, ne::tp_allreduce_sum_f32(m->partial, (size_t)R * H, m->tp_comm, s), s);
@@ -512,7 +576,8 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
   const int lm_max = rows->lm_max;
   rc = note(m, NE_K_RMSNORM,
             ne::launch_rmsnorm(m->h, static_cast<const __nv_bfloat16*>(m->head.final_norm), m->x, lm_max,
-                               rows->lm_count, rows->lm_rows, H, c.rms_norm_eps, m->keys, s, nccl_add, lk,
+                               rows->lm_count, rows->lm_rows, H, c.rms_norm_eps, m->keys, s,
+                               pending ? m->split : nccl_add, pending ? pending : 1, (long long)R * H, lk,
                                m->status), s);
   if (rc) return rc;
   if (lm_mode == NE_LM_NONE) return NE_OK;

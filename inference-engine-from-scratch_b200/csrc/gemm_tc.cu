@@ -83,6 +83,34 @@ __device__ __forceinline__ void tmem_to_smem(uint32_t tmem_lane_base, int c0, in
         for (int i = 0; i < 8; ++i) dst[(c + 8 * q + i) * GEMM_BM + row] = __uint_as_float(r[q][i]);
   }
 }
+// EPI_SPLIT_F32: TMEM columns [0, cnt) (tokens) of all 128 lanes (output rows) straight to global
+// ``dst`` [token][ld] fp32: warp w reads lane quarter w % 4, warps w and w + 4 split the tokens;
+// for each token a warp stores 32 consecutive floats (128 coalesced bytes).
+__device__ __forceinline__ void tmem_tile_to_global(uint32_t tmem_base, int cnt, float* dst, long long ld) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q = warp & 3, h = warp >> 2;
+  const int cnt8 = (cnt + 7) & ~7;
+  const int first = ((cnt8 / 2) + 7) & ~7;
+  const int begin = h == 0 ? 0 : first;
+  const int len = h == 0 ? first : cnt8 - first;
+  const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+  float* col = dst + q * 32 + lane;
+  for (int c = 0; c < len; c += 32) {
+    uint32_t r[4][8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (c + 8 * j < len) tmem_ld8_nowait(lane_base + (uint32_t)(begin + c + 8 * j), r[j]);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int t = begin + c + 8 * j + i;
+        if (c + 8 * j < len && t < cnt) col[(long long)t * ld] = __uint_as_float(r[j][i]);
+      }
+  }
+}
+
 __device__ __forceinline__ uint32_t map_peer(uint32_t local_addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
@@ -417,6 +445,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                    const GemmParams p) {
   constexpr bool W8 = (CONV & CONV_W8) != 0;
   constexpr bool NX = (CONV & CONV_NX) != 0;
+  constexpr bool SPLIT_OUT = MODE == EPI_SPLIT_F32;  // split-K partials to global, no cluster
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -500,7 +529,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   int issued = pre;
   if (t_actual <= 0) {
     // no rows for this m-block (the whole cluster shares it): retire the prefetched weight copies
-    if (S > 1) {
+    if (S > 1 && !SPLIT_OUT) {
       if (tid == 0) mbar_arrive(recv_bar);
       cluster_arrive();
       cluster_wait();
@@ -523,7 +552,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   // other splits' partials of those tokens (S - 1 pushes of own_cnt rows)
   const int slice = (((t_actual + S - 1) / S) + 7) & ~7;
   const int own_cnt = max(0, min(slice, t_actual - split * slice));
-  if (S > 1 && tid == 0) mbar_arrive_expect_tx(recv_bar, (uint32_t)((S - 1) * own_cnt * GEMM_BM * 4));
+  if (S > 1 && !SPLIT_OUT && tid == 0) mbar_arrive_expect_tx(recv_bar, (uint32_t)((S - 1) * own_cnt * GEMM_BM * 4));
   const int n_loads = (t_actual + GEMM_XBOX - 1) / GEMM_XBOX;
   const int n_pad = (t_actual + 15) & ~15;
   const int part0 = n_pad < 256 ? n_pad : 256;
@@ -631,7 +660,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   float* stage_acc = reinterpret_cast<float*>(smem);  // pipeline smem is free once ``done`` fired
   const int m_begin = m0;
-  if (S == 1) {
+  if (SPLIT_OUT) {
+    // this split's partial tile to global memory, straight from TMEM (zeros for a split without
+    // K chunks, whose accumulator was never written)
+    float* dst = p.epi.out_f32 + (long long)split * p.epi.split_stride + (long long)m_begin * p.epi.ldo +
+                 tile_n * GEMM_BM;
+    if (ok && nk > 0) {
+      tmem_tile_to_global(tmem_base, t_actual, dst, p.epi.ldo);
+    } else if (ok) {
+      for (int u = tid; u < t_actual * (GEMM_BM / 4); u += GEMM_THREADS)
+        *reinterpret_cast<float4*>(dst + (long long)(u >> 5) * p.epi.ldo + (u & 31) * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    __syncwarp();
+  } else if (S == 1) {
     for (int c0 = 0; c0 < t_actual; c0 += 128) {
       const int cnt = min(128, t_actual - c0);
       if (ok) tmem_tile_to_smem(tmem_base, c0, cnt, stage_acc);
@@ -834,7 +875,7 @@ int active_clusters_mode(int splits, int smem) {
   X(EPI_STORE, 0) X(EPI_STORE, CONV_W8) X(EPI_RESIDUAL, 0) X(EPI_RESIDUAL, CONV_W8) X(EPI_SWIGLU, 0)   \
   X(EPI_SWIGLU, CONV_W8) X(EPI_SWIGLU, CONV_NX) X(EPI_SWIGLU, CONV_W8 | CONV_NX) X(EPI_QKV, 0)          \
   X(EPI_QKV, CONV_W8) X(EPI_QKV, CONV_NX) X(EPI_QKV, CONV_W8 | CONV_NX) X(EPI_ARGMAX, 0) X(EPI_LOGITS, 0) \
-  X(EPI_STORE_F32, 0) X(EPI_PUSH_F32, 0)
+  X(EPI_STORE_F32, 0) X(EPI_PUSH_F32, 0) X(EPI_SPLIT_F32, 0) X(EPI_SPLIT_F32, CONV_W8)
 
 int conv_bits(const GemmParams& p) { return (p.w_scale ? CONV_W8 : 0) | (p.x_norm_w ? CONV_NX : 0); }
 
@@ -906,7 +947,7 @@ int max_stages() {
 int plan_uncached(GemmParams& p, int num_sms) {
   if (p.N % GEMM_BM || p.K % GEMM_BK || p.M_max <= 0) return NE_ERR_INVALID;
   if ((p.w_scale && p.epi.mode != EPI_STORE && p.epi.mode != EPI_RESIDUAL && p.epi.mode != EPI_SWIGLU &&
-       p.epi.mode != EPI_QKV) ||
+       p.epi.mode != EPI_QKV && p.epi.mode != EPI_SPLIT_F32) ||
       (p.x_norm_w && p.epi.mode != EPI_SWIGLU && p.epi.mode != EPI_QKV) ||
       (p.x_norm_w && (!p.x_ssq || p.ssq_tiles <= 0)))
     return NE_ERR_UNSUPPORTED;
@@ -920,7 +961,9 @@ int plan_uncached(GemmParams& p, int num_sms) {
   const int par = n_tiles * (p.M_max > 512 ? m_blocks : 1);
   int S = std::max(1, std::min(max_splits(), num_sms / std::max(1, par)));
   if (p.epi.mode == EPI_ARGMAX || p.epi.mode == EPI_LOGITS) S = 1;
+  const bool split_out = p.epi.mode == EPI_SPLIT_F32;
   auto staging_bytes = [&](int s, int tb) {
+    if (split_out) return 0;  // partial tiles go from TMEM straight to global memory
     if (s == 1) return 128 * GEMM_BM * 4 + 2 * GEMM_MAX_TOKENS * 4;  // accumulator block + epilogue scratch
     const int slice = (((tb + s - 1) / s) + 7) & ~7;
     return (s + 1) * slice * GEMM_BM * 4;
@@ -968,7 +1011,7 @@ int plan_with_occupancy(GemmParams& p, int num_sms) {
   if (rc != NE_OK) return rc;
   const int m_blocks = (p.M_max + p.t_block - 1) / p.t_block;
   const int par = n_tiles * (p.M_max > 512 ? m_blocks : 1);
-  while (p.splits > 1) {
+  while (p.splits > 1 && p.epi.mode != EPI_SPLIT_F32) {  // (split partials need no cluster)
     const int fit = active_clusters(p.epi.mode, conv_bits(p), p.splits, p.smem_data + 256 + GEMM_RSTD_BYTES + 1024);
     if (fit >= par) break;
     const int want = p.splits - 1;
@@ -990,7 +1033,7 @@ int gemm_launch(const CUtensorMap* tm_w, const CUtensorMap* tm_x, const GemmPara
   cfg.stream = stream;
   cudaLaunchAttribute attrs[2];
   attrs[0].id = cudaLaunchAttributeClusterDimension;
-  attrs[0].val.clusterDim.x = p.splits;
+  attrs[0].val.clusterDim.x = p.epi.mode == EPI_SPLIT_F32 ? 1 : p.splits;
   attrs[0].val.clusterDim.y = 1;
   attrs[0].val.clusterDim.z = 1;
   attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -9,6 +9,8 @@
 // the same 128 x T output tile, park their fp32 partial tiles in shared memory, and after a
 // cluster barrier each CTA sums the S partials of its own token slice (in split order, so the
 // result is deterministic) by reading its peers' shared memory (DSMEM). No global scratch.
+// EPI_SPLIT_F32 instead leaves the S partial tiles in global memory straight from TMEM (no
+// cluster, no exchange) for a consumer that reads the rows anyway to add them up.
 //
 // Roles (256 threads): warp 0 lane 0 issues TMA, warp 1 lane 0 issues tcgen05.mma, warp 2 owns
 // the TMEM allocation; with int8 weights warps 4-7 turn each stage's int8 tile into the bf16
@@ -47,6 +49,8 @@ enum EpilogueMode : int {
   EPI_STORE_F32 = 6, // out_f32[m, n] = y (fp32 partial sums of a row-parallel shard, for an all-reduce)
   EPI_PUSH_F32 = 7,  // y (fp32 partial sums) stored into every rank's exchange slot over NVLink, then
                      // each CTA signals every rank (peer exchange of a tensor-parallel split)
+  EPI_SPLIT_F32 = 8, // split-K without the cluster exchange: split s stores its fp32 partial tile to
+                     // out_f32 + s * split_stride; the consumer (the next RMSNorm) sums the splits
 };
 
 struct Epilogue {
@@ -76,8 +80,9 @@ struct Epilogue {
   // EPI_ARGMAX / EPI_LOGITS
   unsigned long long* argmax_keys;  // [M]
   int index_offset;                 // vocabulary id of the tile's first row (LM-head shard offset)
-  // EPI_STORE_F32
+  // EPI_STORE_F32 / EPI_SPLIT_F32 ([splits][M][ldo] fp32, split_stride elements apart)
   float* out_f32;
+  long long split_stride;
   // EPI_RESIDUAL: per (row, 128-wide output tile) fp32 sums of squares of the updated residual
   // rows, [M, ssq_tiles] (the RMSNorm statistics the next GEMM's normalised X operand needs)
   float* ssq_out;

@@ -49,59 +49,72 @@ __global__ void embed_kernel(const __nv_bfloat16* __restrict__ embed, const int3
 }
 
 // ------------------------------------------------------------------ RMSNorm (models/qwen3.py:39-44)
-// fp32 mean of squares, x * rsqrt(var + eps) cast back to bf16, then times the bf16 weight. A warp
-// per row; the row stays in registers (CPL 16-byte chunks per lane, hidden = 256 * CPL), and the
-// weight is read before waiting for the previous kernel (it does not depend on it).
-template <int CPL>
-__global__ void rmsnorm_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+// fp32 mean of squares, x * rsqrt(var + eps) cast back to bf16, then times the bf16 weight. WPR
+// warps per row (4 rows per 128-thread CTA for WPR = 1, one row for WPR = 4), the row in registers
+// (CPL 16-byte chunks per row and lane, hidden = 256 * CPL; a warp holds CPL / WPR of them), the
+// warps' sums of squares added in warp order through shared memory. The weight is read before
+// waiting for the previous kernel (it does not depend on it).
+template <int CPL, int WPR>
+__global__ void __launch_bounds__(128) rmsnorm_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                                __nv_bfloat16* __restrict__ y, int max_rows, const int32_t* rows_dev,
                                const int32_t* gather, int hidden, float eps, unsigned long long* zero_keys,
-                               const float* __restrict__ add, const TpLink link, int* status) {
+                               const float* __restrict__ add, int add_count, long long add_stride,
+                               const TpLink link, int* status) {
+  constexpr int C = CPL / WPR;  // chunks per lane
+  static_assert(CPL % WPR == 0 && 4 % WPR == 0, "warps per row");
+  __shared__ float part_ss[4];
   pdl_trigger();
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int warp = threadIdx.x >> 5;
+  const int row = blockIdx.x * (4 / WPR) + warp / WPR;
   const int lane = threadIdx.x & 31;
-  uint4 wv[CPL];
+  const int c0 = lane + 32 * (warp % WPR) * C;  // this lane's first chunk (chunks 32 apart)
+  uint4 wv[C];
   const uint4* wr = reinterpret_cast<const uint4*>(w);
 #pragma unroll
-  for (int j = 0; j < CPL; ++j) wv[j] = wr[lane + 32 * j];
+  for (int j = 0; j < C; ++j) wv[j] = wr[c0 + 32 * j];
   pdl_wait();
   const int n = rows_dev ? min(*rows_dev, max_rows) : max_rows;
   // peer exchange: every CTA waits for the sources, reads its rows' slots, and counts itself done
   const bool exch = link.world > 0;
   const unsigned inst = exch ? tp_wait_all(link, status) : 0u;
-  if (row < n) {
-    const int src = gather ? gather[row] : row;
-    uint4* xr = reinterpret_cast<uint4*>(x + (long long)src * hidden);
-    uint4 u[CPL];
+  const bool active = row < n;
+  const int src = active ? (gather ? gather[row] : row) : 0;
+  uint4* xr = reinterpret_cast<uint4*>(x + (long long)src * hidden);
+  uint4 u[C];
+  float ss = 0.f;
+  if (active) {
 #pragma unroll
-    for (int j = 0; j < CPL; ++j) u[j] = xr[lane + 32 * j];
-    float ss = 0.f;
+    for (int j = 0; j < C; ++j) u[j] = xr[c0 + 32 * j];
 #pragma unroll
-    for (int j = 0; j < CPL; ++j) {
+    for (int j = 0; j < C; ++j) {
       __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&u[j]);
       if (add || exch) {
-        // residual update first: x = bf16(x + bf16(sum of the ranks' partials)), the sum in rank
-        // order (an all-reduced buffer, or the exchange slots of the current parity)
+        // residual update first: x = bf16(x + bf16(sum of the partials)), the sum in slice / rank
+        // order (split-K partials, an all-reduced buffer, or the exchange slots of the current parity)
         float av[8];
-        if (exch) {
 #pragma unroll
-          for (int k = 0; k < 8; ++k) av[k] = 0.f;
+        for (int k = 0; k < 8; ++k) av[k] = 0.f;
+        if (exch) {
           for (int q = 0; q < link.world; ++q) {
             const float4* ar = reinterpret_cast<const float4*>(tp_row_slot(link, inst & 1u, q, src) +
-                                                               (lane + 32 * j) * 8);
+                                                               (c0 + 32 * j) * 8);
             const float4 a0 = __ldcg(ar), a1 = __ldcg(ar + 1);
             av[0] += a0.x; av[1] += a0.y; av[2] += a0.z; av[3] += a0.w;
             av[4] += a1.x; av[5] += a1.y; av[6] += a1.z; av[7] += a1.w;
           }
         } else {
-          const float4* ar = reinterpret_cast<const float4*>(add + (long long)src * hidden + (lane + 32 * j) * 8);
-          const float4 a0 = ar[0], a1 = ar[1];
-          av[0] = a0.x; av[1] = a0.y; av[2] = a0.z; av[3] = a0.w;
-          av[4] = a1.x; av[5] = a1.y; av[6] = a1.z; av[7] = a1.w;
+          const float* base = add + (long long)src * hidden + (c0 + 32 * j) * 8;
+#pragma unroll 8
+          for (int sl = 0; sl < add_count; ++sl) {
+            const float4* ar = reinterpret_cast<const float4*>(base + sl * add_stride);
+            const float4 a0 = __ldcg(ar), a1 = __ldcg(ar + 1);
+            av[0] += a0.x; av[1] += a0.y; av[2] += a0.z; av[3] += a0.w;
+            av[4] += a1.x; av[5] += a1.y; av[6] += a1.z; av[7] += a1.w;
+          }
         }
 #pragma unroll
         for (int k = 0; k < 8; ++k) e[k] = __float2bfloat16_rn(__bfloat162float(e[k]) + bf16r(av[k]));
-        xr[lane + 32 * j] = u[j];
+        xr[c0 + 32 * j] = u[j];
       }
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
@@ -110,10 +123,20 @@ __global__ void rmsnorm_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat1
       }
     }
     ss = warp_sum(ss);
+  }
+  if (WPR > 1) {
+    if (lane == 0) part_ss[warp] = ss;
+    __syncthreads();
+    const int w0 = (warp / WPR) * WPR;
+    ss = part_ss[w0];
+#pragma unroll
+    for (int i = 1; i < WPR; ++i) ss += part_ss[w0 + i];
+  }
+  if (active) {
     const float r = 1.0f / sqrtf(ss / (float)hidden + eps);
     uint4* yr = reinterpret_cast<uint4*>(y + (long long)row * hidden);
 #pragma unroll
-    for (int j = 0; j < CPL; ++j) {
+    for (int j = 0; j < C; ++j) {
       const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&u[j]);
       const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv[j]);
       uint4 o;
@@ -121,9 +144,9 @@ __global__ void rmsnorm_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat1
 #pragma unroll
       for (int k = 0; k < 8; ++k)
         oe[k] = __float2bfloat16_rn(bf16r(__bfloat162float(e[k]) * r) * __bfloat162float(we[k]));
-      yr[lane + 32 * j] = o;
+      yr[c0 + 32 * j] = o;
     }
-    if (zero_keys && lane == 0) zero_keys[row] = 0ull;
+    if (zero_keys && threadIdx.x % (32 * WPR) == 0) zero_keys[row] = 0ull;
   }
   if (exch) tp_reader_done(link, inst);
 }
@@ -500,25 +523,28 @@ int launch_embed(const __nv_bfloat16* embed, const int32_t* tokens, const int32_
 
 int launch_rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int max_rows,
                    const int32_t* rows_dev, const int32_t* gather, int hidden, float eps,
-                   unsigned long long* zero_keys, cudaStream_t stream, const float* add, const TpLink* link,
-                   int* status) {
+                   unsigned long long* zero_keys, cudaStream_t stream, const float* add, int add_count,
+                   long long add_stride, const TpLink* link, int* status) {
   if (link && (link->world < 1 || link->hidden != hidden || max_rows > link->max_rows || add)) return NE_ERR_INVALID;
+  if (add && add_count < 1) return NE_ERR_INVALID;
+  // four warps per row from hidden 1024 up (more loads in flight per row), a warp per row below
+  const int wpr = hidden >= 1024 ? 4 : 1;
   // a reader launch runs even without rows: it closes the exchange its writer opened
-  const int blocks = std::max((max_rows + 3) / 4, link ? 1 : 0);
+  const int blocks = std::max((max_rows + 4 / wpr - 1) / (4 / wpr), link ? 1 : 0);
   if (blocks == 0) return NE_OK;
   const TpLink lk = link ? *link : TpLink{};
   cudaError_t err;
-  switch (hidden) {  // 256 x chunks per lane
-#define NE_NORM_CASE(H, CPL)                                                                                   \
-  case H:                                                                                                      \
-    err = launch_kernel(rmsnorm_kernel<CPL>, dim3(blocks), dim3(128), 0, stream, x, w, y, max_rows, rows_dev,  \
-                        gather, hidden, eps, zero_keys, add, lk, status);                                      \
+  switch (hidden) {  // 256 x chunks per row and lane
+#define NE_NORM_CASE(H, CPL, WPR)                                                                               \
+  case H:                                                                                                       \
+    err = launch_kernel(rmsnorm_kernel<CPL, WPR>, dim3(blocks), dim3(128), 0, stream, x, w, y, max_rows, rows_dev, \
+                        gather, hidden, eps, zero_keys, add, add_count, add_stride, lk, status);                \
     break;
-    NE_NORM_CASE(256, 1)
-    NE_NORM_CASE(512, 2)
-    NE_NORM_CASE(1024, 4)
-    NE_NORM_CASE(2048, 8)
-    NE_NORM_CASE(4096, 16)
+    NE_NORM_CASE(256, 1, 1)
+    NE_NORM_CASE(512, 2, 1)
+    NE_NORM_CASE(1024, 4, 4)
+    NE_NORM_CASE(2048, 8, 4)
+    NE_NORM_CASE(4096, 16, 4)
 #undef NE_NORM_CASE
     default: return NE_ERR_UNSUPPORTED;  // hidden sizes other than 256 x {1, 2, 4, 8, 16}
   }

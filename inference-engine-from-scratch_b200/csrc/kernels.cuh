@@ -25,14 +25,16 @@ struct RowBuffers {
 // ``ssq`` (may be NULL): per (row, 128-wide tile) fp32 sums of squares of the embedded rows.
 int launch_embed(const __nv_bfloat16* embed, const int32_t* tokens, const int32_t* num_rows, int max_rows, int hidden,
                  int vocab, __nv_bfloat16* out, int* status, cudaStream_t stream, float* ssq = nullptr);
-// ``add`` (fp32 [rows, hidden], may be NULL): first x[src] = bf16(x[src] + bf16(add[src])) in place (the
-// residual update after a tensor-parallel all-reduce), then the norm of the updated row. ``link``
-// (may be NULL; then ``add`` must be NULL): the partial rows come from the peer exchange instead,
-// the launch waits for them (bounded; NE_DEV_TIMEOUT into ``status``) and closes the exchange.
+// ``add`` (fp32 [add_count][rows, hidden] slices ``add_stride`` elements apart, may be NULL): first
+// x[src] = bf16(x[src] + bf16(sum of the slices' rows src, in slice order)) in place (the residual
+// update after split-K partials or a tensor-parallel all-reduce), then the norm of the updated row.
+// ``link`` (may be NULL; then ``add`` must be NULL): the partial rows come from the peer exchange
+// instead; the launch waits for them (bounded; NE_DEV_TIMEOUT into ``status``) and closes the exchange.
 int launch_rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int max_rows,
                    const int32_t* rows_dev, const int32_t* gather, int hidden, float eps,
                    unsigned long long* zero_keys, cudaStream_t stream, const float* add = nullptr,
-                   const TpLink* link = nullptr, int* status = nullptr);
+                   int add_count = 1, long long add_stride = 0, const TpLink* link = nullptr,
+                   int* status = nullptr);
 // Peer exchange of the LM head's argmax keys over a vocabulary split: push this rank's keys
 // [count] to every rank, wait (bounded) for every rank's, keep the largest (one CTA).
 int launch_tp_keys_exchange(unsigned long long* keys, const int32_t* count, int max_count, const TpLink& link,
