@@ -11,7 +11,8 @@
 * ``e2e``: the whole short_chat job (64 prompts from pinned host memory, prefill, every step until
   each user has 128 tokens, one device->host read of the results per step) through the public API
   ``B200SpeculativeEngine.generate``; emitted tokens / time.
-* ``roofline``: the dominant kernel of one profiled step (CUDA events around every launch), its
+* ``roofline``: the dominant kernel of one profiled step (a CUDA graph of the step with an event
+  after every launch, replayed once: device time per kernel without host launch gaps), its
   algorithmic bytes per launch over its average duration, against MEASURED_PEAKS.json.
 * ``cpu_baseline``: the CPU oracle (the reference's serial speculative path restated, fp32, config 1's
   prompt) on this host's cores for a bounded sample.
@@ -59,6 +60,8 @@ def parse_args():
     p.add_argument("--steps", type=int, default=30)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--no-kv-copies", action="store_true",
+                   help="c3: convert the shared prefix's int8 blocks in every attention launch (no bf16 copies)")
     p.add_argument("--tp-exchange-rows", type=int, default=512,
                    help="c5b: steps of up to this many rows use the NVLink peer exchange (0: NCCL only)")
     p.add_argument("--workload", choices=("c2", "c3", "c4", "c5b"), default="c2",
@@ -423,9 +426,11 @@ def run_b200(args, dist: Dist) -> None:
         cfg = tp_mod.rank_config(cfg, plan)  # per-rank shapes for the byte counts below
     else:
         weights = pkg.make_weights(cfg, seed=0)
+        # int8 KV with a shared prefix: the prefix blocks are dequantised once (engine.add_prefix)
+        copies = wl.shared_prefix // 16 if (wl.kv_int8 and wl.shared_prefix and not args.no_kv_copies) else 0
         model = model_mod.B200Model(cfg, weights, num_slots=num_blocks * 16, device=device,
                                     max_positions=max_model_len + k + 16, max_rows=max_rows, max_seqs=users + 1,
-                                    kv_int8=wl.kv_int8, weight_int8=wl.weight_int8)
+                                    kv_int8=wl.kv_int8, weight_int8=wl.weight_int8, kv_copy_blocks=copies)
     del weights
     engine = engine_mod.B200SpeculativeEngine(model, k=k, max_ngram=3, max_seqs=users + (1 if wl.shared_prefix else 0),
                                               max_model_len=max_model_len, num_blocks=num_blocks, cuda_graphs=True,
@@ -481,11 +486,21 @@ def run_b200(args, dist: Dist) -> None:
     nk = len(lib_mod.KERNEL_KINDS)
     ms_by = (ctypes.c_float * nk)()
     n_by = (ctypes.c_int * nk)()
-    lib_mod.check(model.lib.ne_model_profile_begin(model.handle, stream.cuda_stream), "profile_begin")
     engine._set_slots(slots, len(slots))
-    engine._launch_step(len(slots))
+    # the step is captured with an event-record node after every launch and replayed once, so the
+    # intervals are device time per kernel (serialised by the events) without host launch gaps
+    lib_mod.check(model.lib.ne_model_profile_begin(model.handle, stream.cuda_stream), "profile_begin")  # events
+    lib_mod.check(model.lib.ne_model_profile_end(model.handle, ms_by, n_by, nk), "profile_end")
+    torch.cuda.synchronize()
+    prof_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(prof_graph):
+        cap = torch.cuda.current_stream().cuda_stream
+        lib_mod.check(model.lib.ne_model_profile_begin(model.handle, cap), "profile_begin")
+        engine._launch_step(len(slots))
+    prof_graph.replay()
     lib_mod.check(model.lib.ne_model_profile_end(model.handle, ms_by, n_by, nk), "profile_end")
     res = engine._collect(slots)
+    del prof_graph
     launches_per_step = model.lib.ne_model_launch_count(model.handle) - launches_before
     M = len(slots) + res.proposed
     ctx_sum = ctx_before + res.proposed  # keys visible to the last row of every sequence

@@ -286,6 +286,24 @@ NE_API int ne_verify_logits(const ne_batch_state* state, const int32_t* seq_slot
                             int lm_rows, void* scratch, size_t scratch_bytes, const ne_step_outputs* out,
                             int32_t* status, void* stream);
 
+/* ---------------------------------------------------------------- shared int8 KV blocks */
+/*
+ * Dequantised copies of int8 KV blocks that many sequences share (a prompt prefix held by one
+ * slot and shared with ne_state_share_blocks): ``shadow`` holds [num_layers][2][shadow_blocks * 16]
+ * [num_kv_heads][128] bf16, ``block_map`` one int32 per pool block ((num_cache_slots - 1) / 16
+ * entries, all -1 initially). ne_kv_shadow_fill writes copies first_copy.. of the first
+ * ``num_blocks`` blocks of ``src_slot``'s table -- bf16(q * scale), the values the attention's
+ * conversion produces -- and then maps those pool blocks to them; the attention then reads a
+ * mapped block's copy instead of converting it per sequence and head. ne_kv_shadow_clear unmaps
+ * them (before the holder's blocks are freed). int8 KV models only (NE_ERR_INVALID otherwise).
+ */
+NE_API int ne_model_set_kv_shadow(ne_model* model, void* shadow, int shadow_blocks, int32_t* block_map,
+                                  int map_entries);
+NE_API int ne_kv_shadow_fill(ne_model* model, const ne_batch_state* state, int src_slot, int num_blocks,
+                             int first_copy, void* stream);
+NE_API int ne_kv_shadow_clear(ne_model* model, const ne_batch_state* state, int src_slot, int num_blocks,
+                              void* stream);
+
 /* ---------------------------------------------------------------- tensor parallelism */
 /*
  * A model split over 2/4/8 GPUs, one process per GPU: column-parallel QKV (whole KV heads per rank)
@@ -342,9 +360,11 @@ NE_API int ne_model_tp_exchange_open(ne_model* model, const void* ipc_handles);
 /* Kernels this model has launched so far (every entry point that takes the model counts). */
 NE_API long long ne_model_launch_count(const ne_model* model);
 /*
- * Time every kernel the model launches on ``stream`` between begin and end with CUDA events
- * (eager launches only, not inside a graph capture). end synchronizes and fills, per kind,
- * the summed device milliseconds and the number of launches.
+ * Time every kernel the model launches on ``stream`` between begin and end with CUDA events.
+ * Eagerly, or inside a stream capture: the events then become event-record nodes of the graph,
+ * and end (called after the graph was launched) reads the times of its last launch, free of the
+ * host's launch gaps. end synchronizes and fills, per kind, the summed device milliseconds and
+ * the number of launches.
  */
 NE_API int ne_model_profile_begin(ne_model* model, void* stream);
 NE_API int ne_model_profile_end(ne_model* model, float* ms_by_kind, int* launches_by_kind, int num_kinds);

@@ -71,6 +71,9 @@ EXPORTS = {
     "ne_tp_unique_id": (c_int, [ctypes.c_char_p, c_void_p]),
     "ne_model_set_tp": (c_int, [c_void_p, ctypes.c_char_p, c_int, c_int, c_void_p]),
     "ne_model_tp_exchange_create": (c_int, [c_void_p, c_int, c_void_p]),
+    "ne_model_set_kv_shadow": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int]),
+    "ne_kv_shadow_fill": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "ne_kv_shadow_clear": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "ne_model_tp_exchange_open": (c_int, [c_void_p, c_void_p]),
     "ne_model_launch_count": (c_longlong, [c_void_p]),
     "ne_model_profile_begin": (c_int, [c_void_p, c_void_p]),

@@ -72,6 +72,7 @@ struct Ctx {
   int nh, nkv, h, G, r0, nvec;
   long long num_cache_slots;
   int* status;
+  KvShadow sh;
 };
 
 // Stage one 16-token K and V block (block id ``blk``) into smem at k_s / v_s, using ``nthr``
@@ -111,6 +112,16 @@ __device__ __forceinline__ void stage_block(const Ctx& c, long long blk, uint32_
       asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(vo + 16), "r"(vw[4]), "r"(vw[5]), "r"(vw[6]),
                    "r"(vw[7]));
     }
+  }
+}
+
+// Stage dequantised copy ``sh`` of a shared int8 block (bf16, the pool's row layout) by cp.async.
+__device__ __forceinline__ void stage_shadow(const Ctx& c, int sh, uint32_t k_s, uint32_t v_s, int lane) {
+  for (int i = lane; i < 16 * 16; i += 32) {
+    const int tok = i >> 4, ch = i & 15;
+    const long long off = (((long long)sh * 16 + tok) * c.nkv + c.h) * D + ch * 8;
+    cp_async16(k_s + tok * ROW_BYTES + ch * 16, c.sh.k + off);
+    cp_async16(v_s + tok * ROW_BYTES + ch * 16, c.sh.v + off);
   }
 }
 
@@ -356,13 +367,23 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
     const int kbj = kb0 + phase + per_tile * (j0 + lane);
     return (kbj < kb1 && kbj < stride) ? c.table[kbj] : -1;
   };
+  // int8 pool with dequantised copies: each lane also holds the copy index of its table entry
+  auto copy_of = [&](int id) -> int {
+    if (!INT8 || !c.sh.map || id < 0 || (long long)(id + 1) * 16 > c.num_cache_slots - 1) return -1;
+    const int v = c.sh.map[id];
+    return v < c.sh.blocks ? v : -1;
+  };
   int tbl = table_chunk(0);
+  int shm = copy_of(tbl);
   int kb = kb0 + phase;
   long long blk = kb < kb1 ? (kb < stride ? checked_block(c, __shfl_sync(0xFFFFFFFFu, tbl, 0)) : block_id(c, kb, stride)) : -1;
+  int shv = (blk >= 0 && kb < stride) ? __shfl_sync(0xFFFFFFFFu, shm, 0) : -1;  // (warp-uniform)
   uint32_t scales = 0;
   // each warp's first K/V block goes out before the query tiles (they do not depend on it)
   if (blk >= 0) {
-    if (INT8) {
+    if (INT8 && shv >= 0) {
+      stage_shadow(c, shv, wbuf, wbuf + BLOCK_BYTES, lane);
+    } else if (INT8) {
       stage_raw_int8(c, blk, wbuf, lane);
       scales = load_scales_int8(c, blk, lane);
     } else {
@@ -378,8 +399,44 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
     __syncthreads();
     if (my_tile == t) tile_init(ts, smem_u32(q_s), spos + 16 * t, lane);
   }
-  int stage = 0;
-  for (int j = 0; kb < kb1; kb += per_tile, ++j) {
+  int stage = 0, j = 0;
+  if (INT8 && shv >= 0) {
+    // leading blocks with dequantised copies (a shared prefix): the bf16 pipeline, two K/V stages
+    while (kb < kb1 && shv >= 0) {
+      const int nkb = kb + per_tile;
+      if (((j + 1) & 31) == 0) {  // warp-uniform
+        tbl = table_chunk(j + 1);
+        shm = copy_of(tbl);
+      }
+      const int nraw_id = __shfl_sync(0xFFFFFFFFu, tbl, (j + 1) & 31);
+      const int nsh_lane = __shfl_sync(0xFFFFFFFFu, shm, (j + 1) & 31);
+      const long long nblk_id = nkb < kb1 ? (nkb < stride ? checked_block(c, nraw_id) : block_id(c, nkb, stride)) : -1;
+      const int nsh = (nblk_id >= 0 && nkb < stride) ? nsh_lane : -1;
+      const uint32_t nxt = wbuf + (stage ^ 1) * 2 * BLOCK_BYTES;
+      if (nsh >= 0) stage_shadow(c, nsh, nxt, nxt + BLOCK_BYTES, lane);
+      cp_commit();
+      cp_wait<1>();
+      __syncwarp();
+      const uint32_t cur = wbuf + stage * 2 * BLOCK_BYTES;
+      tile_block(ts, cur, cur + BLOCK_BYTES, kb, lane);
+      __syncwarp();
+      blk = nblk_id;
+      shv = nsh;
+      stage ^= 1;
+      kb = nkb;
+      ++j;
+    }
+    cp_wait<0>();
+    __syncwarp();
+    // the blocks without copies start the int8 pipeline afresh (its buffers overlap the stages)
+    stage = 0;
+    if (kb < kb1 && blk >= 0) {
+      stage_raw_int8(c, blk, wbuf, lane);
+      scales = load_scales_int8(c, blk, lane);
+    }
+    cp_commit();
+  }
+  for (; kb < kb1; kb += per_tile, ++j) {
     const int nkb = kb + per_tile;
     if (((j + 1) & 31) == 0) tbl = table_chunk(j + 1);  // warp-uniform
     const int nraw_id = __shfl_sync(0xFFFFFFFFu, tbl, (j + 1) & 31);
@@ -475,7 +532,7 @@ __global__ void __launch_bounds__(32 * NW, NW == 4 ? 3 : 5)
     attention_kernel(const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out, const void* __restrict__ kc,
                      const void* __restrict__ vc, const __nv_bfloat16* __restrict__ ks,
                      const __nv_bfloat16* __restrict__ vs, ne_rows rows, int nh, int nkv, long long num_cache_slots,
-                     AttnSplit sp, int* status) {
+                     AttnSplit sp, int* status, KvShadow shadow) {
   pdl_prologue();
   extern __shared__ __align__(16) uint8_t smem[];
   const int b = blockIdx.x, h = blockIdx.y, split = blockIdx.z;
@@ -497,6 +554,7 @@ __global__ void __launch_bounds__(32 * NW, NW == 4 ? 3 : 5)
   c.nvec = ql * c.G;
   c.num_cache_slots = num_cache_slots;
   c.status = status;
+  c.sh = shadow;
   c.table = rows.block_tables + (long long)(rows.table_index ? rows.table_index[b] : b) * rows.block_table_stride;
   const int ctx = rows.positions[c.r0 + ql - 1] + 1;  // the last row sees the whole context
   const int nblk = (ctx + 15) / 16;
@@ -601,6 +659,52 @@ __global__ void clear_partials_kernel(AttnSplit sp, long long n) {
 
 }  // namespace
 
+// Dequantised copy of logical block blockIdx.x of a table row, one layer: K (blockIdx.y == 0) or
+// V, bf16(q * scale) per element -- the value the attention's in-shared-memory conversion makes.
+__global__ void kv_shadow_fill_kernel(const int32_t* __restrict__ table, int first, const int8_t* __restrict__ kc,
+                                      const int8_t* __restrict__ vc, const __nv_bfloat16* __restrict__ ks,
+                                      const __nv_bfloat16* __restrict__ vs, int nkv, long long num_cache_slots,
+                                      __nv_bfloat16* __restrict__ shk, __nv_bfloat16* __restrict__ shv,
+                                      int* status) {
+  pdl_prologue();
+  const long long blk = table[blockIdx.x];
+  if (blk < 0 || (blk + 1) * 16 > num_cache_slots - 1) {
+    if (threadIdx.x == 0) report(status, NE_DEV_BAD_SLOT);
+    return;
+  }
+  const int8_t* src = blockIdx.y == 0 ? kc : vc;
+  const __nv_bfloat16* scale = blockIdx.y == 0 ? ks : vs;
+  __nv_bfloat16* dst = blockIdx.y == 0 ? shk : shv;
+  const int units = 16 * nkv * (D / 8);  // (token, head, 8-element chunk)
+  for (int u = threadIdx.x; u < units; u += blockDim.x) {
+    const int ch = u % (D / 8), th = u / (D / 8), head = th % nkv, tok = th / nkv;
+    const long long slot = blk * 16 + tok;
+    const float s = __bfloat162float(scale[slot * nkv + head]);
+    const uint2 raw = *reinterpret_cast<const uint2*>(src + (slot * nkv + head) * D + ch * 8);
+    const int8_t* q8 = reinterpret_cast<const int8_t*>(&raw);
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ow[i] = pack_bf16((float)q8[2 * i] * s, (float)q8[2 * i + 1] * s);
+    const long long to = (((long long)(first + blockIdx.x) * 16 + tok) * nkv + head) * D + ch * 8;
+    *reinterpret_cast<uint4*>(dst + to) = o;
+  }
+}
+
+// map[table[i]] = first + i (first >= 0) or -1 (first < 0) for the row's first num_blocks blocks.
+__global__ void kv_shadow_map_kernel(const int32_t* __restrict__ table, int num_blocks, int first, int32_t* map,
+                                     long long num_cache_slots, int* status) {
+  pdl_prologue();
+  for (int i = threadIdx.x; i < num_blocks; i += blockDim.x) {
+    const long long blk = table[i];
+    if (blk < 0 || (blk + 1) * 16 > num_cache_slots - 1) {
+      report(status, NE_DEV_BAD_SLOT);
+      continue;
+    }
+    map[blk] = first >= 0 ? first + i : -1;
+  }
+}
+
 size_t attention_smem_bytes_nw(int nw) {
   if (nw == 4) return attention_smem_bytes();
   // Q tile + positions + max(nw warps x 2 stages x (K, V) blocks, the merge area)
@@ -645,7 +749,7 @@ int attention_plan_splits(int num_seqs, int nkv, int max_context, int max_vec, i
 int launch_attention_tc(const __nv_bfloat16* q, __nv_bfloat16* out, const void* k_cache, const void* v_cache,
                         const __nv_bfloat16* k_scale, const __nv_bfloat16* v_scale, int kv_int8, const ne_rows& rows,
                         int num_heads, int num_kv_heads, long long num_cache_slots, const AttnSplit& sp, int* status,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, const KvShadow& shadow) {
   if (num_kv_heads <= 0 || num_heads % num_kv_heads || rows.num_seqs <= 0 || sp.splits < 1) return NE_ERR_INVALID;
   if (sp.splits > 1 && (!sp.part_o || !sp.part_m || !sp.part_l || sp.max_vec < 1)) return NE_ERR_INVALID;
   // one query tile per (entry, KV head) (the speculative step) and a grid that five 2-warp CTAs
@@ -673,8 +777,9 @@ int launch_attention_tc(const __nv_bfloat16* q, __nv_bfloat16* out, const void* 
       return NE_ERR_CUDA;
   }
   dim3 grid(rows.num_seqs, num_kv_heads, sp.splits);
+  if (shadow.map && (!kv_int8 || !shadow.k || !shadow.v || shadow.blocks < 1)) return NE_ERR_INVALID;
   if (launch_kernel(kernel, grid, dim3(32 * nw), smem, stream, q, out, k_cache, v_cache, k_scale, v_scale, rows,
-                    num_heads, num_kv_heads, num_cache_slots, sp, status) != cudaSuccess)
+                    num_heads, num_kv_heads, num_cache_slots, sp, status, shadow) != cudaSuccess)
     return NE_ERR_CUDA;
   if (sp.splits > 1) {
     if (launch_kernel(combine_kernel, dim3(rows.num_seqs, num_kv_heads), dim3(D), 0, stream, rows, num_heads,
@@ -682,6 +787,27 @@ int launch_attention_tc(const __nv_bfloat16* q, __nv_bfloat16* out, const void* 
       return NE_ERR_CUDA;
   }
   return NE_OK;
+}
+
+int launch_kv_shadow_fill(const int32_t* table, int num_blocks, int first, const void* k_cache, const void* v_cache,
+                          const __nv_bfloat16* k_scale, const __nv_bfloat16* v_scale, int nkv,
+                          long long num_cache_slots, __nv_bfloat16* shadow_k, __nv_bfloat16* shadow_v, int* status,
+                          cudaStream_t stream) {
+  if (!table || num_blocks < 0 || first < 0 || !k_cache || !v_cache || !k_scale || !v_scale || !shadow_k ||
+      !shadow_v || nkv < 1)
+    return NE_ERR_INVALID;
+  if (num_blocks == 0) return NE_OK;
+  return launch_kernel(kv_shadow_fill_kernel, dim3(num_blocks, 2), dim3(256), 0, stream, table, first,
+                       static_cast<const int8_t*>(k_cache), static_cast<const int8_t*>(v_cache), k_scale, v_scale, nkv,
+                       num_cache_slots, shadow_k, shadow_v, status) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
+}
+
+int launch_kv_shadow_map(const int32_t* table, int num_blocks, int first, int32_t* map, long long num_cache_slots,
+                         int* status, cudaStream_t stream) {
+  if (!table || !map || num_blocks < 0) return NE_ERR_INVALID;
+  if (num_blocks == 0) return NE_OK;
+  return launch_kernel(kv_shadow_map_kernel, dim3(1), dim3(256), 0, stream, table, num_blocks, first, map,
+                       num_cache_slots, status) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 
 }  // namespace ne

@@ -40,6 +40,10 @@ struct ne_model {
   void* tp_comm = nullptr;
   int tp_rank = 0, tp_world = 1;
   float* partial = nullptr;  // fp32 [max_rows, H]: row-parallel projection outputs, all-reduced
+  // dequantised copies of shared int8 KV blocks: [L][2][blocks * 16][nkv][128] bf16 + pool-block map
+  __nv_bfloat16* kv_shadow = nullptr;
+  int32_t* kv_shadow_map = nullptr;
+  int kv_shadow_blocks = 0;
   // peer exchange (steps of up to link.max_rows rows): own region, peers' regions mapped here
   void* tp_region = nullptr;
   size_t tp_region_bytes = 0;
@@ -114,6 +118,15 @@ Layout workspace_layout(const ne_model_config& c, int R, int B, int tp_world) {
 
 cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Record a profiling event; inside a stream capture as an event-record node of the graph, so that
+// replaying the graph times the launches on the device without the host's launch gaps.
+cudaError_t record_profile_event(cudaEvent_t e, cudaStream_t stream) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) return cudaErrorUnknown;
+  return cs == cudaStreamCaptureStatusActive ? cudaEventRecordWithFlags(e, stream, cudaEventRecordExternal)
+                                             : cudaEventRecord(e, stream);
+}
+
 // Count one launch of ``kind``; while profiling, close its timing interval with an event.
 int note(ne_model* m, int kind, int rc, cudaStream_t stream) {
   if (rc != NE_OK) return rc;
@@ -124,7 +137,7 @@ int note(ne_model* m, int kind, int rc, cudaStream_t stream) {
       if (cudaEventCreate(&e) != cudaSuccess) return NE_ERR_CUDA;
       m->events.push_back(e);
     }
-    if (cudaEventRecord(m->events[m->events_used], stream) != cudaSuccess) return NE_ERR_CUDA;
+    if (record_profile_event(m->events[m->events_used], stream) != cudaSuccess) return NE_ERR_CUDA;
     m->event_kinds.push_back(kind);
     ++m->events_used;
   }
@@ -412,6 +425,53 @@ int ne_model_set_tp(ne_model* m, const char* nccl_library, int rank, int world, 
   return NE_OK;
 }
 
+// Layer l's K (kv = 0) or V (kv = 1) copies.
+__nv_bfloat16* shadow_layer(const ne_model* m, int l, int kv) {
+  const ne_model_config& c = m->cfg;
+  return m->kv_shadow + ((size_t)l * 2 + kv) * m->kv_shadow_blocks * 16 * c.num_kv_heads * 128;
+}
+
+int ne_model_set_kv_shadow(ne_model* m, void* shadow, int shadow_blocks, int32_t* block_map, int map_entries) {
+  if (!m || !m->cfg.kv_int8 || !shadow || !block_map || shadow_blocks < 1 ||
+      (long long)map_entries * 16 != m->cfg.num_cache_slots - 1 || (reinterpret_cast<uintptr_t>(shadow) & 15u))
+    return NE_ERR_INVALID;
+  m->kv_shadow = static_cast<__nv_bfloat16*>(shadow);
+  m->kv_shadow_map = block_map;
+  m->kv_shadow_blocks = shadow_blocks;
+  return NE_OK;
+}
+
+int ne_kv_shadow_fill(ne_model* m, const ne_batch_state* st, int src_slot, int num_blocks, int first_copy,
+                      void* stream) {
+  if (!m || !st || !m->kv_shadow || !m->ws || src_slot < 0 || src_slot >= st->max_seqs || num_blocks < 0 ||
+      num_blocks > st->block_table_stride || first_copy < 0 || first_copy + num_blocks > m->kv_shadow_blocks)
+    return NE_ERR_INVALID;
+  for (char set : m->layer_set)
+    if (!set) return NE_ERR_INVALID;
+  cudaStream_t s = as_stream(stream);
+  const ne_model_config& c = m->cfg;
+  const int32_t* row = st->block_tables + (size_t)src_slot * st->block_table_stride;
+  for (int l = 0; l < c.num_layers; ++l) {
+    const ne_layer_weights& w = m->layers[l];
+    const int rc = ne::launch_kv_shadow_fill(row, num_blocks, first_copy, w.k_cache, w.v_cache,
+                                             static_cast<const __nv_bfloat16*>(w.k_scale),
+                                             static_cast<const __nv_bfloat16*>(w.v_scale), c.num_kv_heads,
+                                             c.num_cache_slots, shadow_layer(m, l, 0), shadow_layer(m, l, 1), m->status, s);
+    if (rc) return rc;
+  }
+  // mapped only once every layer's copy is written (stream order)
+  return ne::launch_kv_shadow_map(row, num_blocks, first_copy, m->kv_shadow_map, c.num_cache_slots, m->status, s);
+}
+
+int ne_kv_shadow_clear(ne_model* m, const ne_batch_state* st, int src_slot, int num_blocks, void* stream) {
+  if (!m || !st || !m->kv_shadow || !m->ws || src_slot < 0 || src_slot >= st->max_seqs || num_blocks < 0 ||
+      num_blocks > st->block_table_stride)
+    return NE_ERR_INVALID;
+  const int32_t* row = st->block_tables + (size_t)src_slot * st->block_table_stride;
+  return ne::launch_kv_shadow_map(row, num_blocks, -1, m->kv_shadow_map, m->cfg.num_cache_slots, m->status,
+                                  as_stream(stream));
+}
+
 int ne_model_tp_exchange_create(ne_model* m, int max_rows, void* ipc_handle) {
   if (!m || !ipc_handle || m->tp_world < 2 || m->tp_region || max_rows < 1 || max_rows > (1 << 16))
     return NE_ERR_INVALID;
@@ -518,7 +578,10 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
               ne::launch_attention_tc(m->q, m->attn, w.k_cache, w.v_cache,
                                       static_cast<const __nv_bfloat16*>(w.k_scale),
                                       static_cast<const __nv_bfloat16*>(w.v_scale), c.kv_int8, *rows, c.num_heads,
-                                      c.num_kv_heads, c.num_cache_slots, attn, m->status, s), s);
+                                      c.num_kv_heads, c.num_cache_slots, attn, m->status, s,
+                                      m->kv_shadow ? ne::KvShadow{m->kv_shadow_map, shadow_layer(m, l, 0),
+                                                                  shadow_layer(m, l, 1), m->kv_shadow_blocks}
+                                                   : ne::KvShadow{}), s);
     if (rc) return rc;
     ne::Epilogue eo{};
     eo.mode = px ? ne::EPI_PUSH_F32 : tp ? ne::EPI_STORE_F32 : ne::EPI_RESIDUAL;
@@ -608,16 +671,20 @@ long long ne_model_launch_count(const ne_model* m) { return m ? m->launches : -1
 int ne_model_profile_begin(ne_model* m, void* stream) {
   if (!m) return NE_ERR_INVALID;
   cudaStream_t s = as_stream(stream);
-  if (m->events.empty()) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cs) != cudaSuccess) return NE_ERR_CUDA;
+  // events are created outside captures (a step launches a few hundred kernels)
+  while (cs == cudaStreamCaptureStatusNone && m->events.size() < 1024) {
     cudaEvent_t e;
     if (cudaEventCreate(&e) != cudaSuccess) return NE_ERR_CUDA;
     m->events.push_back(e);
   }
+  if (m->events.empty()) return NE_ERR_INVALID;
   m->event_kinds.clear();
   m->events_used = 1;
   m->profile_stream = s;
   m->profiling = true;
-  return cudaEventRecord(m->events[0], s) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
+  return record_profile_event(m->events[0], s) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 
 int ne_model_profile_end(ne_model* m, float* ms_by_kind, int* launches_by_kind, int num_kinds) {

@@ -132,7 +132,7 @@ class B200SpeculativeEngine:
             nbytes = int(self.lib.ne_sampling_buffer_bytes(model.handle, self._sample_rows))
             self._sample_buf = torch.empty(nbytes, dtype=torch.uint8, device=model.device)
         self._uncached: dict[int, int] = {}       # slot -> prompt tokens still to prefill
-        self._prefixes: dict[int, list] = {}      # holder slot -> [tokens, shared blocks, users]
+        self._prefixes: dict[int, list] = {}      # holder slot -> [tokens, shared blocks, users, copies]
         self._prefix_of: dict[int, int] = {}      # slot -> holder slot of its shared prefix
         self.proposed_total = 0
         self.accepted_total = 0
@@ -171,13 +171,23 @@ class B200SpeculativeEngine:
         pass the returned handle as ``prefix`` and reuse its full 16-token blocks."""
         holder = self.add_request(tokens, 1, ignore_eos=True)
         self.prefill([holder])
-        self._prefixes[holder] = [list(tokens), len(tokens) // 16, 0]
+        blocks = len(tokens) // 16
+        # int8 KV: dequantise the shared blocks once (the attention reads the copies)
+        first = self.model.take_kv_copies(blocks) if blocks else None
+        if first is not None:
+            _lib.check(self.lib.ne_kv_shadow_fill(self.model.handle, self.state.ref, holder, blocks, first,
+                                                  _lib.stream_handle()), "ne_kv_shadow_fill")
+        self._prefixes[holder] = [list(tokens), blocks, 0, first]
         return holder
 
     def drop_prefix(self, prefix: int) -> None:
         if self._prefixes[prefix][2]:
             raise RuntimeError("requests still share this prefix")
-        del self._prefixes[prefix]
+        _, blocks, _, first = self._prefixes.pop(prefix)
+        if first is not None:  # unmap before the holder's blocks return to the pool
+            _lib.check(self.lib.ne_kv_shadow_clear(self.model.handle, self.state.ref, prefix, blocks,
+                                                   _lib.stream_handle()), "ne_kv_shadow_clear")
+            self.model.return_kv_copies(first, blocks)
         self.state.release([prefix])
 
     def _bind_sampler(self) -> None:

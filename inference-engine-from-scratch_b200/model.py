@@ -70,10 +70,12 @@ class B200Model:
         weight_int8: bool = False,
         tp=None,
         lm_offset: int = 0,
+        kv_copy_blocks: int = 0,
     ) -> None:
         """``tp`` (tp.TensorParallel): this process is one rank of a split model; ``cfg`` is then the
         rank's shape (tp.rank_config), ``weights`` its shard (tp.shard_weights / make_sharded_weights)
-        and ``lm_offset`` the first vocabulary id of its LM-head rows."""
+        and ``lm_offset`` the first vocabulary id of its LM-head rows. ``kv_copy_blocks`` (int8 KV):
+        room for that many dequantised copies of shared prefix blocks (ne_model_set_kv_shadow)."""
         self.lib = _lib.load()
         self.cfg = cfg
         self.device = torch.device(device)
@@ -187,6 +189,37 @@ class B200Model:
         _lib.check(self.lib.ne_model_set_workspace(handle, base, nbytes.value, max_rows, max_seqs),
                    "ne_model_set_workspace")
         self.status_ptr = self.lib.ne_model_status_word(handle)
+        self.kv_copies = None
+        self._copy_free: list[tuple[int, int]] = []
+        if kv_copy_blocks > 0 and kv_int8:
+            if num_slots % 16:
+                raise ValueError("dequantised block copies need a pool of whole 16-slot blocks")
+            self.kv_copies = torch.empty((L, 2, kv_copy_blocks * 16, nkv, d), dtype=bf16, device=dev)
+            self.kv_copy_map = torch.full((num_slots // 16,), -1, dtype=torch.int32, device=dev)
+            _lib.check(self.lib.ne_model_set_kv_shadow(handle, self.kv_copies.data_ptr(), kv_copy_blocks,
+                                                       self.kv_copy_map.data_ptr(), num_slots // 16),
+                       "ne_model_set_kv_shadow")
+            self._copy_free = [(0, kv_copy_blocks)]
+
+    # ------------------------------------------------------------------ dequantised block copies
+    def take_kv_copies(self, blocks: int) -> int | None:
+        """First index of ``blocks`` contiguous free copies, or None (no copies / no room: the
+        attention then converts those blocks itself)."""
+        for i, (start, n) in enumerate(self._copy_free):
+            if n >= blocks:
+                self._copy_free[i] = (start + blocks, n - blocks)
+                return start
+        return None
+
+    def return_kv_copies(self, first: int, blocks: int) -> None:
+        free = sorted(self._copy_free + [(first, blocks)])
+        merged: list[tuple[int, int]] = []
+        for start, n in free:
+            if merged and merged[-1][0] + merged[-1][1] == start:
+                merged[-1] = (merged[-1][0], merged[-1][1] + n)
+            elif n:
+                merged.append((start, n))
+        self._copy_free = merged
 
     # ------------------------------------------------------------------ views
     def k_cache(self, layer: int) -> torch.Tensor:

@@ -8,6 +8,8 @@
 
 from __future__ import annotations
 
+import ctypes
+
 import pytest
 import torch
 
@@ -201,3 +203,81 @@ def test_fused_rmsnorm_path_serves_the_reference_outputs() -> None:
          "-k", "serial_drop_in or continuous_batching or int8_engine"],
         cwd=REPO, env=env, capture_output=True, text=True, timeout=900)
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-2000:]
+
+
+def test_profile_times_every_launch_eagerly_and_inside_a_captured_step(small) -> None:
+    """ne_model_profile_*: one interval per kernel launch of the step, whether the step runs eagerly
+    or was captured into a CUDA graph (event-record nodes) and replayed."""
+    _, _, model = small
+    lib_mod = submodule("_lib")
+    pkg = package()
+    eng = _engine(model, 4, graphs=False)
+    prompts = pkg.make_prompts(4, model.cfg.vocab_size, length=40, seed=3)
+    slots = [eng.add_request(p, 64, ignore_eos=True) for p in prompts]
+    eng.prefill(slots)
+    nk = len(lib_mod.KERNEL_KINDS)
+    lib = model.lib
+    results = []
+    for captured in (False, True):
+        ms_by = (ctypes.c_float * nk)()
+        n_by = (ctypes.c_int * nk)()
+        lib_mod.check(lib.ne_model_profile_begin(model.handle, lib_mod.stream_handle()), "profile_begin")
+        lib_mod.check(lib.ne_model_profile_end(model.handle, ms_by, n_by, nk), "profile_end")  # creates events
+        eng._set_slots(slots, len(slots))
+        before = lib.ne_model_launch_count(model.handle)
+        if captured:
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                lib_mod.check(lib.ne_model_profile_begin(model.handle, lib_mod.stream_handle()), "profile_begin")
+                eng._launch_step(len(slots))
+            graph.replay()
+        else:
+            lib_mod.check(lib.ne_model_profile_begin(model.handle, lib_mod.stream_handle()), "profile_begin")
+            eng._launch_step(len(slots))
+        lib_mod.check(lib.ne_model_profile_end(model.handle, ms_by, n_by, nk), "profile_end")
+        launches = lib.ne_model_launch_count(model.handle) - before
+        eng._collect(slots)
+        model.raise_on_device_error()
+        assert sum(n_by) == launches > 0
+        assert all(ms_by[i] > 0 for i in range(nk) if n_by[i])
+        results.append([n_by[i] for i in range(nk)])
+    assert results[0] == results[1]
+    eng.release(slots)
+
+
+def test_int8_shared_prefix_reads_dequantised_block_copies() -> None:
+    """int8 KV: the shared prefix's blocks are dequantised once (bf16(q * scale), the attention's
+    own conversion) and the attention reads the copies; outputs equal the unshared run, the copies
+    equal the pool blocks they stand for, and dropping the prefix unmaps them."""
+    submodule("build").build()
+    pkg = package()
+    cfg = pkg.SMALL_TEST
+    model = submodule("model").B200Model(cfg, pkg.make_weights(cfg, seed=0), num_slots=64 * 16, device="cuda:0",
+                                         max_positions=512, max_rows=512, max_seqs=8, kv_int8=True,
+                                         weight_int8=True, kv_copy_blocks=4)
+    g = torch.Generator().manual_seed(17)
+    prefix = torch.randint(0, cfg.vocab_size, (40,), generator=g).tolist()  # 2 full blocks + 8 tokens
+    prompts = [prefix + t for t in pkg.make_prompts(4, cfg.vocab_size, length=30, seed=3)]
+    plain = _engine(model, 2, True).generate(prompts, 24)
+    assert int((model.kv_copy_map >= 0).sum()) == 0
+    eng = _engine(model, 2, True)
+    shared = eng.generate(prompts, 24, shared_prefix=len(prefix))
+    assert shared == plain
+    assert int((model.kv_copy_map >= 0).sum()) == 0  # generate dropped its prefix
+    holder = eng.add_prefix(prefix)
+    mapped = (model.kv_copy_map >= 0).nonzero().flatten().tolist()
+    assert sorted(mapped) == sorted(eng.state.block_table(holder)[:2])
+    for blk in mapped:
+        c = int(model.kv_copy_map[blk])
+        for layer in range(cfg.num_hidden_layers):
+            for kv in range(2):
+                q = model.kv[layer, kv, blk * 16:(blk + 1) * 16].float()
+                s = model.kv_scales[layer, kv, blk * 16:(blk + 1) * 16].float()
+                want = (q * s[..., None]).to(torch.bfloat16)
+                assert torch.equal(model.kv_copies[layer, kv, c * 16:(c + 1) * 16], want)
+    eng.drop_prefix(holder)
+    torch.cuda.synchronize()
+    assert int((model.kv_copy_map >= 0).sum()) == 0
+    model.raise_on_device_error()
+    model.close()
