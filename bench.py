@@ -62,6 +62,8 @@ def parse_args():
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--no-kv-copies", action="store_true",
                    help="c3: convert the shared prefix's int8 blocks in every attention launch (no bf16 copies)")
+    p.add_argument("--tp-two-phase", choices=("auto", "0", "1"), default="auto",
+                   help="c5b: two-phase peer exchange (auto: from 8 ranks up)")
     p.add_argument("--tp-exchange-rows", type=int, default=512,
                    help="c5b: steps of up to this many rows use the NVLink peer exchange (0: NCCL only)")
     p.add_argument("--workload", choices=("c2", "c3", "c4", "c5b"), default="c2",
@@ -350,6 +352,7 @@ class Workload:
                             "all-reduce above; vocabulary-split LM head, argmax keys exchanged the same way), "
                             "32 users, 512-token prompts (50% motif-repeated), 256 outputs, n-gram n=3 k=4, greedy",
                 "users": 32, "k": 4, "parallelism": f"tp{args.gpus}", "tp_exchange_rows": args.tp_exchange_rows,
+                "tp_two_phase": args.tp_two_phase,
                 "l2": "no flush: every step streams 15.1 GB / N of weights + KV (> 126 MB L2)"}
         else:
             self.users, self.k, self.max_new = 256, 4, 256
@@ -417,6 +420,8 @@ def run_b200(args, dist: Dist) -> None:
         plan = tp_mod.shard_plan(cfg, dist.rank, dist.world)
         lib_path = tp_mod.nccl_library_path()
         uid = dist.broadcast_bytes(tp_mod.unique_id(lib_path) if dist.rank == 0 else None)
+        if args.tp_two_phase != "auto":
+            os.environ["NE_TP_TWO_PHASE"] = args.tp_two_phase
         weights = tp_mod.make_sharded_weights(cfg, plan, seed=0, device=device)
         model = model_mod.B200Model(tp_mod.rank_config(cfg, plan), weights, num_slots=num_blocks * 16, device=device,
                                     max_positions=max_model_len + k + 16, max_rows=max_rows, max_seqs=users + 1,

@@ -502,7 +502,13 @@ int ne_model_tp_exchange_open(ne_model* m, const void* ipc_handles) {
     }
     bases[r] = m->tp_peer[r];
   }
-  m->link = ne::tp_make_link(bases, m->tp_world, m->tp_rank, m->tp_exchange_rows, m->cfg.hidden_size);
+  // two phases from 8 ranks up (NE_TP_TWO_PHASE=0/1 overrides): measured at 160 rows, one phase
+  // is faster at 2 and 4 ranks (the middle launch costs more than the NVLink bytes it saves);
+  // each rank's column slice must hold whole 128-column GEMM tiles
+  const char* env = getenv("NE_TP_TWO_PHASE");
+  int two = env ? (env[0] == '1') : (m->tp_world >= 8);
+  if (m->cfg.hidden_size % (128 * m->tp_world)) two = 0;
+  m->link = ne::tp_make_link(bases, m->tp_world, m->tp_rank, m->tp_exchange_rows, m->cfg.hidden_size, two);
   return NE_OK;
 }
 
@@ -584,7 +590,7 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
                                                    : ne::KvShadow{}), s);
     if (rc) return rc;
     ne::Epilogue eo{};
-    eo.mode = px ? ne::EPI_PUSH_F32 : tp ? ne::EPI_STORE_F32 : ne::EPI_RESIDUAL;
+    eo.mode = px ? (m->link.two_phase ? ne::EPI_PUSH_RS : ne::EPI_PUSH_F32) : tp ? ne::EPI_STORE_F32 : ne::EPI_RESIDUAL;
     eo.link = m->link;
     eo.status = m->status;
     eo.out = m->h;
@@ -599,6 +605,10 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
     if (tp && !px) {
       rc = note(m, NE_K_COLLECTIVE, ne::tp_allreduce_sum_f32(m->partial, (size_t)R * H, m->tp_comm, s), s);
       if (rc) return rc;
+    } else if (px && m->link.two_phase) {
+      rc = note(m, NE_K_COLLECTIVE, ne::launch_tp_rs_reduce(rows->num_rows, R, m->link, m->status, s), s);
+      if (rc) return rc;
+      ++m->launches;  // (our kernel, unlike the NCCL collectives)
     }
     if (!fuse) {
       rc = note(m, NE_K_RMSNORM,
@@ -617,7 +627,7 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
                                             H, eg, s, w.w_gateup_scale, fuse ? w.ln_post : nullptr), s);
     if (rc) return rc;
     ne::Epilogue ed{};
-    ed.mode = px ? ne::EPI_PUSH_F32 : tp ? ne::EPI_STORE_F32 : ne::EPI_RESIDUAL;
+    ed.mode = px ? (m->link.two_phase ? ne::EPI_PUSH_RS : ne::EPI_PUSH_F32) : tp ? ne::EPI_STORE_F32 : ne::EPI_RESIDUAL;
     ed.link = m->link;
     ed.status = m->status;
     ed.out = m->h;
@@ -633,6 +643,10 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
     if (tp && !px) {
       rc = note(m, NE_K_COLLECTIVE, ne::tp_allreduce_sum_f32(m->partial, (size_t)R * H, m->tp_comm, s), s);
       if (rc) return rc;
+    } else if (px && m->link.two_phase) {
+      rc = note(m, NE_K_COLLECTIVE, ne::launch_tp_rs_reduce(rows->num_rows, R, m->link, m->status, s), s);
+      if (rc) return rc;
+      ++m->launches;  // (our kernel, unlike the NCCL collectives)
     }
   }
   // final norm over the rows that get logits (gathered to the front of x), keys cleared

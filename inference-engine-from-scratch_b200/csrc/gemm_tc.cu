@@ -246,6 +246,18 @@ __device__ void epilogue_rows(const Epilogue& e, int tile_n, int m_begin, int co
       for (int r = 0; r < TP_MAX_WORLD; ++r)
         if (r < l.world) *reinterpret_cast<float4*>(l.rows[r] + off) = a;
     }
+  } else if (MODE == EPI_PUSH_RS) {
+    // unit = 4 consecutive fp32 outputs of one row, stored once: into the owner's slice slot
+    const TpLink& l = e.link;
+    const int slice = l.hidden / l.world;
+    const int dst = n0 / slice;
+    const unsigned par = __ldcg(l.instance) & 1u;
+    const int units = count * (GEMM_BM / 4);
+    for (int u = tid; u < units; u += GEMM_THREADS) {
+      const int m = u >> 5, c = (u & 31) * 4;
+      const float4 a = lds_f4(acc_s + (uint32_t)((m * GEMM_BM + c) * 4));
+      *reinterpret_cast<float4*>(tp_slice_slot(l, dst, par, l.rank, m_begin + m) + (n0 - dst * slice) + c) = a;
+    }
   } else if (MODE == EPI_SWIGLU) {
     // unit = 8 consecutive features j of one row: gate rows j, up rows 64 + j of the tile
     const int units = count * 8;
@@ -545,6 +557,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tmem_dealloc(tmem_base, tmem_cols);
     }
     if (MODE == EPI_PUSH_F32) tp_signal_cta(p.epi.link);  // every CTA counts, rows or not
+    if (MODE == EPI_PUSH_RS) tp_signal_owner_cta(p.epi.link, tile_n);
     return;
   }
 
@@ -769,6 +782,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   // every CTA signals, whatever its rows and even after a timeout, so that no peer waits on it
   if (MODE == EPI_PUSH_F32) tp_signal_cta(p.epi.link);
+  if (MODE == EPI_PUSH_RS) tp_signal_owner_cta(p.epi.link, tile_n);
 
   // ------------------------------------------------------------------ teardown
   if (!ok && warp == 0 && lane == 0) {
@@ -875,7 +889,7 @@ int active_clusters_mode(int splits, int smem) {
   X(EPI_STORE, 0) X(EPI_STORE, CONV_W8) X(EPI_RESIDUAL, 0) X(EPI_RESIDUAL, CONV_W8) X(EPI_SWIGLU, 0)   \
   X(EPI_SWIGLU, CONV_W8) X(EPI_SWIGLU, CONV_NX) X(EPI_SWIGLU, CONV_W8 | CONV_NX) X(EPI_QKV, 0)          \
   X(EPI_QKV, CONV_W8) X(EPI_QKV, CONV_NX) X(EPI_QKV, CONV_W8 | CONV_NX) X(EPI_ARGMAX, 0) X(EPI_LOGITS, 0) \
-  X(EPI_STORE_F32, 0) X(EPI_PUSH_F32, 0) X(EPI_SPLIT_F32, 0) X(EPI_SPLIT_F32, CONV_W8)
+  X(EPI_STORE_F32, 0) X(EPI_PUSH_F32, 0) X(EPI_SPLIT_F32, 0) X(EPI_SPLIT_F32, CONV_W8) X(EPI_PUSH_RS, 0)
 
 int conv_bits(const GemmParams& p) { return (p.w_scale ? CONV_W8 : 0) | (p.x_norm_w ? CONV_NX : 0); }
 

@@ -51,6 +51,8 @@ enum EpilogueMode : int {
                      // each CTA signals every rank (peer exchange of a tensor-parallel split)
   EPI_SPLIT_F32 = 8, // split-K without the cluster exchange: split s stores its fp32 partial tile to
                      // out_f32 + s * split_stride; the consumer (the next RMSNorm) sums the splits
+  EPI_PUSH_RS = 9,   // two-phase peer exchange: the fp32 tile goes only to the rank owning its
+                     // column slice (reduce-scatter), then the CTA signals that rank
 };
 
 struct Epilogue {

@@ -94,7 +94,14 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(__nv_bfloat16* __restrict_
         float av[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) av[k] = 0.f;
-        if (exch) {
+        if (exch && link.two_phase) {  // the sums, gathered: each column slice from its owner
+          const int col = (c0 + 32 * j) * 8, slice = hidden / link.world, owner = col / slice;
+          const float4* ar = reinterpret_cast<const float4*>(tp_slice_slot(link, link.rank, inst & 1u, owner, src) +
+                                                             (col - owner * slice));
+          const float4 a0 = __ldcg(ar), a1 = __ldcg(ar + 1);
+          av[0] = a0.x; av[1] = a0.y; av[2] = a0.z; av[3] = a0.w;
+          av[4] = a1.x; av[5] = a1.y; av[6] = a1.z; av[7] = a1.w;
+        } else if (exch) {
           for (int q = 0; q < link.world; ++q) {
             const float4* ar = reinterpret_cast<const float4*>(tp_row_slot(link, inst & 1u, q, src) +
                                                                (c0 + 32 * j) * 8);
@@ -157,6 +164,32 @@ __global__ void keys_to_ids_kernel(const unsigned long long* keys, const int32_t
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   const int n = count ? min(*count, max_count) : max_count;
   if (i < n) ids[i] = (int32_t)argmax_key_index(keys[i]);
+}
+
+// Middle of a two-phase peer exchange: wait for every rank's partial tiles of this rank's column
+// slice (reduce-scatter), add them in rank order, push the sums to every rank's slot of this rank
+// (all-gather) and signal; the next RMSNorm reads the gathered rows. Closes one exchange and opens
+// the next, so the exchange count advances by two per reduction.
+__global__ void tp_rs_reduce_kernel(const int32_t* rows_dev, int max_rows, const TpLink link, int* status) {
+  pdl_prologue();
+  const int n = rows_dev ? min(*rows_dev, max_rows) : max_rows;
+  const unsigned inst = tp_wait_all(link, status);
+  const unsigned par = inst & 1u, npar = (inst + 1u) & 1u;
+  const int slice = link.hidden / link.world, per_row = slice / 4;
+  const long long units = (long long)n * per_row;
+  for (long long u = (long long)blockIdx.x * blockDim.x + threadIdx.x; u < units; u += (long long)gridDim.x * blockDim.x) {
+    const int row = (int)(u / per_row), c = (int)(u % per_row) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < link.world; ++q) {
+      const float4 a = __ldcg(reinterpret_cast<const float4*>(tp_slice_slot(link, link.rank, par, q, row) + c));
+      acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+    }
+#pragma unroll
+    for (int r = 0; r < TP_MAX_WORLD; ++r)
+      if (r < link.world) *reinterpret_cast<float4*>(tp_slice_slot(link, r, npar, link.rank, row) + c) = acc;
+  }
+  tp_signal_cta(link);            // opens the all-gather exchange
+  tp_reader_done(link, inst);     // closes the reduce-scatter exchange
 }
 
 // Argmax keys of a vocabulary-split LM head: every rank pushes its per-row maxima into every
@@ -556,6 +589,14 @@ int launch_tp_keys_exchange(unsigned long long* keys, const int32_t* count, int 
   if (link.world < 1 || max_count > link.max_rows) return NE_ERR_INVALID;
   if (max_count <= 0) return NE_OK;
   return launch_kernel(tp_keys_exchange_kernel, dim3(1), dim3(256), 0, stream, keys, count, max_count, link,
+                       status) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
+}
+
+int launch_tp_rs_reduce(const int32_t* rows_dev, int max_rows, const TpLink& link, int* status, cudaStream_t stream) {
+  if (link.world < 1 || !link.two_phase || max_rows > link.max_rows || max_rows < 1) return NE_ERR_INVALID;
+  const long long units = (long long)max_rows * (link.hidden / link.world / 4);
+  const int blocks = (int)std::min<long long>(148, std::max<long long>(1, (units + 255) / 256));
+  return launch_kernel(tp_rs_reduce_kernel, dim3(blocks), dim3(256), 0, stream, rows_dev, max_rows, link,
                        status) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 

@@ -35,6 +35,8 @@ int launch_rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, i
                    unsigned long long* zero_keys, cudaStream_t stream, const float* add = nullptr,
                    int add_count = 1, long long add_stride = 0, const TpLink* link = nullptr,
                    int* status = nullptr);
+// Middle launch of a two-phase peer exchange (reduce-scatter sums -> all-gather pushes).
+int launch_tp_rs_reduce(const int32_t* rows_dev, int max_rows, const TpLink& link, int* status, cudaStream_t stream);
 // Peer exchange of the LM head's argmax keys over a vocabulary split: push this rank's keys
 // [count] to every rank, wait (bounded) for every rank's, keep the largest (one CTA).
 int launch_tp_keys_exchange(unsigned long long* keys, const int32_t* count, int max_count, const TpLink& link,

@@ -97,7 +97,7 @@ TpRegionLayout tp_region_layout(int world, int max_rows, int hidden) {
   return l;
 }
 
-TpLink tp_make_link(void* const* bases, int world, int rank, int max_rows, int hidden) {
+TpLink tp_make_link(void* const* bases, int world, int rank, int max_rows, int hidden, int two_phase) {
   const TpRegionLayout lay = tp_region_layout(world, max_rows, hidden);
   TpLink l{};
   for (int r = 0; r < world; ++r) {
@@ -113,6 +113,7 @@ TpLink tp_make_link(void* const* bases, int world, int rank, int max_rows, int h
   l.rank = rank;
   l.max_rows = max_rows;
   l.hidden = hidden;
+  l.two_phase = two_phase;
   return l;
 }
 

@@ -50,6 +50,11 @@ struct TpLink {
   int rank;
   int max_rows;
   int hidden;
+  // two phases per reduction (default from 8 ranks): the row-parallel GEMM pushes each output tile only to
+  // the rank that owns its hidden / world columns (reduce-scatter), that rank adds the world
+  // partials of its columns and pushes the sums to every rank (all-gather), so a rank sends
+  // 2 (world - 1) / world of the rows over NVLink instead of world - 1 times them
+  int two_phase;
 };
 
 struct TpRegionLayout {
@@ -60,12 +65,24 @@ int tp_exchange_alloc(size_t bytes, void** ptr, void* ipc_handle);
 int tp_exchange_open(const void* ipc_handle, void** ptr);
 void tp_exchange_close(void* ptr, bool own);
 // View of the regions (``bases[r]``: rank r's region as mapped here) for the kernels.
-TpLink tp_make_link(void* const* bases, int world, int rank, int max_rows, int hidden);
+TpLink tp_make_link(void* const* bases, int world, int rank, int max_rows, int hidden, int two_phase);
 
 #ifdef __CUDACC__
 // Release one source's arrivals on rank ``dst``'s counter (after this CTA's stores; see above).
 __device__ __forceinline__ void tp_signal(const TpLink& l, int dst, unsigned long long inc) {
   asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(l.arrivals[dst] + l.rank), "l"(inc) : "memory");
+}
+// Every CTA of a reduce-scatter writer launch (grid: splits x tiles x m-blocks over the output
+// columns), all threads: signal the one rank whose column slice this CTA's tile belongs to. The
+// CTAs of one slice add exactly TP_QUANTUM to their owner's counter of this source.
+__device__ __forceinline__ void tp_signal_owner_cta(const TpLink& l, int tile_n) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int tps = l.hidden / l.world / 128;  // 128-column tiles per slice
+    const unsigned long long per_owner = (unsigned long long)gridDim.x * tps * gridDim.z;
+    const bool first = blockIdx.x == 0 && blockIdx.z == 0 && tile_n % tps == 0;
+    tp_signal(l, tile_n / tps, first ? TP_QUANTUM - (per_owner - 1) : 1ull);
+  }
 }
 // Every CTA of a writer launch, all threads: signal every rank once this CTA's stores are issued.
 __device__ __forceinline__ void tp_signal_cta(const TpLink& l) {
@@ -120,6 +137,11 @@ __device__ __forceinline__ void tp_reader_done(const TpLink& l, unsigned inst) {
 // Row slot of source ``src`` on this rank for parity ``par``.
 __device__ __forceinline__ const float* tp_row_slot(const TpLink& l, unsigned par, int src, int row) {
   return l.rows[l.rank] + (((size_t)par * l.world + src) * l.max_rows + row) * (size_t)l.hidden;
+}
+// Two-phase slots hold column slices: rank r's slot of source ``src``, row ``row`` ([hidden / world]).
+__device__ __forceinline__ float* tp_slice_slot(const TpLink& l, int r, unsigned par, int src, int row) {
+  const int slice = l.hidden / l.world;
+  return l.rows[r] + (((size_t)par * l.world + src) * l.max_rows + row) * (size_t)slice;
 }
 #endif
 

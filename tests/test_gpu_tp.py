@@ -41,8 +41,8 @@ def test_two_rank_split_serves_the_unsplit_outputs(tmp_path) -> None:
     r1 = json.loads((tmp_path / "rank.1.json").read_text())
     assert r0["peer_exchange"] and r1["peer_exchange"]
     # both ranks take the same decisions (max-reduced argmax keys), eagerly and through graphs,
-    # over the peer exchange, the exchange for steps only, and NCCL only
-    for name in ("eager", "graphs", "mixed", "nccl"):
+    # over the peer exchange (one and two phases), the exchange for steps only, and NCCL only
+    for name in ("eager", "graphs", "mixed", "nccl", "two_phase"):
         assert r0[name] == r1[name] == r0["graphs"], name
     # and they equal the unsplit model's tokens (fp32 partial sums: only the summation order differs)
     assert r0["graphs"] == r0["unsplit"]

@@ -2,7 +2,8 @@
 
 Every rank serves the same prompts on its shard of a small Qwen3-8B-like model (TP = world size,
 greedy): with the peer exchange for every call (eagerly and through CUDA graphs), with the
-exchange for the steps only (prefill through NCCL), and through NCCL only. Then rank 0 prefills
+exchange for the steps only (prefill through NCCL), through NCCL only, and with the two-phase
+exchange. Then rank 0 prefills
 alone on a split model, so that its bounded exchange waits run out. Rank 0 finally serves the
 prompts on the unsplit model (TP = 1, the oracle for the split: the same seeded weights). Each rank
 writes its outputs to ``<out>.<rank>.json``.
@@ -76,6 +77,13 @@ def main() -> None:
         model = split_model(rows)
         result[name] = serve(model, prompts, graphs=True)
         model.close()
+    # the two-phase exchange (reduce-scatter in the GEMM, all-gather by the middle launch), which
+    # the split uses from eight ranks up, forced on two
+    os.environ["NE_TP_TWO_PHASE"] = "1"
+    model = split_model(512)
+    result["two_phase"] = serve(model, prompts, graphs=True)
+    model.close()
+    del os.environ["NE_TP_TWO_PHASE"]
     # a rank that stops taking part: rank 0 prefills alone, its bounded waits run out (1 s per
     # exchange) and the device status reports the timeout; rank 1 launches nothing
     model = split_model(512)
