@@ -10,6 +10,7 @@ Follows (paths relative to ``nanoengine/src/nanoengine``):
 * ``SpeculativeGenerator._generate`` / ``_run_speculative_step``
                                          engine/speculative/speculative_generator.py:50-85
 * ``find_finish_reason``                 engine/sampling.py:54-62
+* ``DraftModelProposer``                 engine/speculative/proposers.py:63-106 (``DraftProposer``)
 
 Every step is recorded (draft, block table after the reservation, verify logits, emitted tokens,
 ``num_cached_tokens`` after the rollback), which is what the parity tests compare.
@@ -176,6 +177,56 @@ class OracleRunner:
         return qwen3.compute_logits(self.weights, self.cfg, hidden[0, :count])
 
 
+class DraftProposer:
+    """engine/speculative/proposers.py:63-106: a draft model of the same family runs
+    ``num_tokens`` steps ahead of the target on its own paged cache (``runner``); the first step
+    catches up on the tokens the target added. Greedy drafts are the draft's argmax; sampled ones
+    are drawn from the request's uniform stream (the same stream verification reads)."""
+
+    def __init__(self, runner: OracleRunner, stable: bool = False) -> None:
+        self.runner = runner
+        self.stable = stable
+        self.drafts: dict[str, Seq] = {}
+
+    def propose(self, seq: Seq, num_tokens: int, uniforms) -> tuple[list[int], torch.Tensor | None]:
+        draft = self._sync(seq)
+        guesses: list[int] = []
+        distributions = []
+        for _ in range(num_tokens):
+            self.runner.tables.reserve(draft.request_id, draft.num_tokens)
+            logits = self.runner.score_tokens(draft, draft.num_tokens - draft.num_cached_tokens)[-1]
+            probabilities = verify.token_probabilities(logits, seq.temperature, seq.top_p, self.stable)
+            if seq.temperature == verify.GREEDY_TEMPERATURE:
+                guess = int(torch.argmax(probabilities).item())
+            else:
+                guess = verify.inverse_cdf(probabilities, next(uniforms))
+            draft.token_ids.append(guess)
+            guesses.append(guess)
+            distributions.append(probabilities)
+        return guesses, torch.stack(distributions) if distributions else None
+
+    def release(self, seq: Seq) -> None:
+        if self.drafts.pop(seq.request_id, None) is not None:
+            self.runner.tables.free(seq.request_id)
+
+    def _sync(self, seq: Seq) -> Seq:
+        """proposers.py:93-106: the draft's tokens become the target's; its cache is kept for
+        the common prefix."""
+        draft = self.drafts.get(seq.request_id)
+        if draft is None:
+            draft = Seq(seq.request_id, list(seq.token_ids[: seq.num_prompt_tokens]), seq.num_prompt_tokens,
+                        seq.max_new_tokens, seq.temperature, seq.top_p, seq.ignore_eos)
+            self.drafts[seq.request_id] = draft
+        common = 0
+        for a, b in zip(draft.token_ids, seq.token_ids):
+            if a != b:
+                break
+            common += 1
+        draft.token_ids = list(seq.token_ids)
+        draft.num_cached_tokens = min(draft.num_cached_tokens, common)
+        return draft
+
+
 @dataclass
 class StepRecord:
     draft: list[int]
@@ -220,9 +271,11 @@ def generate(
     keep_logits: bool = True,
     free_at_end: bool = True,
     stable: bool = False,
+    proposer: DraftProposer | None = None,
 ) -> Generation:
-    """engine/speculative/speculative_generator.py:42-85 with ``NgramProposer`` drafts
-    (``stable``: top-p ties by ascending id, as ``verify.apply_top_p`` documents)."""
+    """engine/speculative/speculative_generator.py:42-85 with ``NgramProposer`` drafts, or the
+    draft model's (``proposer``) (``stable``: top-p ties by ascending id, as
+    ``verify.apply_top_p`` documents)."""
     stream = _CountingStream(uniforms if uniforms is not None else iter(()))
     out = Generation()
     try:
@@ -241,14 +294,18 @@ def generate(
             before = stream.count
             remaining = seq.max_new_tokens - seq.num_generated_tokens
             num_guesses = max(0, min(num_speculative_tokens, remaining - 1))
-            draft = ngram.propose(seq.token_ids, num_guesses, max_ngram) if num_guesses else []
+            draft_probabilities = None
+            if proposer is not None:
+                draft, draft_probabilities = proposer.propose(seq, num_guesses, stream) if num_guesses else ([], None)
+            else:
+                draft = ngram.propose(seq.token_ids, num_guesses, max_ngram) if num_guesses else []
             length_before = seq.num_tokens
             seq.token_ids.extend(draft)
             runner.tables.reserve(seq.request_id, seq.num_tokens)
             table = list(runner.tables.tables[seq.request_id])
             target_logits = runner.score_tokens(seq, 1 + len(draft))
             new_tokens = verify.verify_proposal(
-                draft, None, target_logits, seq.temperature, seq.top_p, stream, stable
+                draft, draft_probabilities, target_logits, seq.temperature, seq.top_p, stream, stable
             )
             kept = len(new_tokens) - 1
             del seq.token_ids[length_before:]
@@ -268,3 +325,5 @@ def generate(
     finally:
         if free_at_end:
             runner.tables.free(seq.request_id)
+        if proposer is not None:
+            proposer.release(seq)

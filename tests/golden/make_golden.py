@@ -18,6 +18,9 @@ Fixtures written (all small):
 * ``quant_cases.pt``         quantize_vectors
 * ``spec_small_<mode>.pt``   serial speculative runs of a small d=128 Qwen3 (fp32, bf16, int8,
                              sampled): per step draft, block table, logits digest, new tokens
+* ``spec_small_draft_bf16.pt`` / ``spec_small_draft_same_bf16.pt``
+                             the same with DraftModelProposer drafts: a one-layer draft (seed 1),
+                             and the target itself as its own draft (every guess accepted)
 * ``spec_config1_fp32.pt``   BASELINE config 1 exactly (Qwen3-0.6B fp32, seed 0, 64-token motif
                              prompt, 128 greedy tokens, n=3, k=4, 16-token blocks)
 """
@@ -211,7 +214,9 @@ def quant_cases(ref: Ref) -> dict:
 
 
 def spec_run(ref: Ref, inj: UniformInjector, cfg, weights, dtype, prompts, *, max_new, k, max_ngram,
-             num_blocks, int8=False, temperature=0.0, top_p=1.0, seeds=None, stop_ids=frozenset()):
+             num_blocks, int8=False, temperature=0.0, top_p=1.0, seeds=None, stop_ids=frozenset(), draft=None):
+    """``draft`` = (config, weights): DraftModelProposer over that model (its own paged cache of
+    ``num_blocks`` blocks) instead of NgramProposer; the draft's top-2 logits per guess are kept."""
     model = build_model(ref, cfg, weights, dtype)
     if int8:
         ref.int8.quantize_linear_layers(model)
@@ -246,9 +251,33 @@ def spec_run(ref: Ref, inj: UniformInjector, cfg, weights, dtype, prompts, *, ma
 
     ref.specgen.verify_proposal = recording_verify
     metrics = ref.metrics.EngineMetrics()
-    gen = ref.specgen.SpeculativeGenerator(
-        runner, ref.proposers.NgramProposer(max_ngram), k, stop_ids, cpu, metrics
-    )
+    if draft is None:
+        proposer = ref.proposers.NgramProposer(max_ngram)
+    else:
+        draft_cfg, draft_weights = draft
+        draft_model = build_model(ref, draft_cfg, draft_weights, dtype)
+        draft_pool = ref.pool.KVCachePool(draft_model.config, num_blocks * 16, cpu, dtype)
+        draft_allocator = ref.paged.PagedSlotAllocator(num_blocks, 16, cpu)
+        pending_top2: list = []
+
+        class DraftRecordingRunner(ref.runner.ModelRunner):
+            def score_tokens(self, sequence, token_count):
+                logits = super().score_tokens(sequence, token_count)
+                pending_top2.append(torch.topk(logits[-1].float(), 2).values)
+                return logits
+
+        proposer = ref.proposers.DraftModelProposer(
+            DraftRecordingRunner(draft_model, draft_pool, draft_allocator, cpu), cpu)
+        real_score = RecordingRunner.score_tokens
+
+        def score_with_draft_record(self, sequence, token_count):
+            logits = real_score(self, sequence, token_count)
+            current["steps"][-1]["draft_top2"] = torch.stack(pending_top2) if pending_top2 else torch.empty(0, 2)
+            pending_top2.clear()
+            return logits
+
+        RecordingRunner.score_tokens = score_with_draft_record
+    gen = ref.specgen.SpeculativeGenerator(runner, proposer, k, stop_ids, cpu, metrics)
     try:
         for index, prompt in enumerate(prompts):
             seed = None if seeds is None else seeds[index]
@@ -274,29 +303,41 @@ def spec_run(ref: Ref, inj: UniformInjector, cfg, weights, dtype, prompts, *, ma
     accepted = metrics.registry.get_sample_value("nanoengine_speculative_accepted_tokens_total")
     return {"records": records, "digest_ids": ids, "proposed": proposed, "accepted": accepted,
             "k": k, "max_ngram": max_ngram, "max_new": max_new, "num_blocks": num_blocks,
-            "temperature": temperature, "top_p": top_p, "int8": int8, "dtype": str(dtype)}
+            "temperature": temperature, "top_p": top_p, "int8": int8, "dtype": str(dtype),
+            "proposer": "ngram" if draft is None else "draft"}
 
 
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, help="the reference's nanoengine/src directory")
     parser.add_argument("--skip-full", action="store_true", help="skip the Qwen3-0.6B config-1 run")
+    parser.add_argument("--only-draft", action="store_true", help="write only the draft-model fixtures")
     args = parser.parse_args()
     torch.set_num_threads(max(1, torch.get_num_threads()))
     ref = Ref(args.reference)
     inj = UniformInjector(ref)
     pkg = importlib.import_module("inference-engine-from-scratch_b200")
 
-    (HERE / "ngram_cases.json").write_text(json.dumps(ngram_cases(ref)))
-    torch.save(verify_cases(ref, inj), HERE / "verify_cases.pt")
-    torch.save(top_p_cases(ref), HERE / "top_p_cases.pt")
-    torch.save(quant_cases(ref), HERE / "quant_cases.pt")
-
     cfg = pkg.SMALL_TEST
     weights = pkg.make_weights(cfg, seed=0)
     prompts = [pkg.make_prompt(cfg.vocab_size, 48, 0, True), pkg.make_prompt(cfg.vocab_size, 40, 1, False),
                pkg.make_prompt(cfg.vocab_size, 33, 2, True)]
     common = dict(max_new=40, k=4, max_ngram=3, num_blocks=64)
+    # DraftModelProposer: a one-layer draft of the same family (seed 1), and the target itself
+    draft_cfg = pkg.Qwen3Config(**{**{f: getattr(cfg, f) for f in cfg.__dataclass_fields__}, "num_hidden_layers": 1})
+    torch.save(spec_run(ref, inj, cfg, weights, torch.bfloat16, prompts,
+                        draft=(draft_cfg, pkg.make_weights(draft_cfg, seed=1)), **common),
+               HERE / "spec_small_draft_bf16.pt")
+    torch.save(spec_run(ref, inj, cfg, weights, torch.bfloat16, prompts, draft=(cfg, weights), **common),
+               HERE / "spec_small_draft_same_bf16.pt")
+    if args.only_draft:
+        return
+
+    (HERE / "ngram_cases.json").write_text(json.dumps(ngram_cases(ref)))
+    torch.save(verify_cases(ref, inj), HERE / "verify_cases.pt")
+    torch.save(top_p_cases(ref), HERE / "top_p_cases.pt")
+    torch.save(quant_cases(ref), HERE / "quant_cases.pt")
+
     torch.save(spec_run(ref, inj, cfg, weights, torch.float32, prompts, **common), HERE / "spec_small_fp32.pt")
     torch.save(spec_run(ref, inj, cfg, weights, torch.bfloat16, prompts, **common), HERE / "spec_small_bf16.pt")
     torch.save(spec_run(ref, inj, cfg, weights, torch.bfloat16, prompts, int8=True, **common),

@@ -85,12 +85,17 @@ def test_quantize_vectors_is_bit_exact() -> None:
             assert torch.all((back - case["values"]).abs() <= s / 2 + 1e-6)
 
 
-def _check_run(golden, cfg, weights, dtype, atol):
+def _check_run(golden, cfg, weights, dtype, atol, draft=None):
     int8 = golden["int8"]
     w = {k: v.to(dtype) for k, v in weights.items()}
     if int8:
         w = qwen3.quantize_weights(w)
     runner = speculative.OracleRunner(w, cfg, golden["num_blocks"], 16, dtype, int8_kv=int8)
+    proposer = None
+    if draft is not None:  # (config, weights) of the draft model, its own cache
+        draft_cfg, draft_weights = draft
+        proposer = speculative.DraftProposer(speculative.OracleRunner(
+            {k: v.to(dtype) for k, v in draft_weights.items()}, draft_cfg, golden["num_blocks"], 16, dtype))
     ids = golden["digest_ids"]
     for index, record in enumerate(golden["records"]):
         seq = speculative.Seq(
@@ -99,7 +104,7 @@ def _check_run(golden, cfg, weights, dtype, atol):
         )
         seed = record["seed"]
         stream = philox.UniformStream(0 if seed is None else seed)
-        out = speculative.generate(runner, seq, golden["k"], golden["max_ngram"], uniforms=stream)
+        out = speculative.generate(runner, seq, golden["k"], golden["max_ngram"], uniforms=stream, proposer=proposer)
         assert out.prefill_block_table == record["prefill_block_table"]
         assert len(out.steps) == len(record["steps"])
         for mine, ref in zip(out.steps, record["steps"]):
@@ -136,3 +141,20 @@ def test_serial_speculation_config1_qwen3_0_6b_fp32() -> None:
     assert golden["proposed"] == 63 and golden["accepted"] == 62
     _check_run(golden, pkg.QWEN3_0_6B, pkg.make_weights(pkg.QWEN3_0_6B, seed=0), torch.float32,
                FP32_LOGITS_ATOL)
+
+
+@pytest.mark.parametrize("fixture", ["spec_small_draft_bf16.pt", "spec_small_draft_same_bf16.pt"])
+def test_serial_speculation_with_a_draft_model(fixture) -> None:
+    """DraftModelProposer (proposers.py:63-106): a one-layer draft of the same family, and the
+    target as its own draft (every guess kept)."""
+    pkg = package()
+    cfg = pkg.SMALL_TEST
+    golden = load_golden(fixture)
+    assert golden["proposer"] == "draft"
+    if "same" in fixture:
+        draft = (cfg, pkg.make_weights(cfg, seed=0))
+        assert golden["accepted"] == golden["proposed"] > 0
+    else:
+        draft_cfg = pkg.Qwen3Config(**{**{f: getattr(cfg, f) for f in cfg.__dataclass_fields__}, "num_hidden_layers": 1})
+        draft = (draft_cfg, pkg.make_weights(draft_cfg, seed=1))
+    _check_run(golden, cfg, pkg.make_weights(cfg, seed=0), torch.bfloat16, BF16_LOGITS_ATOL, draft=draft)
