@@ -256,6 +256,26 @@ NE_API int ne_prefill(ne_model* model, const ne_batch_state* state, const int32_
 NE_API int ne_spec_step(ne_model* model, const ne_batch_state* state, const int32_t* seq_slot, int num_seqs,
                  int k, int max_ngram, const ne_step_outputs* out, void* stream);
 
+/*
+ * Draft-model drafts (DraftModelProposer, engine/speculative/proposers.py:63-106), greedy: the
+ * draft model has its own ne_batch_state ``draft`` (same slots, same history stride, its own KV
+ * pool and block FIFO; max_new_tokens large, ignore-eos, temperature 0). Per step:
+ *   ne_draft_sync(target, draft, ...)   the draft sequences take the target's tokens and keep
+ *                                       their cache for the common prefix (_sync_draft);
+ *   k x ne_prefill(draft model, draft)  each forwards the draft's uncached tokens (the first call
+ *                                       catches up on the target's new tokens) and appends the
+ *                                       draft's argmax: k guesses;
+ *   ne_spec_step_drafted(target model)  the guesses after the target's tokens become the drafts
+ *                                       (cap max(0, min(k, remaining - 1)), -1 for idle entries),
+ *                                       then the same verify and acceptance as ne_spec_step.
+ * The draft's guesses are one-hot drafts (the draft is greedy), so acceptance is the greedy one.
+ */
+NE_API int ne_draft_sync(const ne_batch_state* target, const ne_batch_state* draft, const int32_t* seq_slot,
+                         int num_seqs, int k, void* stream);
+NE_API int ne_spec_step_drafted(ne_model* model, const ne_batch_state* state, const ne_batch_state* draft,
+                                const int32_t* seq_slot, int num_seqs, int k, const ne_step_outputs* out,
+                                void* stream);
+
 /* ---------------------------------------------------------------- sampled acceptance */
 /*
  * Sequences with temperature > 0 are verified against their full target distribution

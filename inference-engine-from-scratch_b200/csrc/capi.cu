@@ -828,16 +828,13 @@ int ne_prefill(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, i
                                        s), s);
 }
 
-int ne_spec_step(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int k, int max_ngram,
-                 const ne_step_outputs* out, void* stream) {
-  if (!m || !st || !seq_slot || !out || num_seqs <= 0 || k < 1 || max_ngram < 1) return NE_ERR_INVALID;
+namespace {
+// The speculative step after its drafts (m->rb.draft_len, histories) are in place: reserve and
+// plan, verify forward, acceptance.
+int spec_step_tail(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int k,
+                   const ne_step_outputs* out, cudaStream_t s) {
   const int max_rows = num_seqs * (k + 1);
-  if (max_rows > m->max_rows || num_seqs > m->max_seqs) return NE_ERR_WORKSPACE;
-  cudaStream_t s = as_stream(stream);
-  int rc = note(m, NE_K_NGRAM, ne::launch_ngram(*st, seq_slot, num_seqs, k, max_ngram, 1, m->rb.draft_len, m->status, s),
-                s);
-  if (rc) return rc;
-  rc = note(m, NE_K_PLAN,
+  int rc = note(m, NE_K_PLAN,
             ne::launch_plan(*st, seq_slot, num_seqs, ne::PLAN_SPEC, max_rows, 0, m->cfg.block_size,
                             m->cfg.num_cache_slots, m->rb, m->status, s), s);
   if (rc) return rc;
@@ -846,11 +843,42 @@ int ne_spec_step(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot,
     if (max_rows > m->sample_rows) return NE_ERR_WORKSPACE;
     return sampled_tail(m, st, seq_slot, num_seqs, k, rows, true, out, s);
   }
-  rc = ne_forward(m, &rows, NE_LM_ARGMAX, nullptr, nullptr, stream);
+  rc = ne_forward(m, &rows, NE_LM_ARGMAX, nullptr, nullptr, s);
   if (rc) return rc;
   return note(m, NE_K_ACCEPT,
               ne::launch_accept_greedy(*st, seq_slot, num_seqs, k, ne::PLAN_SPEC, m->rb, m->keys, *out, m->status, s),
               s);
+}
+}  // namespace
+
+int ne_spec_step(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int k, int max_ngram,
+                 const ne_step_outputs* out, void* stream) {
+  if (!m || !st || !seq_slot || !out || num_seqs <= 0 || k < 1 || max_ngram < 1) return NE_ERR_INVALID;
+  const int max_rows = num_seqs * (k + 1);
+  if (max_rows > m->max_rows || num_seqs > m->max_seqs) return NE_ERR_WORKSPACE;
+  cudaStream_t s = as_stream(stream);
+  const int rc = note(m, NE_K_NGRAM,
+                      ne::launch_ngram(*st, seq_slot, num_seqs, k, max_ngram, 1, m->rb.draft_len, m->status, s), s);
+  if (rc) return rc;
+  return spec_step_tail(m, st, seq_slot, num_seqs, k, out, s);
+}
+
+int ne_draft_sync(const ne_batch_state* target, const ne_batch_state* draft, const int32_t* seq_slot, int num_seqs,
+                  int k, void* stream) {
+  if (!target || !draft || !seq_slot || num_seqs <= 0 || k < 1) return NE_ERR_INVALID;
+  return ne::launch_draft_sync(*target, *draft, seq_slot, num_seqs, k, as_stream(stream));
+}
+
+int ne_spec_step_drafted(ne_model* m, const ne_batch_state* st, const ne_batch_state* draft, const int32_t* seq_slot,
+                         int num_seqs, int k, const ne_step_outputs* out, void* stream) {
+  if (!m || !st || !draft || !seq_slot || !out || num_seqs <= 0 || k < 1) return NE_ERR_INVALID;
+  const int max_rows = num_seqs * (k + 1);
+  if (max_rows > m->max_rows || num_seqs > m->max_seqs) return NE_ERR_WORKSPACE;
+  cudaStream_t s = as_stream(stream);
+  const int rc = note(m, NE_K_NGRAM,
+                      ne::launch_draft_propose(*st, *draft, seq_slot, num_seqs, k, m->rb.draft_len, m->status, s), s);
+  if (rc) return rc;
+  return spec_step_tail(m, st, seq_slot, num_seqs, k, out, s);
 }
 
 int ne_gemm_bf16(const void* x, const void* w, void* y, int M, int N, int K, int32_t* status, void* stream) {

@@ -220,6 +220,58 @@ __global__ void tp_keys_exchange_kernel(unsigned long long* keys, const int32_t*
   tp_reader_done(link, inst);
 }
 
+// ------------------------------------------------------------------ draft-model drafts
+// DraftModelProposer._sync_draft (engine/speculative/proposers.py:93-106) for one batch entry per
+// CTA: the draft sequence (same slot in the draft model's state) takes the target's tokens and
+// keeps its cache for the common prefix. Only the draft's last k positions can differ from the
+// target (its guesses of the previous step), so the first mismatch is searched there.
+__global__ void draft_sync_kernel(ne_batch_state st, ne_batch_state dt, const int32_t* __restrict__ seq_slot, int k) {
+  pdl_prologue();
+  const int s = seq_slot[blockIdx.x];
+  if (s < 0 || s >= st.max_seqs || s >= dt.max_seqs || (st.flags[s] & NE_SEQ_FINISHED)) return;
+  const int Lt = st.seq_len[s], Ld = dt.seq_len[s];
+  const int32_t* ht = st.history + (long long)s * st.history_stride;
+  int32_t* hd = dt.history + (long long)s * dt.history_stride;
+  const int lo = max(0, Ld - k), hi = min(Ld, Lt);
+  __shared__ int first;
+  if (threadIdx.x == 0) first = max(lo, hi);
+  __syncthreads();
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x)
+    if (hd[i] != ht[i]) atomicMin(&first, i);
+  __syncthreads();
+  const int common = min(first, Lt);
+  for (int i = common + threadIdx.x; i < Lt && i < dt.history_stride; i += blockDim.x) hd[i] = ht[i];
+  if (threadIdx.x == 0) {
+    dt.seq_len[s] = Lt;
+    dt.num_cached[s] = min(dt.num_cached[s], common);
+  }
+}
+
+// The draft's guesses after the target's tokens become the step's drafts: the SpeculativeGenerator
+// cap (speculative_generator.py:71-72) as for n-gram drafts, -1 for idle or finished entries.
+__global__ void draft_propose_kernel(ne_batch_state st, ne_batch_state dt, const int32_t* __restrict__ seq_slot,
+                                     int num_seqs, int k, int32_t* __restrict__ draft_len, int* status) {
+  pdl_prologue();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= num_seqs) return;
+  const int s = seq_slot[b];
+  if (s < 0 || s >= st.max_seqs || s >= dt.max_seqs || (st.flags[s] & NE_SEQ_FINISHED)) {
+    draft_len[b] = -1;
+    return;
+  }
+  const int L = st.seq_len[s];
+  const int remaining = st.max_new_tokens[s] - (L - st.num_prompt[s]);
+  int cap = max(0, min(k, remaining - 1));
+  if (L + cap > st.history_stride || L + cap > dt.seq_len[s]) {
+    if (L + cap > st.history_stride) report(status, NE_DEV_HISTORY_FULL);
+    cap = max(0, min(cap, min(st.history_stride, dt.seq_len[s]) - L));
+  }
+  const int32_t* hd = dt.history + (long long)s * dt.history_stride;
+  int32_t* ht = st.history + (long long)s * st.history_stride;
+  for (int j = 0; j < cap; ++j) ht[L + j] = hd[L + j];
+  draft_len[b] = cap;
+}
+
 // ------------------------------------------------------------------ n-gram drafts
 // NgramProposer.propose (engine/speculative/proposers.py:44-57) for one batch entry per CTA:
 // for n = max_ngram .. min_ngram (skipped when len <= n), the most recent earlier occurrence of the
@@ -598,6 +650,23 @@ int launch_tp_rs_reduce(const int32_t* rows_dev, int max_rows, const TpLink& lin
   const int blocks = (int)std::min<long long>(148, std::max<long long>(1, (units + 255) / 256));
   return launch_kernel(tp_rs_reduce_kernel, dim3(blocks), dim3(256), 0, stream, rows_dev, max_rows, link,
                        status) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
+}
+
+int launch_draft_sync(const ne_batch_state& st, const ne_batch_state& dt, const int32_t* seq_slot, int num_seqs, int k,
+                      cudaStream_t stream) {
+  if (num_seqs <= 0) return NE_OK;
+  if (k < 1 || st.history_stride != dt.history_stride) return NE_ERR_INVALID;
+  return launch_kernel(draft_sync_kernel, dim3(num_seqs), dim3(128), 0, stream, st, dt, seq_slot, k) == cudaSuccess
+             ? NE_OK
+             : NE_ERR_CUDA;
+}
+
+int launch_draft_propose(const ne_batch_state& st, const ne_batch_state& dt, const int32_t* seq_slot, int num_seqs,
+                         int k, int32_t* draft_len, int* status, cudaStream_t stream) {
+  if (num_seqs <= 0) return NE_OK;
+  if (k < 1 || !draft_len) return NE_ERR_INVALID;
+  return launch_kernel(draft_propose_kernel, dim3((num_seqs + 127) / 128), dim3(128), 0, stream, st, dt, seq_slot,
+                       num_seqs, k, draft_len, status) == cudaSuccess ? NE_OK : NE_ERR_CUDA;
 }
 
 int launch_keys_to_ids(const unsigned long long* keys, const int32_t* count, int max_count, int32_t* ids,

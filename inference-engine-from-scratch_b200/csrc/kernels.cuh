@@ -45,6 +45,12 @@ int launch_keys_to_ids(const unsigned long long* keys, const int32_t* count, int
                        cudaStream_t stream);
 int launch_ngram(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int k, int max_ngram,
                  int min_ngram, int32_t* draft_len, int* status, cudaStream_t stream);
+// Draft-model drafts: the draft state's sequences take the target's tokens (cache kept for the
+// common prefix), and after the draft model's k greedy steps its guesses become the drafts.
+int launch_draft_sync(const ne_batch_state& st, const ne_batch_state& dt, const int32_t* seq_slot, int num_seqs, int k,
+                      cudaStream_t stream);
+int launch_draft_propose(const ne_batch_state& st, const ne_batch_state& dt, const int32_t* seq_slot, int num_seqs,
+                         int k, int32_t* draft_len, int* status, cudaStream_t stream);
 int launch_plan(const ne_batch_state& st, const int32_t* seq_slot, int num_seqs, int mode, int max_rows, int chunk,
                 int block_size, long long num_cache_slots, const RowBuffers& rb, int* status, cudaStream_t stream);
 int launch_share_blocks(const ne_batch_state& st, int src_slot, const int32_t* dst_slots, int num_dst, int num_blocks,

@@ -99,7 +99,12 @@ class B200SpeculativeEngine:
         cuda_graphs: bool = True,
         max_prefill_rows: int | None = None,
         sampling: bool = False,
+        draft_model: B200Model | None = None,
+        draft_num_blocks: int | None = None,
     ) -> None:
+        """``draft_model``: drafts come from this smaller model of the same family
+        (DraftModelProposer, engine/speculative/proposers.py:63-106; greedy requests) instead of
+        n-gram lookup; it keeps its own batch state and KV pool (``draft_num_blocks`` blocks)."""
         self.lib = _lib.load()
         self.model = model
         self.k = k
@@ -131,6 +136,24 @@ class B200SpeculativeEngine:
         if sampling:
             nbytes = int(self.lib.ne_sampling_buffer_bytes(model.handle, self._sample_rows))
             self._sample_buf = torch.empty(nbytes, dtype=torch.uint8, device=model.device)
+        # draft model: its own batch state (same slots and history stride) and result buffer
+        self.draft_model = draft_model
+        self.draft_state = None
+        if draft_model is not None:
+            if draft_model is model:
+                raise ValueError("the draft model needs a model object (and KV pool) of its own")
+            if draft_model.cfg.vocab_size != model.cfg.vocab_size:
+                raise ValueError("the draft model needs the target's vocabulary")
+            if draft_model.max_seqs < max_seqs or draft_model.max_rows < max_seqs * (k + 1):
+                raise ValueError("the draft model workspace is smaller than max_seqs x (k + 1) rows")
+            if max_model_len + k + 1 > draft_model.max_positions:
+                raise ValueError("max_model_len + k exceeds the draft model's RoPE table")
+            dblocks = draft_num_blocks if draft_num_blocks is not None else draft_model.num_slots // 16
+            if dblocks * 16 > draft_model.num_slots:
+                raise ValueError("more draft blocks than the draft KV pool holds")
+            self.draft_state = DeviceBatchState(max_seqs, max_model_len, k, dblocks, 16, (), model.device)
+            self._draft_outs = _Outputs(max_seqs, k, model.device)
+            self.max_prefill_rows = min(self.max_prefill_rows, draft_model.max_rows)
         self._uncached: dict[int, int] = {}       # slot -> prompt tokens still to prefill
         self._prefixes: dict[int, list] = {}      # holder slot -> [tokens, shared blocks, users, copies]
         self._prefix_of: dict[int, int] = {}      # slot -> holder slot of its shared prefix
@@ -147,6 +170,8 @@ class B200SpeculativeEngine:
         (from ``add_prefix``) shares the KV blocks of a prompt prefix the request starts with."""
         if temperature != 0.0 and not self.sampling:
             raise ValueError("temperature > 0 needs an engine built with sampling=True")
+        if self.draft_state is not None and (temperature != 0.0 or prefix is not None):
+            raise ValueError("draft-model drafts serve greedy requests without shared prefixes")
         if prefix is not None:
             tokens = self._prefixes[prefix][0]
             if prompt[: len(tokens)] != tokens:
@@ -164,6 +189,11 @@ class B200SpeculativeEngine:
             self._prefix_of[slot] = prefix
             shared = blocks * 16
         self._uncached[slot] = len(prompt) - shared
+        if self.draft_state is not None:
+            # the draft sequence never finishes on its own: it follows the target (ne_draft_sync)
+            self.draft_state.load(slot, prompt, self.state.max_model_len - len(prompt), ignore_eos=True)
+            self.draft_state.max_new_tokens[slot] = 1 << 30
+            self.h2d_bytes += 4 * len(prompt) + 5 * 4 + 4 + 4 + 8 + 8
         return slot
 
     def add_prefix(self, tokens: list[int]) -> int:
@@ -205,6 +235,8 @@ class B200SpeculativeEngine:
 
     def release(self, slots: list[int]) -> None:
         self.state.release(slots)
+        if self.draft_state is not None:
+            self.draft_state.release(slots)
         for s in slots:
             self._uncached.pop(s, None)
             holder = self._prefix_of.pop(s, None)
@@ -273,16 +305,38 @@ class B200SpeculativeEngine:
         _lib.check(self.lib.ne_prefill(self.model.handle, self.state.ref, self._slots_dev.data_ptr(), len(slots),
                                        max(rows, 1), self.k, chunk, ctypes.byref(self.outputs.struct),
                                        _lib.stream_handle()), "ne_prefill")
+        if self.draft_state is not None:
+            # the draft model prefills the same prompt tokens into its own cache (its own first
+            # token is replaced by the target's at the next ne_draft_sync)
+            _lib.check(self.lib.ne_prefill(self.draft_model.handle, self.draft_state.ref, self._slots_dev.data_ptr(),
+                                           len(slots), max(rows, 1), self.k, chunk,
+                                           ctypes.byref(self._draft_outs.struct), _lib.stream_handle()),
+                       "ne_prefill (draft)")
         res = self._collect(slots)
         self.model.raise_on_device_error()
+        if self.draft_model is not None:
+            self.draft_model.raise_on_device_error()
         return res
 
     # ------------------------------------------------------------------ speculative step
     def _launch_step(self, bucket: int, buf: int = 0) -> None:
         self._bind_sampler()
-        _lib.check(self.lib.ne_spec_step(self.model.handle, self.state.ref, self._slots_dev.data_ptr(), bucket,
-                                         self.k, self.max_ngram, ctypes.byref(self._outs[buf].struct),
-                                         _lib.stream_handle()), "ne_spec_step")
+        if self.draft_state is None:
+            _lib.check(self.lib.ne_spec_step(self.model.handle, self.state.ref, self._slots_dev.data_ptr(), bucket,
+                                             self.k, self.max_ngram, ctypes.byref(self._outs[buf].struct),
+                                             _lib.stream_handle()), "ne_spec_step")
+            return
+        # draft model: sync with the target, k greedy draft steps (the first catches up), verify
+        stream, slots = _lib.stream_handle(), self._slots_dev.data_ptr()
+        _lib.check(self.lib.ne_draft_sync(self.state.ref, self.draft_state.ref, slots, bucket, self.k, stream),
+                   "ne_draft_sync")
+        for _ in range(self.k):
+            _lib.check(self.lib.ne_prefill(self.draft_model.handle, self.draft_state.ref, slots, bucket,
+                                           bucket * (self.k + 1), self.k, 0, ctypes.byref(self._draft_outs.struct),
+                                           stream), "ne_prefill (draft step)")
+        _lib.check(self.lib.ne_spec_step_drafted(self.model.handle, self.state.ref, self.draft_state.ref, slots, bucket,
+                                                 self.k, ctypes.byref(self._outs[buf].struct), stream),
+                   "ne_spec_step_drafted")
 
     def launch(self, slots: list[int], buf: int = 0) -> int:
         """Enqueue one step for ``slots`` (no host sync) writing result buffer ``buf``; returns the

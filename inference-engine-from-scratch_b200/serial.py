@@ -322,6 +322,52 @@ class NgramProposer:
         return None
 
 
+class DraftModelProposer:
+    """DraftModelProposer (engine/speculative/proposers.py:63-106) on the GPU: ``runner`` is a
+    ``B200ModelRunner`` over the draft model and its own paged allocator; each proposal syncs the
+    draft sequence with the target (common-prefix cache kept, ``_sync_draft``) and runs
+    ``num_tokens`` draft steps, the first catching up on the target's new tokens. Greedy requests:
+    the guesses are the draft's argmax ids, returned as one-hot drafts (``probabilities`` None,
+    which ``verify_proposal`` reads as one-hot rows, the distributions the reference stacks for a
+    greedy draft). Sampled drafts would need the draft's rows in the verify kernel: refused."""
+
+    def __init__(self, runner: B200ModelRunner, device=None) -> None:
+        self._runner = runner
+        self._device = device
+        self._draft_sequences: dict[str, Sequence] = {}
+
+    def propose(self, sequence, num_tokens: int) -> Proposal:
+        if sequence.sampling_params.temperature != GREEDY_TEMPERATURE:
+            raise NotImplementedError("draft-model proposals on the B200 path are greedy")
+        draft = self._sync_draft(sequence)
+        guesses: list[int] = []
+        for _ in range(num_tokens):
+            self._runner.allocator.reserve(draft, draft.num_tokens)
+            guess = self._runner.run_step([draft])[0]  # the argmax after the draft's uncached tokens
+            draft.token_ids.append(guess)
+            guesses.append(guess)
+        return Proposal(guesses)
+
+    def release(self, sequence) -> None:
+        draft = self._draft_sequences.pop(sequence.request_id, None)
+        if draft is not None:
+            self._runner.allocator.free(draft)
+
+    def _sync_draft(self, sequence) -> Sequence:
+        draft = self._draft_sequences.get(sequence.request_id)
+        if draft is None:
+            draft = Sequence.from_request(sequence.request, self._device)
+            self._draft_sequences[sequence.request_id] = draft
+        common = 0
+        for draft_token, target_token in zip(draft.token_ids, sequence.token_ids):
+            if draft_token != target_token:
+                break
+            common += 1
+        draft.token_ids = list(sequence.token_ids)
+        draft.num_cached_tokens = min(draft.num_cached_tokens, common)
+        return draft
+
+
 class _LogitsVerifier:
     """``ne_verify_logits`` for one proposal at a time: a one-slot device state holds the guesses,
     the request's sampling parameters and its Philox position."""
@@ -437,7 +483,7 @@ class SpeculativeCounters:
 class SpeculativeGenerator:
     """engine/speculative/speculative_generator.py:21-90 over ``B200ModelRunner``."""
 
-    def __init__(self, runner: B200ModelRunner, proposer: NgramProposer, num_speculative_tokens: int,
+    def __init__(self, runner: B200ModelRunner, proposer: "NgramProposer | DraftModelProposer", num_speculative_tokens: int,
                  stop_token_ids: frozenset[int], device=None, metrics: SpeculativeCounters | None = None) -> None:
         self._runner = runner
         self._proposer = proposer
