@@ -66,3 +66,12 @@ def test_new_entry_points_refuse_bad_arguments_without_a_gpu() -> None:
 
 def _lib_status(lib, name: str) -> int:
     return {"invalid": 1, "cuda": 2, "device": 3, "unsupported": 4, "workspace": 5}[name]
+
+
+def test_quality_report_renders_the_reference_table() -> None:
+    quality = submodule("quality")
+    report = quality.QualityReport(12.5, 13.0, 0.9375, 6, 8, "weights=int8, kv_cache=int8")
+    text = quality.render_quality_markdown(report)
+    assert "| Perplexity on the fixed token sequence | 12.500 | 13.000 |" in text
+    assert "| Greedy token agreement | 100% | 93.8% |" in text
+    assert "| Identical completions | 8 | 6 |" in text
