@@ -21,6 +21,9 @@ Fixtures written (all small):
 * ``spec_small_draft_bf16.pt`` / ``spec_small_draft_same_bf16.pt``
                              the same with DraftModelProposer drafts: a one-layer draft (seed 1),
                              and the target itself as its own draft (every guess accepted)
+* ``spec_small_draft_sampled.pt``  the one-layer draft, sampled (T=0.8, top-p 0.95): drafts drawn
+                             from the draft's distribution on the request's stream, verified
+                             against it (rejection sampling with the draft's rows)
 * ``spec_config1_fp32.pt``   BASELINE config 1 exactly (Qwen3-0.6B fp32, seed 0, 64-token motif
                              prompt, 128 greedy tokens, n=3, k=4, 16-token blocks)
 """
@@ -90,6 +93,7 @@ class UniformInjector:
         ref.verifier.torch = TorchProxy()
         ref.verifier.sample_from_probabilities = sample
         ref.sampling.sample_from_probabilities = sample
+        ref.proposers.sample_from_probabilities = sample  # DraftModelProposer's sampled drafts
 
     def start(self, seed: int) -> None:
         self.stream = self.philox.UniformStream(seed)
@@ -330,6 +334,9 @@ def main() -> None:
                HERE / "spec_small_draft_bf16.pt")
     torch.save(spec_run(ref, inj, cfg, weights, torch.bfloat16, prompts, draft=(cfg, weights), **common),
                HERE / "spec_small_draft_same_bf16.pt")
+    torch.save(spec_run(ref, inj, cfg, weights, torch.bfloat16, prompts, temperature=0.8, top_p=0.95,
+                        seeds=[11, 12, 13], draft=(draft_cfg, pkg.make_weights(draft_cfg, seed=1)), **common),
+               HERE / "spec_small_draft_sampled.pt")
     if args.only_draft:
         return
 

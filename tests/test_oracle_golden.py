@@ -111,7 +111,9 @@ def _check_run(golden, cfg, weights, dtype, atol, draft=None):
             assert mine.draft == ref["draft"]
             assert mine.block_table == ref["block_table"]
             assert mine.new_tokens == ref["new_tokens"]
-            assert mine.uniforms_used == ref["draws"]
+            # (a sampled draft model draws one uniform per guess before verification does)
+            draft_draws = len(ref["draft"]) if draft is not None and golden["temperature"] > 0 else 0
+            assert mine.uniforms_used == ref["draws"] + draft_draws
             d = ref["logits"]
             assert torch.equal(torch.argmax(mine.logits, dim=-1).to(torch.int32), d["argmax"])
             torch.testing.assert_close(mine.logits.float()[:, ids], d["at_ids"], atol=atol, rtol=0)
@@ -143,10 +145,12 @@ def test_serial_speculation_config1_qwen3_0_6b_fp32() -> None:
                FP32_LOGITS_ATOL)
 
 
-@pytest.mark.parametrize("fixture", ["spec_small_draft_bf16.pt", "spec_small_draft_same_bf16.pt"])
+@pytest.mark.parametrize("fixture", ["spec_small_draft_bf16.pt", "spec_small_draft_same_bf16.pt",
+                                     "spec_small_draft_sampled.pt"])
 def test_serial_speculation_with_a_draft_model(fixture) -> None:
-    """DraftModelProposer (proposers.py:63-106): a one-layer draft of the same family, and the
-    target as its own draft (every guess kept)."""
+    """DraftModelProposer (proposers.py:63-106): a one-layer draft of the same family (greedy and
+    sampled: drafts drawn from the draft's distribution, rejection sampling against its rows), and
+    the target as its own draft (every guess kept)."""
     pkg = package()
     cfg = pkg.SMALL_TEST
     golden = load_golden(fixture)
