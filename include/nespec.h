@@ -305,6 +305,20 @@ NE_API int ne_verify_logits(const ne_batch_state* state, const int32_t* seq_slot
                             const int32_t* draft_len, const int32_t* lm_start, const void* logits, int vocab,
                             int lm_rows, void* scratch, size_t scratch_bytes, const ne_step_outputs* out,
                             int32_t* status, void* stream);
+/*
+ * ne_verify_logits for draft-model proposals (DraftModelProposer, proposers.py:63-106): the
+ * guesses were drawn from the draft's distributions, whose logits rows ``draft_logits`` (bf16
+ * [draft_rows, vocab]; entry b's guess j at row draft_start[b] + j) take the place of one-hot
+ * drafts: acceptance min(1, p(g) / max(q(g), 1e-12)) and, on a rejection, a draw from
+ * max(0, p - q) renormalised (the target when that is empty), verifier.py:27-60. q is the draft
+ * row's softmax(x / T) with top-p at the entry's own parameters. ``scratch`` holds
+ * (lm_rows + draft_rows) x 32 bytes.
+ */
+NE_API int ne_verify_logits_drafted(const ne_batch_state* state, const int32_t* seq_slot, int num_seqs, int k,
+                                    const int32_t* draft_len, const int32_t* lm_start, const void* logits, int vocab,
+                                    int lm_rows, const void* draft_logits, const int32_t* draft_start, int draft_rows,
+                                    void* scratch, size_t scratch_bytes, const ne_step_outputs* out, int32_t* status,
+                                    void* stream);
 
 /* ---------------------------------------------------------------- shared int8 KV blocks */
 /*

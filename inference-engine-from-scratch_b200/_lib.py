@@ -70,6 +70,11 @@ EXPORTS = {
         [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p,
          c_void_p, c_void_p],
     ),
+    "ne_verify_logits_drafted": (
+        c_int,
+        [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int,
+         c_void_p, c_size_t, c_void_p, c_void_p, c_void_p],
+    ),
     "ne_tp_unique_id": (c_int, [ctypes.c_char_p, c_void_p]),
     "ne_model_set_tp": (c_int, [c_void_p, ctypes.c_char_p, c_int, c_int, c_void_p]),
     "ne_model_tp_exchange_create": (c_int, [c_void_p, c_int, c_void_p]),

@@ -807,6 +807,29 @@ int ne_verify_logits(const ne_batch_state* st, const int32_t* seq_slot, int num_
                                    nullptr, *out, status, s);
 }
 
+int ne_verify_logits_drafted(const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int k,
+                             const int32_t* draft_len, const int32_t* lm_start, const void* logits, int vocab,
+                             int lm_rows, const void* draft_logits, const int32_t* draft_start, int draft_rows,
+                             void* scratch, size_t scratch_bytes, const ne_step_outputs* out, int32_t* status,
+                             void* stream) {
+  if (!st || !seq_slot || !draft_len || !lm_start || !logits || !draft_logits || !draft_start || !out ||
+      num_seqs <= 0 || k < 1 || vocab <= 0 || lm_rows <= 0 || draft_rows <= 0 || !scratch || !st->temperature ||
+      !st->top_p || !st->rng_seed || !st->rng_draws)
+    return NE_ERR_INVALID;
+  if (scratch_bytes < (size_t)(lm_rows + draft_rows) * sizeof(ne::SampleStats)) return NE_ERR_WORKSPACE;
+  cudaStream_t s = as_stream(stream);
+  const __nv_bfloat16* lg = static_cast<const __nv_bfloat16*>(logits);
+  const __nv_bfloat16* dl = static_cast<const __nv_bfloat16*>(draft_logits);
+  ne::SampleStats* stats = static_cast<ne::SampleStats*>(scratch);
+  ne::SampleStats* dstats = stats + lm_rows;
+  int rc = ne::launch_sample_stats(*st, seq_slot, num_seqs, lm_start, nullptr, nullptr, lm_rows, lg, vocab, stats, s);
+  if (rc) return rc;
+  rc = ne::launch_sample_stats(*st, seq_slot, num_seqs, draft_start, nullptr, nullptr, draft_rows, dl, vocab, dstats, s);
+  if (rc) return rc;
+  return ne::launch_accept_sampled(*st, seq_slot, num_seqs, k, draft_len, nullptr, lm_start, lg, vocab, stats,
+                                   nullptr, *out, status, s, dl, draft_start, dstats);
+}
+
 int ne_prefill(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int max_rows, int k,
                int chunk, const ne_step_outputs* out, void* stream) {
   if (!m || !st || !seq_slot || !out || num_seqs <= 0 || k < 1 || chunk < 0) return NE_ERR_INVALID;

@@ -439,6 +439,7 @@ struct DrawShared {
   unsigned long long warp_sum[WARPS];
   unsigned long long warp_ex[WARPS];
   uint32_t warp_ties[WARPS];
+  uint32_t warp_ties_q[WARPS];  // (residual draws: the draft row's tie counts)
   int result;
 };
 
@@ -579,6 +580,106 @@ __device__ int draw_token(const __nv_bfloat16* row, int vocab, float T, const Sa
   return tok;
 }
 
+// Draw from the residual of a rejected draft-model guess (verifier.py:53-57): max(0, p - q) over
+// the target row ``prow`` (stats ``ps``) and the draft row ``qrow`` (stats ``qs``, the same T and
+// top-p), renormalised; when the residual is empty, from the target itself. Fixed-point sums as in
+// draw_token (the renormalised values v / norm are what the prefix sums add). Block-wide.
+__device__ int draw_residual(const __nv_bfloat16* prow, const SampleStats& ps, const __nv_bfloat16* qrow,
+                             const SampleStats& qs, int vocab, float T, uint32_t u24, DrawShared& sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int len = ((vocab + THREADS - 1) / THREADS) * 32;
+  const int begin = warp * len, end = min(vocab, begin + len);
+  uint32_t pties = 0, qties = 0;
+  const bool pt = partial_ties(ps), qt = partial_ties(qs);
+  if (pt || qt) {
+    for (int base = begin; base < end; base += 32) {
+      const int i = base + lane;
+      if (pt) pties += __popc(__ballot_sync(FULL, i < end && prob(scaled(prow, i, T), ps.m, ps.z) == ps.tau));
+      if (qt) qties += __popc(__ballot_sync(FULL, i < end && prob(scaled(qrow, i, T), qs.m, qs.z) == qs.tau));
+    }
+  }
+  if (lane == 0) {
+    sh.warp_ties[warp] = pties;
+    sh.warp_ties_q[warp] = qties;
+  }
+  __syncthreads();
+  uint32_t pbase = 0, qbase = 0;
+  for (int w = 0; w < warp; ++w) {
+    pbase += sh.warp_ties[w];
+    qbase += sh.warp_ties_q[w];
+  }
+  // pass 1: the residual's total, to renormalise
+  unsigned long long sum = 0;
+  {
+    uint32_t pr = pbase, qr = qbase;
+    for (int base = begin; base < end; base += 32) {
+      const int i = base + lane;
+      const float p = chunk_value(prow, i, i < end, T, ps, pr);
+      const float q = chunk_value(qrow, i, i < end, T, qs, qr);
+      sum += to_fix(fmaxf(p - q, 0.f));
+    }
+  }
+  sum = warp_sum_u64(sum);
+  if (lane == 0) sh.warp_sum[warp] = sum;
+  __syncthreads();
+  unsigned long long total = 0;
+  for (int w = 0; w < WARPS; ++w) total += sh.warp_sum[w];
+  __syncthreads();
+  if (total == 0ull) return draw_token(prow, vocab, T, ps, -1, u24, sh);  // residual empty: the target
+  const float norm = (float)((double)total / FIX_ONE);
+  // pass 2: per-range sums of the renormalised residual
+  sum = 0;
+  {
+    uint32_t pr = pbase, qr = qbase;
+    for (int base = begin; base < end; base += 32) {
+      const int i = base + lane;
+      const float p = chunk_value(prow, i, i < end, T, ps, pr);
+      const float q = chunk_value(qrow, i, i < end, T, qs, qr);
+      sum += to_fix(fmaxf(p - q, 0.f) / norm);
+    }
+  }
+  sum = warp_sum_u64(sum);
+  if (lane == 0) sh.warp_sum[warp] = sum;
+  __syncthreads();
+  total = 0;
+  for (int w = 0; w < WARPS; ++w) total += sh.warp_sum[w];
+  const unsigned long long hi = __umul64hi((unsigned long long)u24, total);
+  const unsigned long long lo = (unsigned long long)u24 * total;
+  const unsigned long long target = (hi << 40) | (lo >> 24);
+  unsigned long long before = 0;
+  int owner = -1;
+  for (int w = 0; w < WARPS; ++w) {
+    if (before + sh.warp_sum[w] > target) {
+      owner = w;
+      break;
+    }
+    before += sh.warp_sum[w];
+  }
+  if (threadIdx.x == 0) sh.result = -1;
+  __syncthreads();
+  if (warp == owner) {
+    unsigned long long run = before;
+    uint32_t pr = pbase, qr = qbase;
+    for (int base = begin; base < end; base += 32) {
+      const int i = base + lane;
+      const float p = chunk_value(prow, i, i < end, T, ps, pr);
+      const float q = chunk_value(qrow, i, i < end, T, qs, qr);
+      const unsigned long long f = to_fix(fmaxf(p - q, 0.f) / norm);
+      const unsigned long long incl = run + warp_incl_scan_u64(f, lane);
+      const uint32_t hit = __ballot_sync(FULL, i < end && incl > target);
+      if (hit) {
+        if (lane == 0) sh.result = base + __ffs(hit) - 1;
+        break;
+      }
+      run = __shfl_sync(FULL, incl, 31);
+    }
+  }
+  __syncthreads();
+  const int tok = sh.result;
+  __syncthreads();
+  return tok;
+}
+
 // torch.argmax of a bf16 row (lowest id among equal maxima). Block-wide.
 __device__ int row_argmax(const __nv_bfloat16* row, int vocab, DrawShared& sh) {
   unsigned long long best = 0;
@@ -609,7 +710,8 @@ __global__ void __launch_bounds__(THREADS)
                           const int32_t* __restrict__ draft_len, const int32_t* __restrict__ q_len_arr,
                           const int32_t* __restrict__ lm_start, const __nv_bfloat16* __restrict__ logits, int vocab,
                           const SampleStats* __restrict__ stats, const unsigned long long* __restrict__ keys,
-                          ne_step_outputs out, int* status) {
+                          ne_step_outputs out, int* status, const __nv_bfloat16* __restrict__ draft_logits,
+                          const int32_t* __restrict__ draft_start, const SampleStats* __restrict__ draft_stats) {
   pdl_prologue();
   __shared__ DrawShared sh;
   const int b = blockIdx.x;
@@ -668,7 +770,7 @@ __global__ void __launch_bounds__(THREADS)
     // every thread takes the same (deterministic) decisions; the draws are block-wide
     const unsigned long long seed = st.rng_seed[s];
     unsigned long long draws = st.rng_draws[s];
-    int stop_row = ls + g, exclude = -1;
+    int stop_row = ls + g, exclude = -1, draft_row = -1;
     for (int j = 0; j < g; ++j) {
       const int r = ls + j;
       const SampleStats sj = stats[r];
@@ -681,7 +783,17 @@ __global__ void __launch_bounds__(THREADS)
       }
       const float p = prob(scaled(row, guess, T), sj.m, sj.z);
       const int rank = (partial_ties(sj) && p == sj.tau) ? ties_below(row, guess, T, sj, sh) : 0;
-      const float a = fminf(kept_p(p, sj, rank), 1.0f);
+      float a = fminf(kept_p(p, sj, rank), 1.0f);
+      if (draft_logits) {
+        // the draft's probability of its guess: acceptance min(1, p / max(q, 1e-12))
+        const int dr = draft_start[b] + j;
+        const SampleStats qj = draft_stats[dr];
+        const __nv_bfloat16* qrow = draft_logits + (long long)dr * vocab;
+        const float q = prob(scaled(qrow, guess, T), qj.m, qj.z);
+        const int qrank = (partial_ties(qj) && q == qj.tau) ? ties_below(qrow, guess, T, qj, sh) : 0;
+        a = fminf(kept_p(p, sj, rank) / fmaxf(kept_p(q, qj, qrank), 1e-12f), 1.0f);
+        draft_row = dr;
+      }
       bool accept = a >= 1.0f;
       if (!accept && a > 0.f) {
         accept = (float)uniform24(seed, draws) * (1.0f / 16777216.0f) < a;
@@ -693,10 +805,15 @@ __global__ void __launch_bounds__(THREADS)
         break;
       }
       ++kept;
+      draft_row = -1;
     }
     const uint32_t u24 = uniform24(seed, draws);
     ++draws;
-    last = draw_token(logits + (long long)stop_row * vocab, vocab, T, stats[stop_row], exclude, u24, sh);
+    if (draft_logits && draft_row >= 0)  // a rejected draft-model guess: the residual max(0, p - q)
+      last = draw_residual(logits + (long long)stop_row * vocab, stats[stop_row],
+                           draft_logits + (long long)draft_row * vocab, draft_stats[draft_row], vocab, T, u24, sh);
+    else
+      last = draw_token(logits + (long long)stop_row * vocab, vocab, T, stats[stop_row], exclude, u24, sh);
     if (threadIdx.x != 0) return;
     if (last < 0) {
       report(status, NE_DEV_BAD_TOKEN);
@@ -758,10 +875,13 @@ int launch_accept_sampled(const ne_batch_state& st, const int32_t* seq_slot, int
                           const int32_t* draft_len, const int32_t* q_len, const int32_t* lm_start,
                           const __nv_bfloat16* logits, int vocab, const SampleStats* stats,
                           const unsigned long long* keys, const ne_step_outputs& out, int* status,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, const __nv_bfloat16* draft_logits, const int32_t* draft_start,
+                          const SampleStats* draft_stats) {
   if (num_seqs <= 0) return NE_OK;
+  if (draft_logits && (!draft_start || !draft_stats || !draft_len)) return NE_ERR_INVALID;
   return launch_kernel(accept_sampled_kernel, dim3(num_seqs), dim3(THREADS), 0, stream, st, seq_slot, k, draft_len,
-                       q_len, lm_start, logits, vocab, stats, keys, out, status) == cudaSuccess
+                       q_len, lm_start, logits, vocab, stats, keys, out, status, draft_logits, draft_start,
+                       draft_stats) == cudaSuccess
              ? NE_OK
              : NE_ERR_CUDA;
 }

@@ -288,6 +288,9 @@ class B200ModelRunner:
 class Proposal:
     token_ids: list[int]
     probabilities: torch.Tensor | None = None
+    # a sampled draft model's logits rows of its guesses (bf16 [len(token_ids), vocab] on the GPU):
+    # the verify kernel takes their softmax / top-p as the draft distributions
+    draft_logits: torch.Tensor | None = None
 
 
 class NgramProposer:
@@ -329,7 +332,9 @@ class DraftModelProposer:
     ``num_tokens`` draft steps, the first catching up on the target's new tokens. Greedy requests:
     the guesses are the draft's argmax ids, returned as one-hot drafts (``probabilities`` None,
     which ``verify_proposal`` reads as one-hot rows, the distributions the reference stacks for a
-    greedy draft). Sampled drafts would need the draft's rows in the verify kernel: refused."""
+    greedy draft). Sampled requests: each guess is drawn from the draft's distribution on the
+    request's generator (one uniform, as ``sample_from_probabilities``), and the draft's logits rows
+    go with the proposal (``draft_logits``) for verification against them."""
 
     def __init__(self, runner: B200ModelRunner, device=None) -> None:
         self._runner = runner
@@ -337,16 +342,22 @@ class DraftModelProposer:
         self._draft_sequences: dict[str, Sequence] = {}
 
     def propose(self, sequence, num_tokens: int) -> Proposal:
-        if sequence.sampling_params.temperature != GREEDY_TEMPERATURE:
-            raise NotImplementedError("draft-model proposals on the B200 path are greedy")
+        params = sequence.sampling_params
+        sampled = params.temperature != GREEDY_TEMPERATURE
         draft = self._sync_draft(sequence)
         guesses: list[int] = []
+        rows: list[torch.Tensor] = []
         for _ in range(num_tokens):
             self._runner.allocator.reserve(draft, draft.num_tokens)
-            guess = self._runner.run_step([draft])[0]  # the argmax after the draft's uncached tokens
+            if not sampled:
+                guess = self._runner.run_step([draft])[0]  # the argmax after the draft's uncached tokens
+            else:
+                row = self._runner.score_tokens(draft, draft.num_uncached_tokens)[-1:]
+                guess = _logits_verifier(row.device).verify([], row, params, sequence.sampling_generator)[0]
+                rows.append(row)
             draft.token_ids.append(guess)
             guesses.append(guess)
-        return Proposal(guesses)
+        return Proposal(guesses, draft_logits=torch.cat(rows) if rows else None)
 
     def release(self, sequence) -> None:
         draft = self._draft_sequences.pop(sequence.request_id, None)
@@ -384,7 +395,7 @@ class _LogitsVerifier:
         self.slot = torch.zeros(1, **i32)
         self.lm_start = torch.zeros(1, **i32)
         self.draft_len = torch.zeros(1, **i32)
-        self.scratch = torch.zeros((k + 1) * 32, dtype=torch.uint8, device=self.device)
+        self.scratch = torch.zeros((2 * k + 1) * 32, dtype=torch.uint8, device=self.device)
         self.out = torch.zeros(k + 1 + 4, **i32)
         base = self.out.data_ptr()
         self.out_struct = _lib.StepOutputs(tokens=base, count=base + 4 * (k + 1), finish=base + 4 * (k + 2),
@@ -392,7 +403,7 @@ class _LogitsVerifier:
         self.status = torch.zeros(1, **i32)
 
     def verify(self, guesses: list[int], logits: torch.Tensor, params: SamplingParams,
-               generator: PhiloxGenerator | None) -> list[int]:
+               generator: PhiloxGenerator | None, draft_logits: torch.Tensor | None = None) -> list[int]:
         g = len(guesses)
         if g > self.MAX_GUESSES:
             raise ValueError(f"at most {self.MAX_GUESSES} guesses per proposal")
@@ -416,10 +427,22 @@ class _LogitsVerifier:
             st.rng_draws.fill_(generator.draws)
         self.draft_len.fill_(g)
         logits = logits.contiguous()
-        _lib.check(self.lib.ne_verify_logits(
-            st.ref, self.slot.data_ptr(), 1, self.MAX_GUESSES, self.draft_len.data_ptr(), self.lm_start.data_ptr(),
-            logits.data_ptr(), logits.shape[1], g + 1, self.scratch.data_ptr(), self.scratch.numel(),
-            ctypes.byref(self.out_struct), self.status.data_ptr(), _lib.stream_handle()), "ne_verify_logits")
+        if draft_logits is not None and sampled and g > 0:
+            if draft_logits.shape != (g, logits.shape[1]) or draft_logits.dtype != torch.bfloat16:
+                raise ValueError("draft logits must be bf16 [len(guesses), vocab]")
+            draft_logits = draft_logits.contiguous()
+            _lib.check(self.lib.ne_verify_logits_drafted(
+                st.ref, self.slot.data_ptr(), 1, self.MAX_GUESSES, self.draft_len.data_ptr(),
+                self.lm_start.data_ptr(), logits.data_ptr(), logits.shape[1], g + 1, draft_logits.data_ptr(),
+                self.lm_start.data_ptr(), g, self.scratch.data_ptr(), self.scratch.numel(),
+                ctypes.byref(self.out_struct), self.status.data_ptr(), _lib.stream_handle()),
+                "ne_verify_logits_drafted")
+        else:
+            _lib.check(self.lib.ne_verify_logits(
+                st.ref, self.slot.data_ptr(), 1, self.MAX_GUESSES, self.draft_len.data_ptr(),
+                self.lm_start.data_ptr(), logits.data_ptr(), logits.shape[1], g + 1, self.scratch.data_ptr(),
+                self.scratch.numel(), ctypes.byref(self.out_struct), self.status.data_ptr(), _lib.stream_handle()),
+                "ne_verify_logits")
         out = self.out.tolist()
         count = out[self.MAX_GUESSES + 1]
         word = int(self.status.item())
@@ -443,17 +466,18 @@ def _logits_verifier(device) -> _LogitsVerifier:
 
 def verify_proposal(proposal: Proposal, target_logits: torch.Tensor, params: SamplingParams, generator=None,
                     target_argmax: list[int] | None = None) -> list[int]:
-    """verifier.py:27-60 with one-hot (n-gram) drafts: kept guesses + one target token.
+    """verifier.py:27-60 with one-hot drafts (n-gram, greedy draft model) or a sampled draft model's
+    rows (``proposal.draft_logits``): kept guesses + one target token.
 
     Greedy: ``target_argmax`` (the kernel's per-row argmax ids, lowest index on ties) are compared
     on the host; without them the verify kernel takes the argmax itself. Sampled: rejection
     sampling on the GPU with ``generator`` (the request's ``PhiloxGenerator``), which advances.
     """
     if proposal.probabilities is not None:
-        raise ValueError("the B200 verify takes one-hot (n-gram) drafts")
+        raise ValueError("the B200 verify takes one-hot drafts or a draft model's logits rows (draft_logits)")
     if params.temperature != GREEDY_TEMPERATURE or target_argmax is None:
         return _logits_verifier(target_logits.device).verify(list(proposal.token_ids), target_logits, params,
-                                                             generator)
+                                                             generator, draft_logits=proposal.draft_logits)
     kept: list[int] = []
     for index, guess in enumerate(proposal.token_ids):
         if guess == target_argmax[index]:

@@ -1,0 +1,265 @@
+"""Sampled draft-model speculation on the GPU (DraftModelProposer with temperature > 0,
+engine/speculative/proposers.py:63-106 and verifier.py:27-60 with the draft's rows).
+
+The guesses are drawn from the draft's distribution on the request's Philox stream and verified
+against it: acceptance min(1, p(g) / q(g)), and on a rejection a draw from max(0, p - q)
+renormalised. As for one-hot drafts (tests/test_gpu_sampling.py), the GPU's own softmax differs
+from torch's in the last bits, so a decision whose two sides are closer than MARGIN may fall the
+other way; every mismatch with the oracle must be such a near-tie and most cases must match.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import philox
+from oracle import verify as overify
+from tests.conftest import load_golden, package, submodule
+
+pytestmark = pytest.mark.gpu
+
+MARGIN = 1e-5
+TOPP_MARGIN = 1e-6
+MIN_EXACT = 0.9
+
+
+def _kept(logits: torch.Tensor, temperature: float, top_p: float):
+    """float64 stable-top-p distributions of the rows, and the smallest |mass-before - top_p| at a cut."""
+    p = torch.softmax((logits.float() / temperature).double(), dim=-1).numpy()
+    margin = 1.0
+    if top_p >= 1.0:
+        return p, margin
+    rows = []
+    for r in range(p.shape[0]):
+        order = np.argsort(-p[r], kind="stable")
+        srt = p[r][order]
+        before = np.cumsum(srt) - srt
+        cut = int((before < top_p).sum())
+        for i in (cut - 1, cut):
+            if 0 <= i < len(before):
+                margin = min(margin, abs(before[i] - top_p))
+        kept = np.zeros_like(p[r])
+        kept[order[:cut]] = srt[:cut]
+        rows.append(kept / kept.sum())
+    return np.stack(rows), margin
+
+
+def draft_margin(case) -> float:
+    """Smallest distance, along the float64 replay of one drafted verification, between a uniform
+    and what it is compared with (acceptance ratio, inverse-CDF boundary), or of a top-p cut."""
+    p, mp = _kept(case["logits"], case["temperature"], case["top_p"])
+    q, mq = _kept(case["draft_logits"], case["temperature"], case["top_p"]) if case["guesses"] else (None, 1.0)
+    margin = min(mp, mq)
+    stream = philox.UniformStream(case["seed"], case["start"])
+
+    def draw(dist):
+        nonlocal margin
+        u = next(stream)
+        c = np.cumsum(dist) / dist.sum()
+        i = int(np.searchsorted(c, u, side="right"))
+        for j in (i - 1, i):
+            if 0 <= j < len(c):
+                margin = min(margin, abs(c[j] - u))
+
+    for j, g in enumerate(case["guesses"]):
+        ratio = p[j, g] / max(q[j, g], 1e-12)
+        margin = min(margin, abs(1.0 - ratio))
+        a = min(ratio, 1.0)
+        if a >= 1.0:
+            continue
+        if a > 0.0:
+            u = next(stream)
+            margin = min(margin, abs(u - a))
+            if u < a:
+                continue
+        residual = np.clip(p[j] - q[j], 0.0, None)
+        if residual.sum() <= 0:
+            residual = p[j]
+        draw(residual)
+        return margin
+    draw(p[len(case["guesses"])])
+    return margin
+
+
+def oracle_drafted(case):
+    stream = philox.UniformStream(case["seed"], case["start"])
+    q = None
+    if case["guesses"]:
+        q = torch.stack([overify.token_probabilities(r, case["temperature"], case["top_p"], True)
+                         for r in case["draft_logits"].float()])
+    got = overify.verify_proposal(case["guesses"], q, case["logits"].float(), case["temperature"], case["top_p"],
+                                  stream, True)
+    return got, stream.index
+
+
+def run_drafted(cases, device="cuda:0"):
+    """Every case through ne_verify_logits_drafted in one batch; (tokens, Philox position) per case."""
+    _lib = submodule("_lib")
+    lib = _lib.load()
+    state_mod = submodule("state")
+    B = len(cases)
+    K = max(1, max(len(c["guesses"]) for c in cases))
+    vocab = cases[0]["logits"].shape[-1]
+    st = state_mod.DeviceBatchState(B, 8, K, 1, device=device)
+    hist = torch.zeros(B, st.history_stride, dtype=torch.int32)
+    lm, dr, draft = [], [], []
+    rows = drows = 0
+    for b, c in enumerate(cases):
+        g = len(c["guesses"])
+        if g:
+            hist[b, :g] = torch.tensor(c["guesses"], dtype=torch.int32)
+        lm.append(rows)
+        dr.append(drows)
+        draft.append(g)
+        rows += g + 1
+        drows += g
+    st.history.copy_(hist)
+    st.seq_len.zero_()
+    st.num_cached.zero_()
+    st.num_prompt.zero_()
+    st.max_new_tokens.fill_(1 << 30)
+    st.flags.fill_(_lib.NE_SEQ_IGNORE_EOS)
+    st.temperature.copy_(torch.tensor([float(c["temperature"]) for c in cases]))
+    st.top_p.copy_(torch.tensor([float(c["top_p"]) for c in cases]))
+    st.rng_seed.copy_(torch.tensor([state_mod.seed_as_int64(c["seed"]) for c in cases], dtype=torch.int64))
+    st.rng_draws.copy_(torch.tensor([int(c["start"]) for c in cases], dtype=torch.int64))
+    logits = torch.cat([c["logits"].to(torch.bfloat16) for c in cases]).to(device).contiguous()
+    dlogits = torch.cat([c["draft_logits"].to(torch.bfloat16) for c in cases if c["guesses"]]).to(device).contiguous()
+    i32 = dict(dtype=torch.int32, device=device)
+    slots = torch.arange(B, **i32)
+    lm_start, draft_start, draft_len = torch.tensor(lm, **i32), torch.tensor(dr, **i32), torch.tensor(draft, **i32)
+    scratch = torch.zeros((rows + drows) * 32, dtype=torch.uint8, device=device)
+    w = K + 1
+    out = torch.zeros(B * w + 4 * B, **i32)
+    base = out.data_ptr()
+    outs = _lib.StepOutputs(tokens=base, count=base + 4 * B * w, finish=base + 4 * B * (w + 1),
+                            proposed=base + 4 * B * (w + 2), accepted=base + 4 * B * (w + 3))
+    status = torch.zeros(1, **i32)
+    _lib.check(lib.ne_verify_logits_drafted(
+        st.ref, slots.data_ptr(), B, K, draft_len.data_ptr(), lm_start.data_ptr(), logits.data_ptr(), vocab, rows,
+        dlogits.data_ptr(), draft_start.data_ptr(), drows, scratch.data_ptr(), scratch.numel(), ctypes.byref(outs),
+        status.data_ptr(), _lib.stream_handle()), "ne_verify_logits_drafted")
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    host = out.cpu()
+    tokens, count = host[: B * w].view(B, w), host[B * w: B * (w + 1)]
+    return [tokens[b, : int(count[b])].tolist() for b in range(B)], st.rng_draws.cpu().tolist()
+
+
+def check(cases, got, draws):
+    exact = 0
+    for case, g, d in zip(cases, got, draws):
+        e, ed = oracle_drafted(case)
+        if g == e and d == ed:
+            exact += 1
+            continue
+        m = draft_margin(case)
+        assert m < MARGIN or m < TOPP_MARGIN, f"mismatch without a near-tie: got {g} ({d}), expected {e} ({ed})"
+    assert exact >= MIN_EXACT * len(cases), f"only {exact} of {len(cases)} match exactly"
+
+
+@pytest.mark.parametrize("vocab,temperature,top_p", [(512, 0.8, 0.95), (151936, 0.8, 0.95), (4096, 1.0, 1.0),
+                                                     (4096, 0.3, 0.5)])
+def test_drafted_verification_matches_the_oracle(vocab, temperature, top_p) -> None:
+    """Random target and draft rows; the guesses drawn from the draft's distributions (so that
+    acceptance ratios below and above one both occur)."""
+    submodule("build").build()
+    g = torch.Generator().manual_seed(vocab + int(100 * temperature))
+    cases = []
+    for i in range(48):
+        k = i % 5
+        logits = torch.randn(k + 1, vocab, generator=g) * 2.0
+        # drafts close to the target for some cases (high acceptance), unrelated for others
+        noise = 0.3 if i % 2 else 3.0
+        dlogits = logits[:k] + noise * torch.randn(k, vocab, generator=g) if k else torch.zeros(0, vocab)
+        guesses = []
+        for j in range(k):
+            q = overify.token_probabilities(dlogits[j].to(torch.bfloat16).float(), temperature, top_p, True)
+            guesses.append(int(torch.multinomial(q, 1, generator=g).item()))
+        cases.append({"logits": logits.to(torch.bfloat16), "draft_logits": dlogits.to(torch.bfloat16),
+                      "guesses": guesses, "temperature": temperature, "top_p": top_p, "seed": 77 + i,
+                      "start": i % 3})
+    got, draws = run_drafted(cases)
+    check(cases, got, draws)
+
+
+def test_serial_sampled_draft_model_replays_on_the_oracle() -> None:
+    """The serial drop-in with a sampled one-layer draft (the reference's run of
+    spec_small_draft_sampled.pt: same models, prompts, seeds): reproducible, and every step (the
+    draft's draws, then verification) replays on the oracle from the GPU's own logits. The emitted
+    tokens are not compared with the reference's: at T = 0.8 the random-init rows are nearly flat
+    over the vocabulary, so a logit difference of one bf16 ulp between the CPU and GPU forwards
+    moves an inverse-CDF draw to a neighbouring token (the oracle pins the decisions instead)."""
+    submodule("build").build()
+    pkg = package()
+    serial = submodule("serial")
+    cfg = pkg.SMALL_TEST
+    golden = load_golden("spec_small_draft_sampled.pt")
+    mk = submodule("model").B200Model
+    target = mk(cfg, pkg.make_weights(cfg, seed=0), num_slots=64 * 16, device="cuda:0", max_positions=512,
+                max_rows=512, max_seqs=8)
+    dcfg = pkg.Qwen3Config(**{**{f: getattr(cfg, f) for f in cfg.__dataclass_fields__}, "num_hidden_layers": 1})
+    draft_model = mk(dcfg, pkg.make_weights(dcfg, seed=1), num_slots=64 * 16, device="cuda:0", max_positions=512,
+                     max_rows=512, max_seqs=8)
+
+    class Recording(serial.DraftModelProposer):
+        def __init__(self, runner):
+            super().__init__(runner, "cuda:0")
+            self.proposals = []
+
+        def propose(self, sequence, num_tokens):
+            start = sequence.sampling_generator.draws
+            prop = super().propose(sequence, num_tokens)
+            self.proposals.append((prop, start))
+            return prop
+
+    T, P = golden["temperature"], golden["top_p"]
+    cases, got, draws, guess_cases = [], [], [], []
+    for index, record in enumerate(golden["records"]):
+        runs = []
+        for _ in range(2):
+            runner = serial.B200ModelRunner(target, serial.PagedSlotAllocator(golden["num_blocks"], 16))
+            proposer = Recording(serial.B200ModelRunner(draft_model, serial.PagedSlotAllocator(golden["num_blocks"], 16)))
+            counters = serial.SpeculativeCounters()
+            gen = serial.SpeculativeGenerator(runner, proposer, golden["k"], frozenset(), metrics=counters)
+            params = serial.SamplingParams(max_new_tokens=golden["max_new"], temperature=T, top_p=P,
+                                           seed=record["seed"], ignore_eos=True)
+            tokens = [e.token_id for e in gen.generate(serial.GenerationRequest(f"r{index}", record["prompt"], params))]
+            runs.append((tokens, counters.steps, proposer.proposals))
+        assert runs[0][0] == runs[1][0]
+        tokens, steps, proposals = runs[0]
+        for (draft, _table, logits, new_tokens), (prop, start) in zip(steps, proposals):
+            assert list(prop.token_ids) == list(draft)
+            # the draft's draws: guess j from the draft's row j at stream position start + j
+            for j, guess in enumerate(draft):
+                row = prop.draft_logits[j].float().cpu()
+                dist = overify.token_probabilities(row, T, P, True)
+                u = next(philox.UniformStream(record["seed"], start + j))
+                expect = overify.inverse_cdf(dist, u)
+                c = np.cumsum(dist.double().numpy()) / float(dist.double().sum())
+                i = int(np.searchsorted(c, u, side="right"))
+                near = min(abs(c[x] - u) for x in (i - 1, i) if 0 <= x < len(c))
+                assert guess == expect or near < MARGIN
+            case = {"logits": logits.float().cpu(), "draft_logits": prop.draft_logits.float().cpu()
+                    if prop.draft_logits is not None else torch.zeros(0, logits.shape[1]),
+                    "guesses": list(draft), "temperature": T, "top_p": P, "seed": record["seed"],
+                    "start": start + len(draft)}
+            cases.append(case)
+            got.append(list(new_tokens))
+            draws.append(None)
+    # verification replays (positions follow the oracle's own draw counts)
+    exact = 0
+    for case, g in zip(cases, got):
+        e, _ = oracle_drafted(case)
+        if g == e:
+            exact += 1
+            continue
+        assert draft_margin(case) < MARGIN, f"mismatch without a near-tie: got {g}, expected {e}"
+    assert exact >= MIN_EXACT * len(cases)
+    assert len(cases) >= len(golden["records"]) and any(c["guesses"] for c in cases)
+    target.close()
+    draft_model.close()
