@@ -51,6 +51,7 @@ struct ne_model {
   void* tp_peer[ne::TP_MAX_WORLD] = {};
   ne::TpLink link{};         // link.world > 0 once every peer region is open
   float* split = nullptr;    // fp32 split-K partials of the residual GEMMs (split_rows x H)
+  int rows_hint = 0;         // a speculative step's expected rows (GEMM planning), 0 otherwise
   long long split_rows = 0;
   float* ssq = nullptr;      // fp32 [max_rows, H / 128]: residual rows' sums of squares per 128-wide tile
   CUtensorMap tm_h{};        // the residual rows as a GEMM X operand (RMSNorm fused into the GEMM)
@@ -82,8 +83,9 @@ size_t sampling_logits_bytes(const ne_model_config& c, int rows) {
 }  // split-KV partials (few sequences, long contexts)
 
 // Split-K partials of o_proj / down_proj left for the next RMSNorm: room for GEMM_MAX_SPLITS
-// slices of up to 512 rows (verify steps; larger steps run unsplit or keep the in-GEMM reduction).
-size_t split_rows_cap(int R) { return (size_t)ne::GEMM_MAX_SPLITS * std::min(R, 512); }
+// slices of up to 1536 rows (verify steps up to 256 users x 6 rows; larger steps run unsplit or
+// keep the in-GEMM reduction).
+size_t split_rows_cap(int R) { return (size_t)ne::GEMM_MAX_SPLITS * std::min(R, 1536); }
 
 struct Layout {
   size_t status, h, x, q, attn, act, keys, rows_i32, seqs_i32, scalars, attn_scratch, partial, split, ssq, total;
@@ -182,6 +184,7 @@ int run_gemm(ne_model* m, const CUtensorMap* tw, const CUtensorMap* tx, int M_ma
   p.N = N;
   p.K = K;
   p.status = m->status;
+  p.rows_hint = m->rows_hint;
   p.epi = epi;
   int rc = ne::gemm_plan(p, m->num_sms);
   if (rc != NE_OK) return rc;
@@ -211,6 +214,7 @@ int residual_gemm(ne_model* m, const CUtensorMap* tw, const CUtensorMap* tx, int
   p.N = N;
   p.K = K;
   p.status = m->status;
+  p.rows_hint = m->rows_hint;
   p.epi.status = m->status;
   p.epi.ldo = N;
   if (m->split && split_partials_enabled()) {
@@ -862,11 +866,19 @@ int spec_step_tail(ne_model* m, const ne_batch_state* st, const int32_t* seq_slo
                             m->cfg.num_cache_slots, m->rb, m->status, s), s);
   if (rc) return rc;
   ne_rows rows = make_step_rows(m, st, seq_slot, num_seqs, max_rows, max_rows, k + 1);
+  // a step's rows are a device count: about one draft per sequence is typical, far below the bound
+  m->rows_hint = std::min(max_rows, 2 * num_seqs);
   if (m->sample_logits) {
-    if (max_rows > m->sample_rows) return NE_ERR_WORKSPACE;
-    return sampled_tail(m, st, seq_slot, num_seqs, k, rows, true, out, s);
+    if (max_rows > m->sample_rows) {
+      m->rows_hint = 0;
+      return NE_ERR_WORKSPACE;
+    }
+    rc = sampled_tail(m, st, seq_slot, num_seqs, k, rows, true, out, s);
+    m->rows_hint = 0;
+    return rc;
   }
   rc = ne_forward(m, &rows, NE_LM_ARGMAX, nullptr, nullptr, s);
+  m->rows_hint = 0;
   if (rc) return rc;
   return note(m, NE_K_ACCEPT,
               ne::launch_accept_greedy(*st, seq_slot, num_seqs, k, ne::PLAN_SPEC, m->rb, m->keys, *out, m->status, s),

@@ -904,9 +904,9 @@ int active_clusters(int mode, int conv, int splits, int smem) {
 // Choose tokens per CTA, split-K (cluster size) and pipeline depth for an [M_max, K] x [N, K]^T GEMM.
 namespace {
 struct PlanKey {
-  int M, N, K, mode, conv, sms;
+  int M, N, K, mode, conv, sms, hint;
   bool operator<(const PlanKey& o) const {
-    return std::tie(M, N, K, mode, conv, sms) < std::tie(o.M, o.N, o.K, o.mode, o.conv, o.sms);
+    return std::tie(M, N, K, mode, conv, sms, hint) < std::tie(o.M, o.N, o.K, o.mode, o.conv, o.sms, o.hint);
   }
 };
 struct PlanVal {
@@ -921,7 +921,7 @@ int plan_with_occupancy(GemmParams& p, int num_sms);
 
 // Cached per (rows, N, K, epilogue, SMs); the first plan of a shape queries cluster occupancy.
 int gemm_plan(GemmParams& p, int num_sms) {
-  const PlanKey key{p.M_max, p.N, p.K, p.epi.mode, conv_bits(p), num_sms};
+  const PlanKey key{p.M_max, p.N, p.K, p.epi.mode, conv_bits(p), num_sms, p.rows_hint};
   {
     std::lock_guard<std::mutex> lock(g_plan_mutex);
     auto it = g_plans.find(key);
@@ -958,6 +958,15 @@ int max_stages() {
   return cap;
 }
 
+// The m-blocks expected to hold rows: all of them for a prefill-sized bound (the rows fill it),
+// the first for a verify step under 512 rows, and for a larger verify bound (a big batch bucket)
+// the blocks the host's expected row count covers.
+int active_m_blocks(const GemmParams& p, int t_block, int m_blocks) {
+  if (p.M_max <= 512) return 1;
+  if (p.rows_hint > 0) return std::max(1, std::min(m_blocks, (p.rows_hint + t_block - 1) / t_block));
+  return m_blocks;
+}
+
 int plan_uncached(GemmParams& p, int num_sms) {
   if (p.N % GEMM_BM || p.K % GEMM_BK || p.M_max <= 0) return NE_ERR_INVALID;
   if ((p.w_scale && p.epi.mode != EPI_STORE && p.epi.mode != EPI_RESIDUAL && p.epi.mode != EPI_SWIGLU &&
@@ -972,7 +981,7 @@ int plan_uncached(GemmParams& p, int num_sms) {
   int m_blocks = (p.M_max + t_block - 1) / t_block;
   // a verify step's row count is a device value well below its bound: size split-K for the first
   // m-block (a later one that gets rows is a second wave); prefill-sized steps split by m-blocks
-  const int par = n_tiles * (p.M_max > 512 ? m_blocks : 1);
+  const int par = n_tiles * active_m_blocks(p, t_block, m_blocks);
   int S = std::max(1, std::min(max_splits(), num_sms / std::max(1, par)));
   if (p.epi.mode == EPI_ARGMAX || p.epi.mode == EPI_LOGITS) S = 1;
   const bool split_out = p.epi.mode == EPI_SPLIT_F32;
@@ -1024,7 +1033,7 @@ int plan_with_occupancy(GemmParams& p, int num_sms) {
   int rc = plan_uncached(p, num_sms);
   if (rc != NE_OK) return rc;
   const int m_blocks = (p.M_max + p.t_block - 1) / p.t_block;
-  const int par = n_tiles * (p.M_max > 512 ? m_blocks : 1);
+  const int par = n_tiles * active_m_blocks(p, p.t_block, m_blocks);
   while (p.splits > 1 && p.epi.mode != EPI_SPLIT_F32) {  // (split partials need no cluster)
     const int fit = active_clusters(p.epi.mode, conv_bits(p), p.splits, p.smem_data + 256 + GEMM_RSTD_BYTES + 1024);
     if (fit >= par) break;

@@ -115,6 +115,9 @@ struct GemmParams {
   const float* x_ssq;
   int ssq_tiles;
   float x_eps;
+  // verify steps: rows the step is expected to hold (M_dev is then far below M_max); 0 = unknown.
+  // Split-K is sized for the m-blocks these rows fill instead of for every m-block of M_max.
+  int rows_hint;
   Epilogue epi;
 };
 
