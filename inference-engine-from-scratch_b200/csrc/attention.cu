@@ -734,6 +734,12 @@ int attention_plan_splits(int num_seqs, int nkv, int max_context, int max_vec, i
   }();
   const int pairs = num_seqs * nkv;
   int splits = (2 * num_sms + pairs - 1) / pairs;
+  static const int forced = [] {  // NE_ATTN_SPLITS (tuning knob): a fixed split count, capped below
+    const char* v = getenv("NE_ATTN_SPLITS");
+    const int n = v ? atoi(v) : 0;
+    return n >= 1 && n <= 32 ? n : 0;
+  }();
+  if (forced) splits = forced;
   const int max_blocks = (max_context + 15) / 16;
   const int by_length = max_blocks / 8;
   splits = splits > by_length ? by_length : splits;
