@@ -157,17 +157,21 @@ class B200SpeculativeEngine:
         self._uncached: dict[int, int] = {}       # slot -> prompt tokens still to prefill
         self._prefixes: dict[int, list] = {}      # holder slot -> [tokens, shared blocks, users, copies]
         self._prefix_of: dict[int, int] = {}      # slot -> holder slot of its shared prefix
+        self._shared_count: dict[int, int] = {}   # slot -> blocks it shares with its prefix holder
         self.proposed_total = 0
         self.accepted_total = 0
         self.h2d_bytes = 0  # host->device bytes copied for requests and steps
         self.d2h_bytes = 0  # device->host bytes read back (step results)
         self.steps_run = 0  # prefill and speculative steps whose results were read
+        self.preemptions = 0  # sequences generate() preempted to free KV blocks
 
     # ------------------------------------------------------------------ request lifecycle
     def add_request(self, prompt: list[int], max_new_tokens: int, *, ignore_eos: bool = False,
-                    temperature: float = 0.0, top_p: float = 1.0, seed: int = 0, prefix: int | None = None) -> int:
-        """Load a request into a free slot. ``seed`` keys the request's Philox stream; ``prefix``
-        (from ``add_prefix``) shares the KV blocks of a prompt prefix the request starts with."""
+                    temperature: float = 0.0, top_p: float = 1.0, seed: int = 0, prefix: int | None = None,
+                    draws: int = 0) -> int:
+        """Load a request into a free slot. ``seed`` keys the request's Philox stream (``draws``:
+        the uniforms it already used, for a preempted request that resumes); ``prefix`` (from
+        ``add_prefix``) shares the KV blocks of a prompt prefix the request starts with."""
         if temperature != 0.0 and not self.sampling:
             raise ValueError("temperature > 0 needs an engine built with sampling=True")
         if self.draft_state is not None and (temperature != 0.0 or prefix is not None):
@@ -178,7 +182,7 @@ class B200SpeculativeEngine:
                 raise ValueError("the prompt does not start with the shared prefix")
         slot = self.state.acquire()
         self.state.load(slot, prompt, max_new_tokens, ignore_eos=ignore_eos, temperature=temperature,
-                        top_p=top_p, seed=seed)
+                        top_p=top_p, seed=seed, draws=draws)
         self.h2d_bytes += 4 * len(prompt) + 5 * 4 + 4 + 4 + 8 + 8
         shared = 0
         if prefix is not None:
@@ -187,6 +191,7 @@ class B200SpeculativeEngine:
             self.state.share_blocks(prefix, [slot], blocks)
             self._prefixes[prefix][2] += 1
             self._prefix_of[slot] = prefix
+            self._shared_count[slot] = blocks
             shared = blocks * 16
         self._uncached[slot] = len(prompt) - shared
         if self.draft_state is not None:
@@ -239,6 +244,7 @@ class B200SpeculativeEngine:
             self.draft_state.release(slots)
         for s in slots:
             self._uncached.pop(s, None)
+            self._shared_count.pop(s, None)
             holder = self._prefix_of.pop(s, None)
             if holder is not None:
                 self._prefixes[holder][2] -= 1
@@ -385,24 +391,74 @@ class B200SpeculativeEngine:
         """Serve every prompt with continuous batching (up to ``max_seqs`` at a time); request i
         samples with ``seeds[i]`` (default i) when ``temperature`` > 0. ``shared_prefix`` > 0: the
         prompts' common first tokens are prefilled once and their KV blocks shared (one slot holds
-        them); ``prefill_chunk``: chunked prefill."""
+        them); ``prefill_chunk``: chunked prefill.
+
+        KV blocks: before each step the host bounds every running sequence's blocks (its length
+        plus the guesses a step may reserve) and, when the next step could exhaust the pool,
+        preempts the newest sequences as the reference's ContinuousBatchScheduler does
+        (engine/scheduling/batch_scheduler.py:67-85): their blocks are freed and they return to the
+        front of the queue with their tokens so far, to be prefilled again (recompute) and
+        continued on the same random stream."""
         outputs: list[list[int]] = [[] for _ in prompts]
         pending = list(range(len(prompts)))
         running: dict[int, int] = {}  # slot -> request index
+        order: dict[int, int] = {}    # slot -> admission number (the newest is preempted first)
+        resume: dict[int, tuple[list[int], int, int]] = {}  # index -> (tokens, new tokens left, draws)
         prefix = self.add_prefix(prompts[0][:shared_prefix]) if shared_prefix else None
+        prefix_blocks = -(-(shared_prefix + 1) // 16) if prefix is not None else 0
+        k, bs = self.k, 16
+        admitted_total = [0]
+
+        def tokens_of(index: int) -> list[int]:
+            return resume[index][0] if index in resume else prompts[index]
+
+        def length(slot: int) -> int:  # prompt + tokens emitted so far (read back)
+            index = running[slot]
+            return len(prompts[index]) + len(outputs[index])
+
+        def blocks_bound(extra: int) -> int:
+            """Blocks the running sequences may hold after ``extra`` more tokens each (their
+            rejected guesses stay reserved, so k more), shared prefix blocks counted once."""
+            used = prefix_blocks
+            for slot in running:
+                used += max(0, -(-(length(slot) + extra + k) // bs) - self._shared_count.get(slot, 0))
+            return used
+
+        def preempt(slot: int) -> None:
+            index = running.pop(slot)
+            order.pop(slot, None)
+            left = max_new_tokens - len(outputs[index])
+            draws = int(self.state.rng_draws[slot].item())
+            self.release([slot])
+            resume[index] = (prompts[index] + outputs[index], left, draws)
+            pending.insert(0, index)
+            self.preemptions += 1
 
         def admit() -> None:
             admitted = []
             while pending and self.state.free_slots:
-                index = pending.pop(0)
-                slot = self.add_request(prompts[index], max_new_tokens, ignore_eos=ignore_eos,
-                                        temperature=temperature, top_p=top_p,
-                                        seed=seeds[index] if seeds is not None else index, prefix=prefix)
+                index = pending[0]
+                tokens = tokens_of(index)
+                # the new prefill's blocks and one step of growth for everyone must fit the pool
+                need = -(-(len(tokens) + 1 + k) // bs)
+                if running and blocks_bound(k + 1) + need > self.state.num_blocks:
+                    break
+                pending.pop(0)
+                left, draws = (resume[index][1], resume[index][2]) if index in resume else (max_new_tokens, 0)
+                slot = self.add_request(tokens, left, ignore_eos=ignore_eos, temperature=temperature, top_p=top_p,
+                                        seed=seeds[index] if seeds is not None else index, prefix=prefix,
+                                        draws=draws)
                 running[slot] = index
+                order[slot] = admitted_total[0]
+                admitted_total[0] += 1
                 admitted.append(slot)
             if admitted:
                 res = self.prefill(admitted, chunk=prefill_chunk)
                 self._absorb(res, running, outputs)
+
+        def make_room(extra: int) -> None:
+            while len(running) > 1 and blocks_bound(extra) > self.state.num_blocks:
+                preempt(max(running, key=lambda s: order.get(s, -1)))
 
         # Steps run one ahead of the host: step i + 1 is enqueued before step i's results are
         # read, so the host work of a step overlaps the next one on the GPU. A sequence that
@@ -413,12 +469,19 @@ class B200SpeculativeEngine:
         while pending or running or inflight:
             if inflight is None:
                 admit()
+                make_room(k + 1)
                 if running:
                     slots = sorted(running)
                     self.launch(slots, buf)
                     self._outs[buf].start_fetch()
                     inflight = (slots, buf)
                     buf ^= 1
+                continue
+            if running and blocks_bound(2 * (k + 1)) > self.state.num_blocks:
+                # the pool is tight: read the step in flight first (exact lengths), then decide
+                res = self._collect(inflight[0], self._outs[inflight[1]])
+                self._absorb(res, running, outputs)
+                inflight = None
                 continue
             nxt = None
             if running:

@@ -95,7 +95,7 @@ class DeviceBatchState:
         _lib.check(self.lib.ne_state_reset_blocks(self.ref, _lib.stream_handle()), "ne_state_reset_blocks")
 
     def load(self, slot: int, prompt: list[int], max_new_tokens: int, *, ignore_eos: bool = False,
-             temperature: float = 0.0, top_p: float = 1.0, seed: int = 0) -> None:
+             temperature: float = 0.0, top_p: float = 1.0, seed: int = 0, draws: int = 0) -> None:
         """Copy one request into sequence slot ``slot`` (Sequence.from_request)."""
         if len(prompt) == 0 or len(prompt) + max_new_tokens > self.max_model_len:
             raise ValueError(f"prompt of {len(prompt)} + {max_new_tokens} new tokens exceeds max_model_len")
@@ -113,7 +113,7 @@ class DeviceBatchState:
         self.temperature[slot] = float(temperature)
         self.top_p[slot] = float(top_p)
         self.rng_seed[slot] = seed_as_int64(seed)
-        self.rng_draws[slot] = 0
+        self.rng_draws[slot] = int(draws)
 
     def acquire(self) -> int:
         if not self.free_slots:

@@ -281,3 +281,22 @@ def test_int8_shared_prefix_reads_dequantised_block_copies() -> None:
     assert int((model.kv_copy_map >= 0).sum()) == 0
     model.raise_on_device_error()
     model.close()
+
+
+def test_generate_preempts_when_the_kv_pool_runs_short(small) -> None:
+    """A pool too small for every request's full length: generate() preempts the newest
+    sequences (ContinuousBatchScheduler.reserve_next_tokens, batch_scheduler.py:67-85), which
+    resume later by recompute; greedy outputs equal the roomy run and every block returns."""
+    cfg, _, model = small
+    pkg = package()
+    prompts = pkg.make_prompts(4, cfg.vocab_size, length=48, seed=21)
+    roomy = _engine(model, 4, False)
+    expected = roomy.generate(prompts, 64)
+    assert roomy.preemptions == 0
+    tight = submodule("engine").B200SpeculativeEngine(model, k=4, max_ngram=3, max_seqs=4, max_model_len=256,
+                                                      num_blocks=20, cuda_graphs=False)
+    got = tight.generate(prompts, 64)
+    assert tight.preemptions > 0
+    assert got == expected
+    assert tight.state.num_free_blocks() == 20
+    model.raise_on_device_error()
