@@ -125,6 +125,7 @@ class B200SpeculativeEngine:
         self.buckets = build_buckets(max_seqs)
         self.cuda_graphs = cuda_graphs
         self._slots_dev = torch.full((max_seqs,), -1, dtype=torch.int32, device=model.device)
+        self._dev_slots_key = None  # (slots, bucket) the device slot list holds
         self._slots_hosts = [torch.full((max_seqs,), -1, dtype=torch.int32).pin_memory() for _ in range(2)]
         self._slots_host = self._slots_hosts[0]
         self._graphs: dict[tuple[int, int], torch.cuda.CUDAGraph] = {}
@@ -250,12 +251,17 @@ class B200SpeculativeEngine:
                 self._prefixes[holder][2] -= 1
 
     def _set_slots(self, slots: list[int], bucket: int, host: int = 0) -> None:
+        # consecutive steps usually list the same slots: the device copy is then already current
+        key = (tuple(slots), bucket)
+        if key == self._dev_slots_key:
+            return
         # the pinned source of an asynchronous copy must not change before the copy runs: the two
         # in-flight steps of generate() use two host buffers
         h = self._slots_hosts[host]
         h.fill_(-1)
         h[: len(slots)] = torch.tensor(slots, dtype=torch.int32)
         self._slots_dev[:bucket].copy_(h[:bucket], non_blocking=True)
+        self._dev_slots_key = key
         self.h2d_bytes += 4 * bucket
 
     def _collect(self, slots: list[int], outs: _Outputs | None = None) -> StepResult:
@@ -264,12 +270,13 @@ class B200SpeculativeEngine:
         self.d2h_bytes += outs.buf.numel() * 4
         self.steps_run += 1
         result = StepResult()
+        # one host conversion per field (per-slot tensor slicing costs more than the step's GPU time)
+        rows, counts, fins = tokens.tolist(), count.tolist(), finish.tolist()
         for i, slot in enumerate(slots):
-            c = int(count[i])
-            result.tokens[slot] = tokens[i, :c].tolist()
-            result.finish[slot] = FINISH_REASONS.get(int(finish[i]))
-        result.proposed = int(proposed.sum())
-        result.accepted = int(accepted.sum())
+            result.tokens[slot] = rows[i][: counts[i]]
+            result.finish[slot] = FINISH_REASONS.get(fins[i])
+        result.proposed = sum(proposed.tolist())
+        result.accepted = sum(accepted.tolist())
         self.proposed_total += result.proposed
         self.accepted_total += result.accepted
         return result
@@ -368,7 +375,7 @@ class B200SpeculativeEngine:
         """Capture one bucket's step. The capture itself changes no state: every slot in the
         bucket is idle (-1) while capturing, so the captured kernels find no work."""
         saved = self._slots_dev.clone()
-        self._slots_dev.fill_(-1)
+        self._slots_dev.fill_(-1)  # (restored below, so the slot list key stays valid)
         torch.cuda.synchronize()
         stream = torch.cuda.Stream()
         stream.wait_stream(torch.cuda.current_stream())
