@@ -272,9 +272,28 @@ NE_API int ne_spec_step(ne_model* model, const ne_batch_state* state, const int3
  */
 NE_API int ne_draft_sync(const ne_batch_state* target, const ne_batch_state* draft, const int32_t* seq_slot,
                          int num_seqs, int k, void* stream);
+/*
+ * Sampled requests with draft-model drafts: the draft model (with a sampling buffer) draws its
+ * guesses on the request's stream -- the draft state's stream position follows the target's
+ * (ne_draft_sync) and the target's advances by the guesses used -- and the draft's logits rows of
+ * every guess stay for verification: entry b's guess j at row start[b] + j * stride of ``logits``
+ * (bf16, ``vocab`` wide; each draft step's rows in their own region), with ``stats`` room for as
+ * many rows. Acceptance is then min(1, p / q) with the residual max(0, p - q) (ne_verify_logits_drafted).
+ */
+typedef struct {
+  const void* logits;
+  const int32_t* start;  /* [num_seqs] (the draft model's lm-row start of each entry: ne_model_lm_start) */
+  int stride;            /* rows between a guess's row and the next one's */
+  int rows;              /* rows the regions hold in total */
+  void* stats;           /* rows x 32 bytes */
+} ne_draft_rows;
+
+/* ``draft_rows`` NULL: greedy drafts (one-hot). */
 NE_API int ne_spec_step_drafted(ne_model* model, const ne_batch_state* state, const ne_batch_state* draft,
                                 const int32_t* seq_slot, int num_seqs, int k, const ne_step_outputs* out,
-                                void* stream);
+                                void* stream, const ne_draft_rows* draft_rows);
+/* The model's per-entry lm-row starts of its last forward (device, inside the workspace). */
+NE_API const int32_t* ne_model_lm_start(const ne_model* model);
 
 /* ---------------------------------------------------------------- sampled acceptance */
 /*

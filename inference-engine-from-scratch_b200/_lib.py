@@ -49,7 +49,9 @@ EXPORTS = {
     "ne_state_share_blocks": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "ne_spec_step": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "ne_draft_sync": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
-    "ne_spec_step_drafted": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "ne_spec_step_drafted": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p,
+                                     c_void_p]),
+    "ne_model_lm_start": (c_void_p, [c_void_p]),
     "ne_gemm_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "ne_gemm_w8": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "ne_paged_attention": (
@@ -169,6 +171,10 @@ class BatchState(ctypes.Structure):
     ]
 
 
+class DraftRows(ctypes.Structure):
+    _fields_ = [("logits", c_void_p), ("start", c_void_p), ("stride", c_int), ("rows", c_int), ("stats", c_void_p)]
+
+
 class StepOutputs(ctypes.Structure):
     _fields_ = [(name, c_void_p) for name in ("tokens", "count", "finish", "proposed", "accepted")]
 
@@ -218,6 +224,18 @@ def ptr(t: torch.Tensor | None) -> int | None:
 def stream_handle(stream: torch.cuda.Stream | None = None) -> int:
     s = stream if stream is not None else torch.cuda.current_stream()
     return s.cuda_stream
+
+
+class _DeviceArray:
+    """A device array the library owns, seen by torch through ``__cuda_array_interface__``."""
+
+    def __init__(self, address: int, n: int, typestr: str):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (address, False), "version": 3}
+
+
+def device_int32(address: int, n: int, device) -> torch.Tensor:
+    """A copy of ``n`` int32 values at a device address returned by the library."""
+    return torch.as_tensor(_DeviceArray(address, n, "<i4"), device=device).clone()
 
 
 def require_cuda(t: torch.Tensor, name: str) -> None:

@@ -755,7 +755,8 @@ namespace {
 // Forward with logits into the sampling buffer, per-row statistics, then acceptance for greedy
 // and sampled entries alike.
 int sampled_tail(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int k,
-                 const ne_rows& rows, bool spec, const ne_step_outputs* out, cudaStream_t s) {
+                 const ne_rows& rows, bool spec, const ne_step_outputs* out, cudaStream_t s,
+                 const ne_draft_rows* dr = nullptr) {
   if (m->tp_world > 1) return NE_ERR_UNSUPPORTED;
   int rc = ne_forward(m, &rows, NE_LM_LOGITS, m->sample_logits, nullptr, s);
   if (rc) return rc;
@@ -763,10 +764,24 @@ int sampled_tail(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot,
             ne::launch_sample_stats(*st, seq_slot, num_seqs, m->rb.lm_start, m->rb.q_len, m->rb.lm_count, rows.lm_max,
                                     m->sample_logits, m->cfg.vocab_size, m->sample_stats, s), s);
   if (rc) return rc;
+  const __nv_bfloat16* dl = nullptr;
+  ne::SampleStats* ds = nullptr;
+  if (dr) {  // the draft's rows of every guess: their statistics, one region (draft step) at a time
+    dl = static_cast<const __nv_bfloat16*>(dr->logits);
+    ds = static_cast<ne::SampleStats*>(dr->stats);
+    for (int j = 0; j < k; ++j) {
+      rc = note(m, NE_K_SAMPLE,
+                ne::launch_sample_stats(*st, seq_slot, num_seqs, dr->start, nullptr, nullptr, num_seqs,
+                                        dl + (size_t)j * dr->stride * m->cfg.vocab_size, m->cfg.vocab_size,
+                                        ds + (size_t)j * dr->stride, s), s);
+      if (rc) return rc;
+    }
+  }
   return note(m, NE_K_ACCEPT,
               ne::launch_accept_sampled(*st, seq_slot, num_seqs, k, spec ? m->rb.draft_len : nullptr, m->rb.q_len,
                                         m->rb.lm_start, m->sample_logits, m->cfg.vocab_size, m->sample_stats,
-                                        m->keys, *out, m->status, s), s);
+                                        m->keys, *out, m->status, s, dl, dr ? dr->start : nullptr, ds,
+                                        dr ? dr->stride : 1), s);
 }
 
 }  // namespace
@@ -859,7 +874,7 @@ namespace {
 // The speculative step after its drafts (m->rb.draft_len, histories) are in place: reserve and
 // plan, verify forward, acceptance.
 int spec_step_tail(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int k,
-                   const ne_step_outputs* out, cudaStream_t s) {
+                   const ne_step_outputs* out, cudaStream_t s, const ne_draft_rows* dr = nullptr) {
   const int max_rows = num_seqs * (k + 1);
   int rc = note(m, NE_K_PLAN,
             ne::launch_plan(*st, seq_slot, num_seqs, ne::PLAN_SPEC, max_rows, 0, m->cfg.block_size,
@@ -873,7 +888,7 @@ int spec_step_tail(ne_model* m, const ne_batch_state* st, const int32_t* seq_slo
       m->rows_hint = 0;
       return NE_ERR_WORKSPACE;
     }
-    rc = sampled_tail(m, st, seq_slot, num_seqs, k, rows, true, out, s);
+    rc = sampled_tail(m, st, seq_slot, num_seqs, k, rows, true, out, s, dr);
     m->rows_hint = 0;
     return rc;
   }
@@ -904,16 +919,21 @@ int ne_draft_sync(const ne_batch_state* target, const ne_batch_state* draft, con
   return ne::launch_draft_sync(*target, *draft, seq_slot, num_seqs, k, as_stream(stream));
 }
 
+const int32_t* ne_model_lm_start(const ne_model* m) { return m && m->ws ? m->rb.lm_start : nullptr; }
+
 int ne_spec_step_drafted(ne_model* m, const ne_batch_state* st, const ne_batch_state* draft, const int32_t* seq_slot,
-                         int num_seqs, int k, const ne_step_outputs* out, void* stream) {
+                         int num_seqs, int k, const ne_step_outputs* out, void* stream, const ne_draft_rows* dr) {
   if (!m || !st || !draft || !seq_slot || !out || num_seqs <= 0 || k < 1) return NE_ERR_INVALID;
+  if (dr && (!dr->logits || !dr->start || !dr->stats || dr->stride < num_seqs || dr->rows < k * dr->stride ||
+             !m->sample_logits))
+    return NE_ERR_INVALID;
   const int max_rows = num_seqs * (k + 1);
   if (max_rows > m->max_rows || num_seqs > m->max_seqs) return NE_ERR_WORKSPACE;
   cudaStream_t s = as_stream(stream);
   const int rc = note(m, NE_K_NGRAM,
                       ne::launch_draft_propose(*st, *draft, seq_slot, num_seqs, k, m->rb.draft_len, m->status, s), s);
   if (rc) return rc;
-  return spec_step_tail(m, st, seq_slot, num_seqs, k, out, s);
+  return spec_step_tail(m, st, seq_slot, num_seqs, k, out, s, dr);
 }
 
 int ne_gemm_bf16(const void* x, const void* w, void* y, int M, int N, int K, int32_t* status, void* stream) {

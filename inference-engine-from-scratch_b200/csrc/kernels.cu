@@ -244,6 +244,7 @@ __global__ void draft_sync_kernel(ne_batch_state st, ne_batch_state dt, const in
   if (threadIdx.x == 0) {
     dt.seq_len[s] = Lt;
     dt.num_cached[s] = min(dt.num_cached[s], common);
+    if (dt.rng_draws && st.rng_draws) dt.rng_draws[s] = st.rng_draws[s];  // sampled drafts: the same stream
   }
 }
 
@@ -270,6 +271,8 @@ __global__ void draft_propose_kernel(ne_batch_state st, ne_batch_state dt, const
   int32_t* ht = st.history + (long long)s * st.history_stride;
   for (int j = 0; j < cap; ++j) ht[L + j] = hd[L + j];
   draft_len[b] = cap;
+  // a sampled draft drew one uniform per guess: verification continues after the guesses used
+  if (st.temperature && st.rng_draws && st.temperature[s] > 0.f) st.rng_draws[s] += cap;
 }
 
 // ------------------------------------------------------------------ n-gram drafts

@@ -711,7 +711,8 @@ __global__ void __launch_bounds__(THREADS)
                           const int32_t* __restrict__ lm_start, const __nv_bfloat16* __restrict__ logits, int vocab,
                           const SampleStats* __restrict__ stats, const unsigned long long* __restrict__ keys,
                           ne_step_outputs out, int* status, const __nv_bfloat16* __restrict__ draft_logits,
-                          const int32_t* __restrict__ draft_start, const SampleStats* __restrict__ draft_stats) {
+                          const int32_t* __restrict__ draft_start, const SampleStats* __restrict__ draft_stats,
+                          int draft_stride) {
   pdl_prologue();
   __shared__ DrawShared sh;
   const int b = blockIdx.x;
@@ -786,7 +787,7 @@ __global__ void __launch_bounds__(THREADS)
       float a = fminf(kept_p(p, sj, rank), 1.0f);
       if (draft_logits) {
         // the draft's probability of its guess: acceptance min(1, p / max(q, 1e-12))
-        const int dr = draft_start[b] + j;
+        const int dr = draft_start[b] + j * draft_stride;
         const SampleStats qj = draft_stats[dr];
         const __nv_bfloat16* qrow = draft_logits + (long long)dr * vocab;
         const float q = prob(scaled(qrow, guess, T), qj.m, qj.z);
@@ -876,12 +877,12 @@ int launch_accept_sampled(const ne_batch_state& st, const int32_t* seq_slot, int
                           const __nv_bfloat16* logits, int vocab, const SampleStats* stats,
                           const unsigned long long* keys, const ne_step_outputs& out, int* status,
                           cudaStream_t stream, const __nv_bfloat16* draft_logits, const int32_t* draft_start,
-                          const SampleStats* draft_stats) {
+                          const SampleStats* draft_stats, int draft_stride) {
   if (num_seqs <= 0) return NE_OK;
-  if (draft_logits && (!draft_start || !draft_stats || !draft_len)) return NE_ERR_INVALID;
+  if (draft_logits && (!draft_start || !draft_stats || !draft_len || draft_stride < 1)) return NE_ERR_INVALID;
   return launch_kernel(accept_sampled_kernel, dim3(num_seqs), dim3(THREADS), 0, stream, st, seq_slot, k, draft_len,
                        q_len, lm_start, logits, vocab, stats, keys, out, status, draft_logits, draft_start,
-                       draft_stats) == cudaSuccess
+                       draft_stats, draft_stride) == cudaSuccess
              ? NE_OK
              : NE_ERR_CUDA;
 }

@@ -155,6 +155,17 @@ class B200SpeculativeEngine:
             self.draft_state = DeviceBatchState(max_seqs, max_model_len, k, dblocks, 16, (), model.device)
             self._draft_outs = _Outputs(max_seqs, k, model.device)
             self.max_prefill_rows = min(self.max_prefill_rows, draft_model.max_rows)
+            self._draft_rows = None
+            if sampling:
+                # sampled drafts: each of the k draft steps keeps its rows (one per entry) in its own
+                # region of one buffer, regions a whole number of vocabulary rows apart, for the
+                # verification against the draft's distributions
+                row_bytes = 2 * draft_model.cfg.vocab_size
+                need = int(self.lib.ne_sampling_buffer_bytes(draft_model.handle, max_seqs))
+                self._region_rows = -(-need // row_bytes)
+                self._region_bytes = self._region_rows * row_bytes
+                self._draft_regions = torch.empty(k * self._region_bytes, dtype=torch.uint8, device=model.device)
+                self._draft_stats = torch.empty(k * self._region_rows * 32, dtype=torch.uint8, device=model.device)
         self._uncached: dict[int, int] = {}       # slot -> prompt tokens still to prefill
         self._prefixes: dict[int, list] = {}      # holder slot -> [tokens, shared blocks, users, copies]
         self._prefix_of: dict[int, int] = {}      # slot -> holder slot of its shared prefix
@@ -175,8 +186,8 @@ class B200SpeculativeEngine:
         ``add_prefix``) shares the KV blocks of a prompt prefix the request starts with."""
         if temperature != 0.0 and not self.sampling:
             raise ValueError("temperature > 0 needs an engine built with sampling=True")
-        if self.draft_state is not None and (temperature != 0.0 or prefix is not None):
-            raise ValueError("draft-model drafts serve greedy requests without shared prefixes")
+        if self.draft_state is not None and prefix is not None:
+            raise ValueError("draft-model drafts serve requests without shared prefixes")
         if prefix is not None:
             tokens = self._prefixes[prefix][0]
             if prompt[: len(tokens)] != tokens:
@@ -197,7 +208,8 @@ class B200SpeculativeEngine:
         self._uncached[slot] = len(prompt) - shared
         if self.draft_state is not None:
             # the draft sequence never finishes on its own: it follows the target (ne_draft_sync)
-            self.draft_state.load(slot, prompt, self.state.max_model_len - len(prompt), ignore_eos=True)
+            self.draft_state.load(slot, prompt, self.state.max_model_len - len(prompt), ignore_eos=True,
+                                  temperature=temperature, top_p=top_p, seed=seed, draws=draws)
             self.draft_state.max_new_tokens[slot] = 1 << 30
             self.h2d_bytes += 4 * len(prompt) + 5 * 4 + 4 + 4 + 8 + 8
         return slot
@@ -238,6 +250,16 @@ class B200SpeculativeEngine:
             raise ValueError("the engine was built without sampling")
         vocab = self.model.cfg.vocab_size
         return self._sample_buf[: rows * vocab * 2].view(torch.bfloat16).view(rows, vocab)
+
+    def draft_logits(self, num_entries: int) -> tuple[torch.Tensor, list[int]]:
+        """The last sampled draft-model step's draft rows: ``[k, rows, vocab]`` bf16 (draft step j
+        in region j) and, per batch entry, its row in every region."""
+        if self.draft_state is None or not self.sampling:
+            raise ValueError("the engine has no sampled draft model")
+        vocab = self.draft_model.cfg.vocab_size
+        regions = self._draft_regions.view(torch.bfloat16).view(self.k, -1)[:, : self._region_rows * vocab]
+        start = _lib.device_int32(self.lib.ne_model_lm_start(self.draft_model.handle), num_entries, self.model.device)
+        return regions.reshape(self.k, self._region_rows, vocab), start.cpu().tolist()
 
     def release(self, slots: list[int]) -> None:
         self.state.release(slots)
@@ -321,6 +343,7 @@ class B200SpeculativeEngine:
         if self.draft_state is not None:
             # the draft model prefills the same prompt tokens into its own cache (its own first
             # token is replaced by the target's at the next ne_draft_sync)
+            self._bind_draft_region(0)
             _lib.check(self.lib.ne_prefill(self.draft_model.handle, self.draft_state.ref, self._slots_dev.data_ptr(),
                                            len(slots), max(rows, 1), self.k, chunk,
                                            ctypes.byref(self._draft_outs.struct), _lib.stream_handle()),
@@ -343,13 +366,28 @@ class B200SpeculativeEngine:
         stream, slots = _lib.stream_handle(), self._slots_dev.data_ptr()
         _lib.check(self.lib.ne_draft_sync(self.state.ref, self.draft_state.ref, slots, bucket, self.k, stream),
                    "ne_draft_sync")
-        for _ in range(self.k):
+        for j in range(self.k):
+            self._bind_draft_region(j)  # (sampled drafts: step j's rows stay in region j)
             _lib.check(self.lib.ne_prefill(self.draft_model.handle, self.draft_state.ref, slots, bucket,
                                            bucket * (self.k + 1), self.k, 0, ctypes.byref(self._draft_outs.struct),
                                            stream), "ne_prefill (draft step)")
+        rows = None
+        if self.sampling:
+            rows = _lib.DraftRows(logits=self._draft_regions.data_ptr(),
+                                  start=self.lib.ne_model_lm_start(self.draft_model.handle),
+                                  stride=self._region_rows, rows=self.k * self._region_rows,
+                                  stats=self._draft_stats.data_ptr())
         _lib.check(self.lib.ne_spec_step_drafted(self.model.handle, self.state.ref, self.draft_state.ref, slots, bucket,
-                                                 self.k, ctypes.byref(self._outs[buf].struct), stream),
+                                                 self.k, ctypes.byref(self._outs[buf].struct), stream,
+                                                 ctypes.byref(rows) if rows is not None else None),
                    "ne_spec_step_drafted")
+
+    def _bind_draft_region(self, j: int) -> None:
+        if self.draft_state is None or not self.sampling:
+            return
+        _lib.check(self.lib.ne_model_set_sampling_buffer(
+            self.draft_model.handle, self._draft_regions.data_ptr() + j * self._region_bytes, self._region_bytes,
+            self.max_seqs), "ne_model_set_sampling_buffer (draft)")
 
     def launch(self, slots: list[int], buf: int = 0) -> int:
         """Enqueue one step for ``slots`` (no host sync) writing result buffer ``buf``; returns the

@@ -104,13 +104,14 @@ def test_batched_engine_with_a_draft_model(models, graphs, same) -> None:
         (twin if same else draft).raise_on_device_error()
 
 
-def test_draft_engine_refuses_sampled_requests_and_a_shared_kv_pool(models) -> None:
+def test_draft_engine_refuses_shared_prefixes_and_a_shared_kv_pool(models) -> None:
     _, target, draft, _ = models
     engine = submodule("engine")
     eng = engine.B200SpeculativeEngine(target, k=4, max_seqs=2, max_model_len=256, num_blocks=64,
-                                       cuda_graphs=False, sampling=True, draft_model=draft)
+                                       cuda_graphs=False, draft_model=draft)
+    holder = eng.add_prefix(list(range(1, 40)))
     with pytest.raises(ValueError):
-        eng.add_request([1, 2, 3], 4, temperature=0.8)
+        eng.add_request(list(range(1, 50)), 4, prefix=holder)
     with pytest.raises(ValueError):  # the draft needs a KV pool of its own
         engine.B200SpeculativeEngine(target, k=4, max_seqs=2, max_model_len=256, num_blocks=64,
                                      cuda_graphs=False, draft_model=target)

@@ -263,3 +263,110 @@ def test_serial_sampled_draft_model_replays_on_the_oracle() -> None:
     assert len(cases) >= len(golden["records"]) and any(c["guesses"] for c in cases)
     target.close()
     draft_model.close()
+
+
+@pytest.mark.parametrize("cuda_graphs", [False, True])
+def test_batched_engine_sampled_draft_steps_replay_on_the_oracle(cuda_graphs) -> None:
+    """The batched engine with a sampled one-layer draft: every step's guesses are the draft's
+    draws on the request's stream, and its verification replays on the oracle from the step's own
+    target and draft rows; greedy requests in the same batch keep the argmax rule."""
+    submodule("build").build()
+    pkg = package()
+    cfg = pkg.SMALL_TEST
+    mk = submodule("model").B200Model
+    target = mk(cfg, pkg.make_weights(cfg, seed=0), num_slots=96 * 16, device="cuda:0", max_positions=512,
+                max_rows=512, max_seqs=8)
+    dcfg = pkg.Qwen3Config(**{**{f: getattr(cfg, f) for f in cfg.__dataclass_fields__}, "num_hidden_layers": 1})
+    draft_model = mk(dcfg, pkg.make_weights(dcfg, seed=1), num_slots=96 * 16, device="cuda:0", max_positions=512,
+                     max_rows=512, max_seqs=8)
+    k, max_new = 4, 24
+    eng = submodule("engine").B200SpeculativeEngine(target, k=k, max_seqs=4, max_model_len=256, num_blocks=96,
+                                                    cuda_graphs=cuda_graphs, sampling=True, draft_model=draft_model,
+                                                    draft_num_blocks=96)
+    prompts = pkg.make_prompts(4, cfg.vocab_size, length=40, seed=13)
+    params = [(0.8, 0.95), (1.0, 1.0), (0.0, 1.0), (0.5, 0.9)]
+    slots, meta = [], {}
+    for i, (prompt, (t, p)) in enumerate(zip(prompts, params)):
+        slot = eng.add_request(prompt, max_new, ignore_eos=True, temperature=t, top_p=p, seed=300 + i)
+        slots.append(slot)
+        meta[slot] = (t, p, 300 + i, len(prompt))
+    eng.prefill(slots)
+    running = list(slots)
+    vocab = cfg.vocab_size
+    exact = total = 0
+    while running:
+        L = {s: int(eng.state.seq_len[s].item()) for s in running}
+        draws_before = {s: int(eng.state.rng_draws[s].item()) for s in running}
+        res = eng.step(running)
+        draws_after = {s: int(eng.state.rng_draws[s].item()) for s in running}
+        regions, lm_draft = eng.draft_logits(len(running))  # entry b of draft step j: regions[j, lm_draft[b]]
+        row = 0
+        sampled_rows = sum(min(k, max_new - (L[s] - meta[s][3]) - 1) + 1 for s in running)
+        target_logits = eng.sampled_logits(sampled_rows)
+        for b, s in enumerate(running):
+            t, p, seed, plen = meta[s]
+            g = max(0, min(k, max_new - (L[s] - plen) - 1))
+            guesses = eng.draft_state.history[s, L[s]:L[s] + g].tolist()
+            case = {"logits": target_logits[row:row + g + 1].float().cpu(),
+                    "draft_logits": regions[:g, lm_draft[b]].float().cpu() if g else torch.zeros(0, vocab),
+                    "guesses": guesses, "temperature": t, "top_p": p, "seed": seed, "start": draws_before[s] + g}
+            row += g + 1
+            if t > 0:
+                for j, guess in enumerate(guesses):  # the draft's draws
+                    dist = overify.token_probabilities(case["draft_logits"][j], t, p, True)
+                    u = next(philox.UniformStream(seed, draws_before[s] + j))
+                    c = np.cumsum(dist.double().numpy()) / float(dist.double().sum())
+                    i = int(np.searchsorted(c, u, side="right"))
+                    near = min(abs(c[x] - u) for x in (i - 1, i) if 0 <= x < len(c))
+                    assert guess == overify.inverse_cdf(dist, u) or near < MARGIN
+                expect, expect_draws = oracle_drafted(case)
+                got = res.tokens[s]
+                total += 1
+                if got == expect and draws_after[s] == expect_draws:
+                    exact += 1
+                else:
+                    assert draft_margin(case) < MARGIN, f"mismatch without a near-tie: {got} vs {expect}"
+            else:  # greedy: the kept guesses are the target's argmax run
+                am = case["logits"].argmax(dim=-1).tolist()
+                kept = 0
+                while kept < g and guesses[kept] == am[kept]:
+                    kept += 1
+                assert res.tokens[s] == (guesses[:kept] + [am[kept]])[: len(res.tokens[s])]
+        running = [s for s in running if res.finish[s] is None]
+    assert total > 0 and exact >= MIN_EXACT * total
+    target.raise_on_device_error()
+    draft_model.raise_on_device_error()
+    del eng
+    target.close()
+    draft_model.close()
+
+
+
+def test_batched_engine_sampled_draft_generate_is_reproducible() -> None:
+    """generate() with a sampled draft model (6 requests through 4 slots): the same outputs eager
+    and from CUDA graphs."""
+    submodule("build").build()
+    pkg = package()
+    cfg = pkg.SMALL_TEST
+    mk = submodule("model").B200Model
+    engine = submodule("engine")
+    dcfg = pkg.Qwen3Config(**{**{f: getattr(cfg, f) for f in cfg.__dataclass_fields__}, "num_hidden_layers": 1})
+    prompts = pkg.make_prompts(6, cfg.vocab_size, length=36, seed=5)
+    outs = []
+    for graphs in (False, True):
+        target = mk(cfg, pkg.make_weights(cfg, seed=0), num_slots=128 * 16, device="cuda:0", max_positions=512,
+                    max_rows=512, max_seqs=8)
+        draft_model = mk(dcfg, pkg.make_weights(dcfg, seed=1), num_slots=128 * 16, device="cuda:0",
+                         max_positions=512, max_rows=512, max_seqs=8)
+        eng = engine.B200SpeculativeEngine(target, k=4, max_seqs=4, max_model_len=256, num_blocks=128,
+                                           cuda_graphs=graphs, sampling=True, draft_model=draft_model,
+                                           draft_num_blocks=128)
+        outs.append(eng.generate(prompts, 20, temperature=0.8, top_p=0.95, seeds=[40 + i for i in range(6)]))
+        assert eng.proposed_total > 0
+        target.raise_on_device_error()
+        draft_model.raise_on_device_error()
+        del eng
+        target.close()
+        draft_model.close()
+    assert outs[0] == outs[1]
+    assert all(len(o) == 20 for o in outs[0])
