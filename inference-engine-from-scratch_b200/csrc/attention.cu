@@ -8,7 +8,8 @@
 //
 // * One query tile (the speculative step: (k+1) x G <= 16 vectors): the four warps take every
 //   fourth block of the split, each with its own cp.async double buffer, and merge their
-//   (max, sum, O) through shared memory at the end.
+//   (max, sum, O) through shared memory at the end. Two tiles (17-32 vectors) get one CTA each
+//   (grid z = split x tile), so that an entry with two tiles takes no longer than one with one.
 // * More tiles (prefill): the CTA loads each block once into a shared double buffer and warp w
 //   works on query tiles w, w+4, ...
 // * Split-KV (few sequences): each split writes its unnormalised partial (O, max, sum) and
@@ -154,35 +155,42 @@ __device__ __forceinline__ uint32_t dq_pair(uint32_t word, uint32_t sel, uint32_
   asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(q), "r"(scale2));
   return r;
 }
-// Raw int8 block (staged by stage_raw_int8) -> bf16 K / V blocks in the padded row layout.
-__device__ __forceinline__ void convert_raw_int8(uint32_t raw, uint32_t k_s, uint32_t v_s, uint32_t scales,
-                                                 int lane) {
+// 16 raw int8 rows (16 tokens x 128, at ``raw``) -> bf16 rows in the padded layout at ``dst``; the
+// scale of token t is lane ``scale_lane + t``'s ``scales``. All four loads go out before the
+// conversion (one shared-memory latency per block, not one per chunk).
+__device__ __forceinline__ void convert_half_int8(uint32_t raw, uint32_t dst, uint32_t scales, int scale_lane,
+                                                  int lane) {
+  uint32_t w[4][4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int i = lane + 32 * j, tok = i >> 3, ch = i & 7;
-    const uint32_t ks = __shfl_sync(0xFFFFFFFFu, scales, tok), vs = __shfl_sync(0xFFFFFFFFu, scales, 16 + tok);
-    const uint32_t ks2 = ks | (ks << 16), vs2 = vs | (vs << 16);
-#pragma unroll
-    for (int kv = 0; kv < 2; ++kv) {
-      uint32_t w[4];
-      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                   : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
-                   : "r"(raw + kv * 2048 + tok * 128 + ch * 16));
-      const uint32_t s2 = kv ? vs2 : ks2;
-      uint32_t o[8];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        o[2 * t] = dq_pair(w[t], 0x4140u, s2);
-        o[2 * t + 1] = dq_pair(w[t], 0x4342u, s2);
-      }
-      const uint32_t dst = (kv ? v_s : k_s) + tok * ROW_BYTES + ch * 32;
-      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3])
-                   : "memory");
-      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst + 16), "r"(o[4]), "r"(o[5]), "r"(o[6]),
-                   "r"(o[7])
-                   : "memory");
-    }
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(w[j][0]), "=r"(w[j][1]), "=r"(w[j][2]), "=r"(w[j][3])
+                 : "r"(raw + tok * 128 + ch * 16));
   }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int i = lane + 32 * j, tok = i >> 3, ch = i & 7;
+    const uint32_t sc = __shfl_sync(0xFFFFFFFFu, scales, scale_lane + tok);
+    const uint32_t s2 = sc | (sc << 16);
+    uint32_t o[8];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      o[2 * t] = dq_pair(w[j][t], 0x4140u, s2);
+      o[2 * t + 1] = dq_pair(w[j][t], 0x4342u, s2);
+    }
+    const uint32_t d = dst + tok * ROW_BYTES + ch * 32;
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(d), "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3])
+                 : "memory");
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(d + 16), "r"(o[4]), "r"(o[5]), "r"(o[6]), "r"(o[7])
+                 : "memory");
+  }
+}
+// Raw int8 block (staged by stage_raw_int8) -> bf16 K / V blocks in the padded row layout.
+__device__ __forceinline__ void convert_raw_int8(uint32_t raw, uint32_t k_s, uint32_t v_s, uint32_t scales,
+                                                 int lane) {
+  convert_half_int8(raw, k_s, scales, 0, lane);
+  convert_half_int8(raw + 2048, v_s, scales, 16, lane);
 }
 
 // A block-table entry checked against the pool: the id, or -1 (reported) when it names no block.
@@ -298,12 +306,15 @@ __device__ __forceinline__ void tile_block(TileState& ts, uint32_t k_s, uint32_t
     psum[r] += __shfl_xor_sync(0xFFFFFFFFu, psum[r], 2);
     ts.l[r] = ts.l[r] * corr[r] + psum[r];
   }
+  // (a max that did not move leaves every factor at exactly 1: the products are skipped)
+  if (__any_sync(0xFFFFFFFFu, corr[0] != 1.f || corr[1] != 1.f)) {
 #pragma unroll
-  for (int t = 0; t < 16; ++t) {
-    ts.o[t][0] *= corr[0];
-    ts.o[t][1] *= corr[0];
-    ts.o[t][2] *= corr[1];
-    ts.o[t][3] *= corr[1];
+    for (int t = 0; t < 16; ++t) {
+      ts.o[t][0] *= corr[0];
+      ts.o[t][1] *= corr[0];
+      ts.o[t][2] *= corr[1];
+      ts.o[t][3] *= corr[1];
+    }
   }
 #pragma unroll
   for (int t = 0; t < 16; t += 2) {
@@ -355,7 +366,7 @@ __device__ __forceinline__ void tile_store(const Ctx& c, const AttnSplit& sp, co
 template <bool INT8, int NT, int NW>
 __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& rows, const AttnSplit& sp, int b, int h,
                                                  int split, int kb0, int kb1, uint8_t* q_s, int* spos, uint8_t* buf,
-                                                 __nv_bfloat16* out, int nh, int nkv) {
+                                                 __nv_bfloat16* out, int nh, int nkv, int v_base = 0) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t buf_u = smem_u32(buf);
   const int per_tile = NW / NT, my_tile = warp % NT, phase = warp / NT;
@@ -391,11 +402,11 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
     }
   }
   cp_commit();
-  if (tid < 32) spos[tid] = tid < c.nvec ? rows.positions[c.r0 + tid / c.G] : -1;
+  if (tid < 32) spos[tid] = v_base + tid < c.nvec ? rows.positions[c.r0 + (v_base + tid) / c.G] : -1;
   TileState ts;
   for (int t = 0; t < NT; ++t) {  // one Q staging area: tile t's warps take their fragments in turn
     if (t > 0) __syncthreads();
-    load_q_tile(c, 16 * t, q_s, tid, 32 * NW);
+    load_q_tile(c, v_base + 16 * t, q_s, tid, 32 * NW);
     __syncthreads();
     if (my_tile == t) tile_init(ts, smem_u32(q_s), spos + 16 * t, lane);
   }
@@ -481,7 +492,7 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const int row = (lane >> 2) + 8 * r;
-    if (my_tile * 16 + row >= c.nvec) continue;  // padding rows of the tile are never read
+    if (v_base + my_tile * 16 + row >= c.nvec) continue;  // padding rows of the tile are never read
 #pragma unroll
     for (int t = 0; t < 16; ++t) {
       const int d = 8 * t + 2 * (lane & 3);
@@ -493,7 +504,7 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
     }
   }
   __syncthreads();
-  for (int v = 0; v < min(16 * NT, c.nvec); ++v) {
+  for (int v = 0; v < min(16 * NT, c.nvec - v_base); ++v) {
     const int t = v >> 4, row = v & 15;
     float m = NEG_INF;
     for (int i = 0; i < per_tile; ++i) m = fmaxf(m, mm[(t + NT * i) * 16 + row]);
@@ -510,11 +521,11 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
         }
       }
       if (sp.splits == 1) {
-        const int orow = c.r0 + v / c.G;
-        const int head = c.h * c.G + v % c.G;
+        const int orow = c.r0 + (v_base + v) / c.G;
+        const int head = c.h * c.G + (v_base + v) % c.G;
         out[((long long)orow * nh + head) * D + d] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
       } else {
-        const long long base = (((long long)b * nkv + h) * sp.splits + split) * sp.max_vec + v;
+        const long long base = (((long long)b * nkv + h) * sp.splits + split) * sp.max_vec + v_base + v;
         sp.part_o[base * D + d] = o;
         if (d == 0) {
           sp.part_m[base] = m;
@@ -535,7 +546,10 @@ __global__ void __launch_bounds__(32 * NW, NW == 4 ? 3 : 5)
                      AttnSplit sp, int* status, KvShadow shadow) {
   pdl_prologue();
   extern __shared__ __align__(16) uint8_t smem[];
-  const int b = blockIdx.x, h = blockIdx.y, split = blockIdx.z;
+  // z = split * tile slots + tile: with more than one tile slot, CTA (b, h, z) serves query tile
+  // z % slots of the entry alone (an entry with fewer tiles leaves the CTA idle)
+  const int slots = gridDim.z / sp.splits;
+  const int b = blockIdx.x, h = blockIdx.y, split = blockIdx.z / slots, tile = blockIdx.z % slots;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ql = rows.q_len[b];
   if (ql <= 0) return;
@@ -567,10 +581,13 @@ __global__ void __launch_bounds__(32 * NW, NW == 4 ? 3 : 5)
   uint8_t* buf = smem + BLOCK_BYTES + 256;               // K/V stages
   const uint32_t buf_u = smem_u32(buf);
 
-  if (ntiles == 1) {
+  if (slots > 1) {
+    if (tile < ntiles)
+      warp_split_tiles<INT8, 1, NW>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 16 * tile);
+  } else if (ntiles == 1) {
     warp_split_tiles<INT8, 1, NW>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv);
   } else if (NW != 4) {
-    report(status, NE_DEV_BAD_SLOT);  // the host launches the 2-warp kernel only for one-tile rows
+    report(status, NE_DEV_BAD_SLOT);  // the host launches the 2-warp kernel only for one-tile CTAs
   } else if (ntiles == 2) {
     warp_split_tiles<INT8, 2, 4>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv);
   } else {
@@ -765,7 +782,15 @@ int launch_attention_tc(const __nv_bfloat16* q, __nv_bfloat16* out, const void* 
   int sms = 148, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const long long ctas = (long long)rows.num_seqs * num_kv_heads * sp.splits;
-  const int nw = (max_vec <= 16 && ctas <= 5LL * sms && ctas > 3LL * sms) ? 2 : 4;
+  // Two query tiles (17-32 vectors: k = 8 drafts at G = 2): one CTA per tile, so that an entry with
+  // two tiles takes no longer than one with one (NE_ATTN_TILE_CTAS=0: both tiles in one CTA).
+  static const bool tile_ctas = [] {
+    const char* e = getenv("NE_ATTN_TILE_CTAS");
+    return !(e && e[0] == '0');
+  }();
+  const int tile_slots = (tile_ctas && max_vec > 16 && max_vec <= 32) ? 2 : 1;
+  // two warps (five CTAs per SM) when one-tile CTAs would spill into a second wave of four-warp CTAs
+  const int nw = ((max_vec <= 16 || tile_slots > 1) && ctas <= 5LL * sms && ctas > 3LL * sms) ? 2 : 4;
   const size_t smem = attention_smem_bytes_nw(nw);
   static bool attr_set[4] = {false, false, false, false};
   auto kernel = kv_int8 ? (nw == 2 ? attention_kernel<true, 2> : attention_kernel<true, 4>)
@@ -782,7 +807,7 @@ int launch_attention_tc(const __nv_bfloat16* q, __nv_bfloat16* out, const void* 
     if (launch_kernel(clear_partials_kernel, dim3(blocks), dim3(256), 0, stream, sp, n) != cudaSuccess)
       return NE_ERR_CUDA;
   }
-  dim3 grid(rows.num_seqs, num_kv_heads, sp.splits);
+  dim3 grid(rows.num_seqs, num_kv_heads, sp.splits * tile_slots);
   if (shadow.map && (!kv_int8 || !shadow.k || !shadow.v || shadow.blocks < 1)) return NE_ERR_INVALID;
   if (launch_kernel(kernel, grid, dim3(32 * nw), smem, stream, q, out, k_cache, v_cache, k_scale, v_scale, rows,
                     num_heads, num_kv_heads, num_cache_slots, sp, status, shadow) != cudaSuccess)

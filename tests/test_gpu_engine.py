@@ -246,10 +246,12 @@ def test_profile_times_every_launch_eagerly_and_inside_a_captured_step(small) ->
     eng.release(slots)
 
 
-def test_int8_shared_prefix_reads_dequantised_block_copies() -> None:
+@pytest.mark.parametrize("k", [4, 8])
+def test_int8_shared_prefix_reads_dequantised_block_copies(k) -> None:
     """int8 KV: the shared prefix's blocks are dequantised once (bf16(q * scale), the attention's
     own conversion) and the attention reads the copies; outputs equal the unshared run, the copies
-    equal the pool blocks they stand for, and dropping the prefix unmaps them."""
+    equal the pool blocks they stand for, and dropping the prefix unmaps them. k = 8 gives two
+    query tiles per KV head (the warps of a pair share each int8 block's conversion)."""
     submodule("build").build()
     pkg = package()
     cfg = pkg.SMALL_TEST
@@ -259,9 +261,9 @@ def test_int8_shared_prefix_reads_dequantised_block_copies() -> None:
     g = torch.Generator().manual_seed(17)
     prefix = torch.randint(0, cfg.vocab_size, (40,), generator=g).tolist()  # 2 full blocks + 8 tokens
     prompts = [prefix + t for t in pkg.make_prompts(4, cfg.vocab_size, length=30, seed=3)]
-    plain = _engine(model, 2, True).generate(prompts, 24)
+    plain = _engine(model, 2, True, k=k).generate(prompts, 24)
     assert int((model.kv_copy_map >= 0).sum()) == 0
-    eng = _engine(model, 2, True)
+    eng = _engine(model, 2, True, k=k)
     shared = eng.generate(prompts, 24, shared_prefix=len(prefix))
     assert shared == plain
     assert int((model.kv_copy_map >= 0).sum()) == 0  # generate dropped its prefix

@@ -161,6 +161,8 @@ ATTENTION_CASES = [
     # two query tiles per KV head (k = 8 drafts, G = 2): warp-split path, with and without split-KV
     (16, 8, [9, 3, 9], [700, 40, 300], 8),
     (16, 8, [9, 7], [1100, 160], 0),
+    # enough (entry, KV head) pairs for the two-warp launch (one wave of five CTAs per SM)
+    (16, 8, [9] * 60, [30 + (i * 37) % 350 for i in range(60)], 0),
 ]
 
 
@@ -168,7 +170,7 @@ ATTENTION_CASES = [
 @pytest.mark.parametrize("kv_int8", [False, True])
 def test_paged_attention_matches_fp32_reference(lib, cuda_device, nh, nkv, q_lens, ctx, scratch_mb, kv_int8) -> None:
     g = torch.Generator().manual_seed(sum(ctx) + kv_int8)
-    num_blocks = 96
+    num_blocks = max(96, sum((c + 15) // 16 for c in ctx))
     shape = (num_blocks * 16 + 1, nkv, 128)
     k_cache = torch.randn(shape, generator=g).to(torch.bfloat16)
     v_cache = torch.randn(shape, generator=g).to(torch.bfloat16)
