@@ -522,8 +522,14 @@ def run_b200(args, dist: Dist) -> None:
     bytes_launch = algorithmic_bytes(dominant, cfg, M, ctx_sum, per_layer_kv, wb)
     peak, peak_src = measured_peak()
     achieved = bytes_launch / (avg_ms / 1000.0) / 1e9
-    # DRAM bytes per launch from the committed ncu capture (attention scaled to this step's context)
-    t_rec = ncu_traffic().get(dominant)
+    # DRAM bytes per launch from the committed ncu capture of the same kernel variant (attention
+    # scaled to this step's context); int8 KV / int8 weights have captures of their own
+    variant = dominant
+    if dominant == "attention" and model.kv_int8:
+        variant = "attention_int8"
+    elif dominant != "attention" and wl.weight_int8:
+        variant = dominant + "_w8"
+    t_rec = ncu_traffic().get(variant)
     traffic = None
     if isinstance(t_rec, dict) and "dram_bytes" in t_rec:
         traffic = float(t_rec["dram_bytes"])
