@@ -440,6 +440,9 @@ def run_b200(args, dist: Dist) -> None:
     engine = engine_mod.B200SpeculativeEngine(model, k=k, max_ngram=3, max_seqs=users + (1 if wl.shared_prefix else 0),
                                               max_model_len=max_model_len, num_blocks=num_blocks, cuda_graphs=True,
                                               sampling=wl.sampled)
+    if not args.profile_step and not wl.tp:
+        # every bucket's step graph before any timing, as the reference's runtime does at start-up
+        engine.capture_all_buckets()
 
     # ------------------------------------------------------------ steady state (value)
     prefix = engine.add_prefix(prompts[0][: wl.shared_prefix]) if wl.shared_prefix else None

@@ -409,6 +409,18 @@ class B200SpeculativeEngine:
         self.launch(slots)
         return self._collect(slots)
 
+    def capture_all_buckets(self) -> int:
+        """Capture every batch bucket's step up front (both result buffers), largest first, so
+        that no step waits for a capture while requests are served: the reference's
+        DecodeGraphRunner.capture_all_buckets (engine/generation/cuda_graph_runner.py:93-104),
+        which its runtime calls at start-up (engine/runtime.py:160). Returns the graphs held."""
+        if self.cuda_graphs:
+            for bucket in reversed(self.buckets):
+                for buf in (0, 1):
+                    if (bucket, buf) not in self._graphs:
+                        self._capture(bucket, buf)
+        return len(self._graphs)
+
     def _capture(self, bucket: int, buf: int = 0) -> torch.cuda.CUDAGraph:
         """Capture one bucket's step. The capture itself changes no state: every slot in the
         bucket is idle (-1) while capturing, so the captured kernels find no work."""

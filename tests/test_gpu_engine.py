@@ -302,3 +302,18 @@ def test_generate_preempts_when_the_kv_pool_runs_short(small) -> None:
     assert got == expected
     assert tight.state.num_free_blocks() == 20
     model.raise_on_device_error()
+
+
+def test_capture_all_buckets_before_serving(small) -> None:
+    """Every bucket's step graph captured up front (DecodeGraphRunner.capture_all_buckets,
+    cuda_graph_runner.py:93-104): both result buffers per bucket, no capture while serving, and
+    the served tokens equal the eager engine's."""
+    cfg, _, model = small
+    pkg = package()
+    prompts = pkg.make_prompts(6, cfg.vocab_size, length=40, seed=9)
+    eager = _engine(model, 4, False).generate(prompts, 24)
+    eng = _engine(model, 4, True)
+    held = eng.capture_all_buckets()
+    assert held == 2 * len(eng.buckets)
+    assert eng.generate(prompts, 24) == eager
+    assert len(eng._graphs) == held
