@@ -184,35 +184,59 @@ class B200SpeculativeEngine:
         """Load a request into a free slot. ``seed`` keys the request's Philox stream (``draws``:
         the uniforms it already used, for a preempted request that resumes); ``prefix`` (from
         ``add_prefix``) shares the KV blocks of a prompt prefix the request starts with."""
+        return self.add_requests([prompt], [max_new_tokens], ignore_eos=ignore_eos, temperature=temperature,
+                                 top_p=top_p, seeds=[seed], prefix=prefix, draws=[draws])[0]
+
+    def add_requests(self, prompts: list[list[int]], max_new_tokens: list[int], *, ignore_eos: bool = False,
+                     temperature: float = 0.0, top_p: float = 1.0, seeds: list[int] | None = None,
+                     prefix: int | None = None, draws: list[int] | None = None) -> list[int]:
+        """``add_request`` for many requests at once, in order: one host->device copy per field
+        for all of them, and one block-sharing launch per shared-block count."""
+        n = len(prompts)
+        seeds = list(seeds) if seeds is not None else [0] * n
+        draws = list(draws) if draws is not None else [0] * n
+        if len(max_new_tokens) != n or len(seeds) != n or len(draws) != n:
+            raise ValueError("one max_new_tokens, seed and draws value per prompt")
         if temperature != 0.0 and not self.sampling:
             raise ValueError("temperature > 0 needs an engine built with sampling=True")
         if self.draft_state is not None and prefix is not None:
             raise ValueError("draft-model drafts serve requests without shared prefixes")
         if prefix is not None:
             tokens = self._prefixes[prefix][0]
-            if prompt[: len(tokens)] != tokens:
+            if any(p[: len(tokens)] != tokens for p in prompts):
                 raise ValueError("the prompt does not start with the shared prefix")
-        slot = self.state.acquire()
-        self.state.load(slot, prompt, max_new_tokens, ignore_eos=ignore_eos, temperature=temperature,
-                        top_p=top_p, seed=seed, draws=draws)
-        self.h2d_bytes += 4 * len(prompt) + 5 * 4 + 4 + 4 + 8 + 8
-        shared = 0
-        if prefix is not None:
-            # whole blocks only, and at least one prompt token left to prefill (it yields the first token)
-            blocks = min(self._prefixes[prefix][1], (len(prompt) - 1) // 16)
-            self.state.share_blocks(prefix, [slot], blocks)
-            self._prefixes[prefix][2] += 1
-            self._prefix_of[slot] = prefix
-            self._shared_count[slot] = blocks
-            shared = blocks * 16
-        self._uncached[slot] = len(prompt) - shared
+        if n > len(self.state.free_slots):
+            raise RuntimeError("no free sequence slot")
+        for prompt, new in zip(prompts, max_new_tokens):  # (checked before any slot is taken)
+            if len(prompt) == 0 or len(prompt) + new > self.state.max_model_len:
+                raise ValueError(f"prompt of {len(prompt)} + {new} new tokens exceeds max_model_len")
+        slots = [self.state.acquire() for _ in range(n)]
+        self.state.load_many(slots, prompts, list(max_new_tokens), ignore_eos=[ignore_eos] * n,
+                             temperature=[temperature] * n, top_p=[top_p] * n, seed=seeds, draws=draws)
+        per_request = 5 * 4 + 4 + 4 + 8 + 8
+        self.h2d_bytes += sum(4 * len(p) + per_request for p in prompts)
+        groups: dict[int, list[int]] = {}
+        for slot, prompt in zip(slots, prompts):
+            shared = 0
+            if prefix is not None:
+                # whole blocks only, and at least one prompt token left to prefill (it yields the first token)
+                blocks = min(self._prefixes[prefix][1], (len(prompt) - 1) // 16)
+                groups.setdefault(blocks, []).append(slot)
+                self._prefixes[prefix][2] += 1
+                self._prefix_of[slot] = prefix
+                self._shared_count[slot] = blocks
+                shared = blocks * 16
+            self._uncached[slot] = len(prompt) - shared
+        for blocks, group in groups.items():
+            self.state.share_blocks(prefix, group, blocks)
         if self.draft_state is not None:
             # the draft sequence never finishes on its own: it follows the target (ne_draft_sync)
-            self.draft_state.load(slot, prompt, self.state.max_model_len - len(prompt), ignore_eos=True,
-                                  temperature=temperature, top_p=top_p, seed=seed, draws=draws)
-            self.draft_state.max_new_tokens[slot] = 1 << 30
-            self.h2d_bytes += 4 * len(prompt) + 5 * 4 + 4 + 4 + 8 + 8
-        return slot
+            self.draft_state.load_many(slots, prompts, [self.state.max_model_len - len(p) for p in prompts],
+                                       ignore_eos=[True] * n, temperature=[temperature] * n, top_p=[top_p] * n,
+                                       seed=seeds, draws=draws)
+            self.draft_state.max_new_tokens[torch.tensor(slots, device=self.model.device)] = 1 << 30
+            self.h2d_bytes += sum(4 * len(p) + per_request for p in prompts)
+        return slots
 
     def add_prefix(self, tokens: list[int]) -> int:
         """Prefill a prompt prefix once (its own slot holds the blocks); requests that start with it
@@ -492,26 +516,33 @@ class B200SpeculativeEngine:
             self.preemptions += 1
 
         def admit() -> None:
-            admitted = []
-            while pending and self.state.free_slots:
+            batch: list[int] = []
+            added = 0  # blocks the batch's sequences may hold, counted as blocks_bound(k + 1) does
+            free = len(self.state.free_slots)
+            while pending and len(batch) < free:
                 index = pending[0]
                 tokens = tokens_of(index)
                 # the new prefill's blocks and one step of growth for everyone must fit the pool
                 need = -(-(len(tokens) + 1 + k) // bs)
-                if running and blocks_bound(k + 1) + need > self.state.num_blocks:
+                if (running or batch) and blocks_bound(k + 1) + added + need > self.state.num_blocks:
                     break
                 pending.pop(0)
-                left, draws = (resume[index][1], resume[index][2]) if index in resume else (max_new_tokens, 0)
-                slot = self.add_request(tokens, left, ignore_eos=ignore_eos, temperature=temperature, top_p=top_p,
-                                        seed=seeds[index] if seeds is not None else index, prefix=prefix,
-                                        draws=draws)
+                batch.append(index)
+                shared = min(self._prefixes[prefix][1], (len(tokens) - 1) // 16) if prefix is not None else 0
+                added += max(0, -(-(len(tokens) + (k + 1) + k) // bs) - shared)
+            if not batch:
+                return
+            slots = self.add_requests(
+                [tokens_of(i) for i in batch], [resume[i][1] if i in resume else max_new_tokens for i in batch],
+                ignore_eos=ignore_eos, temperature=temperature, top_p=top_p,
+                seeds=[seeds[i] if seeds is not None else i for i in batch], prefix=prefix,
+                draws=[resume[i][2] if i in resume else 0 for i in batch])
+            for slot, index in zip(slots, batch):
                 running[slot] = index
                 order[slot] = admitted_total[0]
                 admitted_total[0] += 1
-                admitted.append(slot)
-            if admitted:
-                res = self.prefill(admitted, chunk=prefill_chunk)
-                self._absorb(res, running, outputs)
+            res = self.prefill(slots, chunk=prefill_chunk)
+            self._absorb(res, running, outputs)
 
         def make_room(extra: int) -> None:
             while len(running) > 1 and blocks_bound(extra) > self.state.num_blocks:

@@ -97,23 +97,47 @@ class DeviceBatchState:
     def load(self, slot: int, prompt: list[int], max_new_tokens: int, *, ignore_eos: bool = False,
              temperature: float = 0.0, top_p: float = 1.0, seed: int = 0, draws: int = 0) -> None:
         """Copy one request into sequence slot ``slot`` (Sequence.from_request)."""
-        if len(prompt) == 0 or len(prompt) + max_new_tokens > self.max_model_len:
-            raise ValueError(f"prompt of {len(prompt)} + {max_new_tokens} new tokens exceeds max_model_len")
-        check_sampling(temperature, top_p)
-        L = len(prompt)
-        self.history[slot, :L].copy_(torch.tensor(prompt, dtype=torch.int32), non_blocking=False)
-        scalars = torch.tensor([L, 0, L, max_new_tokens, _lib.NE_SEQ_IGNORE_EOS if ignore_eos else 0],
-                               dtype=torch.int32)
-        vals = scalars.to(self.device)
-        self.seq_len[slot] = vals[0]
-        self.num_cached[slot] = vals[1]
-        self.num_prompt[slot] = vals[2]
-        self.max_new_tokens[slot] = vals[3]
-        self.flags[slot] = vals[4]
-        self.temperature[slot] = float(temperature)
-        self.top_p[slot] = float(top_p)
-        self.rng_seed[slot] = seed_as_int64(seed)
-        self.rng_draws[slot] = int(draws)
+        self.load_many([slot], [prompt], [max_new_tokens], ignore_eos=[ignore_eos], temperature=[temperature],
+                       top_p=[top_p], seed=[seed], draws=[draws])
+
+    def load_many(self, slots: list[int], prompts: list[list[int]], max_new_tokens: list[int], *,
+                  ignore_eos: list[bool], temperature: list[float], top_p: list[float], seed: list[int],
+                  draws: list[int]) -> None:
+        """Copy requests into their slots (Sequence.from_request for each): the prompts as one
+        padded block and every per-sequence field as one vector, each a single host->device copy
+        from pinned memory scattered by slot index."""
+        n = len(slots)
+        for prompt, new in zip(prompts, max_new_tokens):
+            if len(prompt) == 0 or len(prompt) + new > self.max_model_len:
+                raise ValueError(f"prompt of {len(prompt)} + {new} new tokens exceeds max_model_len")
+        for t, p in zip(temperature, top_p):
+            check_sampling(t, p)
+        width = max(len(p) for p in prompts)
+        block = torch.zeros((n, width), dtype=torch.int32, pin_memory=True)
+        for i, prompt in enumerate(prompts):
+            block[i, : len(prompt)] = torch.tensor(prompt, dtype=torch.int32)
+        lens = [len(p) for p in prompts]
+        ints = torch.tensor([lens, [0] * n, lens, list(max_new_tokens),
+                             [_lib.NE_SEQ_IGNORE_EOS if e else 0 for e in ignore_eos]], dtype=torch.int32).pin_memory()
+        floats = torch.tensor([list(temperature), list(top_p)], dtype=torch.float32).pin_memory()
+        longs = torch.tensor([[seed_as_int64(v) for v in seed], [int(v) for v in draws]], dtype=torch.int64).pin_memory()
+        idx = torch.tensor(slots, dtype=torch.long).pin_memory().to(self.device, non_blocking=True)
+        dev_block = block.to(self.device, non_blocking=True)
+        self.history[idx, :width] = dev_block
+        i_dev = ints.to(self.device, non_blocking=True)
+        self.seq_len[idx] = i_dev[0]
+        self.num_cached[idx] = i_dev[1]
+        self.num_prompt[idx] = i_dev[2]
+        self.max_new_tokens[idx] = i_dev[3]
+        self.flags[idx] = i_dev[4]
+        f_dev = floats.to(self.device, non_blocking=True)
+        self.temperature[idx] = f_dev[0]
+        self.top_p[idx] = f_dev[1]
+        l_dev = longs.to(self.device, non_blocking=True)
+        self.rng_seed[idx] = l_dev[0]
+        self.rng_draws[idx] = l_dev[1]
+        # the pinned sources must outlive the asynchronous copies
+        self._pinned = (block, ints, floats, longs)
 
     def acquire(self) -> int:
         if not self.free_slots:
