@@ -28,6 +28,9 @@ constexpr int D = 128;
 constexpr int ROW_BYTES = D * 2 + 16;            // padded smem row: conflict-free ldmatrix
 constexpr int BLOCK_BYTES = 16 * ROW_BYTES;      // one 16-token K (or V) block in smem
 constexpr int THREADS = 128;
+// Blocks per softmax update in the many-tile (prefill) path. Measured on B200 (config 4's prefill
+// of 259K prompt tokens, attention share): 1 block 765 ms, 2 668 ms, 3 666 ms, 4 742 ms (spills).
+constexpr int CHUNK_BLOCKS = 3;
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float SCALE_LOG2 = 0.08838834764831845f * LOG2E;  // 1/sqrt(128) folded into exp2
 #define NEG_INF (-__int_as_float(0x7f800000))
@@ -327,6 +330,94 @@ __device__ __forceinline__ void tile_block(TileState& ts, uint32_t k_s, uint32_t
   }
 }
 
+// Up to NB consecutive blocks (logical kb .. kb + NB - 1; bit i of ``valid``: block kb + i is
+// staged, K at k_s + i * BLOCK_BYTES, V at v_s + i * BLOCK_BYTES) against the tile with one
+// online-softmax update for their keys: S for every block, one max and rescale, then P V block by
+// block. Blocks that are not staged are skipped, so no stale shared memory reaches P V.
+template <int NB>
+__device__ __forceinline__ void tile_chunk(TileState& ts, uint32_t k_s, uint32_t v_s, int kb, unsigned valid,
+                                           int lane) {
+  float s[NB][2][4];
+  float mx[2] = {NEG_INF, NEG_INF};
+#pragma unroll
+  for (int i = 0; i < NB; ++i) {
+    if (!(valid >> i & 1u)) continue;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      s[i][j][0] = s[i][j][1] = s[i][j][2] = s[i][j][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 8; kk += 2) {
+        uint32_t b[4];
+        const int tok = 8 * j + (lane & 7);
+        const int col = 16 * kk + 8 * (lane >> 3);
+        ldsm_x4(b, k_s + i * BLOCK_BYTES + tok * ROW_BYTES + col * 2);
+        mma16816(s[i][j], ts.qa[kk], b[0], b[1]);
+        mma16816(s[i][j], ts.qa[kk + 1], b[2], b[3]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = e >> 1;
+        const int key = (kb + i) * 16 + 8 * j + 2 * (lane & 3) + (e & 1);
+        float v = s[i][j][e] * SCALE_LOG2;
+        if (key > ts.pos[r]) v = NEG_INF;
+        s[i][j][e] = v;
+        mx[r] = fmaxf(mx[r], v);
+      }
+    }
+  }
+  float corr[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xFFFFFFFFu, mx[r], 1));
+    mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xFFFFFFFFu, mx[r], 2));
+    const float m_new = fmaxf(ts.m[r], mx[r]);
+    corr[r] = (m_new == NEG_INF || ts.m[r] == NEG_INF) ? (m_new == NEG_INF ? 1.f : 0.f) : exp2f(ts.m[r] - m_new);
+    ts.m[r] = m_new;
+  }
+  if (__any_sync(0xFFFFFFFFu, corr[0] != 1.f || corr[1] != 1.f)) {
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      ts.o[t][0] *= corr[0];
+      ts.o[t][1] *= corr[0];
+      ts.o[t][2] *= corr[1];
+      ts.o[t][3] *= corr[1];
+    }
+  }
+  float psum[2] = {0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < NB; ++i) {
+    if (!(valid >> i & 1u)) continue;
+    uint32_t pa[4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float p[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = e >> 1;
+        p[e] = (s[i][j][e] == NEG_INF) ? 0.f : exp2f(s[i][j][e] - ts.m[r]);
+        psum[r] += p[e];
+      }
+      pa[2 * j] = pack_bf16(p[0], p[1]);
+      pa[2 * j + 1] = pack_bf16(p[2], p[3]);
+    }
+#pragma unroll
+    for (int t = 0; t < 16; t += 2) {
+      uint32_t b[4];
+      const int tok = (lane & 7) + 8 * ((lane >> 3) & 1);
+      const int col = 8 * t + 8 * (lane >> 4);
+      ldsm_x4_t(b, v_s + i * BLOCK_BYTES + tok * ROW_BYTES + col * 2);
+      mma16816(ts.o[t], pa, b[0], b[1]);
+      mma16816(ts.o[t + 1], pa, b[2], b[3]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    psum[r] += __shfl_xor_sync(0xFFFFFFFFu, psum[r], 1);
+    psum[r] += __shfl_xor_sync(0xFFFFFFFFu, psum[r], 2);
+    ts.l[r] = ts.l[r] * corr[r] + psum[r];
+  }
+}
+
 // Write a finished tile: normalised bf16 output (one split) or the unnormalised partial.
 __device__ __forceinline__ void tile_store(const Ctx& c, const AttnSplit& sp, const TileState& ts, int v0, int lane,
                                            int b, int split) {
@@ -592,16 +683,35 @@ __global__ void __launch_bounds__(32 * NW, NW == 4 ? 3 : 5)
     warp_split_tiles<INT8, 2, 4>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv);
   } else {
     // ---------------------------------------------------------------- many tiles, shared blocks
+    // Four query tiles at a time (one per warp) against the split's blocks CH at a time: the CTA
+    // stages a chunk of up to CH K and CH V blocks (two stages of 2 CH x BLOCK_BYTES); the query
+    // tiles pass through stage 1 before the first prefetch into it.
+    constexpr int CH = CHUNK_BLOCKS;
+    const int stride = rows.block_table_stride;
+    const uint32_t st0 = buf_u, st1 = buf_u + 2 * CH * BLOCK_BYTES;
+    __shared__ int tpos[4][16];
     for (int t0 = 0; t0 < ntiles; t0 += 4) {
       const int tile = t0 + warp;
       __syncthreads();
-      // each warp stages its own query tile into its slot of the Q area (4 tiles)
-      uint8_t* my_q = buf + 4 * BLOCK_BYTES + warp * BLOCK_BYTES;
-      int* my_pos = spos;  // not used for positions here
-      (void)my_pos;
+      // the last query row of this tile group bounds the blocks it needs
+      const int v_last = min(c.nvec, (t0 + 4) * 16) - 1;
+      const int grp_end = min(kb1, (rows.positions[c.r0 + v_last / c.G]) / 16 + 1);
+      // blocks kbc .. kbc + CH - 1 into stage ``dst`` (every thread computes the same ids); the valid ones
+      auto stage_chunk = [&](int kbc, uint32_t dst) -> unsigned {
+        unsigned valid = 0;
+        for (int i = 0; i < CH && kbc + i < grp_end; ++i) {
+          const long long blk = block_id(c, kbc + i, stride);
+          if (blk < 0) continue;
+          stage_block<INT8>(c, blk, dst + i * BLOCK_BYTES, dst + (CH + i) * BLOCK_BYTES, tid, THREADS);
+          valid |= 1u << i;
+        }
+        return valid;
+      };
+      unsigned cur_valid = kb0 < grp_end ? stage_chunk(kb0, st0) : 0u;
+      cp_commit();
+      // each warp stages its own query tile into its slot of stage 1 and takes its fragments
+      uint8_t* my_q = buf + 2 * CH * BLOCK_BYTES + warp * BLOCK_BYTES;
       if (tile < ntiles) load_q_tile(c, tile * 16, my_q, lane, 32);
-      __syncwarp();
-      __shared__ int tpos[4][16];
       if (lane < 16) {
         const int v = tile * 16 + lane;
         tpos[warp][lane] = (tile < ntiles && v < c.nvec) ? rows.positions[c.r0 + v / c.G] : -1;
@@ -609,24 +719,17 @@ __global__ void __launch_bounds__(32 * NW, NW == 4 ? 3 : 5)
       __syncwarp();
       TileState ts;
       if (tile < ntiles) tile_init(ts, smem_u32(my_q), tpos[warp], lane);
-      // the last query row of this tile group bounds the blocks it needs
-      const int v_last = min(c.nvec, (t0 + 4) * 16) - 1;
-      const int grp_end = min(kb1, (rows.positions[c.r0 + v_last / c.G]) / 16 + 1);
-      long long blk = kb0 < grp_end ? block_id(c, kb0, rows.block_table_stride) : -1;
-      if (blk >= 0) stage_block<INT8>(c, blk, buf_u, buf_u + BLOCK_BYTES, tid, THREADS);
-      cp_commit();
+      __syncthreads();  // every warp holds its fragments: stage 1 may take the next chunk
       int stage = 0;
-      for (int kb = kb0; kb < grp_end; ++kb) {
-        long long nb = kb + 1 < grp_end ? block_id(c, kb + 1, rows.block_table_stride) : -1;
-        const uint32_t nxt = buf_u + (stage ^ 1) * 2 * BLOCK_BYTES;
-        if (nb >= 0) stage_block<INT8>(c, nb, nxt, nxt + BLOCK_BYTES, tid, THREADS);
+      for (int kb = kb0; kb < grp_end; kb += CH) {
+        const unsigned nxt_valid = kb + CH < grp_end ? stage_chunk(kb + CH, stage ? st0 : st1) : 0u;
         cp_commit();
         cp_wait<1>();
         __syncthreads();
-        const uint32_t cur = buf_u + stage * 2 * BLOCK_BYTES;
-        if (tile < ntiles && blk >= 0) tile_block(ts, cur, cur + BLOCK_BYTES, kb, lane);
+        const uint32_t cur = stage ? st1 : st0;
+        if (tile < ntiles && cur_valid) tile_chunk<CH>(ts, cur, cur + CH * BLOCK_BYTES, kb, cur_valid, lane);
         __syncthreads();
-        blk = nb;
+        cur_valid = nxt_valid;
         stage ^= 1;
       }
       cp_wait<0>();
