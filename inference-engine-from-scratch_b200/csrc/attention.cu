@@ -31,6 +31,9 @@ constexpr int THREADS = 128;
 // Blocks per softmax update in the many-tile (prefill) path. Measured on B200 (config 4's prefill
 // of 259K prompt tokens, attention share): 1 block 765 ms, 2 668 ms, 3 666 ms, 4 742 ms (spills).
 constexpr int CHUNK_BLOCKS = 3;
+// The eight-warp prefill kernel (up to 255 registers, one CTA per SM) takes six blocks per update
+// without spilling: 466 / 440 / 422 ms of attention for 3 / 4 / 6 blocks on the same prefill.
+constexpr int CHUNK_BLOCKS_8 = 6;
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float SCALE_LOG2 = 0.08838834764831845f * LOG2E;  // 1/sqrt(128) folded into exp2
 #define NEG_INF (-__int_as_float(0x7f800000))
@@ -630,7 +633,7 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
 // NW warps per CTA: 4 (three CTAs per SM, registers <= 168; every path), or 2 (one query tile
 // only: five CTAs per SM, so that a speculative step's (entry, KV head) pairs fit in one wave).
 template <bool INT8, int NW>
-__global__ void __launch_bounds__(32 * NW, NW == 4 ? 3 : 5)
+__global__ void __launch_bounds__(32 * NW, NW == 8 ? 1 : NW == 4 ? 3 : 5)
     attention_kernel(const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out, const void* __restrict__ kc,
                      const void* __restrict__ vc, const __nv_bfloat16* __restrict__ ks,
                      const __nv_bfloat16* __restrict__ vs, ne_rows rows, int nh, int nkv, long long num_cache_slots,
@@ -672,29 +675,37 @@ __global__ void __launch_bounds__(32 * NW, NW == 4 ? 3 : 5)
   uint8_t* buf = smem + BLOCK_BYTES + 256;               // K/V stages
   const uint32_t buf_u = smem_u32(buf);
 
-  if (slots > 1) {
-    if (tile < ntiles)
-      warp_split_tiles<INT8, 1, NW>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 16 * tile);
-  } else if (ntiles == 1) {
-    warp_split_tiles<INT8, 1, NW>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv);
-  } else if (NW != 4) {
-    report(status, NE_DEV_BAD_SLOT);  // the host launches the 2-warp kernel only for one-tile CTAs
-  } else if (ntiles == 2) {
-    warp_split_tiles<INT8, 2, 4>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv);
-  } else {
+  bool shared_blocks = NW == 8;  // the 8-warp kernel (prefill) takes every entry that way
+  if constexpr (NW != 8) {
+    if (slots > 1) {
+      if (tile < ntiles)
+        warp_split_tiles<INT8, 1, NW>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 16 * tile);
+    } else if (ntiles == 1) {
+      warp_split_tiles<INT8, 1, NW>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv);
+    } else if (NW != 4) {
+      report(status, NE_DEV_BAD_SLOT);  // the host launches the 2-warp kernel only for one-tile CTAs
+    } else if (ntiles == 2) {
+      warp_split_tiles<INT8, 2, 4>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv);
+    } else {
+      shared_blocks = true;
+    }
+  }
+  if (shared_blocks) {
     // ---------------------------------------------------------------- many tiles, shared blocks
-    // Four query tiles at a time (one per warp) against the split's blocks CH at a time: the CTA
+    // NW query tiles at a time (one per warp) against the split's blocks CH at a time: the CTA
     // stages a chunk of up to CH K and CH V blocks (two stages of 2 CH x BLOCK_BYTES); the query
-    // tiles pass through stage 1 before the first prefetch into it.
-    constexpr int CH = CHUNK_BLOCKS;
+    // tiles pass through stage 1 before the first prefetch into it (four warps) or sit behind the
+    // stages (eight).
+    constexpr int CH = NW == 8 ? CHUNK_BLOCKS_8 : CHUNK_BLOCKS;
     const int stride = rows.block_table_stride;
     const uint32_t st0 = buf_u, st1 = buf_u + 2 * CH * BLOCK_BYTES;
-    __shared__ int tpos[4][16];
-    for (int t0 = 0; t0 < ntiles; t0 += 4) {
+    __shared__ int tpos[NW][16];
+    const uint32_t q_area = NW * BLOCK_BYTES <= 2 * CH * BLOCK_BYTES ? st1 : buf_u + 4 * CH * BLOCK_BYTES;
+    for (int t0 = 0; t0 < ntiles; t0 += NW) {
       const int tile = t0 + warp;
       __syncthreads();
       // the last query row of this tile group bounds the blocks it needs
-      const int v_last = min(c.nvec, (t0 + 4) * 16) - 1;
+      const int v_last = min(c.nvec, (t0 + NW) * 16) - 1;
       const int grp_end = min(kb1, (rows.positions[c.r0 + v_last / c.G]) / 16 + 1);
       // blocks kbc .. kbc + CH - 1 into stage ``dst`` (every thread computes the same ids); the valid ones
       auto stage_chunk = [&](int kbc, uint32_t dst) -> unsigned {
@@ -702,15 +713,15 @@ __global__ void __launch_bounds__(32 * NW, NW == 4 ? 3 : 5)
         for (int i = 0; i < CH && kbc + i < grp_end; ++i) {
           const long long blk = block_id(c, kbc + i, stride);
           if (blk < 0) continue;
-          stage_block<INT8>(c, blk, dst + i * BLOCK_BYTES, dst + (CH + i) * BLOCK_BYTES, tid, THREADS);
+          stage_block<INT8>(c, blk, dst + i * BLOCK_BYTES, dst + (CH + i) * BLOCK_BYTES, tid, 32 * NW);
           valid |= 1u << i;
         }
         return valid;
       };
       unsigned cur_valid = kb0 < grp_end ? stage_chunk(kb0, st0) : 0u;
       cp_commit();
-      // each warp stages its own query tile into its slot of stage 1 and takes its fragments
-      uint8_t* my_q = buf + 2 * CH * BLOCK_BYTES + warp * BLOCK_BYTES;
+      // each warp stages its own query tile into its slot of the Q area and takes its fragments
+      uint8_t* my_q = buf + (q_area - buf_u) + warp * BLOCK_BYTES;
       if (tile < ntiles) load_q_tile(c, tile * 16, my_q, lane, 32);
       if (lane < 16) {
         const int v = tile * 16 + lane;
@@ -827,6 +838,8 @@ __global__ void kv_shadow_map_kernel(const int32_t* __restrict__ table, int num_
 
 size_t attention_smem_bytes_nw(int nw) {
   if (nw == 4) return attention_smem_bytes();
+  // eight warps (prefill only): two stages of CHUNK_BLOCKS (K, V) blocks + eight Q tiles behind them
+  if (nw == 8) return BLOCK_BYTES + 256 + (size_t)(4 * CHUNK_BLOCKS_8 + 8) * BLOCK_BYTES;
   // Q tile + positions + max(nw warps x 2 stages x (K, V) blocks, the merge area)
   const size_t stages = (size_t)nw * 4 * BLOCK_BYTES;
   const size_t merge = ((size_t)nw * 16 * D + 2 * nw * 16) * sizeof(float);
@@ -892,13 +905,22 @@ int launch_attention_tc(const __nv_bfloat16* q, __nv_bfloat16* out, const void* 
     return !(e && e[0] == '0');
   }();
   const int tile_slots = (tile_ctas && max_vec > 16 && max_vec <= 32) ? 2 : 1;
-  // two warps (five CTAs per SM) when one-tile CTAs would spill into a second wave of four-warp CTAs
-  const int nw = ((max_vec <= 16 || tile_slots > 1) && ctas <= 5LL * sms && ctas > 3LL * sms) ? 2 : 4;
+  // two warps (five CTAs per SM) when one-tile CTAs would spill into a second wave of four-warp CTAs;
+  // eight warps for prefill rows (more than two tiles): each staged block serves twice the queries
+  // (NE_ATTN_PREFILL_WARPS=4: the four-warp kernel)
+  static const int prefill_warps = [] {
+    const char* e = getenv("NE_ATTN_PREFILL_WARPS");
+    return e && e[0] == '4' ? 4 : 8;
+  }();
+  const int nw = max_vec > 32 && tile_slots == 1 ? prefill_warps
+                 : ((max_vec <= 16 || tile_slots > 1) && ctas <= 5LL * sms && ctas > 3LL * sms) ? 2 : 4;
   const size_t smem = attention_smem_bytes_nw(nw);
-  static bool attr_set[4] = {false, false, false, false};
-  auto kernel = kv_int8 ? (nw == 2 ? attention_kernel<true, 2> : attention_kernel<true, 4>)
-                        : (nw == 2 ? attention_kernel<false, 2> : attention_kernel<false, 4>);
-  const int ai = (kv_int8 ? 2 : 0) + (nw == 2 ? 1 : 0);
+  static bool attr_set[6] = {false, false, false, false, false, false};
+  auto kernel = kv_int8 ? (nw == 2 ? attention_kernel<true, 2> : nw == 8 ? attention_kernel<true, 8>
+                                                                          : attention_kernel<true, 4>)
+                        : (nw == 2 ? attention_kernel<false, 2> : nw == 8 ? attention_kernel<false, 8>
+                                                                           : attention_kernel<false, 4>);
+  const int ai = (kv_int8 ? 3 : 0) + (nw == 2 ? 1 : nw == 8 ? 2 : 0);
   if (!attr_set[ai]) {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return NE_ERR_CUDA;

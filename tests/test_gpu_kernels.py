@@ -93,15 +93,17 @@ def test_gemm_is_deterministic(lib, cuda_device) -> None:
 
 @pytest.mark.parametrize("rows,hidden", [(1, 1024), (37, 1024), (320, 256), (5, 4096)])
 def test_rmsnorm_matches_reference_arithmetic(lib, cuda_device, rows, hidden) -> None:
-    x = torch.randn(rows, hidden).to(torch.bfloat16)
-    w = (1 + 0.1 * torch.randn(hidden)).to(torch.bfloat16)
+    g = torch.Generator().manual_seed(rows * hidden)
+    x = torch.randn(rows, hidden, generator=g).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(hidden, generator=g)).to(torch.bfloat16)
     y = torch.empty(rows, hidden, dtype=torch.bfloat16, device=cuda_device)
     assert lib.ne_rmsnorm(x.to(cuda_device).data_ptr(), w.to(cuda_device).data_ptr(), y.data_ptr(), rows, hidden,
                           1e-6, _stream()) == 0
     want = oq.rms_norm(x, w, 1e-6)
     got = y.cpu()
-    # the only freedom is the fp32 summation order of mean(x^2): at most one bf16 step apart
-    torch.testing.assert_close(got.float(), want.float(), rtol=8e-3, atol=1e-3)
+    # the only freedom is the fp32 summation order of mean(x^2): bf16(x * r) at most one bf16 step
+    # apart, which the rounded product with the weight can widen to two steps of the output
+    torch.testing.assert_close(got.float(), want.float(), rtol=1.6e-2, atol=1e-3)
     assert (got == want).float().mean() > 0.99
 
 
