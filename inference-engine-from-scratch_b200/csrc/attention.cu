@@ -640,8 +640,9 @@ __global__ void __launch_bounds__(32 * NW, NW == 8 ? 1 : NW == 4 ? 3 : 5)
                      AttnSplit sp, int* status, KvShadow shadow) {
   pdl_prologue();
   extern __shared__ __align__(16) uint8_t smem[];
-  // z = split * tile slots + tile: with more than one tile slot, CTA (b, h, z) serves query tile
-  // z % slots of the entry alone (an entry with fewer tiles leaves the CTA idle)
+  // z = split * slots + slot: with more than one slot, CTA (b, h, z) serves query tile z % slots
+  // of the entry alone (eight warps: query group z % slots, eight tiles); an entry with fewer
+  // tiles leaves the CTA idle
   const int slots = gridDim.z / sp.splits;
   const int b = blockIdx.x, h = blockIdx.y, split = blockIdx.z / slots, tile = blockIdx.z % slots;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -701,7 +702,10 @@ __global__ void __launch_bounds__(32 * NW, NW == 8 ? 1 : NW == 4 ? 3 : 5)
     const uint32_t st0 = buf_u, st1 = buf_u + 2 * CH * BLOCK_BYTES;
     __shared__ int tpos[NW][16];
     const uint32_t q_area = NW * BLOCK_BYTES <= 2 * CH * BLOCK_BYTES ? st1 : buf_u + 4 * CH * BLOCK_BYTES;
-    for (int t0 = 0; t0 < ntiles; t0 += NW) {
+    // with more than one slot (eight warps), CTA z % slots takes query group z % slots alone
+    const int t_first = slots > 1 ? tile * NW : 0;
+    const int t_end = slots > 1 ? min(ntiles, t_first + NW) : ntiles;
+    for (int t0 = t_first; t0 < t_end; t0 += NW) {
       const int tile = t0 + warp;
       __syncthreads();
       // the last query row of this tile group bounds the blocks it needs
@@ -932,7 +936,10 @@ int launch_attention_tc(const __nv_bfloat16* q, __nv_bfloat16* out, const void* 
     if (launch_kernel(clear_partials_kernel, dim3(blocks), dim3(256), 0, stream, sp, n) != cudaSuccess)
       return NE_ERR_CUDA;
   }
-  dim3 grid(rows.num_seqs, num_kv_heads, sp.splits * tile_slots);
+  // eight-warp prefill: one CTA per group of eight query tiles (groups are independent outputs),
+  // so that a long chunk's groups run side by side instead of one after another in one CTA
+  const int group_slots = nw == 8 ? std::min(1024, (max_vec + 127) / 128) : 1;
+  dim3 grid(rows.num_seqs, num_kv_heads, sp.splits * tile_slots * group_slots);
   if (shadow.map && (!kv_int8 || !shadow.k || !shadow.v || shadow.blocks < 1)) return NE_ERR_INVALID;
   if (launch_kernel(kernel, grid, dim3(32 * nw), smem, stream, q, out, k_cache, v_cache, k_scale, v_scale, rows,
                     num_heads, num_kv_heads, num_cache_slots, sp, status, shadow) != cudaSuccess)
