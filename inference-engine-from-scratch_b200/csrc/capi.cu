@@ -858,7 +858,10 @@ int ne_prefill(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, i
                 ne::launch_plan(*st, seq_slot, num_seqs, ne::PLAN_PREFILL, max_rows, chunk, m->cfg.block_size,
                                 m->cfg.num_cache_slots, m->rb, m->status, s), s);
   if (rc) return rc;
-  ne_rows rows = make_step_rows(m, st, seq_slot, num_seqs, max_rows, num_seqs, max_rows);
+  // a sequence takes at most ``chunk`` rows of a chunked call: the attention sizes its query-tile
+  // grid by that bound
+  const int q_bound = chunk > 0 ? std::min(max_rows, chunk) : max_rows;
+  ne_rows rows = make_step_rows(m, st, seq_slot, num_seqs, max_rows, num_seqs, q_bound);
   if (m->sample_logits) {
     if (num_seqs > m->sample_rows) return NE_ERR_WORKSPACE;
     return sampled_tail(m, st, seq_slot, num_seqs, k, rows, false, out, s);

@@ -348,7 +348,8 @@ class B200SpeculativeEngine:
                 rows += r
             if rows > self.max_prefill_rows:
                 raise ValueError(f"a prefill call of {rows} rows exceeds the workspace; use chunk=")
-            res = self._prefill_call(group, rows, chunk or 0)
+            # (without chunking, the group's longest take bounds every sequence's rows the same way)
+            res = self._prefill_call(group, rows, chunk or max(take.values()))
             for s in group:
                 remaining[s] -= take[s]
                 if remaining[s] == 0:
