@@ -1009,6 +1009,13 @@ int plan_uncached(GemmParams& p, int num_sms) {
     static const int lm_cap = getenv("NE_LM_MAX_STAGES") ? env_cap("NE_LM_MAX_STAGES", GEMM_MAX_STAGES) : 2;
     stages = std::min(stages, lm_cap);
   }
+  if (p.epi.mode == EPI_SWIGLU && p.M_max > 512 && p.rows_hint == 0) {
+    // a prefill-sized gate/up GEMM (many waves of 256-token blocks): two stages let two CTAs share
+    // an SM, one streaming while the other runs its SwiGLU epilogue. Measured on config 4's prefill:
+    // gate/up 155 -> 105 ms; the other epilogues lost with two stages (QKV 194 -> 203, o_proj
+    // 47 -> 60, down_proj 60 -> 81 ms), so they keep the deep pipeline.
+    stages = std::min(stages, 2);
+  }
   if (stages < 1) return NE_ERR_INVALID;
   const int staging = staging_bytes(S, t_block);
   int data = std::max(stages * stage_bytes, staging);
