@@ -473,6 +473,43 @@ __device__ __forceinline__ float chunk_value(const __nv_bfloat16* row, int i, bo
   return v;
 }
 
+// chunk_value of a logit already loaded (``x``: row[i], any value when i is out of range).
+__device__ __forceinline__ float chunk_value_of(__nv_bfloat16 x, bool in_range, float T, const SampleStats& s,
+                                                uint32_t& rank) {
+  float p = 0.f;
+  if (in_range) p = prob(__bfloat162float(x) / T, s.m, s.z);
+  const bool tie = in_range && s.top_p_active && p == s.tau;
+  const uint32_t tmask = __ballot_sync(FULL, tie);
+  const int lane = threadIdx.x & 31;
+  const float v = in_range ? kept_p(p, s, (int)(rank + __popc(tmask & ((1u << lane) - 1u)))) : 0.f;
+  rank += __popc(tmask);
+  return v;
+}
+
+// Visit a warp's range [begin, end) 32 tokens at a time, in index order, calling
+// f(base, i = base + lane, row[i]) (warp-collective; f returns false to stop). The logits of
+// CHUNKS_AHEAD chunks are loaded before the first of them is used, so their loads overlap.
+// (measured on config 4's acceptance: 4 chunks 0.42 ms, 8 0.43 ms, 16 0.47 ms; 1 chunk 0.49 ms)
+constexpr int CHUNKS_AHEAD = 4;
+template <typename F>
+__device__ __forceinline__ void for_each_chunk(const __nv_bfloat16* row, int begin, int end, F&& f) {
+  const int lane = threadIdx.x & 31;
+  for (int base = begin; base < end; base += 32 * CHUNKS_AHEAD) {
+    __nv_bfloat16 x[CHUNKS_AHEAD];
+#pragma unroll
+    for (int u = 0; u < CHUNKS_AHEAD; ++u) {
+      const int i = base + 32 * u + lane;
+      x[u] = i < end ? row[i] : __float2bfloat16_rn(0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < CHUNKS_AHEAD; ++u) {
+      const int b = base + 32 * u;
+      if (b >= end) return;  // warp-uniform
+      if (!f(b, b + lane, x[u])) return;
+    }
+  }
+}
+
 // Draw from row ``row``'s target distribution with token ``exclude`` (>= 0) removed and the rest
 // renormalised (the rejection residual), using uniform u = u24 * 2^-24.
 __device__ int draw_token(const __nv_bfloat16* row, int vocab, float T, const SampleStats& s, int exclude,
@@ -483,11 +520,11 @@ __device__ int draw_token(const __nv_bfloat16* row, int vocab, float T, const Sa
   // tie counts per range (only when the cut splits a tie group), exclusive prefix over ranges
   uint32_t ties = 0;
   if (partial_ties(s)) {
-    for (int base = begin; base < end; base += 32) {
-      const int i = base + lane;
-      const bool tie = i < end && prob(scaled(row, i, T), s.m, s.z) == s.tau;
+    for_each_chunk(row, begin, end, [&](int, int i, __nv_bfloat16 x) {
+      const bool tie = i < end && prob(__bfloat162float(x) / T, s.m, s.z) == s.tau;
       ties += __popc(__ballot_sync(FULL, tie));
-    }
+      return true;
+    });
   }
   if (lane == 0) sh.warp_ties[warp] = ties;
   __syncthreads();
@@ -497,12 +534,12 @@ __device__ int draw_token(const __nv_bfloat16* row, int vocab, float T, const Sa
   unsigned long long sum = 0, ex = 0;
   {
     uint32_t rank = tie_base;
-    for (int base = begin; base < end; base += 32) {
-      const int i = base + lane;
-      const unsigned long long f = to_fix(chunk_value(row, i, i < end, T, s, rank));
+    for_each_chunk(row, begin, end, [&](int, int i, __nv_bfloat16 x) {
+      const unsigned long long f = to_fix(chunk_value_of(x, i < end, T, s, rank));
       sum += f;
       if (i == exclude) ex = f;
-    }
+      return true;
+    });
   }
   sum = warp_sum_u64(sum);
   ex = warp_sum_u64(ex);
@@ -531,11 +568,11 @@ __device__ int draw_token(const __nv_bfloat16* row, int vocab, float T, const Sa
   if (renorm) {  // pass 2: per-range sums of the renormalised residual
     sum = 0;
     uint32_t rank = tie_base;
-    for (int base = begin; base < end; base += 32) {
-      const int i = base + lane;
-      const float v = chunk_value(row, i, i < end, T, s, rank);
+    for_each_chunk(row, begin, end, [&](int, int i, __nv_bfloat16 x) {
+      const float v = chunk_value_of(x, i < end, T, s, rank);
       sum += i == exclude ? 0ull : to_fix(v / norm);
-    }
+      return true;
+    });
     sum = warp_sum_u64(sum);
     if (lane == 0) sh.warp_sum[warp] = sum;
     __syncthreads();
@@ -560,19 +597,19 @@ __device__ int draw_token(const __nv_bfloat16* row, int vocab, float T, const Sa
   if (warp == owner) {
     unsigned long long run = before;
     uint32_t rank = tie_base;
-    for (int base = begin; base < end; base += 32) {
-      const int i = base + lane;
-      float v = chunk_value(row, i, i < end, T, s, rank);
+    for_each_chunk(row, begin, end, [&](int base, int i, __nv_bfloat16 x) {
+      float v = chunk_value_of(x, i < end, T, s, rank);
       if (i == exclude) v = 0.f;
       const unsigned long long f = renorm ? to_fix(v / norm) : to_fix(v);
       const unsigned long long incl = run + warp_incl_scan_u64(f, lane);
       const uint32_t hit = __ballot_sync(FULL, i < end && incl > target);
       if (hit) {
         if (lane == 0) sh.result = base + __ffs(hit) - 1;
-        break;
+        return false;
       }
       run = __shfl_sync(FULL, incl, 31);
-    }
+      return true;
+    });
   }
   __syncthreads();
   const int tok = sh.result;
