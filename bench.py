@@ -446,8 +446,8 @@ def run_b200(args, dist: Dist) -> None:
 
     # ------------------------------------------------------------ steady state (value)
     prefix = engine.add_prefix(prompts[0][: wl.shared_prefix]) if wl.shared_prefix else None
-    slots = [engine.add_request(p, steady_new, ignore_eos=True, temperature=wl.temperature, top_p=wl.top_p,
-                                seed=i, prefix=prefix) for i, p in enumerate(prompts)]
+    slots = engine.add_requests(prompts, [steady_new] * len(prompts), ignore_eos=True, temperature=wl.temperature,
+                                top_p=wl.top_p, seeds=list(range(len(prompts))), prefix=prefix)
     engine.prefill(slots, chunk=wl.prefill_chunk)
     if args.profile_step:
         # two eager steps; print what each processed so that ncu byte counts can be scaled per unit
