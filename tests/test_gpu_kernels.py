@@ -165,6 +165,8 @@ ATTENTION_CASES = [
     (16, 8, [9, 7], [1100, 160], 0),
     # enough (entry, KV head) pairs for the two-warp launch (one wave of five CTAs per SM)
     (16, 8, [9] * 60, [30 + (i * 37) % 350 for i in range(60)], 0),
+    # prefill rows: eight-warp CTAs, one per query group of 128 vectors, with split-KV partials
+    (16, 8, [300, 5], [600, 200], 32),
 ]
 
 
