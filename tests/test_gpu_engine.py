@@ -317,3 +317,30 @@ def test_capture_all_buckets_before_serving(small) -> None:
     assert held == 2 * len(eng.buckets)
     assert eng.generate(prompts, 24) == eager
     assert len(eng._graphs) == held
+
+
+def test_add_requests_validates_before_taking_slots(small) -> None:
+    """add_requests refuses a batch with a prompt that does not fit, mismatched per-request lists
+    or more requests than free slots, and takes no slot when it does; an accepted batch lands in
+    order and prefills to the same first tokens as one request at a time."""
+    cfg, _, model = small
+    pkg = package()
+    eng = _engine(model, 4, False)
+    free = list(eng.state.free_slots)
+    prompts = pkg.make_prompts(3, cfg.vocab_size, length=20, seed=4)
+    with pytest.raises(ValueError):
+        eng.add_requests(prompts[:2] + [list(range(1, 300))], [8, 8, 8])
+    with pytest.raises(ValueError):
+        eng.add_requests(prompts, [8, 8])
+    with pytest.raises(RuntimeError):
+        eng.add_requests(pkg.make_prompts(5, cfg.vocab_size, length=20, seed=5), [8] * 5)
+    assert eng.state.free_slots == free
+    slots = eng.add_requests(prompts, [8, 8, 8], ignore_eos=True)
+    assert slots == free[:3]
+    batched = eng.prefill(slots)
+    eng.release(slots)
+    one = _engine(model, 4, False)
+    singles = [one.add_request(p, 8, ignore_eos=True) for p in prompts]
+    single = one.prefill(singles)
+    assert [batched.tokens[s] for s in slots] == [single.tokens[s] for s in singles]
+    one.release(singles)
