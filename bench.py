@@ -76,6 +76,8 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=15.0)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-extra", action="store_true",
+                   help="skip the 1/4/16-user lines and the config 3 / 4 block of the default run")
     p.add_argument("--profile-step", action="store_true",
                    help="prefill, then two eager speculative steps and exit (a short target for ncu)")
     p.add_argument("--profile-users", type=int, default=0,
@@ -289,7 +291,11 @@ def run_reference(args, dist: Dist) -> None:
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
         "warmup": args.warmup, "ms_per_step": 1000 * seconds / max(steps, 1), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-        "config": workload_config(args),
+        "config": {"workload": "BASELINE config 1 (the reference's CPU configuration): Qwen3-0.6B random-init "
+                               "(seed 0) fp32, 1 user, 64-token motif prompt, 128 greedy outputs, n-gram n=3 k=4, "
+                               "16-token paged KV; the reference serves requests one at a time, so this is also "
+                               "its rate at 64 users",
+                   "users_per_gpu": 1, "k": 4, "parallelism": "cpu (host cores)"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -377,6 +383,127 @@ class Workload:
 
 
 # ---------------------------------------------------------------------------- B200 arm
+def time_steady_steps(engine, engine_mod, slots: list[int], steps: int, warmup: int, dist=None, sampler=None):
+    """Warm-up steps, then exactly ``steps`` replays of the bucket's CUDA graph between CUDA events
+    (barrier + synchronize on both sides). Returns (ms, emitted tokens, clock summary or None)."""
+    for _ in range(warmup):
+        engine.step(slots)
+    engine.model.raise_on_device_error()
+    bucket = engine_mod.round_up_to_bucket(len(slots), engine.buckets)
+    engine._set_slots(slots, bucket)
+    lens_before = engine.state.seq_len.sum().item()
+    graph = engine._graphs[(bucket, 0)]
+    stream = torch.cuda.current_stream()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = sampler or _NoClocks()
+    with sampler:
+        start.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    emitted = engine.state.seq_len.sum().item() - lens_before
+    engine.model.raise_on_device_error()
+    return start.elapsed_time(end), emitted, graph
+
+
+class _NoClocks:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return None
+
+
+def step_bytes_of(model, engine, slots: list[int], ms_per_step: float, steps: int, emitted: int,
+                  shared_prefix: int = 0) -> float:
+    """Algorithmic bytes of an average timed step: weights + the KV each row reads (shared prefix
+    blocks once) + the KV rows written, from the contexts after the timed steps."""
+    lens = engine.state.seq_len[torch.tensor(slots, device=model.device).long()]
+    rows = emitted / steps  # ~ verify rows that were kept per step; the written rows are >= this
+    ctx = float(lens.sum().item()) - emitted / 2.0  # mean context over the timed steps
+    if shared_prefix:
+        ctx -= (len(slots) - 1) * (shared_prefix // 16 * 16)
+    per_token = model.kv_bytes_per_token()
+    return model.weight_bytes + ctx * per_token + rows * per_token
+
+
+def per_user_counts(args, pkg, engine, engine_mod, model, peak: float) -> dict:
+    """BASELINE config 2 at 1, 4 and 16 users (the metric's "at 1 & 64 users"): the same engine, model
+    and captured bucket graphs, a fresh set of requests per count."""
+    out = {}
+    for users in (1, 4, 16):
+        prompts = pkg.make_prompts(users, pkg.QWEN3_0_6B.vocab_size, args.prompt_len, seed=100 + users)
+        new = max(args.max_new, (args.warmup + args.steps + 3) * (args.k + 1))
+        slots = engine.add_requests(prompts, [new] * users, ignore_eos=True, seeds=list(range(users)))
+        engine.prefill(slots)
+        ms, emitted, _ = time_steady_steps(engine, engine_mod, slots, args.steps, max(3, args.warmup))
+        ms_step = ms / args.steps
+        nbytes = step_bytes_of(model, engine, slots, ms_step, args.steps, emitted)
+        out[str(users)] = {"value": round(emitted / (ms / 1000.0), 1), "unit": UNIT, "ms_per_step": round(ms_step, 4),
+                           "step_bytes": int(nbytes), "step_frac": round(nbytes / (ms_step / 1000.0) / 1e9 / peak, 4),
+                           "tokens_per_step_per_user": round(emitted / args.steps / users, 3)}
+        engine.release(slots)
+    return out
+
+
+def other_workloads(args, pkg, model_mod, engine_mod, device, peak: float) -> dict:
+    """Compact steady-state lines (no e2e) of BASELINE configs 3 and 4 on this GPU, so the default
+    run carries them: a model and engine per workload, built, timed and freed in turn."""
+    out = {}
+    for name in ("c3", "c4"):
+        try:
+            sub = argparse.Namespace(**{**vars(args), "workload": name, "profile_step": False, "profile_users": 0})
+            wl = Workload(sub, pkg, pkg.QWEN3_0_6B.vocab_size, 0)
+            steps = max(5, args.steps // 2)
+            warm = 3
+            longest = max(len(p) for p in wl.prompts)
+            new = max(wl.max_new, (warm + steps + 3) * (wl.k + 1))
+            max_len = longest + new + 8
+            blocks = (wl.users + 1) * -(-(max_len + wl.k + 1) // 16) + 16
+            weights = pkg.make_weights(wl.cfg, seed=0)
+            copies = wl.shared_prefix // 16 if (wl.kv_int8 and wl.shared_prefix) else 0
+            model = model_mod.B200Model(wl.cfg, weights, num_slots=blocks * 16, device=device,
+                                        max_positions=max_len + wl.k + 16,
+                                        max_rows=max(wl.users * (wl.k + 1), 16384), max_seqs=wl.users + 1,
+                                        kv_int8=wl.kv_int8, weight_int8=wl.weight_int8, kv_copy_blocks=copies)
+            del weights
+            engine = engine_mod.B200SpeculativeEngine(model, k=wl.k, max_ngram=3,
+                                                      max_seqs=wl.users + (1 if wl.shared_prefix else 0),
+                                                      max_model_len=max_len, num_blocks=blocks, cuda_graphs=True,
+                                                      sampling=wl.sampled)
+            prefix = engine.add_prefix(wl.prompts[0][: wl.shared_prefix]) if wl.shared_prefix else None
+            slots = engine.add_requests(wl.prompts, [new] * wl.users, ignore_eos=True, temperature=wl.temperature,
+                                        top_p=wl.top_p, seeds=list(range(wl.users)), prefix=prefix)
+            engine.prefill(slots, chunk=wl.prefill_chunk)
+            bucket = engine_mod.round_up_to_bucket(len(slots), engine.buckets)
+            for buf in (0, 1):
+                engine._capture(bucket, buf)
+            ms, emitted, graph = time_steady_steps(engine, engine_mod, slots, steps, warm)
+            ms_step = ms / steps
+            nbytes = step_bytes_of(model, engine, slots, ms_step, steps, emitted, wl.shared_prefix)
+            out[name] = {"metric": wl.metric, "value": round(emitted / (ms / 1000.0), 1), "unit": UNIT,
+                         "ms_per_step": round(ms_step, 4), "steps": steps, "warmup": warm,
+                         "step_bytes": int(nbytes),
+                         "step_frac": round(nbytes / (ms_step / 1000.0) / 1e9 / peak, 4),
+                         "workload": wl.config["workload"]}
+            del graph
+            engine._graphs.clear()
+            del engine
+            torch.cuda.synchronize()
+            model.close()
+            del model
+            torch.cuda.empty_cache()
+        except Exception as exc:  # the headline line must still print
+            out[name] = {"error": f"{type(exc).__name__}: {exc}"}
+    return out
+
+
 def algorithmic_bytes(kind: str, cfg, M: int, ctx_sum: int, kv_bytes_per_token_layer: int, wb: float = 2.0) -> float:
     """Unique bytes one launch of ``kind`` must move (weights at ``wb`` bytes per element plus one
     bf16 scale per row when int8, activations in/out, KV)."""
@@ -463,26 +590,9 @@ def run_b200(args, dist: Dist) -> None:
         model.raise_on_device_error()
         model.close()
         return
-    for _ in range(args.warmup):
-        engine.step(slots)
-    model.raise_on_device_error()
-    engine._set_slots(slots, engine_mod.round_up_to_bucket(len(slots), engine.buckets))
-    lens_before = engine.state.seq_len.sum().item()
-    graph = engine._graphs[(engine_mod.round_up_to_bucket(len(slots), engine.buckets), 0)]
+    clocks = ClockSampler(dist.local_rank)
+    ms, emitted, graph = time_steady_steps(engine, engine_mod, slots, args.steps, args.warmup, dist, clocks)
     stream = torch.cuda.current_stream()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(dist.local_rank) as clocks:
-        start.record(stream)
-        for _ in range(args.steps):
-            graph.replay()
-        end.record(stream)
-        torch.cuda.synchronize()
-    dist.barrier()
-    ms = start.elapsed_time(end)
-    emitted = engine.state.seq_len.sum().item() - lens_before
-    model.raise_on_device_error()
     max_ms = dist.max(ms)
     total_emitted = emitted if wl.tp else dist.sum(emitted)  # a split model's ranks emit the same tokens
     value = total_emitted / (max_ms / 1000.0)
@@ -546,6 +656,13 @@ def run_b200(args, dist: Dist) -> None:
     unique_ctx = ctx_sum - (len(slots) - 1) * (wl.shared_prefix // 16 * 16) if wl.shared_prefix else ctx_sum
     step_bytes = model.weight_bytes + unique_ctx * model.kv_bytes_per_token() + M * model.kv_bytes_per_token()
     step_time_s = max_ms / 1000.0 / args.steps
+    # the profiled step serialises its launches with an event after each one; inside the timed
+    # graph the launches overlap (programmatic dependent launch), so the same kernel takes a
+    # smaller share of a shorter step: its in-graph time, scaled so that all kernels sum to the
+    # timed step, and the fraction of the peak that time gives
+    scale = (1000.0 * step_time_s) / step_ms_profiled if step_ms_profiled > 0 else 1.0
+    roofline["avg_launch_ms_in_graph"] = round(avg_ms * scale, 5)
+    roofline["frac_in_graph"] = round(bytes_launch / (avg_ms * scale / 1000.0) / 1e9 / peak, 4)
     step_roofline = {"bytes_per_step": int(step_bytes), "ms_per_step": round(1000 * step_time_s, 4),
                      "achieved_gbs": round(step_bytes / step_time_s / 1e9, 1),
                      "frac": round(step_bytes / step_time_s / 1e9 / peak, 4),
@@ -576,6 +693,11 @@ def run_b200(args, dist: Dist) -> None:
                "steps": n_steps, "tokens": int(tokens), "ms": round(e_ms, 3)}
         model.raise_on_device_error()
 
+    # ------------------------------------------------------------ config 2 at 1 / 4 / 16 users (N = 1)
+    per_users = None
+    if wl.name == "c2" and dist.world == 1 and not args.no_extra:
+        per_users = per_user_counts(args, pkg, engine, engine_mod, model, peak)
+
     # ------------------------------------------------------------ CPU baseline (rank 0, N = 1)
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline and wl.name == "c2":
@@ -586,6 +708,19 @@ def run_b200(args, dist: Dist) -> None:
                "sample": f"CPU oracle (reference serial speculative path restated), fp32, config 1's request "
                          f"served repeatedly one at a time (prefill + steps to 128 tokens), {c_steps} steps "
                          f"(prefills included) in {c_seconds:.1f} s"}
+
+    workloads = None
+    if wl.name == "c2" and dist.world == 1 and not args.no_extra:
+        # free the headline's model first: config 4's KV pool alone takes ~70 GB
+        del graph
+        engine._graphs.clear()
+        del engine
+        torch.cuda.synchronize()
+        model.close()
+        torch.cuda.empty_cache()
+        engine = graph = None
+        model = None
+        workloads = other_workloads(args, pkg, model_mod, engine_mod, device, peak)
 
     if dist.rank == 0:
         line = {
@@ -601,13 +736,18 @@ def run_b200(args, dist: Dist) -> None:
             "tokens_per_step_per_user": round(total_emitted / (1 if wl.tp else dist.world) / args.steps / users, 3),
             "kernel_profile": profile,
         }
+        if per_users is not None:
+            line["per_users"] = per_users
+        if workloads is not None:
+            line["workloads"] = workloads
         print(json.dumps(line), flush=True)
     # CUDA graphs hold the model's NCCL calls (tensor parallel): release them before the communicator
-    del graph
-    engine._graphs.clear()
-    del engine
-    torch.cuda.synchronize()
-    model.close()
+    if model is not None:
+        del graph
+        engine._graphs.clear()
+        del engine
+        torch.cuda.synchronize()
+        model.close()
 
 
 def main() -> None:

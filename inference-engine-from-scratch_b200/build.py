@@ -5,11 +5,14 @@
 nvcc compiles every ``csrc/*.cu`` with ``-gencode arch=compute_100a,code=sm_100a`` and links the
 CUDA runtime statically, so the library needs only the NVIDIA driver at run time (it resolves the
 driver's ``cuTensorMapEncodeTiled`` through ``cudaGetDriverEntryPoint``). The build is skipped when
-the library is newer than every source.
+the SHA-256 of every source, header and flag, recorded next to the library at its last build
+(``libnespec.so.sha256``), still matches: a prebuilt library whose sources changed is rebuilt,
+whatever the files' modification times say. The sources compile in parallel.
 """
 
 from __future__ import annotations
 
+import hashlib
 import os
 import shutil
 import subprocess
@@ -21,6 +24,7 @@ REPO = PACKAGE_DIR.parent
 CSRC = PACKAGE_DIR / "csrc"
 INCLUDE = REPO / "include"
 LIBRARY = PACKAGE_DIR / "libnespec.so"
+LIBRARY_HASH = PACKAGE_DIR / "libnespec.so.sha256"
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
     "-O3",
@@ -78,11 +82,21 @@ def headers() -> list[Path]:
     return sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
 
 
+def source_hash() -> str:
+    """SHA-256 over the build inputs: every source and header (name and bytes) and the flags."""
+    h = hashlib.sha256()
+    h.update(" ".join(ARCH_FLAGS + NVCC_FLAGS).encode())
+    for path in sources() + headers():
+        h.update(path.name.encode() + b"\0")
+        h.update(path.read_bytes())
+        h.update(b"\0")
+    return h.hexdigest()
+
+
 def is_stale() -> bool:
-    if not LIBRARY.exists():
+    if not LIBRARY.exists() or not LIBRARY_HASH.exists():
         return True
-    built = LIBRARY.stat().st_mtime
-    return any(p.stat().st_mtime > built for p in sources() + headers())
+    return LIBRARY_HASH.read_text().strip() != source_hash()
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
@@ -102,24 +116,31 @@ def build(force: bool = False, verbose: bool = False) -> Path:
 
 
 def _build(build_dir: Path, verbose: bool) -> Path:
+    from concurrent.futures import ThreadPoolExecutor
+
     nvcc = nvcc_path()
-    objects = []
-    for src in sources():
-        obj = build_dir / (src.stem + ".o")
-        cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, f"-I{INCLUDE}", f"-I{CSRC}", *nccl_include(), "-c", str(src), "-o",
-               str(obj)]
-        proc = subprocess.run(cmd, capture_output=True, text=True)
+    digest = source_hash()
+    srcs = sources()
+    objects = [str(build_dir / (src.stem + ".o")) for src in srcs]
+
+    def compile_one(src: Path, obj: str):
+        cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, f"-I{INCLUDE}", f"-I{CSRC}", *nccl_include(), "-c", str(src), "-o", obj]
+        return src, subprocess.run(cmd, capture_output=True, text=True)
+
+    with ThreadPoolExecutor(max_workers=max(1, min(len(srcs), os.cpu_count() or 1))) as pool:
+        results = list(pool.map(compile_one, srcs, objects))
+    for src, proc in results:
         if proc.returncode != 0:
             raise RuntimeError(f"nvcc failed on {src.name}:\n{proc.stderr}")
         if verbose:
             sys.stderr.write(proc.stderr)
-        objects.append(str(obj))
     tmp = LIBRARY.with_suffix(f".so.{os.getpid()}.tmp")
     cmd = [nvcc, *ARCH_FLAGS, "-shared", "-cudart", "static", "-o", str(tmp), *objects, "-ldl"]
     proc = subprocess.run(cmd, capture_output=True, text=True)
     if proc.returncode != 0:
         raise RuntimeError(f"nvcc link failed:\n{proc.stderr}")
     os.replace(tmp, LIBRARY)
+    LIBRARY_HASH.write_text(digest + "\n")
     return LIBRARY
 
 

@@ -439,6 +439,12 @@ __device__ __forceinline__ void tile_store(const Ctx& c, const AttnSplit& sp, co
         *reinterpret_cast<__nv_bfloat162*>(o + d) = __floats2bfloat162_rn(ts.o[t][2 * r] * inv, ts.o[t][2 * r + 1] * inv);
       }
     } else {
+      // the partial area holds max_vec vectors per (entry, head): a device q_len above the host's
+      // bound is reported and its partials dropped instead of written past the area
+      if (v >= sp.max_vec) {
+        if (lane == 0) report(c.status, NE_DEV_BAD_SLOT);
+        continue;
+      }
       const long long base = (((long long)b * c.nkv + c.h) * sp.splits + split) * sp.max_vec + v;
       float* o = sp.part_o + base * D;
 #pragma unroll
@@ -618,6 +624,8 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
         const int orow = c.r0 + (v_base + v) / c.G;
         const int head = c.h * c.G + (v_base + v) % c.G;
         out[((long long)orow * nh + head) * D + d] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
+      } else if (v_base + v >= sp.max_vec) {
+        if (d == 0) report(c.status, NE_DEV_BAD_SLOT);  // beyond the partial area (see tile_store)
       } else {
         const long long base = (((long long)b * nkv + h) * sp.splits + split) * sp.max_vec + v_base + v;
         sp.part_o[base * D + d] = o;
@@ -772,7 +780,10 @@ __global__ void __launch_bounds__(D) combine_kernel(const ne_rows rows, int nh, 
       for (int s = 0; s < sp.splits; ++s) {
         const long long base = base0 + (long long)s * sp.max_vec;
         const float ms = sp.part_m[base];
-        const float f = ms == NEG_INF ? 0.f : exp2f(ms - m);
+        // a split without blocks left part_o untouched (stale or never written): skip it rather
+        // than scale it by zero, which would turn a stale NaN / Inf into the output
+        if (ms == NEG_INF) continue;
+        const float f = exp2f(ms - m);
         l += sp.part_l[base] * f;
         o += sp.part_o[base * D + d] * f;
       }
@@ -919,16 +930,19 @@ int launch_attention_tc(const __nv_bfloat16* q, __nv_bfloat16* out, const void* 
   const int nw = max_vec > 32 && tile_slots == 1 ? prefill_warps
                  : ((max_vec <= 16 || tile_slots > 1) && ctas <= 5LL * sms && ctas > 3LL * sms) ? 2 : 4;
   const size_t smem = attention_smem_bytes_nw(nw);
-  static bool attr_set[6] = {false, false, false, false, false, false};
+  // the shared-memory limit is a per-device function attribute: set once per (device, variant)
+  constexpr int MAX_DEVICES = 64;
+  static bool attr_set[MAX_DEVICES][6] = {};
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return NE_ERR_CUDA;
   auto kernel = kv_int8 ? (nw == 2 ? attention_kernel<true, 2> : nw == 8 ? attention_kernel<true, 8>
                                                                           : attention_kernel<true, 4>)
                         : (nw == 2 ? attention_kernel<false, 2> : nw == 8 ? attention_kernel<false, 8>
                                                                            : attention_kernel<false, 4>);
   const int ai = (kv_int8 ? 3 : 0) + (nw == 2 ? 1 : nw == 8 ? 2 : 0);
-  if (!attr_set[ai]) {
+  if (!attr_set[dev][ai]) {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return NE_ERR_CUDA;
-    attr_set[ai] = true;
+    attr_set[dev][ai] = true;
   }
   if (sp.splits > 1) {
     const long long n = (long long)rows.num_seqs * num_kv_heads * sp.splits * sp.max_vec;

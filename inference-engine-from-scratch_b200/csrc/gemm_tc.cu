@@ -840,17 +840,22 @@ bool make_tmap_w8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t co
   return r == CUDA_SUCCESS;
 }
 
+// Function attributes belong to the device they were set on: set them once per (device, variant).
 template <int MODE, int CONV>
 cudaError_t prepare_mode() {
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_tc_kernel<MODE, CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    GEMM_SMEM_BYTES);
-    if (attr_err == cudaSuccess)
-      attr_err = cudaFuncSetAttribute(gemm_tc_kernel<MODE, CONV>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  });
-  return attr_err;
+  constexpr int MAX_DEVICES = 64;
+  static std::mutex mu;
+  static bool done[MAX_DEVICES] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done[dev]) return cudaSuccess;
+  cudaError_t err = cudaFuncSetAttribute(gemm_tc_kernel<MODE, CONV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         GEMM_SMEM_BYTES);
+  if (err == cudaSuccess)
+    err = cudaFuncSetAttribute(gemm_tc_kernel<MODE, CONV>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (err == cudaSuccess) done[dev] = true;
+  return err;
 }
 
 template <int MODE, int CONV>

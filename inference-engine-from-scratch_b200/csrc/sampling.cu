@@ -891,9 +891,14 @@ __global__ void __launch_bounds__(THREADS)
 }  // namespace
 
 namespace {
+// Function attributes belong to the device they were set on: set once per (device, kernel).
 template <typename K>
-bool allow_hist_smem(K kernel) {
-  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, HIST_WORDS * 4) == cudaSuccess;
+bool allow_hist_smem(K kernel, bool (&done)[64]) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  if (done[dev]) return true;
+  done[dev] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, HIST_WORDS * 4) == cudaSuccess;
+  return done[dev];
 }
 }  // namespace
 
@@ -901,8 +906,8 @@ int launch_sample_stats(const ne_batch_state& st, const int32_t* seq_slot, int n
                         const int32_t* q_len, const int32_t* lm_count, int lm_max, const __nv_bfloat16* logits,
                         int vocab, SampleStats* stats, cudaStream_t stream) {
   if (lm_max <= 0 || num_seqs <= 0) return NE_OK;
-  static const bool attr = allow_hist_smem(sample_stats_kernel);
-  if (!attr) return NE_ERR_CUDA;
+  static bool attr_done[64] = {};
+  if (!allow_hist_smem(sample_stats_kernel, attr_done)) return NE_ERR_CUDA;
   return launch_kernel(sample_stats_kernel, dim3(lm_max), dim3(THREADS), HIST_WORDS * 4, stream, st, seq_slot, num_seqs, lm_start,
                        q_len, lm_count, lm_max, logits, vocab, stats) == cudaSuccess
              ? NE_OK
@@ -927,7 +932,8 @@ int launch_accept_sampled(const ne_batch_state& st, const int32_t* seq_slot, int
 int launch_sample_stats_rows(const __nv_bfloat16* logits, int rows, int vocab, const float* temperature,
                              const float* top_p, SampleStats* stats, cudaStream_t stream) {
   if (rows <= 0) return NE_OK;
-  static const bool attr = allow_hist_smem(sample_stats_rows_kernel);
+  static bool attr_done[64] = {};
+  const bool attr = allow_hist_smem(sample_stats_rows_kernel, attr_done);
   if (!attr) return NE_ERR_CUDA;
   return launch_kernel(sample_stats_rows_kernel, dim3(rows), dim3(THREADS), HIST_WORDS * 4, stream, logits, vocab, temperature,
                        top_p, stats) == cudaSuccess

@@ -27,7 +27,7 @@ from torch.nn import functional
 from .config import QWEN3_0_6B, SMALL_TEST, Qwen3Config
 from .engine import B200SpeculativeEngine
 from .model import B200Model
-from .serial import B200ModelRunner, GenerationRequest, PagedSlotAllocator, SamplingParams, Sequence
+from .serial import B200ModelRunner
 from .weights import make_weights
 
 NUM_PROMPTS = 8
@@ -46,17 +46,33 @@ class QualityReport:
     settings: str
 
 
+@dataclass
+class _Tokens:
+    """The fields of a sequence ``B200ModelRunner.score_tokens`` reads (and advances)."""
+
+    token_ids: list[int]
+    num_cached_tokens: int = 0
+
+
+class _WholePool:
+    """A block table over the first blocks of the pool, for one scoring pass."""
+
+    block_size = 16
+
+    def __init__(self, num_tokens: int) -> None:
+        self._table = list(range(math.ceil(num_tokens / self.block_size)))
+
+    def block_table(self, sequence) -> list[int]:
+        return list(self._table)
+
+
 def compute_perplexity(model: B200Model, token_ids: list[int]) -> float:
     """exp(mean cross-entropy of token i + 1 given tokens 0..i), one forward over the sequence."""
-    blocks = math.ceil(len(token_ids) / 16)
-    runner = B200ModelRunner(model, PagedSlotAllocator(blocks, 16))
-    seq = Sequence.from_request(GenerationRequest("ppl", list(token_ids), SamplingParams(max_new_tokens=1)))
-    runner.allocator.reserve(seq, seq.num_tokens)
-    try:
-        logits = runner.score_tokens(seq, seq.num_tokens)
-        loss = functional.cross_entropy(logits[:-1].float(), torch.tensor(token_ids[1:], device=logits.device))
-    finally:
-        runner.allocator.free(seq)
+    if math.ceil(len(token_ids) / 16) * 16 > model.num_slots:
+        raise ValueError("the sequence does not fit the model's KV pool")
+    runner = B200ModelRunner(model, _WholePool(len(token_ids)))
+    logits = runner.score_tokens(_Tokens(list(token_ids)), len(token_ids))
+    loss = functional.cross_entropy(logits[:-1].float(), torch.tensor(token_ids[1:], device=logits.device))
     return math.exp(loss.item())
 
 

@@ -1,20 +1,30 @@
-"""The reference's serial speculative API on the B200 kernels (one request at a time).
+"""The B200 parts of the reference's serial speculative API (one request at a time).
 
-Same names, arguments and semantics as the reference (paths relative to nanoengine/src/nanoengine):
+These plug into the reference's own serial classes (paths relative to nanoengine/src/nanoengine):
+the reference's ``SpeculativeGenerator`` (engine/speculative/speculative_generator.py:21-90) drives
+them with its own ``Sequence`` (engine/sequence_state.py:12-57) and ``PagedSlotAllocator``
+(engine/memory/paged_allocator.py:21-79), exactly as ``runtime.create_engine`` wires its
+``ModelRunner`` and proposer (engine/runtime.py:162-171). Built here:
 
-* ``SamplingParams`` / ``GenerationRequest`` / ``TokenEvent``  engine/interface.py:9-30
-* ``Sequence``                 engine/sequence_state.py:12-57
-* ``BlockAllocator``           engine/memory/block_allocator.py:8-33 (FIFO free list)
-* ``PagedSlotAllocator``       engine/memory/paged_allocator.py:21-79
-* ``B200ModelRunner``          engine/generation/model_runner.py:14-80 (``run_step``, ``score_tokens``)
+* ``B200ModelRunner``          ModelRunner (engine/generation/model_runner.py:14-80): ``run_step`` and
+                               ``score_tokens`` over ``ne_forward``; it reads the sequence's
+                               ``token_ids`` / ``num_cached_tokens`` and the allocator's
+                               ``block_table`` / ``block_size``, and calls ``on_tokens_cached``
 * ``NgramProposer``            engine/speculative/proposers.py:39-60 (the suffix match runs on the GPU)
-* ``create_sampling_generator`` engine/sampling.py:12-18 (a Philox4x32-10 stream instead of torch's)
-* ``verify_proposal``          engine/speculative/verifier.py:27-60 (greedy: kernel argmax per row;
-  sampled: ``ne_verify_logits``, rejection sampling on the request's Philox stream)
-* ``SpeculativeGenerator``     engine/speculative/speculative_generator.py:21-90
+* ``DraftModelProposer``       engine/speculative/proposers.py:63-106 over a ``B200ModelRunner``
+* ``PhiloxGenerator`` / ``create_sampling_generator``
+                               a request's random stream (Philox4x32-10) where the reference keeps a
+                               ``torch.Generator`` (engine/sampling.py:12-18)
+* ``verify_proposal``          engine/speculative/verifier.py:27-60 on the GPU (greedy: the kernel's
+                               per-row argmax; sampled: ``ne_verify_logits``, rejection sampling on the
+                               request's Philox stream)
 
-so that a reference user can swap the runner (and proposer) of the serial speculative path. The
-batched path (``engine.B200SpeculativeEngine``) runs the same step for many requests at once.
+The reference's own ``verify_proposal`` also works on the bf16 logits ``score_tokens`` returns (it
+is plain torch); this module's ``verify_proposal`` is the device path, whose sampled decisions are
+bit-comparable with the reference's when both draw from the same Philox stream. A reference
+``Sequence`` carries a ``torch.Generator``: sampled first tokens (``run_step``) then draw from a
+Philox stream keyed by that generator's seed (``initial_seed()``), one stream per generator.
+The batched path (``engine.B200SpeculativeEngine``) runs the same step for many requests at once.
 """
 
 from __future__ import annotations
@@ -22,9 +32,8 @@ from __future__ import annotations
 import ctypes
 import math
 import os
-from collections import deque
-from collections.abc import Iterator
-from dataclasses import dataclass, field
+from collections import OrderedDict
+from dataclasses import dataclass
 
 import torch
 
@@ -34,31 +43,6 @@ from .state import DeviceBatchState
 from .state import seed_as_int64 as _seed_as_int64
 
 GREEDY_TEMPERATURE = 0.0
-PADDING_TOKEN_ID = 0
-
-
-@dataclass(frozen=True)
-class SamplingParams:
-    max_new_tokens: int
-    temperature: float = 0.0
-    top_p: float = 1.0
-    seed: int | None = None
-    ignore_eos: bool = False
-
-
-@dataclass(frozen=True)
-class GenerationRequest:
-    request_id: str
-    prompt_token_ids: list[int]
-    sampling_params: SamplingParams
-
-
-@dataclass(frozen=True)
-class TokenEvent:
-    request_id: str
-    token_id: int
-    is_finished: bool
-    finish_reason: str | None
 
 
 class PhiloxGenerator:
@@ -74,122 +58,38 @@ class PhiloxGenerator:
 
 
 def create_sampling_generator(seed: int | None, device=None) -> PhiloxGenerator:
-    """engine/sampling.py:12-18."""
+    """engine/sampling.py:12-18, with a Philox stream in place of the ``torch.Generator``."""
     return PhiloxGenerator(seed)
 
 
-@dataclass(eq=False)
-class Sequence:
-    request: GenerationRequest
-    token_ids: list[int]
-    num_prompt_tokens: int
-    num_cached_tokens: int = 0
-    sampling_generator: PhiloxGenerator | None = None
-
-    @classmethod
-    def from_request(cls, request: GenerationRequest, device=None) -> "Sequence":
-        return cls(request=request, token_ids=list(request.prompt_token_ids),
-                   num_prompt_tokens=len(request.prompt_token_ids),
-                   sampling_generator=create_sampling_generator(request.sampling_params.seed, device))
-
-    @property
-    def request_id(self) -> str:
-        return self.request.request_id
-
-    @property
-    def sampling_params(self) -> SamplingParams:
-        return self.request.sampling_params
-
-    @property
-    def num_tokens(self) -> int:
-        return len(self.token_ids)
-
-    @property
-    def num_generated_tokens(self) -> int:
-        return len(self.token_ids) - self.num_prompt_tokens
-
-    @property
-    def num_uncached_tokens(self) -> int:
-        return len(self.token_ids) - self.num_cached_tokens
+# torch.Generator objects take no weak references: the streams of reference generators are held
+# by object id (with the generator, so a recycled id is noticed) until ``release_stream``, and at
+# most _MAX_TORCH_STREAMS of them (the least recently used is dropped; the serial path serves one
+# request at a time)
+_MAX_TORCH_STREAMS = 1024
+_TORCH_STREAMS: "OrderedDict[int, tuple[object, PhiloxGenerator]]" = OrderedDict()
 
 
-class OutOfKVMemoryError(Exception):
-    """No free block is left in the KV cache pool (engine/memory/slot_allocator.py:10-11)."""
+def philox_stream(generator) -> PhiloxGenerator:
+    """The Philox stream a request draws from: its own ``PhiloxGenerator``, or for the reference's
+    ``torch.Generator`` one stream per generator object, keyed by its ``initial_seed()``."""
+    if isinstance(generator, PhiloxGenerator):
+        return generator
+    if generator is None:
+        raise ValueError("sampled decoding needs the request's generator")
+    held = _TORCH_STREAMS.get(id(generator))
+    if held is None or held[0] is not generator:
+        held = (generator, PhiloxGenerator(int(generator.initial_seed())))
+        _TORCH_STREAMS[id(generator)] = held
+        while len(_TORCH_STREAMS) > _MAX_TORCH_STREAMS:
+            _TORCH_STREAMS.popitem(last=False)
+    _TORCH_STREAMS.move_to_end(id(generator))
+    return held[1]
 
 
-class BlockAllocator:
-    def __init__(self, num_blocks: int) -> None:
-        self.num_blocks = num_blocks
-        self._free_blocks: deque[int] = deque(range(num_blocks))
-        self._used_blocks: set[int] = set()
-
-    @property
-    def num_free_blocks(self) -> int:
-        return len(self._free_blocks)
-
-    @property
-    def num_used_blocks(self) -> int:
-        return len(self._used_blocks)
-
-    def allocate(self) -> int:
-        if not self._free_blocks:
-            raise OutOfKVMemoryError("no free KV blocks")
-        block = self._free_blocks.popleft()
-        self._used_blocks.add(block)
-        return block
-
-    def free(self, block: int) -> None:
-        if block not in self._used_blocks:
-            raise ValueError(f"block {block} is not allocated")
-        self._used_blocks.remove(block)
-        self._free_blocks.append(block)
-
-
-class PagedSlotAllocator:
-    def __init__(self, num_blocks: int, block_size: int = 16) -> None:
-        self.block_size = block_size
-        self._blocks = BlockAllocator(num_blocks)
-        self._block_tables: dict[str, list[int]] = {}
-
-    @property
-    def num_total_slots(self) -> int:
-        return self._blocks.num_blocks * self.block_size
-
-    @property
-    def num_reserved_slots(self) -> int:
-        return self._blocks.num_used_blocks * self.block_size
-
-    @property
-    def num_free_blocks(self) -> int:
-        return self._blocks.num_free_blocks
-
-    def block_table(self, sequence) -> list[int]:
-        return list(self._block_tables.get(sequence.request_id, []))
-
-    def count_missing_blocks(self, sequence, num_tokens: int) -> int:
-        owned = len(self._block_tables.get(sequence.request_id, []))
-        return max(0, math.ceil(num_tokens / self.block_size) - owned)
-
-    def can_reserve(self, sequence, num_tokens: int) -> bool:
-        return self.count_missing_blocks(sequence, num_tokens) <= self._blocks.num_free_blocks
-
-    def reserve(self, sequence, num_tokens: int) -> None:
-        if not self.can_reserve(sequence, num_tokens):
-            raise OutOfKVMemoryError(f"no blocks for {num_tokens} tokens of {sequence.request_id}")
-        table = self._block_tables.setdefault(sequence.request_id, [])
-        for _ in range(self.count_missing_blocks(sequence, num_tokens)):
-            table.append(self._blocks.allocate())
-
-    def free(self, sequence) -> None:
-        for block in self._block_tables.pop(sequence.request_id, []):
-            self._blocks.free(block)
-
-    @property
-    def num_prefix_hit_tokens(self) -> int:
-        return 0
-
-    def on_tokens_cached(self, sequence) -> None:
-        return None
+def release_stream(generator) -> None:
+    """Forget the Philox stream of a finished request's ``torch.Generator``."""
+    _TORCH_STREAMS.pop(id(generator), None)
 
 
 class _HostRows:
@@ -225,9 +125,13 @@ class _HostRows:
 
 
 class B200ModelRunner:
-    """ModelRunner (engine/generation/model_runner.py:14-80) whose step is ``ne_forward``."""
+    """ModelRunner (engine/generation/model_runner.py:14-80) whose step is ``ne_forward``.
 
-    def __init__(self, model: B200Model, allocator: PagedSlotAllocator, device=None) -> None:
+    ``allocator`` is the reference's ``PagedSlotAllocator`` (or any object with ``block_size``,
+    ``block_table(sequence)`` and ``on_tokens_cached(sequence)``); sequences are the reference's
+    ``Sequence`` (``token_ids``, ``num_cached_tokens``, ``sampling_params``, ``sampling_generator``)."""
+
+    def __init__(self, model: B200Model, allocator, device=None) -> None:
         self.lib = _lib.load()
         self._model = model
         self.allocator = allocator
@@ -269,9 +173,9 @@ class B200ModelRunner:
                 logits = torch.empty((1, self.vocab_size), dtype=torch.bfloat16, device=self._device)
             ids = self._forward(seq, count, [count - 1], logits)
             seq.num_cached_tokens += count
-            self.allocator.on_tokens_cached(seq)
+            self._cached(seq)
             if sampled:
-                ids = _logits_verifier(self._device).verify([], logits, params, seq.sampling_generator)
+                ids = _logits_verifier(self._device).verify([], logits, params, philox_stream(seq.sampling_generator))
             out.append(ids[0])
         return out
 
@@ -280,8 +184,13 @@ class B200ModelRunner:
         logits = torch.empty((token_count, self.vocab_size), dtype=torch.bfloat16, device=self._device)
         self.last_argmax = self._forward(sequence, token_count, list(range(token_count)), logits)
         sequence.num_cached_tokens += token_count
-        self.allocator.on_tokens_cached(sequence)
+        self._cached(sequence)
         return logits
+
+    def _cached(self, sequence) -> None:
+        hook = getattr(self.allocator, "on_tokens_cached", None)  # (the prefix-cache hook)
+        if hook is not None:
+            hook(sequence)
 
 
 @dataclass(frozen=True)
@@ -339,7 +248,7 @@ class DraftModelProposer:
     def __init__(self, runner: B200ModelRunner, device=None) -> None:
         self._runner = runner
         self._device = device
-        self._draft_sequences: dict[str, Sequence] = {}
+        self._draft_sequences: dict = {}
 
     def propose(self, sequence, num_tokens: int) -> Proposal:
         params = sequence.sampling_params
@@ -353,7 +262,7 @@ class DraftModelProposer:
                 guess = self._runner.run_step([draft])[0]  # the argmax after the draft's uncached tokens
             else:
                 row = self._runner.score_tokens(draft, draft.num_uncached_tokens)[-1:]
-                guess = _logits_verifier(row.device).verify([], row, params, sequence.sampling_generator)[0]
+                guess = _logits_verifier(row.device).verify([], row, params, philox_stream(sequence.sampling_generator))[0]
                 rows.append(row)
             draft.token_ids.append(guess)
             guesses.append(guess)
@@ -364,10 +273,11 @@ class DraftModelProposer:
         if draft is not None:
             self._runner.allocator.free(draft)
 
-    def _sync_draft(self, sequence) -> Sequence:
+    def _sync_draft(self, sequence):
         draft = self._draft_sequences.get(sequence.request_id)
         if draft is None:
-            draft = Sequence.from_request(sequence.request, self._device)
+            # a sequence of the caller's own class (the reference's Sequence) for the draft model
+            draft = type(sequence).from_request(sequence.request, self._device)
             self._draft_sequences[sequence.request_id] = draft
         common = 0
         for draft_token, target_token in zip(draft.token_ids, sequence.token_ids):
@@ -402,8 +312,8 @@ class _LogitsVerifier:
                                            proposed=base + 4 * (k + 3), accepted=base + 4 * (k + 4))
         self.status = torch.zeros(1, **i32)
 
-    def verify(self, guesses: list[int], logits: torch.Tensor, params: SamplingParams,
-               generator: PhiloxGenerator | None, draft_logits: torch.Tensor | None = None) -> list[int]:
+    def verify(self, guesses: list[int], logits: torch.Tensor, params, generator: PhiloxGenerator | None,
+               draft_logits: torch.Tensor | None = None) -> list[int]:
         g = len(guesses)
         if g > self.MAX_GUESSES:
             raise ValueError(f"at most {self.MAX_GUESSES} guesses per proposal")
@@ -464,7 +374,7 @@ def _logits_verifier(device) -> _LogitsVerifier:
     return _VERIFIERS[key]
 
 
-def verify_proposal(proposal: Proposal, target_logits: torch.Tensor, params: SamplingParams, generator=None,
+def verify_proposal(proposal, target_logits: torch.Tensor, params, generator=None,
                     target_argmax: list[int] | None = None) -> list[int]:
     """verifier.py:27-60 with one-hot drafts (n-gram, greedy draft model) or a sampled draft model's
     rows (``proposal.draft_logits``): kept guesses + one target token.
@@ -476,8 +386,9 @@ def verify_proposal(proposal: Proposal, target_logits: torch.Tensor, params: Sam
     if proposal.probabilities is not None:
         raise ValueError("the B200 verify takes one-hot drafts or a draft model's logits rows (draft_logits)")
     if params.temperature != GREEDY_TEMPERATURE or target_argmax is None:
+        stream = philox_stream(generator) if params.temperature != GREEDY_TEMPERATURE else None
         return _logits_verifier(target_logits.device).verify(list(proposal.token_ids), target_logits, params,
-                                                             generator, draft_logits=proposal.draft_logits)
+                                                             stream, draft_logits=getattr(proposal, "draft_logits", None))
     kept: list[int] = []
     for index, guess in enumerate(proposal.token_ids):
         if guess == target_argmax[index]:
@@ -485,78 +396,3 @@ def verify_proposal(proposal: Proposal, target_logits: torch.Tensor, params: Sam
             continue
         return [*kept, target_argmax[index]]
     return [*kept, target_argmax[len(proposal.token_ids)]]
-
-
-def find_finish_reason(token_id: int, num_generated_tokens: int, params: SamplingParams,
-                       stop_token_ids: frozenset[int]) -> str | None:
-    """engine/sampling.py:54-62."""
-    if not params.ignore_eos and token_id in stop_token_ids:
-        return "stop"
-    if num_generated_tokens >= params.max_new_tokens:
-        return "length"
-    return None
-
-
-@dataclass
-class SpeculativeCounters:
-    proposed: int = 0
-    accepted: int = 0
-    steps: list = field(default_factory=list)
-
-
-class SpeculativeGenerator:
-    """engine/speculative/speculative_generator.py:21-90 over ``B200ModelRunner``."""
-
-    def __init__(self, runner: B200ModelRunner, proposer: "NgramProposer | DraftModelProposer", num_speculative_tokens: int,
-                 stop_token_ids: frozenset[int], device=None, metrics: SpeculativeCounters | None = None) -> None:
-        self._runner = runner
-        self._proposer = proposer
-        self._num_speculative_tokens = num_speculative_tokens
-        self._stop_token_ids = stop_token_ids
-        self._metrics = metrics
-
-    @property
-    def vocab_size(self) -> int:
-        return self._runner.vocab_size
-
-    def generate(self, request: GenerationRequest) -> Iterator[TokenEvent]:
-        sequence = Sequence.from_request(request)
-        try:
-            yield from self._generate(sequence)
-        finally:
-            self._runner.allocator.free(sequence)
-            self._proposer.release(sequence)
-
-    def _generate(self, sequence: Sequence) -> Iterator[TokenEvent]:
-        self._runner.allocator.reserve(sequence, sequence.num_tokens)
-        new_tokens = self._runner.run_step([sequence])
-        while True:
-            for token_id in new_tokens:
-                sequence.token_ids.append(token_id)
-                reason = find_finish_reason(token_id, sequence.num_generated_tokens, sequence.sampling_params,
-                                            self._stop_token_ids)
-                yield TokenEvent(sequence.request_id, token_id, reason is not None, reason)
-                if reason is not None:
-                    return
-            new_tokens = self._run_speculative_step(sequence)
-
-    def _run_speculative_step(self, sequence: Sequence) -> list[int]:
-        remaining = sequence.sampling_params.max_new_tokens - sequence.num_generated_tokens
-        num_guesses = max(0, min(self._num_speculative_tokens, remaining - 1))
-        proposal = self._proposer.propose(sequence, num_guesses) if num_guesses else Proposal([])
-        length_before = sequence.num_tokens
-        sequence.token_ids.extend(proposal.token_ids)
-        self._runner.allocator.reserve(sequence, sequence.num_tokens)
-        table = self._runner.allocator.block_table(sequence)
-        target_logits = self._runner.score_tokens(sequence, 1 + len(proposal.token_ids))
-        sampled = sequence.sampling_params.temperature != GREEDY_TEMPERATURE
-        new_tokens = verify_proposal(proposal, target_logits, sequence.sampling_params, sequence.sampling_generator,
-                                     target_argmax=None if sampled else self._runner.last_argmax)
-        num_kept = len(new_tokens) - 1
-        del sequence.token_ids[length_before:]
-        sequence.num_cached_tokens = length_before + num_kept
-        if self._metrics is not None:
-            self._metrics.proposed += len(proposal.token_ids)
-            self._metrics.accepted += num_kept
-            self._metrics.steps.append((list(proposal.token_ids), table, target_logits, list(new_tokens)))
-        return new_tokens

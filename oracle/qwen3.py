@@ -191,7 +191,8 @@ def forward(weights, cfg, token_ids: torch.Tensor, ctx: StepContext | None, pool
         positions = torch.arange(token_ids.shape[1]).expand(token_ids.shape)
     else:
         positions = ctx.positions
-    cos, sin = rotary_tables(positions, cfg.head_dim, cfg.rope_theta, dtype)
+    # (tables from CPU positions; moved to the weights' device when they live on a GPU)
+    cos, sin = (t.to(hidden.device) for t in rotary_tables(positions.cpu(), cfg.head_dim, cfg.rope_theta, dtype))
     b, q, _ = hidden.shape
     nh, nkv, d = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
     for layer in range(cfg.num_hidden_layers):

@@ -26,6 +26,17 @@ Fixtures written (all small):
                              against it (rejection sampling with the draft's rows)
 * ``spec_config1_fp32.pt``   BASELINE config 1 exactly (Qwen3-0.6B fp32, seed 0, 64-token motif
                              prompt, 128 greedy tokens, n=3, k=4, 16-token blocks)
+* ``spec_full_bf16.pt``      the benchmarked shape: Qwen3-0.6B (28 layers, vocab 151,936) in bf16,
+                             config 1's prompt and two config-2 short_chat prompts, 40 greedy
+                             tokens each, n=3, k=4
+* ``spec_full_int8.pt``      the same model with int8 weights and int8 KV (config 3's arithmetic),
+                             k=8
+* ``spec_small_stop_draft.pt`` / ``spec_small_stop.pt`` / ``spec_small_stop_sampled.pt``
+                             stop tokens (tests/engine/test_speculative_decoding.py:100-112): with
+                             the target as its own draft the stop id is a token the stop-free run
+                             emits as a KEPT GUESS in the middle of one step's accepted run, so
+                             the step must be cut there; the n-gram runs (greedy, sampled) stop
+                             at a token's first appearance
 """
 
 from __future__ import annotations
@@ -236,6 +247,10 @@ def spec_run(ref: Ref, inj: UniformInjector, cfg, weights, dtype, prompts, *, ma
             current["prefill_table"] = allocator.block_table(sequences[0])
             return super().run_step(sequences, token_counts)
 
+        def _sample(self, logits, sequences):  # the prefill's last-row logits (the first token's row)
+            current["prefill_logits"] = digest(logits, ids)
+            return super()._sample(logits, sequences)
+
         def score_tokens(self, sequence, token_count):
             table = allocator.block_table(sequence)
             logits = super().score_tokens(sequence, token_count)
@@ -297,6 +312,7 @@ def spec_run(ref: Ref, inj: UniformInjector, cfg, weights, dtype, prompts, *, ma
                 "tokens": [e.token_id for e in events],
                 "finish_reason": events[-1].finish_reason,
                 "prefill_block_table": current["prefill_table"],
+                "prefill_logits": current.get("prefill_logits"),
                 "steps": current["steps"],
                 "seed": seed,
                 "free_blocks_after": allocator.num_free_blocks,
@@ -311,16 +327,75 @@ def spec_run(ref: Ref, inj: UniformInjector, cfg, weights, dtype, prompts, *, ma
             "proposer": "ngram" if draft is None else "draft"}
 
 
+def pick_stop_token(run: dict, mid_run: bool) -> tuple[int, int] | None:
+    """(record index, token) such that the token first appears in that record's output at a step
+    after the prefill, with ``mid_run`` as a kept guess that has more tokens after it in the same
+    step (the step must be cut), else anywhere in a step's tokens."""
+    for index, record in enumerate(run["records"]):
+        seen = set(record["tokens"][:1])  # the prefill's first token
+        for step in record["steps"]:
+            new = step["new_tokens"]
+            for j, token in enumerate(new):
+                if token not in seen and (not mid_run or j < len(new) - 1):
+                    return index, token
+                seen.add(token)
+    return None
+
+
+def stop_fixtures(ref: Ref, inj: UniformInjector, pkg) -> None:
+    """Random-init greedy output collapses to one repeated token, so an n-gram guess is kept only
+    once that token has appeared already: a mid-run cut needs guesses the target keeps while its
+    output still changes, which a draft model equal to the target gives (every guess kept). The
+    n-gram runs stop at a token's first appearance wherever it falls in its step."""
+    cfg = pkg.SMALL_TEST
+    weights = pkg.make_weights(cfg, seed=0)
+    prompts = [pkg.make_prompt(cfg.vocab_size, 48, 0, True), pkg.make_prompt(cfg.vocab_size, 40, 1, False),
+               pkg.make_prompt(cfg.vocab_size, 33, 2, True)]
+    common = dict(max_new=40, k=4, max_ngram=3, num_blocks=64)
+    cases = (("spec_small_stop_draft.pt", True, dict(draft=(cfg, weights))),
+             ("spec_small_stop.pt", False, {}),
+             ("spec_small_stop_sampled.pt", False, dict(temperature=0.8, top_p=0.95, seeds=[11, 12, 13])))
+    for name, mid_run, extra in cases:
+        free = spec_run(ref, inj, cfg, weights, torch.bfloat16, prompts, **common, **extra)
+        pick = pick_stop_token(free, mid_run)
+        if pick is None:
+            raise RuntimeError(f"{name}: no token to stop on")
+        index, token = pick
+        run = spec_run(ref, inj, cfg, weights, torch.bfloat16, prompts, stop_ids=frozenset({token}), **common, **extra)
+        assert run["records"][index]["finish_reason"] == "stop", run["records"][index]["finish_reason"]
+        run["stop_ids"] = [token]
+        run["stop_record"] = index
+        torch.save(run, HERE / name)
+        print(name, "stop", token, "record", index, "tokens", run["records"][index]["tokens"][:12], flush=True)
+
+
+def full_fixtures(ref: Ref, inj: UniformInjector, pkg) -> None:
+    full = pkg.QWEN3_0_6B
+    weights = pkg.make_weights(full, seed=0)
+    short_chat = pkg.make_prompts(3, full.vocab_size, 64, seed=0)  # user 0 is config 1's prompt
+    torch.save(spec_run(ref, inj, full, weights, torch.bfloat16, short_chat, max_new=40, k=4, max_ngram=3,
+                        num_blocks=32), HERE / "spec_full_bf16.pt")
+    torch.save(spec_run(ref, inj, full, weights, torch.bfloat16, short_chat, max_new=40, k=8, max_ngram=3,
+                        num_blocks=32, int8=True), HERE / "spec_full_int8.pt")
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, help="the reference's nanoengine/src directory")
     parser.add_argument("--skip-full", action="store_true", help="skip the Qwen3-0.6B config-1 run")
     parser.add_argument("--only-draft", action="store_true", help="write only the draft-model fixtures")
+    parser.add_argument("--only", choices=("stop", "full"), help="write only the stop-token or full-shape fixtures")
     args = parser.parse_args()
     torch.set_num_threads(max(1, torch.get_num_threads()))
     ref = Ref(args.reference)
     inj = UniformInjector(ref)
     pkg = importlib.import_module("inference-engine-from-scratch_b200")
+    if args.only == "stop":
+        stop_fixtures(ref, inj, pkg)
+        return
+    if args.only == "full":
+        full_fixtures(ref, inj, pkg)
+        return
 
     cfg = pkg.SMALL_TEST
     weights = pkg.make_weights(cfg, seed=0)
@@ -357,6 +432,8 @@ def main() -> None:
         prompt = pkg.make_prompt(full.vocab_size, 64, 0, True)
         torch.save(spec_run(ref, inj, full, weights, torch.float32, [prompt], max_new=128, k=4,
                             max_ngram=3, num_blocks=64), HERE / "spec_config1_fp32.pt")
+        full_fixtures(ref, inj, pkg)
+    stop_fixtures(ref, inj, pkg)
 
 
 if __name__ == "__main__":

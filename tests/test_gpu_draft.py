@@ -16,6 +16,7 @@ from __future__ import annotations
 import pytest
 import torch
 
+from tests import reference_seam as seam
 from tests.conftest import load_golden, package, submodule
 
 pytestmark = pytest.mark.gpu
@@ -53,16 +54,16 @@ def test_serial_drop_in_with_a_draft_model(models, same) -> None:
     draft_model = twin if same else draft
     serial = submodule("serial")
     golden = load_golden("spec_small_draft_same_bf16.pt" if same else "spec_small_draft_bf16.pt")
-    allocator = serial.PagedSlotAllocator(golden["num_blocks"], 16)
+    allocator = seam.PagedSlotAllocator(golden["num_blocks"], 16)
     runner = serial.B200ModelRunner(target, allocator)
-    draft_runner = serial.B200ModelRunner(draft_model, serial.PagedSlotAllocator(golden["num_blocks"], 16))
+    draft_runner = serial.B200ModelRunner(draft_model, seam.PagedSlotAllocator(golden["num_blocks"], 16))
     proposer = serial.DraftModelProposer(draft_runner, "cuda:0")
     excused = 0
     for index, record in enumerate(golden["records"]):
-        counters = serial.SpeculativeCounters()
-        gen = serial.SpeculativeGenerator(runner, proposer, golden["k"], frozenset(), metrics=counters)
-        params = serial.SamplingParams(max_new_tokens=golden["max_new"], ignore_eos=True)
-        events = list(gen.generate(serial.GenerationRequest(f"r{index}", record["prompt"], params)))
+        counters = seam.StepRecords()
+        gen = seam.SpeculativeGenerator(runner, proposer, golden["k"], frozenset(), metrics=counters)
+        params = seam.SamplingParams(max_new_tokens=golden["max_new"], ignore_eos=True)
+        events = list(gen.generate(seam.GenerationRequest(f"r{index}", record["prompt"], params)))
         # greedy speculation emits the target's own greedy tokens, whatever the drafts
         assert [e.token_id for e in events] == record["tokens"]
         for (draft_ids, table, _, new_tokens), ref in zip(counters.steps, record["steps"]):

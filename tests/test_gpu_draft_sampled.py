@@ -18,6 +18,7 @@ import torch
 
 from oracle import philox
 from oracle import verify as overify
+from tests import reference_seam as seam
 from tests.conftest import load_golden, package, submodule
 
 pytestmark = pytest.mark.gpu
@@ -212,7 +213,7 @@ def test_serial_sampled_draft_model_replays_on_the_oracle() -> None:
             self.proposals = []
 
         def propose(self, sequence, num_tokens):
-            start = sequence.sampling_generator.draws
+            start = serial.philox_stream(sequence.sampling_generator).draws
             prop = super().propose(sequence, num_tokens)
             self.proposals.append((prop, start))
             return prop
@@ -222,13 +223,13 @@ def test_serial_sampled_draft_model_replays_on_the_oracle() -> None:
     for index, record in enumerate(golden["records"]):
         runs = []
         for _ in range(2):
-            runner = serial.B200ModelRunner(target, serial.PagedSlotAllocator(golden["num_blocks"], 16))
-            proposer = Recording(serial.B200ModelRunner(draft_model, serial.PagedSlotAllocator(golden["num_blocks"], 16)))
-            counters = serial.SpeculativeCounters()
-            gen = serial.SpeculativeGenerator(runner, proposer, golden["k"], frozenset(), metrics=counters)
-            params = serial.SamplingParams(max_new_tokens=golden["max_new"], temperature=T, top_p=P,
+            runner = serial.B200ModelRunner(target, seam.PagedSlotAllocator(golden["num_blocks"], 16))
+            proposer = Recording(serial.B200ModelRunner(draft_model, seam.PagedSlotAllocator(golden["num_blocks"], 16)))
+            counters = seam.StepRecords()
+            gen = seam.SpeculativeGenerator(runner, proposer, golden["k"], frozenset(), metrics=counters)
+            params = seam.SamplingParams(max_new_tokens=golden["max_new"], temperature=T, top_p=P,
                                            seed=record["seed"], ignore_eos=True)
-            tokens = [e.token_id for e in gen.generate(serial.GenerationRequest(f"r{index}", record["prompt"], params))]
+            tokens = [e.token_id for e in gen.generate(seam.GenerationRequest(f"r{index}", record["prompt"], params))]
             runs.append((tokens, counters.steps, proposer.proposals))
         assert runs[0][0] == runs[1][0]
         tokens, steps, proposals = runs[0]

@@ -14,6 +14,7 @@ import pytest
 import torch
 
 from oracle import speculative as ospec
+from tests import reference_seam as seam
 from tests.conftest import load_golden, package, submodule
 
 pytestmark = pytest.mark.gpu
@@ -57,14 +58,14 @@ def test_serial_drop_in_matches_the_reference_step_by_step(small, small_int8, va
     golden = load_golden(f"spec_small_{variant}.pt")
     assert golden["int8"] == (variant == "int8")
     ids = golden["digest_ids"]
-    allocator = serial.PagedSlotAllocator(golden["num_blocks"], 16)
+    allocator = seam.PagedSlotAllocator(golden["num_blocks"], 16)
     runner = serial.B200ModelRunner(model, allocator)
     proposer = serial.NgramProposer(golden["max_ngram"], max_model_len=256, device="cuda:0")
     for index, record in enumerate(golden["records"]):
-        counters = serial.SpeculativeCounters()
-        gen = serial.SpeculativeGenerator(runner, proposer, golden["k"], frozenset(), metrics=counters)
-        params = serial.SamplingParams(max_new_tokens=golden["max_new"], ignore_eos=True)
-        events = list(gen.generate(serial.GenerationRequest(f"r{index}", record["prompt"], params)))
+        counters = seam.StepRecords()
+        gen = seam.SpeculativeGenerator(runner, proposer, golden["k"], frozenset(), metrics=counters)
+        params = seam.SamplingParams(max_new_tokens=golden["max_new"], ignore_eos=True)
+        events = list(gen.generate(seam.GenerationRequest(f"r{index}", record["prompt"], params)))
         assert [e.token_id for e in events] == record["tokens"]
         assert len(counters.steps) == len(record["steps"])
         for (draft, table, logits, new_tokens), ref in zip(counters.steps, record["steps"]):
@@ -154,11 +155,11 @@ def test_verify_with_full_length_drafts_matches_the_oracle(small) -> None:
     serial = submodule("serial")
     bf16 = {k: v.to(torch.bfloat16) for k, v in weights.items()}
     oracle_runner = ospec.OracleRunner(bf16, cfg, 64, 16, torch.bfloat16)
-    allocator = serial.PagedSlotAllocator(64, 16)
+    allocator = seam.PagedSlotAllocator(64, 16)
     runner = serial.B200ModelRunner(model, allocator)
     g = torch.Generator().manual_seed(3)
     prompt = torch.randint(0, cfg.vocab_size, (37,), generator=g).tolist()
-    mine = serial.Sequence.from_request(serial.GenerationRequest("a", prompt, serial.SamplingParams(64)))
+    mine = seam.Sequence.from_request(seam.GenerationRequest("a", prompt, seam.SamplingParams(64)))
     ref = ospec.Seq("a", list(prompt), len(prompt), 64)
     allocator.reserve(mine, mine.num_tokens)
     oracle_runner.tables.reserve("a", ref.num_tokens)

@@ -23,6 +23,7 @@ import torch
 from oracle import ngram as ongram
 from oracle import philox
 from oracle import verify as overify
+from tests import reference_seam as seam
 from tests.conftest import load_golden, package, submodule
 
 pytestmark = pytest.mark.gpu
@@ -375,13 +376,13 @@ def test_serial_sampled_generation_is_reproducible_and_replays_on_the_oracle(sma
     prompt = pkg.make_prompts(1, cfg.vocab_size, length=48, seed=9)[0]
     runs = []
     for _ in range(2):
-        allocator = serial.PagedSlotAllocator(64, 16)
+        allocator = seam.PagedSlotAllocator(64, 16)
         runner = serial.B200ModelRunner(model, allocator)
         proposer = serial.NgramProposer(3, max_model_len=256, device="cuda:0")
-        counters = serial.SpeculativeCounters()
-        gen = serial.SpeculativeGenerator(runner, proposer, 4, frozenset(), metrics=counters)
-        params = serial.SamplingParams(max_new_tokens=32, temperature=0.8, top_p=0.95, seed=42, ignore_eos=True)
-        tokens = [e.token_id for e in gen.generate(serial.GenerationRequest("r", prompt, params))]
+        counters = seam.StepRecords()
+        gen = seam.SpeculativeGenerator(runner, proposer, 4, frozenset(), metrics=counters)
+        params = seam.SamplingParams(max_new_tokens=32, temperature=0.8, top_p=0.95, seed=42, ignore_eos=True)
+        tokens = [e.token_id for e in gen.generate(seam.GenerationRequest("r", prompt, params))]
         runs.append((tokens, counters.steps))
     assert runs[0][0] == runs[1][0]
     assert len(runs[0][0]) == 32
