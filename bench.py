@@ -522,6 +522,10 @@ def algorithmic_bytes(kind: str, cfg, M: int, ctx_sum: int, kv_bytes_per_token_l
         return V * H * 2 + M * H * 2 + M * 8
     if kind == "attention":
         return ctx_sum * kv_bytes_per_token_layer + 2 * M * q * 2
+    if kind == "step":  # the persistent kernel: every layer's projections, attention and the LM head
+        layer = sum(algorithmic_bytes(k, cfg, M, ctx_sum, kv_bytes_per_token_layer, wb)
+                    for k in ("gemm_qkv", "attention", "gemm_o", "gemm_gateup", "gemm_down"))
+        return cfg.num_hidden_layers * layer + algorithmic_bytes("lm_head", cfg, M, ctx_sum, kv_bytes_per_token_layer)
     return 0.0
 
 

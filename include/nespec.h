@@ -41,7 +41,7 @@ extern "C" {
 #define NE_DEV_HISTORY_FULL 16  /* a sequence outgrew its history row or block-table row */
 #define NE_DEV_NO_SAMPLER 32    /* temperature > 0 on a model without a sampling buffer */
 
-#define NE_ABI_VERSION 2
+#define NE_ABI_VERSION 3
 
 NE_API int ne_abi_version(void);
 NE_API const char* ne_status_string(int status);
@@ -408,10 +408,25 @@ NE_API int ne_model_tp_exchange_open(ne_model* model, const void* ipc_handles);
 #define NE_K_OTHER 11
 #define NE_K_SAMPLE 12       /* per-row softmax / top-p statistics of sampled sequences */
 #define NE_K_COLLECTIVE 13   /* NCCL all-reduce (tensor parallelism; not counted as a launch of ours) */
-#define NE_NUM_KINDS 14
+#define NE_K_STEP 14         /* the persistent verify-step kernel: every layer and the LM head in one launch */
+#define NE_NUM_KINDS 15
 
 /* Kernels this model has launched so far (every entry point that takes the model counts). */
 NE_API long long ne_model_launch_count(const ne_model* model);
+/*
+ * Where the persistent step kernel's last launch gave up, if a bounded wait ran out
+ * (NE_DEV_TIMEOUT): out[0..6] = recorded, site (1 counter, 2 mbarrier), which, target, seen, CTA,
+ * warp; zeros otherwise. For diagnosis (no counterpart in the reference).
+ */
+NE_API int ne_model_step_wait_record(const ne_model* model, int32_t* out, int n);
+/*
+ * Timeline of the persistent step kernel, for diagnosis (no counterpart in the reference): with a
+ * caller-owned device buffer of ne_model_step_trace_bytes() bytes set, every later step kernel
+ * launch zeroes it and writes %globaltimer stamps [CTA][phase][8] (phases: 5 per layer -- QKV,
+ * attention, o_proj, gate/up, down -- then final norm, LM head). NULL turns it off.
+ */
+NE_API size_t ne_model_step_trace_bytes(const ne_model* model);
+NE_API int ne_model_set_step_trace(ne_model* model, void* buffer, size_t bytes);
 /*
  * Time every kernel the model launches on ``stream`` between begin and end with CUDA events.
  * Eagerly, or inside a stream capture: the events then become event-record nodes of the graph,

@@ -32,6 +32,9 @@ TP_HANDLE_BYTES = 64  # NE_TP_HANDLE_BYTES (CUDA IPC handle)
 
 EXPORTS = {
     "ne_abi_version": (c_int, []),
+    "ne_model_step_wait_record": (c_int, [c_void_p, c_void_p, c_int]),
+    "ne_model_step_trace_bytes": (c_size_t, [c_void_p]),
+    "ne_model_set_step_trace": (c_int, [c_void_p, c_void_p, c_size_t]),
     "ne_status_string": (ctypes.c_char_p, [c_int]),
     "ne_read_status": (c_int, [c_void_p, c_int, POINTER(c_int32), c_void_p]),
     "ne_model_create": (c_int, [c_void_p, POINTER(c_void_p)]),
@@ -90,7 +93,7 @@ EXPORTS = {
 }
 
 KERNEL_KINDS = ("embed", "rmsnorm", "gemm_qkv", "attention", "gemm_o", "gemm_gateup", "gemm_down", "lm_head",
-                "ngram", "plan", "accept", "other", "sample", "collective")
+                "ngram", "plan", "accept", "other", "sample", "collective", "step")
 
 
 class ModelConfig(ctypes.Structure):

@@ -10,6 +10,7 @@
 #include "gemm_tc.cuh"
 #include "kernels.cuh"
 #include "sampling.cuh"
+#include "step_kernel.cuh"
 #include "tp.cuh"
 
 using ne::GemmParams;
@@ -57,6 +58,14 @@ struct ne_model {
   CUtensorMap tm_h{};        // the residual rows as a GEMM X operand (RMSNorm fused into the GEMM)
   CUtensorMap tm_x{}, tm_attn{}, tm_act{};
   int num_sms = 148;
+  // the persistent step kernel (step_kernel.cu): its cut of the projections, split-K partial areas,
+  // counters, per-layer pointers (workspace) and tensor maps (a kernel parameter)
+  ne::SkParams sk{};         // shapes and pointers fixed at workspace binding
+  ne::SkMaps sk_maps{};
+  bool sk_ready = false;
+  int sk_rows = 0;           // rows the partial areas hold
+  size_t sk_sync_bytes = 0;
+  unsigned long long* sk_trace = nullptr;  // optional timeline buffer (caller's memory)
   // launch accounting / profiling
   long long launches = 0;
   bool profiling = false;
@@ -88,10 +97,33 @@ size_t sampling_logits_bytes(const ne_model_config& c, int rows) {
 size_t split_rows_cap(int R) { return (size_t)ne::GEMM_MAX_SPLITS * std::min(R, 1536); }
 
 struct Layout {
-  size_t status, h, x, q, attn, act, keys, rows_i32, seqs_i32, scalars, attn_scratch, partial, split, ssq, total;
+  size_t status, h, x, q, attn, act, keys, rows_i32, seqs_i32, scalars, attn_scratch, partial, split, ssq;
+  size_t sk_part, sk_sync, sk_desc;  // persistent step kernel (0 bytes when it cannot run)
+  size_t sk_part_bytes, sk_sync_bytes, sk_desc_bytes;
+  size_t total;
 };
 
-Layout workspace_layout(const ne_model_config& c, int R, int B, int tp_world) {
+// The persistent step kernel's cut for this model on ``num_sms`` CTAs (no pointers yet).
+ne::SkParams step_shape(const ne_model_config& c, int num_sms) {
+  ne::SkParams p{};
+  p.L = c.num_layers;
+  p.H = c.hidden_size;
+  p.I = c.intermediate_size;
+  p.nh = c.num_heads;
+  p.nkv = c.num_kv_heads;
+  p.grid = num_sms;
+  p.eps = c.rms_norm_eps;
+  ne::step_plan_cuts(p, c.lm_rows);
+  return p;
+}
+
+// It serves unsplit bf16 models (weights and KV) with a whole LM head.
+bool step_kernel_supported(const ne_model_config& c, int tp_world) {
+  return tp_world == 1 && !c.kv_int8 && !c.weight_int8 && c.lm_offset == 0 && c.lm_rows == c.vocab_size &&
+         c.num_layers <= ne::SK_MAX_LAYERS && c.hidden_size % 128 == 0 && c.intermediate_size % 64 == 0;
+}
+
+Layout workspace_layout(const ne_model_config& c, int R, int B, int tp_world, int num_sms) {
   Layout l{};
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -114,6 +146,16 @@ Layout workspace_layout(const ne_model_config& c, int R, int B, int tp_world) {
   l.partial = tp_world > 1 ? take((size_t)R * c.hidden_size * 4) : 0;
   l.split = tp_world > 1 ? 0 : take(split_rows_cap(R) * c.hidden_size * 4);
   l.ssq = take((size_t)R * (c.hidden_size / 128) * 4);
+  if (step_kernel_supported(c, tp_world)) {
+    const ne::SkParams sp = step_shape(c, num_sms);
+    const int rows = std::min(R, ne::SK_MAX_ROWS);
+    l.sk_part_bytes = ne::step_partial_bytes(ne::step_max_units(sp), rows);
+    l.sk_sync_bytes = ne::step_sync_ints(sp.L, sp.max_stripes, sp.nkv) * sizeof(int);
+    l.sk_desc_bytes = (size_t)sp.L * sizeof(ne::SkLayer);
+    l.sk_part = take(2 * l.sk_part_bytes);
+    l.sk_sync = take(l.sk_sync_bytes);
+    l.sk_desc = take(l.sk_desc_bytes);
+  }
   l.total = off;
   return l;
 }
@@ -236,6 +278,102 @@ int residual_gemm(ne_model* m, const CUtensorMap* tw, const CUtensorMap* tx, int
   return run_gemm(m, tw, tx, R, M_dev, N, K, e, stream, w_scale);
 }
 
+// The step kernel's tensor maps ([4 L weight maps | LM head | X maps over h, attn, act, x], a kernel
+// parameter) and its per-layer pointers, copied once into the workspace.
+int upload_step_descriptors(ne_model* m) {
+  m->sk_ready = false;
+  if (!m->ws || !m->head_set || !m->sk.layers) return NE_OK;
+  for (char set : m->layer_set)
+    if (!set) return NE_OK;
+  const int L = m->cfg.num_layers;
+  CUtensorMap* maps = m->sk_maps.m;
+  std::vector<ne::SkLayer> layers(L);
+  for (int l = 0; l < L; ++l) {
+    maps[4 * l + 0] = m->tm_qkv[l];
+    maps[4 * l + 1] = m->tm_o[l];
+    maps[4 * l + 2] = m->tm_gateup[l];
+    maps[4 * l + 3] = m->tm_down[l];
+    const ne_layer_weights& w = m->layers[l];
+    layers[l] = ne::SkLayer{static_cast<const __nv_bfloat16*>(w.ln_in), static_cast<const __nv_bfloat16*>(w.ln_post),
+                            static_cast<const __nv_bfloat16*>(w.q_norm), static_cast<const __nv_bfloat16*>(w.k_norm),
+                            static_cast<__nv_bfloat16*>(w.k_cache), static_cast<__nv_bfloat16*>(w.v_cache)};
+  }
+  maps[4 * L] = m->tm_lm;
+  maps[4 * L + 1] = m->tm_h;
+  maps[4 * L + 2] = m->tm_attn;
+  maps[4 * L + 3] = m->tm_act;
+  maps[4 * L + 4] = m->tm_x;
+  if (cudaMemcpy(const_cast<ne::SkLayer*>(m->sk.layers), layers.data(), layers.size() * sizeof(ne::SkLayer),
+                 cudaMemcpyHostToDevice) != cudaSuccess)
+    return NE_ERR_CUDA;
+  m->sk_ready = true;
+  return NE_OK;
+}
+
+// NE_STEP_KERNEL=1 runs eligible verify steps as the persistent kernel; otherwise (the default,
+// while it measures slower than the per-projection launches) every step launches kernel by
+// kernel. Read at every forward, so a process can compare the two.
+bool step_kernel_enabled() {
+  const char* v = getenv("NE_STEP_KERNEL");
+  return v && v[0] == '1';
+}
+
+// Whether this forward runs as the persistent step kernel: greedy (argmax) lm rows, rows within the
+// partial areas and the kernel's shared memory, at most 16 query vectors per (entry, KV head).
+bool use_step_kernel(const ne_model* m, const ne_rows* rows, int lm_mode) {
+  if (!m->sk_ready || !step_kernel_enabled() || lm_mode != NE_LM_ARGMAX || m->kv_shadow) return false;
+  const int G = m->cfg.num_heads / m->cfg.num_kv_heads;
+  int xs = 0, xsb = 0;
+  return rows->max_rows <= m->sk_rows && rows->lm_max <= rows->max_rows &&
+         std::max(1, rows->max_q_len) * G <= ne::SK_MAX_QVEC && rows->num_seqs >= 1 &&
+         ne::step_smem_bytes(rows->max_rows, &xs, &xsb) > 0;
+}
+
+int step_forward(ne_model* m, const ne_rows* rows, int32_t* argmax_out, cudaStream_t s) {
+  const ne_model_config& c = m->cfg;
+  const int R = rows->max_rows;
+  int rc = note(m, NE_K_EMBED,
+                ne::launch_embed(static_cast<const __nv_bfloat16*>(m->head.embed), rows->token_ids, rows->num_rows, R,
+                                 c.hidden_size, c.vocab_size, m->h, m->status, s, m->ssq), s);
+  if (rc) return rc;
+  if (cudaMemsetAsync(m->sk.sync, 0, m->sk_sync_bytes, s) != cudaSuccess) return NE_ERR_CUDA;
+  ne::SkParams p = m->sk;
+  p.R_max = R;
+  p.num_seqs = rows->num_seqs;
+  ne::step_smem_bytes(R, &p.x_stages, &p.x_stage_bytes);
+  p.num_rows = rows->num_rows;
+  p.positions = rows->positions;
+  p.slot_mapping = rows->slot_mapping;
+  p.q_start = rows->q_start;
+  p.q_len = rows->q_len;
+  p.block_tables = rows->block_tables;
+  p.table_index = rows->table_index;
+  p.table_stride = rows->block_table_stride;
+  p.lm_rows = rows->lm_rows;
+  p.lm_count = rows->lm_count;
+  p.num_cache_slots = c.num_cache_slots;
+  p.max_positions = c.max_positions;
+  p.h = m->h;
+  p.ssq = m->ssq;
+  p.q = m->q;
+  p.attn = m->attn;
+  p.act = m->act;
+  p.x_lm = m->x;
+  p.keys = m->keys;
+  p.status = m->status;
+  p.rope_cos = static_cast<const __nv_bfloat16*>(m->head.rope_cos);
+  p.rope_sin = static_cast<const __nv_bfloat16*>(m->head.rope_sin);
+  p.final_norm = static_cast<const __nv_bfloat16*>(m->head.final_norm);
+  p.lm_index_offset = c.lm_offset;
+  p.trace = m->sk_trace;
+  if (p.trace && cudaMemsetAsync(p.trace, 0, ne::step_trace_bytes(p.grid, p.L), s) != cudaSuccess) return NE_ERR_CUDA;
+  rc = note(m, NE_K_STEP, ne::launch_step_kernel(m->sk_maps, p, s), s);
+  if (rc) return rc;
+  if (argmax_out)
+    rc = note(m, NE_K_OTHER, ne::launch_keys_to_ids(m->keys, rows->lm_count, rows->lm_max, argmax_out, s), s);
+  return rc;
+}
+
 ne_rows make_step_rows(ne_model* m, const ne_batch_state* st, const int32_t* seq_slot, int num_seqs, int max_rows,
                        int lm_max, int max_q_len) {
   ne_rows r{};
@@ -342,7 +480,7 @@ int ne_model_set_layer(ne_model* m, int layer, const ne_layer_weights* w) {
     stored.w_qkv_scale = stored.w_o_scale = stored.w_gateup_scale = stored.w_down_scale = nullptr;
   }
   m->layer_set[layer] = 1;
-  return NE_OK;
+  return m->ws ? upload_step_descriptors(m) : NE_OK;
 }
 
 int ne_model_set_head(ne_model* m, const ne_head_weights* hw) {
@@ -352,19 +490,19 @@ int ne_model_set_head(ne_model* m, const ne_head_weights* hw) {
     return NE_ERR_INVALID;
   m->head = *hw;
   m->head_set = true;
-  return NE_OK;
+  return m->ws ? upload_step_descriptors(m) : NE_OK;
 }
 
 int ne_model_workspace_bytes(const ne_model* m, int max_rows, int max_seqs, size_t* bytes) {
   if (!m || !bytes || max_rows <= 0 || max_seqs <= 0 || max_seqs > 1024) return NE_ERR_INVALID;
-  *bytes = workspace_layout(m->cfg, max_rows, max_seqs, m->tp_world).total;
+  *bytes = workspace_layout(m->cfg, max_rows, max_seqs, m->tp_world, m->num_sms).total;
   return NE_OK;
 }
 
 int ne_model_set_workspace(ne_model* m, void* ws, size_t bytes, int max_rows, int max_seqs) {
   if (!m || !ws || max_rows <= 0 || max_seqs <= 0 || max_seqs > 1024) return NE_ERR_INVALID;
   if (reinterpret_cast<uintptr_t>(ws) & 255u) return NE_ERR_INVALID;
-  Layout l = workspace_layout(m->cfg, max_rows, max_seqs, m->tp_world);
+  Layout l = workspace_layout(m->cfg, max_rows, max_seqs, m->tp_world, m->num_sms);
   if (bytes < l.total) return NE_ERR_WORKSPACE;
   const ne_model_config& c = m->cfg;
   char* base = static_cast<char*>(ws);
@@ -405,6 +543,19 @@ int ne_model_set_workspace(ne_model* m, void* ws, size_t bytes, int max_rows, in
             ne::make_tmap_bf16(&m->tm_act, m->act, max_rows, c.intermediate_size, ne::GEMM_XBOX, ne::GEMM_BK);
   if (!ok) return NE_ERR_INVALID;
   if (cudaMemset(ws, 0, l.total) != cudaSuccess) return NE_ERR_CUDA;
+  m->sk_ready = false;
+  if (l.sk_desc_bytes > 0) {
+    ne::SkParams& sp = m->sk;
+    sp = step_shape(c, m->num_sms);
+    m->sk_rows = std::min(max_rows, ne::SK_MAX_ROWS);
+    m->sk_sync_bytes = l.sk_sync_bytes;
+    sp.part[0] = reinterpret_cast<float*>(base + l.sk_part);
+    sp.part[1] = reinterpret_cast<float*>(base + l.sk_part + l.sk_part_bytes);
+    sp.sync = reinterpret_cast<int*>(base + l.sk_sync);
+    sp.layers = reinterpret_cast<const ne::SkLayer*>(base + l.sk_desc);
+    const int rc = upload_step_descriptors(m);
+    if (rc != NE_OK) return rc;
+  }
   return NE_OK;
 }
 
@@ -526,6 +677,7 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
   if (lm_mode == NE_LM_LOGITS && !logits) return NE_ERR_INVALID;
   const bool tp = m->tp_world > 1;
   if (tp && lm_mode == NE_LM_LOGITS) return NE_ERR_UNSUPPORTED;  // logits are split over the ranks
+  if (use_step_kernel(m, rows, lm_mode)) return step_forward(m, rows, argmax_out, as_stream(stream));
   // a split model exchanges partial rows through peer memory when they fit the exchange slots
   // (every rank takes the same branch: R and lm_max are the same host values on all ranks)
   const bool px = tp && m->link.world > 0 && R <= m->link.max_rows && rows->lm_max <= m->link.max_rows;
@@ -685,6 +837,30 @@ int ne_forward(ne_model* m, const ne_rows* rows, int lm_mode, void* logits, int3
 }
 
 long long ne_model_launch_count(const ne_model* m) { return m ? m->launches : -1; }
+
+size_t ne_model_step_trace_bytes(const ne_model* m) {
+  return m && m->sk_ready ? ne::step_trace_bytes(m->sk.grid, m->sk.L) : 0;
+}
+
+int ne_model_set_step_trace(ne_model* m, void* buffer, size_t bytes) {
+  if (!m) return NE_ERR_INVALID;
+  if (buffer && (!m->sk_ready || bytes < ne::step_trace_bytes(m->sk.grid, m->sk.L) ||
+                 (reinterpret_cast<uintptr_t>(buffer) & 7u)))
+    return NE_ERR_INVALID;
+  m->sk_trace = static_cast<unsigned long long*>(buffer);
+  return NE_OK;
+}
+
+int ne_model_step_wait_record(const ne_model* m, int32_t* out, int n) {
+  if (!m || !out || n < ne::SK_RECORD_INTS) return NE_ERR_INVALID;
+  if (!m->sk_ready || m->sk_sync_bytes < ne::SK_RECORD_INTS * sizeof(int)) {
+    for (int i = 0; i < ne::SK_RECORD_INTS; ++i) out[i] = 0;
+    return NE_OK;
+  }
+  const char* rec = reinterpret_cast<const char*>(m->sk.sync) + m->sk_sync_bytes - ne::SK_RECORD_INTS * sizeof(int);
+  return cudaMemcpy(out, rec, ne::SK_RECORD_INTS * sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess ? NE_OK
+                                                                                                  : NE_ERR_CUDA;
+}
 
 int ne_model_profile_begin(ne_model* m, void* stream) {
   if (!m) return NE_ERR_INVALID;
