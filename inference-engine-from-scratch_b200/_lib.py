@@ -13,6 +13,7 @@ from pathlib import Path
 import torch
 
 LIBRARY_PATH = Path(__file__).resolve().parent / "libnespec.so"
+ABI_VERSION = 3  # NE_ABI_VERSION of include/nespec.h
 
 NE_OK = 0
 NE_LM_NONE, NE_LM_ARGMAX, NE_LM_LOGITS = 0, 1, 2

@@ -857,7 +857,9 @@ int ne_model_step_wait_record(const ne_model* m, int32_t* out, int n) {
     for (int i = 0; i < ne::SK_RECORD_INTS; ++i) out[i] = 0;
     return NE_OK;
   }
-  const char* rec = reinterpret_cast<const char*>(m->sk.sync) + m->sk_sync_bytes - ne::SK_RECORD_INTS * sizeof(int);
+  const ne::SkParams& sp = m->sk;
+  const size_t line = (size_t)2 * sp.L * 4 * sp.max_stripes + (size_t)sp.L * sp.nkv + 2;  // the record's line
+  const char* rec = reinterpret_cast<const char*>(m->sk.sync) + line * ne::SK_LINE * sizeof(int);
   return cudaMemcpy(out, rec, ne::SK_RECORD_INTS * sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess ? NE_OK
                                                                                                   : NE_ERR_CUDA;
 }

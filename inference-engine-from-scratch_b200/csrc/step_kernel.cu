@@ -47,6 +47,8 @@ constexpr int WORK_BYTES = NCW * ATT_WARP + NCW * 16 * 2 * 4;
 constexpr int QTILE_BYTES = 16 * 256;
 constexpr int CHUNK_ROWS = 64;         // rows per epilogue chunk (32 KB of fp32 staging)
 constexpr float LOG2E = 1.4426950408889634f;
+constexpr int SK_META_UNITS = 8;   // attention pairs per CTA whose metadata is kept in shared memory
+constexpr int SK_META_BLOCKS = 16; // context blocks per pair kept (256 tokens); later ones read the table
 #define SK_NEG_INF (-__int_as_float(0x7f800000))
 
 // ------------------------------------------------------------------ memory-model helpers
@@ -97,16 +99,24 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
   return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u));
 }
 
+// One (entry, KV head) attention pair's step metadata: the same in every layer.
+struct AttnMeta {
+  int b, kvh, ql, r0, nvec, ctx, nblk, first_new;  // first_new: position of the entry's first new row
+  int qpos[16];                                    // each query vector's position (-1: padding)
+  int blocks[SK_META_BLOCKS];                      // block table entries (-1: beyond the context)
+};
+
 // ------------------------------------------------------------------ counters
 struct Sync {
   int* base;
   int L, maxs, nkv;
-  __device__ int* arrive(int l, int kind, int s) const { return base + (l * 4 + kind) * maxs + s; }
-  __device__ int* done(int l, int kind, int s) const { return base + L * 4 * maxs + (l * 4 + kind) * maxs + s; }
-  __device__ int* head(int l, int h) const { return base + 2 * L * 4 * maxs + l * nkv + h; }
-  __device__ int* final_rows() const { return base + 2 * L * 4 * maxs + L * nkv; }
-  __device__ int* abort_flag() const { return final_rows() + 1; }
-  __device__ int* record() const { return final_rows() + 2; }
+  __device__ int* at(int i) const { return base + i * SK_LINE; }
+  __device__ int* arrive(int l, int kind, int s) const { return at((l * 4 + kind) * maxs + s); }
+  __device__ int* done(int l, int kind, int s) const { return at(L * 4 * maxs + (l * 4 + kind) * maxs + s); }
+  __device__ int* head(int l, int h) const { return at(2 * L * 4 * maxs + l * nkv + h); }
+  __device__ int* final_rows() const { return at(2 * L * 4 * maxs + L * nkv); }
+  __device__ int* abort_flag() const { return at(2 * L * 4 * maxs + L * nkv + 1); }
+  __device__ int* record() const { return at(2 * L * 4 * maxs + L * nkv + 2); }
   // the first wait of the launch that ran out says where it was
   __device__ void note_timeout(int site, int what, int target, int seen) const {
     int* r = record();
@@ -145,10 +155,10 @@ __device__ bool wait_counter(const int* addr, int target, const Sync& sy, int* s
   uint64_t start = 0;
   for (uint32_t it = 0;; ++it) {
     if (ld_acquire(addr) >= target) return true;
-    if ((it & 15u) == 15u &&
-        give_up(sy, status, abort_s, start, 1, (int)(addr - sy.base), target, ld_relaxed(addr)))
+    if ((it & 63u) == 63u &&
+        give_up(sy, status, abort_s, start, 1, (int)(addr - sy.base) / SK_LINE, target, ld_relaxed(addr)))
       return false;
-    __nanosleep(32);
+    __nanosleep(it < 8 ? 32 : 128);
   }
 }
 
@@ -168,7 +178,7 @@ __device__ bool wait_ranges(const Ranges& rg, int target, const Sync& sy, int* s
       for (int i = 0; i < rg.n[r]; i += 8) {
         int v[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = i + k < rg.n[r] ? ld_relaxed(rg.first[r] + i + k) : target;
+        for (int k = 0; k < 8; ++k) v[k] = i + k < rg.n[r] ? ld_relaxed(rg.first[r] + (i + k) * SK_LINE) : target;
 #pragma unroll
         for (int k = 0; k < 8; ++k) ok = ok && v[k] >= target;
       }
@@ -177,10 +187,10 @@ __device__ bool wait_ranges(const Ranges& rg, int target, const Sync& sy, int* s
       asm volatile("fence.acq_rel.gpu;" ::: "memory");
       return true;
     }
-    if ((it & 15u) == 15u &&
-        give_up(sy, status, abort_s, start, 1, (int)(rg.first[0] - sy.base), target, ld_relaxed(rg.first[0])))
+    if ((it & 63u) == 63u &&
+        give_up(sy, status, abort_s, start, 1, (int)(rg.first[0] - sy.base) / SK_LINE, target, ld_relaxed(rg.first[0])))
       return false;
-    __nanosleep(32);
+    __nanosleep(it < 8 ? 32 : 128);
   }
 }
 __device__ __forceinline__ Ranges one_range(const int* first, int n) {
@@ -234,6 +244,12 @@ __device__ __forceinline__ bool is_gemm(int kind) { return kind <= SK_LM; }
 
 // The first unit of this CTA in a phase whose deal starts at CTA ``off``.
 __device__ __forceinline__ int first_unit(int cta, int off, int grid) { return ((cta - off) % grid + grid) % grid; }
+// Where the next phase's deal starts. Attention phases are always dealt from CTA 0 and move no
+// deal: every layer gives a CTA the same (entry, KV head) pairs, whose metadata it keeps.
+__device__ __forceinline__ int phase_offset(const Phase& P, int off) { return P.kind == SK_ATTN ? 0 : off; }
+__device__ __forceinline__ int next_offset(const Phase& P, int off, int grid) {
+  return P.kind == SK_ATTN ? off : (off + P.units) % grid;
+}
 
 struct Unit {
   int kind, layer, stripe, split, k0, nk;
@@ -303,6 +319,10 @@ struct Smem {
   int* x_issued;             // [SK_MAX_X_STAGES]
   int* x_seen;
   int* conv_uses;            // [SK_MAX_X_STAGES] completions of x_conv[s] the MMA issuer has waited for
+  struct AttnMeta* meta;     // [SK_META_UNITS] this CTA's attention pairs (the same every layer)
+  // the activation ring cut for this launch's rows: stages of ceil(R / 64) boxes, as many as the
+  // region (sized on the host for R_max rows) holds, at most SK_MAX_X_STAGES
+  int xs, xsb;
 };
 
 __device__ Smem carve(uint8_t* base, const SkParams& p) {
@@ -338,11 +358,13 @@ __device__ Smem carve(uint8_t* base, const SkParams& p) {
   s.x_issued = s.w_seen + SK_W_STAGES;
   s.x_seen = s.x_issued + SK_MAX_X_STAGES;
   s.conv_uses = s.x_seen + SK_MAX_X_STAGES;
+  s.meta = reinterpret_cast<AttnMeta*>(s.conv_uses + SK_MAX_X_STAGES);
   return s;
 }
 constexpr int SMEM_FIXED = SK_W_STAGES * W_STAGE + WORK_BYTES + QTILE_BYTES + SK_MAX_ROWS * 4 + 16 * 4 +
                            (2 * SK_W_STAGES + 3 * SK_MAX_X_STAGES + 5) * 8 +
-                           (4 + 2 * SK_W_STAGES + 3 * SK_MAX_X_STAGES) * 4;
+                           (4 + 2 * SK_W_STAGES + 3 * SK_MAX_X_STAGES) * 4 +
+                           (SK_META_UNITS + 1) * (int)sizeof(AttnMeta);
 
 // ------------------------------------------------------------------ role: weight producer
 __device__ void weight_producer(const SkMaps& maps, const SkParams& p, const Sync& sy, const Smem& sm, int lm_cnt) {
@@ -352,7 +374,7 @@ __device__ void weight_producer(const SkMaps& maps, const SkParams& p, const Syn
   for (int ph = 0; ph < nph; ++ph) {
     const Phase P = phase_at(p, ph, lm_cnt);
     if (is_gemm(P.kind)) {
-      for (int u = first_unit(blockIdx.x, off, p.grid); u < P.units; u += p.grid) {
+      for (int u = first_unit(blockIdx.x, phase_offset(P, off), p.grid); u < P.units; u += p.grid) {
         const Unit g = gemm_unit(p, P, u);
         const CUtensorMap* map = w_map(maps, p, g);
         for (int i = 0; i < g.nk; ++i, ++w_iter) {
@@ -365,7 +387,7 @@ __device__ void weight_producer(const SkMaps& maps, const SkParams& p, const Syn
         }
       }
     }
-    off = (off + P.units) % p.grid;
+    off = next_offset(P, off, p.grid);
   }
 }
 
@@ -381,23 +403,23 @@ __device__ void act_producer(const SkMaps& maps, const SkParams& p, const Sync& 
       const CUtensorMap* map = x_map(maps, p, P.kind);
       const int rows = P.kind == SK_LM ? lm_cnt : R;
       const int boxes = (rows + 63) / 64;
-      for (int u = first_unit(blockIdx.x, off, p.grid); u < P.units; u += p.grid) {
+      for (int u = first_unit(blockIdx.x, phase_offset(P, off), p.grid); u < P.units; u += p.grid) {
         const Unit g = gemm_unit(p, P, u);
         if (!wait_unit_inputs(p, sy, g, lm_cnt, sm.abort_s)) return;
         stamp(p, ph, 6, true);
         fence_proxy_async_global();  // generic-proxy writes of other CTAs -> our TMA reads
         for (int i = 0; i < g.nk; ++i, ++x_iter) {
-          const int s = x_iter % p.x_stages;
-          if (!bar_wait(&sm.x_empty[s], ((x_iter / p.x_stages) & 1) ^ 1, sm.abort_s, sy, p.status, sm.w_full))
+          const int s = x_iter % sm.xs;
+          if (!bar_wait(&sm.x_empty[s], ((x_iter / sm.xs) & 1) ^ 1, sm.abort_s, sy, p.status, sm.w_full))
             return;
           mbar_arrive_expect_tx(&sm.x_full[s], (uint32_t)(boxes * XBOX));
           for (int b = 0; b < boxes; ++b)
-            tma_load_2d(sm.x_ring + s * p.x_stage_bytes + b * XBOX, map, &sm.x_full[s], (g.k0 + i) * 64, b * 64);
+            tma_load_2d(sm.x_ring + s * sm.xsb + b * XBOX, map, &sm.x_full[s], (g.k0 + i) * 64, b * 64);
           sm.x_issued[s] += 1;
         }
       }
     }
-    off = (off + P.units) % p.grid;
+    off = next_offset(P, off, p.grid);
   }
 }
 
@@ -418,7 +440,7 @@ __device__ void mma_issuer(const SkParams& p, const Sync& sy, const Smem& sm, ui
       const uint32_t idesc0 = idesc_bf16_f32(128, part0);
       const uint32_t idesc1 = part1 > 0 ? idesc_bf16_f32(128, part1) : 0u;
       const bool nx = is_nx(P.kind);
-      for (int u = first_unit(blockIdx.x, off, p.grid); u < P.units; u += p.grid) {
+      for (int u = first_unit(blockIdx.x, phase_offset(P, off), p.grid); u < P.units; u += p.grid) {
         const Unit g = gemm_unit(p, P, u);
         const int buf = nbuf == 2 ? (acc_iter & 1) : 0;
         const int use = acc_iter / nbuf;  // earlier units on this accumulator buffer
@@ -427,19 +449,19 @@ __device__ void mma_issuer(const SkParams& p, const Sync& sy, const Smem& sm, ui
         const uint32_t d = tmem + (uint32_t)(buf * 256);
         for (int i = 0; i < g.nk; ++i, ++w_iter, ++x_iter) {
           const int ws = w_iter % SK_W_STAGES;
-          const int xs = x_iter % p.x_stages;
+          const int xs = x_iter % sm.xs;
           if (!bar_wait(&sm.w_full[ws], (w_iter / SK_W_STAGES) & 1, sm.abort_s, sy, p.status, sm.w_full)) return;
           sm.w_seen[ws] += 1;
           if (nx) {
             if (!bar_wait(&sm.x_conv[xs], sm.conv_uses[xs] & 1, sm.abort_s, sy, p.status, sm.w_full)) return;
             sm.conv_uses[xs] += 1;
           } else {
-            if (!bar_wait(&sm.x_full[xs], (x_iter / p.x_stages) & 1, sm.abort_s, sy, p.status, sm.w_full)) return;
+            if (!bar_wait(&sm.x_full[xs], (x_iter / sm.xs) & 1, sm.abort_s, sy, p.status, sm.w_full)) return;
             sm.x_seen[xs] += 1;
           }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sm.w_ring + ws * W_STAGE);
-          const uint32_t b_addr = smem_u32(sm.x_ring + xs * p.x_stage_bytes);
+          const uint32_t b_addr = smem_u32(sm.x_ring + xs * sm.xsb);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t a_desc = smem_desc_sw128(a_addr + kk * 32);
@@ -455,7 +477,7 @@ __device__ void mma_issuer(const SkParams& p, const Sync& sy, const Smem& sm, ui
         ++acc_iter;
       }
     }
-    off = (off + P.units) % p.grid;
+    off = next_offset(P, off, p.grid);
   }
 }
 
@@ -480,13 +502,34 @@ __device__ __forceinline__ void nx_chunk(uint32_t addr, float rstd, uint4 w) {
 
 // ------------------------------------------------------------------ compute: epilogues on a row chunk
 // ``acc`` is [count][128] fp32 in shared memory (the reduced tile rows r0 .. r0 + count - 1).
-__device__ void epilogue_qkv(const SkParams& p, const Unit& g, const float* acc, int r0, int count) {
-  const int cw = (threadIdx.x >> 5) - 4, lane = threadIdx.x & 31;
+// The rows' positions and slots (``rows_s``: 2 x 64 ints) and their RoPE cos / sin rows
+// (``rope_s``: [count][128] bf16 each) are staged in shared memory first, all loads in flight at
+// once, so that the per-row work below reads no global memory. Called by every compute thread.
+__device__ void epilogue_qkv(const SkParams& p, const Unit& g, const float* acc, int r0, int count, int* rows_s,
+                             __nv_bfloat16* rope_s) {
+  const int tid = threadIdx.x - 128, cw = tid >> 5, lane = tid & 31;
   const int head = g.stripe;
   const bool is_q = head < p.nh;
   const bool is_k = !is_q && head < p.nh + p.nkv;
   const bool rope = is_q || is_k;
   const SkLayer& L = p.layers[g.layer];
+  if (tid < count) {
+    int pos = p.positions[r0 + tid];
+    rows_s[tid] = pos < 0 ? 0 : (pos >= p.max_positions ? p.max_positions - 1 : pos);
+    rows_s[64 + tid] = is_q ? 0 : p.slot_mapping[r0 + tid];
+  }
+  compute_sync();
+  __nv_bfloat16* cos_s = rope_s;
+  __nv_bfloat16* sin_s = rope_s + count * 128;
+  if (rope) {
+    for (int e = tid; e < count * 16; e += SK_COMPUTE) {
+      const int m = e >> 4, ch = e & 15;
+      const long long src = (long long)rows_s[m] * 128 + ch * 8;
+      *reinterpret_cast<uint4*>(cos_s + m * 128 + ch * 8) = __ldg(reinterpret_cast<const uint4*>(p.rope_cos + src));
+      *reinterpret_cast<uint4*>(sin_s + m * 128 + ch * 8) = __ldg(reinterpret_cast<const uint4*>(p.rope_sin + src));
+    }
+  }
+  compute_sync();
   const int d0 = 4 * lane;
   float wn[4] = {1.f, 1.f, 1.f, 1.f};
   if (rope) {
@@ -500,10 +543,8 @@ __device__ void epilogue_qkv(const SkParams& p, const Unit& g, const float* acc,
     const float4 a = *reinterpret_cast<const float4*>(acc + m * 128 + d0);
     float v[4] = {bf16r(a.x), bf16r(a.y), bf16r(a.z), bf16r(a.w)};
     if (rope) {
-      int pos = p.positions[row];
-      pos = pos < 0 ? 0 : (pos >= p.max_positions ? p.max_positions - 1 : pos);
-      const uint2 cr = *reinterpret_cast<const uint2*>(p.rope_cos + (long long)pos * 128 + d0);
-      const uint2 sr = *reinterpret_cast<const uint2*>(p.rope_sin + (long long)pos * 128 + d0);
+      const uint2 cr = *reinterpret_cast<const uint2*>(cos_s + m * 128 + d0);
+      const uint2 sr = *reinterpret_cast<const uint2*>(sin_s + m * 128 + d0);
       const float2 c0 = unpack_bf16x2(cr.x), c1 = unpack_bf16x2(cr.y), s0 = unpack_bf16x2(sr.x),
                    s1 = unpack_bf16x2(sr.y);
       const float cs[4] = {c0.x, c0.y, c1.x, c1.y}, sn[4] = {s0.x, s0.y, s1.x, s1.y};
@@ -529,7 +570,7 @@ __device__ void epilogue_qkv(const SkParams& p, const Unit& g, const float* acc,
       *reinterpret_cast<uint2*>(p.q + (long long)row * (p.nh * 128) + head * 128 + d0) = packed;
       continue;
     }
-    const long long slot = p.slot_mapping[row];
+    const long long slot = rows_s[64 + m];
     if (slot < 0 || slot >= p.num_cache_slots) {
       if (lane == 0) report(p.status, NE_DEV_BAD_SLOT);
       continue;
@@ -665,36 +706,77 @@ __device__ __forceinline__ void issue_block(const SkParams& p, const SkLayer& L,
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
+// The step metadata of attention pair ``u`` (entry u / nkv, KV head u % nkv) into ``M``, by one warp.
+__device__ void build_meta(const SkParams& p, int u, AttnMeta& M) {
+  const int lane = threadIdx.x & 31;
+  const int b = u / p.nkv, kvh = u % p.nkv, G = p.nh / p.nkv;
+  const int ql = p.q_len[b];
+  const int r0 = ql > 0 ? p.q_start[b] : 0;
+  const int ctx = ql > 0 ? p.positions[r0 + ql - 1] + 1 : 0;  // keys the last row sees
+  const int nvec = ql > 0 ? min(ql * G, SK_MAX_QVEC) : 0;
+  const int nblk = ql > 0 ? min((ctx + 15) / 16, p.table_stride) : 0;
+  if (lane < 16) {
+    M.qpos[lane] = lane < nvec ? p.positions[r0 + lane / G] : -1;
+    const int32_t* table =
+        ql > 0 ? p.block_tables + (long long)(p.table_index ? p.table_index[b] : b) * p.table_stride : nullptr;
+    M.blocks[lane] = lane < nblk && lane < SK_META_BLOCKS ? table[lane] : -1;
+  }
+  if (lane == 0) {
+    M.b = b;
+    M.kvh = kvh;
+    M.ql = ql;
+    M.r0 = r0;
+    M.nvec = nvec;
+    M.ctx = ctx;
+    M.nblk = nblk;
+    M.first_new = ql > 0 ? p.positions[r0] : 0;
+  }
+}
+
+__device__ __forceinline__ long long meta_block(const SkParams& p, const AttnMeta& M, int j) {
+  if (j < SK_META_BLOCKS) return M.blocks[j];
+  return p.block_tables[(long long)(p.table_index ? p.table_index[M.b] : M.b) * p.table_stride + j];
+}
+
+// Before the pair's inputs are complete: each warp starts loading its first block if every token
+// of it is from an earlier step (only the new rows' K / V are written by this layer's QKV). Returns
+// whether this warp's first block is in flight.
+__device__ bool attention_issue_old(const SkParams& p, const Smem& sm, int l, const AttnMeta& M) {
+  const int tid = threadIdx.x - 128, cw = tid >> 5, lane = tid & 31;
+  if (M.ql <= 0 || cw >= M.nblk || cw * 16 + 15 >= M.first_new) return false;
+  const long long blk = meta_block(p, M, cw);
+  const long long max_block = (p.num_cache_slots - 1) / 16;
+  if (blk < 0 || blk >= max_block) return false;  // reported when the unit runs
+  const uint32_t kb = smem_u32(sm.work + cw * ATT_WARP);
+  issue_block(p, p.layers[l], blk, M.kvh, kb, kb + 4096, lane);
+  return true;
+}
+
 // One (entry b, KV head kvh) pair: its <= 16 query vectors (rows x grouped q heads) against the
 // entry's paged context, models/attention_context.py:66-109 (scaled dot product with the causal
 // mask of each row's position), eight warps splitting the 16-token blocks, merged at the end.
-__device__ void attention_unit(const SkParams& p, const Smem& sm, int l, int b, int kvh) {
+// ``issued``: this warp's first block is already in flight (attention_issue_old).
+__device__ void attention_unit(const SkParams& p, const Smem& sm, int l, const AttnMeta& M, bool issued) {
   const int tid = threadIdx.x - 128, cw = tid >> 5, lane = tid & 31;
-  const int ql = p.q_len[b];
-  if (ql <= 0) return;
+  if (M.ql <= 0) return;
   const int G = p.nh / p.nkv;
-  const int nvec = min(ql * G, SK_MAX_QVEC);
-  const int r0 = p.q_start[b];
+  const int kvh = M.kvh, nvec = M.nvec, r0 = M.r0, nblk = M.nblk;
   const int qs = p.nh * 128;
   const SkLayer& L = p.layers[l];
-  const int ctx = p.positions[r0 + ql - 1] + 1;  // keys the last row sees
-  const int nblk = min((ctx + 15) / 16, p.table_stride);
-  const int32_t* table = p.block_tables + (long long)(p.table_index ? p.table_index[b] : b) * p.table_stride;
   uint8_t* kbuf = sm.work + cw * ATT_WARP;
   const uint32_t kb = smem_u32(kbuf), vb = kb + 4096;
   const long long max_block = (p.num_cache_slots - 1) / 16;  // whole blocks below the scratch slot
   // each warp's first block is in flight while the query tile loads
-  long long blk = cw < nblk ? table[cw] : -1;
+  long long blk = cw < nblk ? meta_block(p, M, cw) : -1;
   bool valid = blk >= 0 && blk < max_block;
   if (cw < nblk && !valid && lane == 0) report(p.status, NE_DEV_BAD_SLOT);
-  if (valid) issue_block(p, L, blk, kvh, kb, vb, lane);
-  // query tile (16 vectors x 128 dims, bf16, swizzled) and each vector's position
+  if (valid && !issued) issue_block(p, L, blk, kvh, kb, vb, lane);
+  // query tile (16 vectors x 128 dims, bf16, swizzled)
   {
     const int v = tid >> 4, ch = tid & 15;  // 256 threads = 16 vectors x 16 chunks
     uint4 val = make_uint4(0, 0, 0, 0);
     if (v < nvec) val = ldcg_u4(p.q + (long long)(r0 + v / G) * qs + (kvh * G + v % G) * 128 + ch * 8);
     *reinterpret_cast<uint4*>(sm.qtile + tile_off(v, ch)) = val;
-    if (tid < 16) sm.qpos[tid] = tid < nvec ? p.positions[r0 + tid / G] : -1;
   }
   compute_sync();
   const uint32_t qbase = smem_u32(sm.qtile);
@@ -705,7 +787,7 @@ __device__ void attention_unit(const SkParams& p, const Smem& sm, int l, int b, 
     ldsm_x4(qa[k], qbase + tile_off((mi & 1) * 8 + ri, 2 * k + (mi >> 1)));
   }
   const int g = lane >> 2, t4 = lane & 3;
-  const int pos0 = sm.qpos[g], pos1 = sm.qpos[g + 8];
+  const int pos0 = M.qpos[g], pos1 = M.qpos[g + 8];
   float m_run[2] = {SK_NEG_INF, SK_NEG_INF}, l_run[2] = {0.f, 0.f};
   float o[16][4];
 #pragma unroll
@@ -778,7 +860,7 @@ __device__ void attention_unit(const SkParams& p, const Smem& sm, int l, int b, 
       __syncwarp();  // the buffer is refilled by the next block's copies
     }
     const int nj = j + NCW;
-    blk = nj < nblk ? table[nj] : -1;
+    blk = nj < nblk ? meta_block(p, M, nj) : -1;
     valid = blk >= 0 && blk < max_block;
     if (nj < nblk && !valid && lane == 0) report(p.status, NE_DEV_BAD_SLOT);
     if (valid) issue_block(p, L, blk, kvh, kb, vb, lane);
@@ -809,14 +891,14 @@ __device__ void attention_unit(const SkParams& p, const Smem& sm, int l, int b, 
   {
     const int v = tid >> 4, d0 = (tid & 15) * 8;
     const float* mlb = reinterpret_cast<const float*>(sm.work + NCW * ATT_WARP);
-    float M = SK_NEG_INF;
-    for (int w = 0; w < NCW; ++w) M = fmaxf(M, mlb[w * 32 + v]);
+    float Mx = SK_NEG_INF;
+    for (int w = 0; w < NCW; ++w) Mx = fmaxf(Mx, mlb[w * 32 + v]);
     float Ls = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (M != SK_NEG_INF) {
+    if (Mx != SK_NEG_INF) {
       for (int w = 0; w < NCW; ++w) {
         const float mw = mlb[w * 32 + v];
         if (mw == SK_NEG_INF) continue;
-        const float f = exp2f(mw - M);
+        const float f = exp2f(mw - Mx);
         Ls += mlb[w * 32 + 16 + v] * f;
         const float* src = reinterpret_cast<const float*>(sm.work + w * ATT_WARP) + v * 128 + d0;
         const float4 x0 = *reinterpret_cast<const float4*>(src), x1 = *reinterpret_cast<const float4*>(src + 4);
@@ -837,25 +919,21 @@ __device__ void attention_unit(const SkParams& p, const Smem& sm, int l, int b, 
   compute_sync();  // the buffers are reused by the next unit
 }
 
-// The K and V blocks this CTA's attention units of layer ``l`` will read, prefetched into L2
-// while the layer's QKV projection runs (whole 16-token slabs of all KV heads: the units of the
-// other heads, on other CTAs, read the rest of them; the L2 keeps one copy). The new tokens' rows
-// are written later by the QKV epilogues; prefetching their lines early is harmless.
-__device__ void prefetch_attention_kv(const SkParams& p, int l, int off_attn) {
+// The K and V blocks this CTA's attention pairs will read in layer ``l``, prefetched into L2 while
+// the layer's QKV projection runs (whole 16-token slabs of all KV heads: the pairs of the other
+// heads, on other CTAs, read the rest of them; the L2 keeps one copy). The new tokens' rows are
+// written later by the QKV epilogues; prefetching their lines early is harmless.
+__device__ void prefetch_attention_kv(const SkParams& p, const Smem& sm, int l) {
   const int tid = threadIdx.x - 128;
   const int units = p.num_seqs * p.nkv;
   const long long slab = 16LL * p.nkv * 128;  // bf16 elements of one block across the heads
   const long long max_block = (p.num_cache_slots - 1) / 16;
   const SkLayer& L = p.layers[l];
-  for (int u = first_unit(blockIdx.x, off_attn, p.grid); u < units; u += p.grid) {
-    const int b = u / p.nkv;
-    const int ql = p.q_len[b];
-    if (ql <= 0) continue;
-    const int ctx = p.positions[p.q_start[b] + ql - 1] + 1;
-    const int nblk = min((ctx + 15) / 16, p.table_stride);
-    const int32_t* table = p.block_tables + (long long)(p.table_index ? p.table_index[b] : b) * p.table_stride;
-    for (int j = tid; j < nblk; j += SK_COMPUTE) {
-      const long long blk = table[j];
+  int k = 0;
+  for (int u = blockIdx.x; u < units && k < SK_META_UNITS; u += p.grid, ++k) {
+    const AttnMeta& M = sm.meta[k];
+    for (int j = tid; j < M.nblk; j += SK_COMPUTE) {
+      const long long blk = meta_block(p, M, j);
       if (blk < 0 || blk >= max_block) continue;
       asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(L.k_cache + blk * slab),
                    "r"((uint32_t)(slab * 2))
@@ -923,18 +1001,32 @@ __device__ void compute_loop(const SkParams& p, const Sync& sy, const Smem& sm, 
   int off = 0;
   const int nph = num_phases(p);
   float* stage = reinterpret_cast<float*>(sm.work);  // reduction / epilogue staging
+  {  // this CTA's attention pairs (dealt from CTA 0 in every layer): their metadata, once
+    const int units = p.num_seqs * p.nkv;
+    int k = tid >> 5;
+    for (int u = blockIdx.x + k * p.grid; u < units && k < SK_META_UNITS; u += NCW * p.grid, k += NCW)
+      build_meta(p, u, sm.meta[k]);
+    compute_sync();
+  }
   for (int ph = 0; ph < nph; ++ph) {
     const Phase P = phase_at(p, ph, lm_cnt);
-    if (P.kind == SK_QKV) prefetch_attention_kv(p, P.layer, (off + P.units) % p.grid);
-    for (int u = first_unit(blockIdx.x, off, p.grid); u < P.units; u += p.grid) {
+    if (P.kind == SK_QKV) prefetch_attention_kv(p, sm, P.layer);
+    for (int u = first_unit(blockIdx.x, phase_offset(P, off), p.grid); u < P.units; u += p.grid) {
       compute_sync();  // every thread is done with the previous unit (and its decisions)
       if (tid == 0) stamp(p, ph, 0, true);
       if (P.kind == SK_ATTN) {
-        const int b = u / p.nkv, kvh = u % p.nkv;
+        const int k = (u - (int)blockIdx.x) / p.grid;  // this CTA's k-th pair
+        AttnMeta& M = sm.meta[k < SK_META_UNITS ? k : SK_META_UNITS];
+        if (k >= SK_META_UNITS) {  // beyond the kept metadata: built now into the spare slot
+          if (tid < 32) build_meta(p, u, M);
+          compute_sync();
+        }
+        const int kvh = M.kvh;
         const int G = p.nh / p.nkv;
+        const bool issued = attention_issue_old(p, sm, P.layer, M);
         if (tid == 0) {
           bool ok = !*sm.abort_s;
-          if (ok && p.q_len[b] > 0) {  // an idle entry reads nothing
+          if (ok && M.ql > 0) {  // an idle entry reads nothing
             Ranges rg{};  // the q heads of the group, k, v
             rg.first[0] = sy.done(P.layer, SK_QKV, kvh * G);
             rg.n[0] = G;
@@ -949,7 +1041,7 @@ __device__ void compute_loop(const SkParams& p, const Sync& sy, const Smem& sm, 
         }
         if (!group_read(sm)) return;
         if (tid == 0) stamp(p, ph, 1, true);
-        attention_unit(p, sm, P.layer, b, kvh);
+        attention_unit(p, sm, P.layer, M, issued);
         if (tid == 0) {
           __threadfence();
           red_release_add(sy.head(P.layer, kvh), 1);
@@ -992,10 +1084,10 @@ __device__ void compute_loop(const SkParams& p, const Sync& sy, const Smem& sm, 
         compute_sync();
         const __nv_bfloat16* lnw = P.kind == SK_QKV ? p.layers[P.layer].ln_in : p.layers[P.layer].ln_post;
         for (int i = 0; i < g.nk; ++i, ++x_iter) {
-          const int xs = x_iter % p.x_stages;
-          if (!group_bar_wait(sm, sy, p, &sm.x_full[xs], (x_iter / p.x_stages) & 1, tid)) return;
+          const int xs = x_iter % sm.xs;
+          if (!group_bar_wait(sm, sy, p, &sm.x_full[xs], (x_iter / sm.xs) & 1, tid)) return;
           if (tid == 0) sm.x_seen[xs] += 1;
-          const uint32_t st = smem_u32(sm.x_ring + xs * p.x_stage_bytes);
+          const uint32_t st = smem_u32(sm.x_ring + xs * sm.xsb);
           const uint4* wk = reinterpret_cast<const uint4*>(lnw + (g.k0 + i) * 64);
           for (int e = tid; e < rows * 8; e += SK_COMPUTE) {
             const int row = e >> 3, j = e & 7, r64 = row & 63;
@@ -1058,7 +1150,7 @@ __device__ void compute_loop(const SkParams& p, const Sync& sy, const Smem& sm, 
       for (int c0 = lo; c0 < hi; c0 += chunk_rows) {
         const int cnt = min(chunk_rows, hi - c0);
         const int per = cnt * 32;  // float4s of one split's chunk
-#pragma unroll 4
+#pragma unroll 8
         for (int e = tid; e < S * per; e += SK_COMPUTE) {
           const int j = e / per, f = e - j * per;
           const float4 v = ldcg_f4(stripe_parts + ((long long)j * p.R_max + c0) * 128 + f * 4);
@@ -1074,8 +1166,9 @@ __device__ void compute_loop(const SkParams& p, const Sync& sy, const Smem& sm, 
           *reinterpret_cast<float4*>(stage + f * 4) = a;
         }
         compute_sync();
-        if (P.kind == SK_QKV)
-          epilogue_qkv(p, g, stage, c0, cnt);
+        if (P.kind == SK_QKV)  // (staging past the reduced rows, which are all that is live now)
+          epilogue_qkv(p, g, stage, c0, cnt, reinterpret_cast<int*>(sm.rstd),
+                       reinterpret_cast<__nv_bfloat16*>(stage + cnt * 128));
         else if (P.kind == SK_GATEUP)
           epilogue_swiglu(p, g, stage, c0, cnt);
         else
@@ -1088,7 +1181,7 @@ __device__ void compute_loop(const SkParams& p, const Sync& sy, const Smem& sm, 
         stamp(p, ph, 5);
       }
     }
-    off = (off + P.units) % p.grid;
+    off = next_offset(P, off, p.grid);
   }
 }
 
@@ -1097,7 +1190,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  const Smem sm = carve(base, p);
+  Smem sm = carve(base, p);
   const Sync sy{p.sync, p.L, p.max_stripes, p.nkv};
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
@@ -1129,7 +1222,9 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *sm.tmem_slot;
   const int R = min(max(*p.num_rows, 0), p.R_max);
-  const int lm_cnt = min(max(*p.lm_count, 0), p.R_max);
+  const int lm_cnt = min(max(*p.lm_count, 0), R);
+  sm.xsb = max(1, (R + 63) / 64) * XBOX;
+  sm.xs = min(SK_MAX_X_STAGES, (p.x_stages * p.x_stage_bytes) / sm.xsb);
   const int nbuf = p.R_max <= 256 ? 2 : 1;
   if (R > 0 && gridDim.x == (unsigned)p.grid) {
     if (warp == 0) {
@@ -1144,6 +1239,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
       if (lane == 0) act_producer(maps, p, sy, sm, R, lm_cnt);
     } else if (warp >= 4) {
       compute_loop(p, sy, sm, tmem, R, lm_cnt, nbuf);
+      asm volatile("cp.async.wait_all;" ::: "memory");  // (an abort may leave block copies in flight)
     }
   } else if (R > 0 && tid == 0) {
     report(p.status, NE_DEV_TIMEOUT);  // launched with a grid the plan was not made for
@@ -1153,7 +1249,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
     // copies still in flight (only after an abort) land before the shared memory is released
     for (int s = 0; s < SK_W_STAGES; ++s)
       if (sm.w_issued[s] > sm.w_seen[s]) mbar_wait(&sm.w_full[s], sm.w_seen[s] & 1, nullptr, p.status);
-    for (int s = 0; s < p.x_stages; ++s)
+    for (int s = 0; s < sm.xs; ++s)
       if (sm.x_issued[s] > sm.x_seen[s]) mbar_wait(&sm.x_full[s], sm.x_seen[s] & 1, nullptr, p.status);
   }
   tc_fence_before();

@@ -97,9 +97,13 @@ struct SkMaps {
 // the record of the first wait that ran out: [recorded, site, what, target, seen, cta, warp]
 // (site 1: a counter, ``what`` its index in this array; site 2: an mbarrier, ``what`` its index
 // among the CTA's barriers and ``target`` the parity).
+// SK_LINE ints apart: spreading the counters one per 128-byte L2 line (SK_LINE = 32) was measured
+// to change no phase's time on the 0.6B step (the waits are bound by the L2 round trip, not by
+// line contention), so they stay packed and the per-launch memset stays small.
 constexpr int SK_RECORD_INTS = 7;
+constexpr int SK_LINE = 1;
 inline size_t step_sync_ints(int L, int max_stripes, int nkv) {
-  return (size_t)2 * L * 4 * max_stripes + (size_t)L * nkv + 2 + SK_RECORD_INTS;
+  return ((size_t)2 * L * 4 * max_stripes + (size_t)L * nkv + 2) * SK_LINE + SK_RECORD_INTS;
 }
 // Bytes of one split-K partial area for ``units`` units of up to ``rows`` rows.
 inline size_t step_partial_bytes(int units, int rows) { return (size_t)units * rows * 128 * sizeof(float); }

@@ -26,7 +26,9 @@ def test_binding_declares_exactly_the_header_symbols() -> None:
     lib_mod = submodule("_lib")
     assert sorted(lib_mod.EXPORTS) == sorted(header_symbols())
     lib = lib_mod.load()
-    assert lib.ne_abi_version() == 3
+    assert lib.ne_abi_version() == lib_mod.ABI_VERSION
+    header = (REPO / "include" / "nespec.h").read_text()
+    assert f"#define NE_ABI_VERSION {lib_mod.ABI_VERSION}" in header
     assert lib.ne_status_string(0) == b"ok"
 
 
