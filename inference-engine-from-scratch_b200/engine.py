@@ -285,6 +285,10 @@ class B200SpeculativeEngine:
         start = _lib.device_int32(self.lib.ne_model_lm_start(self.draft_model.handle), num_entries, self.model.device)
         return regions.reshape(self.k, self._region_rows, vocab), start.cpu().tolist()
 
+    def draws_used(self, slot: int) -> int:
+        """Uniforms the request in ``slot`` has drawn from its Philox stream so far (one device read)."""
+        return int(self.state.rng_draws[slot].item())
+
     def release(self, slots: list[int]) -> None:
         self.state.release(slots)
         if self.draft_state is not None:

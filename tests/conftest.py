@@ -3,6 +3,7 @@
 from __future__ import annotations
 
 import importlib
+import os
 import sys
 from pathlib import Path
 
@@ -27,6 +28,15 @@ def package():
 
 def submodule(name: str):
     return importlib.import_module(f"{PACKAGE}.{name}")
+
+
+def reference_src() -> Path | None:
+    """The reference's Python sources, where this host has them (``NANOENGINE_REFERENCE_SRC``, or a
+    ``reference`` checkout beside this repository); GPU hosts have none."""
+    for candidate in (os.environ.get("NANOENGINE_REFERENCE_SRC"), REPO.parent / "reference" / "nanoengine" / "src"):
+        if candidate and (Path(candidate) / "nanoengine" / "engine" / "speculative").is_dir():
+            return Path(candidate)
+    return None
 
 
 def load_golden(name: str):

@@ -11,22 +11,13 @@ from __future__ import annotations
 
 import importlib
 import inspect
-import os
 import sys
-from pathlib import Path
 
 import pytest
 import torch
 
 from tests import reference_seam as seam
-from tests.conftest import REPO, load_golden, package, submodule
-
-
-def reference_src() -> Path | None:
-    for candidate in (os.environ.get("NANOENGINE_REFERENCE_SRC"), REPO.parent / "reference" / "nanoengine" / "src"):
-        if candidate and (Path(candidate) / "nanoengine" / "engine" / "speculative").is_dir():
-            return Path(candidate)
-    return None
+from tests.conftest import REPO, load_golden, package, reference_src, submodule
 
 
 @pytest.fixture(scope="module")
