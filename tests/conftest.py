@@ -22,6 +22,24 @@ def pytest_configure(config) -> None:
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
 
 
+# near-tie excuses of the sampled and full-model parity tests: (test, cases, exact, excused margins)
+NEAR_TIES: list[tuple[str, int, int, list[float]]] = []
+
+
+def report_near_ties(test: str, cases: int, exact: int, margins: list[float]) -> None:
+    """Record how many of a test's cases matched bit for bit and the margins of the excused ones."""
+    NEAR_TIES.append((test, cases, exact, sorted(margins)))
+
+
+def pytest_terminal_summary(terminalreporter) -> None:
+    if not NEAR_TIES:
+        return
+    terminalreporter.section("near-tie excuses (cases matched exactly / excused, largest excused margin)")
+    for test, cases, exact, margins in NEAR_TIES:
+        worst = f"{max(margins):.3g}" if margins else "-"
+        terminalreporter.write_line(f"{test}: {exact}/{cases} exact, {len(margins)} excused, largest margin {worst}")
+
+
 def package():
     return importlib.import_module(PACKAGE)
 

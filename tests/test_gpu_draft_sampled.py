@@ -19,7 +19,7 @@ import torch
 from oracle import philox
 from oracle import verify as overify
 from tests import reference_seam as seam
-from tests.conftest import load_golden, package, submodule
+from tests.conftest import load_golden, package, report_near_ties, submodule
 
 pytestmark = pytest.mark.gpu
 
@@ -151,8 +151,8 @@ def run_drafted(cases, device="cuda:0"):
     return [tokens[b, : int(count[b])].tolist() for b in range(B)], st.rng_draws.cpu().tolist()
 
 
-def check(cases, got, draws):
-    exact = 0
+def check(cases, got, draws, name="drafted verify"):
+    exact, margins = 0, []
     for case, g, d in zip(cases, got, draws):
         e, ed = oracle_drafted(case)
         if g == e and d == ed:
@@ -160,6 +160,8 @@ def check(cases, got, draws):
             continue
         m = draft_margin(case)
         assert m < MARGIN or m < TOPP_MARGIN, f"mismatch without a near-tie: got {g} ({d}), expected {e} ({ed})"
+        margins.append(m)
+    report_near_ties(name, len(cases), exact, margins)
     assert exact >= MIN_EXACT * len(cases), f"only {exact} of {len(cases)} match exactly"
 
 
@@ -253,13 +255,15 @@ def test_serial_sampled_draft_model_replays_on_the_oracle() -> None:
             got.append(list(new_tokens))
             draws.append(None)
     # verification replays (positions follow the oracle's own draw counts)
-    exact = 0
+    exact, margins = 0, []
     for case, g in zip(cases, got):
         e, _ = oracle_drafted(case)
         if g == e:
             exact += 1
             continue
-        assert draft_margin(case) < MARGIN, f"mismatch without a near-tie: got {g}, expected {e}"
+        margins.append(draft_margin(case))
+        assert margins[-1] < MARGIN, f"mismatch without a near-tie: got {g}, expected {e}"
+    report_near_ties("serial drafted replay", len(cases), exact, margins)
     assert exact >= MIN_EXACT * len(cases)
     assert len(cases) >= len(golden["records"]) and any(c["guesses"] for c in cases)
     target.close()
@@ -295,6 +299,7 @@ def test_batched_engine_sampled_draft_steps_replay_on_the_oracle(cuda_graphs) ->
     running = list(slots)
     vocab = cfg.vocab_size
     exact = total = 0
+    margins: list[float] = []
     while running:
         L = {s: int(eng.state.seq_len[s].item()) for s in running}
         draws_before = {s: int(eng.state.rng_draws[s].item()) for s in running}
@@ -326,7 +331,8 @@ def test_batched_engine_sampled_draft_steps_replay_on_the_oracle(cuda_graphs) ->
                 if got == expect and draws_after[s] == expect_draws:
                     exact += 1
                 else:
-                    assert draft_margin(case) < MARGIN, f"mismatch without a near-tie: {got} vs {expect}"
+                    margins.append(draft_margin(case))
+                    assert margins[-1] < MARGIN, f"mismatch without a near-tie: {got} vs {expect}"
             else:  # greedy: the kept guesses are the target's argmax run
                 am = case["logits"].argmax(dim=-1).tolist()
                 kept = 0
@@ -334,6 +340,7 @@ def test_batched_engine_sampled_draft_steps_replay_on_the_oracle(cuda_graphs) ->
                     kept += 1
                 assert res.tokens[s] == (guesses[:kept] + [am[kept]])[: len(res.tokens[s])]
         running = [s for s in running if res.finish[s] is None]
+    report_near_ties("engine drafted steps", total, exact, margins)
     assert total > 0 and exact >= MIN_EXACT * total
     target.raise_on_device_error()
     draft_model.raise_on_device_error()

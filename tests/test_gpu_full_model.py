@@ -24,7 +24,7 @@ import pytest
 import torch
 
 from tests import reference_seam as seam
-from tests.conftest import load_golden, package, submodule
+from tests.conftest import load_golden, package, report_near_ties, submodule
 
 pytestmark = pytest.mark.gpu
 
@@ -121,18 +121,18 @@ def deciding_rows(record: dict) -> list[tuple[dict | None, int]]:
     return rows
 
 
-def compare_tokens(got: list[int], record: dict, tol: float) -> tuple[int, int]:
+def compare_tokens(got: list[int], record: dict, tol: float) -> tuple[int, list[float]]:
     """Tokens equal up to the first difference, which must be an excused near-tie. Returns
-    (tokens compared equal, excused near-ties)."""
+    (tokens compared equal, the reference's top-2 gap at the excused near-tie, if any)."""
     want = record["tokens"]
     for i, (a, b) in enumerate(zip(got, want)):
         if a != b:
             digest, row = deciding_rows(record)[i]
             assert digest is not None and near_tie(digest, row, tol), (
                 f"token {i}: {a} vs the reference's {b}, top-2 gap {None if digest is None else gap(digest, row)}")
-            return i, 1
+            return i, [gap(digest, row)]
     assert len(got) == len(want)
-    return len(want), 0
+    return len(want), []
 
 
 @pytest.mark.parametrize("variant", ["bf16", "int8"])
@@ -148,6 +148,7 @@ def test_teacher_forced_steps_match_the_reference(models, bf16_noise_floor, vari
     ids = golden["digest_ids"]
     model.kv.zero_()
     decisions = excused = 0
+    gaps: list[float] = []  # the reference's top-2 gaps at the excused decisions
     worst = 0.0  # largest logit difference in units of the per-logit tolerance
     compared = beyond_abs = 0  # logits compared, and how many differ by more than the absolute tol
     diffs = []
@@ -164,6 +165,7 @@ def test_teacher_forced_steps_match_the_reference(models, bf16_noise_floor, vari
         if first != record["tokens"][0]:
             assert near_tie(record["prefill_logits"], 0, tol)
             excused += 1
+            gaps.append(gap(record["prefill_logits"], 0))
         seq.token_ids.append(record["tokens"][0])
         for ref in record["steps"]:
             left = params.max_new_tokens - seq.num_generated_tokens
@@ -192,6 +194,7 @@ def test_teacher_forced_steps_match_the_reference(models, bf16_noise_floor, vari
                 if new[i] != want[i]:
                     assert near_tie(ref["logits"], i, tol), (index, i, new, want, gap(ref["logits"], i))
                     excused += 1
+                    gaps.append(gap(ref["logits"], i))
                     break
             else:
                 assert new == want
@@ -206,6 +209,7 @@ def test_teacher_forced_steps_match_the_reference(models, bf16_noise_floor, vari
     d = torch.cat(diffs)
     print(f"[{variant}] |diff| max {d.max().item():.4f} p99.9 {d.quantile(0.999).item():.4f} "
           f"p99 {d.quantile(0.99).item():.4f} mean {d.mean().item():.5f}")
+    report_near_ties(f"full {variant} teacher-forced decisions", decisions, decisions - excused, gaps)
     assert excused <= max(1, decisions // 10)
 
 
@@ -223,17 +227,19 @@ def test_free_running_serial_seam_matches_up_to_near_ties(models, bf16_noise_flo
     allocator = seam.PagedSlotAllocator(golden["num_blocks"], 16)
     runner = serial.B200ModelRunner(model, allocator)
     proposer = serial.NgramProposer(golden["max_ngram"], max_model_len=256, device="cuda:0")
-    equal = excused = 0
+    equal, gaps = 0, []
     for index, record in enumerate(golden["records"]):
         gen = seam.SpeculativeGenerator(runner, proposer, golden["k"], frozenset())
         params = seam.SamplingParams(max_new_tokens=golden["max_new"], ignore_eos=True)
         tokens = [e.token_id for e in gen.generate(seam.GenerationRequest(f"s{index}", record["prompt"], params))]
         n, e = compare_tokens(tokens, record, tol)
         equal += n
-        excused += e
+        gaps += e
     assert allocator.num_free_blocks == golden["num_blocks"]
     model.raise_on_device_error()
-    print(f"\n[{variant} serial] {equal} tokens equal, {excused} excused near-ties")
+    print(f"\n[{variant} serial] {equal} tokens equal, {len(gaps)} excused near-ties")
+    report_near_ties(f"full {variant} serial tokens (to the first near-tie)",
+                     sum(len(r["tokens"]) for r in golden["records"]), equal, gaps)
 
 
 @pytest.mark.parametrize("variant", ["bf16", "int8"])
@@ -248,13 +254,15 @@ def test_free_running_batched_engine_matches_up_to_near_ties(models, bf16_noise_
                                                     cuda_graphs=True)
     eng.capture_all_buckets()
     outs = eng.generate(prompts, golden["max_new"])
-    equal = excused = 0
+    equal, gaps = 0, []
     for out, record in zip(outs, golden["records"]):
         n, e = compare_tokens(out, record, tol)
         equal += n
-        excused += e
+        gaps += e
     model.raise_on_device_error()
-    print(f"\n[{variant} batched, graphed] {equal} tokens equal, {excused} excused near-ties")
+    print(f"\n[{variant} batched, graphed] {equal} tokens equal, {len(gaps)} excused near-ties")
+    report_near_ties(f"full {variant} batched tokens (to the first near-tie)",
+                     sum(len(r["tokens"]) for r in golden["records"]), equal, gaps)
 
 
 def test_lm_head_argmax_over_the_full_vocabulary_takes_the_lowest_index_on_ties(full_weights) -> None:
