@@ -310,23 +310,27 @@ int upload_step_descriptors(ne_model* m) {
   return NE_OK;
 }
 
-// NE_STEP_KERNEL=1 runs eligible verify steps as the persistent kernel; otherwise (the default,
-// while it measures slower than the per-projection launches) every step launches kernel by
-// kernel. Read at every forward, so a process can compare the two.
-bool step_kernel_enabled() {
+// NE_STEP_KERNEL=1 runs every eligible verify step as the persistent kernel, NE_STEP_KERNEL=0 none;
+// unset, the steps whose row bound is at most SK_AUTO_ROWS (where it measures faster than the
+// per-projection launches: 1 to 16 users of the 0.6B model at k = 4) and the launch sequence above.
+// Read at every forward, so a process can compare the two.
+int step_kernel_mode() {
   const char* v = getenv("NE_STEP_KERNEL");
-  return v && v[0] == '1';
+  if (!v || !v[0]) return -1;
+  return v[0] == '1' ? 1 : 0;
 }
 
 // Whether this forward runs as the persistent step kernel: greedy (argmax) lm rows, rows within the
 // partial areas and the kernel's shared memory, at most 16 query vectors per (entry, KV head).
 bool use_step_kernel(const ne_model* m, const ne_rows* rows, int lm_mode) {
-  if (!m->sk_ready || !step_kernel_enabled() || lm_mode != NE_LM_ARGMAX || m->kv_shadow) return false;
+  const int mode = step_kernel_mode();
+  if (!m->sk_ready || mode == 0 || lm_mode != NE_LM_ARGMAX || m->kv_shadow) return false;
+  if (mode < 0 && rows->max_rows > ne::SK_AUTO_ROWS) return false;
   const int G = m->cfg.num_heads / m->cfg.num_kv_heads;
-  int xs = 0, xsb = 0;
+  int ring = 0;
   return rows->max_rows <= m->sk_rows && rows->lm_max <= rows->max_rows &&
          std::max(1, rows->max_q_len) * G <= ne::SK_MAX_QVEC && rows->num_seqs >= 1 &&
-         ne::step_smem_bytes(rows->max_rows, &xs, &xsb) > 0;
+         ne::step_smem_bytes(rows->max_rows, &ring) > 0;
 }
 
 int step_forward(ne_model* m, const ne_rows* rows, int32_t* argmax_out, cudaStream_t s) {
@@ -340,7 +344,7 @@ int step_forward(ne_model* m, const ne_rows* rows, int32_t* argmax_out, cudaStre
   ne::SkParams p = m->sk;
   p.R_max = R;
   p.num_seqs = rows->num_seqs;
-  ne::step_smem_bytes(R, &p.x_stages, &p.x_stage_bytes);
+  ne::step_smem_bytes(R, &p.ring_bytes);
   p.num_rows = rows->num_rows;
   p.positions = rows->positions;
   p.slot_mapping = rows->slot_mapping;

@@ -297,12 +297,13 @@ __device__ bool wait_unit_inputs(const SkParams& p, const Sync& sy, const Unit& 
 
 // ------------------------------------------------------------------ shared memory
 struct Smem {
-  uint8_t* w_ring;     // SK_W_STAGES x 16 KB
-  uint8_t* x_ring;     // x_stages x x_stage_bytes
+  uint8_t* w_ring;     // ws x 16 KB
+  uint8_t* x_ring;     // xs x xsb
   uint8_t* work;       // attention buffers / reduction staging
   uint8_t* qtile;      // 16 x 256 B
   float* rstd;         // [SK_MAX_ROWS]
   int* qpos;           // [16]
+  int* rowinfo;        // [2][SK_MAX_ROWS]: the step's rows' positions (clamped to the RoPE table), slots
   uint64_t* w_full;
   uint64_t* w_empty;
   uint64_t* x_full;
@@ -314,24 +315,42 @@ struct Smem {
   uint32_t* tmem_slot;
   volatile int* abort_s;
   volatile int* flag;        // compute-group broadcast
-  int* w_issued;             // [SK_W_STAGES] loads issued per slot
-  int* w_seen;               // [SK_W_STAGES] completions observed per slot
+  int* w_issued;             // [SK_MAX_W_STAGES] loads issued per slot
+  int* w_seen;               // [SK_MAX_W_STAGES] completions observed per slot
   int* x_issued;             // [SK_MAX_X_STAGES]
   int* x_seen;
   int* conv_uses;            // [SK_MAX_X_STAGES] completions of x_conv[s] the MMA issuer has waited for
   struct AttnMeta* meta;     // [SK_META_UNITS] this CTA's attention pairs (the same every layer)
-  // the activation ring cut for this launch's rows: stages of ceil(R / 64) boxes, as many as the
-  // region (sized on the host for R_max rows) holds, at most SK_MAX_X_STAGES
-  int xs, xsb;
+  // the ring area cut for this launch's rows (ring_split): xs activation stages of ceil(R / 64)
+  // boxes (xsb bytes each), ws weight stages
+  int xs, xsb, ws;
 };
 
-__device__ Smem carve(uint8_t* base, const SkParams& p) {
+// The ring area of ``ring`` bytes cut for R rows: as many activation stages as fit next to
+// SK_MIN_W_STAGES weight stages (at most SK_MAX_X_STAGES), then every byte left as weight stages
+// (at most SK_MAX_W_STAGES). Usable when xs >= 2 and ws >= SK_MIN_W_STAGES.
+__host__ __device__ inline void ring_split(int R, int ring, int& xs, int& xsb, int& ws) {
+  xsb = ((R + 63) / 64 > 1 ? (R + 63) / 64 : 1) * XBOX;
+  xs = (ring - SK_MIN_W_STAGES * W_STAGE) / xsb;
+  xs = xs < SK_MAX_X_STAGES ? xs : SK_MAX_X_STAGES;
+  ws = (ring - xs * xsb) / W_STAGE;
+  ws = ws < SK_MAX_W_STAGES ? ws : SK_MAX_W_STAGES;
+}
+
+constexpr int SMEM_FIXED = WORK_BYTES + QTILE_BYTES + SK_MAX_ROWS * 4 + 16 * 4 + 2 * SK_MAX_ROWS * 4 +
+                           (2 * SK_MAX_W_STAGES + 3 * SK_MAX_X_STAGES + 5) * 8 +
+                           (4 + 2 * SK_MAX_W_STAGES + 3 * SK_MAX_X_STAGES) * 4 +
+                           (SK_META_UNITS + 1) * (int)sizeof(AttnMeta);
+constexpr int SMEM_FIXED_ALIGNED = (SMEM_FIXED + 1023) & ~1023;
+constexpr int SMEM_RING = (227 * 1024 - 1024 - SMEM_FIXED_ALIGNED) & ~1023;
+
+// Layout: the fixed region, then (1024-byte aligned, as the 128-byte swizzle wants) the rings.
+__device__ Smem carve(uint8_t* base, const SkParams& p, int R) {
   Smem s;
+  ring_split(R, p.ring_bytes, s.xs, s.xsb, s.ws);
+  s.w_ring = base + SMEM_FIXED_ALIGNED;
+  s.x_ring = s.w_ring + s.ws * W_STAGE;
   uint8_t* at = base;
-  s.w_ring = at;
-  at += SK_W_STAGES * W_STAGE;
-  s.x_ring = at;
-  at += p.x_stages * p.x_stage_bytes;
   s.work = at;
   at += WORK_BYTES;
   s.qtile = at;
@@ -340,10 +359,12 @@ __device__ Smem carve(uint8_t* base, const SkParams& p) {
   at += SK_MAX_ROWS * 4;
   s.qpos = reinterpret_cast<int*>(at);
   at += 16 * 4;
+  s.rowinfo = reinterpret_cast<int*>(at);
+  at += 2 * SK_MAX_ROWS * 4;
   uint64_t* b = reinterpret_cast<uint64_t*>(at);
   s.w_full = b;
-  s.w_empty = b + SK_W_STAGES;
-  s.x_full = b + 2 * SK_W_STAGES;
+  s.w_empty = b + SK_MAX_W_STAGES;
+  s.x_full = b + 2 * SK_MAX_W_STAGES;
   s.x_empty = s.x_full + SK_MAX_X_STAGES;
   s.x_conv = s.x_empty + SK_MAX_X_STAGES;
   s.acc_full = s.x_conv + SK_MAX_X_STAGES;
@@ -354,17 +375,14 @@ __device__ Smem carve(uint8_t* base, const SkParams& p) {
   s.abort_s = ints + 1;
   s.flag = ints + 2;
   s.w_issued = ints + 4;
-  s.w_seen = s.w_issued + SK_W_STAGES;
-  s.x_issued = s.w_seen + SK_W_STAGES;
+  s.w_seen = s.w_issued + SK_MAX_W_STAGES;
+  s.x_issued = s.w_seen + SK_MAX_W_STAGES;
   s.x_seen = s.x_issued + SK_MAX_X_STAGES;
   s.conv_uses = s.x_seen + SK_MAX_X_STAGES;
   s.meta = reinterpret_cast<AttnMeta*>(s.conv_uses + SK_MAX_X_STAGES);
   return s;
 }
-constexpr int SMEM_FIXED = SK_W_STAGES * W_STAGE + WORK_BYTES + QTILE_BYTES + SK_MAX_ROWS * 4 + 16 * 4 +
-                           (2 * SK_W_STAGES + 3 * SK_MAX_X_STAGES + 5) * 8 +
-                           (4 + 2 * SK_W_STAGES + 3 * SK_MAX_X_STAGES) * 4 +
-                           (SK_META_UNITS + 1) * (int)sizeof(AttnMeta);
+
 
 // ------------------------------------------------------------------ role: weight producer
 __device__ void weight_producer(const SkMaps& maps, const SkParams& p, const Sync& sy, const Smem& sm, int lm_cnt) {
@@ -378,8 +396,8 @@ __device__ void weight_producer(const SkMaps& maps, const SkParams& p, const Syn
         const Unit g = gemm_unit(p, P, u);
         const CUtensorMap* map = w_map(maps, p, g);
         for (int i = 0; i < g.nk; ++i, ++w_iter) {
-          const int s = w_iter % SK_W_STAGES;
-          if (!bar_wait(&sm.w_empty[s], ((w_iter / SK_W_STAGES) & 1) ^ 1, sm.abort_s, sy, p.status, sm.w_full))
+          const int s = w_iter % sm.ws;
+          if (!bar_wait(&sm.w_empty[s], ((w_iter / sm.ws) & 1) ^ 1, sm.abort_s, sy, p.status, sm.w_full))
             return;
           mbar_arrive_expect_tx(&sm.w_full[s], W_STAGE);
           tma_load_2d(sm.w_ring + s * W_STAGE, map, &sm.w_full[s], (g.k0 + i) * 64, g.stripe * 128);
@@ -448,9 +466,9 @@ __device__ void mma_issuer(const SkParams& p, const Sync& sy, const Smem& sm, ui
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(buf * 256);
         for (int i = 0; i < g.nk; ++i, ++w_iter, ++x_iter) {
-          const int ws = w_iter % SK_W_STAGES;
+          const int ws = w_iter % sm.ws;
           const int xs = x_iter % sm.xs;
-          if (!bar_wait(&sm.w_full[ws], (w_iter / SK_W_STAGES) & 1, sm.abort_s, sy, p.status, sm.w_full)) return;
+          if (!bar_wait(&sm.w_full[ws], (w_iter / sm.ws) & 1, sm.abort_s, sy, p.status, sm.w_full)) return;
           sm.w_seen[ws] += 1;
           if (nx) {
             if (!bar_wait(&sm.x_conv[xs], sm.conv_uses[xs] & 1, sm.abort_s, sy, p.status, sm.w_full)) return;
@@ -484,41 +502,81 @@ __device__ void mma_issuer(const SkParams& p, const Sync& sy, const Smem& sm, ui
 // ------------------------------------------------------------------ compute: X normalisation
 // RMSNorm folded into the X operand (models/qwen3.py:39-44 rounding points): in place in the
 // stage, bf16(bf16(h * rstd) * w) pairwise, h * rstd rounded as torch rounds x.float() * rsqrt.
-__device__ __forceinline__ void nx_chunk(uint32_t addr, float rstd, uint4 w) {
-  uint32_t v[4];
-  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]) : "r"(addr));
+__device__ __forceinline__ uint4 nx_vec(uint4 v, float rstd, uint4 w) {
+  const uint32_t a[4] = {v.x, v.y, v.z, v.w};
   const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+  uint32_t o[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float lo = __uint_as_float(v[i] << 16) * rstd, hi = __uint_as_float(v[i] & 0xFFFF0000u) * rstd;
-    uint32_t packed, r;
+    const float lo = __uint_as_float(a[i] << 16) * rstd, hi = __uint_as_float(a[i] & 0xFFFF0000u) * rstd;
+    uint32_t packed;
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(packed) : "f"(hi), "f"(lo));
-    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(packed), "r"(wv[i]));
-    v[i] = r;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(o[i]) : "r"(packed), "r"(wv[i]));
   }
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3])
-               : "memory");
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// One activation stage normalised by the compute threads: thread t owns the 16-byte column t % 8
+// of rows t / 8, t / 8 + 32, ... (the same swizzled column in each, 32 being a multiple of 8), four
+// rows' loads in flight before their stores. ``w``: the norm weights of that column.
+__device__ __forceinline__ void nx_stage(uint8_t* stage, int rows, const float* rstd, uint4 w, int tid) {
+  const int j = tid & 7, r0 = tid >> 3;
+  const int sw = (j ^ (r0 & 7)) << 4;
+  auto at = [&](int row) { return reinterpret_cast<uint4*>(stage + (row >> 6) * XBOX + (row & 63) * 128 + sw); };
+  int row = r0;
+  for (; row + 96 < rows; row += 128) {
+    uint4 v[4];
+    float rs[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      v[u] = *at(row + 32 * u);
+      rs[u] = rstd[row + 32 * u];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) *at(row + 32 * u) = nx_vec(v[u], rs[u], w);
+  }
+  for (; row < rows; row += 32) *at(row) = nx_vec(*at(row), rstd[row], w);
+}
+
+// 1 / sqrt(mean of squares + eps) of residual row r from its per-stripe sums of squares (added in
+// stripe order; the loads issued together)
+__device__ __forceinline__ float row_rstd(const SkParams& p, int r, int tiles) {
+  const float* src = p.ssq + (long long)r * tiles;
+  float ss = 0.f;
+  int t = 0;
+  if ((tiles & 3) == 0) {
+    for (; t + 8 <= tiles; t += 8) {
+      const float4 a = ldcg_f4(src + t), b = ldcg_f4(src + t + 4);
+      ss += a.x;
+      ss += a.y;
+      ss += a.z;
+      ss += a.w;
+      ss += b.x;
+      ss += b.y;
+      ss += b.z;
+      ss += b.w;
+    }
+  }
+  for (; t < tiles; ++t) ss += __ldcg(src + t);
+  return 1.0f / sqrtf(ss / (float)p.H + p.eps);
 }
 
 // ------------------------------------------------------------------ compute: epilogues on a row chunk
 // ``acc`` is [count][128] fp32 in shared memory (the reduced tile rows r0 .. r0 + count - 1).
-// The rows' positions and slots (``rows_s``: 2 x 64 ints) and their RoPE cos / sin rows
-// (``rope_s``: [count][128] bf16 each) are staged in shared memory first, all loads in flight at
-// once, so that the per-row work below reads no global memory. Called by every compute thread.
-__device__ void epilogue_qkv(const SkParams& p, const Unit& g, const float* acc, int r0, int count, int* rows_s,
-                             __nv_bfloat16* rope_s) {
+// The rows' positions and slots come from the step's row table in shared memory (``rowinfo``:
+// clamped positions [SK_MAX_ROWS], then slots); their RoPE cos / sin rows (``rope_s``:
+// [count][128] bf16 each) are staged in shared memory first, all loads in flight at once, so that
+// the per-row work below reads no global memory. Called by every compute thread.
+__device__ void epilogue_qkv(const SkParams& p, const Unit& g, const float* acc, int r0, int count,
+                             const int* rowinfo, __nv_bfloat16* rope_s) {
   const int tid = threadIdx.x - 128, cw = tid >> 5, lane = tid & 31;
   const int head = g.stripe;
   const bool is_q = head < p.nh;
   const bool is_k = !is_q && head < p.nh + p.nkv;
   const bool rope = is_q || is_k;
   const SkLayer& L = p.layers[g.layer];
-  if (tid < count) {
-    int pos = p.positions[r0 + tid];
-    rows_s[tid] = pos < 0 ? 0 : (pos >= p.max_positions ? p.max_positions - 1 : pos);
-    rows_s[64 + tid] = is_q ? 0 : p.slot_mapping[r0 + tid];
-  }
-  compute_sync();
+  const int* rows_s = rowinfo + r0;
+  const int* slots_s = rowinfo + SK_MAX_ROWS + r0;
   __nv_bfloat16* cos_s = rope_s;
   __nv_bfloat16* sin_s = rope_s + count * 128;
   if (rope) {
@@ -570,7 +628,7 @@ __device__ void epilogue_qkv(const SkParams& p, const Unit& g, const float* acc,
       *reinterpret_cast<uint2*>(p.q + (long long)row * (p.nh * 128) + head * 128 + d0) = packed;
       continue;
     }
-    const long long slot = rows_s[64 + m];
+    const long long slot = slots_s[m];
     if (slot < 0 || slot >= p.num_cache_slots) {
       if (lane == 0) report(p.status, NE_DEV_BAD_SLOT);
       continue;
@@ -1001,11 +1059,17 @@ __device__ void compute_loop(const SkParams& p, const Sync& sy, const Smem& sm, 
   int off = 0;
   const int nph = num_phases(p);
   float* stage = reinterpret_cast<float*>(sm.work);  // reduction / epilogue staging
-  {  // this CTA's attention pairs (dealt from CTA 0 in every layer): their metadata, once
+  {  // this CTA's attention pairs (dealt from CTA 0 in every layer): their metadata, once; and the
+     // step's row table (positions clamped to the RoPE table as the QKV epilogue reads them)
     const int units = p.num_seqs * p.nkv;
     int k = tid >> 5;
     for (int u = blockIdx.x + k * p.grid; u < units && k < SK_META_UNITS; u += NCW * p.grid, k += NCW)
       build_meta(p, u, sm.meta[k]);
+    for (int r = tid; r < R; r += SK_COMPUTE) {
+      const int pos = p.positions[r];
+      sm.rowinfo[r] = pos < 0 ? 0 : (pos >= p.max_positions ? p.max_positions - 1 : pos);
+      sm.rowinfo[SK_MAX_ROWS + r] = p.slot_mapping[r];
+    }
     compute_sync();
   }
   for (int ph = 0; ph < nph; ++ph) {
@@ -1072,28 +1136,23 @@ __device__ void compute_loop(const SkParams& p, const Sync& sy, const Smem& sm, 
       const Unit g = gemm_unit(p, P, u);
       const int rows = P.kind == SK_LM ? lm_cnt : R;
       if (is_nx(P.kind)) {
+        // this thread's norm weights for the unit's first chunk, loaded before the inputs wait
+        const __nv_bfloat16* lnw = P.kind == SK_QKV ? p.layers[P.layer].ln_in : p.layers[P.layer].ln_post;
+        const uint4* wcol = reinterpret_cast<const uint4*>(lnw + g.k0 * 64) + (tid & 7);
+        uint4 w_next = __ldg(wcol);
         if (tid == 0) *sm.flag = (!*sm.abort_s && wait_unit_inputs(p, sy, g, lm_cnt, sm.abort_s)) ? 1 : 0;
         if (!group_read(sm)) return;
         if (tid == 0) stamp(p, ph, 1, true);
         const int tiles = p.H / 128;
-        for (int r = tid; r < rows; r += SK_COMPUTE) {
-          float ss = 0.f;
-          for (int t = 0; t < tiles; ++t) ss += __ldcg(p.ssq + (long long)r * tiles + t);
-          sm.rstd[r] = 1.0f / sqrtf(ss / (float)p.H + p.eps);
-        }
+        for (int r = tid; r < rows; r += SK_COMPUTE) sm.rstd[r] = row_rstd(p, r, tiles);
         compute_sync();
-        const __nv_bfloat16* lnw = P.kind == SK_QKV ? p.layers[P.layer].ln_in : p.layers[P.layer].ln_post;
         for (int i = 0; i < g.nk; ++i, ++x_iter) {
+          const uint4 w = w_next;
+          if (i + 1 < g.nk) w_next = __ldg(wcol + (i + 1) * 8);
           const int xs = x_iter % sm.xs;
           if (!group_bar_wait(sm, sy, p, &sm.x_full[xs], (x_iter / sm.xs) & 1, tid)) return;
           if (tid == 0) sm.x_seen[xs] += 1;
-          const uint32_t st = smem_u32(sm.x_ring + xs * sm.xsb);
-          const uint4* wk = reinterpret_cast<const uint4*>(lnw + (g.k0 + i) * 64);
-          for (int e = tid; e < rows * 8; e += SK_COMPUTE) {
-            const int row = e >> 3, j = e & 7, r64 = row & 63;
-            nx_chunk(st + (uint32_t)((row >> 6) * XBOX + r64 * 128 + ((j ^ (r64 & 7)) << 4)), sm.rstd[row],
-                     __ldg(wk + j));
-          }
+          nx_stage(sm.x_ring + xs * sm.xsb, rows, sm.rstd, w, tid);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm.x_conv[xs]);
@@ -1124,6 +1183,7 @@ __device__ void compute_loop(const SkParams& p, const Sync& sy, const Smem& sm, 
       }
       // partial tile -> global, then the accumulator is free for the next unit
       const SkCut& cut = p.cut[P.kind];
+      const int S = cut.splits;
       float* part = p.part[(P.kind == SK_QKV || P.kind == SK_GATEUP) ? 0 : 1];
       float* mine = part + ((long long)(g.stripe * cut.splits + g.split) * p.R_max) * 128;
       tmem_rows_out<true>(acc_t, 0, rows, mine);
@@ -1135,14 +1195,13 @@ __device__ void compute_loop(const SkParams& p, const Sync& sy, const Smem& sm, 
         __threadfence();
         red_release_add(sy.arrive(P.layer, P.kind, g.stripe), 1);
         stamp(p, ph, 3);
-        *sm.flag = wait_counter(sy.arrive(P.layer, P.kind, g.stripe), cut.splits, sy, p.status, sm.abort_s) ? 1 : 0;
+        *sm.flag = wait_counter(sy.arrive(P.layer, P.kind, g.stripe), S, sy, p.status, sm.abort_s) ? 1 : 0;
         stamp(p, ph, 4);
       }
       if (!group_read(sm)) return;
-      // reduce this split's slice of rows over the S partials (split order), then its epilogue: a
-      // chunk of rows at a time, every partial of the chunk first loaded into shared memory (all
-      // loads in flight together), then summed in split order in place
-      const int S = cut.splits;
+      // reduce the slice's rows over the S partials (split order), then its epilogue: a chunk of
+      // rows at a time, every partial of the chunk first loaded into shared memory (all loads in
+      // flight together), then summed in split order in place
       const int slice = (rows + S - 1) / S;
       const int lo = g.split * slice, hi = min(rows, lo + slice);
       const float* stripe_parts = part + ((long long)g.stripe * S * p.R_max) * 128;
@@ -1167,8 +1226,7 @@ __device__ void compute_loop(const SkParams& p, const Sync& sy, const Smem& sm, 
         }
         compute_sync();
         if (P.kind == SK_QKV)  // (staging past the reduced rows, which are all that is live now)
-          epilogue_qkv(p, g, stage, c0, cnt, reinterpret_cast<int*>(sm.rstd),
-                       reinterpret_cast<__nv_bfloat16*>(stage + cnt * 128));
+          epilogue_qkv(p, g, stage, c0, cnt, sm.rowinfo, reinterpret_cast<__nv_bfloat16*>(stage + cnt * 128));
         else if (P.kind == SK_GATEUP)
           epilogue_swiglu(p, g, stage, c0, cnt);
         else
@@ -1190,11 +1248,13 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* base = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  Smem sm = carve(base, p);
+  const int R = min(max(*p.num_rows, 0), p.R_max);
+  const int lm_cnt = min(max(*p.lm_count, 0), R);
+  Smem sm = carve(base, p, R);
   const Sync sy{p.sync, p.L, p.max_stripes, p.nkv};
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    for (int s = 0; s < SK_W_STAGES; ++s) {
+    for (int s = 0; s < SK_MAX_W_STAGES; ++s) {
       mbar_init(&sm.w_full[s], 1);
       mbar_init(&sm.w_empty[s], 1);
       sm.w_issued[s] = sm.w_seen[s] = 0;
@@ -1221,12 +1281,8 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *sm.tmem_slot;
-  const int R = min(max(*p.num_rows, 0), p.R_max);
-  const int lm_cnt = min(max(*p.lm_count, 0), R);
-  sm.xsb = max(1, (R + 63) / 64) * XBOX;
-  sm.xs = min(SK_MAX_X_STAGES, (p.x_stages * p.x_stage_bytes) / sm.xsb);
   const int nbuf = p.R_max <= 256 ? 2 : 1;
-  if (R > 0 && gridDim.x == (unsigned)p.grid) {
+  if (R > 0 && gridDim.x == (unsigned)p.grid && sm.xs >= 2 && sm.ws >= SK_MIN_W_STAGES) {
     if (warp == 0) {
       if (lane == 0) weight_producer(maps, p, sy, sm, lm_cnt);
     } else if (warp == 1) {
@@ -1247,7 +1303,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
   __syncthreads();
   if (tid == 0) {
     // copies still in flight (only after an abort) land before the shared memory is released
-    for (int s = 0; s < SK_W_STAGES; ++s)
+    for (int s = 0; s < sm.ws; ++s)
       if (sm.w_issued[s] > sm.w_seen[s]) mbar_wait(&sm.w_full[s], sm.w_seen[s] & 1, nullptr, p.status);
     for (int s = 0; s < sm.xs; ++s)
       if (sm.x_issued[s] > sm.x_seen[s]) mbar_wait(&sm.x_full[s], sm.x_seen[s] & 1, nullptr, p.status);
@@ -1289,22 +1345,18 @@ int step_max_units(const SkParams& p) {
   return u;
 }
 
-size_t step_smem_bytes(int R_max, int* x_stages, int* x_stage_bytes) {
-  const int boxes = (R_max + 63) / 64;
-  const int xsb = boxes * XBOX;
-  const int avail = 227 * 1024 - 1024 - SMEM_FIXED;
-  const int xs = std::min(SK_MAX_X_STAGES, avail / xsb);
-  *x_stages = xs;
-  *x_stage_bytes = xsb;
-  if (xs < 2) return 0;
-  return (size_t)1024 + SMEM_FIXED + (size_t)xs * xsb;
+size_t step_smem_bytes(int R_max, int* ring_bytes) {
+  int xs = 0, xsb = 0, ws = 0;
+  ring_split(R_max, SMEM_RING, xs, xsb, ws);
+  *ring_bytes = SMEM_RING;
+  if (xs < 2 || ws < SK_MIN_W_STAGES) return 0;
+  return (size_t)1024 + SMEM_FIXED_ALIGNED + SMEM_RING;
 }
 
 int launch_step_kernel(const SkMaps& maps, const SkParams& p, cudaStream_t stream) {
-  int xs = 0, xsb = 0;
-  const size_t smem = step_smem_bytes(p.R_max, &xs, &xsb);
-  if (smem == 0 || xs != p.x_stages || xsb != p.x_stage_bytes || p.R_max > SK_MAX_ROWS || p.L > SK_MAX_LAYERS)
-    return NE_ERR_INVALID;
+  int ring = 0;
+  const size_t smem = step_smem_bytes(p.R_max, &ring);
+  if (smem == 0 || ring != p.ring_bytes || p.R_max > SK_MAX_ROWS || p.L > SK_MAX_LAYERS) return NE_ERR_INVALID;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return NE_ERR_CUDA;
   static std::mutex mu;

@@ -18,10 +18,15 @@ namespace ne {
 constexpr int SK_THREADS = 384;          // warps 0-3: weight producer, MMA issuer, activation producer, spare
 constexpr int SK_COMPUTE = 256;          // warps 4-11: conversions, epilogues, reductions, attention
 constexpr int SK_MAX_ROWS = 320;         // verify rows (64 entries x 5); above 256 the MMA N is split in two
-constexpr int SK_W_STAGES = 4;           // 16 KB weight tiles in flight per CTA
+// The shared-memory ring area is cut per launch: activation stages for the launch's rows first
+// (at most SK_MAX_X_STAGES), the rest as 16 KB weight stages (at least SK_MIN_W_STAGES): few rows
+// leave room for a deeper weight stream.
+constexpr int SK_MIN_W_STAGES = 4;
+constexpr int SK_MAX_W_STAGES = 12;
 constexpr int SK_MAX_X_STAGES = 4;
 constexpr int SK_MAX_LAYERS = 48;
 constexpr int SK_MAX_QVEC = 16;          // query vectors per (entry, KV head): one 16-row MMA tile
+constexpr int SK_AUTO_ROWS = 80;         // row bound up to which steps take this kernel by default
 
 enum SkKind : int { SK_QKV = 0, SK_O = 1, SK_GATEUP = 2, SK_DOWN = 3, SK_LM = 4, SK_ATTN = 5, SK_FINAL = 6 };
 
@@ -46,7 +51,7 @@ struct SkParams {
   int R_max;       // row bound of this launch (the workspace's X tensor maps hold at least R_max rows)
   int num_seqs;    // batch entries (attention units = num_seqs x nkv)
   int grid;        // CTAs (one per SM)
-  int x_stages, x_stage_bytes;
+  int ring_bytes;  // shared memory for the weight and activation rings (cut per launch)
   int max_stripes; // counter stride
   float eps;
   SkCut cut[5];    // SK_QKV .. SK_LM
@@ -112,7 +117,9 @@ inline size_t step_partial_bytes(int units, int rows) { return (size_t)units * r
 void step_plan_cuts(SkParams& p, int vocab_rows);
 // Largest unit count of the four layer projections (sizes the partial areas).
 int step_max_units(const SkParams& p);
-size_t step_smem_bytes(int R_max, int* x_stages, int* x_stage_bytes);
+// Dynamic shared memory of a launch whose rows are at most R_max (0: too many rows), and the ring
+// area within it.
+size_t step_smem_bytes(int R_max, int* ring_bytes);
 int launch_step_kernel(const SkMaps& maps, const SkParams& p, cudaStream_t stream);
 
 }  // namespace ne

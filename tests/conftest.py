@@ -16,6 +16,9 @@ if str(REPO) not in sys.path:
     sys.path.insert(0, str(REPO))
 
 PACKAGE = "inference-engine-from-scratch_b200"
+# pytest loads this file as ``conftest``; the test modules import it as ``tests.conftest``: one
+# module object for both names, so that state the hooks below read is the state the tests write
+sys.modules.setdefault("tests.conftest", sys.modules[__name__])
 
 
 def pytest_configure(config) -> None:

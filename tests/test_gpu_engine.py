@@ -189,21 +189,34 @@ def test_verify_with_full_length_drafts_matches_the_oracle(small) -> None:
         assert mine.token_ids == ref.token_ids
 
 
-def test_fused_rmsnorm_path_serves_the_reference_outputs() -> None:
-    """NE_FUSED_NORM=1 (RMSNorm folded into the QKV and gate/up GEMMs' X operand) in a fresh
-    process: the serial drop-in and continuous batching still reproduce the reference fixtures."""
+def _rerun_in_a_fresh_process(env_overrides: dict, selection: str) -> None:
     import os
     import subprocess
     import sys
 
     from tests.conftest import REPO
 
-    env = dict(os.environ, NE_FUSED_NORM="1")
+    env = dict(os.environ, **env_overrides)
     proc = subprocess.run(
         [sys.executable, "-m", "pytest", "-q", "-x", "-p", "no:cacheprovider", "tests/test_gpu_engine.py",
-         "-k", "serial_drop_in or continuous_batching or int8_engine"],
-        cwd=REPO, env=env, capture_output=True, text=True, timeout=900)
+         "-k", selection], cwd=REPO, env=env, capture_output=True, text=True, timeout=900)
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-2000:]
+
+
+def test_fused_rmsnorm_path_serves_the_reference_outputs() -> None:
+    """NE_FUSED_NORM=1 (RMSNorm folded into the QKV and gate/up GEMMs' X operand) in a fresh
+    process, with every step on the launch sequence (NE_STEP_KERNEL=0): the serial drop-in and
+    continuous batching still reproduce the reference fixtures."""
+    _rerun_in_a_fresh_process({"NE_FUSED_NORM": "1", "NE_STEP_KERNEL": "0"},
+                              "serial_drop_in or continuous_batching or int8_engine")
+
+
+def test_launch_sequence_serves_the_reference_outputs_at_small_batches() -> None:
+    """Small batches take the persistent step kernel by default; with NE_STEP_KERNEL=0 the same
+    batched-engine tests run every step as the per-projection launch sequence."""
+    _rerun_in_a_fresh_process({"NE_STEP_KERNEL": "0"},
+                              "batched_engine_serial or continuous_batching or shared_prefix or full_length_drafts "
+                              "or preempts")
 
 
 def test_profile_times_every_launch_eagerly_and_inside_a_captured_step(small) -> None:
