@@ -5,7 +5,8 @@ greedy): with the peer exchange for every call (eagerly and through CUDA graphs)
 exchange for the steps only (prefill through NCCL), through NCCL only, and with the two-phase
 exchange. Then rank 0 prefills
 alone on a split model, so that its bounded exchange waits run out. Rank 0 finally serves the
-prompts on the unsplit model (TP = 1, the oracle for the split: the same seeded weights). Each rank
+prompts on the unsplit model (TP = 1, the oracle for the split: the same seeded weights, the same
+per-projection launch sequence). Each rank
 writes its outputs to ``<out>.<rank>.json``.
 """
 
@@ -102,7 +103,11 @@ def main() -> None:
         whole_plan = tp.shard_plan(cfg, 0, 1)
         whole = model_mod.B200Model(cfg, tp.make_sharded_weights(cfg, whole_plan, seed=0, device=device),
                                     num_slots=128 * 16, device=device, max_positions=512, max_rows=512, max_seqs=4)
+        # the unsplit model on the same launch sequence as the split one (the persistent step
+        # kernel, which small batches take by default, adds its partials in another order)
+        os.environ["NE_STEP_KERNEL"] = "0"
         result["unsplit"] = serve(whole, prompts, graphs=True)
+        del os.environ["NE_STEP_KERNEL"]
         whole.close()
     Path(f"{args.out}.{rank}.json").write_text(json.dumps(result))
     dist.barrier()
