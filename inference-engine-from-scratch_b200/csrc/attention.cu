@@ -17,8 +17,12 @@
 // * int8 KV: blocks are dequantised while staged (int8 -> bf16, times the bf16 per (slot, head)
 //   scale, as read_from_cache, attention_context.py:57-63).
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "attention.cuh"
+#include "gemm_tc.cuh"
 
 namespace ne {
 
@@ -254,7 +258,18 @@ __device__ __forceinline__ void tile_init(TileState& ts, uint32_t q_s, const int
   ts.pos[1] = spos[(lane >> 2) + 8];
 }
 
+// Shared-memory address of (token, dimension col) in a staged K or V block: the padded row layout
+// (cp.async and conversions), or (SW) the tensor-load layout: two 2 KB boxes of dimensions 0-63 and
+// 64-127, rows of 128 B whose 16-byte chunk c sits at c ^ (token % 8) (the 128-byte swizzle).
+template <bool SW>
+__device__ __forceinline__ uint32_t kv_addr(uint32_t base, int tok, int col) {
+  if (!SW) return base + tok * ROW_BYTES + col * 2;
+  const int c = col >> 3;
+  return base + (c >> 3) * 2048 + tok * 128 + (((c & 7) ^ (tok & 7)) << 4);
+}
+
 // One 16-token block (logical index kb) staged at k_s / v_s against the tile.
+template <bool SW = false>
 __device__ __forceinline__ void tile_block(TileState& ts, uint32_t k_s, uint32_t v_s, int kb, int lane) {
   float s[2][4];
 #pragma unroll
@@ -265,7 +280,7 @@ __device__ __forceinline__ void tile_block(TileState& ts, uint32_t k_s, uint32_t
       uint32_t b[4];
       const int tok = 8 * j + (lane & 7);
       const int col = 16 * kk + 8 * (lane >> 3);
-      ldsm_x4(b, k_s + tok * ROW_BYTES + col * 2);
+      ldsm_x4(b, kv_addr<SW>(k_s, tok, col));
       mma16816(s[j], ts.qa[kk], b[0], b[1]);
       mma16816(s[j], ts.qa[kk + 1], b[2], b[3]);
     }
@@ -327,7 +342,7 @@ __device__ __forceinline__ void tile_block(TileState& ts, uint32_t k_s, uint32_t
     uint32_t b[4];
     const int tok = (lane & 7) + 8 * ((lane >> 3) & 1);
     const int col = 8 * t + 8 * (lane >> 4);
-    ldsm_x4_t(b, v_s + tok * ROW_BYTES + col * 2);
+    ldsm_x4_t(b, kv_addr<SW>(v_s, tok, col));
     mma16816(ts.o[t], pa, b[0], b[1]);
     mma16816(ts.o[t + 1], pa, b[2], b[3]);
   }
@@ -460,17 +475,50 @@ __device__ __forceinline__ void tile_store(const Ctx& c, const AttnSplit& sp, co
   }
 }
 
+// The tensor-load pipeline of a bf16 pool (attention_tma_kernel): the K and V maps (x the head
+// dimension, y the KV head, z the slot) and two stage barriers per warp. A warp's stage is 8 KB
+// (K in two 2 KB boxes, then V), 1024-byte aligned as the 128-byte swizzle wants.
+struct TmaKv {
+  const CUtensorMap* k;
+  const CUtensorMap* v;
+  uint64_t* bars;  // [warps][2]
+};
+constexpr int TMA_STAGE_BYTES = 2 * 16 * D * 2;        // K + V of one block
+constexpr int TMA_WARP_BYTES = 2 * TMA_STAGE_BYTES;    // two stages
+constexpr int TMA_HEAD_BYTES = 5120;                   // Q tile + positions, rounded up to 1024
+
 // One or two query tiles (the speculative step): warp w serves query tile w % NT and every
 // (4 / NT)-th block of the split from its own double buffer (bf16: two K/V stages; int8: two raw
 // stages + one converted K/V pair); the warps of a tile merge (max, sum, O) through smem at the end.
-template <bool INT8, int NT, int NW>
+// TMA (bf16 pools, attention_tma_kernel): each block is two tensor loads of K and two of V issued
+// by lane 0 into the warp's next stage, completion on the stage's mbarrier (bounded wait).
+template <bool INT8, int NT, int NW, bool TMA = false>
 __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& rows, const AttnSplit& sp, int b, int h,
                                                  int split, int kb0, int kb1, uint8_t* q_s, int* spos, uint8_t* buf,
-                                                 __nv_bfloat16* out, int nh, int nkv, int v_base = 0) {
+                                                 __nv_bfloat16* out, int nh, int nkv, int v_base = 0,
+                                                 const TmaKv* tk = nullptr) {
+  static_assert(!(TMA && INT8), "tensor loads serve bf16 pools");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t buf_u = smem_u32(buf);
   const int per_tile = NW / NT, my_tile = warp % NT, phase = warp / NT;
-  const uint32_t wbuf = buf_u + warp * 4 * BLOCK_BYTES;
+  const uint32_t wbuf = buf_u + warp * (TMA ? TMA_WARP_BYTES : 4 * BLOCK_BYTES);
+  uint8_t* wbuf_p = buf + warp * (TMA ? TMA_WARP_BYTES : 4 * BLOCK_BYTES);
+  uint64_t* wbar = TMA ? tk->bars + 2 * warp : nullptr;
+  // loads issued to / waited for on stage 0 and stage 1 (registers, not an indexed array)
+  uint32_t issued0 = 0u, issued1 = 0u, used0 = 0u, used1 = 0u;
+  bool tma_ok = true;  // warp-uniform: no wait has run out
+  auto tma_issue = [&](long long blk_id, int st) {
+    if (lane == 0) {
+      uint8_t* dst = wbuf_p + st * TMA_STAGE_BYTES;
+      const int z = (int)(blk_id * 16);
+      mbar_arrive_expect_tx(&wbar[st], TMA_STAGE_BYTES);
+      tma_load_3d(dst, tk->k, &wbar[st], 0, c.h, z);
+      tma_load_3d(dst + 2048, tk->k, &wbar[st], 64, c.h, z);
+      tma_load_3d(dst + 4096, tk->v, &wbar[st], 0, c.h, z);
+      tma_load_3d(dst + 6144, tk->v, &wbar[st], 64, c.h, z);
+    }
+    if (st) ++issued1; else ++issued0;
+  };
   // the table entries of this warp's blocks (the j-th is logical block kb0 + phase + per_tile * j),
   // 32 at a time in the lanes of a register: no dependent global load inside the block loop
   const int stride = rows.block_table_stride;
@@ -497,6 +545,8 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
     } else if (INT8) {
       stage_raw_int8(c, blk, wbuf, lane);
       scales = load_scales_int8(c, blk, lane);
+    } else if (TMA) {
+      tma_issue(blk, 0);
     } else {
       stage_block<INT8>(c, blk, wbuf, wbuf + BLOCK_BYTES, lane, 32);
     }
@@ -570,6 +620,18 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
       }
       __syncwarp();
       scales = next_scales;
+    } else if (TMA) {
+      // the next block into the other stage (read by the previous iteration, which ended with a
+      // __syncwarp), then this block's stage
+      if (nblk_id >= 0 && tma_ok) tma_issue(nblk_id, stage ^ 1);
+      if (blk >= 0 && tma_ok) {
+        const uint32_t parity = (stage ? used1 : used0) & 1u;
+        tma_ok = __all_sync(0xFFFFFFFFu, mbar_wait(&wbar[stage], parity, nullptr, c.status));
+        if (stage) ++used1; else ++used0;
+        const uint32_t cur = wbuf + stage * TMA_STAGE_BYTES;
+        if (tma_ok) tile_block<true>(ts, cur, cur + TMA_STAGE_BYTES / 2, kb, lane);
+      }
+      __syncwarp();
     } else {
       const uint32_t nxt = wbuf + (stage ^ 1) * 2 * BLOCK_BYTES;
       if (nblk_id >= 0) stage_block<INT8>(c, nblk_id, nxt, nxt + BLOCK_BYTES, lane, 32);
@@ -582,6 +644,12 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
     }
     blk = nblk_id;
     stage ^= 1;
+  }
+  if (TMA) {
+    // every tensor load issued has landed before the buffers become the merge area (bounded: a
+    // wait that runs out has reported the timeout)
+    for (; used0 < issued0; ++used0) mbar_wait(&wbar[0], used0 & 1u, nullptr, c.status);
+    for (; used1 < issued1; ++used1) mbar_wait(&wbar[1], used1 & 1u, nullptr, c.status);
   }
   cp_wait<0>();
   // merge the warps of each tile through smem (reusing the stage buffers)
@@ -762,6 +830,66 @@ __global__ void __launch_bounds__(32 * NW, NW == 8 ? 1 : NW == 4 ? 3 : 5)
 }
 
 // Merge the split partials of every (entry, KV head): softmax-weighted sum in fp32, bf16 output.
+// The speculative step's attention over a bf16 pool with tensor loads (one or two query tiles per
+// CTA, as attention_kernel's warp path): K and V blocks arrive by cp.async.bulk.tensor into 128-byte
+// swizzled stages, two per warp, one elected lane issuing a block's four loads.
+template <int NW>
+__global__ void __launch_bounds__(32 * NW, NW == 4 ? 3 : 5)
+    attention_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                         const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out, ne_rows rows, int nh,
+                         int nkv, long long num_cache_slots, AttnSplit sp, int* status) {
+  pdl_prologue();
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int slots = gridDim.z / sp.splits;
+  const int b = blockIdx.x, h = blockIdx.y, split = blockIdx.z / slots, tile = blockIdx.z % slots;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int ql = rows.q_len[b];
+  if (ql <= 0) return;
+  Ctx c{};
+  c.q = q;
+  c.out = out;
+  c.nh = nh;
+  c.nkv = nkv;
+  c.h = h;
+  c.G = nh / nkv;
+  c.r0 = rows.q_start[b];
+  c.nvec = ql * c.G;
+  c.num_cache_slots = num_cache_slots;
+  c.status = status;
+  c.table = rows.block_tables + (long long)(rows.table_index ? rows.table_index[b] : b) * rows.block_table_stride;
+  const int ctx = rows.positions[c.r0 + ql - 1] + 1;  // the last row sees the whole context
+  const int nblk = (ctx + 15) / 16;
+  const int bps = (nblk + sp.splits - 1) / sp.splits;
+  const int kb0 = split * bps, kb1 = min(nblk, kb0 + bps);
+  const int ntiles = (c.nvec + 15) / 16;
+  uint8_t* q_s = smem;                                     // 16 x ROW_BYTES
+  int* spos = reinterpret_cast<int*>(smem + BLOCK_BYTES);  // 16 ints (+pad)
+  uint8_t* buf = smem + TMA_HEAD_BYTES;                    // NW x two 8 KB stages
+  uint64_t* bars = reinterpret_cast<uint64_t*>(buf + NW * TMA_WARP_BYTES);
+  if (lane == 0) {
+    mbar_init(&bars[2 * warp], 1);
+    mbar_init(&bars[2 * warp + 1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const TmaKv tk{&kmap, &vmap, bars};
+  if (slots > 1) {
+    if (tile < ntiles)
+      warp_split_tiles<false, 1, NW, true>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv,
+                                           16 * tile, &tk);
+  } else if (ntiles == 1) {
+    warp_split_tiles<false, 1, NW, true>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 0, &tk);
+  } else if constexpr (NW == 4) {
+    if (ntiles == 2)
+      warp_split_tiles<false, 2, 4, true>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 0, &tk);
+    else
+      report(status, NE_DEV_BAD_SLOT);  // the host sends only one- and two-tile entries here
+  } else {
+    report(status, NE_DEV_BAD_SLOT);
+  }
+}
+
 __global__ void __launch_bounds__(D) combine_kernel(const ne_rows rows, int nh, int nkv, AttnSplit sp,
                                                     __nv_bfloat16* __restrict__ out) {
   pdl_prologue();
@@ -851,6 +979,42 @@ __global__ void kv_shadow_map_kernel(const int32_t* __restrict__ table, int num_
   }
 }
 
+size_t attention_tma_smem_bytes(int nw) {
+  return 1024 + TMA_HEAD_BYTES + (size_t)nw * TMA_WARP_BYTES + (size_t)nw * 2 * sizeof(uint64_t);
+}
+
+// Tensor maps of a bf16 pool's per-layer K or V array, encoded once per (array, heads, slots).
+bool kv_tensor_map(const void* base, int nkv, long long slots, CUtensorMap* out) {
+  struct Key {
+    const void* base;
+    int nkv;
+    long long slots;
+    bool operator<(const Key& o) const { return std::tie(base, nkv, slots) < std::tie(o.base, o.nkv, o.slots); }
+  };
+  static std::mutex mu;
+  static std::map<Key, CUtensorMap> maps;
+  std::lock_guard<std::mutex> lock(mu);
+  const Key key{base, nkv, slots};
+  auto it = maps.find(key);
+  if (it == maps.end()) {
+    CUtensorMap m;
+    if (!make_tmap_kv(&m, base, nkv, slots)) return false;
+    if (maps.size() > 4096) maps.clear();
+    it = maps.emplace(key, m).first;
+  }
+  *out = it->second;
+  return true;
+}
+
+// NE_ATTN_TMA=0: the bf16 speculative-step attention stages K / V with cp.async instead of tensor loads.
+bool attention_tma_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("NE_ATTN_TMA");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 size_t attention_smem_bytes_nw(int nw) {
   if (nw == 4) return attention_smem_bytes();
   // eight warps (prefill only): two stages of CHUNK_BLOCKS (K, V) blocks + eight Q tiles behind them
@@ -929,19 +1093,26 @@ int launch_attention_tc(const __nv_bfloat16* q, __nv_bfloat16* out, const void* 
   }();
   const int nw = max_vec > 32 && tile_slots == 1 ? prefill_warps
                  : ((max_vec <= 16 || tile_slots > 1) && ctas <= 5LL * sms && ctas > 3LL * sms) ? 2 : 4;
-  const size_t smem = attention_smem_bytes_nw(nw);
+  // the speculative step over a bf16 pool: tensor loads of K / V (the cp.async kernel otherwise)
+  CUtensorMap kmap, vmap;
+  const bool tma = !kv_int8 && !shadow.map && nw != 8 && attention_tma_enabled() &&
+                   kv_tensor_map(k_cache, num_kv_heads, num_cache_slots, &kmap) &&
+                   kv_tensor_map(v_cache, num_kv_heads, num_cache_slots, &vmap);
+  const size_t smem = tma ? attention_tma_smem_bytes(nw) : attention_smem_bytes_nw(nw);
   // the shared-memory limit is a per-device function attribute: set once per (device, variant)
   constexpr int MAX_DEVICES = 64;
-  static bool attr_set[MAX_DEVICES][6] = {};
+  static bool attr_set[MAX_DEVICES][8] = {};
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return NE_ERR_CUDA;
   auto kernel = kv_int8 ? (nw == 2 ? attention_kernel<true, 2> : nw == 8 ? attention_kernel<true, 8>
                                                                           : attention_kernel<true, 4>)
                         : (nw == 2 ? attention_kernel<false, 2> : nw == 8 ? attention_kernel<false, 8>
                                                                            : attention_kernel<false, 4>);
-  const int ai = (kv_int8 ? 3 : 0) + (nw == 2 ? 1 : nw == 8 ? 2 : 0);
+  auto tma_kernel = nw == 2 ? attention_tma_kernel<2> : attention_tma_kernel<4>;
+  const int ai = tma ? (nw == 2 ? 6 : 7) : (kv_int8 ? 3 : 0) + (nw == 2 ? 1 : nw == 8 ? 2 : 0);
   if (!attr_set[dev][ai]) {
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-      return NE_ERR_CUDA;
+    const cudaError_t err = tma ? cudaFuncSetAttribute(tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+                                : cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err != cudaSuccess) return NE_ERR_CUDA;
     attr_set[dev][ai] = true;
   }
   if (sp.splits > 1) {
@@ -955,9 +1126,14 @@ int launch_attention_tc(const __nv_bfloat16* q, __nv_bfloat16* out, const void* 
   const int group_slots = nw == 8 ? std::min(1024, (max_vec + 127) / 128) : 1;
   dim3 grid(rows.num_seqs, num_kv_heads, sp.splits * tile_slots * group_slots);
   if (shadow.map && (!kv_int8 || !shadow.k || !shadow.v || shadow.blocks < 1)) return NE_ERR_INVALID;
-  if (launch_kernel(kernel, grid, dim3(32 * nw), smem, stream, q, out, k_cache, v_cache, k_scale, v_scale, rows,
-                    num_heads, num_kv_heads, num_cache_slots, sp, status, shadow) != cudaSuccess)
+  if (tma) {
+    if (launch_kernel(tma_kernel, grid, dim3(32 * nw), smem, stream, kmap, vmap, q, out, rows, num_heads,
+                      num_kv_heads, num_cache_slots, sp, status) != cudaSuccess)
+      return NE_ERR_CUDA;
+  } else if (launch_kernel(kernel, grid, dim3(32 * nw), smem, stream, q, out, k_cache, v_cache, k_scale, v_scale,
+                           rows, num_heads, num_kv_heads, num_cache_slots, sp, status, shadow) != cudaSuccess) {
     return NE_ERR_CUDA;
+  }
   if (sp.splits > 1) {
     if (launch_kernel(combine_kernel, dim3(rows.num_seqs, num_kv_heads), dim3(D), 0, stream, rows, num_heads,
                       num_kv_heads, sp, out) != cudaSuccess)

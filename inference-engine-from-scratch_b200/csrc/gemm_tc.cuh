@@ -128,6 +128,9 @@ bool make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
                     uint32_t box_cols);
 // int8 weights [rows, cols]: box 128 rows x 64 columns, 64-byte swizzle (conflict-free row reads)
 bool make_tmap_w8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols);
+// A paged bf16 KV pool [slots][nkv][128] as a 3-D map whose box is one KV head's 16-token block,
+// half the head dimension at a time (64 x 1 x 16, 128-byte swizzle): two loads per K or V block.
+bool make_tmap_kv(CUtensorMap* map, const void* base, int nkv, long long slots);
 constexpr int GEMM_W8_TILE_BYTES = GEMM_BM * GEMM_BK;  // int8 staging per stage
 
 }  // namespace ne

@@ -5,7 +5,8 @@ The guesses are drawn from the draft's distribution on the request's Philox stre
 against it: acceptance min(1, p(g) / q(g)), and on a rejection a draw from max(0, p - q)
 renormalised. As for one-hot drafts (tests/test_gpu_sampling.py), the GPU's own softmax differs
 from torch's in the last bits, so a decision whose two sides are closer than MARGIN may fall the
-other way; every mismatch with the oracle must be such a near-tie and most cases must match.
+other way; every mismatch with the oracle must be such a near-tie, and at most 3% of a set's cases
+(at least one) may be excused.
 """
 
 from __future__ import annotations
@@ -25,7 +26,11 @@ pytestmark = pytest.mark.gpu
 
 MARGIN = 1e-5
 TOPP_MARGIN = 1e-6
-MIN_EXACT = 0.9
+MAX_EXCUSED = 0.03  # excused near-ties per set (at least one allowed); observed on B200: none
+
+
+def max_excused(cases: int) -> int:
+    return max(1, int(MAX_EXCUSED * cases))
 
 
 def _kept(logits: torch.Tensor, temperature: float, top_p: float):
@@ -162,7 +167,7 @@ def check(cases, got, draws, name="drafted verify"):
         assert m < MARGIN or m < TOPP_MARGIN, f"mismatch without a near-tie: got {g} ({d}), expected {e} ({ed})"
         margins.append(m)
     report_near_ties(name, len(cases), exact, margins)
-    assert exact >= MIN_EXACT * len(cases), f"only {exact} of {len(cases)} match exactly"
+    assert len(cases) - exact <= max_excused(len(cases)), f"only {exact} of {len(cases)} match exactly"
 
 
 @pytest.mark.parametrize("vocab,temperature,top_p", [(512, 0.8, 0.95), (151936, 0.8, 0.95), (4096, 1.0, 1.0),
@@ -264,7 +269,7 @@ def test_serial_sampled_draft_model_replays_on_the_oracle() -> None:
         margins.append(draft_margin(case))
         assert margins[-1] < MARGIN, f"mismatch without a near-tie: got {g}, expected {e}"
     report_near_ties("serial drafted replay", len(cases), exact, margins)
-    assert exact >= MIN_EXACT * len(cases)
+    assert len(cases) - exact <= max_excused(len(cases))
     assert len(cases) >= len(golden["records"]) and any(c["guesses"] for c in cases)
     target.close()
     draft_model.close()
@@ -341,7 +346,7 @@ def test_batched_engine_sampled_draft_steps_replay_on_the_oracle(cuda_graphs) ->
                 assert res.tokens[s] == (guesses[:kept] + [am[kept]])[: len(res.tokens[s])]
         running = [s for s in running if res.finish[s] is None]
     report_near_ties("engine drafted steps", total, exact, margins)
-    assert total > 0 and exact >= MIN_EXACT * total
+    assert total > 0 and total - exact <= max_excused(total)
     target.raise_on_device_error()
     draft_model.raise_on_device_error()
     del eng

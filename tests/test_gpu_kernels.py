@@ -224,3 +224,20 @@ def test_paged_attention_matches_fp32_reference(lib, cuda_device, nh, nkv, q_len
     want = _attention_reference(q, k_cache, v_cache, tables, q_start, q_lens, positions, nh, nkv, k_scale, v_scale)
     # P is rounded to bf16 before the PV product (as flash attention does); outputs are bf16
     torch.testing.assert_close(out.cpu().float(), want, rtol=2e-2, atol=2e-2)
+
+
+def test_cp_async_staging_matches_the_fp32_reference_too() -> None:
+    """The speculative step's bf16 attention loads K / V with tensor loads (TMA) by default; with
+    NE_ATTN_TMA=0 it stages them with cp.async: the same cases, that path, in a fresh process."""
+    import os
+    import subprocess
+    import sys
+
+    from tests.conftest import REPO
+
+    env = dict(os.environ, NE_ATTN_TMA="0")
+    proc = subprocess.run(
+        [sys.executable, "-m", "pytest", "-q", "-x", "-p", "no:cacheprovider", "tests/test_gpu_kernels.py", "-k",
+         "paged_attention_matches_fp32_reference and False"], cwd=REPO, env=env, capture_output=True, text=True,
+        timeout=900)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-2000:]
