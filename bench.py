@@ -16,11 +16,15 @@
   algorithmic bytes per launch over its average duration, against MEASURED_PEAKS.json.
 * ``cpu_baseline``: the CPU oracle (the reference's serial speculative path restated, fp32, config 1's
   prompt) on this host's cores for a bounded sample.
+* ``repeats``: the steady-state measurement repeated ``--repeats`` times on fresh copies of the
+  workload (per-step times, median, spread); ``value`` is the first.
+* ``per_users`` (config 2 at 1, 4 and 16 users) and ``workloads`` (configs 3 and 4) on one GPU.
 
-Other BASELINE workloads (not the default line): ``--workload c3`` (int8 weights + int8 KV, 64 users,
+Other BASELINE workloads (alone, with ``--workload``): ``--workload c3`` (int8 weights + int8 KV, 64 users,
 k=8, 1024-token prompts whose first 512 tokens are one shared prefix served from shared KV blocks,
 256 outputs) and ``--workload c4`` (256 users, sampled T=0.8 / top-p 0.95 on per-request Philox
-streams, prompt lengths uniform in [32, 2048], chunked prefill of 512 tokens, 256 outputs, k=4), ``--workload c5b`` (Qwen3-8B shape, bf16, tensor-parallel over the N torchrun ranks:
+streams, prompt lengths uniform in [32, 2048], chunked prefill of 512 tokens, 256 outputs, k=4),
+``--workload c5b`` (Qwen3-8B shape, bf16, tensor-parallel over the N torchrun ranks:
 o_proj / down_proj push their fp32 partials into every rank's exchange region over NVLink for
 steps of up to ``--tp-exchange-rows`` rows, NCCL all-reduce above that; 32 users, 512-token
 prompts, 256 outputs, k=4).
@@ -74,6 +78,9 @@ def parse_args():
     p.add_argument("--prompt-len", type=int, default=64)
     p.add_argument("--max-new", type=int, default=128)
     p.add_argument("--cpu-seconds", type=float, default=15.0)
+    p.add_argument("--repeats", type=int, default=4,
+                   help="times the steady-state measurement is repeated on a fresh copy of the workload (reported "
+                        "under 'repeats'; value is the first)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-extra", action="store_true",
@@ -675,6 +682,27 @@ def run_b200(args, dist: Dist) -> None:
     if prefix is not None:
         engine.drop_prefix(prefix)
 
+    # ------------------------------------------------------------ repeats of the steady-state timing
+    # the same measurement again on a fresh copy of the workload (requests loaded and prefilled
+    # anew, the same warm-up, exactly ``steps`` timed replays), so that the line shows how steady
+    # the headline is; ``value`` stays the first timing
+    repeat_ms = [max_ms / args.steps]
+    for _ in range(args.repeats):
+        rep_prefix = engine.add_prefix(prompts[0][: wl.shared_prefix]) if wl.shared_prefix else None
+        rep_slots = engine.add_requests(prompts, [steady_new] * len(prompts), ignore_eos=True,
+                                        temperature=wl.temperature, top_p=wl.top_p, seeds=list(range(len(prompts))),
+                                        prefix=rep_prefix)
+        engine.prefill(rep_slots, chunk=wl.prefill_chunk)
+        rep, _, _ = time_steady_steps(engine, engine_mod, rep_slots, args.steps, args.warmup, dist)
+        repeat_ms.append(dist.max(rep) / args.steps)
+        engine.release(rep_slots)
+        if rep_prefix is not None:
+            engine.drop_prefix(rep_prefix)
+    ordered = sorted(repeat_ms)
+    repeats = {"ms_per_step": [round(x, 4) for x in repeat_ms],
+               "median_ms_per_step": round(ordered[len(ordered) // 2], 4),
+               "spread": round(ordered[-1] / ordered[0] - 1.0, 4)}
+
     # ------------------------------------------------------------ e2e: the whole job through the public API
     e2e = None
     if not args.no_e2e:
@@ -738,7 +766,7 @@ def run_b200(args, dist: Dist) -> None:
             "clocks": clocks.summary(), "gpu_launches": int(launches_per_step * args.steps),
             "launches_per_step": int(launches_per_step), "emitted_tokens": int(total_emitted),
             "tokens_per_step_per_user": round(total_emitted / (1 if wl.tp else dist.world) / args.steps / users, 3),
-            "kernel_profile": profile,
+            "kernel_profile": profile, "repeats": repeats,
         }
         if per_users is not None:
             line["per_users"] = per_users
