@@ -528,10 +528,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   // activation tile's bytes are added below.
   // only m-block 0 prefetches: a later m-block may find no rows (the step's rows are a device count)
   const int pre = blockIdx.z == 0 ? min(stages, nk) : 0;
+  // a verify-sized GEMM reads each weight tile once: it is streamed through L2 evict-first, so that
+  // the activation tiles every CTA re-reads stay (prefill-sized GEMMs re-read weights per m-block)
+  const bool stream_w = p.M_max <= 512;
+  const uint64_t w_policy = l2_evict_first_policy();
+  auto load_w = [&](void* dst, uint64_t* bar, int kx) {
+    if (stream_w)
+      tma_load_2d_hint(dst, &tm_w, bar, kx, tile_n * GEMM_BM, w_policy);
+    else
+      tma_load_2d(dst, &tm_w, bar, kx, tile_n * GEMM_BM);
+  };
   if (warp == 0 && lane == 0) {
     for (int i = 0; i < pre; ++i) {
       mbar_expect_tx(&full[i], w_load_bytes);
-      tma_load_2d(smem + i * stage_bytes + w_dst_off, &tm_w, &full[i], (k_begin + i) * GEMM_BK, tile_n * GEMM_BM);
+      load_w(smem + i * stage_bytes + w_dst_off, &full[i], (k_begin + i) * GEMM_BK);
     }
   }
   pdl_wait();
@@ -589,7 +599,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         uint8_t* st = smem + s * stage_bytes;
         mbar_arrive_expect_tx(&full[s], w_load_bytes + x_bytes);
         const int kx = (k_begin + i) * GEMM_BK;
-        tma_load_2d(st + w_dst_off, &tm_w, &full[s], kx, tile_n * GEMM_BM);
+        load_w(st + w_dst_off, &full[s], kx);
         for (int l = 0; l < n_loads; ++l)
           tma_load_2d(st + w_bytes + l * GEMM_XBOX * GEMM_BK * 2, &tm_x, &full[s], kx, m0 + l * GEMM_XBOX);
         issued = i + 1;

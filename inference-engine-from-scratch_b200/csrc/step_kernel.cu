@@ -389,6 +389,7 @@ __device__ void weight_producer(const SkMaps& maps, const SkParams& p, const Syn
   int w_iter = 0;
   int off = 0;
   const int nph = num_phases(p);
+  const uint64_t stream_once = l2_evict_first_policy();  // every weight tile is read once per step
   for (int ph = 0; ph < nph; ++ph) {
     const Phase P = phase_at(p, ph, lm_cnt);
     if (is_gemm(P.kind)) {
@@ -400,7 +401,7 @@ __device__ void weight_producer(const SkMaps& maps, const SkParams& p, const Syn
           if (!bar_wait(&sm.w_empty[s], ((w_iter / sm.ws) & 1) ^ 1, sm.abort_s, sy, p.status, sm.w_full))
             return;
           mbar_arrive_expect_tx(&sm.w_full[s], W_STAGE);
-          tma_load_2d(sm.w_ring + s * W_STAGE, map, &sm.w_full[s], (g.k0 + i) * 64, g.stripe * 128);
+          tma_load_2d_hint(sm.w_ring + s * W_STAGE, map, &sm.w_full[s], (g.k0 + i) * 64, g.stripe * 128, stream_once);
           sm.w_issued[s] += 1;
         }
       }
