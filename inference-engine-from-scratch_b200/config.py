@@ -115,8 +115,6 @@ class SpeculativeSettings:
                 raise ValueError("the b200 speculative backend computes in bfloat16")
             if self.kv_block_size != 16:
                 raise ValueError("the b200 speculative backend uses 16-token KV blocks")
-            if self.speculative == "draft":
-                raise ValueError("the b200 speculative backend implements the n-gram proposer")
 
     @property
     def is_int8_kv_cache(self) -> bool:

@@ -6,9 +6,9 @@ backend a nanoengine deployment loads, next to its runtime.
 * ``B200EngineSettings``: the reference's ``EngineSettings`` (config.py:23-102) plus
   ``speculative_backend`` (``NANOENGINE_SPECULATIVE_BACKEND``, ``torch`` | ``b200``). The
   reference's validator (config.py:81-99) refuses speculative decoding under a batch scheduler
-  (:91-97); with the b200 backend that one rule is replaced by the backend's own (continuous scheduler, paged KV in
-  16-token blocks, no prefix cache, no chunked prefill, bfloat16, n-gram drafts), and every other
-  check of the reference's validator still runs.
+  (:91-97); with the b200 backend that one rule is replaced by the backend's own (continuous
+  scheduler, paged KV in 16-token blocks, no prefix cache, no chunked prefill, bfloat16, n-gram or
+  draft-model drafts), and every other check of the reference's validator still runs.
 * ``SpeculativeBatchEngineLoop``: the reference's ``BatchEngineLoop`` (engine/scheduling/
   batch_engine_loop.py:35-176) with ``_execute_plan`` (:114-130) running each plan as one batched
   speculative step (``batch_step.SpeculativeBatchExecutor``). The loop's admission, streaming,
@@ -26,7 +26,13 @@ from typing import Literal
 
 import torch
 from nanoengine.config import EngineSettings
-from nanoengine.constants import KV_CACHE_PAGED, SCHEDULER_CONTINUOUS, SPECULATIVE_NGRAM, SPECULATIVE_NONE
+from nanoengine.constants import (
+    KV_CACHE_PAGED,
+    SCHEDULER_CONTINUOUS,
+    SPECULATIVE_DRAFT,
+    SPECULATIVE_NGRAM,
+    SPECULATIVE_NONE,
+)
 from nanoengine.engine.memory.kv_cache_pool import count_slots_for_budget
 from nanoengine.engine.memory.paged_allocator import PagedSlotAllocator
 from nanoengine.engine.metrics import EngineMetrics
@@ -59,8 +65,8 @@ class B200EngineSettings(EngineSettings):
             problems.append("no prefix_cache and no chunked_prefill")
         if self.dtype != "bfloat16":
             problems.append("dtype=bfloat16")
-        if self.speculative != SPECULATIVE_NGRAM:
-            problems.append("speculative=ngram")
+        if self.speculative not in (SPECULATIVE_NGRAM, SPECULATIVE_DRAFT):
+            problems.append("speculative=ngram or draft")
         if problems:
             raise ValueError("speculative_backend=b200 needs " + ", ".join(problems))
         return self
@@ -110,10 +116,12 @@ def num_kv_blocks(model_config, settings: EngineSettings) -> int:
 
 
 def create_b200_engine(model, stop_token_ids: frozenset[int], settings: B200EngineSettings,
-                       metrics: EngineMetrics, *, engine=None) -> SpeculativeBatchEngineLoop:
+                       metrics: EngineMetrics, draft_model=None, *, engine=None) -> SpeculativeBatchEngineLoop:
     """The b200 branch of ``runtime.create_engine``: ``model`` is the reference's
-    ``Qwen3ForCausalLM`` whose weights the B200 model takes (``engine``: a prebuilt
-    ``B200SpeculativeEngine``, or any object with its request API)."""
+    ``Qwen3ForCausalLM`` whose weights the B200 model takes; ``draft_model`` (speculative=draft) the
+    reference's draft model, loaded as ``runtime.create_proposer`` loads it (runtime.py:115-129),
+    whose weights a second B200 model takes with its own KV pool of as many blocks (``engine``: a
+    prebuilt ``B200SpeculativeEngine``, or any object with its request API)."""
     if settings.speculative_backend != BACKEND_B200:
         raise ValueError("create_b200_engine serves speculative_backend=b200")
     device = torch.device(settings.device)
@@ -123,16 +131,25 @@ def create_b200_engine(model, stop_token_ids: frozenset[int], settings: B200Engi
         from .model import B200Model
 
         k = settings.num_speculative_tokens
-        weights = {name: t.detach() for name, t in model.state_dict().items()}
-        b200 = B200Model(b200_config(model.config), weights, num_slots=num_blocks * B200_BLOCK_SIZE, device=device,
-                         max_positions=settings.max_model_len + k + 1, kv_int8=settings.is_int8_kv_cache,
-                         max_rows=max(settings.max_num_seqs * (k + 1), settings.max_prefill_tokens),
-                         max_seqs=settings.max_num_seqs, weight_int8=settings.quantization == "int8")
-        engine = B200SpeculativeEngine(b200, k=k, max_ngram=settings.ngram_max_size,
+
+        def device_model(ref_model, int8: bool):
+            weights = {name: t.detach() for name, t in ref_model.state_dict().items()}
+            return B200Model(b200_config(ref_model.config), weights, num_slots=num_blocks * B200_BLOCK_SIZE,
+                             device=device, max_positions=settings.max_model_len + k + 1,
+                             kv_int8=int8 and settings.is_int8_kv_cache,
+                             max_rows=max(settings.max_num_seqs * (k + 1), settings.max_prefill_tokens),
+                             max_seqs=settings.max_num_seqs, weight_int8=int8 and settings.quantization == "int8")
+
+        draft = None
+        if settings.speculative == SPECULATIVE_DRAFT:
+            if draft_model is None:
+                raise ValueError("speculative=draft needs the draft model (runtime.create_proposer loads it)")
+            draft = device_model(draft_model, int8=False)
+        engine = B200SpeculativeEngine(device_model(model, int8=True), k=k, max_ngram=settings.ngram_max_size,
                                        max_seqs=settings.max_num_seqs, max_model_len=settings.max_model_len,
                                        num_blocks=num_blocks, stop_token_ids=tuple(sorted(stop_token_ids)),
                                        cuda_graphs=settings.cuda_graphs, max_prefill_rows=settings.max_prefill_tokens,
-                                       sampling=True)
+                                       sampling=True, draft_model=draft, draft_num_blocks=num_blocks)
         if settings.cuda_graphs:
             engine.capture_all_buckets()
     executor = SpeculativeBatchExecutor(engine, stop_token_ids)

@@ -19,8 +19,10 @@ from tests.conftest import submodule
 
 class OracleSpecEngine:
     def __init__(self, weights, cfg, k: int, max_ngram: int, max_seqs: int, stop_token_ids=(),
-                 max_prefill_rows: int = 4096) -> None:
-        self.weights, self.cfg = weights, cfg
+                 max_prefill_rows: int = 4096, draft=None) -> None:
+        """``draft``: (config, weights) of a draft model whose greedy guesses replace the n-gram
+        lookup (DraftModelProposer)."""
+        self.weights, self.cfg, self.draft = weights, cfg, draft
         self.k, self.max_ngram, self.max_seqs = k, max_ngram, max_seqs
         self.stop = frozenset(stop_token_ids)
         self.max_prefill_rows = max_prefill_rows
@@ -41,7 +43,13 @@ class OracleSpecEngine:
             slot = self.free.pop(0)
             runner = oracle_spec.OracleRunner(self.weights, self.cfg, 512, 16, torch.float32)
             seq = oracle_spec.Seq(f"slot{slot}", list(prompt), len(prompt), new, ignore_eos=ignore_eos)
-            gen = oracle_spec.generate(runner, seq, self.k, self.max_ngram, self.stop, keep_logits=False)
+            proposer = None
+            if self.draft is not None:
+                draft_cfg, draft_weights = self.draft
+                proposer = oracle_spec.DraftProposer(
+                    oracle_spec.OracleRunner(draft_weights, draft_cfg, 512, 16, torch.float32))
+            gen = oracle_spec.generate(runner, seq, self.k, self.max_ngram, self.stop, keep_logits=False,
+                                       proposer=proposer)
             pieces = [([gen.tokens[0]], 0)] + [(list(s.new_tokens), len(s.draft)) for s in gen.steps]
             chunks, emitted = [], 0
             for piece, proposed in pieces:  # cut at the generation's end (a stop inside a step's kept run)

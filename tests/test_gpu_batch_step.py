@@ -144,3 +144,32 @@ def test_sampled_request_resumes_its_stream_after_preemption(small) -> None:
     assert eng.draws_used(executor.slot_of(seq)) >= drawn
     executor.release(seq)
     model.raise_on_device_error()
+
+
+def test_executor_serves_draft_model_drafts() -> None:
+    """speculative=draft through the executor: the engine with a one-layer draft model (its own KV
+    pool) serves the reference's recorded runs (``spec_small_draft_bf16.pt``), with a preemption."""
+    submodule("build").build()
+    pkg = package()
+    cfg = pkg.SMALL_TEST
+    dcfg = pkg.Qwen3Config(**{**{f: getattr(cfg, f) for f in cfg.__dataclass_fields__}, "num_hidden_layers": 1})
+    mk = submodule("model").B200Model
+    target = mk(cfg, pkg.make_weights(cfg, seed=0), num_slots=64 * 16, device="cuda:0", max_positions=512,
+                max_rows=512, max_seqs=8)
+    draft = mk(dcfg, pkg.make_weights(dcfg, seed=1), num_slots=64 * 16, device="cuda:0", max_positions=512,
+               max_rows=512, max_seqs=8)
+    try:
+        golden = load_golden("spec_small_draft_bf16.pt")
+        eng = submodule("engine").B200SpeculativeEngine(target, k=golden["k"], max_ngram=golden["max_ngram"],
+                                                        max_seqs=4, max_model_len=256, num_blocks=64,
+                                                        cuda_graphs=True, draft_model=draft, draft_num_blocks=64)
+        executor = submodule("batch_step").SpeculativeBatchExecutor(eng)
+        events = drive(executor, sequences_of(golden), frozenset(), {"r1": 2})
+        for i, record in enumerate(golden["records"]):
+            assert [t for t, _ in events[f"r{i}"]] == record["tokens"]
+        assert executor.num_active == 0 and eng.state.num_free_blocks() == 64
+        target.raise_on_device_error()
+        draft.raise_on_device_error()
+    finally:
+        target.close()
+        draft.close()

@@ -59,28 +59,37 @@ def settings(backend_mod, **overrides):
     return backend_mod.B200EngineSettings(**values)
 
 
-def serial_reference(ref_mod, model, prompts, stop_ids) -> list[list[tuple[int, bool, str | None]]]:
-    """The reference's own serial speculative path, request by request (engine/runtime.py:162-171)."""
+def serial_reference(ref_mod, model, prompts, stop_ids, draft_model=None) -> list[list[tuple[int, bool, str | None]]]:
+    """The reference's own serial speculative path, request by request (engine/runtime.py:162-171),
+    with n-gram drafts or (``draft_model``) DraftModelProposer drafts."""
     cpu = torch.device("cpu")
     out = []
     for index, prompt in enumerate(prompts):
         pool = ref_mod.pool.KVCachePool(model.config, 64 * 16, cpu, torch.float32)
         allocator = ref_mod.paged.PagedSlotAllocator(64, 16, cpu)
         runner = ref_mod.runner.ModelRunner(model, pool, allocator, cpu)
-        gen = ref_mod.specgen.SpeculativeGenerator(runner, ref_mod.proposers.NgramProposer(NGRAM), K,
-                                                   frozenset(stop_ids), cpu, None)
+        proposer = ref_mod.proposers.NgramProposer(NGRAM)
+        if draft_model is not None:
+            draft_pool = ref_mod.pool.KVCachePool(draft_model.config, 64 * 16, cpu, torch.float32)
+            proposer = ref_mod.proposers.DraftModelProposer(
+                ref_mod.runner.ModelRunner(draft_model, draft_pool, ref_mod.paged.PagedSlotAllocator(64, 16, cpu), cpu),
+                cpu)
+        gen = ref_mod.specgen.SpeculativeGenerator(runner, proposer, K, frozenset(stop_ids), cpu, None)
         params = ref_mod.iface.SamplingParams(max_new_tokens=MAX_NEW, ignore_eos=not stop_ids)
         out.append([(e.token_id, e.is_finished, e.finish_reason)
                     for e in gen.generate(ref_mod.iface.GenerationRequest(f"r{index}", list(prompt), params))])
     return out
 
 
-def serve(backend_mod, ref_mod, model, cfg, weights, prompts, stop_ids, **setting_overrides):
-    """Every prompt submitted at once to the b200 loop; the events each request streams."""
+def serve(backend_mod, ref_mod, model, cfg, weights, prompts, stop_ids, draft=None, **setting_overrides):
+    """Every prompt submitted at once to the b200 loop; the events each request streams.
+    ``draft``: (config, weights, reference model) of a draft model."""
     s = settings(backend_mod, **setting_overrides)
     metrics = ref_mod.metrics.EngineMetrics()
-    fake = OracleSpecEngine(weights, cfg, K, NGRAM, s.max_num_seqs, stop_ids)
-    loop = backend_mod.create_b200_engine(model, frozenset(stop_ids), s, metrics, engine=fake)
+    fake = OracleSpecEngine(weights, cfg, K, NGRAM, s.max_num_seqs, stop_ids,
+                            draft=draft[:2] if draft is not None else None)
+    loop = backend_mod.create_b200_engine(model, frozenset(stop_ids), s, metrics,
+                                          draft_model=draft[2] if draft is not None else None, engine=fake)
 
     async def run():
         await loop.start()
@@ -200,3 +209,23 @@ def test_guess_room_account_covers_every_step(ref) -> None:
     assert acct.can_reserve(seq, 16 * 8 - 1) and not acct.can_reserve(seq, 16 * 8)
     acct.free(seq)
     assert inner.num_free_blocks == 8
+
+
+def test_batch_loop_serves_draft_model_drafts(ref, tiny) -> None:
+    """speculative=draft (DraftModelProposer, proposers.py:63-106): a one-layer draft of the same
+    family; every request streams what the reference's serial generator with that draft emits."""
+    make_golden, ref_mod, backend = ref
+    cfg, weights, model, prompts = tiny
+    pkg = package()
+    draft_cfg = pkg.Qwen3Config(**{**{f: getattr(cfg, f) for f in cfg.__dataclass_fields__}, "num_hidden_layers": 1})
+    draft_weights = pkg.make_weights(draft_cfg, seed=1)
+    draft_model = make_golden.build_model(ref_mod, draft_cfg, draft_weights, torch.float32)
+    want = serial_reference(ref_mod, model, prompts, (), draft_model=draft_model)
+    got, loop, fake, metrics = serve(backend, ref_mod, model, cfg, weights, prompts, (),
+                                     draft=(draft_cfg, draft_weights, draft_model), speculative="draft",
+                                     kv_cache_memory_mb=64)
+    assert got == want
+    assert metric(metrics, "nanoengine_speculative_proposed_tokens_total") > 0
+    with pytest.raises(ValueError, match="draft model"):
+        backend.create_b200_engine(model, frozenset(), settings(backend, speculative="draft"),
+                                   ref_mod.metrics.EngineMetrics())
