@@ -62,6 +62,9 @@ __device__ __forceinline__ int ld_relaxed(const int* p) {
   asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// Publishing a unit's results: every compute thread's stores, then the group's named barrier, then
+// this release by one thread (the barrier orders the others' stores before it, and release is
+// cumulative: a CTA that acquires the counter sees them all, as in a grid barrier's arrive).
 __device__ __forceinline__ void red_release_add(int* p, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -1108,7 +1111,6 @@ __device__ void compute_loop(const SkParams& p, const Sync& sy, const Smem& sm, 
         if (tid == 0) stamp(p, ph, 1, true);
         attention_unit(p, sm, P.layer, M, issued);
         if (tid == 0) {
-          __threadfence();
           red_release_add(sy.head(P.layer, kvh), 1);
           stamp(p, ph, 5);
         }
@@ -1127,7 +1129,6 @@ __device__ void compute_loop(const SkParams& p, const Sync& sy, const Smem& sm, 
         for (int k = tid >> 5; k < mine; k += NCW) final_rows(p, u + k * p.grid, R);
         compute_sync();
         if (tid == 0) {
-          __threadfence();
           red_release_add(sy.final_rows(), mine);
           stamp(p, ph, 5);
         }
@@ -1193,7 +1194,6 @@ __device__ void compute_loop(const SkParams& p, const Sync& sy, const Smem& sm, 
       if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
       compute_sync();
       if (tid == 0) {
-        __threadfence();
         red_release_add(sy.arrive(P.layer, P.kind, g.stripe), 1);
         stamp(p, ph, 3);
         *sm.flag = wait_counter(sy.arrive(P.layer, P.kind, g.stripe), S, sy, p.status, sm.abort_s) ? 1 : 0;
@@ -1235,7 +1235,6 @@ __device__ void compute_loop(const SkParams& p, const Sync& sy, const Smem& sm, 
         compute_sync();
       }
       if (tid == 0) {
-        __threadfence();
         red_release_add(sy.done(P.layer, P.kind, g.stripe), 1);
         stamp(p, ph, 5);
       }
