@@ -161,7 +161,7 @@ __device__ bool wait_counter(const int* addr, int target, const Sync& sy, int* s
     if ((it & 63u) == 63u &&
         give_up(sy, status, abort_s, start, 1, (int)(addr - sy.base) / SK_LINE, target, ld_relaxed(addr)))
       return false;
-    __nanosleep(it < 8 ? 32 : 128);
+    if (it >= 64) __nanosleep(64);
   }
 }
 
@@ -193,7 +193,7 @@ __device__ bool wait_ranges(const Ranges& rg, int target, const Sync& sy, int* s
     if ((it & 63u) == 63u &&
         give_up(sy, status, abort_s, start, 1, (int)(rg.first[0] - sy.base) / SK_LINE, target, ld_relaxed(rg.first[0])))
       return false;
-    __nanosleep(it < 8 ? 32 : 128);
+    if (it >= 64) __nanosleep(64);
   }
 }
 __device__ __forceinline__ Ranges one_range(const int* first, int n) {
@@ -572,7 +572,8 @@ __device__ __forceinline__ float row_rstd(const SkParams& p, int r, int tiles) {
 // [count][128] bf16 each) are staged in shared memory first, all loads in flight at once, so that
 // the per-row work below reads no global memory. Called by every compute thread.
 __device__ void epilogue_qkv(const SkParams& p, const Unit& g, const float* acc, int r0, int count,
-                             const int* rowinfo, __nv_bfloat16* rope_s) {
+                             const int* rowinfo, __nv_bfloat16* rope_s, const uint4* pre_cos = nullptr,
+                             const uint4* pre_sin = nullptr) {
   const int tid = threadIdx.x - 128, cw = tid >> 5, lane = tid & 31;
   const int head = g.stripe;
   const bool is_q = head < p.nh;
@@ -584,11 +585,18 @@ __device__ void epilogue_qkv(const SkParams& p, const Unit& g, const float* acc,
   __nv_bfloat16* cos_s = rope_s;
   __nv_bfloat16* sin_s = rope_s + count * 128;
   if (rope) {
-    for (int e = tid; e < count * 16; e += SK_COMPUTE) {
-      const int m = e >> 4, ch = e & 15;
-      const long long src = (long long)rows_s[m] * 128 + ch * 8;
-      *reinterpret_cast<uint4*>(cos_s + m * 128 + ch * 8) = __ldg(reinterpret_cast<const uint4*>(p.rope_cos + src));
-      *reinterpret_cast<uint4*>(sin_s + m * 128 + ch * 8) = __ldg(reinterpret_cast<const uint4*>(p.rope_sin + src));
+    if (pre_cos) {  // thread tid's chunk (count * 16 <= SK_COMPUTE), loaded before the partials arrived
+      if (tid < count * 16) {
+        *reinterpret_cast<uint4*>(cos_s + tid * 8) = *pre_cos;
+        *reinterpret_cast<uint4*>(sin_s + tid * 8) = *pre_sin;
+      }
+    } else {
+      for (int e = tid; e < count * 16; e += SK_COMPUTE) {
+        const int m = e >> 4, ch = e & 15;
+        const long long src = (long long)rows_s[m] * 128 + ch * 8;
+        *reinterpret_cast<uint4*>(cos_s + m * 128 + ch * 8) = __ldg(reinterpret_cast<const uint4*>(p.rope_cos + src));
+        *reinterpret_cast<uint4*>(sin_s + m * 128 + ch * 8) = __ldg(reinterpret_cast<const uint4*>(p.rope_sin + src));
+      }
     }
   }
   compute_sync();
@@ -642,15 +650,17 @@ __device__ void epilogue_qkv(const SkParams& p, const Unit& g, const float* acc,
   }
 }
 
-// residual update of this stripe's 128 columns, plus the rows' sums of squares for the next norm
-__device__ void epilogue_residual(const SkParams& p, const Unit& g, const float* acc, int r0, int count) {
+// residual update of this stripe's 128 columns, plus the rows' sums of squares for the next norm.
+// ``pre``: this lane's columns of row r0 + (warp), loaded before the partials arrived (or nullptr)
+__device__ void epilogue_residual(const SkParams& p, const Unit& g, const float* acc, int r0, int count,
+                                  const uint2* pre = nullptr) {
   const int cw = (threadIdx.x >> 5) - 4, lane = threadIdx.x & 31;
   const int n0 = g.stripe * 128, c = 4 * lane;
   const int tiles = p.H / 128;
   for (int m = cw; m < count; m += NCW) {
     const int row = r0 + m;
     __nv_bfloat16* hp = p.h + (long long)row * p.H + n0 + c;
-    const uint2 old = ldcg_u2(hp);
+    const uint2 old = (pre && m == cw) ? *pre : ldcg_u2(hp);
     const float4 y = *reinterpret_cast<const float4*>(acc + m * 128 + c);
     const float2 h0 = unpack_bf16x2(old.x), h1 = unpack_bf16x2(old.y);
     const float o[4] = {h0.x + bf16r(y.x), h0.y + bf16r(y.y), h1.x + bf16r(y.z), h1.y + bf16r(y.w)};
@@ -1196,6 +1206,28 @@ __device__ void compute_loop(const SkParams& p, const Sync& sy, const Smem& sm, 
       if (tid == 0) {
         red_release_add(sy.arrive(P.layer, P.kind, g.stripe), 1);
         stamp(p, ph, 3);
+      }
+      // while the other splits arrive: the epilogue's own inputs of this split's first chunk of rows
+      // (the residual rows of this stripe, or the rows' RoPE cos / sin), which no unit of this phase
+      // writes before this one
+      const int slice = (rows + S - 1) / S;
+      const int lo = g.split * slice, hi = min(rows, lo + slice);
+      const int chunk_rows = max(1, min(CHUNK_ROWS, (NCW * ATT_WARP) / (S * 512)));
+      const int first_cnt = min(chunk_rows, hi - lo);
+      uint2 pre_h = make_uint2(0u, 0u);
+      uint4 pre_cos = make_uint4(0u, 0u, 0u, 0u), pre_sin = pre_cos;
+      const int cw4 = tid >> 5;  // compute warp: row lo + cw4 of the first chunk in epilogue_residual
+      const bool residual = P.kind == SK_O || P.kind == SK_DOWN;
+      const bool rope_pre =
+          P.kind == SK_QKV && g.stripe < p.nh + p.nkv && first_cnt > 0 && first_cnt * 16 <= SK_COMPUTE;
+      if (residual && cw4 < first_cnt)
+        pre_h = ldcg_u2(p.h + (long long)(lo + cw4) * p.H + g.stripe * 128 + 4 * lane);
+      if (rope_pre && tid < first_cnt * 16) {
+        const long long src = (long long)sm.rowinfo[lo + (tid >> 4)] * 128 + (tid & 15) * 8;
+        pre_cos = __ldg(reinterpret_cast<const uint4*>(p.rope_cos + src));
+        pre_sin = __ldg(reinterpret_cast<const uint4*>(p.rope_sin + src));
+      }
+      if (tid == 0) {
         *sm.flag = wait_counter(sy.arrive(P.layer, P.kind, g.stripe), S, sy, p.status, sm.abort_s) ? 1 : 0;
         stamp(p, ph, 4);
       }
@@ -1203,10 +1235,7 @@ __device__ void compute_loop(const SkParams& p, const Sync& sy, const Smem& sm, 
       // reduce the slice's rows over the S partials (split order), then its epilogue: a chunk of
       // rows at a time, every partial of the chunk first loaded into shared memory (all loads in
       // flight together), then summed in split order in place
-      const int slice = (rows + S - 1) / S;
-      const int lo = g.split * slice, hi = min(rows, lo + slice);
       const float* stripe_parts = part + ((long long)g.stripe * S * p.R_max) * 128;
-      const int chunk_rows = max(1, min(CHUNK_ROWS, (NCW * ATT_WARP) / (S * 512)));
       for (int c0 = lo; c0 < hi; c0 += chunk_rows) {
         const int cnt = min(chunk_rows, hi - c0);
         const int per = cnt * 32;  // float4s of one split's chunk
@@ -1226,12 +1255,14 @@ __device__ void compute_loop(const SkParams& p, const Sync& sy, const Smem& sm, 
           *reinterpret_cast<float4*>(stage + f * 4) = a;
         }
         compute_sync();
+        const bool first_chunk = c0 == lo;
         if (P.kind == SK_QKV)  // (staging past the reduced rows, which are all that is live now)
-          epilogue_qkv(p, g, stage, c0, cnt, sm.rowinfo, reinterpret_cast<__nv_bfloat16*>(stage + cnt * 128));
+          epilogue_qkv(p, g, stage, c0, cnt, sm.rowinfo, reinterpret_cast<__nv_bfloat16*>(stage + cnt * 128),
+                       first_chunk && rope_pre ? &pre_cos : nullptr, first_chunk && rope_pre ? &pre_sin : nullptr);
         else if (P.kind == SK_GATEUP)
           epilogue_swiglu(p, g, stage, c0, cnt);
         else
-          epilogue_residual(p, g, stage, c0, cnt);
+          epilogue_residual(p, g, stage, c0, cnt, first_chunk ? &pre_h : nullptr);
         compute_sync();
       }
       if (tid == 0) {
