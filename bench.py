@@ -511,9 +511,12 @@ def other_workloads(args, pkg, model_mod, engine_mod, device, peak: float) -> di
     return out
 
 
-def algorithmic_bytes(kind: str, cfg, M: int, ctx_sum: int, kv_bytes_per_token_layer: int, wb: float = 2.0) -> float:
+def algorithmic_bytes(kind: str, cfg, M: int, ctx_sum: int, kv_bytes_per_token_layer: int, wb: float = 2.0,
+                      slices: int = 8) -> float:
     """Unique bytes one launch of ``kind`` must move (weights at ``wb`` bytes per element plus one
-    bf16 scale per row when int8, activations in/out, KV)."""
+    bf16 scale per row when int8, activations in/out, KV). ``slices``: fp32 partial rows an RMSNorm
+    adds first (the unsplit model's split-K slices of o_proj / down_proj, or one per rank of a split
+    model)."""
     H, I, V = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size
     q, kv = cfg.num_attention_heads * 128, cfg.num_key_value_heads * 128
     sc = 2 if wb == 1 else 0
@@ -529,6 +532,8 @@ def algorithmic_bytes(kind: str, cfg, M: int, ctx_sum: int, kv_bytes_per_token_l
         return V * H * 2 + M * H * 2 + M * 8
     if kind == "attention":
         return ctx_sum * kv_bytes_per_token_layer + 2 * M * q * 2
+    if kind == "rmsnorm":  # partials + residual row in, residual row and normed row out, the weights
+        return slices * M * H * 4 + 3 * M * H * 2 + H * 2
     if kind == "step":  # the persistent kernel: every layer's projections, attention and the LM head
         layer = sum(algorithmic_bytes(k, cfg, M, ctx_sum, kv_bytes_per_token_layer, wb)
                     for k in ("gemm_qkv", "attention", "gemm_o", "gemm_gateup", "gemm_down"))
@@ -643,7 +648,8 @@ def run_b200(args, dist: Dist) -> None:
     di = kinds.index(dominant)
     avg_ms = ms_by[di] / n_by[di]
     wb = 1.0 if wl.weight_int8 else 2.0
-    bytes_launch = algorithmic_bytes(dominant, cfg, M, ctx_sum, per_layer_kv, wb)
+    bytes_launch = algorithmic_bytes(dominant, cfg, M, ctx_sum, per_layer_kv, wb,
+                                     slices=dist.world if wl.tp else 8)
     peak, peak_src = measured_peak()
     achieved = bytes_launch / (avg_ms / 1000.0) / 1e9
     # DRAM bytes per launch from the committed ncu capture of the same kernel variant (attention

@@ -310,22 +310,19 @@ int upload_step_descriptors(ne_model* m) {
   return NE_OK;
 }
 
-// NE_STEP_KERNEL=1 runs every eligible verify step as the persistent kernel, NE_STEP_KERNEL=0 none;
-// unset, the steps whose row bound is at most SK_AUTO_ROWS (where it measures faster than the
-// per-projection launches: 1 to 16 users of the 0.6B model at k = 4) and the launch sequence above.
-// Read at every forward, so a process can compare the two.
-int step_kernel_mode() {
+// NE_STEP_KERNEL=1 runs every eligible verify step as the persistent kernel; otherwise (the
+// default: the per-projection launch sequence measures as fast at 1 and 4 users of the 0.6B model
+// and faster from 16 up) every step launches kernel by kernel. Read at every forward, so a process
+// can compare the two.
+bool step_kernel_enabled() {
   const char* v = getenv("NE_STEP_KERNEL");
-  if (!v || !v[0]) return -1;
-  return v[0] == '1' ? 1 : 0;
+  return v && v[0] == '1';
 }
 
 // Whether this forward runs as the persistent step kernel: greedy (argmax) lm rows, rows within the
 // partial areas and the kernel's shared memory, at most 16 query vectors per (entry, KV head).
 bool use_step_kernel(const ne_model* m, const ne_rows* rows, int lm_mode) {
-  const int mode = step_kernel_mode();
-  if (!m->sk_ready || mode == 0 || lm_mode != NE_LM_ARGMAX || m->kv_shadow) return false;
-  if (mode < 0 && rows->max_rows > ne::SK_AUTO_ROWS) return false;
+  if (!m->sk_ready || !step_kernel_enabled() || lm_mode != NE_LM_ARGMAX || m->kv_shadow) return false;
   const int G = m->cfg.num_heads / m->cfg.num_kv_heads;
   int ring = 0;
   return rows->max_rows <= m->sk_rows && rows->lm_max <= rows->max_rows &&

@@ -26,7 +26,6 @@ constexpr int SK_MAX_W_STAGES = 12;
 constexpr int SK_MAX_X_STAGES = 4;
 constexpr int SK_MAX_LAYERS = 48;
 constexpr int SK_MAX_QVEC = 16;          // query vectors per (entry, KV head): one 16-row MMA tile
-constexpr int SK_AUTO_ROWS = 80;         // row bound up to which steps take this kernel by default
 
 enum SkKind : int { SK_QKV = 0, SK_O = 1, SK_GATEUP = 2, SK_DOWN = 3, SK_LM = 4, SK_ATTN = 5, SK_FINAL = 6 };
 

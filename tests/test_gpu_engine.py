@@ -205,16 +205,15 @@ def _rerun_in_a_fresh_process(env_overrides: dict, selection: str) -> None:
 
 def test_fused_rmsnorm_path_serves_the_reference_outputs() -> None:
     """NE_FUSED_NORM=1 (RMSNorm folded into the QKV and gate/up GEMMs' X operand) in a fresh
-    process, with every step on the launch sequence (NE_STEP_KERNEL=0): the serial drop-in and
-    continuous batching still reproduce the reference fixtures."""
-    _rerun_in_a_fresh_process({"NE_FUSED_NORM": "1", "NE_STEP_KERNEL": "0"},
+    process: the serial drop-in and continuous batching still reproduce the reference fixtures."""
+    _rerun_in_a_fresh_process({"NE_FUSED_NORM": "1"},
                               "serial_drop_in or continuous_batching or int8_engine")
 
 
-def test_launch_sequence_serves_the_reference_outputs_at_small_batches() -> None:
-    """Small batches take the persistent step kernel by default; with NE_STEP_KERNEL=0 the same
-    batched-engine tests run every step as the per-projection launch sequence."""
-    _rerun_in_a_fresh_process({"NE_STEP_KERNEL": "0"},
+def test_persistent_step_kernel_serves_the_reference_outputs() -> None:
+    """NE_STEP_KERNEL=1 (every eligible greedy verify step as the persistent kernel): the same
+    batched-engine tests, in a fresh process."""
+    _rerun_in_a_fresh_process({"NE_STEP_KERNEL": "1"},
                               "batched_engine_serial or continuous_batching or shared_prefix or full_length_drafts "
                               "or preempts")
 

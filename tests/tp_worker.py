@@ -104,7 +104,7 @@ def main() -> None:
         whole = model_mod.B200Model(cfg, tp.make_sharded_weights(cfg, whole_plan, seed=0, device=device),
                                     num_slots=128 * 16, device=device, max_positions=512, max_rows=512, max_seqs=4)
         # the unsplit model on the same launch sequence as the split one (the persistent step
-        # kernel, which small batches take by default, adds its partials in another order)
+        # kernel, opt-in, adds its partials in another order)
         os.environ["NE_STEP_KERNEL"] = "0"
         result["unsplit"] = serve(whole, prompts, graphs=True)
         del os.environ["NE_STEP_KERNEL"]
