@@ -834,7 +834,7 @@ __global__ void __launch_bounds__(32 * NW, NW == 8 ? 1 : NW == 4 ? 3 : 5)
 // CTA, as attention_kernel's warp path): K and V blocks arrive by cp.async.bulk.tensor into 128-byte
 // swizzled stages, two per warp, one elected lane issuing a block's four loads.
 template <int NW>
-__global__ void __launch_bounds__(32 * NW, NW == 4 ? 3 : 5)
+__global__ void __launch_bounds__(32 * NW, NW == 8 ? 1 : NW == 4 ? 3 : 5)
     attention_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                          const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out, ne_rows rows, int nh,
                          int nkv, long long num_cache_slots, AttnSplit sp, int* status) {
@@ -880,9 +880,9 @@ __global__ void __launch_bounds__(32 * NW, NW == 4 ? 3 : 5)
                                            16 * tile, &tk);
   } else if (ntiles == 1) {
     warp_split_tiles<false, 1, NW, true>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 0, &tk);
-  } else if constexpr (NW == 4) {
+  } else if constexpr (NW >= 4) {
     if (ntiles == 2)
-      warp_split_tiles<false, 2, 4, true>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 0, &tk);
+      warp_split_tiles<false, 2, NW, true>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 0, &tk);
     else
       report(status, NE_DEV_BAD_SLOT);  // the host sends only one- and two-tile entries here
   } else {
@@ -1093,24 +1093,33 @@ int launch_attention_tc(const __nv_bfloat16* q, __nv_bfloat16* out, const void* 
     const char* e = getenv("NE_ATTN_PREFILL_WARPS");
     return e && e[0] == '4' ? 4 : 8;
   }();
-  const int nw = max_vec > 32 && tile_slots == 1 ? prefill_warps
+  int nw = max_vec > 32 && tile_slots == 1 ? prefill_warps
                  : ((max_vec <= 16 || tile_slots > 1) && ctas <= 5LL * sms && ctas > 3LL * sms) ? 2 : 4;
   // the speculative step over a bf16 pool: tensor loads of K / V (the cp.async kernel otherwise)
   CUtensorMap kmap, vmap;
   const bool tma = !kv_int8 && !shadow.map && nw != 8 && attention_tma_enabled() &&
                    kv_tensor_map(k_cache, num_kv_heads, num_cache_slots, &kmap) &&
                    kv_tensor_map(v_cache, num_kv_heads, num_cache_slots, &vmap);
+  // with at most one CTA per SM (few entries: the small batches), eight warps per (entry, head) pair
+  // instead of four, each walking half the blocks, on SMs that would otherwise idle
+  static const bool wide = [] {
+    const char* e = getenv("NE_ATTN_WIDE");
+    return !(e && e[0] == '0');
+  }();
+  if (tma && wide && ctas * tile_slots <= sms) nw = 8;
   const size_t smem = tma ? attention_tma_smem_bytes(nw) : attention_smem_bytes_nw(nw);
   // the shared-memory limit is a per-device function attribute: set once per (device, variant)
   constexpr int MAX_DEVICES = 64;
-  static bool attr_set[MAX_DEVICES][8] = {};
+  static bool attr_set[MAX_DEVICES][9] = {};
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return NE_ERR_CUDA;
   auto kernel = kv_int8 ? (nw == 2 ? attention_kernel<true, 2> : nw == 8 ? attention_kernel<true, 8>
                                                                           : attention_kernel<true, 4>)
                         : (nw == 2 ? attention_kernel<false, 2> : nw == 8 ? attention_kernel<false, 8>
                                                                            : attention_kernel<false, 4>);
-  auto tma_kernel = nw == 2 ? attention_tma_kernel<2> : attention_tma_kernel<4>;
-  const int ai = tma ? (nw == 2 ? 6 : 7) : (kv_int8 ? 3 : 0) + (nw == 2 ? 1 : nw == 8 ? 2 : 0);
+  auto tma_kernel = nw == 2 ? attention_tma_kernel<2>
+                    : nw == 8 ? attention_tma_kernel<8>
+                              : attention_tma_kernel<4>;
+  const int ai = tma ? (nw == 2 ? 6 : nw == 8 ? 8 : 7) : (kv_int8 ? 3 : 0) + (nw == 2 ? 1 : nw == 8 ? 2 : 0);
   if (!attr_set[dev][ai]) {
     const cudaError_t err = tma ? cudaFuncSetAttribute(tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
                                 : cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
