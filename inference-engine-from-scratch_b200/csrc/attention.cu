@@ -475,6 +475,67 @@ __device__ __forceinline__ void tile_store(const Ctx& c, const AttnSplit& sp, co
   }
 }
 
+// The warps of each query tile merge their (max, sum, O) through shared memory (the stage buffers,
+// free by now): the normalised bf16 output (one split) or the split's unnormalised partial.
+template <int NT, int NW>
+__device__ __forceinline__ void merge_warp_tiles(const Ctx& c, const AttnSplit& sp, const TileState& ts, int b, int h,
+                                                 int split, uint8_t* buf, __nv_bfloat16* out, int nh, int nkv,
+                                                 int v_base) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per_tile = NW / NT, my_tile = warp % NT;
+  __syncthreads();
+  float* mo = reinterpret_cast<float*>(buf);          // [NW][16][128]
+  float* mm = mo + NW * 16 * D;                       // [NW][16]
+  float* ml = mm + NW * 16;                           // [NW][16]
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = (lane >> 2) + 8 * r;
+    if (v_base + my_tile * 16 + row >= c.nvec) continue;  // padding rows of the tile are never read
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      const int d = 8 * t + 2 * (lane & 3);
+      *reinterpret_cast<float2*>(&mo[(warp * 16 + row) * D + d]) = make_float2(ts.o[t][2 * r], ts.o[t][2 * r + 1]);
+    }
+    if ((lane & 3) == 0) {
+      mm[warp * 16 + row] = ts.m[r];
+      ml[warp * 16 + row] = ts.l[r];
+    }
+  }
+  __syncthreads();
+  for (int v = 0; v < min(16 * NT, c.nvec - v_base); ++v) {
+    const int t = v >> 4, row = v & 15;
+    float m = NEG_INF;
+    for (int i = 0; i < per_tile; ++i) m = fmaxf(m, mm[(t + NT * i) * 16 + row]);
+#pragma unroll
+    for (int d = tid; d < D; d += 32 * NW) {
+      float l = 0.f, o = 0.f;
+      if (m != NEG_INF) {
+        for (int i = 0; i < per_tile; ++i) {
+          const int w = t + NT * i;
+          const float mw = mm[w * 16 + row];
+          const float f = mw == NEG_INF ? 0.f : exp2f(mw - m);
+          l += ml[w * 16 + row] * f;
+          o += mo[(w * 16 + row) * D + d] * f;
+        }
+      }
+      if (sp.splits == 1) {
+        const int orow = c.r0 + (v_base + v) / c.G;
+        const int head = c.h * c.G + (v_base + v) % c.G;
+        out[((long long)orow * nh + head) * D + d] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
+      } else if (v_base + v >= sp.max_vec) {
+        if (d == 0) report(c.status, NE_DEV_BAD_SLOT);  // beyond the partial area (see tile_store)
+      } else {
+        const long long base = (((long long)b * nkv + h) * sp.splits + split) * sp.max_vec + v_base + v;
+        sp.part_o[base * D + d] = o;
+        if (d == 0) {
+          sp.part_m[base] = m;
+          sp.part_l[base] = l;
+        }
+      }
+    }
+  }
+}
+
 // The tensor-load pipeline of a bf16 pool (attention_tma_kernel): the K and V maps (x the head
 // dimension, y the KV head, z the slot) and two stage barriers per warp. A warp's stage is 8 KB
 // (K in two 2 KB boxes, then V), 1024-byte aligned as the 128-byte swizzle wants.
@@ -484,41 +545,110 @@ struct TmaKv {
   uint64_t* bars;  // [warps][2]
 };
 constexpr int TMA_STAGE_BYTES = 2 * 16 * D * 2;        // K + V of one block
-constexpr int TMA_WARP_BYTES = 2 * TMA_STAGE_BYTES;    // two stages
 constexpr int TMA_HEAD_BYTES = 5120;                   // Q tile + positions, rounded up to 1024
+// Stages per warp: three for two-warp CTAs (four of them still fit an SM), two otherwise.
+__host__ __device__ constexpr int tma_stages(int nw) { return nw == 2 ? 3 : 2; }
+
+// One or two query tiles of the speculative step over a bf16 pool by tensor loads: warp w serves
+// query tile w % NT and the blocks kb0 + w / NT + (NW / NT) j of the split, j = 0, 1, ... (the
+// warp's ordinals). Ordinal j goes to stage j % NST, its barrier's phase (j / NST) % 2; lane 0
+// issues each block's four loads NST - 1 ordinals ahead of the one being computed. An ordinal whose
+// table entry names no pool block (reported) loads block 0 instead and is not computed, so that
+// every stage sees one load per ordinal.
+template <int NT, int NW, int NST>
+__device__ __forceinline__ void warp_tiles_tma(const Ctx& c, const ne_rows& rows, const AttnSplit& sp, int b, int h,
+                                               int split, int kb0, int kb1, uint8_t* q_s, int* spos, uint8_t* buf,
+                                               __nv_bfloat16* out, int nh, int nkv, int v_base, const TmaKv& tk) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per_tile = NW / NT, my_tile = warp % NT, phase = warp / NT;
+  uint8_t* wbuf_p = buf + warp * NST * TMA_STAGE_BYTES;
+  const uint32_t wbuf = smem_u32(wbuf_p);
+  uint64_t* wbar = tk.bars + NST * warp;
+  const int first = kb0 + phase;
+  const int count = first < kb1 ? (kb1 - first + per_tile - 1) / per_tile : 0;  // this warp's blocks
+  const int stride = rows.block_table_stride;
+  // table entries of ordinals j0 .. j0 + 31, one per lane
+  auto table_chunk = [&](int j0) -> int {
+    const int kbj = first + per_tile * (j0 + lane);
+    return (kbj < kb1 && kbj < stride) ? c.table[kbj] : -1;
+  };
+  int tbl = table_chunk(0);
+  // the checked pool block of ordinal j (its entry in ``tbl``), -1 when it names none
+  auto block_of = [&](int j) -> long long {
+    const int kb = first + per_tile * j;
+    if (kb >= stride) return block_id(c, kb, stride);
+    return checked_block(c, __shfl_sync(0xFFFFFFFFu, tbl, j & 31));
+  };
+  auto issue = [&](int j, long long blk_id) {
+    if (lane == 0) {
+      const int st = j % NST;
+      uint8_t* dst = wbuf_p + st * TMA_STAGE_BYTES;
+      const int z = blk_id >= 0 ? (int)(blk_id * 16) : 0;
+      mbar_arrive_expect_tx(&wbar[st], TMA_STAGE_BYTES);
+      tma_load_3d(dst, tk.k, &wbar[st], 0, c.h, z);
+      tma_load_3d(dst + 2048, tk.k, &wbar[st], 64, c.h, z);
+      tma_load_3d(dst + 4096, tk.v, &wbar[st], 0, c.h, z);
+      tma_load_3d(dst + 6144, tk.v, &wbar[st], 64, c.h, z);
+    }
+  };
+  // the first NST - 1 blocks go out before the query tiles (they do not depend on them);
+  // win[i] holds the block of ordinal j + i (registers: every index below is a constant)
+  long long win[NST - 1];
+#pragma unroll
+  for (int i = 0; i < NST - 1; ++i) {
+    win[i] = i < count ? block_of(i) : -1;
+    if (i < count) issue(i, win[i]);
+  }
+  int issued = min(count, NST - 1);
+  if (tid < 32) spos[tid] = v_base + tid < c.nvec ? rows.positions[c.r0 + (v_base + tid) / c.G] : -1;
+  TileState ts;
+  for (int t = 0; t < NT; ++t) {  // one Q staging area: tile t's warps take their fragments in turn
+    if (t > 0) __syncthreads();
+    load_q_tile(c, v_base + 16 * t, q_s, tid, 32 * NW);
+    __syncthreads();
+    if (my_tile == t) tile_init(ts, smem_u32(q_s), spos + 16 * t, lane);
+  }
+  int done = 0;  // ordinals whose loads have landed
+  for (int j = 0; j < count; ++j) {
+    // ordinal j + NST - 1 into the stage ordinal j - 1 used (computed last iteration, which ended
+    // with a __syncwarp)
+    const int ja = j + NST - 1;
+    long long next = -1;
+    if (ja < count) {
+      if ((ja & 31) == 0) tbl = table_chunk(ja);  // (warp-uniform)
+      next = block_of(ja);
+      issue(ja, next);
+      ++issued;
+    }
+    const long long cur_id = win[0];
+#pragma unroll
+    for (int i = 0; i < NST - 2; ++i) win[i] = win[i + 1];
+    win[NST - 2] = next;
+    const int st = j % NST;
+    if (!__all_sync(0xFFFFFFFFu, mbar_wait(&wbar[st], (uint32_t)(j / NST) & 1u, nullptr, c.status)))
+      break;  // (warp-uniform; the timeout is reported)
+    ++done;
+    const uint32_t cur = wbuf + st * TMA_STAGE_BYTES;
+    if (cur_id >= 0) tile_block<true>(ts, cur, cur + TMA_STAGE_BYTES / 2, first + per_tile * j, lane);
+    __syncwarp();
+  }
+  // every load issued has landed before the buffers become the merge area (bounded: a wait that
+  // runs out reports the timeout)
+  for (; done < issued; ++done) mbar_wait(&wbar[done % NST], (uint32_t)(done / NST) & 1u, nullptr, c.status);
+  merge_warp_tiles<NT, NW>(c, sp, ts, b, h, split, buf, out, nh, nkv, v_base);
+}
 
 // One or two query tiles (the speculative step): warp w serves query tile w % NT and every
 // (4 / NT)-th block of the split from its own double buffer (bf16: two K/V stages; int8: two raw
 // stages + one converted K/V pair); the warps of a tile merge (max, sum, O) through smem at the end.
-// TMA (bf16 pools, attention_tma_kernel): each block is two tensor loads of K and two of V issued
-// by lane 0 into the warp's next stage, completion on the stage's mbarrier (bounded wait).
-template <bool INT8, int NT, int NW, bool TMA = false>
+template <bool INT8, int NT, int NW>
 __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& rows, const AttnSplit& sp, int b, int h,
                                                  int split, int kb0, int kb1, uint8_t* q_s, int* spos, uint8_t* buf,
-                                                 __nv_bfloat16* out, int nh, int nkv, int v_base = 0,
-                                                 const TmaKv* tk = nullptr) {
-  static_assert(!(TMA && INT8), "tensor loads serve bf16 pools");
+                                                 __nv_bfloat16* out, int nh, int nkv, int v_base = 0) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t buf_u = smem_u32(buf);
   const int per_tile = NW / NT, my_tile = warp % NT, phase = warp / NT;
-  const uint32_t wbuf = buf_u + warp * (TMA ? TMA_WARP_BYTES : 4 * BLOCK_BYTES);
-  uint8_t* wbuf_p = buf + warp * (TMA ? TMA_WARP_BYTES : 4 * BLOCK_BYTES);
-  uint64_t* wbar = TMA ? tk->bars + 2 * warp : nullptr;
-  // loads issued to / waited for on stage 0 and stage 1 (registers, not an indexed array)
-  uint32_t issued0 = 0u, issued1 = 0u, used0 = 0u, used1 = 0u;
-  bool tma_ok = true;  // warp-uniform: no wait has run out
-  auto tma_issue = [&](long long blk_id, int st) {
-    if (lane == 0) {
-      uint8_t* dst = wbuf_p + st * TMA_STAGE_BYTES;
-      const int z = (int)(blk_id * 16);
-      mbar_arrive_expect_tx(&wbar[st], TMA_STAGE_BYTES);
-      tma_load_3d(dst, tk->k, &wbar[st], 0, c.h, z);
-      tma_load_3d(dst + 2048, tk->k, &wbar[st], 64, c.h, z);
-      tma_load_3d(dst + 4096, tk->v, &wbar[st], 0, c.h, z);
-      tma_load_3d(dst + 6144, tk->v, &wbar[st], 64, c.h, z);
-    }
-    if (st) ++issued1; else ++issued0;
-  };
+  const uint32_t wbuf = buf_u + warp * 4 * BLOCK_BYTES;
   // the table entries of this warp's blocks (the j-th is logical block kb0 + phase + per_tile * j),
   // 32 at a time in the lanes of a register: no dependent global load inside the block loop
   const int stride = rows.block_table_stride;
@@ -545,8 +675,6 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
     } else if (INT8) {
       stage_raw_int8(c, blk, wbuf, lane);
       scales = load_scales_int8(c, blk, lane);
-    } else if (TMA) {
-      tma_issue(blk, 0);
     } else {
       stage_block<INT8>(c, blk, wbuf, wbuf + BLOCK_BYTES, lane, 32);
     }
@@ -620,18 +748,6 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
       }
       __syncwarp();
       scales = next_scales;
-    } else if (TMA) {
-      // the next block into the other stage (read by the previous iteration, which ended with a
-      // __syncwarp), then this block's stage
-      if (nblk_id >= 0 && tma_ok) tma_issue(nblk_id, stage ^ 1);
-      if (blk >= 0 && tma_ok) {
-        const uint32_t parity = (stage ? used1 : used0) & 1u;
-        tma_ok = __all_sync(0xFFFFFFFFu, mbar_wait(&wbar[stage], parity, nullptr, c.status));
-        if (stage) ++used1; else ++used0;
-        const uint32_t cur = wbuf + stage * TMA_STAGE_BYTES;
-        if (tma_ok) tile_block<true>(ts, cur, cur + TMA_STAGE_BYTES / 2, kb, lane);
-      }
-      __syncwarp();
     } else {
       const uint32_t nxt = wbuf + (stage ^ 1) * 2 * BLOCK_BYTES;
       if (nblk_id >= 0) stage_block<INT8>(c, nblk_id, nxt, nxt + BLOCK_BYTES, lane, 32);
@@ -645,65 +761,8 @@ __device__ __forceinline__ void warp_split_tiles(const Ctx& c, const ne_rows& ro
     blk = nblk_id;
     stage ^= 1;
   }
-  if (TMA) {
-    // every tensor load issued has landed before the buffers become the merge area (bounded: a
-    // wait that runs out has reported the timeout)
-    for (; used0 < issued0; ++used0) mbar_wait(&wbar[0], used0 & 1u, nullptr, c.status);
-    for (; used1 < issued1; ++used1) mbar_wait(&wbar[1], used1 & 1u, nullptr, c.status);
-  }
   cp_wait<0>();
-  // merge the warps of each tile through smem (reusing the stage buffers)
-  __syncthreads();
-  float* mo = reinterpret_cast<float*>(buf);          // [NW][16][128]
-  float* mm = mo + NW * 16 * D;                       // [NW][16]
-  float* ml = mm + NW * 16;                           // [NW][16]
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int row = (lane >> 2) + 8 * r;
-    if (v_base + my_tile * 16 + row >= c.nvec) continue;  // padding rows of the tile are never read
-#pragma unroll
-    for (int t = 0; t < 16; ++t) {
-      const int d = 8 * t + 2 * (lane & 3);
-      *reinterpret_cast<float2*>(&mo[(warp * 16 + row) * D + d]) = make_float2(ts.o[t][2 * r], ts.o[t][2 * r + 1]);
-    }
-    if ((lane & 3) == 0) {
-      mm[warp * 16 + row] = ts.m[r];
-      ml[warp * 16 + row] = ts.l[r];
-    }
-  }
-  __syncthreads();
-  for (int v = 0; v < min(16 * NT, c.nvec - v_base); ++v) {
-    const int t = v >> 4, row = v & 15;
-    float m = NEG_INF;
-    for (int i = 0; i < per_tile; ++i) m = fmaxf(m, mm[(t + NT * i) * 16 + row]);
-#pragma unroll
-    for (int d = tid; d < D; d += 32 * NW) {
-      float l = 0.f, o = 0.f;
-      if (m != NEG_INF) {
-        for (int i = 0; i < per_tile; ++i) {
-          const int w = t + NT * i;
-          const float mw = mm[w * 16 + row];
-          const float f = mw == NEG_INF ? 0.f : exp2f(mw - m);
-          l += ml[w * 16 + row] * f;
-          o += mo[(w * 16 + row) * D + d] * f;
-        }
-      }
-      if (sp.splits == 1) {
-        const int orow = c.r0 + (v_base + v) / c.G;
-        const int head = c.h * c.G + (v_base + v) % c.G;
-        out[((long long)orow * nh + head) * D + d] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
-      } else if (v_base + v >= sp.max_vec) {
-        if (d == 0) report(c.status, NE_DEV_BAD_SLOT);  // beyond the partial area (see tile_store)
-      } else {
-        const long long base = (((long long)b * nkv + h) * sp.splits + split) * sp.max_vec + v_base + v;
-        sp.part_o[base * D + d] = o;
-        if (d == 0) {
-          sp.part_m[base] = m;
-          sp.part_l[base] = l;
-        }
-      }
-    }
-  }
+  merge_warp_tiles<NT, NW>(c, sp, ts, b, h, split, buf, out, nh, nkv, v_base);
 }
 
 // NW warps per CTA: 4 (three CTAs per SM, registers <= 168; every path), or 2 (one query tile
@@ -834,7 +893,7 @@ __global__ void __launch_bounds__(32 * NW, NW == 8 ? 1 : NW == 4 ? 3 : 5)
 // CTA, as attention_kernel's warp path): K and V blocks arrive by cp.async.bulk.tensor into 128-byte
 // swizzled stages, two per warp, one elected lane issuing a block's four loads.
 template <int NW>
-__global__ void __launch_bounds__(32 * NW, NW == 8 ? 1 : NW == 4 ? 3 : 5)
+__global__ void __launch_bounds__(32 * NW, NW == 8 ? 1 : NW == 4 ? 3 : 4)
     attention_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                          const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out, ne_rows rows, int nh,
                          int nkv, long long num_cache_slots, AttnSplit sp, int* status) {
@@ -863,26 +922,26 @@ __global__ void __launch_bounds__(32 * NW, NW == 8 ? 1 : NW == 4 ? 3 : 5)
   const int bps = (nblk + sp.splits - 1) / sp.splits;
   const int kb0 = split * bps, kb1 = min(nblk, kb0 + bps);
   const int ntiles = (c.nvec + 15) / 16;
+  constexpr int NST = tma_stages(NW);
   uint8_t* q_s = smem;                                     // 16 x ROW_BYTES
   int* spos = reinterpret_cast<int*>(smem + BLOCK_BYTES);  // 16 ints (+pad)
-  uint8_t* buf = smem + TMA_HEAD_BYTES;                    // NW x two 8 KB stages
-  uint64_t* bars = reinterpret_cast<uint64_t*>(buf + NW * TMA_WARP_BYTES);
+  uint8_t* buf = smem + TMA_HEAD_BYTES;                    // NW x NST 8 KB stages
+  uint64_t* bars = reinterpret_cast<uint64_t*>(buf + NW * NST * TMA_STAGE_BYTES);
   if (lane == 0) {
-    mbar_init(&bars[2 * warp], 1);
-    mbar_init(&bars[2 * warp + 1], 1);
+#pragma unroll
+    for (int i = 0; i < NST; ++i) mbar_init(&bars[NST * warp + i], 1);
     fence_mbar_init();
   }
   __syncthreads();
   const TmaKv tk{&kmap, &vmap, bars};
   if (slots > 1) {
     if (tile < ntiles)
-      warp_split_tiles<false, 1, NW, true>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv,
-                                           16 * tile, &tk);
+      warp_tiles_tma<1, NW, NST>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 16 * tile, tk);
   } else if (ntiles == 1) {
-    warp_split_tiles<false, 1, NW, true>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 0, &tk);
+    warp_tiles_tma<1, NW, NST>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 0, tk);
   } else if constexpr (NW >= 4) {
     if (ntiles == 2)
-      warp_split_tiles<false, 2, NW, true>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 0, &tk);
+      warp_tiles_tma<2, NW, NST>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 0, tk);
     else
       report(status, NE_DEV_BAD_SLOT);  // the host sends only one- and two-tile entries here
   } else {
@@ -980,7 +1039,8 @@ __global__ void kv_shadow_map_kernel(const int32_t* __restrict__ table, int num_
 }
 
 size_t attention_tma_smem_bytes(int nw) {
-  return 1024 + TMA_HEAD_BYTES + (size_t)nw * TMA_WARP_BYTES + (size_t)nw * 2 * sizeof(uint64_t);
+  const size_t nst = tma_stages(nw);
+  return 1024 + TMA_HEAD_BYTES + (size_t)nw * nst * TMA_STAGE_BYTES + (size_t)nw * nst * sizeof(uint64_t);
 }
 
 // Tensor maps of a bf16 pool's per-layer K or V array, encoded once per (array, heads, slots).
