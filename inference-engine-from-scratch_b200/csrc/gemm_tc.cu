@@ -982,6 +982,7 @@ int max_splits() {
   static const int cap = env_cap("NE_GEMM_MAX_SPLITS", GEMM_MAX_SPLITS);
   return cap;
 }
+constexpr int VERIFY_TBLOCK_SPLIT = 96;
 int max_stages() {
   static const int cap = env_cap("NE_GEMM_MAX_STAGES", GEMM_MAX_STAGES);
   return cap;
@@ -1007,6 +1008,14 @@ int plan_uncached(GemmParams& p, int num_sms) {
   const int n_tiles = p.N / GEMM_BM;
   const int avail = GEMM_SMEM_DATA_BYTES;
   int t_block = p.M_max <= 256 ? ((p.M_max + 15) & ~15) : 256;
+  // o_proj / down_proj of a verify step of more than 96 rows (a bucket of 32+ users): token blocks
+  // of 96 rows, twice the CTAs with half the rows each, so that each CTA's partial tiles and
+  // epilogue are half as long (the weights are read once from HBM and again from L2). Measured on
+  // config 2 at 64 users (~140 rows): 1.828 -> 1.812 ms per step; blocks of 80 and 64 rows no better.
+  // The same for the QKV and gate/up clusters (80-row blocks, fewer splits) gained at 64 users
+  // (-> 1.791 ms) but lost ~2% at 48 (~90 rows in the same 64-slot bucket, a nearly empty second block).
+  if (p.M_max <= 512 && p.rows_hint > 0 && p.epi.mode == EPI_SPLIT_F32)
+    t_block = std::min(t_block, VERIFY_TBLOCK_SPLIT);
   int m_blocks = (p.M_max + t_block - 1) / t_block;
   // a verify step's row count is a device value well below its bound: size split-K for the first
   // m-block (a later one that gets rows is a second wave); prefill-sized steps split by m-blocks
