@@ -167,6 +167,9 @@ ATTENTION_CASES = [
     (16, 8, [9] * 60, [30 + (i * 37) % 350 for i in range(60)], 0),
     # prefill rows: eight-warp CTAs, one per query group of 128 vectors, with split-KV partials
     (16, 8, [300, 5], [600, 200], 32),
+    # 19-55 entries (more than one CTA per SM, at most three): the four-warp tensor-load kernel, one and two tiles
+    (16, 8, [3] * 30, [24 + (i * 53) % 300 for i in range(30)], 0),
+    (16, 8, [9] * 24, [40 + (i * 71) % 400 for i in range(24)], 0),
     # contexts long enough for the planner to split the KV (32 blocks or more per split): one and two tiles
     (16, 8, [5], [2100], 8),
     (16, 8, [9, 3], [1500, 1300], 8),
