@@ -126,6 +126,16 @@ __device__ __forceinline__ void stage_block(const Ctx& c, long long blk, uint32_
   }
 }
 
+// Shared-memory address of (token, dimension col) in a staged K or V block: the padded row layout
+// (cp.async and conversions), or (SW) the tensor-load layout: two 2 KB boxes of dimensions 0-63 and
+// 64-127, rows of 128 B whose 16-byte chunk c sits at c ^ (token % 8) (the 128-byte swizzle).
+template <bool SW>
+__device__ __forceinline__ uint32_t kv_addr(uint32_t base, int tok, int col) {
+  if (!SW) return base + tok * ROW_BYTES + col * 2;
+  const int c = col >> 3;
+  return base + (c >> 3) * 2048 + tok * 128 + (((c & 7) ^ (tok & 7)) << 4);
+}
+
 // Stage dequantised copy ``sh`` of a shared int8 block (bf16, the pool's row layout) by cp.async.
 __device__ __forceinline__ void stage_shadow(const Ctx& c, int sh, uint32_t k_s, uint32_t v_s, int lane) {
   for (int i = lane; i < 16 * 16; i += 32) {
@@ -202,6 +212,37 @@ __device__ __forceinline__ void convert_raw_int8(uint32_t raw, uint32_t k_s, uin
   convert_half_int8(raw, k_s, scales, 0, lane);
   convert_half_int8(raw + 2048, v_s, scales, 16, lane);
 }
+// The same from a raw block a tensor load wrote (16 rows of 128 int8, 16-byte chunk c of row t at
+// c ^ (t % 8)) into the swizzled bf16 layout ``kv_addr<true>`` reads: chunk c of int8 becomes
+// bf16 chunks 2c and 2c + 1. The same arithmetic as convert_half_int8.
+__device__ __forceinline__ void convert_half_int8_sw(uint32_t raw, uint32_t dst, uint32_t scales, int scale_lane,
+                                                     int lane) {
+  uint32_t w[4][4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int i = lane + 32 * j, tok = i >> 3, ch = i & 7;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(w[j][0]), "=r"(w[j][1]), "=r"(w[j][2]), "=r"(w[j][3])
+                 : "r"(raw + tok * 128 + ((ch ^ (tok & 7)) << 4)));
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int i = lane + 32 * j, tok = i >> 3, ch = i & 7;
+    const uint32_t sc = __shfl_sync(0xFFFFFFFFu, scales, scale_lane + tok);
+    const uint32_t s2 = sc | (sc << 16);
+    uint32_t o[8];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      o[2 * t] = dq_pair(w[j][t], 0x4140u, s2);
+      o[2 * t + 1] = dq_pair(w[j][t], 0x4342u, s2);
+    }
+    const uint32_t d0 = kv_addr<true>(dst, tok, 16 * ch), d1 = kv_addr<true>(dst, tok, 16 * ch + 8);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(d0), "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3])
+                 : "memory");
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(d1), "r"(o[4]), "r"(o[5]), "r"(o[6]), "r"(o[7])
+                 : "memory");
+  }
+}
 
 // A block-table entry checked against the pool: the id, or -1 (reported) when it names no block.
 __device__ __forceinline__ long long checked_block(const Ctx& c, long long blk) {
@@ -256,16 +297,6 @@ __device__ __forceinline__ void tile_init(TileState& ts, uint32_t q_s, const int
   ts.l[0] = ts.l[1] = 0.f;
   ts.pos[0] = spos[lane >> 2];
   ts.pos[1] = spos[(lane >> 2) + 8];
-}
-
-// Shared-memory address of (token, dimension col) in a staged K or V block: the padded row layout
-// (cp.async and conversions), or (SW) the tensor-load layout: two 2 KB boxes of dimensions 0-63 and
-// 64-127, rows of 128 B whose 16-byte chunk c sits at c ^ (token % 8) (the 128-byte swizzle).
-template <bool SW>
-__device__ __forceinline__ uint32_t kv_addr(uint32_t base, int tok, int col) {
-  if (!SW) return base + tok * ROW_BYTES + col * 2;
-  const int c = col >> 3;
-  return base + (c >> 3) * 2048 + tok * 128 + (((c & 7) ^ (tok & 7)) << 4);
 }
 
 // One 16-token block (logical index kb) staged at k_s / v_s against the tile.
@@ -889,6 +920,167 @@ __global__ void __launch_bounds__(32 * NW, NW == 8 ? 1 : NW == 4 ? 3 : 5)
 }
 
 // Merge the split partials of every (entry, KV head): softmax-weighted sum in fp32, bf16 output.
+// The int8 pool's tensor-load pipeline (attention_tma8_kernel): the pool's K / V maps (int8, one
+// load per block each), the bf16 maps of its dequantised shared-prefix copies (when any), and
+// four barriers per warp (two copy stages, two raw stages).
+struct TmaKv8 {
+  const CUtensorMap* k8;
+  const CUtensorMap* v8;
+  const CUtensorMap* shk;
+  const CUtensorMap* shv;
+  uint64_t* bars;  // [warps][4]
+};
+constexpr int TMA8_WARP_BYTES = 16384;  // two 8 KB copy stages, or two 4 KB raw stages + the 8 KB converted block
+
+// int8 pool, one or two query tiles, by tensor loads: as warp_split_tiles<true, ...>. Leading
+// blocks with dequantised copies (a shared prefix) run first through two bf16 stages; then the
+// int8 blocks through two raw stages (4 KB: K then V, each one tensor load), each converted once
+// into the warp's bf16 block (bf16(q * scale), the reference's rounding) before the tile reads
+// it. Raw ordinal i uses stage i % 2 at phase (i / 2) % 2, copy ordinals likewise on their own
+// barriers; an ordinal whose table entry names no pool block loads block 0 and is not computed.
+template <int NT, int NW>
+__device__ __forceinline__ void warp_tiles_tma8(const Ctx& c, const ne_rows& rows, const AttnSplit& sp, int b, int h,
+                                                int split, int kb0, int kb1, uint8_t* q_s, int* spos, uint8_t* buf,
+                                                __nv_bfloat16* out, int nh, int nkv, int v_base, const TmaKv8& tk) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per_tile = NW / NT, my_tile = warp % NT, phase = warp / NT;
+  uint8_t* wbuf_p = buf + warp * TMA8_WARP_BYTES;
+  const uint32_t wbuf = smem_u32(wbuf_p);
+  uint64_t* cbar = tk.bars + 4 * warp;  // copy stages
+  uint64_t* rbar = cbar + 2;            // raw stages
+  const int first = kb0 + phase;
+  const int count = first < kb1 ? (kb1 - first + per_tile - 1) / per_tile : 0;
+  const int stride = rows.block_table_stride;
+  auto table_chunk = [&](int j0) -> int {
+    const int kbj = first + per_tile * (j0 + lane);
+    return (kbj < kb1 && kbj < stride) ? c.table[kbj] : -1;
+  };
+  auto copy_of = [&](int id) -> int {
+    if (!c.sh.map || id < 0 || (long long)(id + 1) * 16 > c.num_cache_slots - 1) return -1;
+    const int v = c.sh.map[id];
+    return v < c.sh.blocks ? v : -1;
+  };
+  int tbl = table_chunk(0);
+  int shm = copy_of(tbl);
+  auto block_of = [&](int j) -> long long {
+    const int kb = first + per_tile * j;
+    if (kb >= stride) return block_id(c, kb, stride);
+    return checked_block(c, __shfl_sync(0xFFFFFFFFu, tbl, j & 31));
+  };
+  auto copy_at = [&](int j, long long id) -> int {  // (warp-uniform)
+    const int v = __shfl_sync(0xFFFFFFFFu, shm, j & 31);
+    return (id >= 0 && first + per_tile * j < stride) ? v : -1;
+  };
+  auto refresh = [&](int j) {  // entries of ordinals j .. j + 31 (j a multiple of 32)
+    tbl = table_chunk(j);
+    shm = copy_of(tbl);
+  };
+  auto issue_copy = [&](int i, int cpy) {
+    if (lane == 0) {
+      const int st = i & 1;
+      uint8_t* dst = wbuf_p + st * 8192;
+      const int z = cpy * 16;
+      mbar_arrive_expect_tx(&cbar[st], 8192);
+      tma_load_3d(dst, tk.shk, &cbar[st], 0, c.h, z);
+      tma_load_3d(dst + 2048, tk.shk, &cbar[st], 64, c.h, z);
+      tma_load_3d(dst + 4096, tk.shv, &cbar[st], 0, c.h, z);
+      tma_load_3d(dst + 6144, tk.shv, &cbar[st], 64, c.h, z);
+    }
+  };
+  auto issue_raw = [&](int i, long long id) {
+    if (lane == 0) {
+      const int st = i & 1;
+      uint8_t* dst = wbuf_p + st * 4096;
+      const int z = id >= 0 ? (int)(id * 16) : 0;
+      mbar_arrive_expect_tx(&rbar[st], 4096);
+      tma_load_3d(dst, tk.k8, &rbar[st], 0, c.h, z);
+      tma_load_3d(dst + 2048, tk.v8, &rbar[st], 0, c.h, z);
+    }
+  };
+  // ordinal 0 goes out before the query tiles
+  int j = 0, ci = 0, ri = 0;  // next ordinal to compute; copy / raw ordinals issued so far
+  int cdone = 0, rdone = 0;   // copy / raw ordinals whose loads have landed
+  long long id0 = count > 0 ? block_of(0) : -1;
+  int cp0 = count > 0 ? copy_at(0, id0) : -1;
+  uint32_t scales = 0;
+  if (count > 0) {
+    if (cp0 >= 0) {
+      issue_copy(ci++, cp0);
+    } else {
+      issue_raw(ri++, id0);
+      scales = load_scales_int8(c, id0 >= 0 ? id0 : 0, lane);
+    }
+  }
+  if (tid < 32) spos[tid] = v_base + tid < c.nvec ? rows.positions[c.r0 + (v_base + tid) / c.G] : -1;
+  TileState ts;
+  for (int t = 0; t < NT; ++t) {
+    if (t > 0) __syncthreads();
+    load_q_tile(c, v_base + 16 * t, q_s, tid, 32 * NW);
+    __syncthreads();
+    if (my_tile == t) tile_init(ts, smem_u32(q_s), spos + 16 * t, lane);
+  }
+  bool ok = true;
+  // leading blocks with copies: two bf16 stages, one ordinal ahead while the next one has a copy
+  long long cur = id0;
+  int cur_cp = cp0;
+  while (ok && j < count && cur_cp >= 0) {
+    long long nid = -1;
+    int ncp = -1;
+    if (j + 1 < count) {
+      if (((j + 1) & 31) == 0) refresh(j + 1);
+      nid = block_of(j + 1);
+      ncp = copy_at(j + 1, nid);
+      if (ncp >= 0) issue_copy(ci++, ncp);
+    }
+    const int st = cdone & 1;
+    ok = __all_sync(0xFFFFFFFFu, mbar_wait(&cbar[st], (uint32_t)(cdone >> 1) & 1u, nullptr, c.status));
+    if (!ok) break;
+    ++cdone;
+    const uint32_t at = wbuf + st * 8192;
+    tile_block<true>(ts, at, at + 4096, first + per_tile * j, lane);
+    __syncwarp();
+    ++j;
+    cur = nid;
+    cur_cp = ncp;
+  }
+  // the int8 blocks: their stages overlap the copy stages, which are all consumed by now
+  if (ok && j < count) {
+    if (ri == 0) {
+      issue_raw(ri++, cur);
+      scales = load_scales_int8(c, cur >= 0 ? cur : 0, lane);
+    }
+    while (j < count) {
+      long long nid = -1;
+      uint32_t next_scales = 0;
+      if (j + 1 < count) {
+        if (((j + 1) & 31) == 0) refresh(j + 1);
+        nid = block_of(j + 1);
+        issue_raw(ri++, nid);
+        next_scales = load_scales_int8(c, nid >= 0 ? nid : 0, lane);
+      }
+      const int st = rdone & 1;
+      ok = __all_sync(0xFFFFFFFFu, mbar_wait(&rbar[st], (uint32_t)(rdone >> 1) & 1u, nullptr, c.status));
+      if (!ok) break;
+      ++rdone;
+      const uint32_t kv = wbuf + 8192;  // the converted K, V
+      if (cur >= 0) {
+        convert_half_int8_sw(wbuf + st * 4096, kv, scales, 0, lane);
+        convert_half_int8_sw(wbuf + st * 4096 + 2048, kv + 4096, scales, 16, lane);
+        __syncwarp();
+        tile_block<true>(ts, kv, kv + 4096, first + per_tile * j, lane);
+      }
+      __syncwarp();
+      ++j;
+      cur = nid;
+      scales = next_scales;
+    }
+  }
+  // every load issued has landed before the buffers become the merge area
+  for (; cdone < ci; ++cdone) mbar_wait(&cbar[cdone & 1], (uint32_t)(cdone >> 1) & 1u, nullptr, c.status);
+  for (; rdone < ri; ++rdone) mbar_wait(&rbar[rdone & 1], (uint32_t)(rdone >> 1) & 1u, nullptr, c.status);
+  merge_warp_tiles<NT, NW>(c, sp, ts, b, h, split, buf, out, nh, nkv, v_base);
+}
+
 // The speculative step's attention over a bf16 pool with tensor loads (one or two query tiles per
 // CTA, as attention_kernel's warp path): K and V blocks arrive by cp.async.bulk.tensor into 128-byte
 // swizzled stages, two per warp, one elected lane issuing a block's four loads.
@@ -944,6 +1136,69 @@ __global__ void __launch_bounds__(32 * NW, NW == 8 ? 1 : NW == 4 ? 3 : 4)
       warp_tiles_tma<2, NW, NST>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 0, tk);
     else
       report(status, NE_DEV_BAD_SLOT);  // the host sends only one- and two-tile entries here
+  } else {
+    report(status, NE_DEV_BAD_SLOT);
+  }
+}
+
+// The speculative step's attention over an int8 pool with tensor loads (as attention_tma_kernel;
+// shared-prefix blocks with dequantised copies read those copies, by bf16 tensor loads).
+template <int NW>
+__global__ void __launch_bounds__(32 * NW, NW == 8 ? 1 : NW == 4 ? 3 : 5)
+    attention_tma8_kernel(const __grid_constant__ CUtensorMap k8map, const __grid_constant__ CUtensorMap v8map,
+                          const __grid_constant__ CUtensorMap shkmap, const __grid_constant__ CUtensorMap shvmap,
+                          const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out,
+                          const __nv_bfloat16* __restrict__ ks, const __nv_bfloat16* __restrict__ vs, ne_rows rows,
+                          int nh, int nkv, long long num_cache_slots, AttnSplit sp, int* status, KvShadow shadow) {
+  pdl_prologue();
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int slots = gridDim.z / sp.splits;
+  const int b = blockIdx.x, h = blockIdx.y, split = blockIdx.z / slots, tile = blockIdx.z % slots;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int ql = rows.q_len[b];
+  if (ql <= 0) return;
+  Ctx c{};
+  c.q = q;
+  c.out = out;
+  c.ks = ks;
+  c.vs = vs;
+  c.nh = nh;
+  c.nkv = nkv;
+  c.h = h;
+  c.G = nh / nkv;
+  c.r0 = rows.q_start[b];
+  c.nvec = ql * c.G;
+  c.num_cache_slots = num_cache_slots;
+  c.status = status;
+  c.sh = shadow;
+  c.table = rows.block_tables + (long long)(rows.table_index ? rows.table_index[b] : b) * rows.block_table_stride;
+  const int ctx = rows.positions[c.r0 + ql - 1] + 1;
+  const int nblk = (ctx + 15) / 16;
+  const int bps = (nblk + sp.splits - 1) / sp.splits;
+  const int kb0 = split * bps, kb1 = min(nblk, kb0 + bps);
+  const int ntiles = (c.nvec + 15) / 16;
+  uint8_t* q_s = smem;
+  int* spos = reinterpret_cast<int*>(smem + BLOCK_BYTES);
+  uint8_t* buf = smem + TMA_HEAD_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(buf + NW * TMA8_WARP_BYTES);
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) mbar_init(&bars[4 * warp + i], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const TmaKv8 tk{&k8map, &v8map, &shkmap, &shvmap, bars};
+  if (slots > 1) {
+    if (tile < ntiles)
+      warp_tiles_tma8<1, NW>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 16 * tile, tk);
+  } else if (ntiles == 1) {
+    warp_tiles_tma8<1, NW>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 0, tk);
+  } else if constexpr (NW >= 4) {
+    if (ntiles == 2)
+      warp_tiles_tma8<2, NW>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 0, tk);
+    else
+      report(status, NE_DEV_BAD_SLOT);
   } else {
     report(status, NE_DEV_BAD_SLOT);
   }
@@ -1043,22 +1298,30 @@ size_t attention_tma_smem_bytes(int nw) {
   return 1024 + TMA_HEAD_BYTES + (size_t)nw * nst * TMA_STAGE_BYTES + (size_t)nw * nst * sizeof(uint64_t);
 }
 
-// Tensor maps of a bf16 pool's per-layer K or V array, encoded once per (array, heads, slots).
-bool kv_tensor_map(const void* base, int nkv, long long slots, CUtensorMap* out) {
+size_t attention_tma8_smem_bytes(int nw) {
+  return 1024 + TMA_HEAD_BYTES + (size_t)nw * TMA8_WARP_BYTES + (size_t)nw * 4 * sizeof(uint64_t);
+}
+
+// Tensor maps of a bf16 pool's per-layer K or V array (or, ``int8``, an int8 pool's), encoded once
+// per (array, heads, slots, element type).
+bool kv_tensor_map(const void* base, int nkv, long long slots, CUtensorMap* out, bool int8 = false) {
   struct Key {
     const void* base;
     int nkv;
     long long slots;
-    bool operator<(const Key& o) const { return std::tie(base, nkv, slots) < std::tie(o.base, o.nkv, o.slots); }
+    bool int8;
+    bool operator<(const Key& o) const {
+      return std::tie(base, nkv, slots, int8) < std::tie(o.base, o.nkv, o.slots, o.int8);
+    }
   };
   static std::mutex mu;
   static std::map<Key, CUtensorMap> maps;
   std::lock_guard<std::mutex> lock(mu);
-  const Key key{base, nkv, slots};
+  const Key key{base, nkv, slots, int8};
   auto it = maps.find(key);
   if (it == maps.end()) {
     CUtensorMap m;
-    if (!make_tmap_kv(&m, base, nkv, slots)) return false;
+    if (!(int8 ? make_tmap_kv8(&m, base, nkv, slots) : make_tmap_kv(&m, base, nkv, slots))) return false;
     if (maps.size() > 4096) maps.clear();
     it = maps.emplace(key, m).first;
   }
@@ -1167,10 +1430,20 @@ int launch_attention_tc(const __nv_bfloat16* q, __nv_bfloat16* out, const void* 
     return !(e && e[0] == '0');
   }();
   if (tma && wide && ctas * tile_slots <= sms) nw = 8;
-  const size_t smem = tma ? attention_tma_smem_bytes(nw) : attention_smem_bytes_nw(nw);
+  // an int8 pool: tensor loads of the raw blocks (and of the dequantised copies, when any)
+  CUtensorMap shkmap, shvmap;
+  const bool tma8 = kv_int8 && nw != 8 && attention_tma_enabled() &&
+                    kv_tensor_map(k_cache, num_kv_heads, num_cache_slots, &kmap, true) &&
+                    kv_tensor_map(v_cache, num_kv_heads, num_cache_slots, &vmap, true) &&
+                    (!shadow.map || (kv_tensor_map(shadow.k, num_kv_heads, (long long)shadow.blocks * 16, &shkmap) &&
+                                     kv_tensor_map(shadow.v, num_kv_heads, (long long)shadow.blocks * 16, &shvmap)));
+  if (tma8 && !shadow.map) shkmap = shvmap = kmap;  // (unread: no block has a copy)
+  const size_t smem = tma ? attention_tma_smem_bytes(nw)
+                      : tma8 ? attention_tma8_smem_bytes(nw)
+                             : attention_smem_bytes_nw(nw);
   // the shared-memory limit is a per-device function attribute: set once per (device, variant)
   constexpr int MAX_DEVICES = 64;
-  static bool attr_set[MAX_DEVICES][9] = {};
+  static bool attr_set[MAX_DEVICES][11] = {};
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return NE_ERR_CUDA;
   auto kernel = kv_int8 ? (nw == 2 ? attention_kernel<true, 2> : nw == 8 ? attention_kernel<true, 8>
                                                                           : attention_kernel<true, 4>)
@@ -1179,10 +1452,15 @@ int launch_attention_tc(const __nv_bfloat16* q, __nv_bfloat16* out, const void* 
   auto tma_kernel = nw == 2 ? attention_tma_kernel<2>
                     : nw == 8 ? attention_tma_kernel<8>
                               : attention_tma_kernel<4>;
-  const int ai = tma ? (nw == 2 ? 6 : nw == 8 ? 8 : 7) : (kv_int8 ? 3 : 0) + (nw == 2 ? 1 : nw == 8 ? 2 : 0);
+  auto tma8_kernel = nw == 2 ? attention_tma8_kernel<2> : attention_tma8_kernel<4>;
+  const int ai = tma ? (nw == 2 ? 6 : nw == 8 ? 8 : 7)
+                 : tma8 ? (nw == 2 ? 9 : 10)
+                        : (kv_int8 ? 3 : 0) + (nw == 2 ? 1 : nw == 8 ? 2 : 0);
   if (!attr_set[dev][ai]) {
-    const cudaError_t err = tma ? cudaFuncSetAttribute(tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
-                                : cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int bytes = (int)smem;
+    const cudaError_t err = tma    ? cudaFuncSetAttribute(tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes)
+                            : tma8 ? cudaFuncSetAttribute(tma8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes)
+                                   : cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (err != cudaSuccess) return NE_ERR_CUDA;
     attr_set[dev][ai] = true;
   }
@@ -1200,6 +1478,10 @@ int launch_attention_tc(const __nv_bfloat16* q, __nv_bfloat16* out, const void* 
   if (tma) {
     if (launch_kernel(tma_kernel, grid, dim3(32 * nw), smem, stream, kmap, vmap, q, out, rows, num_heads,
                       num_kv_heads, num_cache_slots, sp, status) != cudaSuccess)
+      return NE_ERR_CUDA;
+  } else if (tma8) {
+    if (launch_kernel(tma8_kernel, grid, dim3(32 * nw), smem, stream, kmap, vmap, shkmap, shvmap, q, out, k_scale,
+                      v_scale, rows, num_heads, num_kv_heads, num_cache_slots, sp, status, shadow) != cudaSuccess)
       return NE_ERR_CUDA;
   } else if (launch_kernel(kernel, grid, dim3(32 * nw), smem, stream, q, out, k_cache, v_cache, k_scale, v_scale,
                            rows, num_heads, num_kv_heads, num_cache_slots, sp, status, shadow) != cudaSuccess) {

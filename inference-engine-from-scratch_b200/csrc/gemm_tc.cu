@@ -851,6 +851,20 @@ bool make_tmap_kv(CUtensorMap* map, const void* base, int nkv, long long slots) 
   return r == CUDA_SUCCESS;
 }
 
+bool make_tmap_kv8(CUtensorMap* map, const void* base, int nkv, long long slots) {
+  auto encode = get_encode_fn();
+  if (!encode || !base || (reinterpret_cast<uintptr_t>(base) & 127u) || nkv < 1 || slots < 16) return false;
+  // [slots][nkv][128] int8: x = the head dimension (128 bytes), y = the KV head, z = the slot
+  cuuint64_t dims[3] = {128, (cuuint64_t)nkv, (cuuint64_t)slots};
+  cuuint64_t strides[2] = {128, (cuuint64_t)nkv * 128};
+  cuuint32_t box[3] = {128, 1, 16};
+  cuuint32_t estrides[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estrides,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 bool make_tmap_w8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
   auto encode = get_encode_fn();
   if (!encode || !base || (reinterpret_cast<uintptr_t>(base) & 15u) || cols % 16 != 0) return false;

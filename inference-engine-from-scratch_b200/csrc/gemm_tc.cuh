@@ -131,6 +131,8 @@ bool make_tmap_w8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t co
 // A paged bf16 KV pool [slots][nkv][128] as a 3-D map whose box is one KV head's 16-token block,
 // half the head dimension at a time (64 x 1 x 16, 128-byte swizzle): two loads per K or V block.
 bool make_tmap_kv(CUtensorMap* map, const void* base, int nkv, long long slots);
+// The same for an int8 pool [slots][nkv][128]: one load per K or V block (128 x 1 x 16 bytes).
+bool make_tmap_kv8(CUtensorMap* map, const void* base, int nkv, long long slots);
 constexpr int GEMM_W8_TILE_BYTES = GEMM_BM * GEMM_BK;  // int8 staging per stage
 
 }  // namespace ne

@@ -233,8 +233,9 @@ def test_paged_attention_matches_fp32_reference(lib, cuda_device, nh, nkv, q_len
 
 
 def test_cp_async_staging_matches_the_fp32_reference_too() -> None:
-    """The speculative step's bf16 attention loads K / V with tensor loads (TMA) by default; with
-    NE_ATTN_TMA=0 it stages them with cp.async: the same cases, that path, in a fresh process."""
+    """The speculative step's attention loads K / V with tensor loads (TMA) by default, bf16 and int8
+    pools; with NE_ATTN_TMA=0 it stages them with cp.async: the same cases, that path, in a fresh
+    process."""
     import os
     import subprocess
     import sys
@@ -244,6 +245,6 @@ def test_cp_async_staging_matches_the_fp32_reference_too() -> None:
     env = dict(os.environ, NE_ATTN_TMA="0")
     proc = subprocess.run(
         [sys.executable, "-m", "pytest", "-q", "-x", "-p", "no:cacheprovider", "tests/test_gpu_kernels.py", "-k",
-         "paged_attention_matches_fp32_reference and False"], cwd=REPO, env=env, capture_output=True, text=True,
+         "paged_attention_matches_fp32_reference"], cwd=REPO, env=env, capture_output=True, text=True,
         timeout=900)
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-2000:]
