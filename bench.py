@@ -183,7 +183,9 @@ class ClockSampler:
             time.sleep(self.interval)
 
     def __enter__(self):
+        # (re-entered for every timed region: the samples of all of them add up)
         if self.nvml is not None:
+            self._stop.clear()
             self._thread = threading.Thread(target=self._run, daemon=True)
             self._thread.start()
         return self
@@ -699,7 +701,7 @@ def run_b200(args, dist: Dist) -> None:
                                         temperature=wl.temperature, top_p=wl.top_p, seeds=list(range(len(prompts))),
                                         prefix=rep_prefix)
         engine.prefill(rep_slots, chunk=wl.prefill_chunk)
-        rep, _, _ = time_steady_steps(engine, engine_mod, rep_slots, args.steps, args.warmup, dist)
+        rep, _, _ = time_steady_steps(engine, engine_mod, rep_slots, args.steps, args.warmup, dist, clocks)
         repeat_ms.append(dist.max(rep) / args.steps)
         engine.release(rep_slots)
         if rep_prefix is not None:
