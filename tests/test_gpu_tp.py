@@ -16,9 +16,14 @@ import sys
 import pytest
 import torch
 
-from tests.conftest import REPO
+from tests.conftest import REPO, report_near_ties
 
 pytestmark = pytest.mark.gpu
+
+# the split adds its fp32 partial sums in another order than the unsplit model, and the bf16
+# activations between layers can round the other way: a decision may flip only where the unsplit
+# model's two candidates lie within twice the bf16 logit tolerance (2e-2) of each other
+NEAR_TIE = 2 * 2e-2
 
 
 def _free_port() -> int:
@@ -44,8 +49,19 @@ def test_two_rank_split_serves_the_unsplit_outputs(tmp_path) -> None:
     # over the peer exchange (one and two phases), the exchange for steps only, and NCCL only
     for name in ("eager", "graphs", "mixed", "nccl", "two_phase"):
         assert r0[name] == r1[name] == r0["graphs"], name
-    # and they equal the unsplit model's tokens (fp32 partial sums: only the summation order differs)
-    assert r0["graphs"] == r0["unsplit"]
+    # and they equal the unsplit model's tokens up to a first difference at a near-tie
+    ties, margins = r0["ties"], []
+    for r, (split, whole) in enumerate(zip(r0["graphs"], r0["unsplit"])):
+        if split == whole:
+            assert str(r) not in ties
+            continue
+        i, between, top2 = ties[str(r)]
+        assert split[:i] == whole[:i] and split[i] != whole[i]
+        # (the scoring pass is a prefill, its sums in yet another order: the sign is not kept)
+        assert abs(between) <= NEAR_TIE, (r, i, split[i], whole[i], between, top2)
+        margins.append(abs(between))
+    assert len(margins) <= 1, ties  # a flip is rare: at most one of the four requests
+    report_near_ties("test_gpu_tp", len(r0["unsplit"]), len(r0["unsplit"]) - len(margins), margins)
     assert all(len(o) == 32 for o in r0["unsplit"])
     # a rank whose peer launches nothing: its exchange waits end (bounded) with the timeout status
     assert "bounded device wait ran out" in r0["lone_rank"], r0["lone_rank"]

@@ -6,7 +6,8 @@ exchange for the steps only (prefill through NCCL), through NCCL only, and with 
 exchange. Then rank 0 prefills
 alone on a split model, so that its bounded exchange waits run out. Rank 0 finally serves the
 prompts on the unsplit model (TP = 1, the oracle for the split: the same seeded weights, the same
-per-projection launch sequence). Each rank
+per-projection launch sequence) and scores, where a split output leaves the unsplit one, the
+unsplit model's logits at that token. Each rank
 writes its outputs to ``<out>.<rank>.json``.
 """
 
@@ -39,6 +40,35 @@ def serve(model, prompts, graphs: bool):
     model.raise_on_device_error()
     del eng  # its CUDA graphs hold the model's NCCL calls: release them first
     return outs
+
+
+class _Scored:
+    """A sequence as ``B200ModelRunner.score_tokens`` reads it, over the first blocks of the pool."""
+
+    block_size = 16
+
+    def __init__(self, token_ids: list[int]) -> None:
+        self.token_ids, self.num_cached_tokens = token_ids, 0
+
+    def block_table(self, sequence) -> list[int]:
+        return list(range(-(-len(self.token_ids) // self.block_size)))
+
+
+def near_ties(model, prompts, split, unsplit) -> dict[int, list]:
+    """For each request whose split outputs leave the unsplit ones: [index i of the first
+    difference, the unsplit model's logit of its own token i minus that of the split's token i, its
+    top-2 gap], from one scoring pass of the unsplit model over the prompt and tokens 0..i-1."""
+    ties = {}
+    for r, (a, b) in enumerate(zip(split, unsplit)):
+        i = next((j for j, (x, y) in enumerate(zip(a, b)) if x != y), None)
+        if i is None:
+            continue
+        scored = _Scored(list(prompts[r]) + list(b[:i]))
+        row = submodule("serial").B200ModelRunner(model, scored).score_tokens(scored, len(scored.token_ids))[-1]
+        row = row.float()
+        top = torch.topk(row, 2).values
+        ties[r] = [i, float(row[b[i]] - row[a[i]]), float(top[0] - top[1])]
+    return ties
 
 
 def main() -> None:
@@ -107,6 +137,7 @@ def main() -> None:
         # kernel, opt-in, adds its partials in another order)
         os.environ["NE_STEP_KERNEL"] = "0"
         result["unsplit"] = serve(whole, prompts, graphs=True)
+        result["ties"] = near_ties(whole, prompts, result["graphs"], result["unsplit"])
         del os.environ["NE_STEP_KERNEL"]
         whole.close()
     Path(f"{args.out}.{rank}.json").write_text(json.dumps(result))
