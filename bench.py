@@ -86,7 +86,9 @@ def parse_args():
     p.add_argument("--no-extra", action="store_true",
                    help="skip the 1/4/16-user lines and the config 3 / 4 block of the default run")
     p.add_argument("--profile-step", action="store_true",
-                   help="prefill, then two eager speculative steps and exit (a short target for ncu)")
+                   help="prefill, then --profile-steps eager speculative steps and exit (a short target for ncu)")
+    p.add_argument("--profile-steps", type=int, default=2,
+                   help="with --profile-step: how many eager steps (later steps verify more rows)")
     p.add_argument("--profile-users", type=int, default=0,
                    help="with --profile-step: serve this many users instead of the workload's (small ncu captures)")
     return p.parse_args()
@@ -595,8 +597,8 @@ def run_b200(args, dist: Dist) -> None:
                                 top_p=wl.top_p, seeds=list(range(len(prompts))), prefix=prefix)
     engine.prefill(slots, chunk=wl.prefill_chunk)
     if args.profile_step:
-        # two eager steps; print what each processed so that ncu byte counts can be scaled per unit
-        for i in range(2):
+        # eager steps; print what each processed so that ncu byte counts can be scaled per unit
+        for i in range(args.profile_steps):
             idx = torch.tensor(slots, device=device).long()
             ctx_before = int(engine.state.seq_len[idx].sum().item())
             engine._set_slots(slots, len(slots))
