@@ -55,8 +55,8 @@ struct ne_model {
   int rows_hint = 0;         // a speculative step's expected rows (GEMM planning), 0 otherwise
   long long split_rows = 0;
   float* ssq = nullptr;      // fp32 [max_rows, H / 128]: residual rows' sums of squares per 128-wide tile
-  CUtensorMap tm_h{};        // the residual rows as a GEMM X operand (RMSNorm fused into the GEMM)
-  CUtensorMap tm_x{}, tm_attn{}, tm_act{};
+  ne::XMap tm_h{};           // the residual rows as a GEMM X operand (RMSNorm fused into the GEMM)
+  ne::XMap tm_x{}, tm_attn{}, tm_act{};
   int num_sms = 148;
   // the persistent step kernel (step_kernel.cu): its cut of the projections, split-K partial areas,
   // counters, per-layer pointers (workspace) and tensor maps (a kernel parameter)
@@ -210,7 +210,7 @@ int sm_count() {
 
 // ``x_norm_w`` (may be NULL): X is the residual stream h and RMSNorm with this weight is applied to
 // it inside the GEMM (statistics from m->ssq).
-int run_gemm(ne_model* m, const CUtensorMap* tw, const CUtensorMap* tx, int M_max, const int32_t* M_dev, int N, int K,
+int run_gemm(ne_model* m, const CUtensorMap* tw, const ne::XMap* tx, int M_max, const int32_t* M_dev, int N, int K,
              const ne::Epilogue& epi, cudaStream_t stream, const void* w_scale = nullptr,
              const void* x_norm_w = nullptr) {
   GemmParams p{};
@@ -246,7 +246,7 @@ bool split_partials_enabled() {
 // o_proj / down_proj of an unsplit model: out = h + bf16(X W^T). Split over K, the partial tiles
 // stay in m->split for the next RMSNorm to add (*splits = the slice count); unsplit (or when the
 // slices do not fit) the GEMM adds to h itself (*splits = 0).
-int residual_gemm(ne_model* m, const CUtensorMap* tw, const CUtensorMap* tx, int R, const int32_t* M_dev, int N, int K,
+int residual_gemm(ne_model* m, const CUtensorMap* tw, const ne::XMap* tx, int R, const int32_t* M_dev, int N, int K,
                   cudaStream_t stream, const void* w_scale, int* splits) {
   *splits = 0;
   GemmParams p{};
@@ -299,10 +299,10 @@ int upload_step_descriptors(ne_model* m) {
                             static_cast<__nv_bfloat16*>(w.k_cache), static_cast<__nv_bfloat16*>(w.v_cache)};
   }
   maps[4 * L] = m->tm_lm;
-  maps[4 * L + 1] = m->tm_h;
-  maps[4 * L + 2] = m->tm_attn;
-  maps[4 * L + 3] = m->tm_act;
-  maps[4 * L + 4] = m->tm_x;
+  maps[4 * L + 1] = m->tm_h.rows64;
+  maps[4 * L + 2] = m->tm_attn.rows64;
+  maps[4 * L + 3] = m->tm_act.rows64;
+  maps[4 * L + 4] = m->tm_x.rows64;
   if (cudaMemcpy(const_cast<ne::SkLayer*>(m->sk.layers), layers.data(), layers.size() * sizeof(ne::SkLayer),
                  cudaMemcpyHostToDevice) != cudaSuccess)
     return NE_ERR_CUDA;
@@ -538,10 +538,9 @@ int ne_model_set_workspace(ne_model* m, void* ws, size_t bytes, int max_rows, in
   m->split_rows = m->tp_world > 1 ? 0 : (long long)split_rows_cap(max_rows);
   m->ssq = reinterpret_cast<float*>(base + l.ssq);
   const int qs = c.num_heads * 128;
-  bool ok = ne::make_tmap_bf16(&m->tm_x, m->x, max_rows, c.hidden_size, ne::GEMM_XBOX, ne::GEMM_BK) &&
-            ne::make_tmap_bf16(&m->tm_h, m->h, max_rows, c.hidden_size, ne::GEMM_XBOX, ne::GEMM_BK) &&
-            ne::make_tmap_bf16(&m->tm_attn, m->attn, max_rows, qs, ne::GEMM_XBOX, ne::GEMM_BK) &&
-            ne::make_tmap_bf16(&m->tm_act, m->act, max_rows, c.intermediate_size, ne::GEMM_XBOX, ne::GEMM_BK);
+  bool ok = ne::make_xmap(&m->tm_x, m->x, max_rows, c.hidden_size) &&
+            ne::make_xmap(&m->tm_h, m->h, max_rows, c.hidden_size) && ne::make_xmap(&m->tm_attn, m->attn, max_rows, qs) &&
+            ne::make_xmap(&m->tm_act, m->act, max_rows, c.intermediate_size);
   if (!ok) return NE_ERR_INVALID;
   if (cudaMemset(ws, 0, l.total) != cudaSuccess) return NE_ERR_CUDA;
   m->sk_ready = false;
@@ -1122,9 +1121,9 @@ int ne_gemm_bf16(const void* x, const void* w, void* y, int M, int N, int K, int
   if (!x || !w || !y || M <= 0 || N % ne::GEMM_BM || K % ne::GEMM_BK || !aligned16(x) || !aligned16(w) ||
       !aligned16(y))
     return NE_ERR_INVALID;
-  CUtensorMap tw, tx;
-  if (!ne::make_tmap_bf16(&tw, w, N, K, ne::GEMM_BM, ne::GEMM_BK) ||
-      !ne::make_tmap_bf16(&tx, x, M, K, ne::GEMM_XBOX, ne::GEMM_BK))
+  CUtensorMap tw;
+  ne::XMap tx;
+  if (!ne::make_tmap_bf16(&tw, w, N, K, ne::GEMM_BM, ne::GEMM_BK) || !ne::make_xmap(&tx, x, M, K))
     return NE_ERR_INVALID;
   GemmParams p{};
   p.M_max = M;
@@ -1145,8 +1144,9 @@ int ne_gemm_w8(const void* x, const void* w, const void* scale, void* y, int M, 
   if (!x || !w || !scale || !y || M <= 0 || N % ne::GEMM_BM || K % ne::GEMM_BK || !aligned16(x) || !aligned16(w) ||
       !aligned16(y))
     return NE_ERR_INVALID;
-  CUtensorMap tw, tx;
-  if (!ne::make_tmap_w8(&tw, w, N, K) || !ne::make_tmap_bf16(&tx, x, M, K, ne::GEMM_XBOX, ne::GEMM_BK))
+  CUtensorMap tw;
+  ne::XMap tx;
+  if (!ne::make_tmap_w8(&tw, w, N, K) || !ne::make_xmap(&tx, x, M, K))
     return NE_ERR_INVALID;
   GemmParams p{};
   p.M_max = M;

@@ -454,7 +454,7 @@ __device__ __forceinline__ void nx_convert_chunk(uint32_t addr, float rstd, uint
 template <int MODE, int CONV>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
-                   const GemmParams p) {
+                   const __grid_constant__ CUtensorMap tm_x16, const GemmParams p) {
   constexpr bool W8 = (CONV & CONV_W8) != 0;
   constexpr bool NX = (CONV & CONV_NX) != 0;
   constexpr bool SPLIT_OUT = MODE == EPI_SPLIT_F32;  // split-K partials to global, no cluster
@@ -477,7 +477,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   // stage: [bf16 W tile 16 KB][X tile][int8 W tile 8 KB when W8]
   const int w_bytes = GEMM_BM * GEMM_BK * 2;                                     // 16 KB
-  const int x_region = ((p.t_block + GEMM_XBOX - 1) / GEMM_XBOX) * GEMM_XBOX * GEMM_BK * 2;
+  const int x_region = gemm_x_rows(p.t_block) * GEMM_BK * 2;
   const int stage_bytes = w_bytes + x_region + (W8 ? GEMM_W8_TILE_BYTES : 0);
   const int w_dst_off = W8 ? w_bytes + x_region : 0;          // where the W TMA lands in a stage
   const uint32_t w_load_bytes = W8 ? (uint32_t)GEMM_W8_TILE_BYTES : (uint32_t)w_bytes;
@@ -576,20 +576,29 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int slice = (((t_actual + S - 1) / S) + 7) & ~7;
   const int own_cnt = max(0, min(slice, t_actual - split * slice));
   if (S > 1 && !SPLIT_OUT && tid == 0) mbar_arrive_expect_tx(recv_bar, (uint32_t)((S - 1) * own_cnt * GEMM_BM * 4));
-  const int n_loads = (t_actual + GEMM_XBOX - 1) / GEMM_XBOX;
-  const int n_pad = (t_actual + 15) & ~15;
+  // the X tile: whole 64-row boxes while 64 rows remain, then 16-row boxes up to the last row, so
+  // that a CTA loads its rows rounded up to 16 (not to 64) in at most 3 + t / 64 copies
+  const int n_full = t_actual / GEMM_XBOX;
+  const int n_tail = (t_actual - n_full * GEMM_XBOX + GEMM_XBOX_TAIL - 1) / GEMM_XBOX_TAIL;
+  const int n_pad = n_full * GEMM_XBOX + n_tail * GEMM_XBOX_TAIL;  // = t_actual rounded up to 16
   const int part0 = n_pad < 256 ? n_pad : 256;
   const int part1 = n_pad - part0;
-  const uint32_t x_bytes = (uint32_t)(n_loads * GEMM_XBOX * GEMM_BK * 2);
+  const uint32_t x_bytes = (uint32_t)(n_pad * GEMM_BK * 2);
+  auto load_x = [&](uint8_t* dst, uint64_t* bar, int kx) {
+    for (int l = 0; l < n_full; ++l)
+      tma_load_2d(dst + l * GEMM_XBOX * GEMM_BK * 2, &tm_x, bar, kx, m0 + l * GEMM_XBOX);
+    for (int l = 0; l < n_tail; ++l) {
+      const int r = n_full * GEMM_XBOX + l * GEMM_XBOX_TAIL;
+      tma_load_2d(dst + r * GEMM_BK * 2, &tm_x16, bar, kx, m0 + r);
+    }
+  };
 
   if (warp == 0) {
     if (lane == 0) {
       for (int i = 0; i < pre; ++i) {
         uint8_t* st = smem + i * stage_bytes;
         mbar_expect_tx(&full[i], x_bytes);
-        for (int l = 0; l < n_loads; ++l)
-          tma_load_2d(st + w_bytes + l * GEMM_XBOX * GEMM_BK * 2, &tm_x, &full[i], (k_begin + i) * GEMM_BK,
-                      m0 + l * GEMM_XBOX);
+        load_x(st + w_bytes, &full[i], (k_begin + i) * GEMM_BK);
         mbar_arrive(&full[i]);
       }
       for (int i = pre; i < nk; ++i) {
@@ -600,8 +609,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         mbar_arrive_expect_tx(&full[s], w_load_bytes + x_bytes);
         const int kx = (k_begin + i) * GEMM_BK;
         load_w(st + w_dst_off, &full[s], kx);
-        for (int l = 0; l < n_loads; ++l)
-          tma_load_2d(st + w_bytes + l * GEMM_XBOX * GEMM_BK * 2, &tm_x, &full[s], kx, m0 + l * GEMM_XBOX);
+        load_x(st + w_bytes, &full[s], kx);
         issued = i + 1;
       }
     }
@@ -837,6 +845,11 @@ bool make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t 
   return r == CUDA_SUCCESS;
 }
 
+bool make_xmap(XMap* map, const void* base, uint64_t rows, uint64_t cols) {
+  return make_tmap_bf16(&map->rows64, base, rows, cols, GEMM_XBOX, GEMM_BK) &&
+         make_tmap_bf16(&map->rows16, base, rows, cols, GEMM_XBOX_TAIL, GEMM_BK);
+}
+
 bool make_tmap_kv(CUtensorMap* map, const void* base, int nkv, long long slots) {
   auto encode = get_encode_fn();
   if (!encode || !base || (reinterpret_cast<uintptr_t>(base) & 127u) || nkv < 1 || slots < 16) return false;
@@ -897,11 +910,11 @@ cudaError_t prepare_mode() {
 }
 
 template <int MODE, int CONV>
-cudaError_t launch_mode(const cudaLaunchConfig_t& cfg, const CUtensorMap* tm_w, const CUtensorMap* tm_x,
+cudaError_t launch_mode(const cudaLaunchConfig_t& cfg, const CUtensorMap* tm_w, const XMap* tm_x,
                         const GemmParams& p) {
   cudaError_t err = prepare_mode<MODE, CONV>();
   if (err != cudaSuccess) return err;
-  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<MODE, CONV>, *tm_w, *tm_x, p);
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<MODE, CONV>, *tm_w, tm_x->rows64, tm_x->rows16, p);
 }
 
 // Clusters of ``splits`` CTAs with ``smem`` bytes each that the GPU holds at once (0 on error).
@@ -1051,7 +1064,7 @@ int plan_uncached(GemmParams& p, int num_sms) {
     --S;
   }
   if (S > 1 && !fits(S, t_block)) S = 1;
-  const int stage_bytes = GEMM_BM * GEMM_BK * 2 + ((t_block + GEMM_XBOX - 1) / GEMM_XBOX) * GEMM_XBOX * GEMM_BK * 2 +
+  const int stage_bytes = GEMM_BM * GEMM_BK * 2 + gemm_x_rows(t_block) * GEMM_BK * 2 +
                           (p.w_scale ? GEMM_W8_TILE_BYTES : 0);
   const int cps = (num_chunks + S - 1) / S;
   int stages = std::min(std::min(max_stages(), cps), avail / stage_bytes);
@@ -1107,21 +1120,19 @@ int plan_with_occupancy(GemmParams& p, int num_sms) {
 }
 }  // namespace
 
-int gemm_launch(const CUtensorMap* tm_w, const CUtensorMap* tm_x, const GemmParams& p, cudaStream_t stream) {
+int gemm_launch(const CUtensorMap* tm_w, const XMap* tm_x, const GemmParams& p, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.splits, p.N / GEMM_BM, (p.M_max + p.t_block - 1) / p.t_block);
   cfg.blockDim = dim3(GEMM_THREADS);
   cfg.dynamicSmemBytes = p.smem_data + 256 + GEMM_RSTD_BYTES + 1024;
   cfg.stream = stream;
-  cudaLaunchAttribute attrs[2];
+  cudaLaunchAttribute attrs[3];
   attrs[0].id = cudaLaunchAttributeClusterDimension;
   attrs[0].val.clusterDim.x = p.epi.mode == EPI_SPLIT_F32 ? 1 : p.splits;
   attrs[0].val.clusterDim.y = 1;
   attrs[0].val.clusterDim.z = 1;
-  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attrs[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
-  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  cfg.numAttrs = add_common_attrs(attrs, 1, smem_carveout_gemm());
   cudaError_t err = cudaErrorInvalidValue;
   const int conv = conv_bits(p);
   bool found = false;

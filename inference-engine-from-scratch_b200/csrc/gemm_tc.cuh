@@ -28,6 +28,16 @@ namespace ne {
 constexpr int GEMM_BM = 128;         // weight rows per tile (MMA M)
 constexpr int GEMM_BK = 64;          // K elements per stage (128 bytes of bf16)
 constexpr int GEMM_XBOX = 64;        // token rows per X TMA box
+constexpr int GEMM_XBOX_TAIL = 16;   // token rows per X TMA box past a CTA's last whole 64-row box
+// Token rows a pipeline stage reserves for the X tile of a t_block-row CTA: t_block rounded up to
+// 16 for blocks of up to 32 rows (1-4 users of a verify step), to 64 above. A small request lets
+// the CTAs of a small step start beside the previous kernel's last CTAs under programmatic launch
+// (config 2 at 1 user: 1.258 -> 1.228 ms per step); rounding to 16 at 16 users (80-row blocks) and
+// 64 users was slower (1.341 -> 1.351 and 1.817 -> 1.822 ms).
+__host__ __device__ constexpr int gemm_x_rows(int t_block) {
+  return t_block <= 32 ? (t_block + GEMM_XBOX_TAIL - 1) / GEMM_XBOX_TAIL * GEMM_XBOX_TAIL
+                       : (t_block + GEMM_XBOX - 1) / GEMM_XBOX * GEMM_XBOX;
+}
 constexpr int GEMM_THREADS = 256;  // warps 0-3 run TMA / MMA / TMEM roles, all 8 run the epilogue
 constexpr int GEMM_MAX_TOKENS = 512; // tokens per CTA (TMEM columns)
 constexpr int GEMM_SMEM_BYTES = 227 * 1024;
@@ -121,8 +131,15 @@ struct GemmParams {
   Epilogue epi;
 };
 
+// The X operand (activation rows [rows, K] bf16) as two tensor maps over one buffer: 64-row boxes
+// for a CTA's whole 64-row groups, 16-row boxes for the rest of its rows.
+struct XMap {
+  CUtensorMap rows64, rows16;
+};
+bool make_xmap(XMap* map, const void* base, uint64_t rows, uint64_t cols);
+
 // Host side: build the params / launch (gemm_tc.cu).
-int gemm_launch(const CUtensorMap* tm_w, const CUtensorMap* tm_x, const GemmParams& p, cudaStream_t stream);
+int gemm_launch(const CUtensorMap* tm_w, const XMap* tm_x, const GemmParams& p, cudaStream_t stream);
 int gemm_plan(GemmParams& p, int num_sms);
 bool make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
                     uint32_t box_cols);
