@@ -510,6 +510,80 @@ __device__ __forceinline__ void for_each_chunk(const __nv_bfloat16* row, int beg
   }
 }
 
+// Tie ranks of a draw (kept_p's rank of a token equal to tau, counted in token order): one counter
+// per row the draw reads (p: the target row, q: a draft row).
+struct Ranks {
+  uint32_t p, q;
+};
+
+// The end of an inverse-CDF draw, block-wide: the first token of warp ``owner``'s range [ob, oe)
+// whose inclusive prefix exceeds ``target`` (``before``: the mass of the ranges below it; ``base``:
+// the tie ranks at ob). The range is cut into WARPS sub-ranges of whole 32-token chunks; every warp
+// sums its sub-range with the per-token values the scan adds (fixed point, so the sub-range sums add
+// up to the range's sum exactly), and the warp whose sub-range holds the target scans it, so no
+// warp walks more than one sub-range. ``tie_count(i, in_range)``: the chunk's ties per row
+// (warp-collective; called only when ``ties``); ``value(i, in_range, ranks)``: token i's fixed-point
+// value, advancing ``ranks`` by the chunk's ties (warp-collective).
+template <typename TieCount, typename Value>
+__device__ int search_owner_range(int ob, int oe, unsigned long long before, unsigned long long target, Ranks base,
+                                  bool ties, TieCount&& tie_count, Value&& value, DrawShared& sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int per = ((oe - ob + 32 * WARPS - 1) / (32 * WARPS)) * 32;  // tokens per sub-range
+  const int sb = min(oe, ob + warp * per), se = min(oe, sb + per);
+  Ranks mine{0u, 0u};
+  if (ties) {
+    for (int b = sb; b < se; b += 32) {
+      const Ranks d = tie_count(b + lane, b + lane < se);
+      mine.p += d.p;
+      mine.q += d.q;
+    }
+  }
+  __syncthreads();  // every thread has read the per-range sums and ties it needed
+  if (lane == 0) {
+    sh.warp_ties[warp] = mine.p;
+    sh.warp_ties_q[warp] = mine.q;
+  }
+  __syncthreads();
+  Ranks r = base;
+  for (int w = 0; w < warp; ++w) {
+    r.p += sh.warp_ties[w];
+    r.q += sh.warp_ties_q[w];
+  }
+  const Ranks r0 = r;
+  unsigned long long sum = 0;
+  for (int b = sb; b < se; b += 32) sum += value(b + lane, b + lane < se, r);
+  sum = warp_sum_u64(sum);
+  if (lane == 0) sh.warp_sum[warp] = sum;
+  if (threadIdx.x == 0) sh.result = -1;
+  __syncthreads();
+  int sub = -1;
+  unsigned long long run = before;
+  for (int w = 0; w < WARPS; ++w) {
+    if (run + sh.warp_sum[w] > target) {
+      sub = w;
+      break;
+    }
+    run += sh.warp_sum[w];
+  }
+  if (warp == sub) {
+    r = r0;
+    for (int b = sb; b < se; b += 32) {
+      const int i = b + lane;
+      const unsigned long long incl = run + warp_incl_scan_u64(value(i, i < se, r), lane);
+      const uint32_t hit = __ballot_sync(FULL, i < se && incl > target);
+      if (hit) {
+        if (lane == 0) sh.result = b + __ffs(hit) - 1;
+        break;
+      }
+      run = __shfl_sync(FULL, incl, 31);
+    }
+  }
+  __syncthreads();
+  const int tok = sh.result;
+  __syncthreads();
+  return tok;
+}
+
 // Draw from row ``row``'s target distribution with token ``exclude`` (>= 0) removed and the rest
 // renormalised (the rejection residual), using uniform u = u24 * 2^-24.
 __device__ int draw_token(const __nv_bfloat16* row, int vocab, float T, const SampleStats& s, int exclude,
@@ -592,29 +666,26 @@ __device__ int draw_token(const __nv_bfloat16* row, int vocab, float T, const Sa
     }
     before += sh.warp_sum[w];
   }
-  if (threadIdx.x == 0) sh.result = -1;
-  __syncthreads();
-  if (warp == owner) {
-    unsigned long long run = before;
-    uint32_t rank = tie_base;
-    for_each_chunk(row, begin, end, [&](int base, int i, __nv_bfloat16 x) {
-      float v = chunk_value_of(x, i < end, T, s, rank);
-      if (i == exclude) v = 0.f;
-      const unsigned long long f = renorm ? to_fix(v / norm) : to_fix(v);
-      const unsigned long long incl = run + warp_incl_scan_u64(f, lane);
-      const uint32_t hit = __ballot_sync(FULL, i < end && incl > target);
-      if (hit) {
-        if (lane == 0) sh.result = base + __ffs(hit) - 1;
-        return false;
-      }
-      run = __shfl_sync(FULL, incl, 31);
-      return true;
-    });
+  if (owner < 0) {  // (only when the total is 0: no token to draw)
+    __syncthreads();
+    return -1;
   }
-  __syncthreads();
-  const int tok = sh.result;
-  __syncthreads();
-  return tok;
+  // the owner range's tie rank base: its ties are counted again inside the search
+  uint32_t owner_base = 0;
+  for (int w = 0; w < owner; ++w) owner_base += sh.warp_ties[w];
+  const int ob = owner * len, oe = min(vocab, ob + len);
+  return search_owner_range(
+      ob, oe, before, target, Ranks{owner_base, 0u}, partial_ties(s),
+      [&](int i, bool in_range) {
+        const bool tie = in_range && prob(scaled(row, i, T), s.m, s.z) == s.tau;
+        return Ranks{(uint32_t)__popc(__ballot_sync(FULL, tie)), 0u};
+      },
+      [&](int i, bool in_range, Ranks& r) {
+        float v = chunk_value(row, i, in_range, T, s, r.p);
+        if (i == exclude) v = 0.f;
+        return renorm ? to_fix(v / norm) : to_fix(v);
+      },
+      sh);
 }
 
 // Draw from the residual of a rejected draft-model guess (verifier.py:53-57): max(0, p - q) over
@@ -692,29 +763,30 @@ __device__ int draw_residual(const __nv_bfloat16* prow, const SampleStats& ps, c
     }
     before += sh.warp_sum[w];
   }
-  if (threadIdx.x == 0) sh.result = -1;
-  __syncthreads();
-  if (warp == owner) {
-    unsigned long long run = before;
-    uint32_t pr = pbase, qr = qbase;
-    for (int base = begin; base < end; base += 32) {
-      const int i = base + lane;
-      const float p = chunk_value(prow, i, i < end, T, ps, pr);
-      const float q = chunk_value(qrow, i, i < end, T, qs, qr);
-      const unsigned long long f = to_fix(fmaxf(p - q, 0.f) / norm);
-      const unsigned long long incl = run + warp_incl_scan_u64(f, lane);
-      const uint32_t hit = __ballot_sync(FULL, i < end && incl > target);
-      if (hit) {
-        if (lane == 0) sh.result = base + __ffs(hit) - 1;
-        break;
-      }
-      run = __shfl_sync(FULL, incl, 31);
-    }
+  if (owner < 0) {  // (only when the total is 0: no token to draw)
+    __syncthreads();
+    return -1;
   }
-  __syncthreads();
-  const int tok = sh.result;
-  __syncthreads();
-  return tok;
+  Ranks owner_base{0u, 0u};
+  for (int w = 0; w < owner; ++w) {
+    owner_base.p += sh.warp_ties[w];
+    owner_base.q += sh.warp_ties_q[w];
+  }
+  const int ob = owner * len, oe = min(vocab, ob + len);
+  return search_owner_range(
+      ob, oe, before, target, owner_base, pt || qt,
+      [&](int i, bool in_range) {
+        Ranks d{0u, 0u};
+        if (pt) d.p = __popc(__ballot_sync(FULL, in_range && prob(scaled(prow, i, T), ps.m, ps.z) == ps.tau));
+        if (qt) d.q = __popc(__ballot_sync(FULL, in_range && prob(scaled(qrow, i, T), qs.m, qs.z) == qs.tau));
+        return d;
+      },
+      [&](int i, bool in_range, Ranks& r) {
+        const float p = chunk_value(prow, i, in_range, T, ps, r.p);
+        const float q = chunk_value(qrow, i, in_range, T, qs, r.q);
+        return to_fix(fmaxf(p - q, 0.f) / norm);
+      },
+      sh);
 }
 
 // torch.argmax of a bf16 row (lowest id among equal maxima). Block-wide.
