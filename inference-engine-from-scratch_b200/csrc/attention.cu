@@ -589,7 +589,8 @@ __host__ __device__ constexpr int tma_stages(int nw) { return nw == 2 ? 3 : 2; }
 template <int NT, int NW, int NST>
 __device__ __forceinline__ void warp_tiles_tma(const Ctx& c, const ne_rows& rows, const AttnSplit& sp, int b, int h,
                                                int split, int kb0, int kb1, uint8_t* q_s, int* spos, uint8_t* buf,
-                                               __nv_bfloat16* out, int nh, int nkv, int v_base, const TmaKv& tk) {
+                                               __nv_bfloat16* out, int nh, int nkv, int v_base, const TmaKv& tk,
+                                               int tbl_pre) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int per_tile = NW / NT, my_tile = warp % NT, phase = warp / NT;
   uint8_t* wbuf_p = buf + warp * NST * TMA_STAGE_BYTES;
@@ -603,7 +604,9 @@ __device__ __forceinline__ void warp_tiles_tma(const Ctx& c, const ne_rows& rows
     const int kbj = first + per_tile * (j0 + lane);
     return (kbj < kb1 && kbj < stride) ? c.table[kbj] : -1;
   };
-  int tbl = table_chunk(0);
+  // split 0's first chunk was loaded by the caller before the context length was known
+  // (``tbl_pre``: entry phase + per_tile * lane, or -1 past the row); only the mask is left
+  int tbl = split == 0 ? (first + per_tile * lane < kb1 ? tbl_pre : -1) : table_chunk(0);
   // the checked pool block of ordinal j (its entry in ``tbl``), -1 when it names none
   auto block_of = [&](int j) -> long long {
     const int kb = first + per_tile * j;
@@ -1095,7 +1098,12 @@ __global__ void __launch_bounds__(32 * NW, NW == 8 ? 1 : NW == 4 ? 3 : 4)
   const int slots = gridDim.z / sp.splits;
   const int b = blockIdx.x, h = blockIdx.y, split = blockIdx.z / slots, tile = blockIdx.z % slots;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // the entry's fields load together, and the first block-table chunk with the last position (it
+  // does not wait for the context length, only its mask does): two dependent loads, not four,
+  // ahead of the first tensor load
   const int ql = rows.q_len[b];
+  const int r0 = rows.q_start[b];
+  const int ti = rows.table_index ? rows.table_index[b] : b;
   if (ql <= 0) return;
   Ctx c{};
   c.q = q;
@@ -1104,16 +1112,19 @@ __global__ void __launch_bounds__(32 * NW, NW == 8 ? 1 : NW == 4 ? 3 : 4)
   c.nkv = nkv;
   c.h = h;
   c.G = nh / nkv;
-  c.r0 = rows.q_start[b];
+  c.r0 = r0;
   c.nvec = ql * c.G;
   c.num_cache_slots = num_cache_slots;
   c.status = status;
-  c.table = rows.block_tables + (long long)(rows.table_index ? rows.table_index[b] : b) * rows.block_table_stride;
-  const int ctx = rows.positions[c.r0 + ql - 1] + 1;  // the last row sees the whole context
+  c.table = rows.block_tables + (long long)ti * rows.block_table_stride;
+  const int ntiles = (c.nvec + 15) / 16;
+  const int nt = (slots == 1 && ntiles == 2) ? 2 : 1;  // query tiles per warp group (the dispatch below)
+  const int kbj = warp / nt + (NW / nt) * lane;         // split 0's first chunk: ordinal lane of this warp
+  const int tbl_pre = (split == 0 && kbj < rows.block_table_stride) ? c.table[kbj] : -1;
+  const int ctx = rows.positions[r0 + ql - 1] + 1;  // the last row sees the whole context
   const int nblk = (ctx + 15) / 16;
   const int bps = (nblk + sp.splits - 1) / sp.splits;
   const int kb0 = split * bps, kb1 = min(nblk, kb0 + bps);
-  const int ntiles = (c.nvec + 15) / 16;
   constexpr int NST = tma_stages(NW);
   uint8_t* q_s = smem;                                     // 16 x ROW_BYTES
   int* spos = reinterpret_cast<int*>(smem + BLOCK_BYTES);  // 16 ints (+pad)
@@ -1128,12 +1139,13 @@ __global__ void __launch_bounds__(32 * NW, NW == 8 ? 1 : NW == 4 ? 3 : 4)
   const TmaKv tk{&kmap, &vmap, bars};
   if (slots > 1) {
     if (tile < ntiles)
-      warp_tiles_tma<1, NW, NST>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 16 * tile, tk);
+      warp_tiles_tma<1, NW, NST>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 16 * tile, tk,
+                                 tbl_pre);
   } else if (ntiles == 1) {
-    warp_tiles_tma<1, NW, NST>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 0, tk);
+    warp_tiles_tma<1, NW, NST>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 0, tk, tbl_pre);
   } else if constexpr (NW >= 4) {
     if (ntiles == 2)
-      warp_tiles_tma<2, NW, NST>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 0, tk);
+      warp_tiles_tma<2, NW, NST>(c, rows, sp, b, h, split, kb0, kb1, q_s, spos, buf, out, nh, nkv, 0, tk, tbl_pre);
     else
       report(status, NE_DEV_BAD_SLOT);  // the host sends only one- and two-tile entries here
   } else {
