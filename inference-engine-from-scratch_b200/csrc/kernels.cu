@@ -78,11 +78,14 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(__nv_bfloat16* __restrict_
   const bool exch = link.world > 0;
   const unsigned inst = exch ? tp_wait_all(link, status) : 0u;
   const bool active = row < n;
-  const int src = active ? (gather ? gather[row] : row) : 0;
+  // without an exchange or a gather, a row's loads do not wait for the row count: a row past it
+  // (inside the buffer) loads and stores nothing, so the count and the row arrive together
+  const bool early = !exch && !gather && row < max_rows;
+  const int src = early ? row : active ? (gather ? gather[row] : row) : 0;
   uint4* xr = reinterpret_cast<uint4*>(x + (long long)src * hidden);
   uint4 u[C];
   float ss = 0.f;
-  if (active) {
+  if (early || active) {
 #pragma unroll
     for (int j = 0; j < C; ++j) u[j] = xr[c0 + 32 * j];
 #pragma unroll
@@ -121,7 +124,7 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(__nv_bfloat16* __restrict_
         }
 #pragma unroll
         for (int k = 0; k < 8; ++k) e[k] = __float2bfloat16_rn(__bfloat162float(e[k]) + bf16r(av[k]));
-        xr[c0 + 32 * j] = u[j];
+        if (active) xr[c0 + 32 * j] = u[j];
       }
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
