@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(__nv_bfloat16* __restrict_
                                __nv_bfloat16* __restrict__ y, int max_rows, const int32_t* rows_dev,
                                const int32_t* gather, int hidden, float eps, unsigned long long* zero_keys,
                                const float* __restrict__ add, int add_count, long long add_stride,
-                               const TpLink link, int* status) {
+                               const TpLink link, int* status, int early_rows) {
   constexpr int C = CPL / WPR;  // chunks per lane
   static_assert(CPL % WPR == 0 && 4 % WPR == 0, "warps per row");
   __shared__ float part_ss[4];
@@ -78,9 +78,10 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(__nv_bfloat16* __restrict_
   const bool exch = link.world > 0;
   const unsigned inst = exch ? tp_wait_all(link, status) : 0u;
   const bool active = row < n;
-  // without an exchange or a gather, a row's loads do not wait for the row count: a row past it
-  // (inside the buffer) loads and stores nothing, so the count and the row arrive together
-  const bool early = !exch && !gather && row < max_rows;
+  // without an exchange or a gather, the loads of a row below ``early_rows`` do not wait for the
+  // row count: a row past it (inside the buffer) loads and stores nothing, so the count and the row
+  // arrive together
+  const bool early = !exch && !gather && row < early_rows;
   const int src = early ? row : active ? (gather ? gather[row] : row) : 0;
   uint4* xr = reinterpret_cast<uint4*>(x + (long long)src * hidden);
   uint4 u[C];
@@ -615,7 +616,7 @@ int launch_embed(const __nv_bfloat16* embed, const int32_t* tokens, const int32_
 int launch_rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int max_rows,
                    const int32_t* rows_dev, const int32_t* gather, int hidden, float eps,
                    unsigned long long* zero_keys, cudaStream_t stream, const float* add, int add_count,
-                   long long add_stride, const TpLink* link, int* status) {
+                   long long add_stride, const TpLink* link, int* status, int early_rows) {
   if (link && (link->world < 1 || link->hidden != hidden || max_rows > link->max_rows || add)) return NE_ERR_INVALID;
   if (add && add_count < 1) return NE_ERR_INVALID;
   // four warps per row from hidden 1024 up (more loads in flight per row), a warp per row below
@@ -629,7 +630,8 @@ int launch_rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, i
 #define NE_NORM_CASE(H, CPL, WPR)                                                                               \
   case H:                                                                                                       \
     err = launch_kernel(rmsnorm_kernel<CPL, WPR>, dim3(blocks), dim3(128), 0, stream, x, w, y, max_rows, rows_dev, \
-                        gather, hidden, eps, zero_keys, add, add_count, add_stride, lk, status);                \
+                        gather, hidden, eps, zero_keys, add, add_count, add_stride, lk, status,                 \
+                        std::min(std::max(early_rows, 0), max_rows));                                           \
     break;
     NE_NORM_CASE(256, 1, 1)
     NE_NORM_CASE(512, 2, 1)

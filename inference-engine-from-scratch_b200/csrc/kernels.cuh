@@ -30,11 +30,13 @@ int launch_embed(const __nv_bfloat16* embed, const int32_t* tokens, const int32_
 // update after split-K partials or a tensor-parallel all-reduce), then the norm of the updated row.
 // ``link`` (may be NULL; then ``add`` must be NULL): the partial rows come from the peer exchange
 // instead; the launch waits for them (bounded; NE_DEV_TIMEOUT into ``status``) and closes the exchange.
+// ``early_rows``: without an exchange or a gather, rows below it load before the device row count
+// is read (the rows a speculative step is expected to hold; 0: none).
 int launch_rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int max_rows,
                    const int32_t* rows_dev, const int32_t* gather, int hidden, float eps,
                    unsigned long long* zero_keys, cudaStream_t stream, const float* add = nullptr,
                    int add_count = 1, long long add_stride = 0, const TpLink* link = nullptr,
-                   int* status = nullptr);
+                   int* status = nullptr, int early_rows = 0);
 // Middle launch of a two-phase peer exchange (reduce-scatter sums -> all-gather pushes).
 int launch_tp_rs_reduce(const int32_t* rows_dev, int max_rows, const TpLink& link, int* status, cudaStream_t stream);
 // Peer exchange of the LM head's argmax keys over a vocabulary split: push this rank's keys
