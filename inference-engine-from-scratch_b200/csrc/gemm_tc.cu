@@ -289,14 +289,20 @@ __device__ void epilogue_rows(const Epilogue& e, int tile_n, int m_begin, int co
     float wn[4] = {1.f, 1.f, 1.f, 1.f};
     if (rope) unpack4_bf16(*reinterpret_cast<const uint2*>((is_q ? e.q_norm_w : e.k_norm_w) + d0), wn);
     const int kvh = is_q ? 0 : (is_k ? head - e.n_q_heads : head - e.n_q_heads - e.n_kv_heads);
-    int* pos_s = reinterpret_cast<int*>(e.scratch_smem);   // [count] positions, then [count] slots
-    int* slot_s = pos_s + GEMM_MAX_TOKENS;
-    for (int m = tid; m < count; m += GEMM_THREADS) {
-      int pos = rope ? e.positions[m_begin + m] : 0;
-      pos_s[m] = pos < 0 ? 0 : (pos >= e.max_positions ? e.max_positions - 1 : pos);
-      slot_s[m] = is_q ? 0 : e.slot_mapping[m_begin + m];
+    const int* pos_s = e.pre_pos;  // loaded during the mainloop, or here
+    const int* slot_s = e.pre_slot;
+    if (!pos_s) {
+      int* ps = reinterpret_cast<int*>(e.scratch_smem);  // [count] positions, then [count] slots
+      int* ss = ps + GEMM_MAX_TOKENS;
+      for (int m = tid; m < count; m += GEMM_THREADS) {
+        int pos = rope ? e.positions[m_begin + m] : 0;
+        ps[m] = pos < 0 ? 0 : (pos >= e.max_positions ? e.max_positions - 1 : pos);
+        ss[m] = is_q ? 0 : e.slot_mapping[m_begin + m];
+      }
+      pos_s = ps;
+      slot_s = ss;
+      __syncthreads();
     }
-    __syncthreads();
     for (int m0t = warp; m0t < count; m0t += 4 * (GEMM_THREADS / 32)) {
       uint2 cs_raw[4], sn_raw[4];
       float4 acc4[4];
@@ -682,6 +688,45 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   }
 
+  // EPI_QKV without the fused norm: the epilogue's per-row inputs for the rows this CTA finishes
+  // load while the mainloop runs (warps 2-7; warps 0 and 1 issue the loads and MMAs): positions
+  // and slots into the per-token area the fused norm would use, and the rows' RoPE cos / sin lines
+  // into L1, so that the epilogue starts on its arithmetic instead of two dependent loads
+  const int* pre_pos = nullptr;
+  const int* pre_slot = nullptr;
+  if constexpr (MODE == EPI_QKV && !NX) {
+    constexpr int PRE_ROWS = GEMM_RSTD_BYTES / 8;  // positions then slots, one int each
+    const int e0 = S > 1 ? split * slice : 0;
+    const int ecnt = S > 1 ? own_cnt : t_actual;
+    if (ecnt > 0 && ecnt <= PRE_ROWS) {
+      int* pp = reinterpret_cast<int*>(rstd_s);
+      int* psl = pp + PRE_ROWS;
+      const Epilogue& e = p.epi;
+      const int head = tile_n;
+      const bool is_q = head < e.n_q_heads;
+      const bool rope = is_q || head < e.n_q_heads + e.n_kv_heads;
+      if (warp >= 2) {
+        for (int m = tid - 64; m < ecnt; m += GEMM_THREADS - 64) {
+          const int row = m0 + e0 + m;
+          int pos = rope ? e.positions[row] : 0;
+          pos = pos < 0 ? 0 : (pos >= e.max_positions ? e.max_positions - 1 : pos);
+          pp[m] = pos;
+          psl[m] = is_q ? 0 : e.slot_mapping[row];
+          if (rope) {  // 256 bytes of cos and of sin: two 128-byte lines each
+            const __nv_bfloat16* cs = e.rope_cos + (long long)pos * 128;
+            const __nv_bfloat16* sn = e.rope_sin + (long long)pos * 128;
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(cs));
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(cs + 64));
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(sn));
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(sn + 64));
+          }
+        }
+      }
+      pre_pos = pp;
+      pre_slot = psl;
+    }
+  }
+
   // ------------------------------------------------------------------ epilogue
   // one thread waits for the accumulator; the rest wait at the CTA barrier (no spinning)
   if (tid == 64) *done_ok = ((nk == 0) || mbar_wait(done, 0, abort_flag, p.status)) ? 1 : 0;
@@ -711,6 +756,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (ok) {
         Epilogue epi = p.epi;
         epi.scratch_smem = stage_acc + 128 * GEMM_BM;  // past the [128][128] accumulator block
+        epi.pre_pos = pre_pos ? pre_pos + c0 : nullptr;
+        epi.pre_slot = pre_slot ? pre_slot + c0 : nullptr;
         epilogue_rows<MODE>(epi, tile_n, m_begin + c0, cnt, smem_u32(stage_acc));
       }
       __syncthreads();
@@ -792,6 +839,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (ok && got) {
         Epilogue epi = p.epi;
         epi.scratch_smem = send + (size_t)slice * GEMM_BM;  // the second send buffer is free now
+        epi.pre_pos = pre_pos;
+        epi.pre_slot = pre_slot;
         epilogue_rows<MODE>(epi, tile_n, m_begin + split * slice, own_cnt, red_s);
       }
       __syncthreads();

@@ -68,6 +68,10 @@ enum EpilogueMode : int {
 struct Epilogue {
   int mode;
   void* scratch_smem;             // set by the kernel: 2 x GEMM_MAX_TOKENS ints of shared memory
+  // EPI_QKV, set by the kernel when it loaded them during the mainloop (else nullptr): the rows'
+  // clamped positions and their slots (shared memory, indexed from the epilogue's first row)
+  const int* pre_pos;
+  const int* pre_slot;
   int* status;                    // device status word (bad slot reports)
   __nv_bfloat16* out;
   long long ldo;
